@@ -1,0 +1,93 @@
+// Python bindings of the native kernels (module dattri_llm_b200._C).
+//
+// Every entry point validates dtype, device, contiguity and the 16-byte alignment
+// that TMA needs, then launches on the current PyTorch stream.  Kernels report
+// bounded-wait timeouts into the int32 `err` tensor the caller passes in.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+using torch::Tensor;
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+void check_err(const Tensor& err) {
+  check_cuda(err, "err");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32 && err.numel() >= 1, "err must be int32[>=1]");
+}
+
+bw::GemmOperand operand(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2 || t.dim() == 3, name, " must be 2-D or 3-D");
+  TORCH_CHECK(t.stride(-1) == 1, name, " must be contiguous along K");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " must be 16-byte aligned");
+  bw::GemmOperand op;
+  op.ptr = t.data_ptr();
+  op.rows = t.size(-2);
+  op.cols = t.size(-1);
+  op.row_stride = t.dim() >= 2 ? t.stride(-2) : t.size(-1);
+  if (op.rows == 1) op.row_stride = ((op.cols + 7) / 8) * 8;
+  TORCH_CHECK(op.row_stride % 8 == 0, name, " row stride must be a multiple of 8 elements");
+  TORCH_CHECK(op.cols % 8 == 0, name, " K must be a multiple of 8");
+  op.batch = t.dim() == 3 ? t.size(0) : 1;
+  op.batch_stride = t.dim() == 3 ? t.stride(0) : op.rows * op.row_stride;
+  if (op.batch > 1) TORCH_CHECK(op.batch_stride % 8 == 0, name, " batch stride must be 8-aligned");
+  return op;
+}
+
+// C (op)= alpha * A @ B^T, see bw::GemmStore for `mode`.
+void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t splits,
+             bool accumulate, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  TORCH_CHECK(a.cols == b.cols, "A and B disagree on K");
+  check_cuda(C, "C");
+  const bool bf16_out = mode == bw::kStoreBF16 || mode == bw::kStoreBF16T;
+  TORCH_CHECK(C.scalar_type() == (bf16_out ? torch::kBFloat16 : torch::kFloat32),
+              "C dtype does not match the store mode");
+  TORCH_CHECK(C.stride(-1) == 1, "C must be contiguous along its last axis");
+  const int z = static_cast<int>(a.batch);
+  TORCH_CHECK(b.batch == 1 || b.batch == a.batch, "B batch must be 1 or equal A's");
+  bw::GemmParams p{};
+  p.M = static_cast<int>(a.rows);
+  p.N = static_cast<int>(b.rows);
+  p.K = static_cast<int>(a.cols);
+  p.batch = z;
+  p.splits = static_cast<int>(std::max<int64_t>(1, splits));
+  p.b_shared = b.batch == 1 ? 1 : 0;
+  p.c_mode = static_cast<int>(mode);
+  p.beta_accumulate = accumulate ? 1 : 0;
+  p.alpha = static_cast<float>(alpha);
+  p.C = C.data_ptr();
+  p.ldc = C.dim() >= 2 ? C.stride(-2) : 0;
+  p.batch_stride_c = (C.dim() == 3) ? C.stride(0) : 0;
+  if (z > 1) TORCH_CHECK(C.dim() == 3 && C.size(0) == z, "C must be (Z, ., .) for batched A");
+  if (mode == bw::kStoreBF16T) {
+    TORCH_CHECK(C.size(-2) == p.N && C.size(-1) == p.M, "C^T must be (N, M)");
+  } else {
+    TORCH_CHECK(C.size(-2) == p.M && C.size(-1) == p.N, "C must be (M, N)");
+  }
+  TORCH_CHECK(p.splits == 1 || mode == bw::kAtomicF32, "split-K needs the atomic fp32 store");
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of dattri_llm_b200";
+  m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
+  bw::register_kernels(m);
+}

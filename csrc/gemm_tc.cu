@@ -1,0 +1,251 @@
+// Generic batched "TN" GEMM on the 5th-generation tensor cores (sm_100a):
+//
+//     C[z][m][n] (op)= alpha * sum_k A[z][m][k] * B[zb][n][k]
+//
+// A and B are bf16 and K-major (k contiguous), which is how every contraction of
+// the library is laid out (projection  x . P^T, per-sample outer products over
+// tokens, the test x train score, covariance Gram matrices).  One CTA owns one
+// 128 x BN output tile:
+//   warp 0 / lane 0   TMA producer: 128 x 64 A-tile and BN x 64 B-tile per stage
+//   warp 1 / lane 0   MMA issuer:   4 x tcgen05.mma (K=16 each) per stage, fp32 in TMEM
+//   warps 0-3         epilogue:     tcgen05.ld 32 lanes x 32 columns per warp and store
+// Split-K spreads the K loop over gridDim.z (the epilogue then accumulates with
+// fp32 atomics); rows/columns/K beyond the tensor are zero-filled by TMA.
+#include "gemm_tc.cuh"
+#include "tc_common.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace bw {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 128;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kTileA = BM * BK * 2;  // bytes
+  static constexpr int kTileB = BN * BK * 2;
+  static constexpr int kStages = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 4));
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kSmem = kStages * (kTileA + kTileB) + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::kStages * C::kTileA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::kStages * C::kTileB);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* done = empty + C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int z = blockIdx.z / p.splits;
+  const int split = blockIdx.z % p.splits;
+  const int zb = p.b_shared ? 0 : z;
+
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int per = (kblocks + p.splits - 1) / p.splits;
+  const int kb0 = split * per;
+  const int kb1 = min(kblocks, kb0 + per);
+  const int nk = max(0, kb1 - kb0);
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    int issued = 0;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1;
+      if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrWaitEmpty)) break;
+      mbar_arrive_expect_tx(&full[s], C::kTileA + C::kTileB);
+      const int kc = (kb0 + i) * BK;
+      tma_load_3d(sA + s * C::kTileA, &tmA, &full[s], kc, m0, z);
+      tma_load_3d(sB + s * C::kTileB, &tmB, &full[s], kc, n0, zb);
+      issued = i + 1;
+    }
+    // Never leave with a bulk copy still landing in this CTA's shared memory.
+    for (int i = max(0, issued - C::kStages); i < issued; ++i)
+      mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, p.err, kErrWaitFull);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1;
+      if (!mbar_wait(&full[s], ph, p.err, kErrWaitFull)) break;
+      tc_fence_after();
+      const uint64_t da = smem_desc_kmajor_sw128(sA + s * C::kTileA);
+      const uint64_t db = smem_desc_kmajor_sw128(sB + s * C::kTileB);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k)
+        tc_mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+      tc_commit(&empty[s]);
+    }
+    tc_commit(done);
+  }
+  __syncwarp();
+
+  // ---- epilogue: warp w owns accumulator rows [32w, 32w+32) ----
+  const bool ok = nk > 0 ? mbar_wait(done, 0, p.err, kErrWaitDone) : true;
+  __syncwarp();
+  tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  const bool row_ok = row < p.M;
+  const float alpha = p.alpha;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    if (nk > 0) {
+      tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = 0u;
+    }
+    if (!ok || !row_ok) continue;
+    const int nbase = n0 + c0;
+    if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
+      float* Cz = static_cast<float*>(p.C) + (long long)z * p.batch_stride_c +
+                  (long long)row * p.ldc;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) {
+          const float v = alpha * __uint_as_float(r[j]);
+          if (p.c_mode == kStoreF32)
+            Cz[n] = p.beta_accumulate ? Cz[n] + v : v;
+          else
+            atomicAdd(Cz + n, v);
+        }
+      }
+    } else if (p.c_mode == kStoreBF16) {
+      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(p.C) + (long long)z * p.batch_stride_c +
+                          (long long)row * p.ldc;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) Cz[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+      }
+    } else {  // kStoreBF16T: C^T[z][n][m]; consecutive lanes hit consecutive m (coalesced)
+      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(p.C) + (long long)z * p.batch_stride_c;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N)
+          Cz[(long long)n * p.ldc + row] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (fn == nullptr) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+template <int BN>
+void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
+               cudaStream_t stream) {
+  using C = Cfg<BN>;
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, BM);
+  CUtensorMap tb = make_tmap_kmajor_bf16(B, BN);
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(gemm_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         C::kSmem);
+    configured |= 1ull << dev;
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch * p.splits);
+  gemm_tn_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, tb, p);
+}
+
+}  // namespace
+
+CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows) {
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)op.cols, (cuuint64_t)op.rows, (cuuint64_t)op.batch};
+  cuuint64_t strides[2] = {(cuuint64_t)op.row_stride * 2, (cuuint64_t)op.batch_stride * 2};
+  if (op.batch <= 1) strides[1] = (cuuint64_t)op.row_stride * 2 * (cuuint64_t)op.rows;
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(op.ptr),
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string((int)r) +
+                             "): operand must be 16-byte aligned with 16-byte row strides");
+  return map;
+}
+
+int pick_bn(int N) {
+  if (N <= 16) return 16;
+  if (N <= 32) return 32;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  return 256;
+}
+
+void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
+                    cudaStream_t stream) {
+  if (p.splits < 1) p.splits = 1;
+  switch (bn) {
+    case 16: launch_bn<16>(A, B, p, stream); break;
+    case 32: launch_bn<32>(A, B, p, stream); break;
+    case 64: launch_bn<64>(A, B, p, stream); break;
+    case 128: launch_bn<128>(A, B, p, stream); break;
+    case 256: launch_bn<256>(A, B, p, stream); break;
+    default: throw std::runtime_error("gemm_tn: unsupported tile width");
+  }
+}
+
+}  // namespace bw

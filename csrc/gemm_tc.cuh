@@ -1,0 +1,46 @@
+// Host-side interface of the generic tcgen05 GEMM (gemm_tc.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace bw {
+
+// Epilogue modes.
+enum GemmStore : int {
+  kStoreF32 = 0,    // C (fp32) = alpha * AB^T            (or += with beta_accumulate)
+  kStoreBF16 = 1,   // C (bf16) = alpha * AB^T
+  kAtomicF32 = 2,   // C (fp32) += alpha * AB^T with atomics (split-K / cross-CTA sums)
+  kStoreBF16T = 3,  // C^T (bf16): element (m, n) lands at C[z][n * ldc + m]
+};
+
+// A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).
+struct GemmOperand {
+  const void* ptr;
+  long long rows;
+  long long cols;
+  long long row_stride;    // elements between consecutive rows (>= cols, multiple of 8)
+  long long batch;         // 1 for a single matrix
+  long long batch_stride;  // elements between consecutive matrices
+};
+
+struct GemmParams {
+  int M, N, K;
+  int batch;       // number of (A, C) batches; grid.z = batch * splits
+  int splits;      // split-K factor
+  int b_shared;    // 1: every batch uses B[0]
+  int c_mode;      // GemmStore
+  int beta_accumulate;
+  float alpha;
+  void* C;
+  long long ldc;
+  long long batch_stride_c;
+  int* err;
+};
+
+CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows);
+int pick_bn(int N);
+void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
+                    cudaStream_t stream);
+
+}  // namespace bw

@@ -1,0 +1,86 @@
+"""Python entry points of the generic tcgen05 GEMM (``csrc/gemm_tc.cu``)."""
+
+from __future__ import annotations
+
+import torch
+
+STORE_F32 = 0
+STORE_BF16 = 1
+STORE_ATOMIC_F32 = 2
+STORE_BF16_T = 3
+
+_SMS = 148
+
+
+def _k_aligned(x: torch.Tensor) -> torch.Tensor:
+    """Contiguous along K with K padded to a multiple of 8 (TMA's 16-byte rule)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    k = x.shape[-1]
+    if k % 8:
+        x = torch.nn.functional.pad(x, (0, 8 - k % 8))
+    elif x.dim() >= 2 and x.shape[-2] > 1 and x.stride(-2) % 8:
+        x = x.contiguous()
+    if x.data_ptr() % 16:
+        x = x.clone()
+    return x
+
+
+def gemm_tn(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    alpha: float = 1.0,
+    mode: int = STORE_F32,
+    splits: int = 1,
+    accumulate: bool = False,
+) -> torch.Tensor:
+    """``out (op)= alpha * a @ b^T`` on the tensor cores (bf16 in, fp32 accumulate).
+
+    *a* is ``(M, K)`` or ``(Z, M, K)``, *b* ``(N, K)`` (shared by every batch) or
+    ``(Z, N, K)``; both bf16.  *mode* selects the store: fp32, bf16, fp32 atomic
+    accumulation (``splits > 1`` spreads K over CTAs) or a transposed bf16 store
+    into ``out`` shaped ``(Z, N, M)``.
+    """
+    from dattri_llm_b200.ops import error_word, native
+
+    a = _k_aligned(a)
+    b = _k_aligned(b)
+    native().gemm_tn(a, b, out, float(alpha), int(mode), int(splits), bool(accumulate),
+                     error_word(a.device))
+    return out
+
+
+def auto_splits(m: int, n: int, k: int, batch: int = 1, bn: int = 128) -> int:
+    """Split-K factor that gives roughly one CTA per SM for a thin output."""
+    tiles = -(-m // 128) * -(-n // bn) * batch
+    kblocks = -(-k // 64)
+    if tiles >= _SMS or kblocks < 8:
+        return 1
+    return max(1, min(kblocks // 4, _SMS // tiles))
+
+
+def matmul_tn(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    out_dtype: torch.dtype = torch.float32,
+    alpha: float = 1.0,
+) -> torch.Tensor:
+    """``alpha * a @ b^T`` with a freshly allocated output (split-K when thin)."""
+    a2 = a if a.dim() >= 2 else a.unsqueeze(0)
+    lead = a2.shape[:-2]
+    batch = a2.shape[0] if a2.dim() == 3 else 1
+    m, n, k = a2.shape[-2], b.shape[-2], a2.shape[-1]
+    shape = (*lead, m, n)
+    bn = 16 if n <= 16 else 32 if n <= 32 else 64 if n <= 64 else 128 if n <= 128 else 256
+    splits = auto_splits(m, n, k, batch, bn)
+    if out_dtype == torch.float32 and splits > 1:
+        out = torch.zeros(shape, dtype=torch.float32, device=a.device)
+        gemm_tn(a2, b, out, alpha=alpha, mode=STORE_ATOMIC_F32, splits=splits)
+        return out
+    out = torch.empty(shape, dtype=out_dtype, device=a.device)
+    mode = STORE_BF16 if out_dtype == torch.bfloat16 else STORE_F32
+    gemm_tn(a2, b, out, alpha=alpha, mode=mode)
+    return out
