@@ -8,6 +8,7 @@
 #include <torch/extension.h>
 
 #include "gemm_tc.cuh"
+#include "ghost_gram.cuh"
 #include "kernels.cuh"
 
 namespace {
@@ -84,10 +85,44 @@ void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t s
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
+// out[i][j] += sum over token pairs of (a1 . a2)(g1 . g2); factors flattened to rows.
+void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t S2, Tensor out,
+                Tensor err) {
+  const c10::cuda::CUDAGuard guard(a1.device());
+  check_err(err);
+  auto oa1 = operand(a1, "a1");
+  auto oa2 = operand(a2, "a2");
+  auto og1 = operand(g1, "g1");
+  auto og2 = operand(g2, "g2");
+  TORCH_CHECK(a1.dim() == 2 && a2.dim() == 2 && g1.dim() == 2 && g2.dim() == 2,
+              "ghost_gram takes flattened (rows, width) factors");
+  TORCH_CHECK(oa1.cols == oa2.cols && og1.cols == og2.cols, "factor widths disagree");
+  TORCH_CHECK(oa1.rows == og1.rows && oa2.rows == og2.rows, "factor row counts disagree");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.dim() == 2 && out.stride(1) == 1,
+              "out must be a (B1, B2) fp32 matrix");
+  bw::GhostParams p{};
+  p.M = (int)oa1.rows;
+  p.N = (int)oa2.rows;
+  p.K = (int)oa1.cols;
+  p.D = (int)og1.cols;
+  p.S1 = (int)S1;
+  p.S2 = (int)S2;
+  p.B1 = (int)(p.M / p.S1);
+  p.B2 = (int)(p.N / p.S2);
+  TORCH_CHECK(p.B1 * p.S1 == p.M && p.B2 * p.S2 == p.N, "rows must be B*S");
+  TORCH_CHECK(out.size(0) == p.B1 && out.size(1) == p.B2, "out must be (B1, B2)");
+  p.out = out.data_ptr<float>();
+  p.ldo = out.stride(0);
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::ghost_gram_launch(oa1, oa2, og1, og2, p, at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
+  m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   bw::register_kernels(m);
 }

@@ -1,0 +1,193 @@
+// Fused "ghost" cross-gram of factorized per-sample gradients (sm_100a):
+//
+//   out[i][j] += sum_{s in sample i, t in sample j} (a1[s] . a2[t]) * (g1[s] . g2[t])
+//
+// which equals <dW1_i, dW2_j> for dW = g^T a.  Rows r = i*S1 + s of the flattened
+// side-1 factors, columns c = j*S2 + t of side 2.  One CTA owns a 128 x 128 tile of
+// the (B1*S1) x (B2*S2) token-pair grid and keeps BOTH Gram tiles in TMEM:
+//   columns [0,128)   Ka = A1_tile . A2_tile^T   (K loop over activation features)
+//   columns [128,256) Kg = G1_tile . G2_tile^T   (K loop over gradient features)
+// One TMA/mbarrier pipeline streams the activation blocks, then the gradient
+// blocks; the MMA thread switches accumulator at the boundary.  The epilogue
+// multiplies the two tiles elementwise and reduces them to (i, j) partial sums:
+// first along its row within each column segment, then across the lanes of a
+// warp when they share a sample, into shared-memory bins, finally one global
+// fp32 atomic per (i, j) bin.  The (B1 S1) x (B2 S2) products never reach HBM.
+#include "ghost_gram.cuh"
+#include "tc_common.cuh"
+
+namespace bw {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 64;
+constexpr int kStages = 4;
+constexpr int kTile = 128 * BK * 2;  // both operands have 128-row tiles
+constexpr int kBinsMax = 4096;       // fp32 bins in the reused pipeline smem
+constexpr int kSmem = kStages * 2 * kTile + 1024 + 256;
+
+__global__ void __launch_bounds__(128, 1)
+    ghost_gram_kernel(const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tA2,
+                      const __grid_constant__ CUtensorMap tG1, const __grid_constant__ CUtensorMap tG2,
+                      GhostParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+  uint8_t* sX = smem;                       // side-1 tiles
+  uint8_t* sY = smem + kStages * kTile;     // side-2 tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTile);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  float* bins = reinterpret_cast<float*>(smem);  // reused after the main loop
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int nka = (p.K + BK - 1) / BK;
+  const int nkg = (p.D + BK - 1) / BK;
+  const int nk = nka + nkg;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tA1);
+    tma_prefetch_desc(&tA2);
+    tma_prefetch_desc(&tG1);
+    tma_prefetch_desc(&tG2);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    int issued = 0;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&empty[s], ((i / kStages) & 1) ^ 1, p.err, kErrWaitEmpty)) break;
+      mbar_arrive_expect_tx(&full[s], 2 * kTile);
+      const bool act = i < nka;
+      const int kc = (act ? i : i - nka) * BK;
+      tma_load_3d(sX + s * kTile, act ? &tA1 : &tG1, &full[s], kc, m0, 0);
+      tma_load_3d(sY + s * kTile, act ? &tA2 : &tG2, &full[s], kc, n0, 0);
+      issued = i + 1;
+    }
+    for (int i = max(0, issued - kStages); i < issued; ++i)
+      mbar_wait(&full[i % kStages], (i / kStages) & 1, p.err, kErrWaitFull);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(&full[s], (i / kStages) & 1, p.err, kErrWaitFull)) break;
+      tc_fence_after();
+      const bool act = i < nka;
+      const int ii = act ? i : i - nka;
+      const uint32_t acc = tmem + (act ? 0u : 128u);
+      const uint64_t dx = smem_desc_kmajor_sw128(sX + s * kTile);
+      const uint64_t dy = smem_desc_kmajor_sw128(sY + s * kTile);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) tc_mma_f16(acc, dx + 2 * k, dy + 2 * k, idesc, (ii | k) != 0);
+      tc_commit(&empty[s]);
+    }
+    tc_commit(done);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(done, 0, p.err, kErrWaitDone);
+  __syncwarp();
+  tc_fence_after();
+  // Every stage has been consumed (done fired after the last commit), so the
+  // pipeline buffers can be reused as (i, j) bins.
+  const int row = m0 + warp * 32 + lane;
+  const int i_first = m0 / p.S1;
+  const int i_last = min(p.B1 - 1, (min(m0 + BM, p.M) - 1) / p.S1);
+  const int j_first = n0 / p.S2;
+  const int j_last = min(p.B2 - 1, (min(n0 + BN, p.N) - 1) / p.S2);
+  const int ni = i_last - i_first + 1;
+  const int nj = j_last - j_first + 1;
+  const bool use_bins = ni * nj <= kBinsMax;
+  __syncthreads();  // the producer has drained its copies before bins reuse the buffers
+  if (use_bins)
+    for (int e = threadIdx.x; e < ni * nj; e += blockDim.x) bins[e] = 0.f;
+  __syncthreads();
+  const int my_i = row / p.S1;
+  const bool row_ok = ok && row < p.M;
+  const bool warp_uniform_i = __all_sync(0xffffffffu, (m0 + warp * 32) / p.S1 == my_i) &&
+                              __all_sync(0xffffffffu, row < p.M);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t ra[32], rg[32];
+    tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, ra);
+    tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + 128u + (uint32_t)c0, rg);
+    tmem_ld_wait();
+    const int cbase = n0 + c0;
+    if (cbase >= p.N) continue;  // warp-uniform
+    // Walk the 32 columns (static register indexing); a column-sample boundary is
+    // warp-uniform, so each segment is flushed by the whole warp together.
+    auto flush = [&](float v, int j) {
+      if (!row_ok) v = 0.f;
+      if (warp_uniform_i) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane != 0) return;
+      }
+      if (!row_ok || my_i >= p.B1 || j >= p.B2) return;
+      if (use_bins)
+        atomicAdd(&bins[(my_i - i_first) * nj + (j - j_first)], v);
+      else
+        atomicAdd(p.out + (long long)my_i * p.ldo + j, v);
+    };
+    int cur_j = cbase / p.S2;
+    int next_b = (cur_j + 1) * p.S2;
+    float v = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 32; ++cc) {
+      if (cbase + cc >= next_b) {
+        flush(v, cur_j);
+        v = 0.f;
+        ++cur_j;
+        next_b += p.S2;
+      }
+      v += __uint_as_float(ra[cc]) * __uint_as_float(rg[cc]);
+    }
+    flush(v, cur_j);
+  }
+  __syncthreads();
+  if (use_bins && ok) {
+    for (int e = threadIdx.x; e < ni * nj; e += blockDim.x) {
+      const int i = i_first + e / nj, j = j_first + e % nj;
+      atomicAdd(p.out + (long long)i * p.ldo + j, bins[e]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+}  // namespace
+
+void ghost_gram_launch(const GemmOperand& a1, const GemmOperand& a2, const GemmOperand& g1,
+                       const GemmOperand& g2, GhostParams p, cudaStream_t stream) {
+  CUtensorMap t_a1 = make_tmap_kmajor_bf16(a1, BM);
+  CUtensorMap t_a2 = make_tmap_kmajor_bf16(a2, BN);
+  CUtensorMap t_g1 = make_tmap_kmajor_bf16(g1, BM);
+  CUtensorMap t_g2 = make_tmap_kmajor_bf16(g2, BN);
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(ghost_gram_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    configured |= 1ull << dev;
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, 1);
+  ghost_gram_kernel<<<grid, 128, kSmem, stream>>>(t_a1, t_a2, t_g1, t_g2, p);
+}
+
+}  // namespace bw

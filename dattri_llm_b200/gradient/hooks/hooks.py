@@ -1,0 +1,489 @@
+"""Forward/backward capture hooks on individual layers.
+
+``register_linear_io_hooks`` puts a forward hook (input activation) and a full
+backward hook (output gradient) on each selected layer and buffers what they
+see per device.  Forwards are matched to backwards LIFO per device (autograd
+runs a device's graph in reverse creation order), which keeps repeated
+invocations (weight tying, unrolled loops) and DataParallel replica threads
+apart; a forward left unmatched at the end of the backward (activation
+checkpointing's first pass) is discarded by the manager.  Parity: reference
+``dattri_llm/gradient/hooks/hooks.py:81-866``.
+
+Projected capture (``projection_kwargs``): for a linear layer under the
+``logra`` style the activation is projected in the forward hook, so only
+``a P_a`` is held until the backward.  On an sm_100 device with bf16 factors:
+
+* the projection is a tcgen05 GEMM against the cached ``P^T``;
+* layers reading the *same* input tensor with the same matrix (q/k/v, gate/up)
+  share one activation projection per step;
+* when the layer will be materialized (``capture_style`` ``"materialized"`` or
+  ``"auto"`` with ``T >= k_a k_g / (k_a + k_g)``) the projected factors are
+  written token-major ``(B, k, T)`` straight from the GEMM epilogue, so the
+  per-sample ``g_p^T a_p`` is a second tcgen05 GEMM with no transpose copy.
+"""
+
+from __future__ import annotations
+
+import threading
+import warnings
+import weakref
+from collections.abc import Callable
+
+import torch
+from torch import nn
+
+from dattri_llm_b200.gradient import ops
+from dattri_llm_b200.gradient.ops import (
+    canonical_class_name,
+    dtypes,
+    extract_module_kwargs,
+    is_embedding,
+    is_linear,
+    to_3d,
+)
+
+try:
+    from transformers.pytorch_utils import Conv1D as HF_Conv1D
+except ImportError:  # pragma: no cover - transformers is optional
+    HF_Conv1D = None
+
+_LINEAR_IO_TYPES: tuple[type, ...] = (
+    nn.Embedding, nn.EmbeddingBag, nn.LayerNorm, nn.GroupNorm, nn.InstanceNorm1d,
+    nn.InstanceNorm2d, nn.InstanceNorm3d, nn.Linear, nn.Bilinear, nn.Conv1d, nn.Conv2d,
+    nn.Conv3d, nn.ConvTranspose1d, nn.ConvTranspose2d, nn.ConvTranspose3d,
+) + ((HF_Conv1D,) if HF_Conv1D is not None else ()) + ((nn.RMSNorm,) if hasattr(nn, "RMSNorm") else ())
+
+#: One layer's ``linear_io`` capture buffer (a dict; keys documented in _new_buffer).
+LayerBuffer = dict
+#: One layer's ``param_grad`` buffer: ``{param_name: tensor | None}``.
+ParamGradBuffer = dict
+
+
+def is_linear_io_capable(module: nn.Module) -> bool:
+    """Whether *module*'s per-sample gradient factorizes as an outer product (by type)."""
+    return isinstance(module, _LINEAR_IO_TYPES)
+
+
+def has_trainable_params(module: nn.Module) -> bool:
+    """Whether *module* owns (or proxies) a parameter that requires grad."""
+    proxied = getattr(module, "proxied_parameters", None)
+    if proxied is not None:
+        return any(p.requires_grad for p in proxied())
+    return any(p.requires_grad for _, p in module.named_parameters(recurse=False))
+
+
+def _flatten_tokens(t: torch.Tensor, layer_type: str) -> torch.Tensor:
+    if t.ndim > 3 and is_linear(layer_type):
+        return t.reshape(t.shape[0], -1, t.shape[-1])
+    return t
+
+
+def _new_buffer() -> LayerBuffer:
+    return {
+        "activation": None,        # last raw activation seen (raw capture)
+        "grad_output": None,       # last raw output gradient seen (raw capture)
+        "_act_parts": [],          # [(device, a or a_p)]
+        "_grad_parts": [],         # [(device, g or g_p)]
+        "_proj_parts": [],         # [(device, dense per-sample block)]
+        "_proj_kw": None,          # resolved projection config of the layer
+        "_proj_matrix": {},        # {"a"/"g": ProjectionMatrix}
+        "_capture_style": "factorized",
+        "_pending": {},            # {device: [forward entries awaiting a backward]}
+        "_fwd_fires": 0,           # grad-enabled forwards this step
+        "_pair_pos": [],           # [(device, invocation position)] per matched pair
+        "_lock": threading.Lock(),
+    }
+
+
+class _Projected:
+    """A projected activation waiting for its backward; ``token_major`` marks the
+    ``(B, k, T)`` layout written for the fused materialize path."""
+
+    __slots__ = ("a", "token_major")
+
+    def __init__(self, a: torch.Tensor, token_major: bool) -> None:
+        self.a, self.token_major = a, token_major
+
+
+class _StepShare:
+    """Per-step cache of activation projections shared by layers that read the same
+    input tensor (q/k/v, gate/up).  Cleared by the manager at every step end."""
+
+    def __init__(self) -> None:
+        self._store: dict = {}
+        self._lock = threading.Lock()
+
+    def get(self, key):
+        with self._lock:
+            return self._store.get(key)
+
+    def put(self, key, value) -> None:
+        with self._lock:
+            self._store[key] = value
+
+    def clear(self) -> None:
+        with self._lock:
+            self._store.clear()
+
+
+def register_linear_io_hooks(
+    model: nn.Module,
+    layer_names: set[str] | None = None,
+    on_layer_forward: Callable | None = None,
+    on_layer_backward: Callable | None = None,
+    type_overrides: dict[str, str] | None = None,
+    kwargs_overrides: dict[str, dict] | None = None,
+    projection_kwargs: dict[str, dict] | None = None,
+    capture_style: str = "factorized",
+    projector: ops.DattriProjector | None = None,
+    offload_to_cpu: bool = False,
+    preconditioner=None,
+    include_frozen: bool = False,
+    routed=None,
+    step_share: _StepShare | None = None,
+) -> tuple[dict[str, LayerBuffer], list]:
+    """Register forward and backward hooks on linear-family layers.
+
+    Returns ``(buffers, handles)``: ``{layer_name: LayerBuffer}`` and the hook handles.
+    Callbacks receive ``(layer_name, tensor, layer_type, module_kwargs)``; for a
+    pre-projected layer the tensor is the projected factor and the type ``"nn.Linear"``.
+    """
+    root = getattr(model, "module", model)
+    buffers: dict[str, LayerBuffer] = {}
+    handles: list = []
+    share = step_share
+    for name, module in root.named_modules():
+        if (type_overrides is None or name not in type_overrides) and not is_linear_io_capable(module):
+            continue
+        if layer_names is not None and name not in layer_names:
+            continue
+        if not include_frozen and not has_trainable_params(module):
+            continue
+        buf = buffers[name] = _new_buffer()
+        layer_type = (type_overrides or {}).get(name) or canonical_class_name(module)
+        buf["_class_name"] = layer_type
+        if kwargs_overrides is not None and name in kwargs_overrides:
+            buf["_module_kwargs"] = dict(kwargs_overrides[name])
+        else:
+            buf["_module_kwargs"] = extract_module_kwargs(module, layer_type)
+        if projection_kwargs is not None:
+            buf["_proj_kw"] = projection_kwargs.get(name, projection_kwargs.get("__default__"))
+        buf["_capture_style"] = capture_style
+        handles.append(module.register_forward_hook(
+            _forward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
+                          on_layer_forward)))
+        handles.append(module.register_full_backward_hook(
+            _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed,
+                           on_layer_backward)))
+    return buffers, handles
+
+
+def _device_index(t: torch.Tensor) -> int:
+    return t.device.index if t.is_cuda else 0
+
+
+def _forward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback):
+    def hook(_module, inp, _out):
+        if not torch.is_grad_enabled():
+            return  # no backward will follow (eval / log-prob pass)
+        x = inp[0]
+        a = x.detach()
+        dev = _device_index(x)
+        buf = buffers[name]
+        if routed is not None and name in routed.layers:
+            layout = routed.push(name, a, dev)
+            if layout is not None:
+                a = layout.regroup(a)
+        a = _flatten_tokens(a, buf["_class_name"])
+        emit, emit_type, emit_kw = a, buf["_class_name"], buf["_module_kwargs"]
+        if _raw_capture(buf, preconditioner):
+            if offload:
+                a = a.cpu()
+            with buf["_lock"]:
+                buf["_pending"].setdefault(dev, []).append(len(buf["_act_parts"]))
+                buf["_act_parts"].append((dev, a))
+                buf["_fwd_fires"] += 1
+            buf["activation"] = a
+            emit = a
+        else:
+            entry = a
+            if _preprojects_activation(buf["_class_name"], _style(buf)):
+                entry = _project_activation(buf, a, projector, share, x)
+                emit = entry.a.transpose(1, 2) if entry.token_major else entry.a
+                emit_type, emit_kw = "nn.Linear", None
+            with buf["_lock"]:
+                buf["_pending"].setdefault(dev, []).append(entry)
+                buf["_fwd_fires"] += 1
+        if callback is not None:
+            callback(name, emit, emit_type, emit_kw)
+
+    return hook
+
+
+def _backward_hook(name, buffers, projector, preconditioner, offload, routed, callback):
+    def hook(_module, _grad_input, grad_output):
+        g = grad_output[0].detach()
+        dev = _device_index(grad_output[0])
+        buf = buffers[name]
+        if routed is not None and name in routed.layers:
+            layout = routed.pop(name, dev)
+            if layout is not None:
+                g = layout.regroup(g)
+        g = _flatten_tokens(g, buf["_class_name"])
+        emit, emit_type, emit_kw = g, buf["_class_name"], buf["_module_kwargs"]
+        if _raw_capture(buf, preconditioner):
+            if offload:
+                g = g.cpu()
+            with buf["_lock"]:
+                stack = buf["_pending"].get(dev)
+                if not stack:
+                    _warn_orphan_backward(name)
+                    return
+                stack.pop()
+                buf["_pair_pos"].append((dev, len(stack)))
+                buf["_grad_parts"].append((dev, g))
+            buf["grad_output"] = g
+            emit = g
+        else:
+            matched, g_p = _capture_projected(buf, g, dev, projector, offload, preconditioner, name)
+            if not matched:
+                _warn_orphan_backward(name)
+                return
+            if g_p is not None:
+                emit, emit_type, emit_kw = g_p, "nn.Linear", None
+        if callback is not None:
+            callback(name, emit, emit_type, emit_kw)
+
+    return hook
+
+
+def _warn_orphan_backward(layer_name: str) -> None:
+    warnings.warn(
+        f"Discarding a backward fire on layer '{layer_name}' with no matching forward capture "
+        "(e.g. a repeated backward over a retained graph); this is not a normal forward+backward step.",
+        stacklevel=3,
+    )
+
+
+def _projection_matrix(buf: LayerBuffer, side: str, x: torch.Tensor, projector) -> ops.ProjectionMatrix:
+    """The layer's projection for *side* ``"a"`` / ``"g"``, resolved once per dtype/device."""
+    (x,) = dtypes.align(x)
+    pm = buf["_proj_matrix"].get(side)
+    if pm is not None and pm.matches(x):
+        return pm
+    kw = {k: v for k, v in buf["_proj_kw"].items() if k != "style"}
+    seed = kw.pop("proj_seed", 0)
+    mk = buf["_module_kwargs"]
+    with_bias = side == "a" and mk is not None and mk.get("has_bias", False)
+    pm = ops.DattriProjector.coerce(projector).resolve(
+        x.shape[-1], proj_seed=seed + 1 if side == "a" else seed, include_bias=with_bias,
+        device=x.device, dtype=x.dtype, **kw)
+    buf["_proj_matrix"][side] = pm
+    return pm
+
+
+def _token_major_ok(pm: ops.ProjectionMatrix, x: torch.Tensor) -> bool:
+    """The fused token-major path: native bf16 on sm_100, bias-free, 8-aligned widths."""
+    from dattri_llm_b200 import ops as native_ops
+
+    return (pm.matrix_t is not None and pm.bias_row is None and x.dtype == torch.bfloat16
+            and x.ndim == 3 and x.shape[1] % 8 == 0 and x.shape[-1] % 8 == 0
+            and pm.proj_dim % 8 == 0 and native_ops.use_native(x))
+
+
+def project_token_major(pm: ops.ProjectionMatrix, x: torch.Tensor) -> torch.Tensor:
+    """``(x P)`` of ``x (B, T, d)`` written token-major: a ``(B, k, T)`` view whose rows
+    are contiguous over tokens (the tcgen05 epilogue stores the transpose directly)."""
+    from dattri_llm_b200 import ops as native_ops
+
+    b, t, _ = x.shape
+    flat = x.reshape(b * t, x.shape[-1])
+    out_t = torch.empty(pm.proj_dim, b * t, dtype=torch.bfloat16, device=x.device)
+    native_ops.gemm_tn(flat, pm.matrix_t, out_t, mode=native_ops.STORE_BF16_T)
+    return out_t.view(pm.proj_dim, b, t).permute(1, 0, 2)
+
+
+def _project_activation(buf, a, projector, share, source) -> _Projected:
+    a3 = to_3d(dtypes.align(a)[0])
+    pm = _projection_matrix(buf, "a", a3, projector)
+    seq_len = a3.shape[1]
+    k = pm.proj_dim
+    token_major = (ops.should_materialize(buf["_capture_style"], seq_len, k, k)
+                   and _token_major_ok(pm, a3))
+    key = None
+    if share is not None and a3.is_cuda:
+        # id() alone could be recycled by a later tensor once the input is freed (frozen
+        # layers do not save it for backward); the weak reference proves it is the same one.
+        key = (id(source), source._version, source.data_ptr(), tuple(source.shape), id(pm.matrix),
+               token_major)
+        hit = share.get(key)
+        if hit is not None and hit[0]() is source:
+            return hit[1]
+    entry = _Projected(project_token_major(pm, a3) if token_major else pm(a3), token_major)
+    if key is not None:
+        share.put(key, (weakref.ref(source), entry))
+    return entry
+
+
+def _preprojects_activation(layer_type: str, style: str | None) -> bool:
+    return ops.is_linear(layer_type) and style == "logra"
+
+
+def _preconditioning(preconditioner) -> bool:
+    return preconditioner is not None and preconditioner.enabled
+
+
+def _style(buf: LayerBuffer) -> str | None:
+    return None if buf["_proj_kw"] is None else buf["_proj_kw"].get("style", "logra")
+
+
+def _raw_capture(buf: LayerBuffer, preconditioner) -> bool:
+    return (buf["_proj_kw"] is None and buf["_capture_style"] == "factorized"
+            and not _preconditioning(preconditioner))
+
+
+def _keep_factors(buf: LayerBuffer, seq_len: int, k_a: int, k_g: int) -> bool:
+    if buf["_act_parts"]:
+        return True
+    if buf["_proj_parts"]:
+        return False
+    return not ops.should_materialize(buf["_capture_style"], seq_len, k_a, k_g)
+
+
+def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name):
+    """Pair *g* with its forward and store the projected / materialized / preconditioned
+    capture.  Returns ``(matched, projected g to hand the callbacks or None)``."""
+    with buf["_lock"]:
+        stack = buf["_pending"].get(dev)
+        entry = stack.pop() if stack else None
+        pos = (dev, len(stack)) if entry is not None else None
+    if entry is None:
+        return False, None
+    proj_kw = buf["_proj_kw"]
+    kw = dict(proj_kw or {})
+    style = kw.pop("style", "logra") if proj_kw is not None else None
+    pre = preconditioner if _preconditioning(preconditioner) else None
+    layer_type, mk = buf["_class_name"], buf["_module_kwargs"]
+
+    def keep_factors(a_f, g_f):
+        if offload:
+            a_f, g_f = a_f.cpu(), g_f.cpu()
+        with buf["_lock"]:
+            buf["_act_parts"].append((dev, a_f))
+            buf["_grad_parts"].append((dev, g_f))
+            buf["_pair_pos"].append(pos)
+
+    def keep_dense(mat):
+        if offload:
+            mat = mat.cpu()
+        with buf["_lock"]:
+            buf["_proj_parts"].append((dev, mat))
+            buf["_pair_pos"].append(pos)
+
+    if style == "logra":
+        if isinstance(entry, _Projected):
+            g3 = to_3d(dtypes.align(g)[0])
+            pm_g = _projection_matrix(buf, "g", g3, projector)
+            if entry.token_major and _token_major_ok(pm_g, g3) and not buf["_act_parts"]:
+                from dattri_llm_b200 import ops as native_ops
+
+                g_pt = project_token_major(pm_g, g3)
+                b = g_pt.shape[0]
+                dense = torch.empty(b, pm_g.proj_dim, entry.a.shape[1], dtype=g3.dtype, device=g3.device)
+                native_ops.gemm_tn(g_pt, entry.a, dense, mode=native_ops.STORE_BF16)
+                keep_dense(dense.reshape(b, -1))
+                return True, g_pt.transpose(1, 2)
+            a_p = entry.a.transpose(1, 2) if entry.token_major else entry.a
+            g_p = pm_g(g3)
+            emit = g_p
+        else:
+            a = entry
+            if a.ndim == 1 and is_embedding(layer_type):
+                a, g = a.unsqueeze(0), g.unsqueeze(0)
+            a_p, g_p = ops.project_factors(a, g, layer_type, projector, mk, **kw)
+            emit = None
+        seq_len = a_p.shape[1] if a_p.ndim >= 3 else 1
+        if _keep_factors(buf, seq_len, a_p.shape[-1], g_p.shape[-1]):
+            keep_factors(a_p, g_p)
+        else:
+            keep_dense(ops.materialize_factors(a_p, g_p, "nn.Linear"))
+        return True, emit
+    a = entry
+    if a.ndim == 1 and is_embedding(layer_type):
+        a, g = a.unsqueeze(0), g.unsqueeze(0)
+    if style == "mask":
+        mat = ops.mask_factors(a, g, layer_type, projector, mk, **kw)
+        keep_dense(pre(layer_name, mat, proj_kw) if pre is not None else mat)
+        return True, None
+    if style == "dense":
+        if pre is not None:
+            include_bias = bool(kw.pop("include_bias", True))
+            mat = ops.materialize_factors(a, g, layer_type, mk, include_bias)
+            mat = ops.apply_projection(projector, pre(layer_name, mat, proj_kw), **kw)
+        else:
+            mat = ops.project_materialized_factors(a, g, layer_type, projector, mk, **kw)
+        keep_dense(mat)
+        return True, None
+    if pre is not None:
+        keep_dense(pre(layer_name, ops.materialize_factors(a, g, layer_type, mk), None))
+        return True, None
+    seq_len = a.shape[1] if a.ndim >= 3 else 1
+    if _keep_factors(buf, seq_len, a.shape[-1] + 1, g.shape[-1]):
+        keep_factors(a, g)
+    else:
+        keep_dense(ops.materialize_factors(a, g, layer_type, mk))
+    return True, None
+
+
+def remove_hooks(handles: list) -> None:
+    """Remove every handle and clear the list."""
+    for h in handles:
+        h.remove()
+    handles.clear()
+
+
+def register_param_grad_hooks(model: nn.Module, layer_names: set[str] | None = None,
+                              on_param_grad: Callable | None = None, offload_to_cpu: bool = False):
+    """Tensor hooks on every trainable parameter of the selected modules: the batch-level
+    gradient lands in ``buffers[layer][param]``.  Returns ``(buffers, handles)``."""
+    root = getattr(model, "module", model)
+    buffers: dict[str, ParamGradBuffer] = {}
+    handles: list = []
+    for lname, module in root.named_modules():
+        if layer_names is not None and lname not in layer_names:
+            continue
+        trainable = [(pn, p) for pn, p in module.named_parameters(recurse=False) if p.requires_grad]
+        if not trainable:
+            continue
+        buffers[lname] = {pn: None for pn, _ in trainable}
+        for pn, p in trainable:
+            def hook(grad, ln=lname, pn=pn):
+                g = grad.detach()
+                if offload_to_cpu:
+                    g = g.cpu()
+                buffers[ln][pn] = g
+                if on_param_grad is not None:
+                    on_param_grad(ln, pn, g)
+            handles.append(p.register_hook(hook))
+    return buffers, handles
+
+
+def register_linear_param_hooks(model: nn.Module, layer_names: set[str] | None = None,
+                                on_linear_param_grad: Callable | None = None):
+    """Post-accumulate-grad hooks on the trainable parameters of linear-IO layers (the
+    per-step barrier that weight gradients have been written).  Returns ``(count, handles)``."""
+    root = getattr(model, "module", model)
+    count, handles = 0, []
+    for name, module in root.named_modules():
+        if not is_linear_io_capable(module) or (layer_names is not None and name not in layer_names):
+            continue
+        for pn, p in module.named_parameters(recurse=False):
+            if not p.requires_grad:
+                continue
+            count += 1
+
+            def hook(param, ln=name, pn=pn):
+                if on_linear_param_grad is not None:
+                    on_linear_param_grad(ln, pn, param.grad.detach() if param.grad is not None else None)
+            handles.append(p.register_post_accumulate_grad_hook(hook))
+    return count, handles

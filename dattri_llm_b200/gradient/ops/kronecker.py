@@ -1,0 +1,378 @@
+"""K-FAC / EK-FAC factors, inverses, preconditioning and streaming accumulators.
+
+Parity: reference ``dattri_llm/gradient/ops/kronecker.py:33-748`` (same
+definitions: ``A = E[a a^T]``, ``G = E[g g^T]`` over gradient-carrying token rows,
+``F = E[dW dW^T]``; eigenbasis rotation ``U_G^T dW U_A``; damped inverses).
+
+B200 differences: the covariance updates ``A += a^T a`` run as split-K tcgen05
+Gram GEMMs that accumulate straight into the fp32 running sums (no bf16 round
+trip of the update, no extra add kernel); gradient-free rows are masked on the
+device instead of boolean-indexed, so an update never synchronizes the host; and
+the row count is a device tensor until :meth:`result` reads it.  The cross-rank
+reduction can go through the fused NVLink kernel in
+:mod:`dattri_llm_b200.parallel.covariance`.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterable
+from dataclasses import dataclass, field
+
+import torch
+
+from dattri_llm_b200.gradient.ops import dtypes
+from dattri_llm_b200.gradient.ops.dot import cross_gram
+from dattri_llm_b200.gradient.ops.materialize import materialize, materialize_factors
+from dattri_llm_b200.gradient.ops.preprocess import preprocess_factors
+from dattri_llm_b200.gradient.ops.types import is_conv, is_conv_transpose, is_embedding, is_norm
+from dattri_llm_b200.utils.distributed import all_reduce_sum
+
+
+def _flatten_for_kfac(a: torch.Tensor, g: torch.Tensor, layer_type: str):
+    if is_norm(layer_type):
+        raise NotImplementedError("K-FAC is not defined for normalization layers")
+    if is_embedding(layer_type):
+        raise NotImplementedError("K-FAC is not defined for embedding layers")
+    a, g = dtypes.align(a, g)
+    if a.ndim == 4:  # grouped: (G, N, w) per group
+        groups = a.shape[2]
+        return (a.permute(2, 0, 1, 3).reshape(groups, -1, a.shape[-1]),
+                g.permute(2, 0, 1, 3).reshape(groups, -1, g.shape[-1]))
+    return a.reshape(-1, a.shape[-1]), g.reshape(-1, g.shape[-1])
+
+
+def _right_multiply(x: torch.Tensor, matrix: torch.Tensor) -> torch.Tensor:
+    if matrix.ndim == 3:
+        return torch.einsum("...gk,gkj->...gj", x, matrix)
+    return x @ matrix
+
+
+def _row_mask(a_f, g_f, layer_type):
+    """(masked a, g, number of gradient-carrying rows as a 0-d tensor)."""
+    if is_conv(layer_type) or is_conv_transpose(layer_type):
+        return a_f, g_f, torch.tensor(a_f.shape[-2], device=a_f.device)
+    keep = (g_f != 0).any(dim=-1)
+    a_f = a_f * keep.unsqueeze(-1).to(a_f.dtype)
+    return a_f, g_f, keep.sum(dim=-1).reshape(-1)[0] if keep.ndim > 1 else keep.sum()
+
+
+def gram_accumulate(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """``out += x^T x`` (fp32 *out*) for ``x (N, w)`` or grouped ``(G, N, w)``.
+
+    On sm_100 with bf16 rows this is a split-K tcgen05 GEMM whose epilogue adds
+    into *out* with fp32 atomics.
+    """
+    from dattri_llm_b200 import ops as native_ops
+
+    if native_ops.use_native(x, out) and x.dtype == torch.bfloat16 and x.ndim == 2:
+        xt = x.t().contiguous()  # (w, N): the contraction axis contiguous
+        w, n = xt.shape
+        splits = native_ops.gemm.auto_splits(w, w, n, 1, 128 if w > 64 else 64)
+        native_ops.gemm_tn(xt, xt, out, mode=native_ops.STORE_ATOMIC_F32, splits=splits)
+        return out
+    out += (x.transpose(-1, -2) @ x).float()
+    return out
+
+
+def kfac_factors(a, g, layer_type: str, module_kwargs: dict | None = None,
+                 include_bias: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(A, G)`` K-FAC covariances of one batch (fp32, gradient-free rows dropped).
+
+    Raises:
+        ValueError: if every row carries a zero gradient.
+    """
+    a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
+    a_f, g_f = _flatten_for_kfac(a, g, layer_type)
+    a_f, g_f, n = _row_mask(a_f, g_f, layer_type)
+    n = int(n)
+    if n == 0:
+        raise ValueError("K-FAC factors are undefined: every token row carries a zero gradient.")
+    lead = a_f.shape[:-2]
+    A = torch.zeros(*lead, a_f.shape[-1], a_f.shape[-1], device=a_f.device)
+    G = torch.zeros(*lead, g_f.shape[-1], g_f.shape[-1], device=g_f.device)
+    return gram_accumulate(a_f, A) / n, gram_accumulate(g_f, G) / n
+
+
+def fim_factors(a, g, layer_type: str, module_kwargs: dict | None = None,
+                include_bias: bool = True) -> torch.Tensor:
+    """``(d, d)`` empirical Fisher of one batch's per-sample gradients."""
+    grad = materialize_factors(a, g, layer_type, module_kwargs, include_bias)
+    return (grad.T @ grad).float() / grad.shape[0]
+
+
+def sym_inverse(matrix: torch.Tensor, damping: float = 0.0) -> torch.Tensor:
+    """Damped symmetric inverse ``(M + damping I)^-1`` through ``eigh``."""
+    evals, evecs = torch.linalg.eigh(matrix.float())
+    return (evecs / (evals + damping).unsqueeze(-2)) @ evecs.transpose(-1, -2)
+
+
+def dense_inverse(matrix: torch.Tensor, damping: float = 0.0) -> torch.Tensor:
+    """Damped inverse through Cholesky, falling back to :func:`sym_inverse`."""
+    m = matrix.float()
+    damped = m + damping * torch.eye(m.shape[-1], device=m.device, dtype=m.dtype)
+    try:
+        return torch.cholesky_inverse(torch.linalg.cholesky(damped))
+    except RuntimeError:
+        return sym_inverse(matrix, damping)
+
+
+def kfac_cross_factors(a1, g1, a2, g2, layer_type: str, A_inv, G_inv, module_kwargs1=None,
+                       module_kwargs2=None, include_bias: bool = True) -> torch.Tensor:
+    """K-FAC preconditioned cross-gram ``<G^-1 dW1 A^-1, dW2>``."""
+    a1, g1 = preprocess_factors(a1, g1, layer_type, module_kwargs1, include_bias)
+    a2, g2 = preprocess_factors(a2, g2, layer_type, module_kwargs2, include_bias)
+    a1 = _right_multiply(a1.float(), A_inv.float())
+    g1 = _right_multiply(g1.float(), G_inv.float())
+    return cross_gram(a1, g1, a2, g2, layer_type)
+
+
+def kfac_eigh(A: torch.Tensor, G: torch.Tensor):
+    """Eigendecompose both factors: ``(s_A, U_A, s_G, U_G)``."""
+    s_a, u_a = torch.linalg.eigh(A.float())
+    s_g, u_g = torch.linalg.eigh(G.float())
+    return s_a, u_a, s_g, u_g
+
+
+def ekfac_materialize_factors(a, g, layer_type: str, U_A, U_G, module_kwargs=None,
+                              include_bias: bool = True) -> torch.Tensor:
+    """Per-sample weight gradient rotated into the K-FAC eigenbasis: ``U_G^T dW U_A``."""
+    a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
+    a = _right_multiply(a.float(), U_A.float())
+    g = _right_multiply(g.float(), U_G.float())
+    return materialize_factors(a, g, layer_type)
+
+
+def kfac(f, layer_type: str, include_bias: bool = True):
+    """:func:`kfac_factors` on a :class:`Factorized` (batch-first-safe)."""
+    bf = f.as_batch_first()
+    return kfac_factors(bf.activation, bf.pre_activation_grad, layer_type, bf.module_kwargs,
+                        include_bias)
+
+
+def fim(f, layer_type: str, include_bias: bool = True):
+    """:func:`fim_factors` on a :class:`Factorized` (batch-first-safe)."""
+    bf = f.as_batch_first()
+    return fim_factors(bf.activation, bf.pre_activation_grad, layer_type, bf.module_kwargs,
+                       include_bias)
+
+
+def kfac_cross(f1, f2, layer_type: str, A_inv, G_inv, include_bias: bool = True):
+    """:func:`kfac_cross_factors` on two :class:`Factorized` (batch-first-safe)."""
+    b1, b2 = f1.as_batch_first(), f2.as_batch_first()
+    return kfac_cross_factors(b1.activation, b1.pre_activation_grad, b2.activation,
+                              b2.pre_activation_grad, layer_type, A_inv, G_inv, b1.module_kwargs,
+                              b2.module_kwargs, include_bias)
+
+
+def _rotate_block(block, layer_type, U_A, U_G, transpose=False):
+    """``U_G^T dW U_A`` (or ``U_G dW U_A^T`` with *transpose*) of a dense block."""
+    batch = block.shape[0]
+    ua, ug = U_A.float(), U_G.float()
+    if transpose:
+        ua, ug = ua.transpose(-1, -2), ug.transpose(-1, -2)
+    if U_A.ndim == 3:
+        groups, ka, kg = U_A.shape[0], U_A.shape[-1], U_G.shape[-1]
+        if is_conv_transpose(layer_type):
+            dw = block.reshape(batch, groups, ka, kg).float()
+            return torch.einsum("gce,bgcp,gpf->bgef", ua, dw, ug).reshape(batch, -1)
+        dw = block.reshape(batch, groups, kg, ka).float()
+        return torch.einsum("goe,bgoi,gif->bgef", ug, dw, ua).reshape(batch, -1)
+    if is_conv_transpose(layer_type):
+        c_in, p = U_A.shape[0], U_G.shape[0]
+        dw = block.reshape(batch, c_in, p).float()
+        return (ua.transpose(0, 1) @ dw @ ug).reshape(batch, c_in * p)
+    d_out, d_in = U_G.shape[0], U_A.shape[0]
+    dw = block.reshape(batch, d_out, d_in).float()
+    return (ug.transpose(0, 1) @ dw @ ua).reshape(batch, d_out * d_in)
+
+
+def ekfac_materialize(f, layer_type: str, U_A, U_G, include_bias: bool = True) -> torch.Tensor:
+    """Eigenbasis coordinates of a :class:`Factorized` layer, or of a dense block."""
+    if isinstance(f, torch.Tensor):
+        return _rotate_block(f, layer_type, U_A, U_G)
+    bf = f.as_batch_first()
+    return ekfac_materialize_factors(bf.activation, bf.pre_activation_grad, layer_type, U_A, U_G,
+                                     bf.module_kwargs, include_bias)
+
+
+def kfac_precondition(f, layer_type: str, A_inv, G_inv, include_bias: bool = True):
+    """Preprocess and whiten one side's factors: ``(a A^-1, g G^-1)``."""
+    bf = f.as_batch_first()
+    a, g = preprocess_factors(bf.activation, bf.pre_activation_grad, layer_type,
+                              bf.module_kwargs, include_bias)
+    return _right_multiply(a.float(), A_inv.float()), _right_multiply(g.float(), G_inv.float())
+
+
+def kfac_precondition_materialized(block: torch.Tensor, A_inv, G_inv) -> torch.Tensor:
+    """Two-sided ``G^-1 dW A^-1`` of a compact dense block ``(B, k_g * k_a)``."""
+    batch = block.shape[0]
+    kg, ka = G_inv.shape[-1], A_inv.shape[-1]
+    if A_inv.ndim == 3:
+        dw = block.reshape(batch, A_inv.shape[0], kg, ka).float()
+        return torch.einsum("gde,bgek,gkj->bgdj", G_inv.float(), dw, A_inv.float()).reshape(batch, -1)
+    dw = block.reshape(batch, kg, ka).float()
+    return (G_inv.float() @ dw @ A_inv.float()).reshape(batch, kg * ka)
+
+
+def ekfac_precondition(M: torch.Tensor, U_A, U_G, lam: torch.Tensor, layer_type: str) -> torch.Tensor:
+    """Apply the damped EK-FAC inverse to eigenbasis coordinates *M* and rotate back:
+    ``U_G (M / lam) U_A^T``."""
+    return _rotate_block(M / lam, layer_type, U_A, U_G, transpose=True)
+
+
+@dataclass
+class LayerKroneckerAccumulator:
+    """Streaming fp32 ``(A, G)`` sums and gradient-carrying row count of one layer."""
+
+    _A: torch.Tensor | None = field(default=None, init=False, repr=False)
+    _G: torch.Tensor | None = field(default=None, init=False, repr=False)
+    _count: torch.Tensor | int = field(default=0, init=False, repr=False)
+
+    @property
+    def _n(self) -> int:
+        return int(self._count)
+
+    def update(self, a, g, layer_type: str, module_kwargs: dict | None = None,
+               include_bias: bool = True) -> None:
+        """Add one batch's raw (or final) factors."""
+        a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
+        a_f, g_f = _flatten_for_kfac(a, g, layer_type)
+        a_f, g_f, n = _row_mask(a_f, g_f, layer_type)
+        if self._A is None:
+            lead = a_f.shape[:-2]
+            self._A = torch.zeros(*lead, a_f.shape[-1], a_f.shape[-1], device=a_f.device)
+            self._G = torch.zeros(*lead, g_f.shape[-1], g_f.shape[-1], device=g_f.device)
+        gram_accumulate(a_f, self._A)
+        gram_accumulate(g_f, self._G)
+        self._count = self._count + n
+
+    def all_reduce(self) -> None:
+        """Sum the accumulators and counts over ranks."""
+        if self._A is None:
+            raise RuntimeError("No gradient-carrying data has been accumulated")
+        all_reduce_sum(self._A)
+        all_reduce_sum(self._G)
+        n = torch.tensor([self._n], dtype=torch.int64)
+        self._count = int(all_reduce_sum(n).item())
+
+    def result(self, *, consume: bool = False):
+        """``(A, G)`` means; with *consume* the sums are divided in place and released."""
+        n = self._n
+        if self._A is None or n == 0:
+            raise RuntimeError("No gradient-carrying data has been accumulated")
+        if not consume:
+            return self._A / n, self._G / n
+        A, G = self._A.div_(n), self._G.div_(n)
+        self.reset()
+        return A, G
+
+    def reset(self) -> None:
+        """Drop the accumulated state."""
+        self._A, self._G, self._count = None, None, 0
+
+
+@dataclass
+class LayerFisherAccumulator:
+    """Streaming empirical Fisher ``sum_i dW_i dW_i^T`` of one layer."""
+
+    _F: torch.Tensor | None = field(default=None, init=False, repr=False)
+    _n: int = field(default=0, init=False, repr=False)
+
+    def update(self, a, g, layer_type: str, module_kwargs: dict | None = None,
+               include_bias: bool = True) -> None:
+        """Add one batch from raw factors."""
+        self.update_from_grad(materialize_factors(a, g, layer_type, module_kwargs, include_bias))
+
+    def update_from_grad(self, grad: torch.Tensor) -> None:
+        """Add one batch of dense per-sample gradients ``(B, d)``."""
+        if self._F is None:
+            self._F = torch.zeros(grad.shape[-1], grad.shape[-1], dtype=grad.dtype, device=grad.device)
+        self._F += grad.T @ grad
+        self._n += grad.shape[0]
+
+    def all_reduce(self) -> None:
+        """Sum over ranks."""
+        if self._F is None:
+            raise RuntimeError("No data has been accumulated")
+        all_reduce_sum(self._F)
+        self._n = int(all_reduce_sum(torch.tensor([self._n], dtype=torch.int64)).item())
+
+    def result(self) -> torch.Tensor:
+        """The mean Fisher."""
+        if self._F is None:
+            raise RuntimeError("No data has been accumulated")
+        return self._F / self._n
+
+    def reset(self) -> None:
+        """Drop the accumulated state."""
+        self._F, self._n = None, 0
+
+
+class KroneckerAccumulator:
+    """Per-layer :class:`LayerKroneckerAccumulator` over whole gradient blocks."""
+
+    def __init__(self) -> None:
+        self._layers: dict[str, LayerKroneckerAccumulator] = {}
+
+    def update(self, gradient, layers: Iterable[str]) -> None:
+        """Add the named factorized layers of *gradient*."""
+        for name in layers:
+            value = gradient.data[name]
+            if isinstance(value, torch.Tensor):
+                raise TypeError(
+                    f"K-FAC covariances need factorized (activation, output-gradient) factors, "
+                    f"but layer {name!r} holds a materialized tensor; exclude it from the K-FAC "
+                    "layer set.",
+                )
+            bf = value.as_batch_first()
+            self._layers.setdefault(name, LayerKroneckerAccumulator()).update(
+                bf.activation, bf.pre_activation_grad, gradient.layer_types[name], bf.module_kwargs)
+
+    def all_reduce(self) -> None:
+        """Sum every layer over ranks (sorted order: identical on every rank)."""
+        for name in sorted(self._layers):
+            self._layers[name].all_reduce()
+
+    def result(self, *, consume: bool = False) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        """``{layer: (A, G)}``."""
+        out = {n: acc.result(consume=consume) for n, acc in self._layers.items()}
+        if consume:
+            self._layers = {}
+        return out
+
+
+class FisherAccumulator:
+    """Per-layer dense empirical Fishers; layers wider than *max_params* are skipped."""
+
+    def __init__(self, max_params: int | None = None) -> None:
+        self._max_params = max_params
+        self._layers: dict[str, LayerFisherAccumulator] = {}
+        self._skipped: dict[str, int] = {}
+
+    def update(self, gradient, layers: Iterable[str]) -> None:
+        """Add the named layers of *gradient* (any form)."""
+        for name in layers:
+            if name in self._skipped:
+                continue
+            value = gradient.data[name]
+            g = (value.reshape(value.shape[0], -1).float() if isinstance(value, torch.Tensor)
+                 else materialize(value, gradient.layer_types[name]))
+            if self._max_params is not None and g.shape[-1] > self._max_params:
+                self._skipped[name] = g.shape[-1]
+                self._layers.pop(name, None)
+                continue
+            self._layers.setdefault(name, LayerFisherAccumulator()).update_from_grad(g)
+
+    def all_reduce(self) -> None:
+        """Sum every layer over ranks."""
+        for name in sorted(self._layers):
+            self._layers[name].all_reduce()
+
+    def result(self) -> dict[str, torch.Tensor]:
+        """``{layer: F}``."""
+        return {n: acc.result() for n, acc in self._layers.items()}
+
+    @property
+    def skipped(self) -> dict[str, int]:
+        """Layers left out for width, with their width."""
+        return dict(self._skipped)

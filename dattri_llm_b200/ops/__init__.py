@@ -114,6 +114,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     gemm_tn,
     matmul_tn,
 )
+from dattri_llm_b200.ops.gram import ghost_gram, per_sample_outer  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
 
 __all__ = [
@@ -125,8 +126,10 @@ __all__ = [
     "check_device_errors",
     "error_word",
     "gemm_tn",
+    "ghost_gram",
     "matmul_tn",
     "native",
+    "per_sample_outer",
     "projection_matrix_t",
     "use_native",
 ]

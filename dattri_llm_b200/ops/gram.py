@@ -1,0 +1,54 @@
+"""Per-sample outer products and cross-grams on the tensor cores."""
+
+from __future__ import annotations
+
+import torch
+
+from dattri_llm_b200.ops.gemm import STORE_BF16, STORE_F32, gemm_tn
+
+
+def per_sample_outer(
+    left: torch.Tensor,
+    right: torch.Tensor,
+    *,
+    out_dtype: torch.dtype = torch.float32,
+    left_t: torch.Tensor | None = None,
+    right_t: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``out[b] = left[b]^T right[b]`` over the token axis: ``(B, T, L), (B, T, R) -> (B, L, R)``.
+
+    The contraction runs over tokens, so the GEMM operands are the token-major
+    transposes ``(B, L, T)`` / ``(B, R, T)``; callers that already hold them (the
+    capture kernels write projected factors transposed) pass *left_t* / *right_t*.
+    """
+    lt = left_t if left_t is not None else left.transpose(1, 2).contiguous()
+    rt = right_t if right_t is not None else right.transpose(1, 2).contiguous()
+    if lt.dtype != torch.bfloat16:
+        lt = lt.bfloat16()
+    if rt.dtype != torch.bfloat16:
+        rt = rt.bfloat16()
+    b, l_dim, r_dim = lt.shape[0], lt.shape[1], rt.shape[1]
+    out = torch.empty(b, l_dim, r_dim, dtype=out_dtype, device=lt.device)
+    gemm_tn(lt, rt, out, mode=STORE_BF16 if out_dtype == torch.bfloat16 else STORE_F32)
+    return out
+
+
+def ghost_gram(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.Tensor) -> torch.Tensor:
+    """Fused factorized cross-gram ``(B1, B2)`` (fp32) of 3-D bf16 factors
+    ``a (B, S, K)``, ``g (B, S, D)``; the token-pair products stay on chip."""
+    from dattri_llm_b200.ops import error_word, native
+
+    b1, s1 = a1.shape[:2]
+    b2, s2 = a2.shape[:2]
+    out = torch.zeros(b1, b2, dtype=torch.float32, device=a1.device)
+    if b1 == 0 or b2 == 0:
+        return out
+
+    def flat(x):
+        x = x.reshape(-1, x.shape[-1])
+        if x.shape[-1] % 8:
+            x = torch.nn.functional.pad(x, (0, 8 - x.shape[-1] % 8))
+        return x.contiguous().bfloat16()
+
+    native().ghost_gram(flat(a1), flat(g1), flat(a2), flat(g2), s1, s2, out, error_word(a1.device))
+    return out

@@ -1,0 +1,23 @@
+"""Utilities: content hashing, distributed and autograd helpers, the tensor cache."""
+
+from dattri_llm_b200.utils.autograd import (
+    queue_after_backward_finalization,
+    queue_backward_end_callback,
+)
+from dattri_llm_b200.utils.cache import CACHE_RESIDENCIES, CacheBudget, TensorCache, tensor_nbytes
+from dattri_llm_b200.utils.distributed import dist_rank, dist_world_size, is_dist_initialized
+from dattri_llm_b200.utils.hashing import hash_batch, hash_sample
+
+__all__ = [
+    "CACHE_RESIDENCIES",
+    "CacheBudget",
+    "TensorCache",
+    "dist_rank",
+    "dist_world_size",
+    "hash_batch",
+    "hash_sample",
+    "is_dist_initialized",
+    "queue_after_backward_finalization",
+    "queue_backward_end_callback",
+    "tensor_nbytes",
+]

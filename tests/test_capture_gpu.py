@@ -1,0 +1,72 @@
+"""Native capture path on the GPU vs the CPU fp32 reference path of the same ops."""
+
+import copy
+
+import pytest
+import torch
+
+from dattri_llm_b200 import CaptureCallback, HookManager, HookManagerConfig, ops as _ops  # noqa: F401
+from dattri_llm_b200 import ops as native_ops
+from dattri_llm_b200.gradient import ops
+
+pytestmark = pytest.mark.gpu
+
+
+class _Tiny(torch.nn.Module):
+    def __init__(self, vocab=64, d=64, ff=128):
+        super().__init__()
+        self.emb = torch.nn.Embedding(vocab, d)
+        self.q = torch.nn.Linear(d, d, bias=False)
+        self.k = torch.nn.Linear(d, d, bias=False)
+        self.up = torch.nn.Linear(d, ff, bias=False)
+        self.down = torch.nn.Linear(ff, d, bias=False)
+        self.head = torch.nn.Linear(d, vocab, bias=False)
+
+    def forward(self, input_ids):
+        h = self.emb(input_ids)
+        h = h + self.q(h) * torch.sigmoid(self.k(h))
+        h = h + self.down(torch.nn.functional.silu(self.up(h)))
+        return self.head(h)
+
+
+def _capture(model, x, style, proj_dim=16):
+    cb = CaptureCallback()
+    cfg = HookManagerConfig(linear_io=[r"^(q|k|up|down)$"], capture_style=style,
+                            projection_kwargs={"__default__": {"style": "logra", "proj_dim": proj_dim}})
+    hm = HookManager(model, cfg, callbacks=[cb])
+    with hm.collect():
+        out = model(input_ids=x)
+        loss = torch.nn.functional.cross_entropy(out.float().reshape(-1, out.shape[-1]), x.reshape(-1))
+        loss.backward()
+    hm.remove()
+    return cb.record.gradient
+
+
+@pytest.mark.parametrize("style", ["materialized", "factorized"])
+def test_projected_capture_native_matches_cpu(style):
+    torch.manual_seed(0)
+    cpu = _Tiny()
+    gpu = copy.deepcopy(cpu).cuda().bfloat16()
+    x = torch.randint(0, 64, (4, 32))
+    ref = _capture(cpu, x, style).materialize()
+    got = _capture(gpu, x.cuda(), style).materialize()
+    native_ops.check_device_errors()
+    for name in ref.layer_names:
+        r, g = ref.data[name].float(), got.data[name].float().cpu()
+        err = (r - g).norm() / r.norm()
+        assert err < 5e-2, (name, float(err))
+
+
+def test_ghost_route_matches_materialized_route_on_gpu():
+    torch.manual_seed(1)
+    a1 = torch.randn(3, 40, 64, device="cuda").bfloat16()
+    g1 = torch.randn(3, 40, 32, device="cuda").bfloat16()
+    a2 = torch.randn(5, 24, 64, device="cuda").bfloat16()
+    g2 = torch.randn(5, 24, 32, device="cuda").bfloat16()
+    ghost = ops.cross_gram(a1, g1, a2, g2, "nn.Linear", mode="factorized").float()
+    mat = ops.cross_gram(a1, g1, a2, g2, "nn.Linear", mode="materialized").float()
+    ref = ops.cross_gram(a1.double().cpu(), g1.double().cpu(), a2.double().cpu(), g2.double().cpu(),
+                         "nn.Linear", mode="factorized")
+    scale = ref.abs().max().item()
+    torch.testing.assert_close(ghost.cpu().double(), ref, rtol=0, atol=1e-2 * scale)
+    torch.testing.assert_close(mat.cpu().double(), ref, rtol=0, atol=2e-2 * scale)

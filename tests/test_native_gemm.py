@@ -59,3 +59,27 @@ def test_device_projection_matches_host_generator(kind):
     dev = ops.projection_matrix_t(d, k, 3, kind=kind, dtype=torch.float32)
     host = counter_projection_matrix(d, k, 3, kind=kind)
     torch.testing.assert_close(dev.cpu(), host.t(), rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize(("b1", "s1", "b2", "s2", "k", "d"),
+                         [(2, 64, 3, 64, 64, 64), (3, 50, 5, 17, 72, 40), (4, 1, 6, 1, 128, 64),
+                          (2, 300, 2, 200, 256, 128), (1, 7, 300, 3, 16, 24)])
+def test_ghost_gram_matches_dense_oracle(b1, s1, b2, s2, k, d):
+    a1 = torch.randn(b1, s1, k, device="cuda").bfloat16()
+    g1 = torch.randn(b1, s1, d, device="cuda").bfloat16()
+    a2 = torch.randn(b2, s2, k, device="cuda").bfloat16()
+    g2 = torch.randn(b2, s2, d, device="cuda").bfloat16()
+    got = ops.ghost_gram(a1, g1, a2, g2)
+    ops.check_device_errors(a1.device)
+    m1 = torch.einsum("bsk,bsd->bdk", a1.double(), g1.double()).flatten(1)
+    m2 = torch.einsum("bsk,bsd->bdk", a2.double(), g2.double()).flatten(1)
+    ref = (m1 @ m2.T).float()
+    torch.testing.assert_close(got, ref, rtol=2e-3, atol=2e-3 * ref.abs().max().item())
+
+
+def test_per_sample_outer_matches_bmm():
+    left = torch.randn(3, 100, 64, device="cuda").bfloat16()
+    right = torch.randn(3, 100, 48, device="cuda").bfloat16()
+    got = ops.per_sample_outer(left, right)
+    ref = torch.bmm(left.double().transpose(1, 2), right.double()).float()
+    torch.testing.assert_close(got, ref, rtol=1e-3, atol=1e-2)
