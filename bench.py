@@ -1,0 +1,458 @@
+"""Headline benchmark: train samples attributed per second (capture + project + score).
+
+Configuration: Llama-3.2-1B-architecture decoder (16 layers,
+d 2048, 32/8 heads, FFN 8192, vocab 128256), bf16, random init (seed 0), sequence
+length 1024, micro-batch 8 per GPU, data parallel over N GPUs (one process per
+GPU), synthetic uniform token ids.  Capture: every attention / MLP projection
+(7 per layer, 112 layers), factorized and LoGra-projected to 64 x 64 per layer,
+materialized at capture (``capture_style="auto"``).  Scoring: TracIn / GradDot of
+every train sample against 1,024 test samples, with a running per-test top-100.
+
+Usage (one process per GPU; N > 1 under torchrun)::
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a device
+synchronize, timed with CUDA events on the compute stream; the reported time is the
+max over ranks.  Per-step inputs (64 KiB of token ids per GPU) and the 1024 x
+458,752 bf16 test matrix (940 MB) far exceed nothing -- the per-step weight
+traffic (2.4 GB of bf16 parameters) and activations exceed the 126 MB L2, so no
+flush is needed between iterations.  ``e2e`` re-runs K steps through the public
+streaming API with the host->device copy of each step's batch from pinned memory
+and the device->host copy of each step's score rows, timed on the host.
+
+The reference arm runs the unmodified reference (``baseline/_ref``) through its own
+public ``TracInAttributor`` scoring loop on Hugging Face's ``LlamaForCausalLM`` with
+the same projection matrices; its K train steps are timed the same way.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SEQ = 1024
+MICRO_BATCH = 8
+N_TEST = 1024
+PROJ_DIM = 64
+TOPK = 100
+PUBLISHED = None  # BASELINE.md publishes no number for this configuration
+METRIC = "train samples attributed/sec (capture+project+score), device-timed, 1/2/4/8 B200"
+
+
+# --------------------------------------------------------------------------- utilities
+def _env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def _init_dist():
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons of this process's GPU with nvidia-smi."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int) -> None:
+        self.local = local_rank
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self) -> None:
+        try:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = vis.split(",")[self.local] if vis else str(self.local)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "-i", idx, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sms.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8], strict=False):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def counter_projector_factory():
+    """The dattri-protocol projector both arms use: the counter-based Rademacher
+    matrix P[i, j] = +-1/sqrt(k) from SplitMix64(key(seed, d, k) + i*k + j), written in
+    plain torch so the reference arm runs none of this library's code."""
+    m64 = (1 << 64) - 1
+
+    def s64(v):
+        v &= m64
+        return v - (1 << 64) if v >= 1 << 63 else v
+
+    def mix_int(x):
+        x = (x + 0x9E3779B97F4A7C15) & m64
+        z = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & m64
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m64
+        return z ^ (z >> 31)
+
+    def lshr(x, s):
+        return (x >> s) & ((1 << (64 - s)) - 1)
+
+    def mix(x):
+        x = x + s64(0x9E3779B97F4A7C15)
+        z = (x ^ lshr(x, 30)) * s64(0xBF58476D1CE4E5B9)
+        z = (z ^ lshr(z, 27)) * s64(0x94D049BB133111EB)
+        return z ^ lshr(z, 31)
+
+    def factory(feature, batch_size, proj_dim, proj_seed=0, device=None, **_kw):
+        d = feature.shape[-1]
+        dev = torch.device(device) if device is not None else feature.device
+        key = s64(mix_int(mix_int(proj_seed & m64) ^ ((d * 0x100000001B3) & m64) ^ proj_dim))
+        i = torch.arange(d, dtype=torch.int64, device=dev)
+        j = torch.arange(proj_dim, dtype=torch.int64, device=dev)
+        sign = torch.where(mix(key + i[:, None] * proj_dim + j[None, :]) < 0, -1.0, 1.0)
+        mat = sign / math.sqrt(proj_dim)
+        return lambda x: x.to(mat.dtype) @ mat
+
+    return factory
+
+
+def _layers_regex():
+    return [r"\.(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj)$"]
+
+
+def _token_sum_loss(model, batch):
+    import torch.nn.functional as F
+
+    ids = batch["input_ids"]
+    inner = getattr(model, "module", model)
+    if hasattr(inner, "lm_loss"):
+        return model(input_ids=ids, labels=ids, loss_reduction="sum", return_logits=False).loss
+    out = model(input_ids=ids)
+    logits = out.logits
+    return F.cross_entropy(logits[:, :-1].float().reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1),
+                           reduction="sum")
+
+
+class _DS(torch.utils.data.Dataset):
+    """Synthetic uniform-token sequences, deterministic per index."""
+
+    def __init__(self, n: int, vocab: int, seed: int) -> None:
+        g = torch.Generator().manual_seed(seed)
+        self.ids = torch.randint(0, vocab, (n, SEQ), generator=g)
+
+    def __len__(self):
+        return self.ids.shape[0]
+
+    def __getitem__(self, i):
+        return {"input_ids": self.ids[i]}
+
+
+class _TimedBlocks:
+    """Wraps a gradient source: CUDA events (and host times) at block *warm* and after
+    block ``warm + steps - 1`` has been consumed by the scoring loop."""
+
+    def __init__(self, source, warm: int, steps: int) -> None:
+        self.source, self.warm, self.steps = source, warm, steps
+        self.ev0 = torch.cuda.Event(enable_timing=True)
+        self.ev1 = torch.cuda.Event(enable_timing=True)
+        self.t0 = self.t1 = None
+        self.reusable = getattr(source, "reusable", False)
+        self.args = getattr(source, "args", None)
+
+    def __len__(self):
+        return len(self.source)
+
+    def __iter__(self):
+        for i, item in enumerate(self.source):
+            if i == self.warm:
+                torch.cuda.synchronize()
+                self.t0 = time.perf_counter()
+                self.ev0.record()
+            if i == self.warm + self.steps:
+                self.ev1.record()
+                torch.cuda.synchronize()
+                self.t1 = time.perf_counter()
+            yield item
+
+    def __getattr__(self, name):
+        return getattr(self.source, name)
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(rank, world, local, steps, warmup):
+    sys.path.insert(0, HERE)
+    import dattri_llm_b200 as bw
+    from dattri_llm_b200 import ops as native_ops
+    from dattri_llm_b200.attribution.utils import PackedDense, packed_cross_dot
+    from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM
+
+    native_ops.native()  # fail loudly without the extension
+    dev = torch.device("cuda", local)
+    cfg = LlamaConfig.llama_3_2_1b()
+    model = LlamaForCausalLM(cfg, frozen_probe=True)
+    model.reset_parameters(seed=0)
+    model = model.to(dev, torch.bfloat16).eval()
+    model.requires_grad_(False)
+    proj = {"__default__": {"style": "logra", "proj_dim": PROJ_DIM, "proj_type": "rademacher", "proj_seed": 0}}
+    hc = bw.HookManagerConfig(linear_io=_layers_regex(), projection_kwargs=proj, capture_style="auto",
+                              include_frozen=True)
+    cap = bw.CaptureCallback()
+    hm = bw.HookManager(model, hc, callbacks=[cap])
+
+    def step_block(ids):
+        with hm.collect():
+            cap.record = None
+            loss = model(input_ids=ids, labels=ids, loss_reduction="sum", return_logits=False).loss
+            loss.backward()
+        return cap.record.gradient
+
+    # -- test side: this rank's share, then all ranks' packed blocks gathered
+    per_rank = N_TEST // world
+    test_ids = _DS(N_TEST, cfg.vocab_size, seed=1).ids[rank * per_rank:(rank + 1) * per_rank].to(dev)
+    parts = []
+    with torch.no_grad():
+        pass
+    for s in range(0, per_rank, MICRO_BATCH):
+        g = step_block(test_ids[s:s + MICRO_BATCH])
+        parts.append(PackedDense.pack(g).matrix)
+    local_test = torch.cat(parts)
+    layout = PackedDense.layout_of(g)
+    if world > 1:
+        import torch.distributed as dist
+
+        full = torch.empty(N_TEST, local_test.shape[1], dtype=local_test.dtype, device=dev)
+        dist.all_gather_into_tensor(full, local_test)
+        test = PackedDense(full, layout)
+    else:
+        test = PackedDense(local_test, layout)
+    torch.cuda.synchronize()
+
+    n_train = (warmup + steps) * MICRO_BATCH
+    train_ids = _DS(n_train * world, cfg.vocab_size, seed=2).ids[rank * n_train:(rank + 1) * n_train].to(dev)
+    scores = torch.zeros(n_train, N_TEST, dtype=torch.float32, device=dev)
+    top_vals = torch.full((N_TEST, TOPK), -float("inf"), device=dev)
+    top_idx = torch.zeros(N_TEST, TOPK, dtype=torch.long, device=dev)
+
+    def one_step(i):
+        nonlocal top_vals, top_idx
+        ids = train_ids[i * MICRO_BATCH:(i + 1) * MICRO_BATCH]
+        hm.set_sample_ids([f"{rank}:{i}:{j}" for j in range(MICRO_BATCH)])
+        g = step_block(ids)
+        block = packed_cross_dot(PackedDense.pack(g), test)  # (B, N_TEST) fp32
+        scores[i * MICRO_BATCH:(i + 1) * MICRO_BATCH] = block
+        cand_v = torch.cat([top_vals, block.T], dim=1)
+        cand_i = torch.cat([top_idx, torch.arange(i * MICRO_BATCH, (i + 1) * MICRO_BATCH, device=dev)
+                            .expand(N_TEST, MICRO_BATCH)], dim=1)
+        top_vals, pos = torch.topk(cand_v, TOPK, dim=1)
+        top_idx = torch.gather(cand_i, 1, pos)
+
+    for i in range(warmup):
+        one_step(i)
+    native_ops.check_device_errors(dev)
+    clocks = ClockSampler(local)
+    _barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = native_ops.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(warmup, warmup + steps):
+        one_step(i)
+    ev1.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    launches = native_ops.launch_count() - launches0
+    clk = clocks.stop()
+    ms = _max_over_ranks(ev0.elapsed_time(ev1), world) / steps
+    native_ops.check_device_errors(dev)
+    hm.remove()
+
+    # -- end to end through the public streaming API: pinned H2D + per-step D2H
+    e2e = run_ours_e2e(bw, model, hc, test, rank, world, steps, warmup, cfg.vocab_size)
+    return ms, launches, clk, e2e
+
+
+def run_ours_e2e(bw, model, hc, test, rank, world, steps, warmup, vocab):
+    from dattri_llm_b200.attribution.utils import PackedDense, packed_cross_dot
+
+    args = bw.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=MICRO_BATCH,
+                                   dataloader_pin_memory=True)
+    n = (warmup + steps + 1) * MICRO_BATCH
+    ds = _DS(n * world, vocab, seed=3)
+    streamer = bw.GradientStreamer(model, ds, args, batch_size=MICRO_BATCH, loss_fn=_token_sum_loss,
+                                   config=hc, forward_model=model)
+    host_rows = torch.empty(MICRO_BATCH, N_TEST, dtype=torch.float32, pin_memory=True)
+    timed = _TimedBlocks(streamer, warmup, steps)
+    with streamer:
+        for _step, grad, _hashes in timed:
+            block = packed_cross_dot(PackedDense.pack(grad), test)
+            host_rows[: block.shape[0]].copy_(block, non_blocking=True)  # the step's result to the host
+    host = (timed.t1 - timed.t0)
+    host = _max_over_ranks(host, world)
+    return {"value": MICRO_BATCH * world * steps / host, "unit": "train samples/s",
+            "h2d_bytes_per_step": MICRO_BATCH * SEQ * 8, "d2h_bytes_per_step": MICRO_BATCH * N_TEST * 4}
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(rank, world, local, steps, warmup):
+    ref = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "dattri_llm")):
+        return None
+    sys.path.insert(0, ref)
+    import dattri_llm as R  # noqa: N812
+    from transformers import LlamaConfig as HFConfig
+    from transformers import LlamaForCausalLM as HFLlama
+
+    dev = torch.device("cuda", local)
+    hfc = HFConfig(vocab_size=128256, hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                   num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=131072,
+                   rope_theta=500000.0, tie_word_embeddings=True,
+                   rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                 "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+                   attn_implementation="sdpa")
+    torch.manual_seed(0)
+    model = HFLlama(hfc).to(dev, torch.bfloat16).eval()
+    # the reference's frozen-capture recipe: everything frozen but the input embedding
+    model.requires_grad_(False)
+    model.get_input_embeddings().requires_grad_(True)
+    proj = {"__default__": {"style": "logra", "proj_dim": PROJ_DIM, "proj_type": "rademacher", "proj_seed": 0}}
+    hc = R.HookManagerConfig(linear_io=_layers_regex(), projection_kwargs=proj,
+                             projector=counter_projector_factory(), capture_style="auto", include_frozen=True)
+    args = R.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=MICRO_BATCH,
+                                  per_device_eval_batch_size=MICRO_BATCH, dataloader_pin_memory=True)
+    task = R.AttributionTask(_token_sum_loss, model)
+    att = R.TracInAttributor(args, task=task)
+    n = (warmup + steps + 1) * MICRO_BATCH
+    train_ds = _DS(n * world, hfc.vocab_size, seed=2)
+    test_ds = _DS(N_TEST, hfc.vocab_size, seed=1)
+    train = att.generate_train_rep(train_ds, hook_config=hc)
+    test = att.generate_test_rep(test_ds, hook_manager=train.hook_manager, forward_model=train.forward_model,
+                                 shard=False)
+    timed = _TimedBlocks(train, warmup, steps)
+    clocks = ClockSampler(local)
+    clocks.start()
+    with train, test:
+        att.score_sources(timed, test)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(timed.ev0.elapsed_time(timed.ev1), world) / steps
+    host = _max_over_ranks(timed.t1 - timed.t0, world)
+    e2e = {"value": MICRO_BATCH * world * steps / host, "unit": "train samples/s",
+           "h2d_bytes_per_step": MICRO_BATCH * SEQ * 8, "d2h_bytes_per_step": MICRO_BATCH * N_TEST * 4}
+    return ms, clk, e2e
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    rank, world, local = _init_dist()
+    torch.backends.cuda.matmul.allow_tf32 = True
+    cfg_json = {"model": "Llama-3.2-1B-arch (random init)", "global_batch": MICRO_BATCH * world,
+                "micro_batch_per_gpu": MICRO_BATCH, "seq_len": SEQ, "parallelism": f"dp{world}",
+                "n_test": N_TEST, "proj": f"logra {PROJ_DIM}x{PROJ_DIM} per linear (112 layers)",
+                "topk": TOPK, "l2": "per-step traffic (weights 2.5 GB, test matrix 0.94 GB) exceeds the 126 MB L2"}
+    out = {"metric": METRIC, "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
+           "scaling": "weak", "dtype": "bf16", "data": "synthetic uniform token ids, random-init weights",
+           "config": cfg_json}
+    try:
+        if a.impl == "ours":
+            ms, launches, clk, e2e = run_ours(rank, world, local, a.steps, a.warmup)
+            value = MICRO_BATCH * world / (ms / 1e3)
+            out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms,
+                        "vs_baseline": None if PUBLISHED is None else value / PUBLISHED,
+                        "clocks": clk, "e2e": e2e, "gpu_launches": launches})
+        else:
+            res = run_reference(rank, world, local, a.steps, a.warmup)
+            if res is None:
+                out = {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
+            else:
+                ms, clk, e2e = res
+                value = MICRO_BATCH * world / (ms / 1e3)
+                out.update({"impl": "reference", "value": value, "unit": "train samples/s", "ms_per_step": ms,
+                            "vs_baseline": None, "clocks": clk, "e2e": e2e})
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

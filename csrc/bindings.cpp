@@ -9,6 +9,7 @@
 
 #include "gemm_tc.cuh"
 #include "ghost_gram.cuh"
+#include "fused.cuh"
 #include "kernels.cuh"
 
 namespace {
@@ -118,11 +119,90 @@ void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t 
   bw::ghost_gram_launch(oa1, oa2, og1, og2, p, at::cuda::getCurrentCUDAStream());
 }
 
+__nv_bfloat16* bf(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+void check_rows(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16 && t.is_contiguous(), name, " must be contiguous bf16");
+  TORCH_CHECK(t.size(-1) % 8 == 0, name, " width must be a multiple of 8");
+}
+
+std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rows(x, "x");
+  check_rows(w, "w");
+  const int cols = (int)x.size(-1);
+  const int rows = (int)(x.numel() / cols);
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  bw::rmsnorm_fwd(bf(x), bf(w), bf(y), rstd.data_ptr<float>(), rows, cols, (float)eps,
+                  at::cuda::getCurrentCUDAStream());
+  return {y, rstd};
+}
+
+Tensor rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rows(dy, "dy");
+  check_rows(x, "x");
+  const int cols = (int)x.size(-1);
+  const int rows = (int)(x.numel() / cols);
+  auto dx = torch::empty_like(x);
+  bw::rmsnorm_bwd(bf(dy), bf(x), bf(w), rstd.data_ptr<float>(), bf(dx), rows, cols,
+                  at::cuda::getCurrentCUDAStream());
+  return dx;
+}
+
+Tensor swiglu_fwd(Tensor g, Tensor u) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  check_rows(g, "g");
+  check_rows(u, "u");
+  auto h = torch::empty_like(g);
+  bw::swiglu_fwd(bf(g), bf(u), bf(h), g.numel(), at::cuda::getCurrentCUDAStream());
+  return h;
+}
+
+std::vector<Tensor> swiglu_bwd(Tensor dh, Tensor g, Tensor u) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  check_rows(dh, "dh");
+  auto dg = torch::empty_like(g);
+  auto du = torch::empty_like(u);
+  bw::swiglu_bwd(bf(dh), bf(g), bf(u), bf(dg), bf(du), g.numel(), at::cuda::getCurrentCUDAStream());
+  return {dg, du};
+}
+
+std::vector<Tensor> ce_fwd(Tensor logits, Tensor target) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == torch::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+              "logits must be (rows, vocab) bf16, contiguous rows");
+  TORCH_CHECK(logits.size(1) % 8 == 0 && logits.stride(0) % 8 == 0, "vocab must be a multiple of 8");
+  TORCH_CHECK(target.scalar_type() == torch::kInt64 && target.is_contiguous(), "target must be int64");
+  const int rows = (int)logits.size(0);
+  auto loss = torch::empty({rows}, logits.options().dtype(torch::kFloat32));
+  auto lse = torch::empty({rows}, logits.options().dtype(torch::kFloat32));
+  bw::ce_fwd(bf(logits), target.data_ptr<int64_t>(), loss.data_ptr<float>(), lse.data_ptr<float>(), rows,
+             (int)logits.size(1), logits.stride(0), at::cuda::getCurrentCUDAStream());
+  return {loss, lse};
+}
+
+void ce_bwd_inplace(Tensor logits, Tensor lse, Tensor target, Tensor gscale) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  TORCH_CHECK(gscale.scalar_type() == torch::kFloat32 && gscale.is_cuda(), "gscale must be a CUDA float");
+  bw::ce_bwd_inplace(bf(logits), lse.data_ptr<float>(), target.data_ptr<int64_t>(), gscale.data_ptr<float>(),
+                     (int)logits.size(0), (int)logits.size(1), logits.stride(0), at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd_inplace", &ce_bwd_inplace);
   bw::register_kernels(m);
 }

@@ -57,6 +57,14 @@ def is_kfac_eligible(layer_type: str) -> bool:
 
 
 def canonical_class_name(module: nn.Module) -> str:
-    """``"nn.<Class>"`` for torch.nn modules, else ``"<module>.<Class>"``."""
+    """``"nn.<Class>"`` for torch.nn modules, else ``"<module>.<Class>"``.
+
+    A class may declare the layer type it computes with a ``__bw_layer_type__``
+    attribute (e.g. a fused-kernel subclass of ``nn.RMSNorm`` declares
+    ``"nn.RMSNorm"``), which takes precedence.
+    """
+    declared = getattr(type(module), "__bw_layer_type__", None)
+    if declared is not None:
+        return declared
     mod, name = type(module).__module__, type(module).__name__
     return f"nn.{name}" if mod.startswith("torch.nn") else f"{mod}.{name}"

@@ -20,6 +20,17 @@ import torch
 
 _C = None
 _IMPORT_ERROR: Exception | None = None
+_LAUNCHES = [0]
+
+
+def count_launch(n: int = 1) -> None:
+    """Record *n* native kernel launches (every entry point of this package calls it)."""
+    _LAUNCHES[0] += n
+
+
+def launch_count() -> int:
+    """Native kernels launched by this process so far."""
+    return _LAUNCHES[0]
 _lock = threading.Lock()
 _err_words: dict[int, torch.Tensor] = {}
 
@@ -124,8 +135,10 @@ __all__ = [
     "STORE_F32",
     "available",
     "check_device_errors",
+    "count_launch",
     "error_word",
     "gemm_tn",
+    "launch_count",
     "ghost_gram",
     "matmul_tn",
     "native",

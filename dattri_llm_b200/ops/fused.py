@@ -1,0 +1,120 @@
+"""Autograd wrappers of the fused model-path kernels (``csrc/fused.cu``).
+
+:func:`enabled` decides per call: bf16 CUDA tensors on sm_100 with 8-aligned
+widths.  Each op is a ``torch.autograd.Function`` whose backward is the matching
+fused kernel; parameter gradients (RMSNorm weight, LM-head weight) are computed
+only when the parameter requires grad.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def enabled(x: torch.Tensor) -> bool:
+    """Whether the fused kernels apply to *x*."""
+    from dattri_llm_b200.ops import use_native
+
+    return x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and use_native(x)
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        xc = x.contiguous()
+        y, rstd = native().rmsnorm_fwd(xc, w.contiguous(), float(eps))
+        ctx.save_for_backward(xc, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        x, w, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = native().rmsnorm_bwd(dy, x, w.contiguous(), rstd) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            xhat = x.float() * rstd.view(*x.shape[:-1], 1)
+            dw = (dy.float() * xhat).reshape(-1, x.shape[-1]).sum(0).to(w.dtype)
+        return dx, dw, None
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g, u):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        gc, uc = g.contiguous(), u.contiguous()
+        ctx.save_for_backward(gc, uc)
+        return native().swiglu_fwd(gc, uc)
+
+    @staticmethod
+    def backward(ctx, dh):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        g, u = ctx.saved_tensors
+        dg, du = native().swiglu_bwd(dh.contiguous(), g, u)
+        return dg, du
+
+
+class _LinearCrossEntropy(torch.autograd.Function):
+    """Sum over rows of CE(h W^T, target); bf16 logits kept for the backward, which
+    rewrites them into dlogits in place (a second backward through the same graph is
+    rejected)."""
+
+    @staticmethod
+    def forward(ctx, h, weight, target):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        logits = torch.nn.functional.linear(h, weight)
+        loss, lse = native().ce_fwd(logits, target)
+        ctx.logits = logits
+        ctx.save_for_backward(h, weight, lse, target)
+        return loss.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+
+        h, weight, lse, target = ctx.saved_tensors
+        logits = ctx.logits
+        if logits is None:
+            raise RuntimeError("the fused cross-entropy graph was already backpropagated "
+                               "(it reuses its logits buffer in place)")
+        ctx.logits = None
+        native().ce_bwd_inplace(logits, lse, target, g.reshape(1).float().contiguous())
+        dh = logits @ weight if ctx.needs_input_grad[0] else None
+        dw = logits.t() @ h if ctx.needs_input_grad[1] else None
+        return dh, dw, None
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float | None) -> torch.Tensor:
+    """Fused RMSNorm over the last axis."""
+    if eps is None:
+        eps = torch.finfo(x.dtype).eps
+    return _RMSNorm.apply(x, weight, eps)
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """Fused ``silu(g) * u``."""
+    return _SwiGLU.apply(g, u)
+
+
+def linear_cross_entropy(h: torch.Tensor, weight: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    """``sum_i CE(h_i W^T, target_i)`` (targets ``-100`` ignored) without fp32 logits."""
+    return _LinearCrossEntropy.apply(h.contiguous(), weight, target.contiguous().long())

@@ -43,8 +43,9 @@ def gemm_tn(
     accumulation (``splits > 1`` spreads K over CTAs) or a transposed bf16 store
     into ``out`` shaped ``(Z, N, M)``.
     """
-    from dattri_llm_b200.ops import error_word, native
+    from dattri_llm_b200.ops import count_launch, error_word, native
 
+    count_launch()
     a = _k_aligned(a)
     b = _k_aligned(b)
     native().gemm_tn(a, b, out, float(alpha), int(mode), int(splits), bool(accumulate),

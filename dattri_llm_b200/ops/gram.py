@@ -36,8 +36,9 @@ def per_sample_outer(
 def ghost_gram(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.Tensor) -> torch.Tensor:
     """Fused factorized cross-gram ``(B1, B2)`` (fp32) of 3-D bf16 factors
     ``a (B, S, K)``, ``g (B, S, D)``; the token-pair products stay on chip."""
-    from dattri_llm_b200.ops import error_word, native
+    from dattri_llm_b200.ops import count_launch, error_word, native
 
+    count_launch()
     b1, s1 = a1.shape[:2]
     b2, s2 = a2.shape[:2]
     out = torch.zeros(b1, b2, dtype=torch.float32, device=a1.device)

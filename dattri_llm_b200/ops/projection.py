@@ -24,8 +24,9 @@ def projection_matrix_t(
     :func:`dattri_llm_b200.gradient.ops.projection.counter_projection_matrix`,
     the PyTorch statement of the same counter-based generator.
     """
-    from dattri_llm_b200.ops import native
+    from dattri_llm_b200.ops import count_launch, native
 
+    count_launch()
     if kind not in KINDS:
         raise ValueError(f"projection kind must be one of {sorted(KINDS)}, got {kind!r}")
     return native().projection_matrix_t(
