@@ -118,6 +118,11 @@ class AttributionTask:
             self.current_checkpoint_idx = index
         return self._model
 
+    def invalidate_checkpoint(self) -> None:
+        """Forget which checkpoint is loaded: the parameters were changed in place (a
+        trajectory run trained them), so the next :meth:`load_checkpoint` reloads."""
+        self.current_checkpoint_idx = None
+
     @classmethod
     def from_dattri(cls, task: object) -> AttributionTask:
         """Adapt a dattri ``AttributionTask`` (or return an instance of this class as is).
