@@ -325,7 +325,9 @@ def run_ours(rank, world, local, steps, warmup):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for i in range(warmup, warmup + steps):
+        torch.cuda.nvtx.range_push("timed_step")
         one_step(i)
+        torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
     _barrier(world)

@@ -7,10 +7,13 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
+
 #include "gemm_tc.cuh"
 #include "ghost_gram.cuh"
 #include "fused.cuh"
 #include "kernels.cuh"
+#include "rows.cuh"
 
 namespace {
 
@@ -135,9 +138,103 @@ std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
   const int rows = (int)(x.numel() / cols);
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
-  bw::rmsnorm_fwd(bf(x), bf(w), bf(y), rstd.data_ptr<float>(), rows, cols, (float)eps,
-                  at::cuda::getCurrentCUDAStream());
+  if (bw::rows_norm_supported(cols)) {
+    bw::RowsNorm a{bf(x), nullptr, nullptr, bf(w), bf(y), rstd.data_ptr<float>(), rows, cols, (float)eps};
+    bw::rows_norm_fwd(a, at::cuda::getCurrentCUDAStream());
+  } else {
+    bw::rmsnorm_fwd(bf(x), bf(w), bf(y), rstd.data_ptr<float>(), rows, cols, (float)eps,
+                    at::cuda::getCurrentCUDAStream());
+  }
   return {y, rstd};
+}
+
+// h = x + delta (bf16), y = rmsnorm(h) * w: returns {y, h, rstd}.
+std::vector<Tensor> add_rmsnorm_fwd(Tensor x, Tensor delta, Tensor w, double eps) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rows(x, "x");
+  check_rows(delta, "delta");
+  check_rows(w, "w");
+  TORCH_CHECK(x.sizes() == delta.sizes(), "x and delta must have the same shape");
+  const int cols = (int)x.size(-1);
+  const int rows = (int)(x.numel() / cols);
+  TORCH_CHECK(bw::rows_norm_supported(cols), "add_rmsnorm: width must be a multiple of 8 and <= 4096");
+  TORCH_CHECK(w.numel() == cols, "w must have one entry per column");
+  auto y = torch::empty_like(x);
+  auto h = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  bw::RowsNorm a{bf(x), bf(delta), bf(h), bf(w), bf(y), rstd.data_ptr<float>(), rows, cols, (float)eps};
+  bw::rows_norm_fwd(a, at::cuda::getCurrentCUDAStream());
+  return {y, h, rstd};
+}
+
+// dx = rmsnorm_bwd(dy) + dres (dres optional).
+Tensor rmsnorm_bwd_acc(Tensor dy, Tensor x, Tensor w, Tensor rstd, c10::optional<Tensor> dres) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rows(dy, "dy");
+  check_rows(x, "x");
+  const int cols = (int)x.size(-1);
+  const int rows = (int)(x.numel() / cols);
+  TORCH_CHECK(bw::rows_norm_supported(cols), "rmsnorm_bwd_acc: width must be a multiple of 8 and <= 4096");
+  const __nv_bfloat16* dr = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    check_rows(*dres, "dres");
+    TORCH_CHECK(dres->numel() == x.numel(), "dres must match x");
+    dr = bf(*dres);
+  }
+  auto dx = torch::empty_like(x);
+  bw::RowsNormBwd a{bf(dy), bf(x), bf(w), rstd.data_ptr<float>(), dr, bf(dx), rows, cols};
+  bw::rows_norm_bwd(a, at::cuda::getCurrentCUDAStream());
+  return dx;
+}
+
+bw::RopeTensor rope_tensor(const Tensor& in, const Tensor& out, const char* name) {
+  check_cuda(in, name);
+  TORCH_CHECK(in.scalar_type() == torch::kBFloat16 && in.dim() == 4 && in.stride(3) == 1, name,
+              " must be (B, T, H, D) bf16 with a contiguous head dim");
+  for (int d = 0; d < 3; ++d)
+    TORCH_CHECK(in.stride(d) % 8 == 0, name, " strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(in.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+  return bw::RopeTensor{bf(in), bf(out), in.stride(0), in.stride(1), in.stride(2),
+                        out.stride(0), out.stride(1), out.stride(2)};
+}
+
+// Rotate q (B, T, Hq, D) and k (B, T, Hk, D) by position (inverse: by -theta); outputs contiguous.
+std::vector<Tensor> rope(Tensor q, Tensor k, Tensor cos, Tensor sin, bool inverse) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && q.size(0) == k.size(0) && q.size(1) == k.size(1) &&
+                  q.size(3) == k.size(3), "q and k must be (B, T, H, D) with matching B, T, D");
+  const int D = (int)q.size(3);
+  TORCH_CHECK(D % 16 == 0, "head dim must be a multiple of 16");
+  TORCH_CHECK(cos.scalar_type() == torch::kFloat32 && sin.scalar_type() == torch::kFloat32 &&
+                  cos.is_contiguous() && sin.is_contiguous() && cos.dim() == 2 && cos.size(1) == D / 2 &&
+                  cos.size(0) >= q.size(1) && sin.sizes() == cos.sizes(),
+              "cos/sin must be contiguous fp32 (>= T, D/2)");
+  auto qo = torch::empty(q.sizes(), q.options());
+  auto ko = torch::empty(k.sizes(), k.options());
+  bw::RopeArgs a{rope_tensor(q, qo, "q"), rope_tensor(k, ko, "k"), cos.data_ptr<float>(), sin.data_ptr<float>(),
+                 (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)k.size(2), D};
+  bw::rope(a, inverse, at::cuda::getCurrentCUDAStream());
+  return {qo, ko};
+}
+
+// Per-sample Adam direction of g (rows, p) fp32 against moments m0, v0 (p) fp32.
+Tensor adam_direction(Tensor g, Tensor m0, Tensor v0, double b1, double b2, int64_t step, double eps) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  check_cuda(g, "g");
+  TORCH_CHECK(g.scalar_type() == torch::kFloat32 && m0.scalar_type() == torch::kFloat32 &&
+                  v0.scalar_type() == torch::kFloat32, "adam_direction works in fp32");
+  TORCH_CHECK(g.is_contiguous() && m0.is_contiguous() && v0.is_contiguous(), "inputs must be contiguous");
+  const long long p = g.size(-1);
+  TORCH_CHECK(m0.numel() == p && v0.numel() == p, "moments must have one entry per column");
+  TORCH_CHECK(p % 4 == 0, "width must be a multiple of 4");
+  TORCH_CHECK(step >= 1, "step must be >= 1");
+  auto out = torch::empty_like(g);
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  bw::adam_direction(g.data_ptr<float>(), m0.data_ptr<float>(), v0.data_ptr<float>(), out.data_ptr<float>(),
+                     g.numel() / p, p, (float)b1, (float)b2, (float)(1.0 / bc1), (float)(1.0 / std::sqrt(bc2)),
+                     (float)eps, at::cuda::getCurrentCUDAStream());
+  return out;
 }
 
 Tensor rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
@@ -147,8 +244,13 @@ Tensor rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
   const int cols = (int)x.size(-1);
   const int rows = (int)(x.numel() / cols);
   auto dx = torch::empty_like(x);
-  bw::rmsnorm_bwd(bf(dy), bf(x), bf(w), rstd.data_ptr<float>(), bf(dx), rows, cols,
-                  at::cuda::getCurrentCUDAStream());
+  if (bw::rows_norm_supported(cols)) {
+    bw::RowsNormBwd a{bf(dy), bf(x), bf(w), rstd.data_ptr<float>(), nullptr, bf(dx), rows, cols};
+    bw::rows_norm_bwd(a, at::cuda::getCurrentCUDAStream());
+  } else {
+    bw::rmsnorm_bwd(bf(dy), bf(x), bf(w), rstd.data_ptr<float>(), bf(dx), rows, cols,
+                    at::cuda::getCurrentCUDAStream());
+  }
   return dx;
 }
 
@@ -200,6 +302,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd_acc", &rmsnorm_bwd_acc);
+  m.def("rope", &rope);
+  m.def("adam_direction", &adam_direction);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);

@@ -1,0 +1,272 @@
+// Row-parallel fused kernels of the decoder path, one warp per row with the row held in
+// registers (one HBM read and one write per element):
+//   * RMSNorm forward with an optional fused residual add  (h = x + delta; y = rms(h) * w),
+//   * RMSNorm backward with an optional fused residual-gradient add
+//     (dh = rms_bwd(dy) + dres -- the gradient both residual inputs receive),
+//   * rotary position embedding of q and k in one launch (forward rotates by +theta,
+//     backward by -theta; any (b, t, h) strides, head dim contiguous),
+//   * the per-sample Adam direction  m_hat / (sqrt(v_hat) + eps)  of a gradient block
+//     against the optimizer's moments (LESS preconditioning).
+// Arithmetic is fp32; bf16 only at loads and stores.
+#include <cuda_bf16.h>
+
+#include "rows.cuh"
+
+namespace bw {
+namespace {
+
+struct __align__(16) Bf8 {
+  __nv_bfloat162 h[4];
+};
+
+__device__ __forceinline__ void unpack8(const Bf8& v, float (&f)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p = __bfloat1622float2(v.h[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+__device__ __forceinline__ Bf8 pack8(const float (&f)[8]) {
+  Bf8 v;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v.h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kWarps = 8;  // rows per CTA
+
+// ------------------------------------------------------------------ RMSNorm fwd
+// Lane l owns 8-element vectors l, l+32, ..., l+32(kPer-1) of its row.
+template <int kPer>
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(
+    const Bf8* __restrict__ x, const Bf8* __restrict__ delta, Bf8* __restrict__ h, const Bf8* __restrict__ w,
+    Bf8* __restrict__ y, float* __restrict__ rstd, int rows, int nv, float inv_cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const long long base = row * nv;
+  Bf8 keep[kPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      Bf8 xv = x[base + v];
+      if (delta != nullptr) {
+        float a[8], b[8];
+        unpack8(xv, a);
+        unpack8(delta[base + v], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += b[j];
+        xv = pack8(a);  // the residual stream is bf16: normalise the rounded sum
+        h[base + v] = xv;
+      }
+      keep[i] = xv;
+      float f[8];
+      unpack8(xv, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss * inv_cols + eps);
+  if (lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float f[8], g[8];
+      unpack8(keep[i], f);
+      unpack8(w[v], g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+      y[base + v] = pack8(f);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ RMSNorm bwd
+// dx = r * (dy*w - xhat * mean(dy*w*xhat)) + dres,  xhat = x * r
+template <int kPer>
+__global__ void __launch_bounds__(kWarps * 32) rms_bwd_kernel(
+    const Bf8* __restrict__ dy, const Bf8* __restrict__ x, const Bf8* __restrict__ w,
+    const float* __restrict__ rstd, const Bf8* __restrict__ dres, Bf8* __restrict__ dx, int rows, int nv,
+    float inv_cols) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const long long base = row * nv;
+  const float r = rstd[row];
+  Bf8 kdy[kPer], kx[kPer];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      kdy[i] = dy[base + v];
+      kx[i] = x[base + v];
+      float a[8], b[8], c[8];
+      unpack8(kdy[i], a);
+      unpack8(kx[i], b);
+      unpack8(w[v], c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += a[j] * c[j] * b[j];
+    }
+  }
+  const float mean = warp_sum(dot) * r * inv_cols;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float a[8], b[8], c[8], o[8];
+      unpack8(kdy[i], a);
+      unpack8(kx[i], b);
+      unpack8(w[v], c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = r * (a[j] * c[j] - b[j] * r * mean);
+      if (dres != nullptr) {
+        float d[8];
+        unpack8(dres[base + v], d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += d[j];
+      }
+      dx[base + v] = pack8(o);
+    }
+  }
+}
+
+template <int kPer>
+void rms_fwd_launch(const RowsNorm& a, cudaStream_t s) {
+  const int nv = a.cols / 8;
+  const int grid = (a.rows + kWarps - 1) / kWarps;
+  rms_fwd_kernel<kPer><<<grid, kWarps * 32, 0, s>>>(
+      reinterpret_cast<const Bf8*>(a.x), reinterpret_cast<const Bf8*>(a.delta), reinterpret_cast<Bf8*>(a.h),
+      reinterpret_cast<const Bf8*>(a.w), reinterpret_cast<Bf8*>(a.y), a.rstd, a.rows, nv, 1.f / a.cols, a.eps);
+}
+
+template <int kPer>
+void rms_bwd_launch(const RowsNormBwd& a, cudaStream_t s) {
+  const int nv = a.cols / 8;
+  const int grid = (a.rows + kWarps - 1) / kWarps;
+  rms_bwd_kernel<kPer><<<grid, kWarps * 32, 0, s>>>(
+      reinterpret_cast<const Bf8*>(a.dy), reinterpret_cast<const Bf8*>(a.x), reinterpret_cast<const Bf8*>(a.w),
+      a.rstd, reinterpret_cast<const Bf8*>(a.dres), reinterpret_cast<Bf8*>(a.dx), a.rows, nv, 1.f / a.cols);
+}
+
+// ------------------------------------------------------------------ RoPE
+// Rows are (b, t, head) over q's heads then k's; each thread rotates 8 pairs
+// (x[c*8 .. c*8+8), x[half + c*8 ..)) of one row.
+__global__ void rope_kernel(RopeArgs a, float sign) {
+  const int chunks = a.head_dim / 16;
+  const int half = a.head_dim / 2;
+  const int heads = a.hq + a.hk;
+  const long long total = (long long)a.batch * a.seq * heads * chunks;
+  for (long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x; gid < total;
+       gid += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(gid % chunks);
+    long long rest = gid / chunks;
+    int head = (int)(rest % heads);
+    rest /= heads;
+    const int t = (int)(rest % a.seq);
+    const long long b = rest / a.seq;
+    const RopeTensor& T = head < a.hq ? a.q : a.k;
+    if (head >= a.hq) head -= a.hq;
+    const __nv_bfloat16* src = T.in + b * T.in_sb + t * T.in_st + head * T.in_sh;
+    __nv_bfloat16* dst = T.out + b * T.out_sb + t * T.out_st + head * T.out_sh;
+    float x1[8], x2[8], cs[8], sn[8];
+    unpack8(*reinterpret_cast<const Bf8*>(src + c * 8), x1);
+    unpack8(*reinterpret_cast<const Bf8*>(src + half + c * 8), x2);
+    const float4* cp = reinterpret_cast<const float4*>(a.cos + (long long)t * half + c * 8);
+    const float4* sp = reinterpret_cast<const float4*>(a.sin + (long long)t * half + c * 8);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+    float y1[8], y2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sj = sign * sn[j];
+      y1[j] = x1[j] * cs[j] - x2[j] * sj;
+      y2[j] = x2[j] * cs[j] + x1[j] * sj;
+    }
+    *reinterpret_cast<Bf8*>(dst + c * 8) = pack8(y1);
+    *reinterpret_cast<Bf8*>(dst + half + c * 8) = pack8(y2);
+  }
+}
+
+// ------------------------------------------------------------------ Adam direction
+// out[b, i] = (m / bc1) / (sqrt(v / bc2) + eps),  m = b1 m0 + (1-b1) g,  v = b2 v0 + (1-b2) g^2
+__global__ void adam_dir_kernel(const float4* __restrict__ g, const float4* __restrict__ m0,
+                                const float4* __restrict__ v0, float4* __restrict__ out, long long rows,
+                                long long p4, float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps) {
+  const long long total = rows * p4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long c = i % p4;
+    const float4 gv = g[i], mv = m0[c], vv = v0[c];
+    const float ga[4] = {gv.x, gv.y, gv.z, gv.w};
+    const float ma[4] = {mv.x, mv.y, mv.z, mv.w};
+    const float va[4] = {vv.x, vv.y, vv.z, vv.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float m = b1 * ma[j] + (1.f - b1) * ga[j];
+      const float v = b2 * va[j] + (1.f - b2) * ga[j] * ga[j];
+      o[j] = (m * inv_bc1) / (sqrtf(v) * inv_sqrt_bc2 + eps);
+    }
+    out[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+int grid_cap(long long work, int threads) {
+  const long long b = (work + threads - 1) / threads;
+  return (int)(b < 1 ? 1 : (b < 148 * 16 ? b : 148 * 16));
+}
+
+}  // namespace
+
+bool rows_norm_supported(int cols) { return cols % 8 == 0 && cols <= 32 * 8 * 16; }
+
+void rows_norm_fwd(const RowsNorm& a, cudaStream_t s) {
+  if (a.rows <= 0) return;
+  const int per = (a.cols / 8 + 31) / 32;
+  if (per <= 1) rms_fwd_launch<1>(a, s);
+  else if (per <= 2) rms_fwd_launch<2>(a, s);
+  else if (per <= 4) rms_fwd_launch<4>(a, s);
+  else if (per <= 8) rms_fwd_launch<8>(a, s);
+  else rms_fwd_launch<16>(a, s);
+}
+
+void rows_norm_bwd(const RowsNormBwd& a, cudaStream_t s) {
+  if (a.rows <= 0) return;
+  const int per = (a.cols / 8 + 31) / 32;
+  if (per <= 1) rms_bwd_launch<1>(a, s);
+  else if (per <= 2) rms_bwd_launch<2>(a, s);
+  else if (per <= 4) rms_bwd_launch<4>(a, s);
+  else if (per <= 8) rms_bwd_launch<8>(a, s);
+  else rms_bwd_launch<16>(a, s);
+}
+
+void rope(const RopeArgs& a, bool inverse, cudaStream_t s) {
+  const long long work = (long long)a.batch * a.seq * (a.hq + a.hk) * (a.head_dim / 16);
+  if (work <= 0) return;
+  rope_kernel<<<grid_cap(work, 256), 256, 0, s>>>(a, inverse ? -1.f : 1.f);
+}
+
+void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
+                    float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s) {
+  const long long p4 = p / 4;
+  if (rows <= 0 || p4 <= 0) return;
+  adam_dir_kernel<<<grid_cap(rows * p4, 256), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(m0), reinterpret_cast<const float4*>(v0),
+      reinterpret_cast<float4*>(out), rows, p4, b1, b2, inv_bc1, inv_sqrt_bc2, eps);
+}
+
+}  // namespace bw

@@ -1,0 +1,54 @@
+// Host interface of the warp-per-row decoder kernels (rows.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace bw {
+
+// y = rmsnorm(x [+ delta]) * w; with delta, h receives the bf16 sum x + delta.
+struct RowsNorm {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* delta;  // nullable
+  __nv_bfloat16* h;            // written iff delta != nullptr
+  const __nv_bfloat16* w;
+  __nv_bfloat16* y;
+  float* rstd;
+  int rows, cols;
+  float eps;
+};
+
+// dx = rmsnorm_bwd(dy; x, w, rstd) [+ dres]
+struct RowsNormBwd {
+  const __nv_bfloat16* dy;
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w;
+  const float* rstd;
+  const __nv_bfloat16* dres;  // nullable
+  __nv_bfloat16* dx;
+  int rows, cols;
+};
+
+// One rotated tensor: element (b, t, h, d) at in[b*in_sb + t*in_st + h*in_sh + d].
+struct RopeTensor {
+  const __nv_bfloat16* in;
+  __nv_bfloat16* out;
+  long long in_sb, in_st, in_sh;
+  long long out_sb, out_st, out_sh;
+};
+
+struct RopeArgs {
+  RopeTensor q, k;
+  const float* cos;  // (seq, head_dim / 2) fp32
+  const float* sin;
+  int batch, seq, hq, hk, head_dim;
+};
+
+bool rows_norm_supported(int cols);
+void rows_norm_fwd(const RowsNorm& a, cudaStream_t s);
+void rows_norm_bwd(const RowsNormBwd& a, cudaStream_t s);
+void rope(const RopeArgs& a, bool inverse, cudaStream_t s);
+void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
+                    float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s);
+
+}  // namespace bw

@@ -312,16 +312,20 @@ def _project_activation(buf, a, projector, share, source) -> _Projected:
                    and _token_major_ok(pm, a3))
     key = None
     if share is not None and a3.is_cuda:
-        # id() alone could be recycled by a later tensor once the input is freed (frozen
-        # layers do not save it for backward); the weak reference proves it is the same one.
-        key = (id(source), source._version, source.data_ptr(), tuple(source.shape), id(pm.matrix),
-               token_major)
+        # A module with full backward hooks sees its input through a per-module view
+        # (same storage, same version counter), so sibling layers (q/k/v, gate/up) are
+        # matched through the view's base.  id() alone could be recycled once the input is
+        # freed (frozen layers do not save it for backward); the weak reference to the
+        # base proves it is the same tensor.
+        root = source._base if source._base is not None else source
+        key = (id(root), source._version, source.data_ptr(), tuple(source.shape), tuple(source.stride()),
+               id(pm.matrix), token_major)
         hit = share.get(key)
-        if hit is not None and hit[0]() is source:
+        if hit is not None and hit[0]() is root:
             return hit[1]
     entry = _Projected(project_token_major(pm, a3) if token_major else pm(a3), token_major)
     if key is not None:
-        share.put(key, (weakref.ref(source), entry))
+        share.put(key, (weakref.ref(root), entry))
     return entry
 
 

@@ -69,7 +69,8 @@ def _adam(g, state, step, hp):
     from dattri_llm_b200 import ops as native_ops
 
     if (native_ops.use_native(g) and not hp["amsgrad"] and state.get("exp_avg") is not None
-            and state.get("exp_avg_sq") is not None):
+            and state.get("exp_avg_sq") is not None and g.shape[-1] % 4 == 0
+            and state["exp_avg"].numel() == g.shape[-1] == state["exp_avg_sq"].numel()):
         return native_ops.adam_direction(g, state["exp_avg"], state["exp_avg_sq"], step=step,
                                          beta1=b1, beta2=b2, eps=hp["eps"])
     m = _ema(_state(g, state, "exp_avg"), g, b1)

@@ -108,7 +108,20 @@ class RotaryEmbedding(nn.Module):
             freqs = torch.outer(t, self.inv_freq.to(device))
             emb = torch.cat([freqs, freqs], dim=-1)
             hit = (emb.cos().to(dtype), emb.sin().to(dtype))
-            self._cache = {key: hit}
+            self._cache = {k: v for k, v in self._cache.items() if k[0] == "half"}
+            self._cache[key] = hit
+        return hit
+
+    def half_tables(self, seq_len: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp32 ``cos``/``sin`` of the ``(T, d/2)`` distinct angles (the fused RoPE kernel's
+        tables; rotate-half repeats each angle in both halves)."""
+        key = ("half", seq_len, str(device))
+        hit = self._cache.get(key)
+        if hit is None:
+            t = torch.arange(seq_len, device=device, dtype=torch.float32)
+            freqs = torch.outer(t, self.inv_freq.to(device))
+            hit = (freqs.cos().contiguous(), freqs.sin().contiguous())
+            self._cache[key] = hit
         return hit
 
 
@@ -149,12 +162,19 @@ class LlamaAttention(nn.Module):
         self.v_proj = nn.Linear(d, self.n_kv * hd, bias=False)
         self.o_proj = nn.Linear(self.n_heads * hd, d, bias=False)
 
-    def forward(self, x: torch.Tensor, cos, sin, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, cos, sin, attention_mask: torch.Tensor | None = None,
+                half_tables: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+        from dattri_llm_b200.ops import fused
+
         b, t, _ = x.shape
-        q = self.q_proj(x).view(b, t, self.n_heads, self.head_dim).transpose(1, 2)
-        k = self.k_proj(x).view(b, t, self.n_kv, self.head_dim).transpose(1, 2)
+        q = self.q_proj(x).view(b, t, self.n_heads, self.head_dim)
+        k = self.k_proj(x).view(b, t, self.n_kv, self.head_dim)
         v = self.v_proj(x).view(b, t, self.n_kv, self.head_dim).transpose(1, 2)
-        q, k = apply_rope(q, k, cos, sin)
+        if half_tables is not None and fused.rope_enabled(q) and fused.rope_enabled(k):
+            q, k = fused.rope(q, k, *half_tables)
+            q, k = q.transpose(1, 2), k.transpose(1, 2)
+        else:
+            q, k = apply_rope(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
         gqa = self.n_kv != self.n_heads
         if attention_mask is None:
             y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=gqa)
@@ -195,6 +215,21 @@ class LlamaDecoderLayer(nn.Module):
     def forward(self, x, cos, sin, attention_mask=None):
         x = x + self.self_attn(self.input_layernorm(x), cos, sin, attention_mask)
         return x + self.mlp(self.post_attention_layernorm(x))
+
+    def forward_fused(self, x, pending, cos, sin, attention_mask=None, half_tables=None):
+        """The block with each residual add fused into the RMSNorm that reads it: returns
+        ``(h, m)`` whose sum is the block's output (the next block, or the final norm, adds
+        them).  *pending* is the previous block's ``m`` (``None`` for the first block)."""
+        from dattri_llm_b200.ops import fused
+
+        ln1, ln2 = self.input_layernorm, self.post_attention_layernorm
+        if pending is None:
+            n1, h0 = ln1(x), x
+        else:
+            n1, h0 = fused.add_rms_norm(x, pending, ln1.weight, ln1.eps)
+        a = self.self_attn(n1, cos, sin, attention_mask, half_tables)
+        n2, h = fused.add_rms_norm(h0, a, ln2.weight, ln2.eps)
+        return h, self.mlp(n2)
 
 
 class LlamaModel(nn.Module):
@@ -256,9 +291,32 @@ class LlamaForCausalLM(nn.Module):
         if self.frozen_probe and torch.is_grad_enabled() and not x.requires_grad:
             x = x.detach().requires_grad_(True)
         cos, sin = self.model.rotary_emb(input_ids.shape[1], x.device, x.dtype)
+        if not self._fused_blocks(x):
+            for layer in self.model.layers:
+                x = layer(x, cos, sin, attention_mask)
+            return self.model.norm(x)
+        half = self.model.rotary_emb.half_tables(input_ids.shape[1], x.device)
+        pending = None
         for layer in self.model.layers:
-            x = layer(x, cos, sin, attention_mask)
-        return self.model.norm(x)
+            x, pending = layer.forward_fused(x, pending, cos, sin, attention_mask, half)
+        if pending is None:
+            return self.model.norm(x)
+        from dattri_llm_b200.ops import fused
+
+        norm = self.model.norm
+        return fused.add_rms_norm(x, pending, norm.weight, norm.eps)[0]
+
+    def _fused_blocks(self, x: torch.Tensor) -> bool:
+        """Fused residual/norm blocks apply to bf16 sm_100 activations when no hook watches
+        a norm module or a decoder block (a capture of those layers needs their calls)."""
+        from dattri_llm_b200.ops import fused
+
+        if not fused.enabled(x) or x.shape[-1] > 4096:
+            return False
+        watched = (self.model.norm, *(m for layer in self.model.layers
+                                      for m in (layer, layer.input_layernorm, layer.post_attention_layernorm)))
+        return not any(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks or m._backward_pre_hooks
+                       for m in watched)
 
     def forward(self, input_ids: torch.Tensor, attention_mask: torch.Tensor | None = None,
                 labels: torch.Tensor | None = None, *, loss_reduction: str = "mean",

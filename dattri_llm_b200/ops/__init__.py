@@ -126,6 +126,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     matmul_tn,
 )
 from dattri_llm_b200.ops.gram import ghost_gram, per_sample_outer  # noqa: E402
+from dattri_llm_b200.ops.optim import adam_direction  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
 
 __all__ = [
@@ -133,6 +134,7 @@ __all__ = [
     "STORE_BF16",
     "STORE_BF16_T",
     "STORE_F32",
+    "adam_direction",
     "available",
     "check_device_errors",
     "count_launch",

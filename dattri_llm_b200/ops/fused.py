@@ -46,6 +46,67 @@ class _RMSNorm(torch.autograd.Function):
         return dx, dw, None
 
 
+class _AddRMSNorm(torch.autograd.Function):
+    """``h = x + delta`` (the bf16 residual stream) and ``y = rmsnorm(h) * w`` in one
+    pass; the backward adds the residual gradient into the norm's input gradient, which
+    both ``x`` and ``delta`` receive."""
+
+    @staticmethod
+    def forward(ctx, x, delta, w, eps):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+        y, h, rstd = native().add_rmsnorm_fwd(x.contiguous(), delta.contiguous(), w.contiguous(), float(eps))
+        ctx.save_for_backward(h, w, rstd)
+        return y, h
+
+    @staticmethod
+    def backward(ctx, dy, dh):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+        h, w, rstd = ctx.saved_tensors
+        if dy is None:
+            dy = torch.zeros_like(h)
+        dres = None if dh is None else dh.contiguous()
+        dx = native().rmsnorm_bwd_acc(dy.contiguous(), h, w.contiguous(), rstd, dres)
+        dw = None
+        if ctx.needs_input_grad[2]:
+            xhat = h.float() * rstd.view(*h.shape[:-1], 1)
+            dw = (dy.float() * xhat).reshape(-1, h.shape[-1]).sum(0).to(w.dtype)
+        return dx, dx, dw, None
+
+
+class _RoPE(torch.autograd.Function):
+    """Rotary position embedding of ``q (B, T, Hq, D)`` and ``k (B, T, Hk, D)`` with
+    fp32 ``cos``/``sin`` tables ``(T, D/2)``; the backward rotates by ``-theta``."""
+
+    @staticmethod
+    def forward(ctx, q, k, cos, sin):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+        ctx.save_for_backward(cos, sin)
+        ctx.q_shape, ctx.k_shape = q.shape, k.shape
+        qo, ko = native().rope(q, k, cos, sin, False)
+        return qo, ko
+
+    @staticmethod
+    def backward(ctx, dq, dk):
+        from dattri_llm_b200.ops import count_launch, native
+
+        count_launch()
+        cos, sin = ctx.saved_tensors
+        dq = torch.zeros(ctx.q_shape, dtype=torch.bfloat16, device=cos.device) if dq is None else dq
+        dk = torch.zeros(ctx.k_shape, dtype=torch.bfloat16, device=cos.device) if dk is None else dk
+        if dq.stride(-1) != 1:
+            dq = dq.contiguous()
+        if dk.stride(-1) != 1:
+            dk = dk.contiguous()
+        gq, gk = native().rope(dq, dk, cos, sin, True)
+        return gq, gk, None, None
+
+
 class _SwiGLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, g, u):
@@ -108,6 +169,25 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float | None) -> torch.
     if eps is None:
         eps = torch.finfo(x.dtype).eps
     return _RMSNorm.apply(x, weight, eps)
+
+
+def add_rms_norm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor,
+                 eps: float | None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(rmsnorm(x + delta) * weight, x + delta)`` in one fused pass."""
+    if eps is None:
+        eps = torch.finfo(x.dtype).eps
+    return _AddRMSNorm.apply(x, delta, weight, eps)
+
+
+def rope_enabled(q: torch.Tensor) -> bool:
+    """Whether the fused RoPE kernel applies to ``q (B, T, H, D)``."""
+    return (enabled(q) and q.dim() == 4 and q.shape[-1] % 16 == 0 and q.stride(-1) == 1
+            and all(st % 8 == 0 for st in q.stride()[:3]) and q.data_ptr() % 16 == 0)
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """Rotate ``q (B, T, Hq, D)``, ``k (B, T, Hk, D)`` by position (contiguous outputs)."""
+    return _RoPE.apply(q, k, cos, sin)
 
 
 def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:

@@ -52,3 +52,87 @@ def test_linear_cross_entropy_matches_fp32():
     torch.testing.assert_close(h.grad.float(), hr.grad, rtol=5e-2, atol=5e-2)
     torch.testing.assert_close(w.grad.float(), wr.grad, rtol=5e-2, atol=5e-2)
     ops.check_device_errors(h.device)
+
+
+@pytest.mark.parametrize("cols", [2048, 4096, 520])
+def test_add_rms_norm_forward_backward(cols):
+    x = torch.randn(45, cols, device="cuda").bfloat16().requires_grad_()
+    d = torch.randn(45, cols, device="cuda").bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(cols, device="cuda")).bfloat16().requires_grad_()
+    y, h = fused.add_rms_norm(x, d, w, 1e-5)
+    gy, gh = torch.randn_like(y), torch.randn_like(h)
+    (y.float() * gy.float()).sum().add_((h.float() * gh.float()).sum()).backward()
+    xr, dr, wr = (t.detach().float().requires_grad_() for t in (x, d, w))
+    hr = (xr + dr).bfloat16().float()  # the residual stream is bf16
+    hr.retain_grad()
+    yr = torch.nn.functional.rms_norm(hr, (cols,), wr, 1e-5)
+    (yr * gy.float()).sum().add_((hr * gh.float()).sum()).backward()
+    torch.testing.assert_close(h.float(), (xr + dr).detach(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(d.grad.float(), dr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(w.grad.float(), wr.grad, rtol=3e-2, atol=0.5)
+
+
+def _rope_ref(x, cos, sin):
+    """Rotate-half RoPE in fp32 on ``x (B, T, H, D)``."""
+    c = torch.cat([cos, cos], -1)[None, :, None, :]
+    s = torch.cat([sin, sin], -1)[None, :, None, :]
+    h = x.shape[-1] // 2
+    rot = torch.cat([-x[..., h:], x[..., :h]], -1)
+    return x * c + rot * s
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_rope_forward_backward(head_dim):
+    b, t, hq, hk = 3, 77, 8, 2
+    ang = torch.outer(torch.arange(t, device="cuda", dtype=torch.float32),
+                      1.0 / (10000 ** (torch.arange(0, head_dim, 2, device="cuda") / head_dim)))
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q = torch.randn(b, t, hq, head_dim, device="cuda").bfloat16().requires_grad_()
+    k = torch.randn(b, t, hk, head_dim, device="cuda").bfloat16().requires_grad_()
+    qo, ko = fused.rope(q, k, cos, sin)
+    # Gradients arrive strided, as from attention over (B, H, T, D) views.
+    gq = torch.randn(b, hq, t, head_dim, device="cuda").bfloat16().transpose(1, 2)
+    gk = torch.randn(b, hk, t, head_dim, device="cuda").bfloat16().transpose(1, 2)
+    torch.autograd.backward([qo, ko], [gq, gk])
+    qr, kr = q.detach().float().requires_grad_(), k.detach().float().requires_grad_()
+    qor, kor = _rope_ref(qr, cos, sin), _rope_ref(kr, cos, sin)
+    torch.autograd.backward([qor, kor], [gq.float(), gk.float()])
+    torch.testing.assert_close(qo.float(), qor, rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(ko.float(), kor, rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(q.grad.float(), qr.grad, rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(k.grad.float(), kr.grad, rtol=1e-2, atol=2e-2)
+
+
+def test_adam_direction_matches_formula():
+    g = torch.randn(6, 1000, device="cuda")
+    m0 = 0.1 * torch.randn(1000, device="cuda")
+    v0 = 0.01 * torch.rand(1000, device="cuda")
+    out = ops.adam_direction(g, m0, v0, step=3, beta1=0.9, beta2=0.999, eps=1e-8)
+    m = 0.9 * m0.double() + 0.1 * g.double()
+    v = 0.999 * v0.double() + 0.001 * g.double() ** 2
+    want = (m / (1 - 0.9**3)) / ((v / (1 - 0.999**3)).sqrt() + 1e-8)
+    torch.testing.assert_close(out.double(), want, rtol=1e-4, atol=1e-5)
+
+
+def test_llama_fused_blocks_match_unfused():
+    from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig.tiny(hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2)
+    model = LlamaForCausalLM(cfg, frozen_probe=True)
+    model.reset_parameters(seed=0)
+    model = model.cuda().bfloat16().requires_grad_(False)
+    ids = torch.randint(0, cfg.vocab_size, (2, 96), device="cuda")
+    outs = []
+    for fused_on in (True, False):
+        model._fused_blocks = (lambda _x: True) if fused_on else (lambda _x: False)
+        loss = model(input_ids=ids, labels=ids, loss_reduction="sum", return_logits=False).loss
+        emb = model.model.embed_tokens.weight
+        h = model.hidden_states(ids)
+        outs.append((float(loss), h.float()))
+        del emb
+    del model._fused_blocks
+    assert abs(outs[0][0] - outs[1][0]) / abs(outs[1][0]) < 2e-2
+    torch.testing.assert_close(outs[0][1], outs[1][1], rtol=5e-2, atol=5e-2)
+    ops.check_device_errors()
