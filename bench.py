@@ -247,6 +247,47 @@ class _TimedBlocks:
 
 
 # --------------------------------------------------------------------------- our arm
+class _Profiling:
+    """Optional profiling of the timed steps (off unless ``DATTRI_BENCH_PROFILE`` is set):
+    ``cuda`` brackets them with cudaProfilerStart/Stop (for ``ncu --profile-from-start off``,
+    which then sees every launch of those steps, the autograd thread's included);
+    ``torch`` runs them under ``torch.profiler`` and writes the per-kernel device-time table
+    and the device-busy fraction to ``DATTRI_BENCH_PROFILE_OUT`` (default
+    ``bench_profile.txt``).  A number printed by a profiled run is not a benchmark value."""
+
+    def __init__(self, mode: str) -> None:
+        self.mode, self._prof = mode, None
+
+    def start(self) -> None:
+        if self.mode == "cuda":
+            torch.cuda.profiler.start()
+        elif self.mode == "torch":
+            from torch.profiler import ProfilerActivity, profile
+
+            self._prof = profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA])
+            self._prof.__enter__()
+
+    def stop(self, rank: int) -> None:
+        if self.mode == "cuda":
+            torch.cuda.profiler.stop()
+        elif self._prof is not None:
+            self._prof.__exit__(None, None, None)
+            if rank == 0:
+                self._write(self._prof)
+
+    @staticmethod
+    def _write(prof) -> None:
+        kernels = [e for e in prof.events() if e.device_type.name == "CUDA"]
+        busy = sum(e.device_time for e in kernels)
+        t0 = min(e.time_range.start for e in kernels)
+        t1 = max(e.time_range.end for e in kernels)
+        table = prof.key_averages().table(sort_by="device_time_total", row_limit=60, max_name_column_width=90)
+        path = os.environ.get("DATTRI_BENCH_PROFILE_OUT", "bench_profile.txt")
+        with open(path, "w") as f:
+            f.write(f"device busy {busy / 1e3:.3f} ms over a {(t1 - t0) / 1e3:.3f} ms span "
+                    f"({100 * busy / max(t1 - t0, 1):.1f}%), {len(kernels)} kernels\n\n{table}\n")
+
+
 def run_ours(rank, world, local, steps, warmup):
     sys.path.insert(0, HERE)
     import dattri_llm_b200 as bw
@@ -323,13 +364,14 @@ def run_ours(rank, world, local, steps, warmup):
     clocks.start()
     launches0 = native_ops.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prof = _Profiling(os.environ.get("DATTRI_BENCH_PROFILE", ""))
+    prof.start()
     ev0.record()
     for i in range(warmup, warmup + steps):
-        torch.cuda.nvtx.range_push("timed_step")
         one_step(i)
-        torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
+    prof.stop(rank)
     _barrier(world)
     launches = native_ops.launch_count() - launches0
     clk = clocks.stop()

@@ -8,6 +8,9 @@
 #include <torch/extension.h>
 
 #include <cmath>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
 
 #include "gemm_tc.cuh"
 #include "ghost_gram.cuh"
@@ -87,6 +90,154 @@ void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t s
   p.err = err.data_ptr<int>();
   if (p.M == 0 || p.N == 0) return;
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
+}
+
+// C (bf16) = alpha * A @ B^T stored per segment: C is (S, N, T) with S * T = M rows of A.
+void gemm_tn_seg(Tensor A, Tensor B, Tensor C, double alpha, int64_t seg, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  TORCH_CHECK(a.batch == 1 && b.batch == 1, "gemm_tn_seg takes 2-D operands");
+  TORCH_CHECK(a.cols == b.cols, "A and B disagree on K");
+  TORCH_CHECK(seg > 0 && a.rows % seg == 0, "rows of A must be a multiple of the segment length");
+  TORCH_CHECK(C.scalar_type() == torch::kBFloat16 && C.is_contiguous() && C.dim() == 3 &&
+                  C.size(0) == a.rows / seg && C.size(1) == b.rows && C.size(2) == seg,
+              "C must be a contiguous (M / seg, N, seg) bf16 tensor");
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = (int)b.rows;
+  p.K = (int)a.cols;
+  p.batch = 1;
+  p.splits = 1;
+  p.b_shared = 1;
+  p.c_mode = bw::kStoreBF16TB;
+  p.alpha = (float)alpha;
+  p.C = C.data_ptr();
+  p.ldc = seg;
+  p.batch_stride_c = 0;
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
+}
+
+// ---- grouped GEMM: one launch for many same-shaped batched problems --------------------
+struct MapKey {
+  const void* ptr;
+  long long rows, cols, row_stride, batch, batch_stride;
+  int box;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && row_stride == o.row_stride &&
+           batch == o.batch && batch_stride == o.batch_stride && box == o.box;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.ptr);
+    for (long long v : {k.rows, k.cols, k.row_stride, k.batch, k.batch_stride, (long long)k.box})
+      h = h * 1000003u ^ std::hash<long long>()(v);
+    return h;
+  }
+};
+
+// Per-device job-table state: encoded maps, the device table, a pinned staging buffer.
+struct GroupState {
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+  std::vector<uint8_t> last;
+  Tensor dev;
+  uint8_t* host = nullptr;
+  size_t host_cap = 0;
+  cudaEvent_t copied = nullptr;
+};
+std::mutex g_group_mutex;
+std::unordered_map<int, GroupState> g_group;
+
+const CUtensorMap& cached_map(GroupState& st, const bw::GemmOperand& op, int box) {
+  MapKey k{op.ptr, op.rows, op.cols, op.row_stride, op.batch, op.batch_stride, box};
+  auto it = st.maps.find(k);
+  if (it != st.maps.end()) return it->second;
+  if (st.maps.size() > 8192) st.maps.clear();
+  return st.maps.emplace(k, bw::make_tmap_kmajor_bf16(op, box)).first->second;
+}
+
+// For every job i: C_i (op)= alpha * A_i @ B_i^T (batched over the leading axis; B_i may be
+// shared by the batch).  All jobs share M, N, K, batch and the store mode.  The job table is
+// re-uploaded (stream-ordered, same stream as the launch) only when it changed.
+void gemm_grouped(std::vector<Tensor> As, std::vector<Tensor> Bs, std::vector<Tensor> Cs, int64_t mode,
+                  double alpha, Tensor err) {
+  TORCH_CHECK(!As.empty() && As.size() == Bs.size() && As.size() == Cs.size(), "one A, B and C per job");
+  const c10::cuda::CUDAGuard guard(As[0].device());
+  check_err(err);
+  TORCH_CHECK(mode == bw::kStoreF32 || mode == bw::kStoreBF16, "grouped GEMM stores fp32 or bf16");
+  const int n = (int)As.size();
+  auto a0 = operand(As[0], "A");
+  auto b0 = operand(Bs[0], "B");
+  TORCH_CHECK(a0.cols == b0.cols, "A and B disagree on K");
+  TORCH_CHECK(b0.batch == 1 || b0.batch == a0.batch, "B batch must be 1 or equal A's");
+  const auto cdt = mode == bw::kStoreBF16 ? torch::kBFloat16 : torch::kFloat32;
+  bw::GemmParams p{};
+  p.M = (int)a0.rows;
+  p.N = (int)b0.rows;
+  p.K = (int)a0.cols;
+  p.batch = (int)a0.batch;
+  p.splits = 1;
+  p.b_shared = b0.batch == 1 ? 1 : 0;
+  p.c_mode = (int)mode;
+  p.alpha = (float)alpha;
+  p.ldc = Cs[0].stride(-2);
+  p.batch_stride_c = Cs[0].dim() == 3 ? Cs[0].stride(0) : 0;
+  p.err = err.data_ptr<int>();
+  const int bn = bw::pick_bn(p.N);
+  const int dev_idx = As[0].get_device();
+  std::lock_guard<std::mutex> lock(g_group_mutex);
+  GroupState& st = g_group[dev_idx];
+  // table: n jobs (32 B each), padded to 128 B, then 2n maps (128 B each)
+  const size_t jobs_bytes = ((size_t)n * sizeof(bw::GroupJob) + 127) / 128 * 128;
+  const size_t bytes = jobs_bytes + (size_t)2 * n * sizeof(CUtensorMap);
+  if (!st.dev.defined() || (size_t)st.dev.numel() < bytes) {
+    st.dev = torch::empty({(long long)(bytes * 2)}, As[0].options().dtype(torch::kUInt8));
+    st.last.clear();
+  }
+  uint8_t* dbase = st.dev.data_ptr<uint8_t>();
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dbase) % 128 == 0, "job table must be 128-byte aligned");
+  std::vector<uint8_t> table(bytes, 0);
+  auto* jobs = reinterpret_cast<bw::GroupJob*>(table.data());
+  auto* maps = reinterpret_cast<CUtensorMap*>(table.data() + jobs_bytes);
+  for (int i = 0; i < n; ++i) {
+    auto a = operand(As[i], "A");
+    auto b = operand(Bs[i], "B");
+    TORCH_CHECK(a.rows == a0.rows && a.cols == a0.cols && a.batch == a0.batch && b.rows == b0.rows &&
+                    b.cols == b0.cols && b.batch == b0.batch, "grouped jobs must share their shapes");
+    TORCH_CHECK(As[i].get_device() == dev_idx && Bs[i].get_device() == dev_idx && Cs[i].get_device() == dev_idx,
+                "grouped jobs must be on one device");
+    const Tensor& C = Cs[i];
+    TORCH_CHECK(C.scalar_type() == cdt && C.stride(-1) == 1 && C.size(-2) == p.M && C.size(-1) == p.N &&
+                    C.stride(-2) == p.ldc && (C.dim() == 3 ? C.stride(0) : 0) == p.batch_stride_c &&
+                    (p.batch == 1 || (C.dim() == 3 && C.size(0) == p.batch)),
+                "every C must be (batch, M, N) with the same strides and the store mode's dtype");
+    maps[2 * i] = cached_map(st, a, 128);
+    maps[2 * i + 1] = cached_map(st, b, bn);
+    jobs[i].ta = reinterpret_cast<const CUtensorMap*>(dbase + jobs_bytes + (size_t)(2 * i) * sizeof(CUtensorMap));
+    jobs[i].tb = reinterpret_cast<const CUtensorMap*>(dbase + jobs_bytes + (size_t)(2 * i + 1) * sizeof(CUtensorMap));
+    jobs[i].C = C.data_ptr();
+    jobs[i].pad = 0;
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (st.last != table) {
+    if (st.copied == nullptr) C10_CUDA_CHECK(cudaEventCreateWithFlags(&st.copied, cudaEventDisableTiming));
+    else C10_CUDA_CHECK(cudaEventSynchronize(st.copied));  // the staging buffer is free again
+    if (st.host_cap < bytes) {
+      if (st.host != nullptr) C10_CUDA_CHECK(cudaFreeHost(st.host));
+      C10_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&st.host), bytes * 2, cudaHostAllocDefault));
+      st.host_cap = bytes * 2;
+    }
+    std::memcpy(st.host, table.data(), bytes);
+    C10_CUDA_CHECK(cudaMemcpyAsync(dbase, st.host, bytes, cudaMemcpyHostToDevice, stream));
+    C10_CUDA_CHECK(cudaEventRecord(st.copied, stream));
+    st.last.swap(table);
+  }
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_grouped_launch(reinterpret_cast<const bw::GroupJob*>(dbase), n, p, bn, stream);
 }
 
 // out[i][j] += sum over token pairs of (a1 . a2)(g1 . g2); factors flattened to rows.
@@ -204,7 +355,8 @@ std::vector<Tensor> rope(Tensor q, Tensor k, Tensor cos, Tensor sin, bool invers
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && q.size(0) == k.size(0) && q.size(1) == k.size(1) &&
                   q.size(3) == k.size(3), "q and k must be (B, T, H, D) with matching B, T, D");
   const int D = (int)q.size(3);
-  TORCH_CHECK(D % 16 == 0, "head dim must be a multiple of 16");
+  TORCH_CHECK(bw::rope_supported(D, (int)(q.size(2) + k.size(2))),
+              "fused RoPE needs head_dim % 16 == 0 and (q heads + k heads) * head_dim / 16 <= 1024");
   TORCH_CHECK(cos.scalar_type() == torch::kFloat32 && sin.scalar_type() == torch::kFloat32 &&
                   cos.is_contiguous() && sin.is_contiguous() && cos.dim() == 2 && cos.size(1) == D / 2 &&
                   cos.size(0) >= q.size(1) && sin.sizes() == cos.sizes(),
@@ -299,6 +451,8 @@ void ce_bwd_inplace(Tensor logits, Tensor lse, Tensor target, Tensor gscale) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
+  m.def("gemm_tn_seg", &gemm_tn_seg, "A @ B^T stored per segment as (S, N, T) bf16");
+  m.def("gemm_grouped", &gemm_grouped, "one launch for many same-shaped batched A @ B^T problems");
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

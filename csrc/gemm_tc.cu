@@ -35,12 +35,15 @@ struct Cfg {
   static constexpr int kStages = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 4));
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem = kStages * (kTileA + kTileB) + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kRed = BM * BN * 4;  // cluster split-K: the peer's fp32 partial tile
+  static constexpr bool kClusterOK = kSmem + kRed <= 227 * 1024;
 };
 
+// One CTA's 128 x BN output tile of batch (za, zb) -> output batch zc at Cbase.  The tensor
+// maps may live in kernel parameters or in global memory (grouped launches).
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   GemmParams p) {
+__device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmParams& p,
+                                         int za, int zb, int zc, int split, void* Cbase) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
@@ -56,9 +59,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
   const int m0 = blockIdx.y * BM;
-  const int z = blockIdx.z / p.splits;
-  const int split = blockIdx.z % p.splits;
-  const int zb = p.b_shared ? 0 : z;
 
   const int kblocks = (p.K + BK - 1) / BK;
   const int per = (kblocks + p.splits - 1) / p.splits;
@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nk = max(0, kb1 - kb0);
 
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(tmA);
+    tma_prefetch_desc(tmB);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -91,8 +91,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&empty[s], ph ^ 1, p.err, kErrWaitEmpty)) break;
       mbar_arrive_expect_tx(&full[s], C::kTileA + C::kTileB);
       const int kc = (kb0 + i) * BK;
-      tma_load_3d(sA + s * C::kTileA, &tmA, &full[s], kc, m0, z);
-      tma_load_3d(sB + s * C::kTileB, &tmB, &full[s], kc, n0, zb);
+      tma_load_3d(sA + s * C::kTileA, tmA, &full[s], kc, m0, za);
+      tma_load_3d(sB + s * C::kTileB, tmB, &full[s], kc, n0, zb);
       issued = i + 1;
     }
     // Never leave with a bulk copy still landing in this CTA's shared memory.
@@ -124,8 +124,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row = m0 + warp * 32 + lane;
   const bool row_ok = row < p.M;
   const float alpha = p.alpha;
+  // Cluster split-K: the peer CTA (rank 1) writes its fp32 partial tile into rank 0's shared
+  // memory (column-major, so a warp's 32 rows are 32 consecutive words), then both meet at a
+  // cluster barrier and rank 0 stores the sum.
+  const bool clustered = p.cluster_k > 1;
+  const uint32_t crank = clustered ? cluster_ctarank() : 0u;
+  float* red = reinterpret_cast<float*>(smem + C::kStages * (C::kTileA + C::kTileB) + 256);
+  const int red_row = warp * 32 + lane;
+  if (clustered && crank != 0) {
+    const uint32_t dst = map_shared_rank(smem_u32(red), 0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t r[32];
+      if (nk > 0) {
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        tmem_ld_wait();
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < BN - c0) st_cluster_f32(dst + (uint32_t)(((c0 + j) * BM + red_row) * 4),
+                                        (nk > 0 && ok) ? __uint_as_float(r[j]) : 0.f);
+    }
+  }
+  if (clustered) {
+    __syncwarp();
+    cluster_sync_all();
+  }
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
+    if (clustered && crank != 0) break;
     uint32_t r[32];
     if (nk > 0) {
       tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
@@ -134,10 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 32; ++j) r[j] = 0u;
     }
+    if (clustered) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < BN - c0) r[j] = __float_as_uint(__uint_as_float(r[j]) + red[(c0 + j) * BM + red_row]);
+    }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
     if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
-      float* Cz = static_cast<float*>(p.C) + (long long)z * p.batch_stride_c +
+      float* Cz = static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
                   (long long)row * p.ldc;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -151,20 +183,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (p.c_mode == kStoreBF16) {
-      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(p.C) + (long long)z * p.batch_stride_c +
+      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
                           (long long)row * p.ldc;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = nbase + j;
         if (j < BN - c0 && n < p.N) Cz[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
       }
-    } else {  // kStoreBF16T: C^T[z][n][m]; consecutive lanes hit consecutive m (coalesced)
-      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(p.C) + (long long)z * p.batch_stride_c;
+    } else if (p.c_mode == kStoreBF16T) {  // C^T[z][n][m]; consecutive lanes hit consecutive m
+      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = nbase + j;
         if (j < BN - c0 && n < p.N)
           Cz[(long long)n * p.ldc + row] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+      }
+    } else {  // kStoreBF16TB: rows are (segment, t); element (m, n) -> C[m / T][n][m % T], T = ldc
+      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                          (long long)(row / p.ldc) * p.N * p.ldc + row % p.ldc;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) Cz[(long long)n * p.ldc] = __float2bfloat16(alpha * __uint_as_float(r[j]));
       }
     }
   }
@@ -172,6 +212,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmParams p) {
+  const int z = blockIdx.z / p.splits;
+  const int split = blockIdx.z % p.splits;
+  gemm_cta<BN>(&tmA, &tmB, p, z, p.b_shared ? 0 : z, z, split, p.C);
+}
+
+// Grouped launch: CTA z serves job z / batch, batch z % batch of that job; every job has
+// the same M, N, K, batch and store mode, its own operands (tensor maps in global memory,
+// 64-byte aligned, written before the launch) and output.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_grouped_kernel(const GroupJob* __restrict__ jobs, GemmParams p) {
+  const int job = blockIdx.z / p.batch;
+  const int b = blockIdx.z % p.batch;
+  const GroupJob j = jobs[job];
+  gemm_cta<BN>(j.ta, j.tb, p, b, p.b_shared ? 0 : b, b, 0, j.C);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -201,14 +261,66 @@ void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
   cudaGetDevice(&dev);
   if (!(configured >> dev & 1ull)) {
     cudaFuncSetAttribute(gemm_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         C::kSmem);
+                         C::kClusterOK ? C::kSmem + C::kRed : C::kSmem);
     configured |= 1ull << dev;
   }
-  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch * p.splits);
-  gemm_tn_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, tb, p);
+  GemmParams q = p;
+  // A skinny problem (few output tiles, long K) leaves most SMs idle: split K over a
+  // 2-CTA cluster that sums through distributed shared memory (no atomics, no extra pass).
+  const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM) * p.batch;
+  const int kblocks = (p.K + BK - 1) / BK;
+  q.cluster_k = 1;
+  if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 && tiles * 2 <= 160 && kblocks >= 8) {
+    q.cluster_k = 2;
+    q.splits = 2;
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch * q.splits);
+  if (q.cluster_k == 1) {
+    gemm_tn_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, tb, q);
+    return;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem + C::kRed;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 2;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemm_tn_kernel<BN>, ta, tb, q);
+}
+
+template <int BN>
+void launch_grouped_bn(const GroupJob* jobs, int n_jobs, const GemmParams& p, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(gemm_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    configured |= 1ull << dev;
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, n_jobs * p.batch);
+  gemm_grouped_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(jobs, p);
 }
 
 }  // namespace
+
+void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream) {
+  p.splits = 1;
+  switch (bn) {
+    case 16: launch_grouped_bn<16>(jobs, n_jobs, p, stream); break;
+    case 32: launch_grouped_bn<32>(jobs, n_jobs, p, stream); break;
+    case 64: launch_grouped_bn<64>(jobs, n_jobs, p, stream); break;
+    case 128: launch_grouped_bn<128>(jobs, n_jobs, p, stream); break;
+    case 256: launch_grouped_bn<256>(jobs, n_jobs, p, stream); break;
+    default: throw std::runtime_error("gemm_grouped: unsupported tile width");
+  }
+}
 
 CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows) {
   CUtensorMap map;

@@ -12,6 +12,8 @@ enum GemmStore : int {
   kStoreBF16 = 1,   // C (bf16) = alpha * AB^T
   kAtomicF32 = 2,   // C (fp32) += alpha * AB^T with atomics (split-K / cross-CTA sums)
   kStoreBF16T = 3,  // C^T (bf16): element (m, n) lands at C[z][n * ldc + m]
+  kStoreBF16TB = 4, // per-segment C^T (bf16): rows are (s, t) with T = ldc rows per segment;
+                    // element (m, n) lands at C[z][m / T][n][m % T] (a (S, N, T) block)
 };
 
 // A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).
@@ -36,9 +38,19 @@ struct GemmParams {
   long long ldc;
   long long batch_stride_c;
   int* err;
+  int cluster_k;   // >1: the split-K CTAs of a tile form a cluster and sum over DSMEM (set by the launcher)
+};
+
+// One job of a grouped launch (tensor maps in global memory, 64-byte aligned).
+struct GroupJob {
+  const CUtensorMap* ta;
+  const CUtensorMap* tb;
+  void* C;
+  long long pad;
 };
 
 CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows);
+void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream);
 int pick_bn(int N);
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream);

@@ -41,7 +41,7 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-constexpr int kWarps = 8;  // rows per CTA
+constexpr int kWarps = 4;  // rows per CTA
 
 // ------------------------------------------------------------------ RMSNorm fwd
 // Lane l owns 8-element vectors l, l+32, ..., l+32(kPer-1) of its row.
@@ -94,9 +94,11 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(
 }
 
 // ------------------------------------------------------------------ RMSNorm bwd
-// dx = r * (dy*w - xhat * mean(dy*w*xhat)) + dres,  xhat = x * r
+// dx = r * (dy*w - xhat * mean(dy*w*xhat)) + dres,  xhat = x * r.  dy and x stay packed in
+// registers; dres is prefetched into L2 before the reduction and read after it, which keeps
+// the register count low enough for 4 CTAs (16 warps) per SM.
 template <int kPer>
-__global__ void __launch_bounds__(kWarps * 32) rms_bwd_kernel(
+__global__ void __launch_bounds__(kWarps * 32, kPer <= 8 ? 4 : 2) rms_bwd_kernel(
     const Bf8* __restrict__ dy, const Bf8* __restrict__ x, const Bf8* __restrict__ w,
     const float* __restrict__ rstd, const Bf8* __restrict__ dres, Bf8* __restrict__ dx, int rows, int nv,
     float inv_cols) {
@@ -106,13 +108,20 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_kernel(
   const long long base = row * nv;
   const float r = rstd[row];
   Bf8 kdy[kPer], kx[kPer];
-  float dot = 0.f;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int v = lane + 32 * i;
     if (v < nv) {
       kdy[i] = dy[base + v];
       kx[i] = x[base + v];
+      if (dres != nullptr) asm volatile("prefetch.global.L2 [%0];" ::"l"(dres + base + v));
+    }
+  }
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
       float a[8], b[8], c[8];
       unpack8(kdy[i], a);
       unpack8(kx[i], b);
@@ -162,42 +171,57 @@ void rms_bwd_launch(const RowsNormBwd& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ RoPE
-// Rows are (b, t, head) over q's heads then k's; each thread rotates 8 pairs
-// (x[c*8 .. c*8+8), x[half + c*8 ..)) of one row.
-__global__ void rope_kernel(RopeArgs a, float sign) {
-  const int chunks = a.head_dim / 16;
-  const int half = a.head_dim / 2;
-  const int heads = a.hq + a.hk;
-  const long long total = (long long)a.batch * a.seq * heads * chunks;
-  for (long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x; gid < total;
-       gid += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(gid % chunks);
-    long long rest = gid / chunks;
-    int head = (int)(rest % heads);
-    rest /= heads;
-    const int t = (int)(rest % a.seq);
-    const long long b = rest / a.seq;
-    const RopeTensor& T = head < a.hq ? a.q : a.k;
-    if (head >= a.hq) head -= a.hq;
-    const __nv_bfloat16* src = T.in + b * T.in_sb + t * T.in_st + head * T.in_sh;
-    __nv_bfloat16* dst = T.out + b * T.out_sb + t * T.out_st + head * T.out_sh;
-    float x1[8], x2[8], cs[8], sn[8];
-    unpack8(*reinterpret_cast<const Bf8*>(src + c * 8), x1);
-    unpack8(*reinterpret_cast<const Bf8*>(src + half + c * 8), x2);
-    const float4* cp = reinterpret_cast<const float4*>(a.cos + (long long)t * half + c * 8);
-    const float4* sp = reinterpret_cast<const float4*>(a.sin + (long long)t * half + c * 8);
-    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
-    cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-    float y1[8], y2[8];
+// A CTA covers kTok consecutive tokens of one sequence; thread (head, chunk) rotates 8 pairs
+// (x[c*8 .. c*8+8), x[half + c*8 ..)) of its head in each of those tokens.  Consecutive
+// threads read consecutive 16-byte vectors (coalesced), and each thread issues all kTok
+// tokens' loads before any arithmetic.
+constexpr int kTok = 4;
+
+__global__ void __launch_bounds__(1024) rope_kernel(RopeArgs a, float sign) {
+  const int chunks = a.head_dim >> 4;
+  const int half = a.head_dim >> 1;
+  const int per_token = (a.hq + a.hk) * chunks;
+  const int i = threadIdx.x;
+  if (i >= per_token) return;
+  int head = i / chunks;
+  const int c = i - head * chunks;
+  const bool is_q = head < a.hq;
+  if (!is_q) head -= a.hq;
+  const RopeTensor T = is_q ? a.q : a.k;
+  const long long b = blockIdx.y;
+  const int t0 = blockIdx.x * kTok;
+  const __nv_bfloat16* src = T.in + b * T.in_sb + (long long)head * T.in_sh + c * 8;
+  __nv_bfloat16* dst = T.out + b * T.out_sb + (long long)head * T.out_sh + c * 8;
+  Bf8 v1[kTok], v2[kTok];
+#pragma unroll
+  for (int u = 0; u < kTok; ++u) {
+    if (t0 + u < a.seq) {
+      const __nv_bfloat16* p = src + (long long)(t0 + u) * T.in_st;
+      v1[u] = *reinterpret_cast<const Bf8*>(p);
+      v2[u] = *reinterpret_cast<const Bf8*>(p + half);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kTok; ++u) {
+    const int t = t0 + u;
+    if (t >= a.seq) break;
+    const float4* ct = reinterpret_cast<const float4*>(a.cos + (long long)t * half + c * 8);
+    const float4* st = reinterpret_cast<const float4*>(a.sin + (long long)t * half + c * 8);
+    const float4 c0 = ct[0], c1 = ct[1], s0 = st[0], s1 = st[1];
+    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float x1[8], x2[8], y1[8], y2[8];
+    unpack8(v1[u], x1);
+    unpack8(v2[u], x2);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float sj = sign * sn[j];
       y1[j] = x1[j] * cs[j] - x2[j] * sj;
       y2[j] = x2[j] * cs[j] + x1[j] * sj;
     }
-    *reinterpret_cast<Bf8*>(dst + c * 8) = pack8(y1);
-    *reinterpret_cast<Bf8*>(dst + half + c * 8) = pack8(y2);
+    __nv_bfloat16* q = dst + (long long)t * T.out_st;
+    *reinterpret_cast<Bf8*>(q) = pack8(y1);
+    *reinterpret_cast<Bf8*>(q + half) = pack8(y2);
   }
 }
 
@@ -255,10 +279,13 @@ void rows_norm_bwd(const RowsNormBwd& a, cudaStream_t s) {
 }
 
 void rope(const RopeArgs& a, bool inverse, cudaStream_t s) {
-  const long long work = (long long)a.batch * a.seq * (a.hq + a.hk) * (a.head_dim / 16);
-  if (work <= 0) return;
-  rope_kernel<<<grid_cap(work, 256), 256, 0, s>>>(a, inverse ? -1.f : 1.f);
+  const int per_token = (a.hq + a.hk) * (a.head_dim / 16);
+  if ((long long)a.batch * a.seq * per_token <= 0) return;
+  const int threads = ((per_token + 31) / 32) * 32;
+  rope_kernel<<<dim3((a.seq + kTok - 1) / kTok, a.batch), threads, 0, s>>>(a, inverse ? -1.f : 1.f);
 }
+
+bool rope_supported(int head_dim, int heads) { return head_dim % 16 == 0 && heads * (head_dim / 16) <= 1024; }
 
 void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
                     float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s) {

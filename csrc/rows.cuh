@@ -48,6 +48,7 @@ bool rows_norm_supported(int cols);
 void rows_norm_fwd(const RowsNorm& a, cudaStream_t s);
 void rows_norm_bwd(const RowsNormBwd& a, cudaStream_t s);
 void rope(const RopeArgs& a, bool inverse, cudaStream_t s);
+bool rope_supported(int head_dim, int heads);  // heads = q heads + k heads
 void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
                     float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s);
 

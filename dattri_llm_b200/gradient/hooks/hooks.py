@@ -105,12 +105,25 @@ class _Projected:
         self.a, self.token_major = a, token_major
 
 
+class _DeferredOuter:
+    """A layer's per-sample ``g_p^T a_p`` awaiting the step's grouped launch; stands in
+    the layer's buffer until :meth:`_StepShare.flush_outer` replaces it with the result."""
+
+    __slots__ = ("a", "g", "result")
+
+    def __init__(self, g: torch.Tensor, a: torch.Tensor) -> None:
+        self.g, self.a, self.result = g, a, None
+
+
 class _StepShare:
-    """Per-step cache of activation projections shared by layers that read the same
-    input tensor (q/k/v, gate/up).  Cleared by the manager at every step end."""
+    """Per-step state shared by a manager's hooks: the activation projections shared by
+    layers that read the same input tensor (q/k/v, gate/up), and the deferred per-sample
+    outer products that one grouped tcgen05 launch computes at step end.  Cleared by the
+    manager at every step end."""
 
     def __init__(self) -> None:
         self._store: dict = {}
+        self._outer: list[_DeferredOuter] = []
         self._lock = threading.Lock()
 
     def get(self, key):
@@ -121,9 +134,44 @@ class _StepShare:
         with self._lock:
             self._store[key] = value
 
+    def defer_outer(self, g_pt: torch.Tensor, a_pt: torch.Tensor) -> _DeferredOuter:
+        """Queue ``(B, k_g, k_a) = g_pt a_pt^T`` (token-major ``(B, k, T)`` operands)."""
+        job = _DeferredOuter(g_pt, a_pt)
+        with self._lock:
+            self._outer.append(job)
+        return job
+
+    def flush_outer(self) -> None:
+        """Run every queued outer product, one grouped launch per operand shape."""
+        from dattri_llm_b200 import ops as native_ops
+
+        with self._lock:
+            jobs, self._outer = self._outer, []
+        groups: dict = {}
+        for j in jobs:
+            key = (tuple(j.g.shape), tuple(j.a.shape), j.g.device, j.g.dtype)
+            groups.setdefault(key, []).append(j)
+        for (gs, as_, dev, dt), grp in groups.items():
+            out = torch.empty(len(grp), gs[0], gs[1], as_[1], dtype=dt, device=dev)
+            native_ops.gemm_grouped([j.g for j in grp], [j.a for j in grp], list(out.unbind(0)),
+                                    mode=native_ops.STORE_BF16)
+            flat = out.reshape(len(grp), gs[0], -1)
+            for i, j in enumerate(grp):
+                j.result = flat[i]
+
+    @staticmethod
+    def resolve(parts: list) -> None:
+        """Replace finished :class:`_DeferredOuter` stand-ins in a buffer's part list."""
+        for i, (dev, part) in enumerate(parts):
+            if isinstance(part, _DeferredOuter):
+                if part.result is None:
+                    raise RuntimeError("a deferred outer product was never flushed")
+                parts[i] = (dev, part.result)
+
     def clear(self) -> None:
         with self._lock:
             self._store.clear()
+            self._outer.clear()
 
 
 def register_linear_io_hooks(
@@ -173,7 +221,7 @@ def register_linear_io_hooks(
             _forward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
                           on_layer_forward)))
         handles.append(module.register_full_backward_hook(
-            _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed,
+            _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
                            on_layer_backward)))
     return buffers, handles
 
@@ -220,7 +268,7 @@ def _forward_hook(name, buffers, projector, preconditioner, offload, routed, sha
     return hook
 
 
-def _backward_hook(name, buffers, projector, preconditioner, offload, routed, callback):
+def _backward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback):
     def hook(_module, _grad_input, grad_output):
         g = grad_output[0].detach()
         dev = _device_index(grad_output[0])
@@ -245,7 +293,7 @@ def _backward_hook(name, buffers, projector, preconditioner, offload, routed, ca
             buf["grad_output"] = g
             emit = g
         else:
-            matched, g_p = _capture_projected(buf, g, dev, projector, offload, preconditioner, name)
+            matched, g_p = _capture_projected(buf, g, dev, projector, offload, preconditioner, name, share)
             if not matched:
                 _warn_orphan_backward(name)
                 return
@@ -298,9 +346,7 @@ def project_token_major(pm: ops.ProjectionMatrix, x: torch.Tensor) -> torch.Tens
 
     b, t, _ = x.shape
     flat = x.reshape(b * t, x.shape[-1])
-    out_t = torch.empty(pm.proj_dim, b * t, dtype=torch.bfloat16, device=x.device)
-    native_ops.gemm_tn(flat, pm.matrix_t, out_t, mode=native_ops.STORE_BF16_T)
-    return out_t.view(pm.proj_dim, b, t).permute(1, 0, 2)
+    return native_ops.gemm_tn_seg(flat, pm.matrix_t, t)
 
 
 def _project_activation(buf, a, projector, share, source) -> _Projected:
@@ -354,7 +400,7 @@ def _keep_factors(buf: LayerBuffer, seq_len: int, k_a: int, k_g: int) -> bool:
     return not ops.should_materialize(buf["_capture_style"], seq_len, k_a, k_g)
 
 
-def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name):
+def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name, share=None):
     """Pair *g* with its forward and store the projected / materialized / preconditioned
     capture.  Returns ``(matched, projected g to hand the callbacks or None)``."""
     with buf["_lock"]:
@@ -393,6 +439,11 @@ def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_na
 
                 g_pt = project_token_major(pm_g, g3)
                 b = g_pt.shape[0]
+                if share is not None and not offload:
+                    # The per-sample outer product g_p^T a_p of every layer of the step runs
+                    # in one grouped launch at step end (StepShare.flush_outer).
+                    keep_dense(share.defer_outer(g_pt, entry.a))
+                    return True, g_pt.transpose(1, 2)
                 dense = torch.empty(b, pm_g.proj_dim, entry.a.shape[1], dtype=g3.dtype, device=g3.device)
                 native_ops.gemm_tn(g_pt, entry.a, dense, mode=native_ops.STORE_BF16)
                 keep_dense(dense.reshape(b, -1))

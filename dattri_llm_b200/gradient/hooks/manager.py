@@ -483,7 +483,15 @@ class HookManager:
                 grads[pos].append((dev, part))
         return list(zip(acts, grads, projs, strict=True))
 
+    def _flush_deferred(self) -> None:
+        """Run the step's deferred per-sample outer products and put their results in place."""
+        self._share.flush_outer()
+        for buf in self._buffers.values():
+            with buf["_lock"]:
+                _StepShare.resolve(buf["_proj_parts"])
+
     def _assemble_gradient(self) -> Gradient:
+        self._flush_deferred()
         data, rep, types, idx = {}, {}, {}, {}
         for lname, buf in self._buffers.items():
             if buf["_fwd_fires"] == 0:
@@ -583,6 +591,7 @@ class HookManager:
     # ------------------------------------------------------------------ state
     def save_state(self) -> dict:
         """Snapshot of the in-flight step (for a secondary pass through the same hooks)."""
+        self._flush_deferred()
         return {
             "layer_buffers": {n: {
                 "_act_parts": list(b["_act_parts"]), "_grad_parts": list(b["_grad_parts"]),

@@ -170,7 +170,8 @@ class LlamaAttention(nn.Module):
         q = self.q_proj(x).view(b, t, self.n_heads, self.head_dim)
         k = self.k_proj(x).view(b, t, self.n_kv, self.head_dim)
         v = self.v_proj(x).view(b, t, self.n_kv, self.head_dim).transpose(1, 2)
-        if half_tables is not None and fused.rope_enabled(q) and fused.rope_enabled(k):
+        if (half_tables is not None and fused.rope_enabled(q) and fused.rope_enabled(k)
+                and (self.n_heads + self.n_kv) * self.head_dim // 16 <= 1024):
             q, k = fused.rope(q, k, *half_tables)
             q, k = q.transpose(1, 2), k.transpose(1, 2)
         else:

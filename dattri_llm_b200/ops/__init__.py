@@ -122,7 +122,9 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     STORE_BF16,
     STORE_BF16_T,
     STORE_F32,
+    gemm_grouped,
     gemm_tn,
+    gemm_tn_seg,
     matmul_tn,
 )
 from dattri_llm_b200.ops.gram import ghost_gram, per_sample_outer  # noqa: E402
@@ -139,7 +141,9 @@ __all__ = [
     "check_device_errors",
     "count_launch",
     "error_word",
+    "gemm_grouped",
     "gemm_tn",
+    "gemm_tn_seg",
     "launch_count",
     "ghost_gram",
     "matmul_tn",

@@ -85,3 +85,36 @@ def matmul_tn(
     mode = STORE_BF16 if out_dtype == torch.bfloat16 else STORE_F32
     gemm_tn(a2, b, out, alpha=alpha, mode=mode)
     return out
+
+
+def gemm_tn_seg(a: torch.Tensor, b: torch.Tensor, seg: int, *, alpha: float = 1.0,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``(a @ b^T)`` of ``a (S*seg, K)`` and ``b (N, K)`` stored per segment as a contiguous
+    ``(S, N, seg)`` bf16 tensor -- the token-major ``(B, k, T)`` layout of a projected
+    activation, each sample's ``(k, T)`` block contiguous."""
+    from dattri_llm_b200.ops import count_launch, error_word, native
+
+    a = _k_aligned(a)
+    b = _k_aligned(b)
+    s = a.shape[0] // seg
+    if out is None:
+        out = torch.empty(s, b.shape[0], seg, dtype=torch.bfloat16, device=a.device)
+    count_launch()
+    native().gemm_tn_seg(a, b, out, float(alpha), int(seg), error_word(a.device))
+    return out
+
+
+def gemm_grouped(a: list[torch.Tensor], b: list[torch.Tensor], out: list[torch.Tensor], *,
+                 mode: int = STORE_BF16, alpha: float = 1.0) -> list[torch.Tensor]:
+    """``out[i] = alpha * a[i] @ b[i]^T`` for every job ``i`` in ONE launch (each ``a[i]``
+    ``(Z, M, K)``, ``b[i]`` ``(Z, N, K)`` or ``(N, K)``; every job the same shapes).  The job
+    table lives on the device and is re-uploaded only when it changes; use one stream per
+    device for these calls."""
+    from dattri_llm_b200.ops import count_launch, error_word, native
+
+    if not a:
+        return out
+    count_launch()
+    native().gemm_grouped([_k_aligned(x) for x in a], [_k_aligned(x) for x in b], out, int(mode), float(alpha),
+                          error_word(a[0].device))
+    return out

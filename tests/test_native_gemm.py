@@ -83,3 +83,59 @@ def test_per_sample_outer_matches_bmm():
     got = ops.per_sample_outer(left, right)
     ref = torch.bmm(left.double().transpose(1, 2), right.double()).float()
     torch.testing.assert_close(got, ref, rtol=1e-3, atol=1e-2)
+
+
+def test_gemm_tn_seg_layout():
+    b, t, d, k = 3, 96, 256, 64
+    x = torch.randn(b * t, d, device="cuda").bfloat16()
+    p = torch.randn(k, d, device="cuda").bfloat16()
+    out = ops.gemm_tn_seg(x, p, t)
+    assert out.shape == (b, k, t) and out.is_contiguous()
+    want = (x.float() @ p.float().T).view(b, t, k).transpose(1, 2)
+    torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-1)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("shared_b", [False, True])
+@pytest.mark.parametrize("mode", ["bf16", "f32"])
+def test_gemm_grouped_matches_per_job(shared_b, mode):
+    jobs, z, m, n, kk = 5, 4, 64, 48, 320
+    a = [torch.randn(z, m, kk, device="cuda").bfloat16() for _ in range(jobs)]
+    b = [torch.randn(n, kk, device="cuda").bfloat16() if shared_b else torch.randn(z, n, kk, device="cuda").bfloat16()
+         for _ in range(jobs)]
+    dt = torch.bfloat16 if mode == "bf16" else torch.float32
+    out = torch.full((jobs, z, m, n), float("nan"), device="cuda", dtype=dt)
+    store = ops.STORE_BF16 if mode == "bf16" else ops.STORE_F32
+    for _ in range(2):  # the second call reuses the uploaded job table
+        ops.gemm_grouped(a, b, list(out.unbind(0)), mode=store)
+        for i in range(jobs):
+            bi = b[i].float() if b[i].dim() == 3 else b[i].float().expand(z, n, kk)
+            want = a[i].float() @ bi.transpose(1, 2)
+            torch.testing.assert_close(out[i].float(), want, rtol=2e-2, atol=2e-1)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("mode", ["f32", "f32acc", "bf16", "bf16t", "seg"])
+@pytest.mark.parametrize(("m", "n", "k"), [(8192, 64, 2048), (1000, 32, 1032), (4096, 128, 640)])
+def test_skinny_cluster_split_k(mode, m, n, k):
+    """Few output tiles and a long K take the 2-CTA cluster split-K path (DSMEM reduction)."""
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    b = torch.randn(n, k, device="cuda").bfloat16()
+    want = a.float() @ b.float().T
+    if mode == "seg":
+        t = 8 if m % 8 == 0 else 1
+        out = ops.gemm_tn_seg(a, b, t).float()
+        got = out.transpose(1, 2).reshape(m, n)
+    elif mode in ("f32", "f32acc"):
+        out = torch.ones(m, n, device="cuda") if mode == "f32acc" else torch.empty(m, n, device="cuda")
+        ops.gemm_tn(a, b, out, mode=ops.STORE_F32, accumulate=mode == "f32acc")
+        got = out - 1 if mode == "f32acc" else out
+    elif mode == "bf16":
+        out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        got = ops.gemm_tn(a, b, out, mode=ops.STORE_BF16).float()
+    else:
+        out = torch.empty(n, m, device="cuda", dtype=torch.bfloat16)
+        got = ops.gemm_tn(a, b, out, mode=ops.STORE_BF16_T).float().T
+    tol = 2e-2 if mode in ("bf16", "bf16t", "seg") else 1e-3
+    torch.testing.assert_close(got, want, rtol=tol, atol=tol * float(want.abs().max()))
+    ops.check_device_errors()
