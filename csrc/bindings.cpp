@@ -9,6 +9,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <string>
 #include <mutex>
 #include <unordered_map>
 
@@ -17,6 +18,8 @@
 #include "fused.cuh"
 #include "kernels.cuh"
 #include "rows.cuh"
+#include "score_ag.cuh"
+#include "peer_sync.cuh"
 
 namespace {
 
@@ -240,6 +243,89 @@ void gemm_grouped(std::vector<Tensor> As, std::vector<Tensor> Bs, std::vector<Te
   bw::gemm_grouped_launch(reinterpret_cast<const bw::GroupJob*>(dbase), n, p, bn, stream);
 }
 
+// ---- fused all-gather + score GEMM ------------------------------------------------------
+// Device copies of the peers' tensor maps, keyed by the peers' buffer addresses (symmetric
+// buffers are allocated once, so each distinct table is encoded and uploaded once).
+struct PeerTables {
+  std::mutex mu;
+  std::unordered_map<std::string, Tensor> tables;
+};
+PeerTables g_peer_tables;
+
+// out (M, world * R) += alpha * test @ [X_0; ...; X_{world-1}]^T, where X_r = peers[r] is rank
+// r's (R, K) bf16 block read over NVLink (peer-mapped symmetric memory).  out is fp32 and
+// accumulated (the caller zeroes it).
+void ag_score(Tensor test, std::vector<Tensor> peers, Tensor out, double alpha, int64_t splits, Tensor err) {
+  const c10::cuda::CUDAGuard guard(test.device());
+  check_err(err);
+  auto t = operand(test, "test");
+  TORCH_CHECK(t.batch == 1, "test must be 2-D");
+  TORCH_CHECK(!peers.empty(), "at least one peer block");
+  const int world = (int)peers.size();
+  std::string key;
+  std::vector<bw::GemmOperand> ops;
+  for (int r = 0; r < world; ++r) {
+    auto o = operand(peers[r], "peer block");
+    TORCH_CHECK(o.batch == 1 && o.cols == t.cols, "peer blocks must be (R, K) with the test's K");
+    TORCH_CHECK(o.rows == operand(peers[0], "peer block").rows, "peer blocks must have one row count");
+    TORCH_CHECK(o.rows % 8 == 0, "peer blocks need a multiple of 8 rows");
+    ops.push_back(o);
+    key += std::to_string(reinterpret_cast<uintptr_t>(o.ptr)) + ":" + std::to_string(o.rows) + ":" +
+           std::to_string(o.cols) + ":" + std::to_string(o.row_stride) + ";";
+  }
+  const int R = (int)ops[0].rows;
+  TORCH_CHECK(bw::ag_score_tile_n(world * R) > 0, "world * rows per peer must be <= 128");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.dim() == 2 && out.stride(1) == 1 &&
+                  out.size(0) == t.rows && out.size(1) == (long long)world * R,
+              "out must be (M, world * R) fp32 with contiguous rows");
+  Tensor table;
+  {
+    std::lock_guard<std::mutex> lock(g_peer_tables.mu);
+    key += "dev" + std::to_string(test.get_device());
+    auto it = g_peer_tables.tables.find(key);
+    if (it == g_peer_tables.tables.end()) {
+      std::vector<CUtensorMap> maps;
+      for (auto& o : ops) maps.push_back(bw::make_tmap_kmajor_bf16(o, R));
+      auto host = torch::empty({(long long)(maps.size() * sizeof(CUtensorMap))}, torch::kUInt8);
+      std::memcpy(host.data_ptr(), maps.data(), maps.size() * sizeof(CUtensorMap));
+      table = host.to(test.device());  // synchronous upload, once per distinct table
+      TORCH_CHECK(reinterpret_cast<uintptr_t>(table.data_ptr()) % 64 == 0, "tensor-map table must be 64-byte aligned");
+      g_peer_tables.tables.emplace(key, table);
+    } else {
+      table = it->second;
+    }
+  }
+  const int kblocks = (int)((t.cols + 63) / 64);
+  int sp = (int)std::max<int64_t>(1, std::min<int64_t>(splits, kblocks));
+  const int per = (kblocks + sp - 1) / sp;
+  sp = (kblocks + per - 1) / per;  // every split owns at least one K block
+  bw::AgScoreParams p{};
+  p.M = (int)t.rows;
+  p.K = (int)t.cols;
+  p.world = world;
+  p.rows_per_peer = R;
+  p.splits = sp;
+  p.alpha = (float)alpha;
+  p.out = out.data_ptr<float>();
+  p.ldo = out.stride(0);
+  p.err = err.data_ptr<int>();
+  if (p.M == 0) return;
+  const CUtensorMap tmT = bw::make_tmap_kmajor_bf16(t, 128);
+  bw::ag_score_launch(tmT, reinterpret_cast<const CUtensorMap*>(table.data_ptr()), p,
+                      at::cuda::getCurrentCUDAStream());
+}
+
+// Cross-GPU barrier: flag_ptrs is a device int64 tensor of the ranks' flag-array addresses.
+void peer_barrier(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, Tensor err) {
+  const c10::cuda::CUDAGuard guard(flag_ptrs.device());
+  check_err(err);
+  TORCH_CHECK(flag_ptrs.is_cuda() && flag_ptrs.scalar_type() == torch::kInt64 && flag_ptrs.numel() == world,
+              "flag_ptrs must be a CUDA int64 tensor with one address per rank");
+  TORCH_CHECK(world >= 1 && world <= 1024 && rank >= 0 && rank < world, "bad rank / world");
+  bw::peer_barrier(reinterpret_cast<int* const*>(flag_ptrs.data_ptr<int64_t>()), (int)rank, (int)world,
+                   (int)epoch, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
 // out[i][j] += sum over token pairs of (a1 . a2)(g1 . g2); factors flattened to rows.
 void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t S2, Tensor out,
                 Tensor err) {
@@ -454,6 +540,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_seg", &gemm_tn_seg, "A @ B^T stored per segment as (S, N, T) bf16");
   m.def("gemm_grouped", &gemm_grouped, "one launch for many same-shaped batched A @ B^T problems");
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
+  m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
+  m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);

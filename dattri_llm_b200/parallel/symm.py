@@ -1,21 +1,84 @@
-"""Peer-memory collectives over NVLink 5 / NVSwitch (single node, sm_100).
+"""Peer-memory building blocks over NVLink 5 / NVSwitch (one process per GPU, one node).
 
-Buffers are allocated in PyTorch symmetric memory
-(``torch.distributed._symmetric_memory``), which maps every rank's buffer into
-every other rank's address space; the library's kernels then read and write peer
-memory directly (plain P2P loads/stores, no TMA multicast), synchronizing ranks
-with bounded-wait flags that report a timeout instead of hanging.
+Buffers live in PyTorch symmetric memory (``torch.distributed._symmetric_memory``),
+which maps every rank's buffer into every other rank's address space.  The library's
+own kernels then read peer memory directly -- TMA tile loads without cluster multicast,
+or plain loads/stores -- and ranks meet at :class:`PeerBarrier`, a one-CTA kernel whose
+wait is bounded (a lost peer sets the device error word instead of hanging the GPU).
 
-:func:`all_reduce_sum_` returns ``False`` when the fused path does not apply
-(gloo / CPU tensors / one GPU / symmetric memory unavailable), so callers fall
-back to ``dist.all_reduce``.
+:func:`available` says whether this path applies (NCCL process group, CUDA tensors on
+sm_100, world size > 1, symmetric memory importable); callers fall back to
+``torch.distributed`` collectives otherwise.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
+
+
+def available(device: torch.device | None = None) -> bool:
+    """Whether peer-memory kernels can run for the default process group."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() < 2:
+        return False
+    if dist.get_backend() != "nccl" or not torch.cuda.is_available():
+        return False
+    import importlib.util
+
+    if importlib.util.find_spec("torch.distributed._symmetric_memory") is None:
+        return False
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return torch.cuda.get_device_capability(dev)[0] == 10
+
+
+def _group_name(group) -> str:
+    group = group if group is not None else dist.group.WORLD
+    return group.group_name
+
+
+class SymmetricBuffer:
+    """One tensor in symmetric memory plus every peer's view of it."""
+
+    def __init__(self, shape: tuple[int, ...], dtype: torch.dtype, device: torch.device, group=None) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.local = symm_mem.empty(*shape, dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.local, _group_name(group))
+        self.world = self.handle.world_size
+        self.rank = self.handle.rank
+        self.peers = [self.handle.get_buffer(r, tuple(shape), dtype) for r in range(self.world)]
+
+
+class PeerBarrier:
+    """Epoch barrier across the group's GPUs on peer-mapped int32 flags (bounded wait).
+
+    ``wait()`` enqueues the barrier on the current stream: everything this rank enqueued
+    before it is visible to peers once they pass it, and this rank's later work starts
+    after every peer arrived.  Create it on every rank, collectively."""
+
+    def __init__(self, device: torch.device, group=None) -> None:
+        self._flags = SymmetricBuffer((_world(group),), torch.int32, device, group)
+        self._flags.local.zero_()
+        self._ptrs = torch.tensor([int(p.data_ptr()) for p in self._flags.peers], dtype=torch.int64, device=device)
+        self._epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def wait(self) -> None:
+        from dattri_llm_b200.ops import count_launch, error_word, native
+
+        self._epoch += 1
+        count_launch()
+        native().peer_barrier(self._ptrs, self._flags.rank, self._flags.world, self._epoch,
+                              error_word(self._ptrs.device))
+
+
+def _world(group) -> int:
+    return dist.get_world_size(group) if group is not None else dist.get_world_size()
 
 
 def all_reduce_sum_(t: torch.Tensor) -> bool:
-    """In-place SUM over ranks through the NVLink kernel; ``False`` if not applicable."""
+    """In-place SUM over ranks through peer memory; ``False`` when the path does not apply
+    (the caller then uses ``dist.all_reduce``).  Large reductions go to NCCL, whose NVLS
+    all-reduce already reaches the switch's in-network reduction."""
     return False

@@ -1,0 +1,66 @@
+"""Peer-memory kernels on 2+ GPUs (one process per GPU, NCCL): the bounded cross-GPU
+barrier and the fused all-gather + score GEMM against NCCL all-gather + fp32 matmul.
+Skipped with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from dattri_llm_b200 import ops
+        from dattri_llm_b200.parallel.score import AllGatherScorer
+
+        rows, k, n_local = 8, 4160, 200
+        gen = torch.Generator(device=dev).manual_seed(100 + rank)
+        test = torch.randn(n_local, k, device=dev, generator=gen).bfloat16()
+        scorer = AllGatherScorer(test, rows)
+        worst = 0.0
+        for step in range(3):
+            block = torch.randn(rows, k, device=dev, generator=gen).bfloat16()
+            got = scorer.score(block)
+            gathered = [torch.empty_like(block) for _ in range(world)]
+            dist.all_gather(gathered, block)
+            want = test.float() @ torch.cat(gathered).float().T
+            err = float((got - want).abs().max() / want.abs().max())
+            worst = max(worst, err)
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        results[rank] = worst
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_allgather_score_matches_nccl():
+    world = 2
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(errs.values()) < 1e-2, errs
