@@ -20,6 +20,7 @@
 #include "rows.cuh"
 #include "score_ag.cuh"
 #include "peer_sync.cuh"
+#include "allreduce_p2p.cuh"
 
 namespace {
 
@@ -326,6 +327,32 @@ void peer_barrier(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, 
                    (int)epoch, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
 }
 
+// Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
+std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
+  TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
+  std::vector<const float*> ptrs;
+  for (auto& t : peers) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous() && t.numel() >= n,
+                "peer buffers must be contiguous fp32 CUDA tensors holding n elements");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "peer buffers must be 16-byte aligned");
+    ptrs.push_back(t.data_ptr<float>());
+  }
+  return ptrs;
+}
+
+void allreduce_phase(std::vector<Tensor> peers, Tensor out, int64_t n, int64_t phase, int64_t rank) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(n % 4 == 0, "n must be a multiple of 4");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() >= n &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out must be aligned contiguous fp32");
+  auto ptrs = peer_floats(peers, n);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int world = (int)ptrs.size();
+  if (phase == 0) bw::allreduce_oneshot(ptrs.data(), world, out.data_ptr<float>(), n, stream);
+  else if (phase == 1) bw::allreduce_reduce_scatter(ptrs.data(), world, (int)rank, out.data_ptr<float>(), n, stream);
+  else bw::allreduce_all_gather(ptrs.data(), world, out.data_ptr<float>(), n, stream);
+}
+
 // out[i][j] += sum over token pairs of (a1 . a2)(g1 . g2); factors flattened to rows.
 void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t S2, Tensor out,
                 Tensor err) {
@@ -542,6 +569,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
+  m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);

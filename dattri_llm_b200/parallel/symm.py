@@ -77,8 +77,59 @@ def _world(group) -> int:
     return dist.get_world_size(group) if group is not None else dist.get_world_size()
 
 
+_ONESHOT_BYTES = 1 << 20
+_STAGING: dict = {}
+
+
+class _Staging:
+    """A growable symmetric fp32 staging buffer and its barrier, per device."""
+
+    def __init__(self, device: torch.device, n: int) -> None:
+        self.buf = SymmetricBuffer((n,), torch.float32, device)
+        self.barrier = PeerBarrier(device)
+        self.capacity = n
+
+
+def _staging(device: torch.device, n: int) -> _Staging:
+    st = _STAGING.get(device)
+    if st is None or st.capacity < n:
+        # Every rank reduces the same size, so every rank grows here together (collective).
+        st = _Staging(device, max(n, 1 << 20, 2 * (st.capacity if st else 0)))
+        _STAGING[device] = st
+    return st
+
+
 def all_reduce_sum_(t: torch.Tensor) -> bool:
-    """In-place SUM over ranks through peer memory; ``False`` when the path does not apply
-    (the caller then uses ``dist.all_reduce``).  Large reductions go to NCCL, whose NVLS
-    all-reduce already reaches the switch's in-network reduction."""
-    return False
+    """In-place SUM of an fp32 CUDA tensor over the default group through NVLink peer
+    memory; ``False`` when the path does not apply (the caller then uses
+    ``dist.all_reduce``).  Up to 1 MiB one shot (every rank reads every peer's buffer);
+    above, reduce-scatter + all-gather (each rank reduces its slice, then copies the
+    others' from their owners).  Bounded barriers separate the phases."""
+    if t.dtype != torch.float32 or not t.is_cuda or not available(t.device):
+        return False
+    world = dist.get_world_size()
+    if world > 16:
+        return False
+    from dattri_llm_b200.ops import count_launch, native
+
+    n = t.numel()
+    n4 = (n + 3) // 4 * 4
+    st = _staging(t.device, n4)
+    local = st.buf.local
+    local[:n].copy_(t.reshape(-1))
+    if n4 > n:
+        local[n:n4].zero_()
+    rank = st.buf.rank
+    out = torch.empty(n4, dtype=torch.float32, device=t.device)
+    st.barrier.wait()
+    if n4 * 4 <= _ONESHOT_BYTES:
+        count_launch()
+        native().allreduce_phase(st.buf.peers, out, n4, 0, rank)
+    else:
+        count_launch(2)
+        native().allreduce_phase(st.buf.peers, local, n4, 1, rank)
+        st.barrier.wait()
+        native().allreduce_phase(st.buf.peers, out, n4, 2, rank)
+    st.barrier.wait()  # no rank refills its staging buffer while a peer still reads it
+    t.copy_(out[:n].view_as(t))
+    return True

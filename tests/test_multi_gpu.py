@@ -47,6 +47,15 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             want = test.float() @ torch.cat(gathered).float().T
             err = float((got - want).abs().max() / want.abs().max())
             worst = max(worst, err)
+        # NVLink peer all-reduce (one-shot and reduce-scatter + all-gather) against NCCL.
+        from dattri_llm_b200.parallel import symm
+
+        for n in (1000, 3 * (1 << 20) + 5):
+            x = torch.randn(n, device=dev, generator=gen)
+            want = x.clone()
+            dist.all_reduce(want)
+            assert symm.all_reduce_sum_(x)
+            worst = max(worst, float((x - want).abs().max() / want.abs().max()))
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         results[rank] = worst
@@ -56,7 +65,7 @@ def _worker(rank: int, world: int, port: int, results) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_allgather_score_matches_nccl():
+def test_fused_allgather_score_and_peer_allreduce_match_nccl():
     world = 2
     with mp.Manager() as m:
         results = m.dict()
