@@ -323,6 +323,7 @@ class GradientStreamer(GradientSource):
         self._collect_ctx = None
         self._pass_state: _ProbePassState | None = None
         self._hasher: ThreadPoolExecutor | None = None
+        self._host_ids_ok: bool | None = None  # host batch hash == manager's model-input hash
 
     args = property(lambda self: self._args, doc="The run configuration.")
     model = property(lambda self: self._model, doc="The unwrapped model.")
@@ -430,7 +431,7 @@ class GradientStreamer(GradientSource):
             self._end_probe_pass()
             raise
         ids = None
-        hashable = _host_hashable(host_batch)
+        hashable = _host_hashable(host_batch) if self._host_ids_ok is not False else None
         if (hashable and self._hm.sample_id_key is None and self._hm.sample_hash_fields is None
                 and self._hasher is not None):
             ids = self._hasher.submit(hash_batch, hashable)
@@ -445,11 +446,16 @@ class GradientStreamer(GradientSource):
         self._hm.reset_steps(self._index)
         if self._hm.supports_preconditioning:
             self._hm.precondition = self._precondition
+        host_ids = None
         if ids is not None:
             try:
-                self._hm.set_sample_ids(ids.result())
+                host_ids = ids.result()
             except ValueError:
-                self._hm.set_sample_ids(None)
+                host_ids = None
+            # The host hash stands in for the manager's hash of the model's inputs only once
+            # the first step has shown the two agree (the loss_fn may feed the model a subset
+            # of the batch's fields); until then the manager hashes.
+            self._hm.set_sample_ids(host_ids if self._host_ids_ok else None)
         self._forward_backward(batch)
         if self.enable_update:
             self._lrs[self._index] = float(self._optimizer.param_groups[0]["lr"])
@@ -468,6 +474,8 @@ class GradientStreamer(GradientSource):
             raise RuntimeError(f"Step desync: HookManager captured step {record.step} but the streamer is on "
                                f"batch {self._index}. Exactly one capture step is expected per streamed batch.")
         hashes = list(record.input_hash) if isinstance(record.input_hash, list) else [record.input_hash]
+        if self._host_ids_ok is None and host_ids is not None:
+            self._host_ids_ok = list(host_ids) == hashes
         if self._pass_state is not None and not self._pass_state.holds_grads:
             self._fwd.zero_grad(set_to_none=True)
         step = self._index if self.enable_update else self._checkpoint_step

@@ -369,3 +369,75 @@ class TestTrajectoryLive:
         after = task.load_checkpoint(0).state_dict()
         for k, v in before.items():
             torch.testing.assert_close(after[k], v)
+
+
+def _same_scores(a, b) -> None:
+    """Equal per-step score rows, aligned by train id and test id."""
+    assert sorted(set(a.row_steps)) == sorted(set(b.row_steps))
+    for step in set(a.row_steps):
+        ids_a, ma = a.step_matrix(step)
+        ids_b, mb = b.step_matrix(step)
+        assert sorted(ids_a) == sorted(ids_b)
+        ca = [a.test_index[h] for h in a.test_ids]
+        cb = [b.test_index[h] for h in a.test_ids]
+        mb = mb[[ids_b.index(h) for h in ids_a]]
+        torch.testing.assert_close(mb[:, cb], ma[:, ca], rtol=1e-4, atol=1e-6)
+
+
+class TestRecompute:
+    def test_snapshot_replay_equals_stored_trajectory(self, tmp_path):
+        """``recompute_gradients=True`` stores parameters + batches and replays the
+        gradients at attribution time; the scores equal the stored-gradient run."""
+        hc = HookManagerConfig(linear_io=[r"mlp\."])
+        stored, train, test, _ = _live(tmp_path, DVEmbAttributor, "stored", optim="sgd")
+        a = stored.attribute(train, test, hook_config=hc, learning_rate=0.05)
+        replay, train, test, _ = _live(tmp_path, DVEmbAttributor, "replay", optim="sgd", recompute_gradients=True)
+        b = replay.attribute(train, test, hook_config=hc, learning_rate=0.05)
+        _same_scores(a, b)
+
+    def test_adamw_replay_equals_stored(self, tmp_path):
+        hc = HookManagerConfig(linear_io=[r"mlp\."])
+        stored, train, test, _ = _live(tmp_path, AdamWInfluenceAttributor, "s", adam_epsilon=0.1)
+        a = stored.attribute(train, test, hook_config=hc)
+        replay, train, test, _ = _live(tmp_path, AdamWInfluenceAttributor, "r", adam_epsilon=0.1,
+                                       recompute_gradients=True)
+        b = replay.attribute(train, test, hook_config=hc)
+        _same_scores(a, b)
+
+
+class TestLiveAttribute:
+    @pytest.mark.parametrize("residency", ["disk", "memory"])
+    def test_tracin_live_equals_cached(self, tmp_path, residency):
+        model = tiny.make_model()
+        xtr, ytr, xte, yte = tiny.make_data()
+        task = AttributionTask(tiny.sq_loss, model, checkpoints=[{k: v.clone() for k, v in model.state_dict().items()}])
+        args = _args(tmp_path / "o", per_device_train_batch_size=4, per_device_eval_batch_size=4)
+        hc = HookManagerConfig(linear_io=[r"mlp\."])
+        live = TracInAttributor(args, task=task).attribute(tiny.as_dataset(xtr, ytr), tiny.as_dataset(xte, yte),
+                                                           hook_config=hc, gradient_cache_residency=residency)
+        model.load_state_dict(task.checkpoints[0])
+        want = tiny.per_sample_grads(model, xtr, ytr) @ tiny.per_sample_grads(model, xte, yte).T
+        torch.testing.assert_close(_matrix(live, tiny.hashes(xtr, ytr), tiny.hashes(xte, yte)), want,
+                                   rtol=1e-4, atol=1e-4)
+
+    def test_token_granularity_sums_to_instance(self, tmp_path):
+        """Per-token scores of a train sample sum to its instance score (TracIn)."""
+        torch.manual_seed(0)
+        model = torch.nn.Sequential()
+        model.add_module("fc", torch.nn.Linear(6, 3))
+        x = torch.randn(4, 5, 6)
+        data = [{"x": x[i]} for i in range(4)]
+
+        def loss_fn(m, b):
+            return m(b["x"]).pow(2).sum()
+
+        task = AttributionTask(loss_fn, model)
+        args = _args(tmp_path / "o", per_device_train_batch_size=2, per_device_eval_batch_size=2)
+        hc = HookManagerConfig(linear_io=[r"^fc$"])
+        inst = TracInAttributor(args, task=task).attribute(data, data[:2], hook_config=hc)
+        tok = TracInAttributor(_args(tmp_path / "t", per_device_train_batch_size=2, per_device_eval_batch_size=2),
+                               task=task).attribute(data, data[:2], hook_config=hc, attribution_granularity="token")
+        for h in inst.train_ids:
+            for step in set(inst.row_steps):
+                _pos, per_tok = tok.token_scores(h, step)
+                torch.testing.assert_close(per_tok.sum(0), inst.trajectory_agnostic(h), rtol=1e-4, atol=1e-5)

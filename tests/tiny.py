@@ -52,8 +52,9 @@ def hashes(x: torch.Tensor, y: torch.Tensor) -> list[str]:
 
 
 def sq_loss(model, batch) -> torch.Tensor:
-    """Sum over the batch of the squared error (each sample's loss is independent)."""
-    return ((model(x=batch["x"]) - batch["y"]) ** 2).sum()
+    """Sum over the batch of the squared error (each sample's loss is independent).  The
+    model receives both fields, so the manager's hash of its inputs covers ``{x, y}``."""
+    return ((model(x=batch["x"], y=batch["y"]) - batch["y"]) ** 2).sum()
 
 
 def per_sample_grads(model: nn.Module, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
