@@ -152,7 +152,11 @@ struct GroupState {
   uint8_t* host = nullptr;
   size_t host_cap = 0;
   cudaEvent_t copied = nullptr;
+  std::vector<Tensor> graph_tables;  // tables captured into CUDA graphs (kept for their replays)
+  uint8_t* graph_arena = nullptr;    // pinned copy sources of captured tables (never rewritten)
+  size_t graph_arena_used = 0;
 };
+constexpr size_t kGraphArena = 8u << 20;
 std::mutex g_group_mutex;
 std::unordered_map<int, GroupState> g_group;
 
@@ -198,11 +202,13 @@ void gemm_grouped(std::vector<Tensor> As, std::vector<Tensor> Bs, std::vector<Te
   // table: n jobs (32 B each), padded to 128 B, then 2n maps (128 B each)
   const size_t jobs_bytes = ((size_t)n * sizeof(bw::GroupJob) + 127) / 128 * 128;
   const size_t bytes = jobs_bytes + (size_t)2 * n * sizeof(CUtensorMap);
-  if (!st.dev.defined() || (size_t)st.dev.numel() < bytes) {
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  C10_CUDA_CHECK(cudaStreamIsCapturing(at::cuda::getCurrentCUDAStream(), &capturing));
+  if (capturing == cudaStreamCaptureStatusNone && (!st.dev.defined() || (size_t)st.dev.numel() < bytes)) {
     st.dev = torch::empty({(long long)(bytes * 2)}, As[0].options().dtype(torch::kUInt8));
     st.last.clear();
   }
-  uint8_t* dbase = st.dev.data_ptr<uint8_t>();
+  uint8_t* dbase = st.dev.defined() ? st.dev.data_ptr<uint8_t>() : nullptr;
   TORCH_CHECK(reinterpret_cast<uintptr_t>(dbase) % 128 == 0, "job table must be 128-byte aligned");
   std::vector<uint8_t> table(bytes, 0);
   auto* jobs = reinterpret_cast<bw::GroupJob*>(table.data());
@@ -227,6 +233,32 @@ void gemm_grouped(std::vector<Tensor> As, std::vector<Tensor> Bs, std::vector<Te
     jobs[i].pad = 0;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (capturing != cudaStreamCaptureStatusNone) {
+    // Inside a CUDA-graph capture: the graph gets its own table (device memory from the
+    // graph's pool, kept alive with the graph's lifetime by this process) uploaded by a
+    // captured copy from a pinned host buffer that is never rewritten.
+    Tensor dev = torch::empty({(long long)bytes}, As[0].options().dtype(torch::kUInt8));
+    uint8_t* gbase = dev.data_ptr<uint8_t>();
+    for (int i = 0; i < n; ++i) {
+      jobs[i].ta = reinterpret_cast<const CUtensorMap*>(gbase + jobs_bytes + (size_t)(2 * i) * sizeof(CUtensorMap));
+      jobs[i].tb = reinterpret_cast<const CUtensorMap*>(gbase + jobs_bytes + (size_t)(2 * i + 1) * sizeof(CUtensorMap));
+    }
+    // Pinned memory cannot be allocated while a stream captures: carve the graph's copy
+    // source from the pinned arena reserved by an earlier (eager) call on this device.
+    TORCH_CHECK(st.graph_arena != nullptr && st.graph_arena_used + bytes <= kGraphArena,
+                "gemm_grouped: make one eager call on this device before capturing a CUDA graph "
+                "(its pinned staging arena is reserved outside capture)");
+    uint8_t* host = st.graph_arena + st.graph_arena_used;
+    st.graph_arena_used += (bytes + 127) / 128 * 128;
+    std::memcpy(host, table.data(), bytes);
+    C10_CUDA_CHECK(cudaMemcpyAsync(gbase, host, bytes, cudaMemcpyHostToDevice, stream));
+    st.graph_tables.push_back(dev);
+    if (p.M == 0 || p.N == 0) return;
+    bw::gemm_grouped_launch(reinterpret_cast<const bw::GroupJob*>(gbase), n, p, bn, stream);
+    return;
+  }
+  if (st.graph_arena == nullptr)
+    C10_CUDA_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&st.graph_arena), kGraphArena, cudaHostAllocDefault));
   if (st.last != table) {
     if (st.copied == nullptr) C10_CUDA_CHECK(cudaEventCreateWithFlags(&st.copied, cudaEventDisableTiming));
     else C10_CUDA_CHECK(cudaEventSynchronize(st.copied));  // the staging buffer is free again
@@ -325,6 +357,38 @@ void peer_barrier(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, 
   TORCH_CHECK(world >= 1 && world <= 1024 && rank >= 0 && rank < world, "bad rank / world");
   bw::peer_barrier(reinterpret_cast<int* const*>(flag_ptrs.data_ptr<int64_t>()), (int)rank, (int)world,
                    (int)epoch, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+// Cross-rank reduce fused into the GEMM epilogue: every element of alpha * A @ B^T is added
+// with fp32 atomics into its owner rank's copy of C (owner = float4 index / per4), through
+// peer pointers.  C is (M, N) fp32 with row stride ldc on every rank.
+void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t per4, int64_t M, int64_t N,
+                  int64_t ldc, double alpha, int64_t splits, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  TORCH_CHECK(a.batch == 1 && b.batch == 1 && a.cols == b.cols, "2-D operands with one K");
+  TORCH_CHECK(a.rows == M && b.rows == N, "M / N disagree with the operands");
+  TORCH_CHECK(peer_ptrs.is_cuda() && peer_ptrs.scalar_type() == torch::kInt64 && peer_ptrs.numel() == world,
+              "peer_ptrs: one device address per rank");
+  TORCH_CHECK(per4 > 0 && world >= 1, "bad partition");
+  bw::GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)a.cols;
+  p.batch = 1;
+  p.splits = (int)std::max<int64_t>(1, splits);
+  p.b_shared = 1;
+  p.c_mode = bw::kPeerAtomicF32;
+  p.alpha = (float)alpha;
+  p.ldc = ldc;
+  p.peers = reinterpret_cast<float* const*>(peer_ptrs.data_ptr<int64_t>());
+  p.world = (int)world;
+  p.per4 = per4;
+  p.err = err.data_ptr<int>();
+  if (M == 0 || N == 0) return;
+  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
@@ -569,6 +633,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
+  m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

@@ -168,7 +168,19 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
     }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
-    if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
+    if (p.c_mode == kPeerAtomicF32) {
+      const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) {
+          const long long i = rowoff + n;
+          int owner = (int)((i >> 2) / p.per4);
+          owner = owner < p.world ? owner : p.world - 1;
+          atomicAdd(p.peers[owner] + i, alpha * __uint_as_float(r[j]));
+        }
+      }
+    } else if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
       float* Cz = static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
                   (long long)row * p.ldc;
 #pragma unroll
@@ -270,7 +282,8 @@ void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
   const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM) * p.batch;
   const int kblocks = (p.K + BK - 1) / BK;
   q.cluster_k = 1;
-  if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 && tiles * 2 <= 160 && kblocks >= 8) {
+  if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 && p.c_mode != kPeerAtomicF32 &&
+      tiles * 2 <= 160 && kblocks >= 8) {
     q.cluster_k = 2;
     q.splits = 2;
   }

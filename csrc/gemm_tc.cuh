@@ -14,6 +14,8 @@ enum GemmStore : int {
   kStoreBF16T = 3,  // C^T (bf16): element (m, n) lands at C[z][n * ldc + m]
   kStoreBF16TB = 4, // per-segment C^T (bf16): rows are (s, t) with T = ldc rows per segment;
                     // element (m, n) lands at C[z][m / T][n][m % T] (a (S, N, T) block)
+  kPeerAtomicF32 = 5,  // fp32 atomics into the OWNER rank's copy of C over NVLink: element
+                       // i = m * ldc + n goes to peers[(i / 4) / per4][i] (cross-rank reduce)
 };
 
 // A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).
@@ -39,6 +41,9 @@ struct GemmParams {
   long long batch_stride_c;
   int* err;
   int cluster_k;   // >1: the split-K CTAs of a tile form a cluster and sum over DSMEM (set by the launcher)
+  float* const* peers;  // kPeerAtomicF32: device array of every rank's C (peer-mapped)
+  int world;
+  long long per4;       // kPeerAtomicF32: float4 elements owned by each rank
 };
 
 // One job of a grouped launch (tensor maps in global memory, 64-byte aligned).

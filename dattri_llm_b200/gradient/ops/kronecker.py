@@ -227,10 +227,22 @@ class LayerKroneckerAccumulator:
     _A: torch.Tensor | None = field(default=None, init=False, repr=False)
     _G: torch.Tensor | None = field(default=None, init=False, repr=False)
     _count: torch.Tensor | int = field(default=0, init=False, repr=False)
+    # Cross-rank accumulation: the Gram GEMMs add into symmetric buffers over NVLink
+    # (parallel.covariance.SymmetricGram); None when accumulating locally.
+    _symm: tuple | None = field(default=None, init=False, repr=False)
+    fused_reduce: bool | None = None
 
     @property
     def _n(self) -> int:
         return int(self._count)
+
+    def _use_symm(self, a_f: torch.Tensor, g_f: torch.Tensor) -> bool:
+        if self.fused_reduce is False or a_f.ndim != 2 or not a_f.is_cuda or a_f.dtype != torch.bfloat16:
+            return False
+        from dattri_llm_b200.ops import use_native
+        from dattri_llm_b200.parallel import symm
+
+        return use_native(a_f, g_f) and g_f.dtype == torch.bfloat16 and symm.available(a_f.device)
 
     def update(self, a, g, layer_type: str, module_kwargs: dict | None = None,
                include_bias: bool = True) -> None:
@@ -238,16 +250,31 @@ class LayerKroneckerAccumulator:
         a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
         a_f, g_f = _flatten_for_kfac(a, g, layer_type)
         a_f, g_f, n = _row_mask(a_f, g_f, layer_type)
-        if self._A is None:
-            lead = a_f.shape[:-2]
-            self._A = torch.zeros(*lead, a_f.shape[-1], a_f.shape[-1], device=a_f.device)
-            self._G = torch.zeros(*lead, g_f.shape[-1], g_f.shape[-1], device=g_f.device)
-        gram_accumulate(a_f, self._A)
-        gram_accumulate(g_f, self._G)
+        if self._A is None and self._symm is None:
+            if self._use_symm(a_f, g_f):
+                from dattri_llm_b200.parallel.covariance import SymmetricGram
+
+                self._symm = (SymmetricGram(a_f.shape[-1], a_f.device), SymmetricGram(g_f.shape[-1], g_f.device))
+            else:
+                lead = a_f.shape[:-2]
+                self._A = torch.zeros(*lead, a_f.shape[-1], a_f.shape[-1], device=a_f.device)
+                self._G = torch.zeros(*lead, g_f.shape[-1], g_f.shape[-1], device=g_f.device)
+        if self._symm is not None:
+            self._symm[0].add(a_f)
+            self._symm[1].add(g_f)
+        else:
+            gram_accumulate(a_f, self._A)
+            gram_accumulate(g_f, self._G)
         self._count = self._count + n
 
     def all_reduce(self) -> None:
-        """Sum the accumulators and counts over ranks."""
+        """Sum the accumulators and counts over ranks (collective)."""
+        if self._symm is not None:
+            self._A, self._G = self._symm[0].reduced(), self._symm[1].reduced()
+            self._symm = None
+            n = torch.tensor([self._n], dtype=torch.int64)
+            self._count = int(all_reduce_sum(n).item())
+            return
         if self._A is None:
             raise RuntimeError("No gradient-carrying data has been accumulated")
         all_reduce_sum(self._A)
@@ -258,6 +285,8 @@ class LayerKroneckerAccumulator:
     def result(self, *, consume: bool = False):
         """``(A, G)`` means; with *consume* the sums are divided in place and released."""
         n = self._n
+        if self._symm is not None:
+            raise RuntimeError("This accumulator reduces across ranks: call all_reduce() on every rank first")
         if self._A is None or n == 0:
             raise RuntimeError("No gradient-carrying data has been accumulated")
         if not consume:
@@ -268,7 +297,7 @@ class LayerKroneckerAccumulator:
 
     def reset(self) -> None:
         """Drop the accumulated state."""
-        self._A, self._G, self._count = None, None, 0
+        self._A, self._G, self._count, self._symm = None, None, 0, None
 
 
 @dataclass

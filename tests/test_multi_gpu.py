@@ -56,6 +56,25 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             dist.all_reduce(want)
             assert symm.all_reduce_sum_(x)
             worst = max(worst, float((x - want).abs().max() / want.abs().max()))
+        # K-FAC covariances reduced across ranks inside the Gram GEMM epilogue.
+        from dattri_llm_b200.gradient.ops.kronecker import LayerKroneckerAccumulator
+
+        acc = LayerKroneckerAccumulator()
+        ref_a = torch.zeros(192, 192, device=dev)
+        ref_g = torch.zeros(64, 64, device=dev)
+        for _ in range(3):
+            a = torch.randn(4, 100, 192, device=dev, generator=gen).bfloat16()
+            g = torch.randn(4, 100, 64, device=dev, generator=gen).bfloat16()
+            acc.update(a, g, "nn.Linear", include_bias=False)
+            ref_a += a.float().reshape(-1, 192).T @ a.float().reshape(-1, 192)
+            ref_g += g.float().reshape(-1, 64).T @ g.float().reshape(-1, 64)
+        assert acc._symm is not None, "the fused cross-rank path was not taken"
+        acc.all_reduce()
+        dist.all_reduce(ref_a)
+        dist.all_reduce(ref_g)
+        assert acc._n == 3 * 400 * world
+        worst = max(worst, float((acc._A - ref_a).abs().max() / ref_a.abs().max()),
+                    float((acc._G - ref_g).abs().max() / ref_g.abs().max()))
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         results[rank] = worst
@@ -65,7 +84,7 @@ def _worker(rank: int, world: int, port: int, results) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_allgather_score_and_peer_allreduce_match_nccl():
+def test_fused_score_allreduce_and_covariance_match_nccl():
     world = 2
     with mp.Manager() as m:
         results = m.dict()
