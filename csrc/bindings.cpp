@@ -391,6 +391,77 @@ void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t p
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
+// C (op)= alpha * A @ B^T where B lives sharded on the peers (read over NVLink inside the
+// GEMM).  mode 0: peers[r] is (shard, K), B = [peers[0]; peers[1]; ...] by rows;
+// mode 1: peers[r] is (N, shard), B = [peers[0] | peers[1] | ...] along K.
+void gemm_tn_peers(Tensor A, std::vector<Tensor> peers, Tensor C, int64_t mode, int64_t store, double alpha,
+                   Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  TORCH_CHECK(a.batch == 1, "A must be 2-D");
+  const int world = (int)peers.size();
+  TORCH_CHECK(world >= 1 && world <= bw::kMaxPeerMaps, "1..8 peers");
+  TORCH_CHECK(mode == 0 || mode == 1, "mode must be 0 (row shards) or 1 (K shards)");
+  TORCH_CHECK(store == bw::kStoreF32 || store == bw::kStoreBF16, "store must be fp32 or bf16");
+  std::vector<bw::GemmOperand> ops;
+  for (auto& t : peers) ops.push_back(operand(t, "peer shard"));
+  for (auto& o : ops)
+    TORCH_CHECK(o.batch == 1 && o.rows == ops[0].rows && o.cols == ops[0].cols, "peer shards must match");
+  const int shard = mode == 0 ? (int)ops[0].rows : (int)ops[0].cols;
+  const int n_out = mode == 0 ? shard * world : (int)ops[0].rows;
+  const long long k = mode == 0 ? ops[0].cols : (long long)shard * world;
+  TORCH_CHECK(a.cols == k, "A's K does not match the sharded B");
+  int bn = bw::pick_bn(n_out);
+  if (mode == 0) {
+    while (bn > 16 && shard % bn != 0) bn /= 2;  // a CTA's rows must come from one owner
+  }
+  if (mode == 0) {
+    TORCH_CHECK(shard % bn == 0, "row shards must be a multiple of the ", bn, "-row tile");
+  } else {
+    TORCH_CHECK(shard % 64 == 0, "K shards must be a multiple of 64");
+  }
+  const bool bf16_out = store == bw::kStoreBF16;
+  TORCH_CHECK(C.is_cuda() && C.scalar_type() == (bf16_out ? torch::kBFloat16 : torch::kFloat32) && C.dim() == 2 &&
+                  C.size(0) == a.rows && C.size(1) == n_out && C.stride(1) == 1,
+              "C must be (M, N) with contiguous rows and the store's dtype");
+  Tensor table;
+  {
+    std::string key = "peers:" + std::to_string(bn) + ":" + std::to_string(A.get_device()) + ";";
+    for (auto& o : ops)
+      key += std::to_string(reinterpret_cast<uintptr_t>(o.ptr)) + ":" + std::to_string(o.rows) + ":" +
+             std::to_string(o.cols) + ":" + std::to_string(o.row_stride) + ";";
+    std::lock_guard<std::mutex> lock(g_peer_tables.mu);
+    auto it = g_peer_tables.tables.find(key);
+    if (it == g_peer_tables.tables.end()) {
+      std::vector<CUtensorMap> maps;
+      for (auto& o : ops) maps.push_back(bw::make_tmap_kmajor_bf16(o, bn));
+      auto host = torch::empty({(long long)(maps.size() * sizeof(CUtensorMap))}, torch::kUInt8);
+      std::memcpy(host.data_ptr(), maps.data(), maps.size() * sizeof(CUtensorMap));
+      table = host.to(A.device());  // synchronous upload, once per distinct set of shards
+      TORCH_CHECK(reinterpret_cast<uintptr_t>(table.data_ptr()) % 64 == 0, "tensor-map table must be 64-byte aligned");
+      g_peer_tables.tables.emplace(key, table);
+    } else {
+      table = it->second;
+    }
+  }
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = n_out;
+  p.K = (int)k;
+  p.batch = 1;
+  p.splits = 1;
+  p.b_shared = 1;
+  p.c_mode = (int)store;
+  p.alpha = (float)alpha;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_peers_launch(a, reinterpret_cast<const CUtensorMap*>(table.data_ptr()), p, (int)mode, shard, bn,
+                        at::cuda::getCurrentCUDAStream());
+}
+
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
 std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
   TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
@@ -633,6 +704,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
   m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
+  m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -41,9 +41,12 @@ struct Cfg {
 
 // One CTA's 128 x BN output tile of batch (za, zb) -> output batch zc at Cbase.  The tensor
 // maps may live in kernel parameters or in global memory (grouped launches).
+//   b_row_off: subtracted from n0 in B's TMA coordinate (B rows owned by one peer's shard)
+//   kpeers / kshard: B's K range is spread over peers, kshard columns each (per-stage map)
 template <int BN>
 __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmParams& p,
-                                         int za, int zb, int zc, int split, void* Cbase) {
+                                         int za, int zb, int zc, int split, void* Cbase, int b_row_off = 0,
+                                         const CUtensorMap* kpeers = nullptr, int kshard = 0) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
@@ -68,7 +71,7 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(tmA);
-    tma_prefetch_desc(tmB);
+    if (kpeers == nullptr) tma_prefetch_desc(tmB);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -92,7 +95,12 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
       mbar_arrive_expect_tx(&full[s], C::kTileA + C::kTileB);
       const int kc = (kb0 + i) * BK;
       tma_load_3d(sA + s * C::kTileA, tmA, &full[s], kc, m0, za);
-      tma_load_3d(sB + s * C::kTileB, tmB, &full[s], kc, n0, zb);
+      if (kpeers != nullptr) {
+        const int owner = kc / kshard;
+        tma_load_3d(sB + s * C::kTileB, kpeers + owner, &full[s], kc - owner * kshard, n0, zb);
+      } else {
+        tma_load_3d(sB + s * C::kTileB, tmB, &full[s], kc, n0 - b_row_off, zb);
+      }
       issued = i + 1;
     }
     // Never leave with a bulk copy still landing in this CTA's shared memory.
@@ -235,6 +243,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   gemm_cta<BN>(&tmA, &tmB, p, z, p.b_shared ? 0 : z, z, split, p.C);
 }
 
+// B held by the peers (sharded weights, read over NVLink through per-peer tensor maps in the
+// kernel's parameters; no multicast).  mode 0: peer r owns B rows [r*shard, (r+1)*shard)
+// (the forward GEMM of a row-sharded weight); mode 1: peer r owns B's K columns
+// [r*shard, (r+1)*shard) (the input-gradient GEMM against the transposed shards).
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_peers_kernel(const __grid_constant__ CUtensorMap tmA, const CUtensorMap* __restrict__ pm,
+                      GemmParams p, int mode, int shard) {
+  const int z = blockIdx.z / p.splits;
+  const int split = blockIdx.z % p.splits;
+  if (mode == 0) {
+    const int owner = (int)(blockIdx.x * BN) / shard;
+    gemm_cta<BN>(&tmA, pm + owner, p, z, 0, z, split, p.C, owner * shard);
+  } else {
+    gemm_cta<BN>(&tmA, pm, p, z, 0, z, split, p.C, 0, pm, shard);
+  }
+}
+
 // Grouped launch: CTA z serves job z / batch, batch z % batch of that job; every job has
 // the same M, N, K, batch and store mode, its own operands (tensor maps in global memory,
 // 64-byte aligned, written before the launch) and output.
@@ -308,6 +334,22 @@ void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
 }
 
 template <int BN>
+void launch_peers_bn(const GemmOperand& A, const CUtensorMap* pm, const GemmParams& p, int mode, int shard,
+                     cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(gemm_peers_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    configured |= 1ull << dev;
+  }
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, BM);
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch * p.splits);
+  gemm_peers_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, pm, p, mode, shard);
+}
+
+template <int BN>
 void launch_grouped_bn(const GroupJob* jobs, int n_jobs, const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
   static unsigned long long configured = 0;  // one bit per device
@@ -323,6 +365,19 @@ void launch_grouped_bn(const GroupJob* jobs, int n_jobs, const GemmParams& p, cu
 
 }  // namespace
 
+void gemm_peers_launch(const GemmOperand& A, const CUtensorMap* pm, GemmParams p, int mode, int shard, int bn,
+                       cudaStream_t stream) {
+  if (p.splits < 1) p.splits = 1;
+  switch (bn) {
+    case 16: launch_peers_bn<16>(A, pm, p, mode, shard, stream); break;
+    case 32: launch_peers_bn<32>(A, pm, p, mode, shard, stream); break;
+    case 64: launch_peers_bn<64>(A, pm, p, mode, shard, stream); break;
+    case 128: launch_peers_bn<128>(A, pm, p, mode, shard, stream); break;
+    case 256: launch_peers_bn<256>(A, pm, p, mode, shard, stream); break;
+    default: throw std::runtime_error("gemm_peers: unsupported tile width");
+  }
+}
+
 void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream) {
   p.splits = 1;
   switch (bn) {
@@ -336,6 +391,11 @@ void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn,
 }
 
 CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows) {
+  // The encoder is a driver call: make the current device's primary context current on
+  // this thread first (a fresh thread -- e.g. autograd's backward worker -- whose device
+  // was never switched has none yet, and the runtime only binds one lazily).
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
   CUtensorMap map;
   cuuint64_t dims[3] = {(cuuint64_t)op.cols, (cuuint64_t)op.rows, (cuuint64_t)op.batch};
   cuuint64_t strides[2] = {(cuuint64_t)op.row_stride * 2, (cuuint64_t)op.batch_stride * 2};

@@ -54,7 +54,13 @@ struct GroupJob {
   long long pad;
 };
 
+constexpr int kMaxPeerMaps = 8;  // single node
+
 CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows);
+// B sharded over the peers; pm: device array of their tensor maps (64-byte aligned).
+// mode 0: B rows sharded (shard rows each); mode 1: B's K sharded (shard columns each).
+void gemm_peers_launch(const GemmOperand& A, const CUtensorMap* pm, GemmParams p, int mode, int shard, int bn,
+                       cudaStream_t stream);
 void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream);
 int pick_bn(int N);
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,

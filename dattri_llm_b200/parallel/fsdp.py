@@ -1,0 +1,160 @@
+"""Row-sharded linear layers whose collectives live inside their GEMMs (FSDP-style).
+
+:class:`ShardedLinear` keeps ``1/world`` of its weight rows on each rank, in symmetric
+memory, plus the transposed shard.  Nothing is all-gathered into HBM:
+
+* forward   ``y = x W^T``: one tcgen05 GEMM whose CTAs read the B tiles of the weight rows
+  they need straight from the owning peer over NVLink (``gemm_tn_peers`` mode 0);
+* backward  ``dx = dy W``: one GEMM whose K loop walks the peers' transposed shards
+  (mode 1);
+* weight gradient (when the weight trains): ``dW = dy^T x`` computed locally and
+  reduce-scattered INSIDE its epilogue -- fp32 atomics into the owner rank's gradient
+  shard over NVLink (``kPeerAtomicF32``); :func:`sync_sharded_grads` is the barrier after
+  which every rank's shard holds the sum over ranks.
+
+The capture hooks see an ``nn.Linear`` (same module boundary, full-width input and
+output), so per-sample capture is unchanged.  The reference reaches the same math through
+FSDP's NCCL all-gather / reduce-scatter around cuBLAS GEMMs
+(``dattri_llm/gradient/streaming.py:1175-1203``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
+
+
+class _AGLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight_shard, layer):
+        from dattri_llm_b200 import ops
+
+        k = layer.in_features
+        x2 = x.reshape(-1, k)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y = torch.empty(x2.shape[0], layer.out_features, dtype=torch.bfloat16, device=x.device)
+        ops.count_launch()
+        ops.native().gemm_tn_peers(x2, layer._w.peers, y, 0, ops.STORE_BF16, 1.0, ops.error_word(x.device))
+        ctx.layer = layer
+        ctx.save_for_backward(x2 if weight_shard.requires_grad else x2.new_empty(0))
+        ctx.in_shape = x.shape
+        return y.view(*x.shape[:-1], layer.out_features)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from dattri_llm_b200 import ops
+
+        layer = ctx.layer
+        dy2 = dy.reshape(-1, layer.out_features)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(dy2.shape[0], layer.in_features, dtype=torch.bfloat16, device=dy.device)
+            ops.count_launch()
+            ops.native().gemm_tn_peers(dy2, layer._wt.peers, dx, 1, ops.STORE_BF16, 1.0, ops.error_word(dy.device))
+            dx = dx.view(ctx.in_shape)
+        if ctx.needs_input_grad[1]:
+            (x2,) = ctx.saved_tensors
+            layer._reduce_scatter_wgrad(dy2, x2)
+        return dx, None, None
+
+
+class ShardedLinear(nn.Linear):
+    """A bias-free ``nn.Linear`` whose weight rows are sharded over the process group."""
+
+    def __init__(self, linear: nn.Linear, group=None) -> None:
+        nn.Module.__init__(self)
+        if linear.bias is not None:
+            raise ValueError("ShardedLinear shards bias-free linears")
+        w = linear.weight.detach()
+        self.in_features, self.out_features = linear.in_features, linear.out_features
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if self.out_features % (world * 64) or self.in_features % 8:
+            raise ValueError(f"out_features ({self.out_features}) must split into 64-row multiples over "
+                             f"{world} ranks and in_features must be a multiple of 8")
+        rows = self.out_features // world
+        dev = w.device
+        self._w = SymmetricBuffer((rows, self.in_features), torch.bfloat16, dev, group)
+        self._wt = SymmetricBuffer((self.in_features, rows), torch.bfloat16, dev, group)
+        shard = w[rank * rows:(rank + 1) * rows].to(torch.bfloat16)
+        self._w.local.copy_(shard)
+        self._wt.local.copy_(shard.t())
+        self.rows, self.rank, self.world = rows, rank, world
+        self.weight = nn.Parameter(self._w.local, requires_grad=linear.weight.requires_grad)
+        self.register_parameter("bias", None)
+        self._group = group
+        self._grad = None
+        self._barrier = None
+        if self.weight.requires_grad:
+            # Created here, collectively, not lazily in the backward (autograd's thread).
+            shard_elems = rows * self.in_features
+            self._grad = SymmetricBuffer((shard_elems,), torch.float32, dev, group)
+            self._grad.local.zero_()
+            self._barrier = PeerBarrier(dev, group)
+            # Owner r's entries are addressed by the FULL weight's linear index; its pointer
+            # is shifted back by r's first index so index i lands at i - r * shard_elems.
+            self._grad_ptrs = torch.tensor([int(p.data_ptr()) - 4 * r * shard_elems
+                                            for r, p in enumerate(self._grad.peers)],
+                                           dtype=torch.int64, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dtype != torch.bfloat16:
+            x = x.to(torch.bfloat16)
+        return _AGLinear.apply(x, self.weight, self)
+
+    # -- training: weight gradient reduce-scattered inside its GEMM ----------------------
+    def _reduce_scatter_wgrad(self, dy2: torch.Tensor, x2: torch.Tensor) -> None:
+        from dattri_llm_b200 import ops
+
+        if self._grad is None:
+            raise RuntimeError("this ShardedLinear was built with a frozen weight; it keeps no gradient")
+        dyt = dy2.t().contiguous()  # (N, M): tokens contiguous
+        xt = x2.t().contiguous()    # (K, M)
+        ops.count_launch()
+        ops.native().gemm_tn_peer(dyt, xt, self._grad_ptrs, self.world, self.rows * self.in_features // 4,
+                                  self.out_features, self.in_features, self.in_features, 1.0, 1,
+                                  ops.error_word(dy2.device))
+
+    def grad_shard(self) -> torch.Tensor | None:
+        """This rank's ``(rows, in_features)`` fp32 weight-gradient shard (after
+        :func:`sync_sharded_grads`)."""
+        return None if self._grad is None else self._grad.local.view(self.rows, self.in_features)
+
+    def zero_grad_shard(self) -> None:
+        """Zero this rank's gradient shard (collectively, before the next backward)."""
+        if self._grad is not None:
+            self._grad.local.zero_()
+            self._barrier.wait()
+
+
+def sync_sharded_grads(model: nn.Module) -> None:
+    """Barrier after which every :class:`ShardedLinear` gradient shard holds its sum over
+    ranks (the atomics of every rank's weight-gradient GEMM have landed)."""
+    for m in model.modules():
+        if isinstance(m, ShardedLinear) and m._barrier is not None:
+            m._barrier.wait()
+            return
+
+
+def shard_linears(model: nn.Module, names: list[str] | None = None, group=None) -> list[str]:
+    """Replace bias-free ``nn.Linear`` children (all, or those named) by :class:`ShardedLinear`
+    in place, collectively; returns the replaced names."""
+    replaced = []
+    for name, mod in list(model.named_modules()):
+        for child_name, child in list(mod.named_children()):
+            full = f"{name}.{child_name}" if name else child_name
+            if type(child) is not nn.Linear or child.bias is not None:
+                continue
+            if names is not None and full not in names:
+                continue
+            setattr(mod, child_name, ShardedLinear(child, group))
+            replaced.append(full)
+    return replaced

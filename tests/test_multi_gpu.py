@@ -20,6 +20,52 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _fsdp_worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+    import faulthandler
+
+    import torch.distributed as dist
+
+    faulthandler.enable()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from dattri_llm_b200 import ops
+
+        gen = torch.Generator(device=dev).manual_seed(300 + rank)
+        worst = 0.0
+        # Row-sharded linear: all-gather fused into the forward and input-gradient GEMMs,
+        # weight gradient reduce-scattered inside its GEMM.
+        from dattri_llm_b200.parallel.fsdp import ShardedLinear, sync_sharded_grads
+
+        torch.manual_seed(7)
+        full = torch.nn.Linear(320, 256, bias=False).to(dev)
+        w_full = full.weight.detach().bfloat16().float().clone()
+        layer = ShardedLinear(full)
+        x = torch.randn(3, 40, 320, device=dev, generator=gen).bfloat16().requires_grad_()
+        y = layer(x)
+        want_y = x.detach().float() @ w_full.T
+        worst = max(worst, float((y.float() - want_y).abs().max() / want_y.abs().max()))
+        dy = torch.randn_like(y)
+        y.backward(dy)
+        want_dx = dy.float() @ w_full
+        worst = max(worst, float((x.grad.float() - want_dx).abs().max() / want_dx.abs().max()))
+        sync_sharded_grads(torch.nn.ModuleList([layer]))
+        dw = dy.float().reshape(-1, 256).T @ x.detach().float().reshape(-1, 320)
+        dist.all_reduce(dw)
+        mine = dw[rank * layer.rows:(rank + 1) * layer.rows]
+        worst = max(worst, float((layer.grad_shard() - mine).abs().max() / mine.abs().max()))
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        results[rank] = worst
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
 def _worker(rank: int, world: int, port: int, results) -> None:
     import datetime
 
@@ -92,3 +138,14 @@ def test_fused_score_allreduce_and_covariance_match_nccl():
         errs = dict(results)
     assert len(errs) == world
     assert max(errs.values()) < 1e-2, errs
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_linear_fused_collectives_match_dense():
+    world = 2
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_fsdp_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(errs.values()) < 2e-2, errs
