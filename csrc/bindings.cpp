@@ -363,7 +363,7 @@ void peer_barrier(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, 
 // with fp32 atomics into its owner rank's copy of C (owner = float4 index / per4), through
 // peer pointers.  C is (M, N) fp32 with row stride ldc on every rank.
 void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t per4, int64_t M, int64_t N,
-                  int64_t ldc, double alpha, int64_t splits, Tensor err) {
+                  int64_t ldc, double alpha, int64_t splits, Tensor err, int64_t self_rank) {
   const c10::cuda::CUDAGuard guard(A.device());
   check_err(err);
   auto a = operand(A, "A");
@@ -386,6 +386,7 @@ void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t p
   p.peers = reinterpret_cast<float* const*>(peer_ptrs.data_ptr<int64_t>());
   p.world = (int)world;
   p.per4 = per4;
+  p.self_rank = (int)self_rank;
   p.err = err.data_ptr<int>();
   if (M == 0 || N == 0) return;
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());

@@ -32,7 +32,7 @@ template <int BN>
 struct Cfg {
   static constexpr int kTileA = BM * BK * 2;  // bytes
   static constexpr int kTileB = BN * BK * 2;
-  static constexpr int kStages = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 4));
+  static constexpr int kStages = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 3 : 4));
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem = kStages * (kTileA + kTileB) + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int kRed = BM * BN * 4;  // cluster split-K: the peer's fp32 partial tile
@@ -176,7 +176,30 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
     }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
-    if (p.c_mode == kPeerAtomicF32) {
+    if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+        (((long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase) & 3) == 0) {
+      // A float4 never straddles two owners (ownership is assigned in whole float4 units).
+      // 16-byte vector atomics go to this rank's own slice only; other owners get scalar
+      // fp32 atomics, the form peer (NVLink) atomics are known to support.
+      const long long i0 = (long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const long long i = i0 + 4 * q;
+        int owner = (int)((i >> 2) / p.per4);
+        owner = owner < p.world ? owner : p.world - 1;
+        float* dst = p.peers[owner] + i;
+        const float v0 = alpha * __uint_as_float(r[4 * q]), v1 = alpha * __uint_as_float(r[4 * q + 1]);
+        const float v2 = alpha * __uint_as_float(r[4 * q + 2]), v3 = alpha * __uint_as_float(r[4 * q + 3]);
+        if (owner == p.self_rank) {
+          atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v0, v1, v2, v3));
+        } else {
+          atomicAdd(dst, v0);
+          atomicAdd(dst + 1, v1);
+          atomicAdd(dst + 2, v2);
+          atomicAdd(dst + 3, v3);
+        }
+      }
+    } else if (p.c_mode == kPeerAtomicF32) {
       const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -187,6 +210,46 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
           owner = owner < p.world ? owner : p.world - 1;
           atomicAdd(p.peers[owner] + i, alpha * __uint_as_float(r[j]));
         }
+      }
+    } else if ((p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) && c0 + 32 <= BN && nbase + 32 <= p.N &&
+               ((reinterpret_cast<uintptr_t>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                             (long long)row * p.ldc + nbase) & 15) == 0)) {
+      // A whole 32-column chunk in range and 16-byte aligned: 8 vector accesses per thread
+      // instead of 32 scalar ones (the scalar form saturated the LSU pipe on large tiles).
+      float4* Cv = reinterpret_cast<float4*>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                             (long long)row * p.ldc + nbase);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 v = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
+                               alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
+        if (p.c_mode == kAtomicF32) {
+          atomicAdd(Cv + q, v);
+        } else {
+          if (p.beta_accumulate) {
+            const float4 o = Cv[q];
+            v.x += o.x;
+            v.y += o.y;
+            v.z += o.z;
+            v.w += o.w;
+          }
+          Cv[q] = v;
+        }
+      }
+    } else if (p.c_mode == kStoreBF16 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+               ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                             (long long)row * p.ldc + nbase) & 15) == 0)) {
+      uint4* Cv = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                           (long long)row * p.ldc + nbase);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
+                                                         alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
       float* Cz = static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
@@ -235,7 +298,7 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    GemmParams p) {
   const int z = blockIdx.z / p.splits;
@@ -248,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (the forward GEMM of a row-sharded weight); mode 1: peer r owns B's K columns
 // [r*shard, (r+1)*shard) (the input-gradient GEMM against the transposed shards).
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
     gemm_peers_kernel(const __grid_constant__ CUtensorMap tmA, const CUtensorMap* __restrict__ pm,
                       GemmParams p, int mode, int shard) {
   const int z = blockIdx.z / p.splits;

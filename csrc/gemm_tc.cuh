@@ -44,6 +44,7 @@ struct GemmParams {
   float* const* peers;  // kPeerAtomicF32: device array of every rank's C (peer-mapped)
   int world;
   long long per4;       // kPeerAtomicF32: float4 elements owned by each rank
+  int self_rank;        // kPeerAtomicF32: this rank (its own slice takes vector atomics)
 };
 
 // One job of a grouped launch (tensor maps in global memory, 64-byte aligned).

@@ -1,0 +1,157 @@
+"""Timings of the fused compute + collective kernels against their rooflines.
+
+    python -m dattri_llm_b200.parallel.bench_fused --emulate 8          # one GPU, 8 emulated peers
+    torchrun --nproc-per-node N -m dattri_llm_b200.parallel.bench_fused  # N GPUs over NVLink
+
+With ``--emulate W`` every "peer" buffer is a separate allocation on the local GPU, so the
+kernels run their multi-peer code paths with HBM in place of NVLink (the compute side of
+the roofline; this is also the form a single-GPU profiler capture can see).  Under
+torchrun the peers are the other ranks' symmetric-memory buffers.  Each kernel is timed
+with CUDA events after warm-up (max over ranks); the roofline is the slower of the math at
+the measured bf16 peak and the bytes that must cross NVLink (each remote byte once) at the
+measured per-direction peer bandwidth (770 GB/s) or the HBM bytes at the measured copy
+bandwidth (only the latter when emulated).
+Prints one JSON object per kernel.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+BF16_PEAK = 1.63e15     # measured cuBLAS bf16 burst on this B200 pool (FLOP/s)
+HBM = 6.55e12           # measured copy bandwidth (B/s)
+NVLINK = 770e9          # measured peer copy, per direction per GPU (B/s)
+
+
+def _time(fn, iters: int = 20) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters * 1e-3
+
+
+def _max_over_ranks(x: float) -> float:
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def _peers(shape, dtype, world, emulate, gen, device):
+    """``(local tensor, [peer views])``: symmetric buffers, or W local allocations."""
+    if emulate:
+        bufs = [torch.randn(shape, device=device, generator=gen).to(dtype) for _ in range(world)]
+        return bufs[0], bufs
+    from dattri_llm_b200.parallel.symm import SymmetricBuffer
+
+    b = SymmetricBuffer(shape, dtype, device)
+    b.local.copy_(torch.randn(shape, device=device, generator=gen).to(dtype))
+    torch.cuda.synchronize()
+    import torch.distributed as dist
+
+    dist.barrier()
+    return b.local, b.peers
+
+
+def run(world: int, emulate: bool, rank: int) -> list[dict]:
+    from dattri_llm_b200 import ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    nat = ops.native()
+    err = ops.error_word(dev)
+    rows = []
+
+    def report(name, secs, flops, nvlink_bytes, hbm_bytes, extra=None):
+        secs = _max_over_ranks(secs)
+        link = hbm_bytes / HBM if emulate else max(nvlink_bytes / NVLINK, hbm_bytes / HBM)
+        roof = max(flops / BF16_PEAK, link)
+        rows.append({"kernel": name, "world": world, "emulated": emulate, "us": secs * 1e6,
+                     "roofline_us": roof * 1e6, "fraction_of_roofline": roof / secs,
+                     "tflops": flops / secs / 1e12, **(extra or {})})
+
+    # 1) distributed score: all ranks' packed train blocks gathered into the score GEMM
+    k, b, n_local = 458752, 8, 1024 // world
+    test = torch.randn(n_local, k, device=dev, generator=gen).bfloat16()
+    _, blocks = _peers((b, k), torch.bfloat16, world, emulate, gen, dev)
+    out = torch.zeros(n_local, world * b, device=dev)
+    splits = max(1, 148 // ((n_local + 127) // 128))
+    secs = _time(lambda: (out.zero_(), nat.ag_score(test, blocks, out, 1.0, splits, err)))
+    report("ag_score (all-gather + score GEMM)", secs, 2.0 * n_local * world * b * k,
+           (world - 1) * b * k * 2, n_local * k * 2 + world * b * k * 2)
+
+    # 2) sharded-weight forward: weight tiles all-gathered inside the GEMM (Llama-1B q/o shape)
+    m, kk, n = 8192, 2048, 2048
+    x = torch.randn(m, kk, device=dev, generator=gen).bfloat16()
+    _, shards = _peers((n // world, kk), torch.bfloat16, world, emulate, gen, dev)
+    y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    secs = _time(lambda: nat.gemm_tn_peers(x, shards, y, 0, ops.STORE_BF16, 1.0, err))
+    report("gemm_tn_peers mode 0 (FSDP all-gather -> forward GEMM)", secs, 2.0 * m * n * kk,
+           (world - 1) / world * n * kk * 2, (m * kk + m * n) * 2)
+    w_full = torch.cat(list(shards)) if emulate else None
+    if w_full is not None:
+        secs_ref = _time(lambda: torch.matmul(x, w_full.T))
+        rows[-1]["cublas_same_shape_us"] = secs_ref * 1e6
+
+    # 3) input gradient against the peers' transposed shards
+    _, shards_t = _peers((kk, n // world), torch.bfloat16, world, emulate, gen, dev)
+    dy = torch.randn(m, n, device=dev, generator=gen).bfloat16()
+    dx = torch.empty(m, kk, device=dev, dtype=torch.bfloat16)
+    secs = _time(lambda: nat.gemm_tn_peers(dy, shards_t, dx, 1, ops.STORE_BF16, 1.0, err))
+    report("gemm_tn_peers mode 1 (all-gather -> input-gradient GEMM)", secs, 2.0 * m * n * kk,
+           (world - 1) / world * n * kk * 2, (m * n + m * kk) * 2)
+
+    # 4) Gram / weight-gradient GEMM reduced across ranks by epilogue peer atomics
+    w = 2048
+    xt = torch.randn(w, m, device=dev, generator=gen).bfloat16()
+    _, accs = _peers((w * w,), torch.float32, world, emulate, gen, dev)
+    ptrs = torch.tensor([int(p.data_ptr()) for p in accs], dtype=torch.int64, device=dev)
+    per4 = (w * w // 4 + world - 1) // world
+    secs = _time(lambda: nat.gemm_tn_peer(xt, xt, ptrs, world, per4, w, w, w, 1.0, 4, err, rank))
+    report("gemm_tn_peer (Gram / wgrad GEMM + cross-rank reduce in the epilogue)", secs, 2.0 * w * w * m,
+           (world - 1) / world * w * w * 4 * 4, 2 * w * m * 2 + w * w * 4 * 4)
+    ops.check_device_errors(dev)
+    return rows
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--emulate", type=int, default=0, help="emulate this many peers on one GPU")
+    a = ap.parse_args()
+    if a.emulate:
+        torch.cuda.set_device(0)
+        rows = run(a.emulate, True, 0)
+        rank = 0
+    else:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", 0))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        rank = dist.get_rank()
+        rows = run(dist.get_world_size(), False, rank)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

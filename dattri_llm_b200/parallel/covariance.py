@@ -94,7 +94,7 @@ class SymmetricGram:
         splits = native_ops.gemm.auto_splits(w, w, n, 1, 128 if w > 64 else 64)
         native_ops.count_launch()
         native_ops.native().gemm_tn_peer(xt, xt, self.ptrs, self.world, self.per4, w, w, w, 1.0, splits,
-                                         native_ops.error_word(x.device))
+                                         native_ops.error_word(x.device), self.rank)
 
     def reduced(self) -> torch.Tensor:
         """The summed ``(w, w)`` matrix on this rank (collective: every rank calls it)."""

@@ -121,7 +121,7 @@ class ShardedLinear(nn.Linear):
         ops.count_launch()
         ops.native().gemm_tn_peer(dyt, xt, self._grad_ptrs, self.world, self.rows * self.in_features // 4,
                                   self.out_features, self.in_features, self.in_features, 1.0, 1,
-                                  ops.error_word(dy2.device))
+                                  ops.error_word(dy2.device), self.rank)
 
     def grad_shard(self) -> torch.Tensor | None:
         """This rank's ``(rows, in_features)`` fp32 weight-gradient shard (after
