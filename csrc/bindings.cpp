@@ -463,6 +463,86 @@ void gemm_tn_peers(Tensor A, std::vector<Tensor> peers, Tensor C, int64_t mode, 
                         at::cuda::getCurrentCUDAStream());
 }
 
+// C (op)= alpha * A @ B^T with B sharded over the peers, all-gathered INSIDE the launch into
+// the local staging matrix `stage` (each remote byte crosses NVLink once) while the GEMM
+// tiles consume it.  mode 0: peers[r] is (shard, K) and B = rows; mode 1: peers[r] is
+// (N, shard) and B = K columns.  `flags` (int32, one per rank, zeroed once) and `epoch`
+// (1, 2, ... per launch on this staging buffer) gate the tiles.
+void gemm_tn_staged(Tensor A, std::vector<Tensor> peers, Tensor stage, Tensor C, Tensor flags, int64_t epoch,
+                    int64_t mode, int64_t self_rank, int64_t store, double alpha, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  TORCH_CHECK(a.batch == 1, "A must be 2-D");
+  const int world = (int)peers.size();
+  TORCH_CHECK(world >= 1 && world <= bw::kMaxPeerMaps, "1..8 peers");
+  TORCH_CHECK(mode == 0 || mode == 1, "mode must be 0 (row shards) or 1 (K shards)");
+  TORCH_CHECK(self_rank >= 0 && self_rank < world, "bad self rank");
+  TORCH_CHECK(store == bw::kStoreF32 || store == bw::kStoreBF16, "store must be fp32 or bf16");
+  std::vector<bw::GemmOperand> ops;
+  for (auto& t : peers) ops.push_back(operand(t, "peer shard"));
+  for (auto& o : ops)
+    TORCH_CHECK(o.batch == 1 && o.rows == ops[0].rows && o.cols == ops[0].cols && o.row_stride == ops[0].row_stride,
+                "peer shards must match");
+  auto st = operand(stage, "stage");
+  const int shard = mode == 0 ? (int)ops[0].rows : (int)ops[0].cols;
+  const int n_out = mode == 0 ? shard * world : (int)ops[0].rows;
+  const long long k = mode == 0 ? ops[0].cols : (long long)shard * world;
+  TORCH_CHECK(st.batch == 1 && st.rows == n_out && st.cols == k, "stage must be the gathered (N, K) matrix");
+  TORCH_CHECK(a.cols == k, "A's K does not match the sharded B");
+  int bn = bw::pick_bn(n_out);
+  if (mode == 0) {
+    while (bn > 64 && shard % bn != 0) bn /= 2;
+    TORCH_CHECK(shard % bn == 0 && bn >= 64, "row shards must be a multiple of 64 rows");
+  } else {
+    if (bn < 64) bn = 64;
+    TORCH_CHECK(shard % 64 == 0, "K shards must be a multiple of 64");
+  }
+  TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == torch::kInt32 && flags.numel() >= world, "flags: int32[world]");
+  const bool bf16_out = store == bw::kStoreBF16;
+  TORCH_CHECK(C.is_cuda() && C.scalar_type() == (bf16_out ? torch::kBFloat16 : torch::kFloat32) && C.dim() == 2 &&
+                  C.size(0) == a.rows && C.size(1) == n_out && C.stride(1) == 1,
+              "C must be (M, N) with contiguous rows and the store's dtype");
+  bw::StageArgs sa{};
+  const int src_rows = (int)ops[0].rows;
+  const long long row_elems = ops[0].cols;
+  TORCH_CHECK(row_elems % 8 == 0 && ops[0].row_stride % 8 == 0 && st.row_stride % 8 == 0, "rows must be 16-byte multiples");
+  for (int r = 0; r < world; ++r) {
+    sa.src[r] = ops[r].ptr;
+    sa.dst_row0[r] = mode == 0 ? (long long)r * shard : 0;
+    sa.dst_col0[r] = mode == 0 ? 0 : (long long)r * shard;
+  }
+  sa.src_stride = ops[0].row_stride;
+  sa.src_rows = src_rows;
+  sa.row_elems = row_elems;
+  sa.dst = const_cast<void*>(st.ptr);
+  sa.dst_stride = st.row_stride;
+  int pieces = (2 * 148 + world - 1) / world;
+  if (pieces > src_rows / 8) pieces = std::max(1, src_rows / 8);
+  sa.piece_rows = (src_rows + pieces - 1) / pieces;
+  sa.pieces_per_owner = (src_rows + sa.piece_rows - 1) / sa.piece_rows;
+  sa.flags = flags.data_ptr<int>();
+  sa.expect = (int)(epoch * sa.pieces_per_owner);
+  sa.world = world;
+  sa.self = (int)self_rank;
+  sa.mode = (int)mode;
+  sa.shard = shard;
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = n_out;
+  p.K = (int)k;
+  p.batch = 1;
+  p.splits = 1;
+  p.b_shared = 1;
+  p.c_mode = (int)store;
+  p.alpha = (float)alpha;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_staged_launch(a, st, ops[self_rank], p, sa, bn, at::cuda::getCurrentCUDAStream());
+}
+
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
 std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
   TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
@@ -706,6 +786,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
+  m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -39,14 +39,42 @@ struct Cfg {
   static constexpr bool kClusterOK = kSmem + kRed <= 227 * 1024;
 };
 
+// Wait (bounded) until `*flag` reaches `expect` (acquire), then order those generic-proxy
+// writes before this thread's later TMA (async-proxy) reads of the same memory.
+__device__ __forceinline__ void stage_wait(const int* flag, int expect, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= expect) break;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_error(err, kErrWaitStage);
+      break;
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Control block of a staged launch (one per CTA, in registers / local scope).
+struct StageCtl {
+  const CUtensorMap* own;  // this rank's own shard (read in place); a kernel-parameter address
+  const int* flags;  // per owner: pieces copied so far (monotonic across launches)
+  int expect;        // flag value meaning "this launch's copy of the owner is complete"
+  int mode, self, shard;
+  unsigned ready;    // owners already waited for (bit mask)
+};
+
 // One CTA's 128 x BN output tile of batch (za, zb) -> output batch zc at Cbase.  The tensor
 // maps may live in kernel parameters or in global memory (grouped launches).
 //   b_row_off: subtracted from n0 in B's TMA coordinate (B rows owned by one peer's shard)
 //   kpeers / kshard: B's K range is spread over peers, kshard columns each (per-stage map)
+//   stage: B is the local staging copy of peer shards being filled by this very launch
+//          (see gemm_staged_kernel); tiles of the own shard come from stage->own instead
 template <int BN>
 __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmParams& p,
                                          int za, int zb, int zc, int split, void* Cbase, int b_row_off = 0,
-                                         const CUtensorMap* kpeers = nullptr, int kshard = 0) {
+                                         const CUtensorMap* kpeers = nullptr, int kshard = 0,
+                                         const StageCtl* stage = nullptr) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
@@ -95,7 +123,22 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
       mbar_arrive_expect_tx(&full[s], C::kTileA + C::kTileB);
       const int kc = (kb0 + i) * BK;
       tma_load_3d(sA + s * C::kTileA, tmA, &full[s], kc, m0, za);
-      if (kpeers != nullptr) {
+      if (stage != nullptr) {
+        // mode 0: the CTA's B rows belong to one owner; mode 1: the K block's owner.
+        const int owner = stage->mode == 0 ? n0 / stage->shard : kc / stage->shard;
+        if (owner == stage->self) {
+          if (stage->mode == 0)
+            tma_load_3d(sB + s * C::kTileB, stage->own, &full[s], kc, n0 - owner * stage->shard, zb);
+          else
+            tma_load_3d(sB + s * C::kTileB, stage->own, &full[s], kc - owner * stage->shard, n0, zb);
+        } else {
+          if (!(stage->ready >> owner & 1u)) {
+            stage_wait(stage->flags + owner, stage->expect, p.err);
+            const_cast<StageCtl*>(stage)->ready |= 1u << owner;
+          }
+          tma_load_3d(sB + s * C::kTileB, tmB, &full[s], kc, n0, zb);
+        }
+      } else if (kpeers != nullptr) {
         const int owner = kc / kshard;
         tma_load_3d(sB + s * C::kTileB, kpeers + owner, &full[s], kc - owner * kshard, n0, zb);
       } else {
@@ -306,6 +349,49 @@ __global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
   gemm_cta<BN>(&tmA, &tmB, p, z, p.b_shared ? 0 : z, z, split, p.C);
 }
 
+// One launch that all-gathers sharded B into a local staging buffer AND multiplies: the
+// first `copiers` CTAs first pull their share of the remote shards over NVLink (16-byte
+// peer loads, every remote byte once) into `StageArgs::dst`, bumping the owner's flag after
+// each piece; then every CTA runs its GEMM tile, waiting for a remote owner's flag only
+// when it first needs that owner's rows (mode 0) or K range (mode 1).  Tiles of the own
+// shard never wait.  Copiers are the lowest CTA indices, which are dispatched first, so no
+// resident CTA waits on a CTA that has not started; the waits are bounded regardless.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_staged_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmStage,
+                       const __grid_constant__ CUtensorMap tmOwn, GemmParams p, StageArgs sa) {
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (cta < sa.copiers) {
+    const int pieces = sa.pieces_per_owner;
+    const int total = pieces * sa.world;
+    for (int t = cta; t < total; t += sa.copiers) {
+      const int owner = t / pieces, piece = t - owner * pieces;
+      if (owner == sa.self) continue;
+      const int r0 = piece * sa.piece_rows;
+      const int r1 = min(sa.src_rows, r0 + sa.piece_rows);
+      const long long vec_per_row = sa.row_elems / 8;
+      const uint4* src = reinterpret_cast<const uint4*>(sa.src[owner]);
+      for (long long v = threadIdx.x; v < (long long)(r1 - r0) * vec_per_row; v += kThreads) {
+        const long long r = r0 + v / vec_per_row, c = v % vec_per_row;
+        const uint4 x = src[(r * sa.src_stride) / 8 + c];
+        reinterpret_cast<uint4*>(sa.dst)[((sa.dst_row0[owner] + r) * sa.dst_stride + sa.dst_col0[owner]) / 8 + c] = x;
+      }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) atomicAdd(sa.flags + owner, 1);
+    }
+  }
+  StageCtl sc;
+  sc.own = &tmOwn;
+  sc.flags = sa.flags;
+  sc.expect = sa.expect;
+  sc.mode = sa.mode;
+  sc.self = sa.self;
+  sc.shard = sa.shard;
+  sc.ready = 0u;
+  gemm_cta<BN>(&tmA, &tmStage, p, 0, 0, 0, 0, p.C, 0, nullptr, 0, &sc);
+}
+
 // B held by the peers (sharded weights, read over NVLink through per-peer tensor maps in the
 // kernel's parameters; no multicast).  mode 0: peer r owns B rows [r*shard, (r+1)*shard)
 // (the forward GEMM of a row-sharded weight); mode 1: peer r owns B's K columns
@@ -413,6 +499,24 @@ void launch_peers_bn(const GemmOperand& A, const CUtensorMap* pm, const GemmPara
 }
 
 template <int BN>
+void launch_staged_bn(const GemmOperand& A, const GemmOperand& stage_op, const GemmOperand& own,
+                      const GemmParams& p, const StageArgs& sa, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(gemm_staged_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    configured |= 1ull << dev;
+  }
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, BM);
+  CUtensorMap ts = make_tmap_kmajor_bf16(stage_op, BN);
+  CUtensorMap to = make_tmap_kmajor_bf16(own, BN);
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, 1);
+  gemm_staged_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, ts, to, p, sa);
+}
+
+template <int BN>
 void launch_grouped_bn(const GroupJob* jobs, int n_jobs, const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
   static unsigned long long configured = 0;  // one bit per device
@@ -438,6 +542,20 @@ void gemm_peers_launch(const GemmOperand& A, const CUtensorMap* pm, GemmParams p
     case 128: launch_peers_bn<128>(A, pm, p, mode, shard, stream); break;
     case 256: launch_peers_bn<256>(A, pm, p, mode, shard, stream); break;
     default: throw std::runtime_error("gemm_peers: unsupported tile width");
+  }
+}
+
+void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const GemmOperand& own, GemmParams p,
+                        StageArgs sa, int bn, cudaStream_t stream) {
+  p.splits = 1;
+  p.batch = 1;
+  const int ctas = ((p.N + bn - 1) / bn) * ((p.M + BM - 1) / BM);
+  sa.copiers = ctas < 148 ? ctas : 148;
+  switch (bn) {
+    case 64: launch_staged_bn<64>(A, stage_op, own, p, sa, stream); break;
+    case 128: launch_staged_bn<128>(A, stage_op, own, p, sa, stream); break;
+    case 256: launch_staged_bn<256>(A, stage_op, own, p, sa, stream); break;
+    default: throw std::runtime_error("gemm_staged: unsupported tile width");
   }
 }
 

@@ -57,12 +57,33 @@ struct GroupJob {
 
 constexpr int kMaxPeerMaps = 8;  // single node
 
+// A staged launch: copy the remote peers' shards of B into the local staging matrix `dst`
+// (every remote byte once, over NVLink) inside the GEMM launch that consumes it.
+struct StageArgs {
+  const void* src[kMaxPeerMaps];  // each rank's shard (peer-mapped), bf16
+  long long src_stride;           // elements between shard rows
+  int src_rows;                   // rows of a shard
+  long long row_elems;            // elements copied per row (multiple of 8)
+  void* dst;                      // local staging matrix, bf16
+  long long dst_stride;           // elements between staging rows
+  long long dst_row0[kMaxPeerMaps];  // where owner r's rows start in dst
+  long long dst_col0[kMaxPeerMaps];  // where owner r's columns start in dst (multiple of 8)
+  int piece_rows, pieces_per_owner;
+  int* flags;                     // per owner, monotonic
+  int expect;                     // per-owner flag value once this launch's copy is complete
+  int world, self, mode, shard, copiers;
+};
+
 CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows);
 // B sharded over the peers; pm: device array of their tensor maps (64-byte aligned).
 // mode 0: B rows sharded (shard rows each); mode 1: B's K sharded (shard columns each).
 void gemm_peers_launch(const GemmOperand& A, const CUtensorMap* pm, GemmParams p, int mode, int shard, int bn,
                        cudaStream_t stream);
 void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream);
+// mode 0: B rows sharded (stage_op = the (N, K) staging matrix, own = this rank's (shard, K));
+// mode 1: B's K sharded (stage_op = the (N, K) staging matrix, own = this rank's (N, shard)).
+void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const GemmOperand& own, GemmParams p,
+                        StageArgs sa, int bn, cudaStream_t stream);
 int pick_bn(int N);
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream);

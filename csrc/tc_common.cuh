@@ -26,6 +26,7 @@ enum ErrCode : int {
   kErrWaitDone = 3,   // epilogue timed out waiting for the accumulator
   kErrWaitPeer = 4,   // a cross-GPU flag never arrived
   kErrBadArg = 5,
+  kErrWaitStage = 6,  // a staged (peer-copied) tile never became ready
 };
 
 // ~2 s: far above any legitimate wait inside one launch, far below a watchdog.

@@ -97,6 +97,7 @@ _ERR_NAMES = {
     3: "the accumulator never completed",
     4: "a peer GPU flag never arrived",
     5: "a kernel rejected its arguments",
+    6: "a peer-staged tile never became ready",
 }
 
 

@@ -106,6 +106,18 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
         secs_ref = _time(lambda: torch.matmul(x, w_full.T))
         rows[-1]["cublas_same_shape_us"] = secs_ref * 1e6
 
+    stage = torch.empty(n, kk, device=dev, dtype=torch.bfloat16)
+    flags = torch.zeros(world, dtype=torch.int32, device=dev)
+    epoch = [0]
+
+    def staged(a_, peers_, out_, mode):
+        epoch[0] += 1
+        nat.gemm_tn_staged(a_, peers_, stage, out_, flags, epoch[0], mode, rank, ops.STORE_BF16, 1.0, err)
+
+    secs = _time(lambda: staged(x, shards, y, 0))
+    report("gemm_tn_staged mode 0 (FSDP all-gather -> forward GEMM, one launch)", secs, 2.0 * m * n * kk,
+           (world - 1) / world * n * kk * 2, (m * kk + m * n + n * kk) * 2)
+
     # 3) input gradient against the peers' transposed shards
     _, shards_t = _peers((kk, n // world), torch.bfloat16, world, emulate, gen, dev)
     dy = torch.randn(m, n, device=dev, generator=gen).bfloat16()
@@ -113,6 +125,12 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
     secs = _time(lambda: nat.gemm_tn_peers(dy, shards_t, dx, 1, ops.STORE_BF16, 1.0, err))
     report("gemm_tn_peers mode 1 (all-gather -> input-gradient GEMM)", secs, 2.0 * m * n * kk,
            (world - 1) / world * n * kk * 2, (m * n + m * kk) * 2)
+    stage = torch.empty(kk, n, device=dev, dtype=torch.bfloat16)
+    flags = torch.zeros(world, dtype=torch.int32, device=dev)
+    epoch[0] = 0
+    secs = _time(lambda: staged(dy, shards_t, dx, 1))
+    report("gemm_tn_staged mode 1 (all-gather -> input-gradient GEMM, one launch)", secs, 2.0 * m * n * kk,
+           (world - 1) / world * n * kk * 2, (m * n + m * kk + n * kk) * 2)
 
     # 4) Gram / weight-gradient GEMM reduced across ranks by epilogue peer atomics
     w = 2048

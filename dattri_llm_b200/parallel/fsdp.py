@@ -3,9 +3,11 @@
 :class:`ShardedLinear` keeps ``1/world`` of its weight rows on each rank, in symmetric
 memory, plus the transposed shard.  Nothing is all-gathered into HBM:
 
-* forward   ``y = x W^T``: one tcgen05 GEMM whose CTAs read the B tiles of the weight rows
-  they need straight from the owning peer over NVLink (``gemm_tn_peers`` mode 0);
-* backward  ``dx = dy W``: one GEMM whose K loop walks the peers' transposed shards
+* forward   ``y = x W^T``: ONE launch (``gemm_tn_staged`` mode 0) whose first CTAs pull
+  the remote shards over NVLink into a local staging matrix -- every remote byte once --
+  while every CTA's GEMM tile starts on its own shard's rows or waits (bounded) on the
+  flag of the owner whose rows it needs;
+* backward  ``dx = dy W``: the same over the peers' transposed shards, gated per K range
   (mode 1);
 * weight gradient (when the weight trains): ``dW = dy^T x`` computed locally and
   reduce-scattered INSIDE its epilogue -- fp32 atomics into the owner rank's gradient
@@ -27,6 +29,35 @@ from torch import nn
 from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
 
 
+class _Staging:
+    """A local staging matrix for one gathered weight shape, with its copy flags and the
+    launch counter that gates them (shared by every layer of that shape: launches on one
+    stream use it one after another)."""
+
+    _pool: dict = {}
+
+    def __init__(self, rows: int, cols: int, world: int, device: torch.device) -> None:
+        self.buf = torch.empty(rows, cols, dtype=torch.bfloat16, device=device)
+        self.flags = torch.zeros(world, dtype=torch.int32, device=device)
+        self.epoch = 0
+
+    @classmethod
+    def get(cls, rows: int, cols: int, world: int, device: torch.device) -> _Staging:
+        key = (rows, cols, world, device)
+        st = cls._pool.get(key)
+        if st is None:
+            st = cls._pool[key] = cls(rows, cols, world, device)
+        return st
+
+    def launch(self, a: torch.Tensor, peers, out: torch.Tensor, mode: int, self_rank: int) -> None:
+        from dattri_llm_b200 import ops
+
+        self.epoch += 1
+        ops.count_launch()
+        ops.native().gemm_tn_staged(a, peers, self.buf, out, self.flags, self.epoch, mode, self_rank,
+                                    ops.STORE_BF16, 1.0, ops.error_word(a.device))
+
+
 class _AGLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight_shard, layer):
@@ -37,8 +68,7 @@ class _AGLinear(torch.autograd.Function):
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         y = torch.empty(x2.shape[0], layer.out_features, dtype=torch.bfloat16, device=x.device)
-        ops.count_launch()
-        ops.native().gemm_tn_peers(x2, layer._w.peers, y, 0, ops.STORE_BF16, 1.0, ops.error_word(x.device))
+        _Staging.get(layer.out_features, k, layer.world, x.device).launch(x2, layer._w.peers, y, 0, layer.rank)
         ctx.layer = layer
         ctx.save_for_backward(x2 if weight_shard.requires_grad else x2.new_empty(0))
         ctx.in_shape = x.shape
@@ -55,8 +85,8 @@ class _AGLinear(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[0]:
             dx = torch.empty(dy2.shape[0], layer.in_features, dtype=torch.bfloat16, device=dy.device)
-            ops.count_launch()
-            ops.native().gemm_tn_peers(dy2, layer._wt.peers, dx, 1, ops.STORE_BF16, 1.0, ops.error_word(dy.device))
+            _Staging.get(layer.in_features, layer.out_features, layer.world, dy.device).launch(
+                dy2, layer._wt.peers, dx, 1, layer.rank)
             dx = dx.view(ctx.in_shape)
         if ctx.needs_input_grad[1]:
             (x2,) = ctx.saved_tensors
