@@ -21,6 +21,7 @@
 #include "score_ag.cuh"
 #include "peer_sync.cuh"
 #include "allreduce_p2p.cuh"
+#include "moe_ep.cuh"
 
 namespace {
 
@@ -543,6 +544,81 @@ void gemm_tn_staged(Tensor A, std::vector<Tensor> peers, Tensor stage, Tensor C,
   bw::gemm_staged_launch(a, st, ops[self_rank], p, sa, bn, at::cuda::getCurrentCUDAStream());
 }
 
+// A device array of the given tensors' addresses, cached by the address list (symmetric
+// buffers are allocated once).
+Tensor device_ptr_table(const std::vector<Tensor>& ts, const c10::Device& dev) {
+  std::string key = "ptrs:" + std::to_string(dev.index()) + ";";
+  for (auto& t : ts) key += std::to_string(reinterpret_cast<uintptr_t>(t.data_ptr())) + ";";
+  std::lock_guard<std::mutex> lock(g_peer_tables.mu);
+  auto it = g_peer_tables.tables.find(key);
+  if (it != g_peer_tables.tables.end()) return it->second;
+  auto host = torch::empty({(long long)ts.size()}, torch::kInt64);
+  for (size_t i = 0; i < ts.size(); ++i) host[i] = (int64_t) reinterpret_cast<uintptr_t>(ts[i].data_ptr());
+  Tensor table = host.to(dev);
+  g_peer_tables.tables.emplace(key, table);
+  return table;
+}
+
+// Expert-parallel dispatch: row r of src (token r / k) into rank dst_rank[r]'s receive
+// buffer at row dst_row[r], with its origin (self, r) into that rank's origin table.
+void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor dst_row, std::vector<Tensor> peer_rows,
+                  std::vector<Tensor> peer_meta, int64_t self) {
+  const c10::cuda::CUDAGuard guard(src.device());
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.stride(1) == 1 &&
+                  src.stride(0) % 8 == 0 && src.size(1) % 8 == 0, "src must be (T, H) bf16 with 16-byte rows");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "src must be 16-byte aligned");
+  const int world = (int)peer_rows.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && (int)peer_meta.size() == world, "1..8 ranks");
+  const long long rows = src.size(0) * rows_per_token;
+  TORCH_CHECK(dst_rank.scalar_type() == torch::kInt32 && dst_row.scalar_type() == torch::kInt32 &&
+                  dst_rank.numel() == rows && dst_row.numel() == rows && dst_rank.is_contiguous() && dst_row.is_contiguous(),
+              "dst_rank / dst_row: int32 per (token, slot)");
+  std::vector<void*> pr;
+  std::vector<int2*> pm;
+  for (int r = 0; r < world; ++r) {
+    TORCH_CHECK(peer_rows[r].scalar_type() == torch::kBFloat16 && peer_rows[r].size(-1) == src.size(1) &&
+                    peer_rows[r].is_contiguous(), "receive buffers must be (R, H) bf16");
+    TORCH_CHECK(peer_meta[r].scalar_type() == torch::kInt32 && peer_meta[r].is_contiguous(), "origin tables: int32");
+    pr.push_back(peer_rows[r].data_ptr());
+    pm.push_back(reinterpret_cast<int2*>(peer_meta[r].data_ptr<int>()));
+  }
+  bw::moe_dispatch(src.data_ptr(), src.stride(0), dst_rank.data_ptr<int>(), dst_row.data_ptr<int>(), pr.data(),
+                   pm.data(), world, (int)rows, (int)src.size(1), (int)self, (int)rows_per_token,
+                   at::cuda::getCurrentCUDAStream());
+}
+
+// C rows returned to their sources: out row m = alpha * (A @ B^T)[m] is stored into rank
+// scatter[m][0]'s buffer peer_C[...] at row scatter[m][1] (bf16, row length N).
+void gemm_tn_scatter(Tensor A, Tensor B, std::vector<Tensor> peer_C, Tensor scatter, double alpha, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  TORCH_CHECK(a.batch == 1 && b.batch == 1 && a.cols == b.cols, "2-D operands with one K");
+  TORCH_CHECK(scatter.is_cuda() && scatter.scalar_type() == torch::kInt32 && scatter.is_contiguous() &&
+                  scatter.numel() >= 2 * a.rows, "scatter: int32 (M, 2)");
+  for (auto& c : peer_C)
+    TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows,
+                "peer outputs must be contiguous (R, N) bf16");
+  Tensor ptrs = device_ptr_table(peer_C, A.device());
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = (int)b.rows;
+  p.K = (int)a.cols;
+  p.batch = 1;
+  p.splits = 1;
+  p.b_shared = 1;
+  p.c_mode = bw::kStoreBF16Scatter;
+  p.alpha = (float)alpha;
+  p.ldc = b.rows;
+  p.peers = reinterpret_cast<float* const*>(ptrs.data_ptr<int64_t>());
+  p.world = (int)peer_C.size();
+  p.scatter = reinterpret_cast<const int2*>(scatter.data_ptr<int>());
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.N == 0) return;
+  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
+}
+
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
 std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
   TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
@@ -787,6 +863,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
+  m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
+  m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -219,7 +219,31 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
     }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
-    if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+    if (p.c_mode == kStoreBF16Scatter) {
+      // Row m goes home: rank scatter[m].x, row scatter[m].y of that rank's C (peer memory).
+      const int2 dstm = p.scatter[row];
+      __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
+      if (c0 + 32 <= BN && nbase + 32 <= p.N && ((reinterpret_cast<uintptr_t>(Cr + nbase) & 15) == 0)) {
+        uint4* Cv = reinterpret_cast<uint4*>(Cr + nbase);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
+                                                           alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
+            w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = nbase + j;
+          if (j < BN - c0 && n < p.N) Cr[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+        }
+      }
+    } else if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
         (((long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase) & 3) == 0) {
       // A float4 never straddles two owners (ownership is assigned in whole float4 units).
       // 16-byte vector atomics go to this rank's own slice only; other owners get scalar
@@ -370,11 +394,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r0 = piece * sa.piece_rows;
       const int r1 = min(sa.src_rows, r0 + sa.piece_rows);
       const long long vec_per_row = sa.row_elems / 8;
+      const long long nvec = (long long)(r1 - r0) * vec_per_row;
       const uint4* src = reinterpret_cast<const uint4*>(sa.src[owner]);
-      for (long long v = threadIdx.x; v < (long long)(r1 - r0) * vec_per_row; v += kThreads) {
-        const long long r = r0 + v / vec_per_row, c = v % vec_per_row;
-        const uint4 x = src[(r * sa.src_stride) / 8 + c];
-        reinterpret_cast<uint4*>(sa.dst)[((sa.dst_row0[owner] + r) * sa.dst_stride + sa.dst_col0[owner]) / 8 + c] = x;
+      uint4* dst = reinterpret_cast<uint4*>(sa.dst);
+      // Four 16-byte peer loads in flight per thread before their stores.
+      for (long long v0 = threadIdx.x; v0 < nvec; v0 += 4 * kThreads) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long v = v0 + u * kThreads;
+          if (v < nvec) {
+            const long long r = r0 + v / vec_per_row, c = v % vec_per_row;
+            x[u] = src[(r * sa.src_stride) / 8 + c];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long v = v0 + u * kThreads;
+          if (v < nvec) {
+            const long long r = r0 + v / vec_per_row, c = v % vec_per_row;
+            dst[((sa.dst_row0[owner] + r) * sa.dst_stride + sa.dst_col0[owner]) / 8 + c] = x[u];
+          }
+        }
       }
       __threadfence();
       __syncthreads();
@@ -458,6 +499,7 @@ void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
   const int kblocks = (p.K + BK - 1) / BK;
   q.cluster_k = 1;
   if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 && p.c_mode != kPeerAtomicF32 &&
+      p.c_mode != kStoreBF16Scatter &&
       tiles * 2 <= 160 && kblocks >= 8) {
     q.cluster_k = 2;
     q.splits = 2;

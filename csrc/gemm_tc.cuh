@@ -16,6 +16,8 @@ enum GemmStore : int {
                     // element (m, n) lands at C[z][m / T][n][m % T] (a (S, N, T) block)
   kPeerAtomicF32 = 5,  // fp32 atomics into the OWNER rank's copy of C over NVLink: element
                        // i = m * ldc + n goes to peers[(i / 4) / per4][i] (cross-rank reduce)
+  kStoreBF16Scatter = 6,  // bf16 row m stored into rank scatter[m].x's C at row scatter[m].y
+                          // (peer pointers; expert outputs returned to their source ranks)
 };
 
 // A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).
@@ -45,6 +47,7 @@ struct GemmParams {
   int world;
   long long per4;       // kPeerAtomicF32: float4 elements owned by each rank
   int self_rank;        // kPeerAtomicF32: this rank (its own slice takes vector atomics)
+  const int2* scatter;  // kStoreBF16Scatter: (rank, row) of every output row
 };
 
 // One job of a grouped launch (tensor maps in global memory, 64-byte aligned).

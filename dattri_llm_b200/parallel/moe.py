@@ -1,0 +1,215 @@
+"""Expert-parallel sparse MLP (OLMoE-style top-k routing) over NVLink peer memory.
+
+Experts are sharded over the ranks (``n_experts / world`` each); the router is replicated.
+One forward:
+
+1. route: router GEMM, softmax, top-k (PyTorch; its backward reaches the router);
+2. layout: per (owner rank, local expert) row counts are exchanged (a tiny NCCL
+   all-gather -- the control plane), and every rank derives the same receive layout:
+   each owner's rows grouped by local expert, then by source rank;
+3. dispatch: one kernel stores each (token, slot) row straight into its owner's receive
+   buffer (16-byte peer stores, ``moe_dispatch``) with its origin;
+4. experts: per local expert a tcgen05 gate/up GEMM, SwiGLU, and the down GEMM whose
+   EPILOGUE stores every output row back into its source rank's combine buffer over NVLink
+   (``gemm_tn_scatter``) -- the combine all-to-all happens inside the GEMM;
+5. combine: each source sums its k returned rows weighted by the router probabilities.
+
+The backward mirrors it: slot gradients are dispatched to the owners, the experts'
+input-gradient GEMM (against the transposed gate/up weights) returns its rows to the
+sources from its epilogue, and the router weights get ``<dy, expert output>``.
+Bounded cross-GPU barriers separate the phases.  The reference has no expert parallelism
+(it captures MoE layers with replicated experts, ``dattri_llm/gradient/hooks/routing.py``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
+
+
+def _gemm_bf16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    from dattri_llm_b200 import ops
+
+    out = torch.empty(a.shape[0], b.shape[0], dtype=torch.bfloat16, device=a.device)
+    ops.gemm_tn(a.contiguous(), b, out, mode=ops.STORE_BF16)
+    return out
+
+
+class _EPMoE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2, topv, topi, mod):
+        from dattri_llm_b200 import ops
+
+        t, k = topi.shape
+        world, rank, e_l = mod.world, mod.rank, mod.experts_per_rank
+        dev = x2.device
+        if t > mod.max_tokens:
+            raise ValueError(f"{t} tokens exceed this layer's capacity of {mod.max_tokens} per rank")
+        dest = (topi // e_l).reshape(-1)
+        le = (topi % e_l).reshape(-1)
+        key = dest * e_l + le
+        counts = torch.bincount(key, minlength=world * e_l)  # (world_dst * e_l)
+        all_counts = torch.empty(world, world * e_l, dtype=counts.dtype, device=dev)
+        dist.all_gather_into_tensor(all_counts, counts, group=mod.group)
+        cnt = all_counts.view(world, world, e_l)  # [src, dst, local expert]
+        # receive layout of owner r: by local expert, then by source rank
+        per_le = cnt.sum(0)                                       # [dst, le]
+        le_base = torch.cumsum(per_le, 1) - per_le                # [dst, le]
+        src_base = torch.cumsum(cnt, 0) - cnt                     # [src, dst, le]
+        off = le_base[None] + src_base                            # [src, dst, le]
+        order = torch.argsort(key, stable=True)
+        grp_start = torch.cumsum(counts, 0) - counts
+        rank_in = torch.empty_like(key)
+        rank_in[order] = torch.arange(key.numel(), device=dev) - grp_start[key[order]]
+        dst_row = off[rank].reshape(-1)[key] + rank_in
+        mine = per_le[rank]                                       # rows I receive, per local expert
+        total_in = int(mine.sum())
+        if total_in > mod.capacity:
+            raise RuntimeError(f"received {total_in} rows > capacity {mod.capacity}")
+        dest32, row32 = dest.to(torch.int32).contiguous(), dst_row.to(torch.int32).contiguous()
+
+        mod.barrier.wait()  # every rank is done with the previous use of the receive buffers
+        ops.count_launch()
+        ops.native().moe_dispatch(x2, k, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, rank)
+        mod.barrier.wait()  # every row has landed
+
+        bases = (torch.cumsum(mine, 0) - mine).tolist()
+        ns = mine.tolist()
+        hs = []
+        for j in range(e_l):
+            n, b0 = ns[j], bases[j]
+            if n == 0:
+                hs.append(None)
+                continue
+            xe = mod.recv_x.local[b0:b0 + n]
+            h = _gemm_bf16(xe, mod.gate_up[j])                    # (n, 2I)
+            g, u = h.chunk(2, dim=-1)
+            a = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+            ops.count_launch()
+            ops.native().gemm_tn_scatter(a, mod.down[j], mod.combine.peers, mod.recv_meta.local[b0:b0 + n],
+                                         1.0, ops.error_word(dev))
+            hs.append(h)
+        mod.barrier.wait()  # every output row is home
+        slots = mod.combine.local[:t * k].view(t, k, -1).clone()
+        y = (slots.float() * topv.float()[..., None]).sum(1).to(torch.bfloat16)
+        ctx.mod = mod
+        ctx.save_for_backward(topv, slots, dest32, row32)
+        ctx.hs, ctx.ns, ctx.bases = hs, ns, bases
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from dattri_llm_b200 import ops
+
+        mod = ctx.mod
+        topv, slots, dest32, row32 = ctx.saved_tensors
+        t, k = topv.shape
+        dev = dy.device
+        dyf = dy.float()
+        dtopv = (slots.float() * dyf[:, None, :]).sum(-1).to(topv.dtype)
+        dslot = (dyf[:, None, :] * topv.float()[..., None]).to(torch.bfloat16).reshape(t * k, -1).contiguous()
+        mod.barrier.wait()
+        ops.count_launch()
+        ops.native().moe_dispatch(dslot, 1, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, mod.rank)
+        mod.barrier.wait()
+        for j in range(mod.experts_per_rank):
+            n, b0 = ctx.ns[j], ctx.bases[j]
+            if n == 0:
+                continue
+            dout = mod.recv_x.local[b0:b0 + n]
+            da = _gemm_bf16(dout, mod.down_t[j])                  # (n, I)
+            g, u = ctx.hs[j].float().chunk(2, dim=-1)
+            s = torch.sigmoid(g)
+            dg = da.float() * u * (s + g * s * (1 - s))
+            du = da.float() * g * s
+            dh = torch.cat([dg, du], -1).to(torch.bfloat16)
+            ops.count_launch()
+            ops.native().gemm_tn_scatter(dh, mod.gate_up_t[j], mod.dx_slots.peers, mod.recv_meta.local[b0:b0 + n],
+                                         1.0, ops.error_word(dev))
+        mod.barrier.wait()
+        dx = mod.dx_slots.local[:t * k].view(t, k, -1).float().sum(1).to(torch.bfloat16)
+        return dx, dtopv, None, None
+
+
+class _Buffers:
+    """Symmetric receive / combine buffers and the barrier, shared by every EP layer of one
+    shape on a device (the layers run one after another on one stream)."""
+
+    _pool: dict = {}
+
+    def __init__(self, capacity: int, slots: int, hidden: int, dev: torch.device, group) -> None:
+        self.recv_x = SymmetricBuffer((capacity, hidden), torch.bfloat16, dev, group)
+        self.recv_meta = SymmetricBuffer((capacity, 2), torch.int32, dev, group)
+        self.combine = SymmetricBuffer((slots, hidden), torch.bfloat16, dev, group)
+        self.dx_slots = SymmetricBuffer((slots, hidden), torch.bfloat16, dev, group)
+        self.barrier = PeerBarrier(dev, group)
+
+    @classmethod
+    def get(cls, capacity: int, slots: int, hidden: int, dev: torch.device, group) -> _Buffers:
+        key = (capacity, slots, hidden, dev, id(group))
+        if key not in cls._pool:
+            cls._pool[key] = cls(capacity, slots, hidden, dev, group)
+        return cls._pool[key]
+
+
+class ExpertParallelMoE(nn.Module):
+    """Top-k MoE MLP with experts sharded over the process group (frozen experts: the
+    attribution probe's case; the router may train).  Build collectively."""
+
+    def __init__(self, hidden: int, intermediate: int, n_experts: int, top_k: int, *, max_tokens: int,
+                 norm_topk_prob: bool = False, group=None, device: torch.device | None = None) -> None:
+        super().__init__()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_experts % self.world:
+            raise ValueError(f"{n_experts} experts do not split over {self.world} ranks")
+        if hidden % 8 or intermediate % 8:
+            raise ValueError("hidden and intermediate sizes must be multiples of 8")
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.hidden, self.intermediate, self.n_experts, self.top_k = hidden, intermediate, n_experts, top_k
+        self.experts_per_rank = n_experts // self.world
+        self.norm_topk_prob = norm_topk_prob
+        self.max_tokens = max_tokens
+        self.capacity = self.world * max_tokens * top_k
+        self.gate = nn.Linear(hidden, n_experts, bias=False, device=dev, dtype=torch.bfloat16)
+        e_l = self.experts_per_rank
+        self.register_buffer("gate_up", torch.zeros(e_l, 2 * intermediate, hidden, device=dev, dtype=torch.bfloat16))
+        self.register_buffer("down", torch.zeros(e_l, hidden, intermediate, device=dev, dtype=torch.bfloat16))
+        self.register_buffer("gate_up_t", torch.zeros(e_l, hidden, 2 * intermediate, device=dev, dtype=torch.bfloat16))
+        self.register_buffer("down_t", torch.zeros(e_l, intermediate, hidden, device=dev, dtype=torch.bfloat16))
+        bufs = _Buffers.get(self.capacity, max_tokens * top_k, hidden, dev, group)
+        self.recv_x, self.recv_meta = bufs.recv_x, bufs.recv_meta
+        self.combine, self.dx_slots, self.barrier = bufs.combine, bufs.dx_slots, bufs.barrier
+
+    @torch.no_grad()
+    def load_experts(self, gate_up_all: torch.Tensor, down_all: torch.Tensor, router: torch.Tensor) -> None:
+        """Take this rank's slice of the full ``(E, 2I, H)`` / ``(E, H, I)`` expert weights and
+        the ``(E, H)`` router weight (identical on every rank)."""
+        e_l, r = self.experts_per_rank, self.rank
+        gu = gate_up_all[r * e_l:(r + 1) * e_l].to(self.gate_up.device, torch.bfloat16)
+        dn = down_all[r * e_l:(r + 1) * e_l].to(self.down.device, torch.bfloat16)
+        self.gate_up.copy_(gu)
+        self.down.copy_(dn)
+        self.gate_up_t.copy_(gu.transpose(1, 2))
+        self.down_t.copy_(dn.transpose(1, 2))
+        self.gate.weight.copy_(router.to(self.gate.weight.device, torch.bfloat16))
+
+    def route(self, x2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(top-k probabilities, top-k expert ids)`` of every token."""
+        probs = torch.softmax(self.gate(x2).float(), dim=-1)
+        topv, topi = probs.topk(self.top_k, dim=-1)
+        if self.norm_topk_prob:
+            topv = topv / topv.sum(-1, keepdim=True)
+        return topv, topi
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.hidden).to(torch.bfloat16).contiguous()
+        topv, topi = self.route(x2)
+        y = _EPMoE.apply(x2, topv, topi, self)
+        return y.view(*shape[:-1], self.hidden)

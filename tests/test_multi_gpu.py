@@ -140,6 +140,70 @@ def test_fused_score_allreduce_and_covariance_match_nccl():
     assert max(errs.values()) < 1e-2, errs
 
 
+def _moe_worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from dattri_llm_b200 import ops
+        from dattri_llm_b200.parallel.moe import ExpertParallelMoE
+
+        h, inter, n_exp, k = 128, 64, 8, 2
+        g = torch.Generator(device=dev).manual_seed(11)  # same weights on every rank
+        gate_up = (0.1 * torch.randn(n_exp, 2 * inter, h, device=dev, generator=g)).bfloat16()
+        down = (0.1 * torch.randn(n_exp, h, inter, device=dev, generator=g)).bfloat16()
+        router = (0.1 * torch.randn(n_exp, h, device=dev, generator=g)).bfloat16()
+        moe = ExpertParallelMoE(h, inter, n_exp, k, max_tokens=256)
+        moe.load_experts(gate_up, down, router)
+        gx = torch.Generator(device=dev).manual_seed(50 + rank)
+        worst = 0.0
+        for _ in range(2):
+            x = torch.randn(3, 37, h, device=dev, generator=gx).bfloat16().requires_grad_()
+            y = moe(x)
+            dy = torch.randn_like(y)
+            y.backward(dy)
+            # replicated-expert reference in fp32 on this rank's tokens
+            xr = x.detach().float().reshape(-1, h).requires_grad_()
+            # the same bf16 router GEMM as the module, so near-ties pick the same experts
+            probs = torch.softmax(F.linear(xr.bfloat16(), router).float(), -1)
+            topv, topi = probs.topk(k, -1)
+            out = torch.zeros_like(xr)
+            for j in range(k):
+                e = topi[:, j]
+                hh = torch.einsum("th,tnh->tn", xr, gate_up.float()[e])
+                gg, uu = hh.chunk(2, -1)
+                a = F.silu(gg) * uu
+                out = out + topv[:, j:j + 1] * torch.einsum("ti,thi->th", a, down.float()[e])
+            out.backward(dy.float().reshape(-1, h))
+            for got, want in ((y.float().reshape(-1, h), out.detach()), (x.grad.float().reshape(-1, h), xr.grad)):
+                worst = max(worst, float((got - want).abs().max() / want.abs().max()))
+            x.grad = None
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        results[rank] = worst
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_moe_matches_replicated():
+    world = 2
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_moe_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(errs.values()) < 3e-2, errs
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_sharded_linear_fused_collectives_match_dense():
     world = 2
