@@ -141,6 +141,24 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
     secs = _time(lambda: nat.gemm_tn_peer(xt, xt, ptrs, world, per4, w, w, w, 1.0, 4, err, rank))
     report("gemm_tn_peer (Gram / wgrad GEMM + cross-rank reduce in the epilogue)", secs, 2.0 * w * w * m,
            (world - 1) / world * w * w * 4 * 4, 2 * w * m * 2 + w * w * 4 * 4)
+    # 5) expert-parallel MoE (real ranks only): dispatch + experts + combine-in-epilogue
+    if not emulate:
+        from dattri_llm_b200.parallel.moe import ExpertParallelMoE
+
+        h, inter, n_exp, top_k, t = 2048, 1024, 64, 8, 4096
+        g = torch.Generator(device=dev).manual_seed(11)
+        moe = ExpertParallelMoE(h, inter, n_exp, top_k, max_tokens=t)
+        moe.load_experts((0.02 * torch.randn(n_exp, 2 * inter, h, device=dev, generator=g)).bfloat16(),
+                         (0.02 * torch.randn(n_exp, h, inter, device=dev, generator=g)).bfloat16(),
+                         (0.02 * torch.randn(n_exp, h, device=dev, generator=g)).bfloat16())
+        xm = torch.randn(t, h, device=dev, generator=gen).bfloat16()
+        with torch.no_grad():
+            secs = _time(lambda: moe(xm), iters=10)
+        rows_moved = t * top_k * (world - 1) / world
+        report("expert-parallel MoE forward (dispatch + expert GEMMs + combine in the down-GEMM epilogue)",
+               secs, 2.0 * t * top_k * (h * 2 * inter + inter * h) + 2.0 * t * h * n_exp,
+               2 * rows_moved * h * 2, 4 * t * top_k * h * 2,
+               {"tokens_per_rank": t, "experts": n_exp, "top_k": top_k})
     ops.check_device_errors(dev)
     return rows
 
