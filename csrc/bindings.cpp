@@ -22,6 +22,7 @@
 #include "peer_sync.cuh"
 #include "allreduce_p2p.cuh"
 #include "moe_ep.cuh"
+#include "norm_grad.cuh"
 
 namespace {
 
@@ -619,6 +620,33 @@ void gemm_tn_scatter(Tensor A, Tensor B, std::vector<Tensor> peer_C, Tensor scat
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
+// Per-sample LayerNorm / RMSNorm parameter gradients from the raw input x (B, T, d) and the
+// output gradient g: returns (B, d) dgamma, or (B, 2d) [dgamma | dbeta] with `bias`.
+Tensor norm_per_sample_grad(Tensor x, Tensor g, double eps, bool layer_norm, bool bias) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && g.scalar_type() == torch::kBFloat16 &&
+                  x.dim() == 3 && x.sizes() == g.sizes() && x.is_contiguous() && g.is_contiguous(),
+              "x and g must be contiguous (B, T, d) bf16");
+  const int d = (int)x.size(2);
+  TORCH_CHECK(d % 8 == 0 && d <= 16384, "d must be a multiple of 8 and <= 16384");
+  const int B = (int)x.size(0), T = (int)x.size(1);
+  auto out = torch::zeros({B, bias ? 2 * d : d}, x.options().dtype(torch::kFloat32));
+  float* dw = out.data_ptr<float>();
+  // (B, 2d) rows interleave as [dgamma | dbeta]: write through strided views.
+  Tensor wv = bias ? torch::zeros({B, d}, out.options()) : out;
+  Tensor bv = bias ? torch::zeros({B, d}, out.options()) : Tensor();
+  if (bias) dw = wv.data_ptr<float>();
+  bw::norm_per_sample_grad(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                           reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), dw,
+                           bias ? bv.data_ptr<float>() : nullptr, B, T, d, (float)eps, layer_norm,
+                           at::cuda::getCurrentCUDAStream());
+  if (bias) {
+    out.narrow(1, 0, d).copy_(wv);
+    out.narrow(1, d, d).copy_(bv);
+  }
+  return out;
+}
+
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
 std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
   TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
@@ -863,6 +891,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
+  m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
   m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");

@@ -129,6 +129,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     matmul_tn,
 )
 from dattri_llm_b200.ops.gram import ghost_gram, per_sample_outer  # noqa: E402
+from dattri_llm_b200.ops.norm import norm_per_sample_grad  # noqa: E402
 from dattri_llm_b200.ops.optim import adam_direction  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
 
@@ -149,6 +150,7 @@ __all__ = [
     "ghost_gram",
     "matmul_tn",
     "native",
+    "norm_per_sample_grad",
     "per_sample_outer",
     "projection_matrix_t",
     "use_native",

@@ -136,3 +136,25 @@ def test_llama_fused_blocks_match_unfused():
     assert abs(outs[0][0] - outs[1][0]) / abs(outs[1][0]) < 2e-2
     torch.testing.assert_close(outs[0][1], outs[1][1], rtol=5e-2, atol=5e-2)
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("kind", ["nn.RMSNorm", "nn.LayerNorm"])
+@pytest.mark.parametrize("bias", [False, True])
+def test_norm_per_sample_grad_matches_torch(kind, bias):
+    from dattri_llm_b200.gradient.ops.materialize import materialize_factors
+
+    b, t, d = 5, 77, 1024
+    x = torch.randn(b, t, d, device="cuda").bfloat16()
+    g = torch.randn(b, t, d, device="cuda").bfloat16()
+    mk = {"has_bias": bias, "eps": 1e-5, "normalized_shape": (d,)}
+    got = materialize_factors(x, g, kind, mk)
+    xf, gf = x.float(), g.float()
+    if kind == "nn.LayerNorm":
+        xh = (xf - xf.mean(-1, keepdim=True)) / (xf.var(-1, unbiased=False, keepdim=True) + 1e-5).sqrt()
+    else:
+        xh = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)
+    want = (xh * gf).sum(1)
+    if bias:
+        want = torch.cat([want, gf.sum(1)], 1)
+    torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-2)
+    ops.check_device_errors()
