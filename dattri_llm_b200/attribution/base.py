@@ -15,6 +15,7 @@ saving and within the device memory budget; the rest is preprocessed once.
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import AttributionGranularity  # noqa: F401  (re-exported option types)
 import tempfile
 import warnings
 from abc import ABC, abstractmethod

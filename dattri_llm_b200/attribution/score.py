@@ -10,6 +10,7 @@ device holds the scores.
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import ScoreTrajectory  # noqa: F401  (re-exported option types)
 import json
 from collections.abc import Sequence
 from dataclasses import dataclass, field

@@ -19,6 +19,7 @@ B200 execution differences:
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import AttributionGranularity  # noqa: F401  (re-exported option types)
 import json
 import pathlib
 from collections.abc import Callable, Iterable, Mapping

@@ -12,6 +12,7 @@ averaged as one shared row.  These semantics are part of the stored format.
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import CaptureStyle  # noqa: F401  (re-exported option types)
 from collections.abc import Callable, Iterable, Sequence
 from dataclasses import InitVar, dataclass, field
 from typing import Literal

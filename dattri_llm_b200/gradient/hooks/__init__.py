@@ -21,6 +21,12 @@ from dattri_llm_b200.gradient.hooks.hooks import (
     remove_hooks,
 )
 from dattri_llm_b200.gradient.hooks.manager import HookManager
+from dattri_llm_b200.gradient.hooks.override_layers.fused_experts import (
+    RouterLinear,
+    SliceLinear,
+    find_fused_experts,
+)
+from dattri_llm_b200.gradient.hooks.routing import RoutedTokenTracker, RowLayout
 from dattri_llm_b200.gradient.hooks.override_layers import (
     install_fused_experts,
     install_invasive_forward,
@@ -30,6 +36,11 @@ from dattri_llm_b200.gradient.callbacks.base import HookManagerCallback
 
 __all__ = [
     "HF_Conv1D",
+    "RoutedTokenTracker",
+    "RouterLinear",
+    "RowLayout",
+    "SliceLinear",
+    "find_fused_experts",
     "INVASIVE_LINEAR_IO",
     "LINEAR_IO",
     "PARAM_GRAD",

@@ -6,7 +6,7 @@ sm_100 device the hot contractions dispatch to the native kernels of
 :mod:`dattri_llm_b200.ops`.
 """
 
-from dattri_llm_b200.gradient.ops import dtypes
+from dattri_llm_b200.gradient.ops import dtypes, norm
 from dattri_llm_b200.gradient.ops.dot import (
     cross_dot,
     cross_dot_factors,

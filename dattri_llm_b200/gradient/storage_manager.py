@@ -22,6 +22,7 @@ ids continue after the highest existing one).
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import CacheResidency, DiskFormat  # noqa: F401  (re-exported option types)
 import contextlib
 import json
 import operator

@@ -10,6 +10,7 @@ to make room.
 
 from __future__ import annotations
 
+from dattri_llm_b200.options import CacheResidency  # noqa: F401  (re-exported option types)
 import contextlib
 import shutil
 import tempfile
