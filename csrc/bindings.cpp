@@ -647,6 +647,75 @@ Tensor norm_per_sample_grad(Tensor x, Tensor g, double eps, bool layer_norm, boo
   return out;
 }
 
+// Ragged grouped GEMM of expert layers: rows [base[j], base[j] + len[j]) of A times B3[j]^T;
+// output rows stored in C (same row index) or, with `scatter`, returned to their source
+// ranks' buffers peer_C.  tile_prefix / base / len are device int32 arrays; max_tiles bounds
+// the number of 128-row tiles (CTAs past the real count return at once).
+void gemm_ragged(Tensor A, Tensor B3, c10::optional<Tensor> C, Tensor tile_prefix, Tensor base, Tensor len,
+                 int64_t max_tiles, std::vector<Tensor> peer_C, c10::optional<Tensor> scatter, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B3, "B3");
+  TORCH_CHECK(a.batch == 1 && B3.dim() == 3 && a.cols == b.cols, "A (R, K) and B3 (J, N, K)");
+  const int jobs = (int)b.batch;
+  for (auto* t : {&tile_prefix, &base, &len})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(), "job arrays: int32 CUDA");
+  TORCH_CHECK(tile_prefix.numel() == jobs + 1 && base.numel() == jobs && len.numel() == jobs, "job array sizes");
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = (int)b.rows;
+  p.K = (int)a.cols;
+  p.alpha = 1.f;
+  p.err = err.data_ptr<int>();
+  Tensor ptrs;
+  if (scatter.has_value() && scatter->defined()) {
+    TORCH_CHECK(scatter->scalar_type() == torch::kInt32 && scatter->is_contiguous() && scatter->numel() >= 2 * a.rows,
+                "scatter: int32 (R, 2)");
+    for (auto& c : peer_C)
+      TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows,
+                  "peer outputs must be contiguous (R, N) bf16");
+    ptrs = device_ptr_table(peer_C, A.device());
+    p.c_mode = bw::kStoreBF16Scatter;
+    p.peers = reinterpret_cast<float* const*>(ptrs.data_ptr<int64_t>());
+    p.world = (int)peer_C.size();
+    p.scatter = reinterpret_cast<const int2*>(scatter->data_ptr<int>());
+    p.ldc = b.rows;
+  } else {
+    TORCH_CHECK(C.has_value() && C->defined() && C->scalar_type() == torch::kBFloat16 && C->dim() == 2 &&
+                    C->size(0) == a.rows && C->size(1) == b.rows && C->stride(1) == 1, "C must be (R, N) bf16");
+    p.c_mode = bw::kStoreBF16;
+    p.C = C->data_ptr();
+    p.ldc = C->stride(0);
+  }
+  if (max_tiles <= 0 || p.N == 0) return;
+  bw::gemm_ragged_launch(a, b, p, tile_prefix.data_ptr<int>(), base.data_ptr<int>(), len.data_ptr<int>(), jobs,
+                         (int)max_tiles, std::max(64, bw::pick_bn(p.N)), at::cuda::getCurrentCUDAStream());
+}
+
+void swiglu_split(Tensor h, Tensor out, Tensor rows) {
+  const c10::cuda::CUDAGuard guard(h.device());
+  TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && h.is_contiguous() && h.dim() == 2 && h.size(1) % 16 == 0,
+              "h: contiguous (R, 2I) bf16, I % 8 == 0");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) == h.size(0) &&
+                  out.size(1) * 2 == h.size(1), "out: (R, I) bf16");
+  TORCH_CHECK(rows.is_cuda() && rows.scalar_type() == torch::kInt32 && rows.numel() >= 1, "rows: int32 CUDA scalar");
+  bw::swiglu_split(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                   rows.data_ptr<int>(), (int)h.size(0), (int)out.size(1),
+                   at::cuda::getCurrentCUDAStream());
+}
+
+void swiglu_split_bwd(Tensor da, Tensor h, Tensor dh, Tensor rows) {
+  const c10::cuda::CUDAGuard guard(h.device());
+  TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && h.is_contiguous() && da.is_contiguous() && dh.is_contiguous() &&
+                  da.size(1) * 2 == h.size(1) && dh.sizes() == h.sizes() && da.size(1) % 8 == 0,
+              "da (R, I), h and dh (R, 2I): contiguous bf16");
+  bw::swiglu_split_bwd(reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()),
+                       reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dh.data_ptr()),
+                       rows.data_ptr<int>(), (int)h.size(0), (int)da.size(1),
+                       at::cuda::getCurrentCUDAStream());
+}
+
 // Peer all-reduce phases over symmetric fp32 buffers (see allreduce_p2p.cu).
 std::vector<const float*> peer_floats(const std::vector<Tensor>& peers, long long n) {
   TORCH_CHECK(!peers.empty() && (int)peers.size() <= bw::allreduce_max_peers(), "1..16 peer buffers");
@@ -892,6 +961,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
+  m.def("gemm_ragged", &gemm_ragged, "ragged grouped GEMM over expert row segments (optionally scattered home)");
+  m.def("swiglu_split", &swiglu_split);
+  m.def("swiglu_split_bwd", &swiglu_split_bwd);
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
   m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");

@@ -74,7 +74,8 @@ template <int BN>
 __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmParams& p,
                                          int za, int zb, int zc, int split, void* Cbase, int b_row_off = 0,
                                          const CUtensorMap* kpeers = nullptr, int kshard = 0,
-                                         const StageCtl* stage = nullptr) {
+                                         const StageCtl* stage = nullptr, int m0_override = -1,
+                                         int row_limit = -1) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
@@ -89,7 +90,7 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
+  const int m0 = m0_override >= 0 ? m0_override : blockIdx.y * BM;
 
   const int kblocks = (p.K + BK - 1) / BK;
   const int per = (kblocks + p.splits - 1) / p.splits;
@@ -173,7 +174,7 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
   __syncwarp();
   tc_fence_after();
   const int row = m0 + warp * 32 + lane;
-  const bool row_ok = row < p.M;
+  const bool row_ok = row < (row_limit >= 0 ? row_limit : p.M);
   const float alpha = p.alpha;
   // Cluster split-K: the peer CTA (rank 1) writes its fp32 partial tile into rank 0's shared
   // memory (column-major, so a warp's 32 rows are 32 consecutive words), then both meet at a
@@ -433,6 +434,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   gemm_cta<BN>(&tmA, &tmStage, p, 0, 0, 0, 0, p.C, 0, nullptr, 0, &sc);
 }
 
+// Ragged grouped GEMM (expert layers): job j multiplies the rows [base[j], base[j] + len[j])
+// of one A matrix by its own B = B3[j] (a 3-D weight tensor, one map); CTA (x, t) serves
+// N tile x of the t-th 128-row tile in job order (tile_prefix = exclusive prefix of the
+// per-job tile counts, computed on the device).  CTAs past the last tile return at once, so
+// the grid can be an upper bound and no host synchronisation is needed.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ragged_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       GemmParams p, const int* __restrict__ tile_prefix, const int* __restrict__ base,
+                       const int* __restrict__ len, int jobs) {
+  const int t = blockIdx.y;
+  if (t >= tile_prefix[jobs]) return;
+  int j = 0;
+  while (j + 1 < jobs && tile_prefix[j + 1] <= t) ++j;
+  const int m0 = base[j] + (t - tile_prefix[j]) * BM;
+  gemm_cta<BN>(&tmA, &tmB, p, 0, j, 0, 0, p.C, 0, nullptr, 0, nullptr, m0, base[j] + len[j]);
+}
+
 // B held by the peers (sharded weights, read over NVLink through per-peer tensor maps in the
 // kernel's parameters; no multicast).  mode 0: peer r owns B rows [r*shard, (r+1)*shard)
 // (the forward GEMM of a row-sharded weight); mode 1: peer r owns B's K columns
@@ -559,6 +578,23 @@ void launch_staged_bn(const GemmOperand& A, const GemmOperand& stage_op, const G
 }
 
 template <int BN>
+void launch_ragged_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const int* tile_prefix,
+                      const int* base, const int* len, int jobs, int max_tiles, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured >> dev & 1ull)) {
+    cudaFuncSetAttribute(gemm_ragged_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    configured |= 1ull << dev;
+  }
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, BM);
+  CUtensorMap tb = make_tmap_kmajor_bf16(B, BN);
+  dim3 grid((p.N + BN - 1) / BN, max_tiles, 1);
+  gemm_ragged_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, tb, p, tile_prefix, base, len, jobs);
+}
+
+template <int BN>
 void launch_grouped_bn(const GroupJob* jobs, int n_jobs, const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN>;
   static unsigned long long configured = 0;  // one bit per device
@@ -598,6 +634,19 @@ void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const
     case 128: launch_staged_bn<128>(A, stage_op, own, p, sa, stream); break;
     case 256: launch_staged_bn<256>(A, stage_op, own, p, sa, stream); break;
     default: throw std::runtime_error("gemm_staged: unsupported tile width");
+  }
+}
+
+void gemm_ragged_launch(const GemmOperand& A, const GemmOperand& B3, GemmParams p, const int* tile_prefix,
+                        const int* base, const int* len, int jobs, int max_tiles, int bn, cudaStream_t stream) {
+  p.splits = 1;
+  p.batch = 1;
+  p.b_shared = 0;
+  switch (bn) {
+    case 64: launch_ragged_bn<64>(A, B3, p, tile_prefix, base, len, jobs, max_tiles, stream); break;
+    case 128: launch_ragged_bn<128>(A, B3, p, tile_prefix, base, len, jobs, max_tiles, stream); break;
+    case 256: launch_ragged_bn<256>(A, B3, p, tile_prefix, base, len, jobs, max_tiles, stream); break;
+    default: throw std::runtime_error("gemm_ragged: unsupported tile width");
   }
 }
 

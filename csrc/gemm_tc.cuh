@@ -83,6 +83,10 @@ CUtensorMap make_tmap_kmajor_bf16(const GemmOperand& op, int box_rows);
 void gemm_peers_launch(const GemmOperand& A, const CUtensorMap* pm, GemmParams p, int mode, int shard, int bn,
                        cudaStream_t stream);
 void gemm_grouped_launch(const GroupJob* jobs, int n_jobs, GemmParams p, int bn, cudaStream_t stream);
+// Ragged grouped GEMM: A (rows, K) with per-job row segments, B3 (jobs, N, K); device arrays
+// tile_prefix[jobs + 1], base[jobs], len[jobs]; grid height max_tiles (an upper bound).
+void gemm_ragged_launch(const GemmOperand& A, const GemmOperand& B3, GemmParams p, const int* tile_prefix,
+                        const int* base, const int* len, int jobs, int max_tiles, int bn, cudaStream_t stream);
 // mode 0: B rows sharded (stage_op = the (N, K) staging matrix, own = this rank's (shard, K));
 // mode 1: B's K sharded (stage_op = the (N, K) staging matrix, own = this rank's (N, shard)).
 void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const GemmOperand& own, GemmParams p,

@@ -249,6 +249,46 @@ __global__ void adam_dir_kernel(const float4* __restrict__ g, const float4* __re
   }
 }
 
+// ------------------------------------------------------------------ SwiGLU on [gate | up] rows
+// h (rows, 2I) holds the gate half then the up half of each row; out (rows, I) = silu(gate) * up.
+// `rows` is read from device memory (the count of valid rows is known only on the device).
+__global__ void swiglu_split_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ out,
+                                        const int* __restrict__ rows, int inter) {
+  const long long n = (long long)(*rows) * (inter / 8);
+  const int iv = inter / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / iv, c = i % iv;
+    float g[8], u[8];
+    unpack8(reinterpret_cast<const Bf8*>(h + r * 2 * inter)[c], g);
+    unpack8(reinterpret_cast<const Bf8*>(h + r * 2 * inter + inter)[c], u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+    reinterpret_cast<Bf8*>(out + r * inter)[c] = pack8(g);
+  }
+}
+
+// dh[:, :I] = da * u * s * (1 + g (1 - s)),  dh[:, I:] = da * g * s,  s = sigmoid(g)
+__global__ void swiglu_split_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ h,
+                                        __nv_bfloat16* __restrict__ dh, const int* __restrict__ rows, int inter) {
+  const long long n = (long long)(*rows) * (inter / 8);
+  const int iv = inter / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / iv, c = i % iv;
+    float d[8], g[8], u[8], og[8], ou[8];
+    unpack8(reinterpret_cast<const Bf8*>(da + r * inter)[c], d);
+    unpack8(reinterpret_cast<const Bf8*>(h + r * 2 * inter)[c], g);
+    unpack8(reinterpret_cast<const Bf8*>(h + r * 2 * inter + inter)[c], u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sg = 1.f / (1.f + __expf(-g[j]));
+      og[j] = d[j] * u[j] * sg * (1.f + g[j] * (1.f - sg));
+      ou[j] = d[j] * g[j] * sg;
+    }
+    reinterpret_cast<Bf8*>(dh + r * 2 * inter)[c] = pack8(og);
+    reinterpret_cast<Bf8*>(dh + r * 2 * inter + inter)[c] = pack8(ou);
+  }
+}
+
 int grid_cap(long long work, int threads) {
   const long long b = (work + threads - 1) / threads;
   return (int)(b < 1 ? 1 : (b < 148 * 16 ? b : 148 * 16));
@@ -286,6 +326,18 @@ void rope(const RopeArgs& a, bool inverse, cudaStream_t s) {
 }
 
 bool rope_supported(int head_dim, int heads) { return head_dim % 16 == 0 && heads * (head_dim / 16) <= 1024; }
+
+void swiglu_split(const __nv_bfloat16* h, __nv_bfloat16* out, const int* rows, int max_rows, int inter,
+                  cudaStream_t s) {
+  if (max_rows <= 0) return;
+  swiglu_split_fwd_kernel<<<grid_cap((long long)max_rows * inter / 8, 256), 256, 0, s>>>(h, out, rows, inter);
+}
+
+void swiglu_split_bwd(const __nv_bfloat16* da, const __nv_bfloat16* h, __nv_bfloat16* dh, const int* rows,
+                      int max_rows, int inter, cudaStream_t s) {
+  if (max_rows <= 0) return;
+  swiglu_split_bwd_kernel<<<grid_cap((long long)max_rows * inter / 8, 256), 256, 0, s>>>(da, h, dh, rows, inter);
+}
 
 void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
                     float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s) {

@@ -49,6 +49,10 @@ void rows_norm_fwd(const RowsNorm& a, cudaStream_t s);
 void rows_norm_bwd(const RowsNormBwd& a, cudaStream_t s);
 void rope(const RopeArgs& a, bool inverse, cudaStream_t s);
 bool rope_supported(int head_dim, int heads);  // heads = q heads + k heads
+// SwiGLU over [gate | up] rows (rows read from device memory; max_rows sizes the grid).
+void swiglu_split(const __nv_bfloat16* h, __nv_bfloat16* out, const int* rows, int max_rows, int inter, cudaStream_t s);
+void swiglu_split_bwd(const __nv_bfloat16* da, const __nv_bfloat16* h, __nv_bfloat16* dh, const int* rows,
+                      int max_rows, int inter, cudaStream_t s);
 void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
                     float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s);
 

@@ -9,9 +9,10 @@ One forward:
    each owner's rows grouped by local expert, then by source rank;
 3. dispatch: one kernel stores each (token, slot) row straight into its owner's receive
    buffer (16-byte peer stores, ``moe_dispatch``) with its origin;
-4. experts: per local expert a tcgen05 gate/up GEMM, SwiGLU, and the down GEMM whose
-   EPILOGUE stores every output row back into its source rank's combine buffer over NVLink
-   (``gemm_tn_scatter``) -- the combine all-to-all happens inside the GEMM;
+4. experts: ONE ragged tcgen05 GEMM over all local experts' row segments (gate/up), a
+   split SwiGLU, and ONE ragged down GEMM whose EPILOGUE stores every output row back into
+   its source rank's combine buffer over NVLink (``kStoreBF16Scatter``) -- the combine
+   all-to-all happens inside the GEMM;
 5. combine: each source sums its k returned rows weighted by the router probabilities.
 
 The backward mirrors it: slot gradients are dispatched to the owners, the experts'
@@ -31,12 +32,14 @@ from torch import nn
 from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
 
 
-def _gemm_bf16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    from dattri_llm_b200 import ops
-
-    out = torch.empty(a.shape[0], b.shape[0], dtype=torch.bfloat16, device=a.device)
-    ops.gemm_tn(a.contiguous(), b, out, mode=ops.STORE_BF16)
-    return out
+def _jobs(mine: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``(tile_prefix, base, len)`` int32 device arrays of the local experts' row segments."""
+    n = mine.to(torch.int32)
+    base = (torch.cumsum(n, 0) - n).to(torch.int32)
+    tiles = (n + 127) // 128
+    prefix = torch.zeros(n.numel() + 1, dtype=torch.int32, device=n.device)
+    prefix[1:] = torch.cumsum(tiles, 0)
+    return prefix, base.contiguous(), n.contiguous()
 
 
 class _EPMoE(torch.autograd.Function):
@@ -67,38 +70,34 @@ class _EPMoE(torch.autograd.Function):
         rank_in[order] = torch.arange(key.numel(), device=dev) - grp_start[key[order]]
         dst_row = off[rank].reshape(-1)[key] + rank_in
         mine = per_le[rank]                                       # rows I receive, per local expert
-        total_in = int(mine.sum())
-        if total_in > mod.capacity:
-            raise RuntimeError(f"received {total_in} rows > capacity {mod.capacity}")
         dest32, row32 = dest.to(torch.int32).contiguous(), dst_row.to(torch.int32).contiguous()
+        prefix, base, lens = _jobs(mine)
+        total_in = int(mine.sum())  # one host read per layer: sizes the expert buffers exactly
+        max_tiles = (total_in + 127) // 128 + e_l
+        rows_dev = mine.sum().to(torch.int32).reshape(1)
 
         mod.barrier.wait()  # every rank is done with the previous use of the receive buffers
         ops.count_launch()
         ops.native().moe_dispatch(x2, k, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, rank)
         mod.barrier.wait()  # every row has landed
 
-        bases = (torch.cumsum(mine, 0) - mine).tolist()
-        ns = mine.tolist()
-        hs = []
-        for j in range(e_l):
-            n, b0 = ns[j], bases[j]
-            if n == 0:
-                hs.append(None)
-                continue
-            xe = mod.recv_x.local[b0:b0 + n]
-            h = _gemm_bf16(xe, mod.gate_up[j])                    # (n, 2I)
-            g, u = h.chunk(2, dim=-1)
-            a = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
-            ops.count_launch()
-            ops.native().gemm_tn_scatter(a, mod.down[j], mod.combine.peers, mod.recv_meta.local[b0:b0 + n],
-                                         1.0, ops.error_word(dev))
-            hs.append(h)
+        err = ops.error_word(dev)
+        h = torch.empty(max(total_in, 1), 2 * mod.intermediate, dtype=torch.bfloat16, device=dev)
+        a = torch.empty(max(total_in, 1), mod.intermediate, dtype=torch.bfloat16, device=dev)
+        if total_in:
+            xin = mod.recv_x.local[:total_in]
+            ops.count_launch(3)
+            ops.native().gemm_ragged(xin, mod.gate_up, h, prefix, base, lens, max_tiles, [], None, err)
+            ops.native().swiglu_split(h, a, rows_dev)
+            # The down GEMM stores every output row back into its source rank's combine buffer.
+            ops.native().gemm_ragged(a[:total_in], mod.down, None, prefix, base, lens, max_tiles,
+                                     mod.combine.peers, mod.recv_meta.local[:total_in], err)
         mod.barrier.wait()  # every output row is home
         slots = mod.combine.local[:t * k].view(t, k, -1).clone()
         y = (slots.float() * topv.float()[..., None]).sum(1).to(torch.bfloat16)
         ctx.mod = mod
-        ctx.save_for_backward(topv, slots, dest32, row32)
-        ctx.hs, ctx.ns, ctx.bases = hs, ns, bases
+        ctx.save_for_backward(topv, slots, dest32, row32, h, prefix, base, lens, rows_dev)
+        ctx.total_in, ctx.max_tiles = total_in, max_tiles
         return y
 
     @staticmethod
@@ -106,7 +105,7 @@ class _EPMoE(torch.autograd.Function):
         from dattri_llm_b200 import ops
 
         mod = ctx.mod
-        topv, slots, dest32, row32 = ctx.saved_tensors
+        topv, slots, dest32, row32, h, prefix, base, lens, rows_dev = ctx.saved_tensors
         t, k = topv.shape
         dev = dy.device
         dyf = dy.float()
@@ -116,20 +115,18 @@ class _EPMoE(torch.autograd.Function):
         ops.count_launch()
         ops.native().moe_dispatch(dslot, 1, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, mod.rank)
         mod.barrier.wait()
-        for j in range(mod.experts_per_rank):
-            n, b0 = ctx.ns[j], ctx.bases[j]
-            if n == 0:
-                continue
-            dout = mod.recv_x.local[b0:b0 + n]
-            da = _gemm_bf16(dout, mod.down_t[j])                  # (n, I)
-            g, u = ctx.hs[j].float().chunk(2, dim=-1)
-            s = torch.sigmoid(g)
-            dg = da.float() * u * (s + g * s * (1 - s))
-            du = da.float() * g * s
-            dh = torch.cat([dg, du], -1).to(torch.bfloat16)
-            ops.count_launch()
-            ops.native().gemm_tn_scatter(dh, mod.gate_up_t[j], mod.dx_slots.peers, mod.recv_meta.local[b0:b0 + n],
-                                         1.0, ops.error_word(dev))
+        total_in = ctx.total_in
+        if total_in:
+            err = ops.error_word(dev)
+            dout = mod.recv_x.local[:total_in]
+            da = torch.empty(total_in, mod.intermediate, dtype=torch.bfloat16, device=dev)
+            dh = torch.empty_like(h[:total_in])
+            ops.count_launch(3)
+            ops.native().gemm_ragged(dout, mod.down_t, da, prefix, base, lens, ctx.max_tiles, [], None, err)
+            ops.native().swiglu_split_bwd(da, h[:total_in].contiguous(), dh, rows_dev)
+            # The input-gradient GEMM returns every row to its source rank.
+            ops.native().gemm_ragged(dh, mod.gate_up_t, None, prefix, base, lens, ctx.max_tiles,
+                                     mod.dx_slots.peers, mod.recv_meta.local[:total_in], err)
         mod.barrier.wait()
         dx = mod.dx_slots.local[:t * k].view(t, k, -1).float().sum(1).to(torch.bfloat16)
         return dx, dtopv, None, None

@@ -2,6 +2,7 @@
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 from dattri_llm_b200 import ops
 from dattri_llm_b200.ops import fused
@@ -158,3 +159,22 @@ def test_norm_per_sample_grad_matches_torch(kind, bias):
         want = torch.cat([want, gf.sum(1)], 1)
     torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-2)
     ops.check_device_errors()
+
+
+def test_swiglu_split_forward_backward():
+    """SwiGLU over ``[gate | up]`` rows with the valid-row count read from the device."""
+    rows, inter, valid = 300, 256, 217
+    h = torch.randn(rows, 2 * inter, device="cuda").bfloat16()
+    out = torch.zeros(rows, inter, device="cuda", dtype=torch.bfloat16)
+    n = torch.tensor([valid], dtype=torch.int32, device="cuda")
+    ops.native().swiglu_split(h, out, n)
+    hr = h.float().requires_grad_(True)
+    ref = F.silu(hr[:, :inter]) * hr[:, inter:]
+    torch.testing.assert_close(out[:valid].float(), ref[:valid].detach(), rtol=1e-2, atol=2e-2)
+    assert not out[valid:].any()
+    da = torch.randn(rows, inter, device="cuda").bfloat16()
+    dh = torch.zeros_like(h)
+    ops.native().swiglu_split_bwd(da, h, dh, n)
+    ref.backward(da.float())
+    torch.testing.assert_close(dh[:valid].float(), hr.grad[:valid], rtol=1e-2, atol=3e-2)
+    assert not dh[valid:].any()

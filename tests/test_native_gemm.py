@@ -139,3 +139,39 @@ def test_skinny_cluster_split_k(mode, m, n, k):
     tol = 2e-2 if mode in ("bf16", "bf16t", "seg") else 1e-3
     torch.testing.assert_close(got, want, rtol=tol, atol=tol * float(want.abs().max()))
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("scatter", [False, True])
+def test_gemm_ragged_expert_segments(scatter):
+    """Ragged grouped GEMM over expert row segments (empty and partial-tile segments
+    included), stored in place or scattered to rows of several destination buffers."""
+    lens = [0, 130, 7, 256, 0, 61]
+    n, kk = 192, 320
+    rows = sum(lens)
+    a = torch.randn(rows, kk, device="cuda").bfloat16()
+    b3 = torch.randn(len(lens), n, kk, device="cuda").bfloat16()
+    n_i = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    base = (torch.cumsum(n_i, 0) - n_i).int()
+    prefix = torch.zeros(len(lens) + 1, dtype=torch.int32, device="cuda")
+    prefix[1:] = torch.cumsum((n_i + 127) // 128, 0)
+    max_tiles = rows // 128 + len(lens) + 2  # an upper bound: surplus CTAs return at once
+    want = torch.empty(rows, n, device="cuda")
+    start = 0
+    for j, ln in enumerate(lens):
+        want[start:start + ln] = a[start:start + ln].float() @ b3[j].float().T
+        start += ln
+    err = ops.error_word(torch.device("cuda", torch.cuda.current_device()))
+    if not scatter:
+        out = torch.full((rows, n), float("nan"), device="cuda", dtype=torch.bfloat16)
+        ops.native().gemm_ragged(a, b3, out, prefix, base.contiguous(), n_i, max_tiles, [], None, err)
+        got = out.float()
+    else:
+        dests = [torch.full((rows, n), float("nan"), device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+        g = torch.Generator(device="cuda").manual_seed(3)
+        owner = torch.randint(0, 3, (rows,), device="cuda", generator=g)
+        slot = torch.randperm(rows, device="cuda", generator=g)
+        meta = torch.stack([owner, slot], 1).int().contiguous()
+        ops.native().gemm_ragged(a, b3, None, prefix, base.contiguous(), n_i, max_tiles, dests, meta, err)
+        got = torch.stack([dests[int(o)][int(s)] for o, s in meta.tolist()]).float()
+    torch.testing.assert_close(got, want, rtol=2e-2, atol=2e-1)
+    ops.check_device_errors()
