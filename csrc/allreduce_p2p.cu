@@ -45,6 +45,24 @@ __global__ void gather_slices_kernel(PeerPtrs src, int world, float4* out, long 
   }
 }
 
+// out[i] (+)= sum over s of slots[s * slot4 + i]: the owner's half of a reduce-scatter whose
+// sources stored their partials into this rank's slots (local memory only).
+__global__ void slot_reduce_kernel(const float4* __restrict__ slots, int world, long long slot4, float4* out,
+                                   long long n4, int accumulate) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = accumulate ? out[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      const float4 v = slots[r * slot4 + i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    out[i] = acc;
+  }
+}
+
 int grid_for(long long n4) {
   const long long b = (n4 + 255) / 256;
   return (int)(b < 1 ? 1 : (b < 148 * 8 ? b : 148 * 8));
@@ -79,6 +97,14 @@ void allreduce_all_gather(const float* const* peers, int world, float* out, long
   const long long n4 = n / 4;
   if (n4 <= 0) return;
   gather_slices_kernel<<<grid_for(n4), 256, 0, s>>>(pack(peers, world), world, reinterpret_cast<float4*>(out), n4);
+}
+
+void slot_reduce(const float* slots, int world, long long slot, float* out, long long n, bool accumulate,
+                 cudaStream_t s) {
+  const long long n4 = n / 4;
+  if (n4 <= 0) return;
+  slot_reduce_kernel<<<grid_for(n4), 256, 0, s>>>(reinterpret_cast<const float4*>(slots), world, slot / 4,
+                                                  reinterpret_cast<float4*>(out), n4, accumulate ? 1 : 0);
 }
 
 }  // namespace bw

@@ -394,6 +394,55 @@ void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t p
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
+// GEMM -> reduce-scatter in one launch: every element of alpha * A @ B^T is stored (16-byte
+// peer stores) into its owner rank's slot for this rank; owner = float4 index / per4.
+// slot_ptrs[r] is rank r's slot buffer (world * 4 * per4 fp32) as mapped here.  The owners
+// sum their slots with `slot_reduce` after a cross-GPU barrier.
+void gemm_tn_rs(Tensor A, Tensor B, Tensor slot_ptrs, int64_t world, int64_t per4, int64_t M, int64_t N,
+                int64_t ldc, double alpha, Tensor err, int64_t self_rank) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  TORCH_CHECK(a.batch == 1 && b.batch == 1 && a.cols == b.cols, "2-D operands with one K");
+  TORCH_CHECK(a.rows == M && b.rows == N, "M / N disagree with the operands");
+  TORCH_CHECK(slot_ptrs.is_cuda() && slot_ptrs.scalar_type() == torch::kInt64 && slot_ptrs.numel() == world,
+              "slot_ptrs: one device address per rank");
+  TORCH_CHECK(per4 > 0 && world >= 1 && self_rank >= 0 && self_rank < world, "bad partition");
+  TORCH_CHECK((M - 1) * ldc + N <= 4 * per4 * world, "the partition does not cover C");
+  bw::GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)a.cols;
+  p.batch = 1;
+  p.splits = 1;  // one writer per element and rank: plain stores, no atomics
+  p.b_shared = 1;
+  p.c_mode = bw::kPeerSlotF32;
+  p.alpha = (float)alpha;
+  p.ldc = ldc;
+  p.peers = reinterpret_cast<float* const*>(slot_ptrs.data_ptr<int64_t>());
+  p.world = (int)world;
+  p.per4 = per4;
+  p.self_rank = (int)self_rank;
+  p.err = err.data_ptr<int>();
+  if (M == 0 || N == 0) return;
+  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
+}
+
+// out[0, n) (+)= sum over the world slots of this rank's slot buffer.
+void slot_reduce(Tensor slots, int64_t world, int64_t slot, Tensor out, int64_t n, bool accumulate) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == torch::kFloat32 && slots.is_contiguous() &&
+                  slots.numel() >= world * slot, "slots: contiguous fp32 (world * slot)");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() >= n,
+              "out: contiguous fp32");
+  TORCH_CHECK(slot % 4 == 0 && n % 4 == 0 && n <= slot, "slot and n: multiples of 4 floats, n <= slot");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(slots.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "16-byte aligned buffers");
+  bw::slot_reduce(slots.data_ptr<float>(), (int)world, slot, out.data_ptr<float>(), n, accumulate,
+                  at::cuda::getCurrentCUDAStream());
+}
+
 // C (op)= alpha * A @ B^T where B lives sharded on the peers (read over NVLink inside the
 // GEMM).  mode 0: peers[r] is (shard, K), B = [peers[0]; peers[1]; ...] by rows;
 // mode 1: peers[r] is (N, shard), B = [peers[0] | peers[1] | ...] along K.
@@ -967,6 +1016,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
   m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
+  m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");
+  m.def("slot_reduce", &slot_reduce, "owner-side sum of reduce-scatter slots");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

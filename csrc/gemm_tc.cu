@@ -218,6 +218,34 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
       for (int j = 0; j < 32; ++j)
         if (j < BN - c0) r[j] = __float_as_uint(__uint_as_float(r[j]) + red[(c0 + j) * BM + red_row]);
     }
+    if (p.c_mode == kPeerSlotF32 && ok && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 3) == 0 &&
+        (((long long)zc * p.batch_stride_c) & 3) == 0) {
+      // Reduce-scatter chunk through a warp-private transpose in the (now idle) stage memory:
+      // each store instruction then writes four whole 128-byte row segments instead of 32
+      // scattered 16-byte pieces -- full lines on NVLink.
+      float* tw = reinterpret_cast<float*>(smem) + warp * (32 * 33);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
+      __syncwarp();
+      const long long slot = 4 * p.per4;
+      const int limit = row_limit >= 0 ? row_limit : p.M;
+      const int cc = (lane & 7) * 4;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int rr = q * 4 + (lane >> 3);
+        const int grow = m0 + warp * 32 + rr;
+        if (grow < limit) {
+          const long long i = (long long)zc * p.batch_stride_c + (long long)grow * p.ldc + n0 + c0 + cc;
+          int owner = (int)((i >> 2) / p.per4);
+          owner = owner < p.world ? owner : p.world - 1;
+          const float* t = tw + rr * 33 + cc;
+          *reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot)) =
+              make_float4(t[0], t[1], t[2], t[3]);
+        }
+      }
+      __syncwarp();
+      continue;
+    }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
     if (p.c_mode == kStoreBF16Scatter) {
@@ -242,6 +270,33 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
         for (int j = 0; j < 32; ++j) {
           const int n = nbase + j;
           if (j < BN - c0 && n < p.N) Cr[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+        }
+      }
+    } else if (p.c_mode == kPeerSlotF32) {
+      // Reduce-scatter: element i is stored (plain 16-byte peer stores, no atomics) into its
+      // owner's slot for THIS rank; the owner sums its `world` slots after a barrier.
+      const long long slot = 4 * p.per4;
+      const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
+      if (c0 + 32 <= BN && nbase + 32 <= p.N && ((rowoff + nbase) & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const long long i = rowoff + nbase + 4 * q;
+          int owner = (int)((i >> 2) / p.per4);
+          owner = owner < p.world ? owner : p.world - 1;
+          float4* dst = reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot));
+          *dst = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
+                             alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = nbase + j;
+          if (j < BN - c0 && n < p.N) {
+            const long long i = rowoff + n;
+            int owner = (int)((i >> 2) / p.per4);
+            owner = owner < p.world ? owner : p.world - 1;
+            p.peers[owner][p.self_rank * slot + (i - owner * slot)] = alpha * __uint_as_float(r[j]);
+          }
         }
       }
     } else if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&

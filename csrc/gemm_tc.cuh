@@ -18,6 +18,9 @@ enum GemmStore : int {
                        // i = m * ldc + n goes to peers[(i / 4) / per4][i] (cross-rank reduce)
   kStoreBF16Scatter = 6,  // bf16 row m stored into rank scatter[m].x's C at row scatter[m].y
                           // (peer pointers; expert outputs returned to their source ranks)
+  kPeerSlotF32 = 7,  // reduce-scatter: element i (owner o = (i / 4) / per4) is STORED into
+                     // peers[o][self_rank * 4 * per4 + i - o * 4 * per4] (the owner's slot for
+                     // this rank); the owner sums its slots afterwards (splits must be 1)
 };
 
 // A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).

@@ -227,8 +227,8 @@ class LayerKroneckerAccumulator:
     _A: torch.Tensor | None = field(default=None, init=False, repr=False)
     _G: torch.Tensor | None = field(default=None, init=False, repr=False)
     _count: torch.Tensor | int = field(default=0, init=False, repr=False)
-    # Cross-rank accumulation: the Gram GEMMs add into symmetric buffers over NVLink
-    # (parallel.covariance.SymmetricGram); None when accumulating locally.
+    # Multi-GPU accumulation: the Gram GEMMs add into symmetric buffers that are reduced
+    # over NVLink without a packing copy (parallel.covariance.SymmetricGram); None otherwise.
     _symm: tuple | None = field(default=None, init=False, repr=False)
     fused_reduce: bool | None = None
 

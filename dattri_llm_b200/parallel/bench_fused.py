@@ -132,15 +132,51 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
     report("gemm_tn_staged mode 1 (all-gather -> input-gradient GEMM, one launch)", secs, 2.0 * m * n * kk,
            (world - 1) / world * n * kk * 2, (m * n + m * kk + n * kk) * 2)
 
-    # 4) Gram / weight-gradient GEMM reduced across ranks by epilogue peer atomics
+    # 4) weight-gradient GEMM reduce-scattered in its epilogue (FSDP wgrad, Llama-1B q/o shape):
+    #    16-byte peer stores into the owners' slots, a bounded barrier, the owner's slot sum
     w = 2048
+    dyt = torch.randn(w, m, device=dev, generator=gen).bfloat16()
     xt = torch.randn(w, m, device=dev, generator=gen).bfloat16()
-    _, accs = _peers((w * w,), torch.float32, world, emulate, gen, dev)
-    ptrs = torch.tensor([int(p.data_ptr()) for p in accs], dtype=torch.int64, device=dev)
-    per4 = (w * w // 4 + world - 1) // world
-    secs = _time(lambda: nat.gemm_tn_peer(xt, xt, ptrs, world, per4, w, w, w, 1.0, 4, err, rank))
-    report("gemm_tn_peer (Gram / wgrad GEMM + cross-rank reduce in the epilogue)", secs, 2.0 * w * w * m,
-           (world - 1) / world * w * w * 4 * 4, 2 * w * m * 2 + w * w * 4 * 4)
+    shard = w * w // world
+    _, slots = _peers((world * shard,), torch.float32, world, emulate, gen, dev)
+    ptrs = torch.tensor([int(p.data_ptr()) for p in slots], dtype=torch.int64, device=dev)
+    gshard = torch.zeros(shard, device=dev)
+    barrier = None
+    if not emulate:
+        from dattri_llm_b200.parallel.symm import PeerBarrier
+
+        barrier = PeerBarrier(dev)
+
+    def wgrad_rs():
+        nat.gemm_tn_rs(dyt, xt, ptrs, world, shard // 4, w, w, w, 1.0, err, rank)
+        if barrier is not None:
+            barrier.wait()
+        nat.slot_reduce(slots[rank], world, shard, gshard, shard, True)
+
+    secs = _time(wgrad_rs)
+    report("gemm_tn_rs (wgrad GEMM -> reduce-scatter in the epilogue + owner slot sum)", secs, 2.0 * w * w * m,
+           (world - 1) / world * w * w * 4, 2 * w * m * 2 + 2 * w * w * 4 + shard * 4)
+    secs_local = _time(lambda: nat.gemm_tn(dyt, xt, torch.empty(w, w, device=dev), 1.0, ops.STORE_F32, 1, False, err))
+    rows[-1]["local_gemm_only_us"] = secs_local * 1e6
+
+    # 4b) Kronecker covariance: the local Gram partial (2048^2 fp32, symmetric memory)
+    #     all-reduced by the two-shot NVLink peer kernel (real ranks only)
+    if not emulate:
+        from dattri_llm_b200.parallel.symm import SymmetricBuffer
+
+        cov = SymmetricBuffer((w * w,), torch.float32, dev)
+        cov.local.normal_(generator=gen)
+        out_cov = torch.empty(w * w, device=dev)
+
+        def cov_allreduce():
+            barrier.wait()
+            nat.allreduce_phase(cov.peers, cov.local, w * w, 1, rank)
+            barrier.wait()
+            nat.allreduce_phase(cov.peers, out_cov, w * w, 2, rank)
+
+        secs = _time(cov_allreduce)
+        report("covariance all-reduce (two-shot NVLink peer kernel, 2048^2 fp32)", secs, 0.0,
+               2 * (world - 1) / world * w * w * 4, (world + 2) * w * w * 4 / world)
     # 5) expert-parallel MoE (real ranks only): dispatch + experts + combine-in-epilogue
     if not emulate:
         from dattri_llm_b200.parallel.moe import ExpertParallelMoE

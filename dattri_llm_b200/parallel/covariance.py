@@ -25,7 +25,7 @@ def all_reduce_accumulators(accs: list) -> None:
     """
     fused = [a for a in accs if getattr(a, "_symm", None) is not None]
     if fused:
-        for a in fused:  # reduced inside their accumulation GEMMs; gather the owners' slices
+        for a in fused:  # accumulated in symmetric memory: reduced straight out of it
             a.all_reduce()
         accs = [a for a in accs if getattr(a, "_symm", None) is None]
         if not accs:
@@ -60,11 +60,14 @@ def all_reduce_accumulators(accs: list) -> None:
 
 
 class SymmetricGram:
-    """A ``(w, w)`` fp32 Gram sum ``sum x^T x`` reduced ACROSS RANKS inside the accumulation
-    GEMM: the tcgen05 GEMM's epilogue adds every element with fp32 atomics into its owner
-    rank's symmetric buffer over NVLink (``kPeerAtomicF32``), so no separate all-reduce
-    follows the fit; :meth:`reduced` only gathers the owners' slices.  Create collectively
-    (same ``w``, same order on every rank)."""
+    """A ``(w, w)`` fp32 Gram sum ``sum x^T x`` kept in symmetric memory and reduced across
+    ranks over NVLink.  Every :meth:`add` is a local tcgen05 GEMM accumulating in its
+    epilogue (nothing crosses NVLink per batch: the covariance is needed only once, at the
+    end); :meth:`reduced` is a two-shot peer all-reduce straight out of the symmetric
+    buffers (reduce-scatter in place, then every rank gathers the owners' slices), with no
+    packing copy.  The reference all-reduces each factor with NCCL after the fit
+    (``dattri_llm/gradient/ops/kronecker.py:516-527``).  Create collectively (same ``w``,
+    same order on every rank)."""
 
     _barriers: dict = {}
 
@@ -76,33 +79,27 @@ class SymmetricGram:
         self.buf = SymmetricBuffer((self.n4 * 4,), torch.float32, device)
         self.buf.local.zero_()
         self.world, self.rank = self.buf.world, self.buf.rank
-        self.per4 = (self.n4 + self.world - 1) // self.world
-        self.ptrs = torch.tensor([int(p.data_ptr()) for p in self.buf.peers], dtype=torch.int64, device=device)
         if device not in SymmetricGram._barriers:
             SymmetricGram._barriers[device] = PeerBarrier(device)
-        else:  # the zeroed buffers must be in place on every rank before any rank adds
-            torch.cuda.synchronize(device)
-            dist.barrier()
         self.barrier = SymmetricGram._barriers[device]
 
     def add(self, x: torch.Tensor) -> None:
-        """Add ``x^T x`` of ``x (N, w)`` (bf16, CUDA) into the cross-rank sum."""
-        from dattri_llm_b200 import ops as native_ops
+        """Add ``x^T x`` of ``x (N, w)`` (bf16, CUDA) into this rank's partial sum."""
+        from dattri_llm_b200.gradient.ops.kronecker import gram_accumulate
 
-        xt = x.t().contiguous()
-        w, n = xt.shape
-        splits = native_ops.gemm.auto_splits(w, w, n, 1, 128 if w > 64 else 64)
-        native_ops.count_launch()
-        native_ops.native().gemm_tn_peer(xt, xt, self.ptrs, self.world, self.per4, w, w, w, 1.0, splits,
-                                         native_ops.error_word(x.device), self.rank)
+        gram_accumulate(x, self.buf.local[: self.w * self.w].view(self.w, self.w))
 
     def reduced(self) -> torch.Tensor:
         """The summed ``(w, w)`` matrix on this rank (collective: every rank calls it)."""
         from dattri_llm_b200.ops import count_launch, native
 
-        self.barrier.wait()  # every rank's atomics have landed
-        out = torch.empty(self.n4 * 4, dtype=torch.float32, device=self.buf.local.device)
+        n = self.n4 * 4
+        self.barrier.wait()  # every rank's partial sum is complete
         count_launch()
-        native().allreduce_phase(self.buf.peers, out, self.n4 * 4, 2, self.rank)
+        native().allreduce_phase(self.buf.peers, self.buf.local, n, 1, self.rank)  # own slice, in place
         self.barrier.wait()
+        out = torch.empty(n, dtype=torch.float32, device=self.buf.local.device)
+        count_launch()
+        native().allreduce_phase(self.buf.peers, out, n, 2, self.rank)
+        self.barrier.wait()  # nobody reads this buffer any more
         return out[: self.w * self.w].view(self.w, self.w)

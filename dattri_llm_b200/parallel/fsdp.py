@@ -9,10 +9,10 @@ memory, plus the transposed shard.  Nothing is all-gathered into HBM:
   flag of the owner whose rows it needs;
 * backward  ``dx = dy W``: the same over the peers' transposed shards, gated per K range
   (mode 1);
-* weight gradient (when the weight trains): ``dW = dy^T x`` computed locally and
-  reduce-scattered INSIDE its epilogue -- fp32 atomics into the owner rank's gradient
-  shard over NVLink (``kPeerAtomicF32``); :func:`sync_sharded_grads` is the barrier after
-  which every rank's shard holds the sum over ranks.
+* weight gradient (when the weight trains): ``dW = dy^T x`` reduce-scattered INSIDE its
+  GEMM -- the epilogue stores every fp32 element with 16-byte NVLink stores into its
+  owner rank's slot for this rank (``gemm_tn_rs``); after a bounded cross-GPU barrier each
+  owner adds its ``world`` slots into its gradient shard (``slot_reduce``, local memory).
 
 The capture hooks see an ``nn.Linear`` (same module boundary, full-width input and
 output), so per-sample capture is unchanged.  The reference reaches the same math through
@@ -56,6 +56,35 @@ class _Staging:
         ops.count_launch()
         ops.native().gemm_tn_staged(a, peers, self.buf, out, self.flags, self.epoch, mode, self_rank,
                                     ops.STORE_BF16, 1.0, ops.error_word(a.device))
+
+
+class _SlotRing:
+    """Two symmetric slot buffers (``world`` fp32 slots of one weight shard each) shared by
+    every sharded layer of one shape.  Consecutive weight-gradient reductions alternate
+    between them: a source writes buffer ``i`` again only after the barrier that follows
+    the next reduction, which every owner reaches after summing buffer ``i``."""
+
+    _pool: dict = {}
+
+    def __init__(self, shard_elems: int, device: torch.device, group) -> None:
+        world = dist.get_world_size(group)
+        self.bufs = [SymmetricBuffer((world * shard_elems,), torch.float32, device, group) for _ in range(2)]
+        self.ptrs = [torch.tensor([int(p.data_ptr()) for p in b.peers], dtype=torch.int64, device=device)
+                     for b in self.bufs]
+        self.turn = 0
+
+    @classmethod
+    def get(cls, shard_elems: int, device: torch.device, group) -> _SlotRing:
+        key = (shard_elems, device, id(group))
+        ring = cls._pool.get(key)
+        if ring is None:
+            ring = cls._pool[key] = cls(shard_elems, device, group)
+        return ring
+
+    def next(self) -> tuple[SymmetricBuffer, torch.Tensor]:
+        i = self.turn
+        self.turn ^= 1
+        return self.bufs[i], self.ptrs[i]
 
 
 class _AGLinear(torch.autograd.Function):
@@ -124,14 +153,9 @@ class ShardedLinear(nn.Linear):
         if self.weight.requires_grad:
             # Created here, collectively, not lazily in the backward (autograd's thread).
             shard_elems = rows * self.in_features
-            self._grad = SymmetricBuffer((shard_elems,), torch.float32, dev, group)
-            self._grad.local.zero_()
+            self._grad = torch.zeros(shard_elems, dtype=torch.float32, device=dev)
+            self._slots = _SlotRing.get(shard_elems, dev, group)
             self._barrier = PeerBarrier(dev, group)
-            # Owner r's entries are addressed by the FULL weight's linear index; its pointer
-            # is shifted back by r's first index so index i lands at i - r * shard_elems.
-            self._grad_ptrs = torch.tensor([int(p.data_ptr()) - 4 * r * shard_elems
-                                            for r, p in enumerate(self._grad.peers)],
-                                           dtype=torch.int64, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
@@ -148,26 +172,29 @@ class ShardedLinear(nn.Linear):
             raise RuntimeError("this ShardedLinear was built with a frozen weight; it keeps no gradient")
         dyt = dy2.t().contiguous()  # (N, M): tokens contiguous
         xt = x2.t().contiguous()    # (K, M)
-        ops.count_launch()
-        ops.native().gemm_tn_peer(dyt, xt, self._grad_ptrs, self.world, self.rows * self.in_features // 4,
-                                  self.out_features, self.in_features, self.in_features, 1.0, 1,
-                                  ops.error_word(dy2.device), self.rank)
+        shard = self.rows * self.in_features
+        slots, ptrs = self._slots.next()
+        ops.count_launch(2)
+        ops.native().gemm_tn_rs(dyt, xt, ptrs, self.world, shard // 4, self.out_features, self.in_features,
+                                self.in_features, 1.0, ops.error_word(dy2.device), self.rank)
+        self._barrier.wait()  # every source's slot for this rank has landed
+        ops.native().slot_reduce(slots.local, self.world, shard, self._grad, shard, True)
 
     def grad_shard(self) -> torch.Tensor | None:
         """This rank's ``(rows, in_features)`` fp32 weight-gradient shard (after
         :func:`sync_sharded_grads`)."""
-        return None if self._grad is None else self._grad.local.view(self.rows, self.in_features)
+        return None if self._grad is None else self._grad.view(self.rows, self.in_features)
 
     def zero_grad_shard(self) -> None:
         """Zero this rank's gradient shard (collectively, before the next backward)."""
         if self._grad is not None:
-            self._grad.local.zero_()
-            self._barrier.wait()
+            self._grad.zero_()
 
 
 def sync_sharded_grads(model: nn.Module) -> None:
-    """Barrier after which every :class:`ShardedLinear` gradient shard holds its sum over
-    ranks (the atomics of every rank's weight-gradient GEMM have landed)."""
+    """Barrier across the ranks of the sharded layers.  Every :class:`ShardedLinear`
+    gradient shard already holds its sum over ranks in stream order once the backward has
+    run (each reduction ends in the owner's slot sum); this only lines the ranks up."""
     for m in model.modules():
         if isinstance(m, ShardedLinear) and m._barrier is not None:
             m._barrier.wait()

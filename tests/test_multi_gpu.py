@@ -58,6 +58,14 @@ def _fsdp_worker(rank: int, world: int, port: int, results) -> None:
         dist.all_reduce(dw)
         mine = dw[rank * layer.rows:(rank + 1) * layer.rows]
         worst = max(worst, float((layer.grad_shard() - mine).abs().max() / mine.abs().max()))
+        # a second backward accumulates (and takes the other buffer of the slot ring)
+        dy2 = torch.randn_like(y)
+        layer(x).backward(dy2)
+        sync_sharded_grads(torch.nn.ModuleList([layer]))
+        dw2 = dy2.float().reshape(-1, 256).T @ x.detach().float().reshape(-1, 320)
+        dist.all_reduce(dw2)
+        mine = mine + dw2[rank * layer.rows:(rank + 1) * layer.rows]
+        worst = max(worst, float((layer.grad_shard() - mine).abs().max() / mine.abs().max()))
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         results[rank] = worst
@@ -102,7 +110,7 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             dist.all_reduce(want)
             assert symm.all_reduce_sum_(x)
             worst = max(worst, float((x - want).abs().max() / want.abs().max()))
-        # K-FAC covariances reduced across ranks inside the Gram GEMM epilogue.
+        # K-FAC covariances accumulated in symmetric memory, reduced by the peer all-reduce.
         from dattri_llm_b200.gradient.ops.kronecker import LayerKroneckerAccumulator
 
         acc = LayerKroneckerAccumulator()

@@ -175,3 +175,26 @@ def test_gemm_ragged_expert_segments(scatter):
         got = torch.stack([dests[int(o)][int(s)] for o, s in meta.tolist()]).float()
     torch.testing.assert_close(got, want, rtol=2e-2, atol=2e-1)
     ops.check_device_errors()
+
+
+def test_gemm_reduce_scatter_slots_emulated():
+    """GEMM -> reduce-scatter with three ranks emulated on one GPU: every "rank" stores its
+    product into the owners' slots, then every owner sums its slots into its shard."""
+    world, m, n, k = 3, 200, 136, 384
+    elems = m * n
+    per4 = -(-elems // 4 // world)
+    slot = 4 * per4
+    bufs = [torch.full((world * slot,), float("nan"), device="cuda") for _ in range(world)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    a = [torch.randn(m, k, device="cuda").bfloat16() for _ in range(world)]
+    b = [torch.randn(n, k, device="cuda").bfloat16() for _ in range(world)]
+    err = ops.error_word(torch.device("cuda", torch.cuda.current_device()))
+    for s in range(world):
+        ops.native().gemm_tn_rs(a[s], b[s], ptrs, world, per4, m, n, n, 0.5, err, s)
+    want = sum(a[s].float() @ b[s].float().T for s in range(world)).reshape(-1) * 0.5
+    got = torch.empty(world * slot, device="cuda")
+    for r in range(world):
+        got[r * slot:(r + 1) * slot] = 1.0
+        ops.native().slot_reduce(bufs[r], world, slot, got[r * slot:], min(slot, elems - r * slot) // 4 * 4, True)
+    torch.testing.assert_close(got[:elems] - 1.0, want, rtol=1e-3, atol=1e-2)
+    ops.check_device_errors()
