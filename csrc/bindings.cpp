@@ -637,6 +637,49 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
                    at::cuda::getCurrentCUDAStream());
 }
 
+// MoE combine: y (T, H) = sum over the k slots of w (T, k) fp32 * slots (T * k, H) bf16.
+void moe_combine(Tensor slots, Tensor w, Tensor y) {
+  const c10::cuda::CUDAGuard guard(slots.device());
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.dim() == 2, "w: (T, k) fp32");
+  const long long T = w.size(0), k = w.size(1);
+  TORCH_CHECK(slots.scalar_type() == torch::kBFloat16 && slots.is_contiguous() && slots.dim() == 2 &&
+                  slots.size(0) >= T * k && slots.size(1) % 8 == 0, "slots: contiguous (>= T * k, H) bf16");
+  TORCH_CHECK(y.scalar_type() == torch::kBFloat16 && y.is_contiguous() && y.size(0) == T &&
+                  y.size(1) == slots.size(1), "y: contiguous (T, H) bf16");
+  bw::moe_combine(slots.data_ptr(), w.data_ptr<float>(), y.data_ptr(), (int)T, (int)k, (int)slots.size(1),
+                  at::cuda::getCurrentCUDAStream());
+}
+
+// Backward of moe_combine fused with the dispatch of the slot gradients to the owners.
+void moe_combine_bwd_dispatch(Tensor dy, Tensor slots, Tensor w, Tensor dw, Tensor dst_rank, Tensor dst_row,
+                              std::vector<Tensor> peer_rows, std::vector<Tensor> peer_meta, int64_t self) {
+  const c10::cuda::CUDAGuard guard(dy.device());
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.dim() == 2, "w: (T, k) fp32");
+  const long long T = w.size(0), k = w.size(1), rows = T * k;
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous() && dw.numel() == rows, "dw: (T, k) fp32");
+  TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.is_contiguous() && dy.size(0) == T && dy.size(1) % 8 == 0,
+              "dy: contiguous (T, H) bf16");
+  TORCH_CHECK(slots.scalar_type() == torch::kBFloat16 && slots.is_contiguous() && slots.size(0) >= rows &&
+                  slots.size(1) == dy.size(1), "slots: contiguous (T * k, H) bf16");
+  TORCH_CHECK(dst_rank.scalar_type() == torch::kInt32 && dst_row.scalar_type() == torch::kInt32 &&
+                  dst_rank.numel() == rows && dst_row.numel() == rows && dst_rank.is_contiguous() &&
+                  dst_row.is_contiguous(), "dst_rank / dst_row: int32 per (token, slot)");
+  const int world = (int)peer_rows.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && (int)peer_meta.size() == world, "1..8 ranks");
+  std::vector<void*> pr;
+  std::vector<int2*> pm;
+  for (int r = 0; r < world; ++r) {
+    TORCH_CHECK(peer_rows[r].scalar_type() == torch::kBFloat16 && peer_rows[r].is_contiguous() &&
+                    peer_rows[r].size(-1) == dy.size(1), "receive buffers must be (R, H) bf16");
+    TORCH_CHECK(peer_meta[r].scalar_type() == torch::kInt32 && peer_meta[r].is_contiguous(), "origin tables: int32");
+    pr.push_back(peer_rows[r].data_ptr());
+    pm.push_back(reinterpret_cast<int2*>(peer_meta[r].data_ptr<int>()));
+  }
+  bw::moe_combine_bwd_dispatch(dy.data_ptr(), slots.data_ptr(), w.data_ptr<float>(), dw.data_ptr<float>(),
+                               dst_rank.data_ptr<int>(), dst_row.data_ptr<int>(), pr.data(), pm.data(), world, (int)rows,
+                               (int)k, (int)dy.size(1), (int)self, at::cuda::getCurrentCUDAStream());
+}
+
 // C rows returned to their sources: out row m = alpha * (A @ B^T)[m] is stored into rank
 // scatter[m][0]'s buffer peer_C[...] at row scatter[m][1] (bf16, row length N).
 void gemm_tn_scatter(Tensor A, Tensor B, std::vector<Tensor> peer_C, Tensor scatter, double alpha, Tensor err) {
@@ -648,7 +691,8 @@ void gemm_tn_scatter(Tensor A, Tensor B, std::vector<Tensor> peer_C, Tensor scat
   TORCH_CHECK(scatter.is_cuda() && scatter.scalar_type() == torch::kInt32 && scatter.is_contiguous() &&
                   scatter.numel() >= 2 * a.rows, "scatter: int32 (M, 2)");
   for (auto& c : peer_C)
-    TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows,
+    TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows &&
+                    reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
                 "peer outputs must be contiguous (R, N) bf16");
   Tensor ptrs = device_ptr_table(peer_C, A.device());
   bw::GemmParams p{};
@@ -701,7 +745,8 @@ Tensor norm_per_sample_grad(Tensor x, Tensor g, double eps, bool layer_norm, boo
 // ranks' buffers peer_C.  tile_prefix / base / len are device int32 arrays; max_tiles bounds
 // the number of 128-row tiles (CTAs past the real count return at once).
 void gemm_ragged(Tensor A, Tensor B3, c10::optional<Tensor> C, Tensor tile_prefix, Tensor base, Tensor len,
-                 int64_t max_tiles, std::vector<Tensor> peer_C, c10::optional<Tensor> scatter, Tensor err) {
+                 int64_t max_tiles, std::vector<Tensor> peer_C, c10::optional<Tensor> scatter, Tensor err,
+                 int64_t bn) {
   const c10::cuda::CUDAGuard guard(A.device());
   check_err(err);
   auto a = operand(A, "A");
@@ -722,8 +767,9 @@ void gemm_ragged(Tensor A, Tensor B3, c10::optional<Tensor> C, Tensor tile_prefi
     TORCH_CHECK(scatter->scalar_type() == torch::kInt32 && scatter->is_contiguous() && scatter->numel() >= 2 * a.rows,
                 "scatter: int32 (R, 2)");
     for (auto& c : peer_C)
-      TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows,
-                  "peer outputs must be contiguous (R, N) bf16");
+      TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows &&
+                      reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
+                  "peer outputs must be contiguous 16-byte aligned (R, N) bf16");
     ptrs = device_ptr_table(peer_C, A.device());
     p.c_mode = bw::kStoreBF16Scatter;
     p.peers = reinterpret_cast<float* const*>(ptrs.data_ptr<int64_t>());
@@ -739,7 +785,8 @@ void gemm_ragged(Tensor A, Tensor B3, c10::optional<Tensor> C, Tensor tile_prefi
   }
   if (max_tiles <= 0 || p.N == 0) return;
   bw::gemm_ragged_launch(a, b, p, tile_prefix.data_ptr<int>(), base.data_ptr<int>(), len.data_ptr<int>(), jobs,
-                         (int)max_tiles, std::max(64, bw::pick_bn(p.N)), at::cuda::getCurrentCUDAStream());
+                         (int)max_tiles, bn > 0 ? (int)bn : std::max(64, bw::pick_bn(p.N)),
+                         at::cuda::getCurrentCUDAStream());
 }
 
 void swiglu_split(Tensor h, Tensor out, Tensor rows) {
@@ -1010,12 +1057,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
-  m.def("gemm_ragged", &gemm_ragged, "ragged grouped GEMM over expert row segments (optionally scattered home)");
+  m.def("gemm_ragged", &gemm_ragged, "ragged grouped GEMM over expert row segments (optionally scattered home)",
+        py::arg("A"), py::arg("B3"), py::arg("C"), py::arg("tile_prefix"), py::arg("base"), py::arg("len"),
+        py::arg("max_tiles"), py::arg("peer_C"), py::arg("scatter"), py::arg("err"), py::arg("bn") = 0);
   m.def("swiglu_split", &swiglu_split);
   m.def("swiglu_split_bwd", &swiglu_split_bwd);
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
   m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
+  m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
+  m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");
   m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");
   m.def("slot_reduce", &slot_reduce, "owner-side sum of reduce-scatter slots");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");

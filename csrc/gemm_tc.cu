@@ -246,6 +246,35 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
       __syncwarp();
       continue;
     }
+    if (p.c_mode == kStoreBF16Scatter && ok && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 7) == 0) {
+      // Rows sent home through a warp-private transpose: each store instruction writes eight
+      // whole 64-byte row segments instead of 32 scattered 16-byte pieces.
+      float* tw = reinterpret_cast<float*>(smem) + warp * (32 * 33);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
+      __syncwarp();
+      const int limit = row_limit >= 0 ? row_limit : p.M;
+      const int cc = (lane & 3) * 8;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int rr = q * 8 + (lane >> 2);
+        const int grow = m0 + warp * 32 + rr;
+        if (grow < limit) {
+          const int2 dstm = p.scatter[grow];
+          __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
+          const float* t = tw + rr * 33 + cc;
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * e], t[2 * e + 1]);
+            w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(Cr + n0 + c0 + cc) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      __syncwarp();
+      continue;
+    }
     if (!ok || !row_ok) continue;
     const int nbase = n0 + c0;
     if (p.c_mode == kStoreBF16Scatter) {

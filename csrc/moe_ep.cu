@@ -34,7 +34,104 @@ __global__ void dispatch_kernel(const uint4* __restrict__ src, const int* __rest
   }
 }
 
+__device__ __forceinline__ void unpack_bf8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p = __bfloat1622float2(h[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf8(const float (&f)[8]) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+// Combine: y[t] = sum_j w[t, j] * slots[t * k + j] (bf16 rows, fp32 weights and sums).
+__global__ void combine_kernel(const uint4* __restrict__ slots, const float* __restrict__ w, uint4* __restrict__ y,
+                               int tokens, int k, int vec_per_row) {
+  for (int t = blockIdx.x; t < tokens; t += gridDim.x) {
+    for (int v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < k; ++j) {
+        const float wj = w[t * k + j];
+        float x[8];
+        unpack_bf8(slots[(long long)(t * k + j) * vec_per_row + v], x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(wj, x[e], acc[e]);
+      }
+      y[(long long)t * vec_per_row + v] = pack_bf8(acc);
+    }
+  }
+}
+
+// Backward of the combine, fused with the dispatch of the slot gradients: for row
+// r = t * k + j, dw[r] = <slots[r], dy[t]> and bf16(w[r] * dy[t]) is stored straight into
+// owner dst_rank[r]'s receive buffer at row dst_row[r] (16-byte peer stores), with the row's
+// origin (the receive tables are shared by every layer of one shape, so the origin table is
+// rewritten for this layer's backward).
+__global__ void combine_bwd_dispatch_kernel(const uint4* __restrict__ dy, const uint4* __restrict__ slots,
+                                            const float* __restrict__ w, float* __restrict__ dw,
+                                            const int* __restrict__ dst_rank, const int* __restrict__ dst_row,
+                                            PeerRows peers, int rows, int k, int vec_per_row, int self) {
+  __shared__ float part[32];
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int t = r / k;
+    const float wr = w[r];
+    uint4* d = peers.rows[dst_rank[r]] + (long long)dst_row[r] * vec_per_row;
+    if (threadIdx.x == 0) peers.meta[dst_rank[r]][dst_row[r]] = make_int2(self, r);
+    float dot = 0.f;
+    for (int v = threadIdx.x; v < vec_per_row; v += blockDim.x) {
+      float g[8], x[8], o[8];
+      unpack_bf8(dy[(long long)t * vec_per_row + v], g);
+      unpack_bf8(slots[(long long)r * vec_per_row + v], x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        dot = fmaf(g[e], x[e], dot);
+        o[e] = wr * g[e];
+      }
+      d[v] = pack_bf8(o);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += part[i];
+      dw[r] = s;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
+
+void moe_combine(const void* slots, const float* w, void* y, int tokens, int k, int cols, cudaStream_t s) {
+  if (tokens <= 0) return;
+  const int grid = tokens < 148 * 8 ? tokens : 148 * 8;
+  combine_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(slots), w, static_cast<uint4*>(y), tokens, k,
+                                      cols / 8);
+}
+
+void moe_combine_bwd_dispatch(const void* dy, const void* slots, const float* w, float* dw, const int* dst_rank,
+                              const int* dst_row, void* const* peer_rows, int2* const* peer_meta, int world, int rows,
+                              int k, int cols, int self, cudaStream_t s) {
+  PeerRows p{};
+  for (int r = 0; r < world && r < kMaxRanks; ++r) {
+    p.rows[r] = static_cast<uint4*>(peer_rows[r]);
+    p.meta[r] = peer_meta[r];
+  }
+  if (rows <= 0) return;
+  const int grid = rows < 148 * 8 ? rows : 148 * 8;
+  combine_bwd_dispatch_kernel<<<grid, 128, 0, s>>>(static_cast<const uint4*>(dy), static_cast<const uint4*>(slots),
+                                                   w, dw, dst_rank, dst_row, p, rows, k, cols / 8, self);
+}
 
 void moe_dispatch(const void* src, long long token_stride, const int* dst_rank, const int* dst_row,
                   void* const* peer_rows, int2* const* peer_meta, int world, int rows, int cols, int self,

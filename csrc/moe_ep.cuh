@@ -12,4 +12,14 @@ void moe_dispatch(const void* src, long long token_stride, const int* dst_rank, 
                   void* const* peer_rows, int2* const* peer_meta, int world, int rows, int cols, int self,
                   int rows_per_token, cudaStream_t s);
 
+// y[t] = sum_j w[t * k + j] * slots[t * k + j] for t < tokens (bf16 rows of cols, fp32 w).
+void moe_combine(const void* slots, const float* w, void* y, int tokens, int k, int cols, cudaStream_t s);
+
+// Backward of moe_combine fused with the slot-gradient dispatch: dw[r] = <slots[r], dy[r / k]>
+// and bf16(w[r] * dy[r / k]) stored into peer dst_rank[r]'s receive buffer at row dst_row[r],
+// its origin (self, r) into that peer's origin table.
+void moe_combine_bwd_dispatch(const void* dy, const void* slots, const float* w, float* dw, const int* dst_rank,
+                              const int* dst_row, void* const* peer_rows, int2* const* peer_meta, int world, int rows,
+                              int k, int cols, int self, cudaStream_t s);
+
 }  // namespace bw

@@ -93,11 +93,16 @@ class _EPMoE(torch.autograd.Function):
             ops.native().gemm_ragged(a[:total_in], mod.down, None, prefix, base, lens, max_tiles,
                                      mod.combine.peers, mod.recv_meta.local[:total_in], err)
         mod.barrier.wait()  # every output row is home
-        slots = mod.combine.local[:t * k].view(t, k, -1).clone()
-        y = (slots.float() * topv.float()[..., None]).sum(1).to(torch.bfloat16)
+        w = topv.float().contiguous()
+        slots = mod.combine.local[:t * k]
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            slots = slots.clone()  # the combine buffer is reused by the next layer
+        y = torch.empty(t, mod.hidden, dtype=torch.bfloat16, device=dev)
+        ops.count_launch()
+        ops.native().moe_combine(slots, w, y)
         ctx.mod = mod
-        ctx.save_for_backward(topv, slots, dest32, row32, h, prefix, base, lens, rows_dev)
-        ctx.total_in, ctx.max_tiles = total_in, max_tiles
+        ctx.save_for_backward(w, slots, dest32, row32, h, prefix, base, lens, rows_dev)
+        ctx.total_in, ctx.max_tiles, ctx.topv_dtype = total_in, max_tiles, topv.dtype
         return y
 
     @staticmethod
@@ -105,15 +110,16 @@ class _EPMoE(torch.autograd.Function):
         from dattri_llm_b200 import ops
 
         mod = ctx.mod
-        topv, slots, dest32, row32, h, prefix, base, lens, rows_dev = ctx.saved_tensors
-        t, k = topv.shape
+        w, slots, dest32, row32, h, prefix, base, lens, rows_dev = ctx.saved_tensors
+        t, k = w.shape
         dev = dy.device
-        dyf = dy.float()
-        dtopv = (slots.float() * dyf[:, None, :]).sum(-1).to(topv.dtype)
-        dslot = (dyf[:, None, :] * topv.float()[..., None]).to(torch.bfloat16).reshape(t * k, -1).contiguous()
+        dy = dy.to(torch.bfloat16).contiguous()
+        dtopv = torch.empty(t, k, dtype=torch.float32, device=dev)
         mod.barrier.wait()
         ops.count_launch()
-        ops.native().moe_dispatch(dslot, 1, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, mod.rank)
+        # router-weight gradient and the slot gradients' dispatch to the owners in one kernel
+        ops.native().moe_combine_bwd_dispatch(dy, slots, w, dtopv, dest32, row32, mod.recv_x.peers,
+                                              mod.recv_meta.peers, mod.rank)
         mod.barrier.wait()
         total_in = ctx.total_in
         if total_in:
@@ -128,8 +134,10 @@ class _EPMoE(torch.autograd.Function):
             ops.native().gemm_ragged(dh, mod.gate_up_t, None, prefix, base, lens, ctx.max_tiles,
                                      mod.dx_slots.peers, mod.recv_meta.local[:total_in], err)
         mod.barrier.wait()
-        dx = mod.dx_slots.local[:t * k].view(t, k, -1).float().sum(1).to(torch.bfloat16)
-        return dx, dtopv, None, None
+        dx = torch.empty(t, mod.hidden, dtype=torch.bfloat16, device=dev)
+        ops.count_launch()
+        ops.native().moe_combine(mod.dx_slots.local[:t * k], torch.ones_like(w), dx)  # sum of the k slots
+        return dx, dtopv.to(ctx.topv_dtype), None, None
 
 
 class _Buffers:

@@ -165,22 +165,20 @@ def _moe_worker(rank: int, world: int, port: int, results) -> None:
 
         h, inter, n_exp, k = 128, 64, 8, 2
         g = torch.Generator(device=dev).manual_seed(11)  # same weights on every rank
-        gate_up = (0.1 * torch.randn(n_exp, 2 * inter, h, device=dev, generator=g)).bfloat16()
-        down = (0.1 * torch.randn(n_exp, h, inter, device=dev, generator=g)).bfloat16()
-        router = (0.1 * torch.randn(n_exp, h, device=dev, generator=g)).bfloat16()
-        moe = ExpertParallelMoE(h, inter, n_exp, k, max_tokens=256)
-        moe.load_experts(gate_up, down, router)
-        gx = torch.Generator(device=dev).manual_seed(50 + rank)
-        worst = 0.0
-        for _ in range(2):
-            x = torch.randn(3, 37, h, device=dev, generator=gx).bfloat16().requires_grad_()
-            y = moe(x)
-            dy = torch.randn_like(y)
-            y.backward(dy)
-            # replicated-expert reference in fp32 on this rank's tokens
-            xr = x.detach().float().reshape(-1, h).requires_grad_()
+        weights = []
+        layers = []
+        for _ in range(2):  # two stacked layers of one shape share the receive buffers
+            gate_up = (0.1 * torch.randn(n_exp, 2 * inter, h, device=dev, generator=g)).bfloat16()
+            down = (0.1 * torch.randn(n_exp, h, inter, device=dev, generator=g)).bfloat16()
+            router = (0.1 * torch.randn(n_exp, h, device=dev, generator=g)).bfloat16()
+            moe = ExpertParallelMoE(h, inter, n_exp, k, max_tokens=256)
+            moe.load_experts(gate_up, down, router)
+            weights.append((gate_up, down, router.float().requires_grad_()))
+            layers.append(moe)
+
+        def ref_layer(xr, gate_up, down, router):
             # the same bf16 router GEMM as the module, so near-ties pick the same experts
-            probs = torch.softmax(F.linear(xr.bfloat16(), router).float(), -1)
+            probs = torch.softmax(F.linear(xr.bfloat16(), router.bfloat16()).float(), -1)
             topv, topi = probs.topk(k, -1)
             out = torch.zeros_like(xr)
             for j in range(k):
@@ -189,8 +187,32 @@ def _moe_worker(rank: int, world: int, port: int, results) -> None:
                 gg, uu = hh.chunk(2, -1)
                 a = F.silu(gg) * uu
                 out = out + topv[:, j:j + 1] * torch.einsum("ti,thi->th", a, down.float()[e])
+            return out
+
+        gx = torch.Generator(device=dev).manual_seed(50 + rank)
+        worst = 0.0
+        for _ in range(2):
+            for m_ in layers:
+                m_.gate.weight.grad = None
+            for _, _, r_ in weights:
+                r_.grad = None
+            x = torch.randn(3, 37, h, device=dev, generator=gx).bfloat16().requires_grad_()
+            y0 = layers[0](x)
+            y = layers[1](y0)
+            dy = torch.randn_like(y)
+            y.backward(dy)
+            # replicated-expert reference in fp32 on this rank's tokens; layer 1 reads the
+            # module's own layer-0 output so both route on identical inputs
+            xr = x.detach().float().reshape(-1, h).requires_grad_()
+            mid = y0.detach().float().reshape(-1, h).requires_grad_()
+            out = ref_layer(mid, *weights[1])
             out.backward(dy.float().reshape(-1, h))
-            for got, want in ((y.float().reshape(-1, h), out.detach()), (x.grad.float().reshape(-1, h), xr.grad)):
+            mid_ref = ref_layer(xr, *weights[0])
+            mid_ref.backward(mid.grad)
+            pairs = [(y0.float().reshape(-1, h), mid_ref.detach()), (y.float().reshape(-1, h), out.detach()),
+                     (x.grad.float().reshape(-1, h), xr.grad)]
+            pairs += [(m_.gate.weight.grad.float(), w_[2].grad) for m_, w_ in zip(layers, weights)]
+            for got, want in pairs:
                 worst = max(worst, float((got - want).abs().max() / want.abs().max()))
             x.grad = None
         torch.cuda.synchronize()
