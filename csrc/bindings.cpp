@@ -637,6 +637,36 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
                    at::cuda::getCurrentCUDAStream());
 }
 
+// MoE routing histogram (int32 counts, accumulated) of int64 expert ids.
+void moe_count(Tensor topi, Tensor counts) {
+  const c10::cuda::CUDAGuard guard(topi.device());
+  TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous(), "topi: contiguous int64");
+  TORCH_CHECK(counts.scalar_type() == torch::kInt32 && counts.is_contiguous(), "counts: int32");
+  bw::moe_count(reinterpret_cast<const long long*>(topi.data_ptr<int64_t>()), (int)topi.numel(),
+                counts.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+// MoE receive layout (see moe_ep.cu): fills dest / dst_row per routed row and this rank's
+// ragged-GEMM tables (tile_prefix, base, len) and received-row total.
+void moe_place(Tensor topi, Tensor all_counts, int64_t rank, int64_t e_l, Tensor cursor, Tensor dest, Tensor dst_row,
+               Tensor tile_prefix, Tensor base, Tensor len, Tensor total) {
+  const c10::cuda::CUDAGuard guard(topi.device());
+  TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous(), "topi: contiguous int64");
+  TORCH_CHECK(all_counts.scalar_type() == torch::kInt32 && all_counts.is_contiguous() && all_counts.dim() == 2,
+              "all_counts: (world, experts) int32");
+  const int world = (int)all_counts.size(0);
+  TORCH_CHECK(all_counts.size(1) == world * e_l, "experts = world * e_l");
+  for (auto* t : {&cursor, &dest, &dst_row, &tile_prefix, &base, &len, &total})
+    TORCH_CHECK(t->scalar_type() == torch::kInt32 && t->is_contiguous() && t->is_cuda(), "int32 CUDA tables");
+  TORCH_CHECK(cursor.numel() >= world * e_l && dest.numel() == topi.numel() && dst_row.numel() == topi.numel() &&
+                  tile_prefix.numel() == e_l + 1 && base.numel() == e_l && len.numel() == e_l && total.numel() >= 1,
+              "table sizes");
+  bw::moe_place(reinterpret_cast<const long long*>(topi.data_ptr<int64_t>()), (int)topi.numel(),
+                all_counts.data_ptr<int>(), world, (int)rank, (int)e_l, cursor.data_ptr<int>(), dest.data_ptr<int>(),
+                dst_row.data_ptr<int>(), tile_prefix.data_ptr<int>(), base.data_ptr<int>(), len.data_ptr<int>(),
+                total.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
 // MoE combine: y (T, H) = sum over the k slots of w (T, k) fp32 * slots (T * k, H) bf16.
 void moe_combine(Tensor slots, Tensor w, Tensor y) {
   const c10::cuda::CUDAGuard guard(slots.device());
@@ -1065,6 +1095,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
   m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
   m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
+  m.def("moe_count", &moe_count, "MoE routing histogram");
+  m.def("moe_place", &moe_place, "MoE receive layout and owner-side ragged GEMM tables");
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");
   m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");

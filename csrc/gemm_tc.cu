@@ -64,6 +64,237 @@ struct StageCtl {
   unsigned ready;    // owners already waited for (bit mask)
 };
 
+// Store one warp's 32 rows x 32 columns (columns [c0, c0 + 32) of the tile at (m0, n0)) from
+// the accumulator registers `r`; rows at or past `limit` are dropped.  `tw` is warp-private
+// shared scratch (32 x 33 floats) for the transposed peer stores.
+template <int BN>
+__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], void* Cbase, int zc, int m0,
+                                            int n0, int c0, int warp, int lane, int limit, float* tw) {
+  const int row = m0 + warp * 32 + lane;
+  const bool row_ok = row < limit;
+  const float alpha = p.alpha;
+  if (p.c_mode == kPeerSlotF32 && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 3) == 0 &&
+      (((long long)zc * p.batch_stride_c) & 3) == 0) {
+    // Reduce-scatter chunk through a warp-private transpose in the (now idle) stage memory:
+    // each store instruction then writes four whole 128-byte row segments instead of 32
+    // scattered 16-byte pieces -- full lines on NVLink.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
+    __syncwarp();
+    const long long slot = 4 * p.per4;
+    const int cc = (lane & 7) * 4;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int rr = q * 4 + (lane >> 3);
+      const int grow = m0 + warp * 32 + rr;
+      if (grow < limit) {
+        const long long i = (long long)zc * p.batch_stride_c + (long long)grow * p.ldc + n0 + c0 + cc;
+        int owner = (int)((i >> 2) / p.per4);
+        owner = owner < p.world ? owner : p.world - 1;
+        const float* t = tw + rr * 33 + cc;
+        *reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot)) =
+            make_float4(t[0], t[1], t[2], t[3]);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  if (p.c_mode == kStoreBF16Scatter && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 7) == 0) {
+    // Rows sent home through a warp-private transpose: each store instruction writes eight
+    // whole 64-byte row segments instead of 32 scattered 16-byte pieces.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
+    __syncwarp();
+    const int cc = (lane & 3) * 8;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int rr = q * 8 + (lane >> 2);
+      const int grow = m0 + warp * 32 + rr;
+      if (grow < limit) {
+        const int2 dstm = p.scatter[grow];
+        __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
+        const float* t = tw + rr * 33 + cc;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * e], t[2 * e + 1]);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(Cr + n0 + c0 + cc) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  if (!row_ok) return;
+  const int nbase = n0 + c0;
+  if (p.c_mode == kStoreBF16Scatter) {
+    // Row m goes home: rank scatter[m].x, row scatter[m].y of that rank's C (peer memory).
+    const int2 dstm = p.scatter[row];
+    __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
+    if (c0 + 32 <= BN && nbase + 32 <= p.N && ((reinterpret_cast<uintptr_t>(Cr + nbase) & 15) == 0)) {
+      uint4* Cv = reinterpret_cast<uint4*>(Cr + nbase);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
+                                                         alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) Cr[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+      }
+    }
+  } else if (p.c_mode == kPeerSlotF32) {
+    // Reduce-scatter: element i is stored (plain 16-byte peer stores, no atomics) into its
+    // owner's slot for THIS rank; the owner sums its `world` slots after a barrier.
+    const long long slot = 4 * p.per4;
+    const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
+    if (c0 + 32 <= BN && nbase + 32 <= p.N && ((rowoff + nbase) & 3) == 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const long long i = rowoff + nbase + 4 * q;
+        int owner = (int)((i >> 2) / p.per4);
+        owner = owner < p.world ? owner : p.world - 1;
+        float4* dst = reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot));
+        *dst = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
+                           alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        if (j < BN - c0 && n < p.N) {
+          const long long i = rowoff + n;
+          int owner = (int)((i >> 2) / p.per4);
+          owner = owner < p.world ? owner : p.world - 1;
+          p.peers[owner][p.self_rank * slot + (i - owner * slot)] = alpha * __uint_as_float(r[j]);
+        }
+      }
+    }
+  } else if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+      (((long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase) & 3) == 0) {
+    // A float4 never straddles two owners (ownership is assigned in whole float4 units).
+    // 16-byte vector atomics go to this rank's own slice only; other owners get scalar
+    // fp32 atomics, the form peer (NVLink) atomics are known to support.
+    const long long i0 = (long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const long long i = i0 + 4 * q;
+      int owner = (int)((i >> 2) / p.per4);
+      owner = owner < p.world ? owner : p.world - 1;
+      float* dst = p.peers[owner] + i;
+      const float v0 = alpha * __uint_as_float(r[4 * q]), v1 = alpha * __uint_as_float(r[4 * q + 1]);
+      const float v2 = alpha * __uint_as_float(r[4 * q + 2]), v3 = alpha * __uint_as_float(r[4 * q + 3]);
+      if (owner == p.self_rank) {
+        atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v0, v1, v2, v3));
+      } else {
+        atomicAdd(dst, v0);
+        atomicAdd(dst + 1, v1);
+        atomicAdd(dst + 2, v2);
+        atomicAdd(dst + 3, v3);
+      }
+    }
+  } else if (p.c_mode == kPeerAtomicF32) {
+    const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase + j;
+      if (j < BN - c0 && n < p.N) {
+        const long long i = rowoff + n;
+        int owner = (int)((i >> 2) / p.per4);
+        owner = owner < p.world ? owner : p.world - 1;
+        atomicAdd(p.peers[owner] + i, alpha * __uint_as_float(r[j]));
+      }
+    }
+  } else if ((p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) && c0 + 32 <= BN && nbase + 32 <= p.N &&
+             ((reinterpret_cast<uintptr_t>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                           (long long)row * p.ldc + nbase) & 15) == 0)) {
+    // A whole 32-column chunk in range and 16-byte aligned: 8 vector accesses per thread
+    // instead of 32 scalar ones (the scalar form saturated the LSU pipe on large tiles).
+    float4* Cv = reinterpret_cast<float4*>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                           (long long)row * p.ldc + nbase);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 v = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
+                             alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
+      if (p.c_mode == kAtomicF32) {
+        atomicAdd(Cv + q, v);
+      } else {
+        if (p.beta_accumulate) {
+          const float4 o = Cv[q];
+          v.x += o.x;
+          v.y += o.y;
+          v.z += o.z;
+          v.w += o.w;
+        }
+        Cv[q] = v;
+      }
+    }
+  } else if (p.c_mode == kStoreBF16 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+             ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                           (long long)row * p.ldc + nbase) & 15) == 0)) {
+    uint4* Cv = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                                         (long long)row * p.ldc + nbase);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
+                                                       alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
+        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
+    float* Cz = static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
+                (long long)row * p.ldc;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase + j;
+      if (j < BN - c0 && n < p.N) {
+        const float v = alpha * __uint_as_float(r[j]);
+        if (p.c_mode == kStoreF32)
+          Cz[n] = p.beta_accumulate ? Cz[n] + v : v;
+        else
+          atomicAdd(Cz + n, v);
+      }
+    }
+  } else if (p.c_mode == kStoreBF16) {
+    __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                        (long long)row * p.ldc;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase + j;
+      if (j < BN - c0 && n < p.N) Cz[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+    }
+  } else if (p.c_mode == kStoreBF16T) {  // C^T[z][n][m]; consecutive lanes hit consecutive m
+    __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase + j;
+      if (j < BN - c0 && n < p.N)
+        Cz[(long long)n * p.ldc + row] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+    }
+  } else {  // kStoreBF16TB: rows are (segment, t); element (m, n) -> C[m / T][n][m % T], T = ldc
+    __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
+                        (long long)(row / p.ldc) * p.N * p.ldc + row % p.ldc;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase + j;
+      if (j < BN - c0 && n < p.N) Cz[(long long)n * p.ldc] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+    }
+  }
+}
+
 // One CTA's 128 x BN output tile of batch (za, zb) -> output batch zc at Cbase.  The tensor
 // maps may live in kernel parameters or in global memory (grouped launches).
 //   b_row_off: subtracted from n0 in B's TMA coordinate (B rows owned by one peer's shard)
@@ -173,9 +404,6 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
   const bool ok = nk > 0 ? mbar_wait(done, 0, p.err, kErrWaitDone) : true;
   __syncwarp();
   tc_fence_after();
-  const int row = m0 + warp * 32 + lane;
-  const bool row_ok = row < (row_limit >= 0 ? row_limit : p.M);
-  const float alpha = p.alpha;
   // Cluster split-K: the peer CTA (rank 1) writes its fp32 partial tile into rank 0's shared
   // memory (column-major, so a warp's 32 rows are 32 consecutive words), then both meet at a
   // cluster barrier and rank 0 stores the sum.
@@ -218,230 +446,9 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap* tmA, const CUtensorM
       for (int j = 0; j < 32; ++j)
         if (j < BN - c0) r[j] = __float_as_uint(__uint_as_float(r[j]) + red[(c0 + j) * BM + red_row]);
     }
-    if (p.c_mode == kPeerSlotF32 && ok && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 3) == 0 &&
-        (((long long)zc * p.batch_stride_c) & 3) == 0) {
-      // Reduce-scatter chunk through a warp-private transpose in the (now idle) stage memory:
-      // each store instruction then writes four whole 128-byte row segments instead of 32
-      // scattered 16-byte pieces -- full lines on NVLink.
-      float* tw = reinterpret_cast<float*>(smem) + warp * (32 * 33);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
-      __syncwarp();
-      const long long slot = 4 * p.per4;
-      const int limit = row_limit >= 0 ? row_limit : p.M;
-      const int cc = (lane & 7) * 4;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int rr = q * 4 + (lane >> 3);
-        const int grow = m0 + warp * 32 + rr;
-        if (grow < limit) {
-          const long long i = (long long)zc * p.batch_stride_c + (long long)grow * p.ldc + n0 + c0 + cc;
-          int owner = (int)((i >> 2) / p.per4);
-          owner = owner < p.world ? owner : p.world - 1;
-          const float* t = tw + rr * 33 + cc;
-          *reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot)) =
-              make_float4(t[0], t[1], t[2], t[3]);
-        }
-      }
-      __syncwarp();
-      continue;
-    }
-    if (p.c_mode == kStoreBF16Scatter && ok && c0 + 32 <= BN && n0 + c0 + 32 <= p.N && (p.ldc & 7) == 0) {
-      // Rows sent home through a warp-private transpose: each store instruction writes eight
-      // whole 64-byte row segments instead of 32 scattered 16-byte pieces.
-      float* tw = reinterpret_cast<float*>(smem) + warp * (32 * 33);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
-      __syncwarp();
-      const int limit = row_limit >= 0 ? row_limit : p.M;
-      const int cc = (lane & 3) * 8;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int rr = q * 8 + (lane >> 2);
-        const int grow = m0 + warp * 32 + rr;
-        if (grow < limit) {
-          const int2 dstm = p.scatter[grow];
-          __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
-          const float* t = tw + rr * 33 + cc;
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * e], t[2 * e + 1]);
-            w[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(Cr + n0 + c0 + cc) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      __syncwarp();
-      continue;
-    }
-    if (!ok || !row_ok) continue;
-    const int nbase = n0 + c0;
-    if (p.c_mode == kStoreBF16Scatter) {
-      // Row m goes home: rank scatter[m].x, row scatter[m].y of that rank's C (peer memory).
-      const int2 dstm = p.scatter[row];
-      __nv_bfloat16* Cr = reinterpret_cast<__nv_bfloat16*>(p.peers[dstm.x]) + (long long)dstm.y * p.ldc;
-      if (c0 + 32 <= BN && nbase + 32 <= p.N && ((reinterpret_cast<uintptr_t>(Cr + nbase) & 15) == 0)) {
-        uint4* Cv = reinterpret_cast<uint4*>(Cr + nbase);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
-                                                           alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
-            w[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = nbase + j;
-          if (j < BN - c0 && n < p.N) Cr[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
-        }
-      }
-    } else if (p.c_mode == kPeerSlotF32) {
-      // Reduce-scatter: element i is stored (plain 16-byte peer stores, no atomics) into its
-      // owner's slot for THIS rank; the owner sums its `world` slots after a barrier.
-      const long long slot = 4 * p.per4;
-      const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
-      if (c0 + 32 <= BN && nbase + 32 <= p.N && ((rowoff + nbase) & 3) == 0) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const long long i = rowoff + nbase + 4 * q;
-          int owner = (int)((i >> 2) / p.per4);
-          owner = owner < p.world ? owner : p.world - 1;
-          float4* dst = reinterpret_cast<float4*>(p.peers[owner] + p.self_rank * slot + (i - owner * slot));
-          *dst = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
-                             alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = nbase + j;
-          if (j < BN - c0 && n < p.N) {
-            const long long i = rowoff + n;
-            int owner = (int)((i >> 2) / p.per4);
-            owner = owner < p.world ? owner : p.world - 1;
-            p.peers[owner][p.self_rank * slot + (i - owner * slot)] = alpha * __uint_as_float(r[j]);
-          }
-        }
-      }
-    } else if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
-        (((long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase) & 3) == 0) {
-      // A float4 never straddles two owners (ownership is assigned in whole float4 units).
-      // 16-byte vector atomics go to this rank's own slice only; other owners get scalar
-      // fp32 atomics, the form peer (NVLink) atomics are known to support.
-      const long long i0 = (long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const long long i = i0 + 4 * q;
-        int owner = (int)((i >> 2) / p.per4);
-        owner = owner < p.world ? owner : p.world - 1;
-        float* dst = p.peers[owner] + i;
-        const float v0 = alpha * __uint_as_float(r[4 * q]), v1 = alpha * __uint_as_float(r[4 * q + 1]);
-        const float v2 = alpha * __uint_as_float(r[4 * q + 2]), v3 = alpha * __uint_as_float(r[4 * q + 3]);
-        if (owner == p.self_rank) {
-          atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v0, v1, v2, v3));
-        } else {
-          atomicAdd(dst, v0);
-          atomicAdd(dst + 1, v1);
-          atomicAdd(dst + 2, v2);
-          atomicAdd(dst + 3, v3);
-        }
-      }
-    } else if (p.c_mode == kPeerAtomicF32) {
-      const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = nbase + j;
-        if (j < BN - c0 && n < p.N) {
-          const long long i = rowoff + n;
-          int owner = (int)((i >> 2) / p.per4);
-          owner = owner < p.world ? owner : p.world - 1;
-          atomicAdd(p.peers[owner] + i, alpha * __uint_as_float(r[j]));
-        }
-      }
-    } else if ((p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) && c0 + 32 <= BN && nbase + 32 <= p.N &&
-               ((reinterpret_cast<uintptr_t>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
-                                             (long long)row * p.ldc + nbase) & 15) == 0)) {
-      // A whole 32-column chunk in range and 16-byte aligned: 8 vector accesses per thread
-      // instead of 32 scalar ones (the scalar form saturated the LSU pipe on large tiles).
-      float4* Cv = reinterpret_cast<float4*>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
-                                             (long long)row * p.ldc + nbase);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 v = make_float4(alpha * __uint_as_float(r[4 * q]), alpha * __uint_as_float(r[4 * q + 1]),
-                               alpha * __uint_as_float(r[4 * q + 2]), alpha * __uint_as_float(r[4 * q + 3]));
-        if (p.c_mode == kAtomicF32) {
-          atomicAdd(Cv + q, v);
-        } else {
-          if (p.beta_accumulate) {
-            const float4 o = Cv[q];
-            v.x += o.x;
-            v.y += o.y;
-            v.z += o.z;
-            v.w += o.w;
-          }
-          Cv[q] = v;
-        }
-      }
-    } else if (p.c_mode == kStoreBF16 && c0 + 32 <= BN && nbase + 32 <= p.N &&
-               ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
-                                             (long long)row * p.ldc + nbase) & 15) == 0)) {
-      uint4* Cv = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
-                                           (long long)row * p.ldc + nbase);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(alpha * __uint_as_float(r[8 * q + 2 * e]),
-                                                         alpha * __uint_as_float(r[8 * q + 2 * e + 1]));
-          w[e] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        Cv[q] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    } else if (p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) {
-      float* Cz = static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
-                  (long long)row * p.ldc;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = nbase + j;
-        if (j < BN - c0 && n < p.N) {
-          const float v = alpha * __uint_as_float(r[j]);
-          if (p.c_mode == kStoreF32)
-            Cz[n] = p.beta_accumulate ? Cz[n] + v : v;
-          else
-            atomicAdd(Cz + n, v);
-        }
-      }
-    } else if (p.c_mode == kStoreBF16) {
-      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
-                          (long long)row * p.ldc;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = nbase + j;
-        if (j < BN - c0 && n < p.N) Cz[n] = __float2bfloat16(alpha * __uint_as_float(r[j]));
-      }
-    } else if (p.c_mode == kStoreBF16T) {  // C^T[z][n][m]; consecutive lanes hit consecutive m
-      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = nbase + j;
-        if (j < BN - c0 && n < p.N)
-          Cz[(long long)n * p.ldc + row] = __float2bfloat16(alpha * __uint_as_float(r[j]));
-      }
-    } else {  // kStoreBF16TB: rows are (segment, t); element (m, n) -> C[m / T][n][m % T], T = ldc
-      __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
-                          (long long)(row / p.ldc) * p.N * p.ldc + row % p.ldc;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = nbase + j;
-        if (j < BN - c0 && n < p.N) Cz[(long long)n * p.ldc] = __float2bfloat16(alpha * __uint_as_float(r[j]));
-      }
-    }
+    if (!ok) continue;
+    store_chunk<BN>(p, r, Cbase, zc, m0, n0, c0, warp, lane, row_limit >= 0 ? row_limit : p.M,
+                    reinterpret_cast<float*>(smem) + warp * (32 * 33));
   }
   tc_fence_before();
   __syncthreads();
@@ -518,22 +525,194 @@ __global__ void __launch_bounds__(kThreads, 1)
   gemm_cta<BN>(&tmA, &tmStage, p, 0, 0, 0, 0, p.C, 0, nullptr, 0, &sc);
 }
 
-// Ragged grouped GEMM (expert layers): job j multiplies the rows [base[j], base[j] + len[j])
-// of one A matrix by its own B = B3[j] (a 3-D weight tensor, one map); CTA (x, t) serves
-// N tile x of the t-th 128-row tile in job order (tile_prefix = exclusive prefix of the
-// per-job tile counts, computed on the device).  CTAs past the last tile return at once, so
-// the grid can be an upper bound and no host synchronisation is needed.
+// ---------------------------------------------------------------------------------------
+// Persistent GEMM: one CTA per SM walks a list of 128 x BN output tiles.  Warp roles:
+//   warps 0-3  epilogue (TMEM lanes 0-127), warp 4 TMA producer, warp 5 MMA issuer.
+// Two TMEM accumulators alternate between tiles, so the epilogue of tile i (TMEM -> registers
+// -> global / peer memory) runs while the MMAs of tile i + 1 fill the other accumulator, and
+// the stage ring of shared memory runs on across tile boundaries.  Barriers:
+//   full[s] / empty[s]   TMA -> MMA / MMA -> TMA per stage;
+//   acc_full[b]          MMA -> epilogue (tcgen05.commit after the tile's last K block);
+//   acc_empty[b]         epilogue -> MMA (one arrival per epilogue warp).
+// Every wait is bounded; a role whose wait gives up leaves its loop (the others then give up
+// on their next wait), so an error costs a few seconds at most and never hangs the GPU.
+// ---------------------------------------------------------------------------------------
+constexpr int kPThreads = 192;
+
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_ragged_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       GemmParams p, const int* __restrict__ tile_prefix, const int* __restrict__ base,
-                       const int* __restrict__ len, int jobs) {
-  const int t = blockIdx.y;
-  if (t >= tile_prefix[jobs]) return;
-  int j = 0;
-  while (j + 1 < jobs && tile_prefix[j + 1] <= t) ++j;
-  const int m0 = base[j] + (t - tile_prefix[j]) * BM;
-  gemm_cta<BN>(&tmA, &tmB, p, 0, j, 0, 0, p.C, 0, nullptr, 0, nullptr, m0, base[j] + len[j]);
+struct PCfg {
+  static constexpr int kTileA = BM * BK * 2;
+  static constexpr int kTileB = BN * BK * 2;
+  static constexpr int kTw = 4 * 32 * 33 * 4;  // epilogue transpose scratch (4 warps)
+  static constexpr int kStages = (220 * 1024 - kTw) / (kTileA + kTileB);
+  static constexpr int kSmem = kStages * (kTileA + kTileB) + kTw + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTmemCols = 2 * BN;
+};
+
+// Tile list: dense (tiles_n x tiles_m x batch, n fastest) or, with tile_prefix, the ragged
+// row segments of `jobs` expert groups (row tile t of the job j with
+// tile_prefix[j] <= t < tile_prefix[j + 1]; device tables).
+struct TileSched {
+  int tiles_n, tiles_m, batch;
+  const int* tile_prefix;
+  const int* base;
+  const int* len;
+  int jobs;
+};
+
+struct TileCoord {
+  int m0, n0, za, zb, zc, limit;
+};
+
+template <int BN>
+__device__ __forceinline__ TileCoord decode_tile(const TileSched& ts, const GemmParams& p, int tile) {
+  TileCoord c;
+  const int rest = tile / ts.tiles_n;
+  c.n0 = (tile - rest * ts.tiles_n) * BN;
+  if (ts.tile_prefix != nullptr) {
+    int lo = 0, hi = ts.jobs - 1;  // largest j with tile_prefix[j] <= rest
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (ts.tile_prefix[mid] <= rest) lo = mid;
+      else hi = mid - 1;
+    }
+    c.m0 = ts.base[lo] + (rest - ts.tile_prefix[lo]) * BM;
+    c.za = 0;
+    c.zb = lo;
+    c.zc = 0;
+    c.limit = ts.base[lo] + ts.len[lo];
+  } else {
+    const int z = rest / ts.tiles_m;
+    c.m0 = (rest - z * ts.tiles_m) * BM;
+    c.za = z;
+    c.zb = p.b_shared ? 0 : z;
+    c.zc = z;
+    c.limit = p.M;
+  }
+  return c;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           GemmParams p, TileSched ts) {
+  using C = PCfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (sbase & 1023)) & 1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * C::kTileA;
+  float* tw = reinterpret_cast<float*>(sB + S * C::kTileB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tw) + C::kTw);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int total = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
+                                              : ts.tiles_n * ts.tiles_m * ts.batch;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int g = 0;
+      bool alive = true;
+      for (int tile = blockIdx.x; tile < total && alive; tile += gridDim.x) {
+        const TileCoord c = decode_tile<BN>(ts, p, tile);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % S;
+          if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, kErrWaitEmpty)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::kTileA + C::kTileB);
+          tma_load_3d(sA + s * C::kTileA, &tmA, &full[s], kb * BK, c.m0, c.za);
+          tma_load_3d(sB + s * C::kTileB, &tmB, &full[s], kb * BK, c.n0, c.zb);
+          ++g;
+        }
+      }
+      // Never leave with a bulk copy still landing in this CTA's shared memory.
+      for (int i = max(0, g - S); i < g; ++i) mbar_wait(&full[i % S], (i / S) & 1, p.err, kErrWaitFull);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int g = 0, it = 0;
+      bool alive = true;
+      for (int tile = blockIdx.x; tile < total && alive; tile += gridDim.x, ++it) {
+        const int b = it & 1;
+        if (!mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1, p.err, kErrWaitDone)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1, p.err, kErrWaitFull)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_kmajor_sw128(sA + s * C::kTileA);
+          const uint64_t db = smem_desc_kmajor_sw128(sB + s * C::kTileB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) tc_mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    // ---- epilogue (warps 0-3: TMEM lanes 32w .. 32w + 31) ----
+    float* twp = tw + warp * (32 * 33);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const TileCoord c = decode_tile<BN>(ts, p, tile);
+      const int b = it & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, p.err, kErrWaitDone));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN + c0), r);
+        tmem_ld_wait();
+        if (c0 + 32 >= BN) {
+          // the accumulator is in registers: hand it back to the MMA warp before the last stores
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        store_chunk<BN>(p, r, p.C, c.zc, c.m0, c.n0, c0, warp, lane, c.limit, twp);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 // B held by the peers (sharded weights, read over NVLink through per-peer tensor maps in the
@@ -661,21 +840,44 @@ void launch_staged_bn(const GemmOperand& A, const GemmOperand& stage_op, const G
   gemm_staged_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, ts, to, p, sa);
 }
 
+int sm_count() {
+  static int count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (count[dev & 63] == 0) cudaDeviceGetAttribute(&count[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  return count[dev & 63];
+}
+
 template <int BN>
-void launch_ragged_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const int* tile_prefix,
-                      const int* base, const int* len, int jobs, int max_tiles, cudaStream_t stream) {
-  using C = Cfg<BN>;
+void launch_persistent_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const TileSched& ts,
+                          long long max_tiles, cudaStream_t stream) {
+  using C = PCfg<BN>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured >> dev & 1ull)) {
-    cudaFuncSetAttribute(gemm_ragged_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaFuncSetAttribute(gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     configured |= 1ull << dev;
   }
+  if (max_tiles <= 0) return;
   CUtensorMap ta = make_tmap_kmajor_bf16(A, BM);
   CUtensorMap tb = make_tmap_kmajor_bf16(B, BN);
-  dim3 grid((p.N + BN - 1) / BN, max_tiles, 1);
-  gemm_ragged_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(ta, tb, p, tile_prefix, base, len, jobs);
+  const int grid = (int)std::min<long long>(max_tiles, sm_count());
+  gemm_persistent_kernel<BN><<<grid, kPThreads, C::kSmem, stream>>>(ta, tb, p, ts);
+}
+
+template <int BN>
+void launch_ragged_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const int* tile_prefix,
+                      const int* base, const int* len, int jobs, int max_tiles, cudaStream_t stream) {
+  TileSched ts{};
+  ts.tiles_n = (p.N + BN - 1) / BN;
+  ts.tiles_m = 0;
+  ts.batch = 1;
+  ts.tile_prefix = tile_prefix;
+  ts.base = base;
+  ts.len = len;
+  ts.jobs = jobs;
+  launch_persistent_bn<BN>(A, B, p, ts, (long long)max_tiles * ts.tiles_n, stream);
 }
 
 template <int BN>
@@ -779,6 +981,22 @@ int pick_bn(int N) {
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream) {
   if (p.splits < 1) p.splits = 1;
+  // More than one wave of tiles without split-K: the persistent kernel (epilogue of one tile
+  // overlapped with the MMAs of the next).
+  const long long tiles = (long long)((p.N + bn - 1) / bn) * ((p.M + BM - 1) / BM) * p.batch;
+  if (p.splits == 1 && bn >= 64 && p.K > 0 && tiles > sm_count()) {
+    TileSched ts{};
+    ts.tiles_n = (p.N + bn - 1) / bn;
+    ts.tiles_m = (p.M + BM - 1) / BM;
+    ts.batch = p.batch;
+    ts.jobs = 0;
+    switch (bn) {
+      case 64: launch_persistent_bn<64>(A, B, p, ts, tiles, stream); return;
+      case 128: launch_persistent_bn<128>(A, B, p, ts, tiles, stream); return;
+      case 256: launch_persistent_bn<256>(A, B, p, ts, tiles, stream); return;
+      default: break;
+    }
+  }
   switch (bn) {
     case 16: launch_bn<16>(A, B, p, stream); break;
     case 32: launch_bn<32>(A, B, p, stream); break;

@@ -110,7 +110,70 @@ __global__ void combine_bwd_dispatch_kernel(const uint4* __restrict__ dy, const 
   }
 }
 
+// Routing histogram: counts[e] += rows routed to expert e (counts zeroed by the caller).
+__global__ void moe_count_kernel(const long long* __restrict__ topi, int rows, int* __restrict__ counts) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x)
+    atomicAdd(&counts[(int)topi[r]], 1);
+}
+
+// Receive layout of every owner: its rows grouped by local expert, then by source rank.
+// all_counts[src][e] = rows source `src` routes to expert e (e = owner * e_l + local expert).
+// Each block derives this source's first row per expert in shared memory, then places its
+// rows: dst_row = first row of (owner, expert) + a slot claimed with an atomic (the order of
+// rows inside one (source, expert) group does not matter: each row carries its origin).
+// Block 0 also writes this rank's owner-side tables for the ragged expert GEMM.
+__global__ void moe_place_kernel(const long long* __restrict__ topi, int rows, const int* __restrict__ all_counts,
+                                 int world, int rank, int e_l, int* __restrict__ cursor, int* __restrict__ dest,
+                                 int* __restrict__ dst_row, int* __restrict__ tile_prefix, int* __restrict__ base,
+                                 int* __restrict__ len, int* __restrict__ total) {
+  extern __shared__ int first[];  // [world * e_l]
+  const int experts = world * e_l;
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) {
+    const int owner = e / e_l, le = e % e_l;
+    int off = 0;
+    for (int l = 0; l < le; ++l)
+      for (int s = 0; s < world; ++s) off += all_counts[s * experts + owner * e_l + l];
+    for (int s = 0; s < rank; ++s) off += all_counts[s * experts + e];
+    first[e] = off;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    int b = 0, t = 0;
+    for (int l = 0; l < e_l; ++l) {
+      int n = 0;
+      for (int s = 0; s < world; ++s) n += all_counts[s * experts + rank * e_l + l];
+      base[l] = b;
+      len[l] = n;
+      tile_prefix[l] = t;
+      b += n;
+      t += (n + 127) / 128;
+    }
+    tile_prefix[e_l] = t;
+    *total = b;
+  }
+  __syncthreads();
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const int e = (int)topi[r];
+    dest[r] = e / e_l;
+    dst_row[r] = first[e] + atomicAdd(&cursor[e], 1);
+  }
+}
+
 }  // namespace
+
+void moe_count(const long long* topi, int rows, int* counts, cudaStream_t s) {
+  if (rows <= 0) return;
+  const int grid = (rows + 255) / 256 < 148 * 4 ? (rows + 255) / 256 : 148 * 4;
+  moe_count_kernel<<<grid, 256, 0, s>>>(topi, rows, counts);
+}
+
+void moe_place(const long long* topi, int rows, const int* all_counts, int world, int rank, int e_l, int* cursor,
+               int* dest, int* dst_row, int* tile_prefix, int* base, int* len, int* total, cudaStream_t s) {
+  const int blocks = (rows + 255) / 256;
+  const int grid = blocks < 1 ? 1 : (blocks < 148 * 2 ? blocks : 148 * 2);
+  moe_place_kernel<<<grid, 256, (size_t)world * e_l * sizeof(int), s>>>(topi, rows, all_counts, world, rank, e_l,
+                                                                         cursor, dest, dst_row, tile_prefix, base,
+                                                                         len, total);
+}
 
 void moe_combine(const void* slots, const float* w, void* y, int tokens, int k, int cols, cudaStream_t s) {
   if (tokens <= 0) return;

@@ -12,6 +12,14 @@ void moe_dispatch(const void* src, long long token_stride, const int* dst_rank, 
                   void* const* peer_rows, int2* const* peer_meta, int world, int rows, int cols, int self,
                   int rows_per_token, cudaStream_t s);
 
+// counts[e] += number of rows (entries of topi, int64 expert ids) routed to expert e.
+void moe_count(const long long* topi, int rows, int* counts, cudaStream_t s);
+
+// Receive-buffer rows of this rank's routed rows (dest rank, row) from every source's
+// histogram, plus this rank's owner-side ragged-GEMM tables and received-row total.
+void moe_place(const long long* topi, int rows, const int* all_counts, int world, int rank, int e_l, int* cursor,
+               int* dest, int* dst_row, int* tile_prefix, int* base, int* len, int* total, cudaStream_t s);
+
 // y[t] = sum_j w[t * k + j] * slots[t * k + j] for t < tokens (bf16 rows of cols, fp32 w).
 void moe_combine(const void* slots, const float* w, void* y, int tokens, int k, int cols, cudaStream_t s);
 

@@ -191,9 +191,19 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
         with torch.no_grad():
             secs = _time(lambda: moe(xm), iters=10)
         rows_moved = t * top_k * (world - 1) / world
+        fwd_flops = 2.0 * t * top_k * (h * 2 * inter + inter * h) + 2.0 * t * h * n_exp
         report("expert-parallel MoE forward (dispatch + expert GEMMs + combine in the down-GEMM epilogue)",
-               secs, 2.0 * t * top_k * (h * 2 * inter + inter * h) + 2.0 * t * h * n_exp,
-               2 * rows_moved * h * 2, 4 * t * top_k * h * 2,
+               secs, fwd_flops, 2 * rows_moved * h * 2, 4 * t * top_k * h * 2,
+               {"tokens_per_rank": t, "experts": n_exp, "top_k": top_k})
+        xg = xm.clone().requires_grad_()
+
+        def fwd_bwd():
+            y = moe(xg)
+            y.backward(torch.ones_like(y))
+
+        secs = _time(fwd_bwd, iters=10)
+        report("expert-parallel MoE forward + backward (input and router gradients; experts frozen)",
+               secs, 2 * fwd_flops, 4 * rows_moved * h * 2, 8 * t * top_k * h * 2,
                {"tokens_per_rank": t, "experts": n_exp, "top_k": top_k})
     ops.check_device_errors(dev)
     return rows

@@ -4,9 +4,9 @@ Experts are sharded over the ranks (``n_experts / world`` each); the router is r
 One forward:
 
 1. route: router GEMM, softmax, top-k (PyTorch; its backward reaches the router);
-2. layout: per (owner rank, local expert) row counts are exchanged (a tiny NCCL
-   all-gather -- the control plane), and every rank derives the same receive layout:
-   each owner's rows grouped by local expert, then by source rank;
+2. layout: per-expert row counts (``moe_count``) are exchanged (a tiny NCCL all-gather --
+   the control plane); from them ``moe_place`` derives the receive layout (each owner's
+   rows grouped by local expert, then by source rank) and this rank's ragged-GEMM tables;
 3. dispatch: one kernel stores each (token, slot) row straight into its owner's receive
    buffer (16-byte peer stores, ``moe_dispatch``) with its origin;
 4. experts: ONE ragged tcgen05 GEMM over all local experts' row segments (gate/up), a
@@ -32,16 +32,6 @@ from torch import nn
 from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
 
 
-def _jobs(mine: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """``(tile_prefix, base, len)`` int32 device arrays of the local experts' row segments."""
-    n = mine.to(torch.int32)
-    base = (torch.cumsum(n, 0) - n).to(torch.int32)
-    tiles = (n + 127) // 128
-    prefix = torch.zeros(n.numel() + 1, dtype=torch.int32, device=n.device)
-    prefix[1:] = torch.cumsum(tiles, 0)
-    return prefix, base.contiguous(), n.contiguous()
-
-
 class _EPMoE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, topv, topi, mod):
@@ -52,34 +42,33 @@ class _EPMoE(torch.autograd.Function):
         dev = x2.device
         if t > mod.max_tokens:
             raise ValueError(f"{t} tokens exceed this layer's capacity of {mod.max_tokens} per rank")
-        dest = (topi // e_l).reshape(-1)
-        le = (topi % e_l).reshape(-1)
-        key = dest * e_l + le
-        counts = torch.bincount(key, minlength=world * e_l)  # (world_dst * e_l)
-        all_counts = torch.empty(world, world * e_l, dtype=counts.dtype, device=dev)
-        dist.all_gather_into_tensor(all_counts, counts, group=mod.group)
-        cnt = all_counts.view(world, world, e_l)  # [src, dst, local expert]
-        # receive layout of owner r: by local expert, then by source rank
-        per_le = cnt.sum(0)                                       # [dst, le]
-        le_base = torch.cumsum(per_le, 1) - per_le                # [dst, le]
-        src_base = torch.cumsum(cnt, 0) - cnt                     # [src, dst, le]
-        off = le_base[None] + src_base                            # [src, dst, le]
-        order = torch.argsort(key, stable=True)
-        grp_start = torch.cumsum(counts, 0) - counts
-        rank_in = torch.empty_like(key)
-        rank_in[order] = torch.arange(key.numel(), device=dev) - grp_start[key[order]]
-        dst_row = off[rank].reshape(-1)[key] + rank_in
-        mine = per_le[rank]                                       # rows I receive, per local expert
-        dest32, row32 = dest.to(torch.int32).contiguous(), dst_row.to(torch.int32).contiguous()
-        prefix, base, lens = _jobs(mine)
-        total_in = int(mine.sum())  # one host read per layer: sizes the expert buffers exactly
-        max_tiles = (total_in + 127) // 128 + e_l
-        rows_dev = mine.sum().to(torch.int32).reshape(1)
+        n_exp = world * e_l
+        topi = topi.reshape(-1).contiguous()
+        rows = topi.numel()
+        # int32 scratch: [counts | cursor | tile_prefix | base | len | total]
+        work = torch.zeros(2 * n_exp + 3 * e_l + 2, dtype=torch.int32, device=dev)
+        counts, cursor = work[:n_exp], work[n_exp:2 * n_exp]
+        prefix = work[2 * n_exp:2 * n_exp + e_l + 1]
+        base = work[2 * n_exp + e_l + 1:2 * n_exp + 2 * e_l + 1]
+        lens = work[2 * n_exp + 2 * e_l + 1:2 * n_exp + 3 * e_l + 1]
+        rows_dev = work[2 * n_exp + 3 * e_l + 1:]
+        ops.count_launch()
+        ops.native().moe_count(topi, counts)
+        all_counts = torch.empty(world, n_exp, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(all_counts, counts, group=mod.group)  # the control plane
+        dest32 = torch.empty(rows, dtype=torch.int32, device=dev)
+        row32 = torch.empty(rows, dtype=torch.int32, device=dev)
+        ops.count_launch()
+        ops.native().moe_place(topi, all_counts, rank, e_l, cursor, dest32, row32, prefix, base, lens, rows_dev)
 
         mod.barrier.wait()  # every rank is done with the previous use of the receive buffers
         ops.count_launch()
         ops.native().moe_dispatch(x2, k, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, rank)
         mod.barrier.wait()  # every row has landed
+        # One host read per layer (it sizes the expert buffers exactly); the dispatch above is
+        # already queued, so the GPU stays busy while the host waits.
+        total_in = int(rows_dev.item())
+        max_tiles = (total_in + 127) // 128 + e_l
 
         err = ops.error_word(dev)
         h = torch.empty(max(total_in, 1), 2 * mod.intermediate, dtype=torch.bfloat16, device=dev)

@@ -198,3 +198,27 @@ def test_gemm_reduce_scatter_slots_emulated():
         ops.native().slot_reduce(bufs[r], world, slot, got[r * slot:], min(slot, elems - r * slot) // 4 * 4, True)
     torch.testing.assert_close(got[:elems] - 1.0, want, rtol=1e-3, atol=1e-2)
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("mode", ["f32", "f32acc", "bf16", "bf16t", "atomic"])
+@pytest.mark.parametrize(("z", "m", "n", "k"), [(1, 8192, 2048, 512), (1, 8000, 1000, 328), (3, 4096, 640, 256)])
+def test_persistent_gemm_many_tiles(mode, z, m, n, k):
+    """More than one wave of output tiles takes the persistent kernel (two TMEM accumulators,
+    epilogue overlapped with the next tile's MMAs); partial row / column tiles included."""
+    a = torch.randn(z, m, k, device="cuda").bfloat16()
+    b = torch.randn(n, k, device="cuda").bfloat16()
+    want = a.float() @ b.float().T
+    if mode in ("f32", "f32acc", "atomic"):
+        out = torch.ones(z, m, n, device="cuda") if mode != "f32" else torch.empty(z, m, n, device="cuda")
+        store = ops.STORE_ATOMIC_F32 if mode == "atomic" else ops.STORE_F32
+        ops.gemm_tn(a, b, out, mode=store, accumulate=mode == "f32acc")
+        got = out - 1 if mode != "f32" else out
+    elif mode == "bf16":
+        out = torch.empty(z, m, n, device="cuda", dtype=torch.bfloat16)
+        got = ops.gemm_tn(a, b, out, mode=ops.STORE_BF16).float()
+    else:
+        out = torch.empty(z, n, m, device="cuda", dtype=torch.bfloat16)
+        got = ops.gemm_tn(a, b, out, mode=ops.STORE_BF16_T).float().transpose(1, 2)
+    tol = 2e-2 if mode in ("bf16", "bf16t") else 1e-3
+    torch.testing.assert_close(got, want, rtol=tol, atol=tol * float(want.abs().max()))
+    ops.check_device_errors()
