@@ -772,8 +772,9 @@ Tensor norm_per_sample_grad(Tensor x, Tensor g, double eps, bool layer_norm, boo
 
 // Ragged grouped GEMM of expert layers: rows [base[j], base[j] + len[j]) of A times B3[j]^T;
 // output rows stored in C (same row index) or, with `scatter`, returned to their source
-// ranks' buffers peer_C.  tile_prefix / base / len are device int32 arrays; max_tiles bounds
-// the number of 128-row tiles (CTAs past the real count return at once).
+// ranks' buffers peer_C.  tile_prefix / base / len are device int32 arrays (tile_prefix counts
+// 256-row blocks); max_tiles bounds the number of such blocks (the persistent kernel reads
+// the real count on the device).
 void gemm_ragged(Tensor A, Tensor B3, c10::optional<Tensor> C, Tensor tile_prefix, Tensor base, Tensor len,
                  int64_t max_tiles, std::vector<Tensor> peer_C, c10::optional<Tensor> scatter, Tensor err,
                  int64_t bn) {

@@ -550,8 +550,9 @@ struct PCfg {
 };
 
 // Tile list: dense (tiles_n x tiles_m x batch, n fastest) or, with tile_prefix, the ragged
-// row segments of `jobs` expert groups (row tile t of the job j with
-// tile_prefix[j] <= t < tile_prefix[j + 1]; device tables).
+// row segments of `jobs` expert groups: 256-row block t belongs to the job j with
+// tile_prefix[j] <= t < tile_prefix[j + 1] (device tables; tile_prefix counts 256-row
+// blocks, the unit of the CTA-pair kernel).
 struct TileSched {
   int tiles_n, tiles_m, batch;
   const int* tile_prefix;
@@ -570,13 +571,15 @@ __device__ __forceinline__ TileCoord decode_tile(const TileSched& ts, const Gemm
   const int rest = tile / ts.tiles_n;
   c.n0 = (tile - rest * ts.tiles_n) * BN;
   if (ts.tile_prefix != nullptr) {
-    int lo = 0, hi = ts.jobs - 1;  // largest j with tile_prefix[j] <= rest
+    // the tables count 256-row blocks; this kernel's 128-row tiles are their halves
+    const int blk = rest >> 1;
+    int lo = 0, hi = ts.jobs - 1;  // largest j with tile_prefix[j] <= blk
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (ts.tile_prefix[mid] <= rest) lo = mid;
+      if (ts.tile_prefix[mid] <= blk) lo = mid;
       else hi = mid - 1;
     }
-    c.m0 = ts.base[lo] + (rest - ts.tile_prefix[lo]) * BM;
+    c.m0 = ts.base[lo] + (blk - ts.tile_prefix[lo]) * 2 * BM + (rest & 1) * BM;
     c.za = 0;
     c.zb = lo;
     c.zc = 0;
@@ -613,7 +616,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int kblocks = (p.K + BK - 1) / BK;
-  const int total = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
+  const int total = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * 2 * ts.tiles_n
                                               : ts.tiles_n * ts.tiles_m * ts.batch;
 
   if (threadIdx.x == 0) {
@@ -713,6 +716,182 @@ __global__ void __launch_bounds__(kPThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 5) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------------------
+// CTA-pair persistent GEMM (cta_group::2): each cluster of two CTAs on two SMs owns 256 x 256
+// output tiles.  Each CTA loads 128 rows of A and 128 rows of B per stage (32 KB instead of
+// the 48 KB a 128 x 256 single-SM tile needs for the same MMA work per SM), CTA 0 issues one
+// M=256, N=256 MMA per K step over both CTAs' shared memory, and each CTA's epilogue drains
+// its own 128 accumulator rows from its own TMEM.  Barriers as in gemm_persistent_kernel, with
+// the stage "full" barriers and the accumulator "empty" barriers living in CTA 0: both CTAs'
+// TMA loads complete on CTA 0's full barrier (CTA 0 expects the bytes of both), and both
+// CTAs' epilogue warps arrive on CTA 0's accumulator-empty barrier; CTA 0's commits arrive on
+// the stage-empty and accumulator-full barriers of both CTAs.
+// ---------------------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int kTileA = 128 * BK * 2;
+  static constexpr int kTileB = 128 * BK * 2;
+  static constexpr int kTw = 4 * 32 * 33 * 4;
+  static constexpr int kStages = (220 * 1024 - kTw) / (kTileA + kTileB);
+  static constexpr int kSmem = kStages * (kTileA + kTileB) + kTw + 1024 + 256;
+  static constexpr int kTmemCols = 512;  // two 256-column accumulators
+};
+
+__device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const GemmParams& p, int tile) {
+  TileCoord c;
+  const int rest = tile / ts.tiles_n;
+  c.n0 = (tile - rest * ts.tiles_n) * 256;
+  if (ts.tile_prefix != nullptr) {
+    int lo = 0, hi = ts.jobs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (ts.tile_prefix[mid] <= rest) lo = mid;
+      else hi = mid - 1;
+    }
+    c.m0 = ts.base[lo] + (rest - ts.tile_prefix[lo]) * 256;
+    c.za = 0;
+    c.zb = lo;
+    c.zc = 0;
+    c.limit = ts.base[lo] + ts.len[lo];
+  } else {
+    const int z = rest / ts.tiles_m;
+    c.m0 = (rest - z * ts.tiles_m) * 256;
+    c.za = z;
+    c.zb = p.b_shared ? 0 : z;
+    c.zc = z;
+    c.limit = p.M;
+  }
+  return c;
+}
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     GemmParams p, TileSched ts) {
+  using C = PairCfg;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (sbase & 1023)) & 1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * C::kTileA;
+  float* tw = reinterpret_cast<float*>(sB + S * C::kTileB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tw) + C::kTw);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int total = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
+                                              : ts.tiles_n * ts.tiles_m * ts.batch;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // four epilogue warps in each CTA of the pair
+    }
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc_pair(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either CTA signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs) ----
+      int g = 0;
+      bool alive = true;
+      for (int tile = pair; tile < total && alive; tile += pairs) {
+        const TileCoord c = decode_pair_tile(ts, p, tile);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % S;
+          if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, kErrWaitEmpty)) {
+            alive = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::kTileA + C::kTileB));
+          const uint32_t bar = map_shared_rank(smem_u32(&full[s]), 0);
+          tma_load_3d_pair(sA + s * C::kTileA, &tmA, bar, kb * BK, c.m0 + 128 * (int)rank, c.za);
+          tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kb * BK, c.n0 + 128 * (int)rank, c.zb);
+          ++g;
+        }
+      }
+      // CTA 0's full barriers count both CTAs' bytes: once they complete, nothing is landing
+      // in either CTA's shared memory (CTA 1 waits for this at the closing cluster barrier).
+      if (rank == 0)
+        for (int i = max(0, g - S); i < g; ++i) mbar_wait(&full[i % S], (i / S) & 1, p.err, kErrWaitFull);
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer (CTA 0) ----
+      constexpr uint32_t idesc = idesc_bf16_f32(256, 256);
+      int g = 0, it = 0;
+      bool alive = true;
+      for (int tile = pair; tile < total && alive; tile += pairs, ++it) {
+        const int b = it & 1;
+        if (!mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1, p.err, kErrWaitDone)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * 256);
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(&full[s], (g / S) & 1, p.err, kErrWaitFull)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_kmajor_sw128(sA + s * C::kTileA);
+          const uint64_t db = smem_desc_kmajor_sw128(sB + s * C::kTileB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) tc_mma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          tc_commit_pair(&empty[s]);
+        }
+        tc_commit_pair(&acc_full[b]);
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs; warps 0-3 drain this CTA's 128 accumulator rows) ----
+    float* twp = tw + warp * (32 * 33);
+    int it = 0;
+    for (int tile = pair; tile < total; tile += pairs, ++it) {
+      const TileCoord c = decode_pair_tile(ts, p, tile);
+      const int b = it & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, p.err, kErrWaitDone));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = 0; c0 < 256; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 256 + c0), r);
+        tmem_ld_wait();
+        if (c0 + 32 >= 256) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&acc_empty[b]), 0));
+        }
+        store_chunk<256>(p, r, p.C, c.zc, c.m0 + 128 * (int)rank, c.n0, c0, warp, lane, c.limit, twp);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while its partner may still signal its barriers
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc_pair(tmem, C::kTmemCols);
 }
 
 // B held by the peers (sharded weights, read over NVLink through per-peer tensor maps in the
@@ -866,18 +1045,76 @@ void launch_persistent_bn(const GemmOperand& A, const GemmOperand& B, const Gemm
   gemm_persistent_kernel<BN><<<grid, kPThreads, C::kSmem, stream>>>(ta, tb, p, ts);
 }
 
+// Clusters of two resident at once for the pair kernel (its shared memory keeps one CTA per
+// SM; pairs must fit inside a GPC, so this can be below half the SM count).
+int pair_clusters() {
+  static int count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (count[dev & 63] == 0) {
+    cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmem);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(kPThreads, 1, 1);
+    cfg.dynamicSmemBytes = PairCfg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = -1;  // clusters unavailable: callers fall back to the single-SM kernel
+    }
+    count[dev & 63] = n;
+  }
+  return count[dev & 63];
+}
+
+// Launch the pair kernel on up to `max_tiles` 256 x 256 tiles; false if it cannot run here.
+bool launch_pair(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const TileSched& ts,
+                 long long max_tiles, cudaStream_t stream) {
+  const int clusters = pair_clusters();
+  if (clusters <= 0) return false;
+  if (max_tiles <= 0) return true;
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, 128);
+  CUtensorMap tb = make_tmap_kmajor_bf16(B, 128);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(max_tiles, clusters), 1, 1);
+  cfg.blockDim = dim3(kPThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, p, ts);
+  return true;
+}
+
+// max_blocks bounds the number of 256-row blocks of all jobs together.
 template <int BN>
 void launch_ragged_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const int* tile_prefix,
-                      const int* base, const int* len, int jobs, int max_tiles, cudaStream_t stream) {
+                      const int* base, const int* len, int jobs, int max_blocks, cudaStream_t stream) {
   TileSched ts{};
-  ts.tiles_n = (p.N + BN - 1) / BN;
   ts.tiles_m = 0;
   ts.batch = 1;
   ts.tile_prefix = tile_prefix;
   ts.base = base;
   ts.len = len;
   ts.jobs = jobs;
-  launch_persistent_bn<BN>(A, B, p, ts, (long long)max_tiles * ts.tiles_n, stream);
+  if (BN == 256) {
+    ts.tiles_n = (p.N + 255) / 256;
+    if (launch_pair(A, B, p, ts, (long long)max_blocks * ts.tiles_n, stream)) return;
+  }
+  ts.tiles_n = (p.N + BN - 1) / BN;
+  launch_persistent_bn<BN>(A, B, p, ts, (long long)max_blocks * 2 * ts.tiles_n, stream);
 }
 
 template <int BN>
@@ -984,6 +1221,14 @@ void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, in
   // More than one wave of tiles without split-K: the persistent kernel (epilogue of one tile
   // overlapped with the MMAs of the next).
   const long long tiles = (long long)((p.N + bn - 1) / bn) * ((p.M + BM - 1) / BM) * p.batch;
+  if (p.splits == 1 && bn == 256 && p.K > 0 && tiles > sm_count()) {
+    TileSched ts{};
+    ts.tiles_n = (p.N + 255) / 256;
+    ts.tiles_m = (p.M + 255) / 256;
+    ts.batch = p.batch;
+    ts.jobs = 0;
+    if (launch_pair(A, B, p, ts, (long long)ts.tiles_n * ts.tiles_m * ts.batch, stream)) return;
+  }
   if (p.splits == 1 && bn >= 64 && p.K > 0 && tiles > sm_count()) {
     TileSched ts{};
     ts.tiles_n = (p.N + bn - 1) / bn;

@@ -145,7 +145,7 @@ __global__ void moe_place_kernel(const long long* __restrict__ topi, int rows, c
       len[l] = n;
       tile_prefix[l] = t;
       b += n;
-      t += (n + 127) / 128;
+      t += (n + 255) / 256;  // 256-row blocks, the ragged GEMM's unit
     }
     tile_prefix[e_l] = t;
     *total = b;

@@ -177,8 +177,52 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
         secs = _time(cov_allreduce)
         report("covariance all-reduce (two-shot NVLink peer kernel, 2048^2 fp32)", secs, 0.0,
                2 * (world - 1) / world * w * w * 4, (world + 2) * w * w * 4 / world)
-    # 5) expert-parallel MoE (real ranks only): dispatch + experts + combine-in-epilogue
-    if not emulate:
+    # 5) expert-parallel MoE
+    if emulate:
+        # The owner-side kernels with the peers' buffers emulated locally: dispatch of 4096
+        # tokens x top-8 rows into W receive buffers, the ragged gate/up GEMM over this owner's
+        # 64 / W experts, the split SwiGLU, and the ragged down GEMM scattering its rows home.
+        h, inter, n_exp, top_k, t = 2048, 1024, 64, 8, 4096
+        e_l = n_exp // world
+        rows_in = t * top_k
+        x2 = torch.randn(t, h, device=dev, generator=gen).bfloat16()
+        dest = torch.randint(0, world, (rows_in,), device=dev, generator=gen)
+        order = torch.argsort(dest, stable=True)
+        per = torch.bincount(dest, minlength=world)
+        start = torch.cumsum(per, 0) - per
+        row = torch.empty_like(dest)
+        row[order] = torch.arange(rows_in, device=dev) - start[dest[order]]
+        recv = [torch.empty(rows_in, h, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+        meta = [torch.empty(rows_in, 2, device=dev, dtype=torch.int32) for _ in range(world)]
+        d32, r32 = dest.int().contiguous(), row.int().contiguous()
+        secs = _time(lambda: nat.moe_dispatch(x2, top_k, d32, r32, recv, meta, rank))
+        report("moe_dispatch (rows stored into the owners' receive buffers)", secs, 0.0, 0.0,
+               rows_in * h * 2 * 2 + t * h * 2)
+        n_i = torch.full((e_l,), rows_in // e_l, dtype=torch.int32, device=dev)
+        base = (torch.cumsum(n_i, 0) - n_i).int().contiguous()
+        prefix = torch.zeros(e_l + 1, dtype=torch.int32, device=dev)
+        prefix[1:] = torch.cumsum((n_i + 255) // 256, 0)  # 256-row blocks
+        max_tiles = rows_in // 256 + e_l
+        gate_up = (0.02 * torch.randn(e_l, 2 * inter, h, device=dev, generator=gen)).bfloat16()
+        down = (0.02 * torch.randn(e_l, h, inter, device=dev, generator=gen)).bfloat16()
+        xin = torch.randn(rows_in, h, device=dev, generator=gen).bfloat16()
+        hh = torch.empty(rows_in, 2 * inter, device=dev, dtype=torch.bfloat16)
+        secs = _time(lambda: nat.gemm_ragged(xin, gate_up, hh, prefix, base, n_i, max_tiles, [], None, err))
+        report("gemm_ragged gate/up (persistent, all local experts in one launch)", secs,
+               2.0 * rows_in * h * 2 * inter, 0.0, (rows_in * h + rows_in * 2 * inter + e_l * 2 * inter * h) * 2)
+        secs_bmm = _time(lambda: torch.bmm(xin.view(e_l, -1, h), gate_up.transpose(1, 2)))
+        rows[-1]["cublas_bmm_same_flops_us"] = secs_bmm * 1e6
+        act = torch.empty(rows_in, inter, device=dev, dtype=torch.bfloat16)
+        nrows = torch.tensor([rows_in], dtype=torch.int32, device=dev)
+        secs = _time(lambda: nat.swiglu_split(hh, act, nrows))
+        report("swiglu_split", secs, 0.0, 0.0, rows_in * 3 * inter * 2)
+        homes = [torch.empty(rows_in // world + 1, h, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+        idx = torch.arange(rows_in, device=dev)
+        home_meta = torch.stack([idx % world, idx // world], 1).int().contiguous()
+        secs = _time(lambda: nat.gemm_ragged(act, down, None, prefix, base, n_i, max_tiles, homes, home_meta, err))
+        report("gemm_ragged down + scatter home (combine in the epilogue)", secs, 2.0 * rows_in * inter * h, 0.0,
+               (rows_in * inter + rows_in * h + e_l * h * inter) * 2)
+    else:
         from dattri_llm_b200.parallel.moe import ExpertParallelMoE
 
         h, inter, n_exp, top_k, t = 2048, 1024, 64, 8, 4096

@@ -68,7 +68,7 @@ class _EPMoE(torch.autograd.Function):
         # One host read per layer (it sizes the expert buffers exactly); the dispatch above is
         # already queued, so the GPU stays busy while the host waits.
         total_in = int(rows_dev.item())
-        max_tiles = (total_in + 127) // 128 + e_l
+        max_tiles = (total_in + 255) // 256 + e_l  # 256-row blocks of the ragged GEMM
 
         err = ops.error_word(dev)
         h = torch.empty(max(total_in, 1), 2 * mod.intermediate, dtype=torch.bfloat16, device=dev)

@@ -153,8 +153,8 @@ def test_gemm_ragged_expert_segments(scatter):
     n_i = torch.tensor(lens, dtype=torch.int32, device="cuda")
     base = (torch.cumsum(n_i, 0) - n_i).int()
     prefix = torch.zeros(len(lens) + 1, dtype=torch.int32, device="cuda")
-    prefix[1:] = torch.cumsum((n_i + 127) // 128, 0)
-    max_tiles = rows // 128 + len(lens) + 2  # an upper bound: surplus CTAs return at once
+    prefix[1:] = torch.cumsum((n_i + 255) // 256, 0)  # 256-row blocks
+    max_tiles = rows // 256 + len(lens) + 2  # an upper bound: the kernel reads the real count
     want = torch.empty(rows, n, device="cuda")
     start = 0
     for j, ln in enumerate(lens):
