@@ -559,6 +559,8 @@ struct TileSched {
   const int* base;
   const int* len;
   int jobs;
+  int n_rot;    // dense tiles: column-tile index rotation (a sharded B's own columns first)
+  int n_major;  // dense tiles: column tile is the slow index (all row blocks of one B tile in turn)
 };
 
 struct TileCoord {
@@ -740,8 +742,18 @@ struct PairCfg {
 
 __device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const GemmParams& p, int tile) {
   TileCoord c;
-  const int rest = tile / ts.tiles_n;
-  c.n0 = (tile - rest * ts.tiles_n) * 256;
+  int rest, tn;
+  if (ts.n_major) {  // dense only: tile = tn * (tiles_m * batch) + rest
+    const int rows = ts.tiles_m * ts.batch;
+    tn = tile / rows;
+    rest = tile - tn * rows;
+  } else {
+    rest = tile / ts.tiles_n;
+    tn = tile - rest * ts.tiles_n;
+  }
+  tn += ts.n_rot;
+  if (tn >= ts.tiles_n) tn -= ts.tiles_n;
+  c.n0 = tn * 256;
   if (ts.tile_prefix != nullptr) {
     int lo = 0, hi = ts.jobs - 1;
     while (lo < hi) {
@@ -765,9 +777,17 @@ __device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const
   return c;
 }
 
+// kStaged: B is a sharded weight being all-gathered by this very launch (the FSDP forward /
+// input-gradient GEMM): before their epilogues, the epilogue warps of every CTA copy pieces of
+// the remote shards over NVLink (16-byte peer loads) into the local staging matrix that tmB
+// maps, bumping the owner's flag after each piece; the producer reads its own shard in place
+// (tmOwn) and waits (bounded) for a remote owner's flag the first time it needs that owner's
+// rows (mode 0) or K range (mode 1).  Own-shard work is ordered first (column tiles rotated in
+// mode 0, the K loop rotated in mode 1), so the copies overlap the first tiles' MMAs.
+template <bool kStaged>
 __global__ void __launch_bounds__(kPThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     GemmParams p, TileSched ts) {
+                     GemmParams p, TileSched ts, const __grid_constant__ CUtensorMap tmOwn, StageArgs sa) {
   using C = PairCfg;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -794,6 +814,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (kStaged) tma_prefetch_desc(&tmOwn);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -816,18 +837,57 @@ __global__ void __launch_bounds__(kPThreads, 1)
       // ---- TMA producer (both CTAs) ----
       int g = 0;
       bool alive = true;
+      unsigned ready = 0u;  // staged: remote owners already waited for
+      const int kb_rot = (kStaged && sa.mode == 1) ? (sa.self * sa.shard) / BK : 0;
+      const int own_lo = kStaged ? sa.self * sa.shard : 0;
       for (int tile = pair; tile < total && alive; tile += pairs) {
         const TileCoord c = decode_pair_tile(ts, p, tile);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int brow = c.n0 + 128 * (int)rank;
+        // mode 0: this CTA's B rows belong to one owner for the whole tile
+        const CUtensorMap* bmap = &tmB;
+        int brow_map = brow;
+        if constexpr (kStaged) {
+          if (sa.mode == 0) {
+            if (brow >= own_lo && brow < own_lo + sa.shard) {
+              bmap = &tmOwn;
+              brow_map = brow - own_lo;
+            } else {
+              const int owner = brow / sa.shard;
+              if (owner < sa.world && !(ready >> owner & 1u)) {
+                stage_wait(sa.flags + owner, sa.expect, p.err);
+                ready |= 1u << owner;
+              }
+            }
+          }
+        }
+        for (int i = 0; i < kblocks; ++i) {
           const int s = g % S;
           if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, kErrWaitEmpty)) {
             alive = false;
             break;
           }
+          int kb = i + kb_rot;
+          if (kb >= kblocks) kb -= kblocks;
+          const int kc = kb * BK;
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::kTileA + C::kTileB));
           const uint32_t bar = map_shared_rank(smem_u32(&full[s]), 0);
-          tma_load_3d_pair(sA + s * C::kTileA, &tmA, bar, kb * BK, c.m0 + 128 * (int)rank, c.za);
-          tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kb * BK, c.n0 + 128 * (int)rank, c.zb);
+          tma_load_3d_pair(sA + s * C::kTileA, &tmA, bar, kc, c.m0 + 128 * (int)rank, c.za);
+          if constexpr (kStaged) {
+            if (sa.mode == 0) {
+              tma_load_3d_pair(sB + s * C::kTileB, bmap, bar, kc, brow_map, 0);  // rows past N: zero fill
+            } else if (kc >= own_lo && kc < own_lo + sa.shard) {
+              tma_load_3d_pair(sB + s * C::kTileB, &tmOwn, bar, kc - own_lo, brow, 0);
+            } else {
+              const int owner = kc / sa.shard;
+              if (!(ready >> owner & 1u)) {
+                stage_wait(sa.flags + owner, sa.expect, p.err);
+                ready |= 1u << owner;
+              }
+              tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kc, brow, 0);
+            }
+          } else {
+            tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kc, brow, c.zb);
+          }
           ++g;
         }
       }
@@ -865,6 +925,41 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else {
     // ---- epilogue (both CTAs; warps 0-3 drain this CTA's 128 accumulator rows) ----
+    if constexpr (kStaged) {
+      // First the staging copy: pieces of the remote shards, spread over every CTA.
+      const int pieces = sa.pieces_per_owner;
+      const int all = pieces * sa.world;
+      const int et = threadIdx.x;  // 0..127
+      for (int t = blockIdx.x; t < all; t += gridDim.x) {
+        const int owner = t / pieces, piece = t - owner * pieces;
+        if (owner == sa.self) continue;
+        const int r0 = piece * sa.piece_rows;
+        const int r1 = min(sa.src_rows, r0 + sa.piece_rows);
+        const unsigned vec_per_row = (unsigned)(sa.row_elems / 8);
+        const unsigned nvec = (unsigned)(r1 - r0) * vec_per_row;  // one piece: far below 2^32
+        const uint4* src = reinterpret_cast<const uint4*>(sa.src[owner]) + (long long)r0 * (sa.src_stride / 8);
+        uint4* dst = reinterpret_cast<uint4*>(sa.dst) +
+                     ((sa.dst_row0[owner] + r0) * sa.dst_stride + sa.dst_col0[owner]) / 8;
+        const long long sstride = sa.src_stride / 8, dstride = sa.dst_stride / 8;
+        for (unsigned v0 = et; v0 < nvec; v0 += 4 * 128) {
+          uint4 x[4];
+          unsigned rr[4], cc[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const unsigned v = v0 + u * 128;
+            rr[u] = v / vec_per_row;
+            cc[u] = v - rr[u] * vec_per_row;
+            if (v < nvec) x[u] = src[rr[u] * sstride + cc[u]];
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (v0 + u * 128 < nvec) dst[rr[u] * dstride + cc[u]] = x[u];
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
+        if (et == 0) atomicAdd(sa.flags + owner, 1);
+      }
+    }
     float* twp = tw + warp * (32 * 33);
     int it = 0;
     for (int tile = pair; tile < total; tile += pairs, ++it) {
@@ -1052,7 +1147,8 @@ int pair_clusters() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (count[dev & 63] == 0) {
-    cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmem);
+    cudaFuncSetAttribute(gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmem);
+    cudaFuncSetAttribute(gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmem);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * 74, 1, 1);
     cfg.blockDim = dim3(kPThreads, 1, 1);
@@ -1065,7 +1161,7 @@ int pair_clusters() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<false>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = -1;  // clusters unavailable: callers fall back to the single-SM kernel
     }
@@ -1094,7 +1190,43 @@ bool launch_pair(const GemmOperand& A, const GemmOperand& B, const GemmParams& p
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, p, ts);
+  StageArgs none{};
+  cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, p, ts, tb, none);
+  return true;
+}
+
+// The staged (all-gather fused) GEMM on CTA pairs; false if it cannot run here.
+bool launch_pair_staged(const GemmOperand& A, const GemmOperand& stage_op, const GemmOperand& own, GemmParams p,
+                        StageArgs sa, cudaStream_t stream) {
+  const int clusters = pair_clusters();
+  if (clusters <= 0) return false;
+  TileSched ts{};
+  ts.tiles_n = (p.N + 255) / 256;
+  ts.tiles_m = (p.M + 255) / 256;
+  ts.batch = 1;
+  // mode 0: own columns first and column-major tile order, so the first wave of tiles needs
+  // no remote rows at all and the copies run under it
+  ts.n_rot = sa.mode == 0 ? (sa.self * sa.shard / 256) % ts.tiles_n : 0;
+  ts.n_major = sa.mode == 0 ? 1 : 0;
+  const long long tiles = (long long)ts.tiles_n * ts.tiles_m;
+  const int n_clusters = (int)std::min<long long>(tiles, clusters);
+  sa.copiers = 2 * n_clusters;
+  CUtensorMap ta = make_tmap_kmajor_bf16(A, 128);
+  CUtensorMap tb = make_tmap_kmajor_bf16(stage_op, 128);
+  CUtensorMap to = make_tmap_kmajor_bf16(own, 128);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * (unsigned)n_clusters, 1, 1);
+  cfg.blockDim = dim3(kPThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemm_pair_kernel<true>, ta, tb, p, ts, to, sa);
   return true;
 }
 
@@ -1150,6 +1282,10 @@ void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const
                         StageArgs sa, int bn, cudaStream_t stream) {
   p.splits = 1;
   p.batch = 1;
+  // CTA pairs when the 128-row B halves never straddle two owners' shards.
+  if (p.N > 128 && (sa.mode == 0 ? sa.shard % 128 == 0 : sa.shard % BK == 0) &&
+      launch_pair_staged(A, stage_op, own, p, sa, stream))
+    return;
   const int ctas = ((p.N + bn - 1) / bn) * ((p.M + BM - 1) / BM);
   sa.copiers = ctas < 148 ? ctas : 148;
   switch (bn) {
@@ -1221,7 +1357,10 @@ void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, in
   // More than one wave of tiles without split-K: the persistent kernel (epilogue of one tile
   // overlapped with the MMAs of the next).
   const long long tiles = (long long)((p.N + bn - 1) / bn) * ((p.M + BM - 1) / BM) * p.batch;
-  if (p.splits == 1 && bn == 256 && p.K > 0 && tiles > sm_count()) {
+  // Few tiles over a long K go to the 2-CTA cluster split-K form of the per-tile kernel (see
+  // launch_bn); every other wide (N > 128) problem runs on CTA pairs.
+  const bool skinny = tiles * 2 <= 160 && (p.K + BK - 1) / BK >= 8;
+  if (p.splits == 1 && bn == 256 && p.K > 0 && !skinny) {
     TileSched ts{};
     ts.tiles_n = (p.N + 255) / 256;
     ts.tiles_m = (p.M + 255) / 256;

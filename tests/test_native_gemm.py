@@ -222,3 +222,30 @@ def test_persistent_gemm_many_tiles(mode, z, m, n, k):
     tol = 2e-2 if mode in ("bf16", "bf16t") else 1e-3
     torch.testing.assert_close(got, want, rtol=tol, atol=tol * float(want.abs().max()))
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize(("world", "self_rank", "m", "n", "k"), [(4, 1, 1000, 1024, 512), (2, 0, 640, 384, 384),
+                                                                 (3, 2, 512, 384, 192)])
+def test_staged_allgather_gemm_emulated(mode, world, self_rank, m, n, k):
+    """All-gather fused into the GEMM, ranks emulated by separate allocations on one GPU:
+    mode 0 shards B's rows, mode 1 its K columns; the launch copies the other ranks'
+    shards into the staging matrix while its own-shard tiles start."""
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    b = torch.randn(n, k, device="cuda").bfloat16()
+    if mode == 0:
+        shards = [s.contiguous() for s in b.chunk(world, 0)]
+    else:
+        shards = [s.contiguous() for s in b.chunk(world, 1)]
+    if any(s.shape != shards[0].shape for s in shards):
+        pytest.skip("uneven shards")
+    stage = torch.empty(n, k, device="cuda", dtype=torch.bfloat16)
+    flags = torch.zeros(world, dtype=torch.int32, device="cuda")
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    err = ops.error_word(torch.device("cuda", torch.cuda.current_device()))
+    want = a.float() @ b.float().T
+    for epoch in (1, 2):  # the flags keep counting across launches
+        out.fill_(float("nan"))
+        ops.native().gemm_tn_staged(a, shards, stage, out, flags, epoch, mode, self_rank, ops.STORE_BF16, 1.0, err)
+        torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2 * float(want.abs().max()))
+    ops.check_device_errors()
