@@ -67,6 +67,8 @@ void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t s
   auto b = operand(B, "B");
   TORCH_CHECK(a.cols == b.cols, "A and B disagree on K");
   check_cuda(C, "C");
+  TORCH_CHECK(mode == bw::kStoreF32 || mode == bw::kStoreBF16 || mode == bw::kAtomicF32 || mode == bw::kStoreBF16T,
+              "mode: fp32, bf16, fp32 atomic or transposed bf16 store");
   const bool bf16_out = mode == bw::kStoreBF16 || mode == bw::kStoreBF16T;
   TORCH_CHECK(C.scalar_type() == (bf16_out ? torch::kBFloat16 : torch::kFloat32),
               "C dtype does not match the store mode");
@@ -359,39 +361,6 @@ void peer_barrier(Tensor flag_ptrs, int64_t rank, int64_t world, int64_t epoch, 
   TORCH_CHECK(world >= 1 && world <= 1024 && rank >= 0 && rank < world, "bad rank / world");
   bw::peer_barrier(reinterpret_cast<int* const*>(flag_ptrs.data_ptr<int64_t>()), (int)rank, (int)world,
                    (int)epoch, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
-}
-
-// Cross-rank reduce fused into the GEMM epilogue: every element of alpha * A @ B^T is added
-// with fp32 atomics into its owner rank's copy of C (owner = float4 index / per4), through
-// peer pointers.  C is (M, N) fp32 with row stride ldc on every rank.
-void gemm_tn_peer(Tensor A, Tensor B, Tensor peer_ptrs, int64_t world, int64_t per4, int64_t M, int64_t N,
-                  int64_t ldc, double alpha, int64_t splits, Tensor err, int64_t self_rank) {
-  const c10::cuda::CUDAGuard guard(A.device());
-  check_err(err);
-  auto a = operand(A, "A");
-  auto b = operand(B, "B");
-  TORCH_CHECK(a.batch == 1 && b.batch == 1 && a.cols == b.cols, "2-D operands with one K");
-  TORCH_CHECK(a.rows == M && b.rows == N, "M / N disagree with the operands");
-  TORCH_CHECK(peer_ptrs.is_cuda() && peer_ptrs.scalar_type() == torch::kInt64 && peer_ptrs.numel() == world,
-              "peer_ptrs: one device address per rank");
-  TORCH_CHECK(per4 > 0 && world >= 1, "bad partition");
-  bw::GemmParams p{};
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)a.cols;
-  p.batch = 1;
-  p.splits = (int)std::max<int64_t>(1, splits);
-  p.b_shared = 1;
-  p.c_mode = bw::kPeerAtomicF32;
-  p.alpha = (float)alpha;
-  p.ldc = ldc;
-  p.peers = reinterpret_cast<float* const*>(peer_ptrs.data_ptr<int64_t>());
-  p.world = (int)world;
-  p.per4 = per4;
-  p.self_rank = (int)self_rank;
-  p.err = err.data_ptr<int>();
-  if (M == 0 || N == 0) return;
-  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
 // GEMM -> reduce-scatter in one launch: every element of alpha * A @ B^T is stored (16-byte
@@ -708,39 +677,6 @@ void moe_combine_bwd_dispatch(Tensor dy, Tensor slots, Tensor w, Tensor dw, Tens
   bw::moe_combine_bwd_dispatch(dy.data_ptr(), slots.data_ptr(), w.data_ptr<float>(), dw.data_ptr<float>(),
                                dst_rank.data_ptr<int>(), dst_row.data_ptr<int>(), pr.data(), pm.data(), world, (int)rows,
                                (int)k, (int)dy.size(1), (int)self, at::cuda::getCurrentCUDAStream());
-}
-
-// C rows returned to their sources: out row m = alpha * (A @ B^T)[m] is stored into rank
-// scatter[m][0]'s buffer peer_C[...] at row scatter[m][1] (bf16, row length N).
-void gemm_tn_scatter(Tensor A, Tensor B, std::vector<Tensor> peer_C, Tensor scatter, double alpha, Tensor err) {
-  const c10::cuda::CUDAGuard guard(A.device());
-  check_err(err);
-  auto a = operand(A, "A");
-  auto b = operand(B, "B");
-  TORCH_CHECK(a.batch == 1 && b.batch == 1 && a.cols == b.cols, "2-D operands with one K");
-  TORCH_CHECK(scatter.is_cuda() && scatter.scalar_type() == torch::kInt32 && scatter.is_contiguous() &&
-                  scatter.numel() >= 2 * a.rows, "scatter: int32 (M, 2)");
-  for (auto& c : peer_C)
-    TORCH_CHECK(c.scalar_type() == torch::kBFloat16 && c.is_contiguous() && c.size(-1) == b.rows &&
-                    reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
-                "peer outputs must be contiguous (R, N) bf16");
-  Tensor ptrs = device_ptr_table(peer_C, A.device());
-  bw::GemmParams p{};
-  p.M = (int)a.rows;
-  p.N = (int)b.rows;
-  p.K = (int)a.cols;
-  p.batch = 1;
-  p.splits = 1;
-  p.b_shared = 1;
-  p.c_mode = bw::kStoreBF16Scatter;
-  p.alpha = (float)alpha;
-  p.ldc = b.rows;
-  p.peers = reinterpret_cast<float* const*>(ptrs.data_ptr<int64_t>());
-  p.world = (int)peer_C.size();
-  p.scatter = reinterpret_cast<const int2*>(scatter.data_ptr<int>());
-  p.err = err.data_ptr<int>();
-  if (p.M == 0 || p.N == 0) return;
-  bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
 // Per-sample LayerNorm / RMSNorm parameter gradients from the raw input x (B, T, d) and the
@@ -1094,9 +1030,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_split", &swiglu_split);
   m.def("swiglu_split_bwd", &swiglu_split_bwd);
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
-  m.def("gemm_tn_scatter", &gemm_tn_scatter, "A @ B^T with each output row stored back to its source rank");
-  m.def("gemm_tn_peer", &gemm_tn_peer, "A @ B^T reduced across ranks by peer atomics in the epilogue");
-  m.def("moe_count", &moe_count, "MoE routing histogram");
   m.def("moe_place", &moe_place, "MoE receive layout and owner-side ragged GEMM tables");
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");

@@ -179,41 +179,6 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
         }
       }
     }
-  } else if (p.c_mode == kPeerAtomicF32 && c0 + 32 <= BN && nbase + 32 <= p.N &&
-      (((long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase) & 3) == 0) {
-    // A float4 never straddles two owners (ownership is assigned in whole float4 units).
-    // 16-byte vector atomics go to this rank's own slice only; other owners get scalar
-    // fp32 atomics, the form peer (NVLink) atomics are known to support.
-    const long long i0 = (long long)zc * p.batch_stride_c + (long long)row * p.ldc + nbase;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const long long i = i0 + 4 * q;
-      int owner = (int)((i >> 2) / p.per4);
-      owner = owner < p.world ? owner : p.world - 1;
-      float* dst = p.peers[owner] + i;
-      const float v0 = alpha * __uint_as_float(r[4 * q]), v1 = alpha * __uint_as_float(r[4 * q + 1]);
-      const float v2 = alpha * __uint_as_float(r[4 * q + 2]), v3 = alpha * __uint_as_float(r[4 * q + 3]);
-      if (owner == p.self_rank) {
-        atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v0, v1, v2, v3));
-      } else {
-        atomicAdd(dst, v0);
-        atomicAdd(dst + 1, v1);
-        atomicAdd(dst + 2, v2);
-        atomicAdd(dst + 3, v3);
-      }
-    }
-  } else if (p.c_mode == kPeerAtomicF32) {
-    const long long rowoff = (long long)zc * p.batch_stride_c + (long long)row * p.ldc;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = nbase + j;
-      if (j < BN - c0 && n < p.N) {
-        const long long i = rowoff + n;
-        int owner = (int)((i >> 2) / p.per4);
-        owner = owner < p.world ? owner : p.world - 1;
-        atomicAdd(p.peers[owner] + i, alpha * __uint_as_float(r[j]));
-      }
-    }
   } else if ((p.c_mode == kStoreF32 || p.c_mode == kAtomicF32) && c0 + 32 <= BN && nbase + 32 <= p.N &&
              ((reinterpret_cast<uintptr_t>(static_cast<float*>(Cbase) + (long long)zc * p.batch_stride_c +
                                            (long long)row * p.ldc + nbase) & 15) == 0)) {
@@ -1054,7 +1019,7 @@ void launch_bn(const GemmOperand& A, const GemmOperand& B, const GemmParams& p,
   const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM) * p.batch;
   const int kblocks = (p.K + BK - 1) / BK;
   q.cluster_k = 1;
-  if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 && p.c_mode != kPeerAtomicF32 &&
+  if (C::kClusterOK && p.splits == 1 && p.c_mode != kAtomicF32 &&
       p.c_mode != kStoreBF16Scatter &&
       tiles * 2 <= 160 && kblocks >= 8) {
     q.cluster_k = 2;

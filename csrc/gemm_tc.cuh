@@ -14,8 +14,7 @@ enum GemmStore : int {
   kStoreBF16T = 3,  // C^T (bf16): element (m, n) lands at C[z][n * ldc + m]
   kStoreBF16TB = 4, // per-segment C^T (bf16): rows are (s, t) with T = ldc rows per segment;
                     // element (m, n) lands at C[z][m / T][n][m % T] (a (S, N, T) block)
-  kPeerAtomicF32 = 5,  // fp32 atomics into the OWNER rank's copy of C over NVLink: element
-                       // i = m * ldc + n goes to peers[(i / 4) / per4][i] (cross-rank reduce)
+  // 5: unused (an earlier peer-atomic reduce; replaced by kPeerSlotF32)
   kStoreBF16Scatter = 6,  // bf16 row m stored into rank scatter[m].x's C at row scatter[m].y
                           // (peer pointers; expert outputs returned to their source ranks)
   kPeerSlotF32 = 7,  // reduce-scatter: element i (owner o = (i / 4) / per4) is STORED into
@@ -46,10 +45,10 @@ struct GemmParams {
   long long batch_stride_c;
   int* err;
   int cluster_k;   // >1: the split-K CTAs of a tile form a cluster and sum over DSMEM (set by the launcher)
-  float* const* peers;  // kPeerAtomicF32: device array of every rank's C (peer-mapped)
+  float* const* peers;  // kPeerSlotF32 / kStoreBF16Scatter: device array of every rank's buffer (peer-mapped)
   int world;
-  long long per4;       // kPeerAtomicF32: float4 elements owned by each rank
-  int self_rank;        // kPeerAtomicF32: this rank (its own slice takes vector atomics)
+  long long per4;       // kPeerSlotF32: float4 elements owned by each rank
+  int self_rank;        // kPeerSlotF32: this rank (selects its slot in the owners' buffers)
   const int2* scatter;  // kStoreBF16Scatter: (rank, row) of every output row
 };
 
