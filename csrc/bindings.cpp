@@ -807,7 +807,7 @@ void allreduce_phase(std::vector<Tensor> peers, Tensor out, int64_t n, int64_t p
 
 // out[i][j] += sum over token pairs of (a1 . a2)(g1 . g2); factors flattened to rows.
 void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t S2, Tensor out,
-                Tensor err) {
+                Tensor err, bool diag_only) {
   const c10::cuda::CUDAGuard guard(a1.device());
   check_err(err);
   auto oa1 = operand(a1, "a1");
@@ -833,9 +833,45 @@ void ghost_gram(Tensor a1, Tensor g1, Tensor a2, Tensor g2, int64_t S1, int64_t 
   TORCH_CHECK(out.size(0) == p.B1 && out.size(1) == p.B2, "out must be (B1, B2)");
   p.out = out.data_ptr<float>();
   p.ldo = out.stride(0);
+  p.diag_only = diag_only ? 1 : 0;
   p.err = err.data_ptr<int>();
   if (p.M == 0 || p.N == 0) return;
   bw::ghost_gram_launch(oa1, oa2, og1, og2, p, at::cuda::getCurrentCUDAStream());
+}
+
+// Embedding-layer cross-gram: out[i][j] += sum over token pairs with equal ids of g1 . g2
+// (tok: flattened int64 ids of B*S rows; g: (B*S, E) bf16).
+void ghost_gram_tokens(Tensor tok1, Tensor g1, Tensor tok2, Tensor g2, int64_t S1, int64_t S2, Tensor out,
+                       Tensor err, bool diag_only) {
+  const c10::cuda::CUDAGuard guard(g1.device());
+  check_err(err);
+  auto og1 = operand(g1, "g1");
+  auto og2 = operand(g2, "g2");
+  TORCH_CHECK(g1.dim() == 2 && g2.dim() == 2 && og1.cols == og2.cols, "g1 / g2: (rows, E) with one E");
+  for (auto* t : {&tok1, &tok2})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt64 && t->is_contiguous(), "token ids: int64 CUDA");
+  TORCH_CHECK(tok1.numel() == og1.rows && tok2.numel() == og2.rows, "one token id per gradient row");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.dim() == 2 && out.stride(1) == 1, "out: (B1, B2) fp32");
+  bw::GhostParams p{};
+  p.M = (int)og1.rows;
+  p.N = (int)og2.rows;
+  p.K = 0;
+  p.D = (int)og1.cols;
+  p.S1 = (int)S1;
+  p.S2 = (int)S2;
+  p.B1 = (int)(p.M / p.S1);
+  p.B2 = (int)(p.N / p.S2);
+  TORCH_CHECK(p.B1 * p.S1 == p.M && p.B2 * p.S2 == p.N, "rows must be B*S");
+  TORCH_CHECK(out.size(0) == p.B1 && out.size(1) == p.B2, "out must be (B1, B2)");
+  p.out = out.data_ptr<float>();
+  p.ldo = out.stride(0);
+  p.err = err.data_ptr<int>();
+  p.tok1 = reinterpret_cast<const long long*>(tok1.data_ptr<int64_t>());
+  p.tok2 = reinterpret_cast<const long long*>(tok2.data_ptr<int64_t>());
+  p.diag_only = diag_only ? 1 : 0;
+  if (p.M == 0 || p.N == 0) return;
+  // the activation maps are unused in token mode; the gradient operands stand in for them
+  bw::ghost_gram_launch(og1, og2, og1, og2, p, at::cuda::getCurrentCUDAStream());
 }
 
 __nv_bfloat16* bf(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
@@ -1018,7 +1054,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
   m.def("gemm_tn_seg", &gemm_tn_seg, "A @ B^T stored per segment as (S, N, T) bf16");
   m.def("gemm_grouped", &gemm_grouped, "one launch for many same-shaped batched A @ B^T problems");
-  m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients");
+  m.def("ghost_gram_tokens", &ghost_gram_tokens, "embedding-layer cross-gram: gradient Gram masked by token equality",
+        py::arg("tok1"), py::arg("g1"), py::arg("tok2"), py::arg("g2"), py::arg("S1"), py::arg("S2"), py::arg("out"),
+        py::arg("err"), py::arg("diag_only") = false);
+  m.def("ghost_gram", &ghost_gram, "fused factorized cross-gram of per-sample gradients", py::arg("a1"), py::arg("g1"),
+        py::arg("a2"), py::arg("g2"), py::arg("S1"), py::arg("S2"), py::arg("out"), py::arg("err"),
+        py::arg("diag_only") = false);
   m.def("ag_score", &ag_score, "fused NVLink all-gather of peer train blocks + score GEMM");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier on peer-mapped flags (bounded wait)");
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");

@@ -13,6 +13,10 @@
 // first along its row within each column segment, then across the lanes of a
 // warp when they share a sample, into shared-memory bins, finally one global
 // fp32 atomic per (i, j) bin.  The (B1 S1) x (B2 S2) products never reach HBM.
+//
+// Embedding layers (token ids given): the activations are one-hot token ids, so
+// Ka[r][c] = [tok1[r] == tok2[c]]; only the gradient Gram runs on the tensor cores and the
+// epilogue masks it by token equality -- no vocab-sized buffer, no (B1 S1) x (B2 S2) mask.
 #include "ghost_gram.cuh"
 #include "tc_common.cuh"
 
@@ -45,7 +49,13 @@ __global__ void __launch_bounds__(128, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
   const int m0 = blockIdx.y * BM;
-  const int nka = (p.K + BK - 1) / BK;
+  if (p.diag_only) {  // uniform over the CTA, before any setup
+    const int ia = m0 / p.S1, ib = (min(m0 + BM, p.M) - 1) / p.S1;
+    const int ja = n0 / p.S2, jb = (min(n0 + BN, p.N) - 1) / p.S2;
+    if (jb < ia || ja > ib) return;
+  }
+  const bool tok = p.tok1 != nullptr;
+  const int nka = tok ? 0 : (p.K + BK - 1) / BK;
   const int nkg = (p.D + BK - 1) / BK;
   const int nk = nka + nkg;
 
@@ -118,16 +128,19 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   const int my_i = row / p.S1;
   const bool row_ok = ok && row < p.M;
+  const long long my_tok = (tok && row < p.M) ? p.tok1[row] : -1;
   const bool warp_uniform_i = __all_sync(0xffffffffu, (m0 + warp * 32) / p.S1 == my_i) &&
                               __all_sync(0xffffffffu, row < p.M);
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
     uint32_t ra[32], rg[32];
-    tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, ra);
+    if (!tok) tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, ra);
     tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + 128u + (uint32_t)c0, rg);
     tmem_ld_wait();
     const int cbase = n0 + c0;
     if (cbase >= p.N) continue;  // warp-uniform
+    // token mode: lane l holds column (cbase + l)'s id; column cc's id is shuffled from lane cc
+    const long long col_tok = (tok && cbase + lane < p.N) ? p.tok2[cbase + lane] : -2;
     // Walk the 32 columns (static register indexing); a column-sample boundary is
     // warp-uniform, so each segment is flushed by the whole warp together.
     auto flush = [&](float v, int j) {
@@ -137,7 +150,7 @@ __global__ void __launch_bounds__(128, 1)
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         if (lane != 0) return;
       }
-      if (!row_ok || my_i >= p.B1 || j >= p.B2) return;
+      if (!row_ok || my_i >= p.B1 || j >= p.B2 || (p.diag_only && j != my_i)) return;
       if (use_bins)
         atomicAdd(&bins[(my_i - i_first) * nj + (j - j_first)], v);
       else
@@ -154,7 +167,12 @@ __global__ void __launch_bounds__(128, 1)
         ++cur_j;
         next_b += p.S2;
       }
-      v += __uint_as_float(ra[cc]) * __uint_as_float(rg[cc]);
+      if (tok) {
+        const long long t2 = __shfl_sync(0xffffffffu, col_tok, cc);
+        if (t2 == my_tok) v += __uint_as_float(rg[cc]);
+      } else {
+        v += __uint_as_float(ra[cc]) * __uint_as_float(rg[cc]);
+      }
     }
     flush(v, cur_j);
   }

@@ -51,6 +51,13 @@ def _embedding_gram(tok1, g1, tok2, g2, per_token: bool = False) -> torch.Tensor
     b1, t1 = tok1.shape
     b2, t2 = tok2.shape
     e = g1.shape[-1]
+    if _native(g1, g2) and tok1.is_cuda and tok2.is_cuda:
+        from dattri_llm_b200 import ops as native_ops
+
+        if per_token:  # every side-1 token is its own "sample"
+            k = native_ops.ghost_gram_tokens(tok1.reshape(-1, 1), g1.reshape(b1 * t1, 1, e), tok2, g2)
+            return k.view(b1, t1, b2).to(g1.dtype)
+        return native_ops.ghost_gram_tokens(tok1, g1, tok2, g2).to(g1.dtype)
     out = torch.zeros((b1, t1, b2) if per_token else (b1, b2), dtype=g1.dtype, device=g1.device)
     flat1, gf1 = tok1.reshape(-1), g1.reshape(-1, e)
     step = max(1, _EMB_CHUNK_ELEMS // max(1, b1 * t1 * t2))
@@ -184,6 +191,10 @@ def dot_factors(a1, g1, a2, g2, layer_type, module_kwargs1=None, module_kwargs2=
     a1, g1 = preprocess_factors(a1, g1, layer_type, module_kwargs1, include_bias)
     a2, g2 = preprocess_factors(a2, g2, layer_type, module_kwargs2, include_bias)
     if is_embedding(layer_type):
+        if _native(g1, g2) and a1.is_cuda and a2.is_cuda:
+            from dattri_llm_b200 import ops as native_ops
+
+            return native_ops.ghost_gram_tokens(a1, g1, a2, g2, diag_only=True).diagonal().to(g1.dtype)
         return torch.stack([
             _embedding_gram(a1[i : i + 1], g1[i : i + 1], a2[i : i + 1], g2[i : i + 1])[0, 0]
             for i in range(a1.shape[0])
@@ -196,6 +207,10 @@ def dot_factors(a1, g1, a2, g2, layer_type, module_kwargs1=None, module_kwargs2=
         ka = torch.einsum("btgd,bsgd->bgts", a1, a2)
         kg = torch.einsum("btge,bsge->bgts", g1, g2)
         return (ka * kg).sum((1, 2, 3))
+    if _native(a1, g1, a2, g2):
+        from dattri_llm_b200 import ops as native_ops
+
+        return native_ops.ghost_dot(a1, g1, a2, g2).to(a1.dtype)
     ka = torch.einsum("btd,bsd->bts", a1, a2)
     kg = torch.einsum("bte,bse->bts", g1, g2)
     return (ka * kg).sum((1, 2))
@@ -206,6 +221,10 @@ def grad_norm_sq_factors(a, g, layer_type, module_kwargs=None, include_bias: boo
     """``(B,)`` per-sample squared Frobenius norms of the weight gradients."""
     a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
     if is_embedding(layer_type):
+        if _native(g) and a.is_cuda:
+            from dattri_llm_b200 import ops as native_ops
+
+            return native_ops.ghost_gram_tokens(a, g, a, g, diag_only=True).diagonal().to(g.dtype)
         return torch.stack([
             _embedding_gram(a[i : i + 1], g[i : i + 1], a[i : i + 1], g[i : i + 1])[0, 0]
             for i in range(a.shape[0])
@@ -232,6 +251,10 @@ def grad_norm_sq_factors(a, g, layer_type, module_kwargs=None, include_bias: boo
             return (m * m).sum(-1).to(a.dtype)
         m = torch.einsum("btk,btd->bkd", a, g).flatten(1)
         return (m * m).sum(-1)
+    if _native(a, g):
+        from dattri_llm_b200 import ops as native_ops
+
+        return native_ops.ghost_dot(a, g, a, g).to(a.dtype)
     ka = torch.einsum("btk,bsk->bts", a, a)
     kg = torch.einsum("btd,bsd->bts", g, g)
     return (ka * kg).sum((1, 2))

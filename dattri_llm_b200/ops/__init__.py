@@ -128,7 +128,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     gemm_tn_seg,
     matmul_tn,
 )
-from dattri_llm_b200.ops.gram import ghost_gram, per_sample_outer  # noqa: E402
+from dattri_llm_b200.ops.gram import ghost_dot, ghost_gram, ghost_gram_tokens, per_sample_outer  # noqa: E402
 from dattri_llm_b200.ops.norm import norm_per_sample_grad  # noqa: E402
 from dattri_llm_b200.ops.optim import adam_direction  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
@@ -147,7 +147,9 @@ __all__ = [
     "gemm_tn",
     "gemm_tn_seg",
     "launch_count",
+    "ghost_dot",
     "ghost_gram",
+    "ghost_gram_tokens",
     "matmul_tn",
     "native",
     "norm_per_sample_grad",

@@ -33,9 +33,12 @@ def per_sample_outer(
     return out
 
 
-def ghost_gram(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.Tensor) -> torch.Tensor:
+def ghost_gram(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.Tensor, *,
+               diag_only: bool = False) -> torch.Tensor:
     """Fused factorized cross-gram ``(B1, B2)`` (fp32) of 3-D bf16 factors
-    ``a (B, S, K)``, ``g (B, S, D)``; the token-pair products stay on chip."""
+    ``a (B, S, K)``, ``g (B, S, D)``; the token-pair products stay on chip.  With
+    *diag_only* (``B1 == B2``) only the ``i == j`` entries are computed (the rest stay 0):
+    per-sample dots / squared norms without the cross terms' work."""
     from dattri_llm_b200.ops import count_launch, error_word, native
 
     count_launch()
@@ -51,5 +54,39 @@ def ghost_gram(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.T
             x = torch.nn.functional.pad(x, (0, 8 - x.shape[-1] % 8))
         return x.contiguous().bfloat16()
 
-    native().ghost_gram(flat(a1), flat(g1), flat(a2), flat(g2), s1, s2, out, error_word(a1.device))
+    native().ghost_gram(flat(a1), flat(g1), flat(a2), flat(g2), s1, s2, out, error_word(a1.device), diag_only)
+    return out
+
+
+def ghost_dot(a1: torch.Tensor, g1: torch.Tensor, a2: torch.Tensor, g2: torch.Tensor) -> torch.Tensor:
+    """``(B,)`` per-sample ``<dW1_i, dW2_i>`` of factorized gradients (``a2 is a1`` and
+    ``g2 is g1`` give squared norms) in one fused launch: the diagonal sample blocks of the
+    token-pair Gram only.  Reference: ``dattri_llm/gradient/ops/dot.py:307-411``."""
+    return ghost_gram(a1, g1, a2, g2, diag_only=True).diagonal().clone()
+
+
+def ghost_gram_tokens(tok1: torch.Tensor, g1: torch.Tensor, tok2: torch.Tensor, g2: torch.Tensor, *,
+                      diag_only: bool = False) -> torch.Tensor:
+    """Embedding-layer cross-gram ``(B1, B2)`` (fp32):
+    ``K[i, j] = sum_{t, s} [tok1_it == tok2_js] <g1_it, g2_js>`` for token ids ``(B, S)``
+    and output gradients ``(B, S, E)``.  One tcgen05 Gram of the gradients whose epilogue
+    applies the token-equality mask and reduces per sample pair (no vocab-sized buffer and
+    no token-pair matrix in HBM).  Reference: ``dattri_llm/gradient/ops/dot.py:58-74``."""
+    from dattri_llm_b200.ops import count_launch, error_word, native
+
+    count_launch()
+    b1, s1 = tok1.shape
+    b2, s2 = tok2.shape
+    out = torch.zeros(b1, b2, dtype=torch.float32, device=g1.device)
+    if b1 == 0 or b2 == 0 or s1 == 0 or s2 == 0:
+        return out
+
+    def flat(x):
+        x = x.reshape(-1, x.shape[-1])
+        if x.shape[-1] % 8:
+            x = torch.nn.functional.pad(x, (0, 8 - x.shape[-1] % 8))
+        return x.contiguous().bfloat16()
+
+    native().ghost_gram_tokens(tok1.reshape(-1).long().contiguous(), flat(g1), tok2.reshape(-1).long().contiguous(),
+                               flat(g2), s1, s2, out, error_word(g1.device), diag_only)
     return out

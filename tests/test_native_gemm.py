@@ -249,3 +249,51 @@ def test_staged_allgather_gemm_emulated(mode, world, self_rank, m, n, k):
         ops.native().gemm_tn_staged(a, shards, stage, out, flags, epoch, mode, self_rank, ops.STORE_BF16, 1.0, err)
         torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2 * float(want.abs().max()))
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("b1", "s1", "b2", "s2", "e", "vocab"), [(3, 100, 5, 37, 64, 50), (8, 256, 4, 256, 200, 1000)])
+def test_embedding_token_gram_matches_dense(b1, s1, b2, s2, e, vocab):
+    """Embedding cross-gram: gradient Gram masked by token equality, per sample pair and per
+    side-1 token, against the fp32 one-hot formula."""
+    from dattri_llm_b200.gradient.ops.dot import _embedding_gram
+
+    tok1 = torch.randint(0, vocab, (b1, s1), device="cuda")
+    tok2 = torch.randint(0, vocab, (b2, s2), device="cuda")
+    g1 = torch.randn(b1, s1, e, device="cuda").bfloat16()
+    g2 = torch.randn(b2, s2, e, device="cuda").bfloat16()
+    match = (tok1.reshape(-1, 1) == tok2.reshape(1, -1)).float()
+    prod = (g1.float().reshape(-1, e) @ g2.float().reshape(-1, e).T) * match
+    want_tok = prod.view(b1, s1, b2, s2).sum(3)
+    got = ops.ghost_gram_tokens(tok1, g1, tok2, g2)
+    torch.testing.assert_close(got, want_tok.sum(1), rtol=1e-3, atol=1e-2)
+    got_tok = _embedding_gram(tok1, g1, tok2, g2, per_token=True).float()
+    torch.testing.assert_close(got_tok, want_tok, rtol=2e-2, atol=2e-1)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("b", "s", "k", "d"), [(6, 100, 64, 96), (4, 300, 128, 64)])
+def test_fused_per_sample_dot_and_norm(b, s, k, d):
+    """Per-sample <dW1_i, dW2_i> and ||dW_i||^2 from factors: the diagonal sample blocks of
+    the fused ghost gram only (linear and embedding layers) against fp32 materialized grads."""
+    from dattri_llm_b200.gradient.ops.dot import dot_factors, grad_norm_sq_factors
+
+    a1, g1 = torch.randn(b, s, k, device="cuda").bfloat16(), torch.randn(b, s, d, device="cuda").bfloat16()
+    a2, g2 = torch.randn(b, s, k, device="cuda").bfloat16(), torch.randn(b, s, d, device="cuda").bfloat16()
+    w1 = torch.einsum("btd,btk->bdk", g1.float(), a1.float())
+    w2 = torch.einsum("btd,btk->bdk", g2.float(), a2.float())
+    want_dot = (w1 * w2).sum((1, 2))
+    want_norm = (w1 * w1).sum((1, 2))
+    got_dot = ops.ghost_dot(a1, g1, a2, g2)
+    torch.testing.assert_close(got_dot, want_dot, rtol=1e-2, atol=1e-2 * float(want_norm.max()))
+    got_norm = grad_norm_sq_factors(a1, g1, "nn.Linear", include_bias=False, mode="factorized").float()
+    torch.testing.assert_close(got_norm, want_norm, rtol=2e-2, atol=0)
+    tok = torch.randint(0, 40, (b, s), device="cuda")
+    onehot = torch.nn.functional.one_hot(tok, 40).float()
+    we = torch.einsum("btd,btv->bvd", g1.float(), onehot)
+    got_emb = grad_norm_sq_factors(tok, g1, "nn.Embedding", include_bias=False).float()
+    torch.testing.assert_close(got_emb, (we * we).sum((1, 2)), rtol=2e-2, atol=0)
+    got_emb_dot = dot_factors(tok, g1, tok, g2, "nn.Embedding", include_bias=False).float()
+    we2 = torch.einsum("btd,btv->bvd", g2.float(), onehot)
+    torch.testing.assert_close(got_emb_dot, (we * we2).sum((1, 2)), rtol=2e-2,
+                               atol=2e-2 * float((we * we).sum((1, 2)).max()))
+    ops.check_device_errors()
