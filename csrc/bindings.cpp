@@ -21,6 +21,7 @@
 #include "score_ag.cuh"
 #include "peer_sync.cuh"
 #include "allreduce_p2p.cuh"
+#include "mask_gather.cuh"
 #include "moe_ep.cuh"
 #include "norm_grad.cuh"
 
@@ -67,8 +68,9 @@ void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t s
   auto b = operand(B, "B");
   TORCH_CHECK(a.cols == b.cols, "A and B disagree on K");
   check_cuda(C, "C");
-  TORCH_CHECK(mode == bw::kStoreF32 || mode == bw::kStoreBF16 || mode == bw::kAtomicF32 || mode == bw::kStoreBF16T,
-              "mode: fp32, bf16, fp32 atomic or transposed bf16 store");
+  TORCH_CHECK(mode == bw::kStoreF32 || mode == bw::kStoreBF16 || mode == bw::kAtomicF32 || mode == bw::kStoreBF16T ||
+                  mode == bw::kSqAccF32,
+              "mode: fp32, bf16, fp32 atomic, transposed bf16 or squared-sum store");
   const bool bf16_out = mode == bw::kStoreBF16 || mode == bw::kStoreBF16T;
   TORCH_CHECK(C.scalar_type() == (bf16_out ? torch::kBFloat16 : torch::kFloat32),
               "C dtype does not match the store mode");
@@ -88,7 +90,11 @@ void gemm_tn(Tensor A, Tensor B, Tensor C, double alpha, int64_t mode, int64_t s
   p.C = C.data_ptr();
   p.ldc = C.dim() >= 2 ? C.stride(-2) : 0;
   p.batch_stride_c = (C.dim() == 3) ? C.stride(0) : 0;
-  if (z > 1) TORCH_CHECK(C.dim() == 3 && C.size(0) == z, "C must be (Z, ., .) for batched A");
+  if (mode == bw::kSqAccF32) {
+    TORCH_CHECK(C.dim() == 2 && p.splits == 1, "the squared-sum store takes one (M, N) matrix and no split-K");
+  } else if (z > 1) {
+    TORCH_CHECK(C.dim() == 3 && C.size(0) == z, "C must be (Z, ., .) for batched A");
+  }
   if (mode == bw::kStoreBF16T) {
     TORCH_CHECK(C.size(-2) == p.N && C.size(-1) == p.M, "C^T must be (N, M)");
   } else {
@@ -606,6 +612,25 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
                    at::cuda::getCurrentCUDAStream());
 }
 
+// Mask projection of factorized gradients: out (B, M) fp32 = sum_t R[b, t, rows] * C[b, t, cols].
+void mask_gather(Tensor R, Tensor C, Tensor rows, Tensor cols, Tensor out) {
+  const c10::cuda::CUDAGuard guard(R.device());
+  for (auto* t : {&R, &C})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->is_contiguous() && t->dim() == 3 &&
+                    t->size(2) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "factors: contiguous 16-byte aligned (B, T, K) bf16 with K % 8 == 0");
+  TORCH_CHECK(R.size(0) == C.size(0) && R.size(1) == C.size(1), "factors disagree on (B, T)");
+  for (auto* t : {&rows, &cols})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(), "coordinates: int32 CUDA");
+  TORCH_CHECK(rows.numel() == cols.numel(), "one row and one column per coordinate");
+  const long long M = rows.numel();
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.dim() == 2 &&
+                  out.size(0) == R.size(0) && out.size(1) == M, "out: (B, M) fp32");
+  bw::mask_gather(reinterpret_cast<const __nv_bfloat16*>(R.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(C.data_ptr()),
+                  rows.data_ptr<int>(), cols.data_ptr<int>(), out.data_ptr<float>(), (int)R.size(0), (int)R.size(1),
+                  (int)R.size(2), (int)C.size(2), (int)M, at::cuda::getCurrentCUDAStream());
+}
+
 // MoE routing histogram (int32 counts, accumulated) of int64 expert ids.
 void moe_count(Tensor topi, Tensor counts) {
   const c10::cuda::CUDAGuard guard(topi.device());
@@ -1071,6 +1096,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_split", &swiglu_split);
   m.def("swiglu_split_bwd", &swiglu_split_bwd);
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch: rows stored into their experts' ranks");
+  m.def("mask_gather", &mask_gather, "mask projection of factorized gradients (gather-contract)");
+  m.def("moe_count", &moe_count, "MoE routing histogram");
   m.def("moe_place", &moe_place, "MoE receive layout and owner-side ragged GEMM tables");
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");

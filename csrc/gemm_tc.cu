@@ -128,6 +128,26 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
   }
   if (!row_ok) return;
   const int nbase = n0 + c0;
+  if (p.c_mode == kSqAccF32) {  // every batch squares into the same matrix
+    float* Cr = static_cast<float*>(Cbase) + (long long)row * p.ldc;
+    if (c0 + 32 <= BN && nbase + 32 <= p.N && ((reinterpret_cast<uintptr_t>(Cr + nbase) & 15) == 0)) {
+      float4* Cv = reinterpret_cast<float4*>(Cr + nbase);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float x0 = alpha * __uint_as_float(r[4 * q]), x1 = alpha * __uint_as_float(r[4 * q + 1]);
+        const float x2 = alpha * __uint_as_float(r[4 * q + 2]), x3 = alpha * __uint_as_float(r[4 * q + 3]);
+        atomicAdd(Cv + q, make_float4(x0 * x0, x1 * x1, x2 * x2, x3 * x3));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nbase + j;
+        const float x = alpha * __uint_as_float(r[j]);
+        if (j < BN - c0 && n < p.N) atomicAdd(Cr + n, x * x);
+      }
+    }
+    return;
+  }
   if (p.c_mode == kStoreBF16Scatter) {
     // Row m goes home: rank scatter[m].x, row scatter[m].y of that rank's C (peer memory).
     const int2 dstm = p.scatter[row];

@@ -17,6 +17,7 @@ enum GemmStore : int {
   // 5: unused (an earlier peer-atomic reduce; replaced by kPeerSlotF32)
   kStoreBF16Scatter = 6,  // bf16 row m stored into rank scatter[m].x's C at row scatter[m].y
                           // (peer pointers; expert outputs returned to their source ranks)
+  kSqAccF32 = 8,     // C (fp32, one matrix) += (alpha * AB^T)^2 summed over the batch (atomics)
   kPeerSlotF32 = 7,  // reduce-scatter: element i (owner o = (i / 4) / per4) is STORED into
                      // peers[o][self_rank * 4 * per4 + i - o * 4 * per4] (the owner's slot for
                      // this rank); the owner sums its slots afterwards (splits must be 1)

@@ -634,9 +634,9 @@ class EKFACAttributor(KroneckerAttributor):
             for layer, (u_a, u_g) in eig.items():
                 if layer not in g.data:
                     continue
-                m = ops.ekfac_materialize(g.data[layer], g.layer_types[layer], u_a.to(dev), u_g.to(dev))
-                lam[layer] = lam.get(layer, 0) + (m * m).sum(0)
-                counts[layer] = counts.get(layer, 0) + m.shape[0]
+                lam[layer], n = ops.ekfac_lambda_accumulate(g.data[layer], g.layer_types[layer], u_a.to(dev),
+                                                            u_g.to(dev), lam.get(layer))
+                counts[layer] = counts.get(layer, 0) + n
         for layer in sorted(lam):
             all_reduce_sum(lam[layer])
             counts[layer] = int(all_reduce_sum(torch.tensor([counts[layer]], dtype=torch.int64)).item())

@@ -39,6 +39,7 @@ from dattri_llm_b200.gradient.ops.kronecker import (
     LayerFisherAccumulator,
     LayerKroneckerAccumulator,
     dense_inverse,
+    ekfac_lambda_accumulate,
     ekfac_materialize,
     ekfac_materialize_factors,
     ekfac_precondition,

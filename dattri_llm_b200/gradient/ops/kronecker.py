@@ -142,6 +142,40 @@ def ekfac_materialize_factors(a, g, layer_type: str, U_A, U_G, module_kwargs=Non
     return materialize_factors(a, g, layer_type)
 
 
+def ekfac_lambda_accumulate(f, layer_type: str, U_A, U_G, lam: torch.Tensor | None,
+                            include_bias: bool = True) -> tuple[torch.Tensor, int]:
+    """``lam += sum_i (U_G^T dW_i U_A)^2`` over one batch; returns ``(lam, batch size)``.
+
+    Factorized linear layers on sm_100 take the fused path: the factors are rotated into
+    the eigenbasis (``a U_A``, ``g U_G``), then ONE batched tcgen05 GEMM forms every
+    sample's rotated gradient and squares it into *lam* in its epilogue -- the per-sample
+    ``(B, d_out * d_in)`` coordinates never reach HBM.  Everything else materializes the
+    coordinates and sums their squares.  Reference:
+    ``dattri_llm/attribution/algorithm/kronecker.py:1530-1563``."""
+    from dattri_llm_b200 import ops as native_ops
+
+    if not isinstance(f, torch.Tensor) and U_A.ndim == 2 and not is_conv_transpose(layer_type):
+        bf = f.as_batch_first()
+        a, g = preprocess_factors(bf.activation, bf.pre_activation_grad, layer_type, bf.module_kwargs,
+                                  include_bias)
+        if (a.ndim == 3 and g.ndim == 3 and native_ops.use_native(a, g) and a.dtype == torch.bfloat16
+                and g.dtype == torch.bfloat16 and a.shape[-1] == U_A.shape[0] and g.shape[-1] == U_G.shape[0]):
+            b, t = a.shape[:2]
+            ka, kg = U_A.shape[-1], U_G.shape[-1]
+            # eigenbasis factors stored token-major, (B, k, T): the operands of the next GEMM
+            ar_t = torch.empty(b, ka, t, dtype=torch.bfloat16, device=a.device)
+            gr_t = torch.empty(b, kg, t, dtype=torch.bfloat16, device=a.device)
+            native_ops.gemm_tn(a.contiguous(), U_A.t().contiguous().bfloat16(), ar_t, mode=native_ops.STORE_BF16_T)
+            native_ops.gemm_tn(g.contiguous(), U_G.t().contiguous().bfloat16(), gr_t, mode=native_ops.STORE_BF16_T)
+            if lam is None:
+                lam = torch.zeros(kg * ka, dtype=torch.float32, device=a.device)
+            native_ops.gemm_tn(gr_t, ar_t, lam.view(kg, ka), mode=native_ops.STORE_SQ_SUM_F32)
+            return lam, b
+    m = ekfac_materialize(f, layer_type, U_A, U_G, include_bias)
+    sq = (m * m).sum(0)
+    return (sq if lam is None else lam.add_(sq)), m.shape[0]
+
+
 def kfac(f, layer_type: str, include_bias: bool = True):
     """:func:`kfac_factors` on a :class:`Factorized` (batch-first-safe)."""
     bf = f.as_batch_first()

@@ -351,7 +351,16 @@ def mask_materialized(x: torch.Tensor, projector, *, proj_dim: int, proj_seed: i
 
 
 def _gather_pairs(rows_src, cols_src, rows, cols, *, one_hot: bool = False) -> torch.Tensor:
-    """``out[:, m] = sum_t rows_src[:, t, rows[m]] * cols_src[:, t, cols[m]]`` chunked over m."""
+    """``out[:, m] = sum_t rows_src[:, t, rows[m]] * cols_src[:, t, cols[m]]`` chunked over m.
+
+    On sm_100 with bf16 factors this is one gather-contract kernel (``csrc/mask_gather.cu``)
+    that stages token tiles of both factors in shared memory."""
+    from dattri_llm_b200 import ops as native_ops
+
+    if (not one_hot and rows_src.ndim == 3 and native_ops.use_native(rows_src, cols_src)
+            and rows_src.dtype == torch.bfloat16 and cols_src.dtype == torch.bfloat16
+            and (rows_src.shape[-1] + cols_src.shape[-1]) * 2 <= 192 * 1024):
+        return native_ops.mask_gather(rows_src, cols_src, rows, cols).to(rows_src.dtype)
     b, t = cols_src.shape[:2]
     chunk = max(1, _MASK_CHUNK_ELEMS // max(1, b * t))
     out = []

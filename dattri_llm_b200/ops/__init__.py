@@ -123,12 +123,19 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     STORE_BF16,
     STORE_BF16_T,
     STORE_F32,
+    STORE_SQ_SUM_F32,
     gemm_grouped,
     gemm_tn,
     gemm_tn_seg,
     matmul_tn,
 )
-from dattri_llm_b200.ops.gram import ghost_dot, ghost_gram, ghost_gram_tokens, per_sample_outer  # noqa: E402
+from dattri_llm_b200.ops.gram import (  # noqa: E402
+    ghost_dot,
+    ghost_gram,
+    ghost_gram_tokens,
+    mask_gather,
+    per_sample_outer,
+)
 from dattri_llm_b200.ops.norm import norm_per_sample_grad  # noqa: E402
 from dattri_llm_b200.ops.optim import adam_direction  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
@@ -137,6 +144,7 @@ __all__ = [
     "STORE_ATOMIC_F32",
     "STORE_BF16",
     "STORE_BF16_T",
+    "STORE_SQ_SUM_F32",
     "STORE_F32",
     "adam_direction",
     "available",
@@ -150,6 +158,7 @@ __all__ = [
     "ghost_dot",
     "ghost_gram",
     "ghost_gram_tokens",
+    "mask_gather",
     "matmul_tn",
     "native",
     "norm_per_sample_grad",

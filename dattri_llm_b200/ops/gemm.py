@@ -8,6 +8,7 @@ STORE_F32 = 0
 STORE_BF16 = 1
 STORE_ATOMIC_F32 = 2
 STORE_BF16_T = 3
+STORE_SQ_SUM_F32 = 8  # C += sum over the batch of (alpha * A_z B_z^T)^2
 
 _SMS = 148
 

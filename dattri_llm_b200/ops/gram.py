@@ -90,3 +90,23 @@ def ghost_gram_tokens(tok1: torch.Tensor, g1: torch.Tensor, tok2: torch.Tensor, 
     native().ghost_gram_tokens(tok1.reshape(-1).long().contiguous(), flat(g1), tok2.reshape(-1).long().contiguous(),
                                flat(g2), s1, s2, out, error_word(g1.device), diag_only)
     return out
+
+
+def mask_gather(rows_src: torch.Tensor, cols_src: torch.Tensor, rows: torch.Tensor, cols: torch.Tensor) -> torch.Tensor:
+    """``(B, M)`` fp32 ``out[b, m] = sum_t rows_src[b, t, rows[m]] * cols_src[b, t, cols[m]]``:
+    fixed coordinates of per-sample gradients ``rows_src_b^T cols_src_b`` gathered without
+    forming them (the ``mask`` projection style)."""
+    from dattri_llm_b200.ops import count_launch, native
+
+    def prep(x):
+        x = x.contiguous().bfloat16()
+        if x.shape[-1] % 8:
+            x = torch.nn.functional.pad(x, (0, 8 - x.shape[-1] % 8))
+        return x
+
+    r, c = prep(rows_src), prep(cols_src)
+    out = torch.empty(r.shape[0], rows.numel(), dtype=torch.float32, device=r.device)
+    count_launch()
+    native().mask_gather(r, c, rows.to(device=r.device, dtype=torch.int32).contiguous(),
+                         cols.to(device=r.device, dtype=torch.int32).contiguous(), out)
+    return out

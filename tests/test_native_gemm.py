@@ -297,3 +297,41 @@ def test_fused_per_sample_dot_and_norm(b, s, k, d):
     torch.testing.assert_close(got_emb_dot, (we * we2).sum((1, 2)), rtol=2e-2,
                                atol=2e-2 * float((we * we).sum((1, 2)).max()))
     ops.check_device_errors()
+
+
+def test_ekfac_lambda_fused_rotate_square_reduce():
+    """EK-FAC eigenvalue accumulation: rotate the factors into the eigenbasis, form every
+    sample's rotated gradient and square-sum it into lambda inside one batched GEMM's
+    epilogue; against fp32 materialized U_G^T dW U_A."""
+    from dattri_llm_b200.gradient.gradient import Factorized
+    from dattri_llm_b200.gradient.ops.kronecker import ekfac_lambda_accumulate
+
+    b, t, k, d = 6, 200, 96, 64
+    a = torch.randn(b, t, k, device="cuda").bfloat16()
+    g = torch.randn(b, t, d, device="cuda").bfloat16()
+    u_a = torch.linalg.qr(torch.randn(k, k, device="cuda"))[0]
+    u_g = torch.linalg.qr(torch.randn(d, d, device="cuda"))[0]
+    f = Factorized(activation=a, pre_activation_grad=g, module_kwargs=None)
+    lam, n = ekfac_lambda_accumulate(f, "nn.Linear", u_a, u_g, None)
+    lam, n2 = ekfac_lambda_accumulate(f, "nn.Linear", u_a, u_g, lam)  # accumulates
+    dw = torch.einsum("btd,btk->bdk", g.float(), a.float())
+    m = u_g.T @ dw @ u_a
+    want = 2 * (m * m).sum(0).reshape(-1)
+    assert n == n2 == b
+    torch.testing.assert_close(lam, want, rtol=3e-2, atol=3e-2 * float(want.mean()))
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("b", "t", "kr", "kc", "m"), [(3, 300, 64, 96, 1000), (2, 1024, 2048, 512, 4096)])
+def test_mask_gather_matches_materialized(b, t, kr, kc, m):
+    """Mask projection: fixed coordinates of every per-sample gradient R_b^T C_b gathered
+    from shared-memory token tiles, against the fp32 materialized gradient."""
+    r = torch.randn(b, t, kr, device="cuda").bfloat16()
+    c = torch.randn(b, t, kc, device="cuda").bfloat16()
+    rows = torch.randint(0, kr, (m,), device="cuda")
+    cols = torch.randint(0, kc, (m,), device="cuda")
+    dense = torch.einsum("btr,btc->brc", r.float(), c.float())
+    want = dense[:, rows, cols]
+    got = ops.mask_gather(r, c, rows, cols)
+    torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-2)
+    ops.check_device_errors()
