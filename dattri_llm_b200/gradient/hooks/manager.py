@@ -389,22 +389,30 @@ class HookManager:
                              f"batch size is {expected}.")
         return [str(i) for i in ids]
 
-    def _input_batch_size(self) -> int:
-        for v in self._last_inputs.values():
+    def _shape_inputs(self) -> list:
+        """The captured model inputs that can tell the batch size: every one but the
+        sample-identifier field (its length is what gets checked against the batch)."""
+        key = self._sample_id_key
+        skip = None if key is None else (f"_arg{key}" if isinstance(key, int) else key)
+        return [v for k, v in self._last_inputs.items() if k != skip]
+
+    def _input_batch_size(self, default: int = 1) -> int:
+        for v in self._shape_inputs():
             if isinstance(v, torch.Tensor) and v.ndim > 0:
                 return v.shape[0]
-        return 1
+        return default
 
     def _step_batch_size(self, gradient: Gradient) -> int:
         try:
             b = gradient.batch_size
         except ValueError:
             return self._input_batch_size()
-        for v in self._last_inputs.values():
+        inputs = self._shape_inputs()
+        for v in inputs:
             if (isinstance(v, torch.Tensor) and v.ndim > 0 and v.shape[0] == b) or (
                     isinstance(v, (list, tuple)) and len(v) == b):
                 return b
-        return self._input_batch_size() if self._last_inputs else b
+        return self._input_batch_size(default=b) if inputs else b
 
     def _finalize_step(self) -> GradientRecord:
         self._last_gradient = None
