@@ -6,7 +6,9 @@
   one by one;
 * live TracIn attribution with the train set sharded over ranks (each rank scores its
   shard against the whole test set) gives, once the rows are merged, the single-process
-  scores.
+  scores;
+* live K-FAC / EK-FAC on sharded data fit the global factors (covariances and EK-FAC's
+  eigenvalue sweep reduced over ranks) and reproduce the single-process scores.
 """
 
 from __future__ import annotations
@@ -16,6 +18,7 @@ import os
 import socket
 import tempfile
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -114,7 +117,7 @@ def test_packed_accumulator_reduction_equals_one_by_one():
             assert n_p == n_s
 
 
-def _scores(world_rank=None):
+def _scores():
     import dattri_llm_b200 as bw
 
     x, y, xt, yt = tiny.make_data(seed=3, n_train=10, n_test=4)
@@ -144,3 +147,35 @@ def test_sharded_live_scores_merge_to_single_process_scores():
     assert set(merged) == set(want)
     for h, row in want.items():
         torch.testing.assert_close(merged[h], row, rtol=1e-5, atol=1e-6)
+
+
+def _kron_scores(cls_name, damping):
+    import dattri_llm_b200 as bw
+
+    x, y, xt, yt = tiny.make_data(seed=8, n_train=12, n_test=3)
+    model = tiny.make_model(seed=9)
+    args = bw.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=2,
+                                   per_device_eval_batch_size=3)
+    att = getattr(bw, cls_name)(args, task=bw.AttributionTask(tiny.sq_loss, model))
+    score = att.attribute(tiny.as_dataset(x, y), tiny.as_dataset(xt, yt),
+                          hook_config=bw.HookManagerConfig(linear_io=tiny.LAYERS), damping=damping)
+    return {h: score.trajectory_agnostic(h) for h in score.train_ids}
+
+
+def _kron_worker_scores(rank, world, cls_name, damping):
+    return _kron_scores(cls_name, damping)
+
+
+@pytest.mark.parametrize("cls_name", ["KFACAttributor", "EKFACAttributor"])
+def test_sharded_kronecker_fit_and_scores_equal_single_process(cls_name):
+    """The covariance fit (and EK-FAC's eigenvalue sweep) run on both ranks' shards and are
+    reduced, so every rank preconditions with the global factors."""
+    res = _spawn(_kron_worker_scores, cls_name, 0.05)
+    want = _kron_scores(cls_name, 0.05)
+    merged = {}
+    for rank in range(2):
+        assert not (set(res[rank]) & set(merged))
+        merged.update(res[rank])
+    assert set(merged) == set(want)
+    for h, row in want.items():
+        torch.testing.assert_close(merged[h], row, rtol=1e-4, atol=1e-5)
