@@ -66,5 +66,12 @@ def canonical_class_name(module: nn.Module) -> str:
     declared = getattr(type(module), "__bw_layer_type__", None)
     if declared is not None:
         return declared
-    mod, name = type(module).__module__, type(module).__name__
+    cls = type(module)
+    # FSDP2 (``fully_shard``) swaps a module's class for a generated ``FSDP<Class>`` subclass:
+    # name the class it was made from.
+    for c in cls.__mro__:
+        if not c.__module__.startswith(("torch.distributed.fsdp", "torch.distributed._composable")):
+            cls = c
+            break
+    mod, name = cls.__module__, cls.__name__
     return f"nn.{name}" if mod.startswith("torch.nn") else f"{mod}.{name}"
