@@ -318,6 +318,7 @@ class GradientStreamer(GradientSource):
         self._it: Iterator | None = None
         self._index = 0
         self._consumed = False
+        self._any_trainable = True
         self._lrs: dict[int, float] = {}
         self._entered = False
         self._collect_ctx = None
@@ -411,6 +412,9 @@ class GradientStreamer(GradientSource):
             self._end_probe_pass()
             self._pass_state = _ProbePassState(self._model, self._fwd)
         self._fwd.train(self.enable_update)
+        # Nothing can hold a parameter gradient when every parameter is frozen (the frozen
+        # probe): then the per-step zero_grad walks of the module tree are skipped.
+        self._any_trainable = any(p.requires_grad for p in self._fwd.parameters())
         self._it = iter(self._loader)
         self._index = 0
         self._accum = 0
@@ -476,7 +480,7 @@ class GradientStreamer(GradientSource):
         hashes = list(record.input_hash) if isinstance(record.input_hash, list) else [record.input_hash]
         if self._host_ids_ok is None and host_ids is not None:
             self._host_ids_ok = list(host_ids) == hashes
-        if self._pass_state is not None and not self._pass_state.holds_grads:
+        if self._pass_state is not None and not self._pass_state.holds_grads and self._any_trainable:
             self._fwd.zero_grad(set_to_none=True)
         step = self._index if self.enable_update else self._checkpoint_step
         self._index += 1
@@ -485,7 +489,7 @@ class GradientStreamer(GradientSource):
     def _forward_backward(self, batch: object) -> torch.Tensor:
         if self.enable_update:
             self._fwd.train()
-        if self._accum == 0:
+        if self._accum == 0 and self._any_trainable:
             hands_back = self._pass_state is not None and self._pass_state.holds_grads
             self._fwd.zero_grad(set_to_none=not hands_back)
         self._capture.record = None
