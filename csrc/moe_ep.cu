@@ -6,6 +6,8 @@
 // loop).  With it goes the row's origin (source rank, source slot row), which the owner's
 // expert down-projection GEMM uses to store its output rows back into the SOURCE rank's
 // combine buffer from inside its epilogue (see kStoreBF16Scatter in gemm_tc.cu).
+// Indices (destination rank and row) come from moe_place_kernel, which keeps every row
+// inside the owner's receive buffer.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -21,16 +23,34 @@ struct PeerRows {
   int2* meta[kMaxRanks];   // each rank's origin table
 };
 
-// Row r of `src` (r = token * k + slot) goes to rank dst_rank[r], row dst_row[r].
+// Row r of `src` (r = token * k + slot) goes to rank dst_rank[r], row dst_row[r].  One warp
+// per row; each lane keeps eight 16-byte loads in flight before its stores (a row-per-CTA
+// loop with two loads per thread was latency-bound).
+constexpr int kDispatchUnroll = 8;
+
 __global__ void dispatch_kernel(const uint4* __restrict__ src, const int* __restrict__ dst_rank,
                                 const int* __restrict__ dst_row, PeerRows peers, int rows, int vec_per_row,
                                 int self, int rows_per_token, int token_stride_vec) {
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
     const int dr = dst_rank[r], drow = dst_row[r];
     const uint4* s = src + (long long)(r / rows_per_token) * token_stride_vec;
     uint4* d = peers.rows[dr] + (long long)drow * vec_per_row;
-    for (int v = threadIdx.x; v < vec_per_row; v += blockDim.x) d[v] = s[v];
-    if (threadIdx.x == 0) peers.meta[dr][drow] = make_int2(self, r);
+    for (int v0 = lane; v0 < vec_per_row; v0 += 32 * kDispatchUnroll) {
+      uint4 x[kDispatchUnroll];
+#pragma unroll
+      for (int u = 0; u < kDispatchUnroll; ++u) {
+        const int v = v0 + u * 32;
+        if (v < vec_per_row) x[u] = s[v];
+      }
+#pragma unroll
+      for (int u = 0; u < kDispatchUnroll; ++u) {
+        const int v = v0 + u * 32;
+        if (v < vec_per_row) d[v] = x[u];
+      }
+    }
+    if (lane == 0) peers.meta[dr][drow] = make_int2(self, r);
   }
 }
 
@@ -205,7 +225,8 @@ void moe_dispatch(const void* src, long long token_stride, const int* dst_rank, 
     p.meta[r] = peer_meta[r];
   }
   if (rows <= 0) return;
-  const int grid = rows < 148 * 8 ? rows : 148 * 8;
+  const int ctas = (rows + 3) / 4;  // four warps (rows) per CTA
+  const int grid = ctas < 148 * 8 ? ctas : 148 * 8;
   dispatch_kernel<<<grid, 128, 0, s>>>(static_cast<const uint4*>(src), dst_rank, dst_row, p, rows, cols / 8, self,
                                        rows_per_token, (int)(token_stride / 8));
 }

@@ -178,3 +178,46 @@ def test_swiglu_split_forward_backward():
     ref.backward(da.float())
     torch.testing.assert_close(dh[:valid].float(), hr.grad[:valid], rtol=1e-2, atol=3e-2)
     assert not dh[valid:].any()
+
+
+def test_moe_dispatch_and_combine_with_emulated_ranks():
+    """Dispatch, combine and the fused combine-backward-dispatch with three "ranks" whose
+    receive buffers are separate allocations on this GPU (the kernels take peer pointers;
+    local ones exercise the same code)."""
+    world, t, k, h = 3, 37, 2, 136
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(t, h, device="cuda", generator=g).bfloat16()
+    rows = t * k
+    dest = torch.randint(0, world, (rows,), device="cuda", generator=g)
+    order = torch.argsort(dest, stable=True)
+    per = torch.bincount(dest, minlength=world)
+    start = torch.cumsum(per, 0) - per
+    row = torch.empty_like(dest)
+    row[order] = torch.arange(rows, device="cuda") - start[dest[order]]
+    recv = [torch.zeros(rows, h, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    meta = [torch.full((rows, 2), -1, device="cuda", dtype=torch.int32) for _ in range(world)]
+    d32, r32 = dest.int().contiguous(), row.int().contiguous()
+    ops.native().moe_dispatch(x, k, d32, r32, recv, meta, 1)
+    for r in range(rows):
+        dr, rr = int(dest[r]), int(row[r])
+        assert torch.equal(recv[dr][rr], x[r // k])
+        assert meta[dr][rr].tolist() == [1, r]
+    # combine: y[t] = sum_j w[t, j] * slots[t * k + j]
+    slots = torch.randn(rows, h, device="cuda", generator=g).bfloat16()
+    w = torch.rand(t, k, device="cuda", generator=g)
+    y = torch.empty(t, h, device="cuda", dtype=torch.bfloat16)
+    ops.native().moe_combine(slots, w, y)
+    want = (slots.float().view(t, k, h) * w[..., None]).sum(1)
+    torch.testing.assert_close(y.float(), want, rtol=1e-2, atol=2e-2)
+    # backward: dw = <slots, dy>, and w * dy dispatched to the owners
+    dy = torch.randn(t, h, device="cuda", generator=g).bfloat16()
+    dw = torch.empty(t, k, device="cuda")
+    for buf in recv:
+        buf.zero_()
+    ops.native().moe_combine_bwd_dispatch(dy, slots, w, dw, d32, r32, recv, meta, 2)
+    torch.testing.assert_close(dw, (slots.float().view(t, k, h) * dy.float()[:, None]).sum(-1), rtol=1e-3, atol=1e-2)
+    for r in range(rows):
+        dr, rr = int(dest[r]), int(row[r])
+        torch.testing.assert_close(recv[dr][rr].float(), (w.reshape(-1)[r] * dy[r // k].float()).bfloat16().float())
+        assert meta[dr][rr].tolist() == [2, r]
+    ops.check_device_errors()
