@@ -197,7 +197,7 @@ def run(world: int, emulate: bool, rank: int) -> list[dict]:
         d32, r32 = dest.int().contiguous(), row.int().contiguous()
         secs = _time(lambda: nat.moe_dispatch(x2, top_k, d32, r32, recv, meta, rank))
         report("moe_dispatch (rows stored into the owners' receive buffers)", secs, 0.0, 0.0,
-               rows_in * h * 2 * 2 + t * h * 2)
+               rows_in * h * 2 + t * h * 2)  # every routed row written once; each token read once
         n_i = torch.full((e_l,), rows_in // e_l, dtype=torch.int32, device=dev)
         base = (torch.cumsum(n_i, 0) - n_i).int().contiguous()
         prefix = torch.zeros(e_l + 1, dtype=torch.int32, device=dev)
