@@ -46,6 +46,19 @@ def _cases():
         "layernorm_nobias": (lambda: nn.LayerNorm(6, bias=False), lambda: torch.randn(B, 4, 6), 24),
         "rmsnorm": (lambda: nn.RMSNorm(6), lambda: torch.randn(B, 4, 6), 24),
         "embedding": (lambda: nn.Embedding(11, 4), lambda: torch.randint(0, 11, (B, 7)), 28),
+        "embedding_padding": (lambda: nn.Embedding(11, 4, padding_idx=0), lambda: torch.randint(0, 3, (B, 7)), 28),
+        "linear4d": (lambda: nn.Linear(6, 4), lambda: torch.randn(B, 2, 3, 6), 24),
+        "conv2d_grouped": (lambda: nn.Conv2d(4, 6, 3, groups=2), lambda: torch.randn(B, 4, 5, 5), 54),
+        "conv2d_strided_dilated": (lambda: nn.Conv2d(2, 3, 3, stride=2, padding=2, dilation=2),
+                                   lambda: torch.randn(B, 2, 7, 7), 48),
+        "conv1d_depthwise": (lambda: nn.Conv1d(4, 4, 3, groups=4, padding=1), lambda: torch.randn(B, 4, 6), 24),
+        "conv_transpose1d": (lambda: nn.ConvTranspose1d(3, 2, 3), lambda: torch.randn(B, 3, 5), 14),
+        "conv_transpose2d": (lambda: nn.ConvTranspose2d(2, 3, 2, stride=2), lambda: torch.randn(B, 2, 3, 3), 108),
+        "embedding_bag_sum": (lambda: nn.EmbeddingBag(11, 4, mode="sum"), lambda: torch.randint(0, 11, (B, 5)), 4),
+        "embedding_bag_mean_padding": (lambda: nn.EmbeddingBag(11, 4, mode="mean", padding_idx=1),
+                                       lambda: torch.randint(0, 4, (B, 6)), 4),
+        "groupnorm": (lambda: nn.GroupNorm(2, 4), lambda: torch.randn(B, 4, 5), 20),
+        "instancenorm_affine": (lambda: nn.InstanceNorm1d(4, affine=True), lambda: torch.randn(B, 4, 5), 20),
     }
 
 
@@ -60,8 +73,18 @@ def _reference(model: Wrap, x: torch.Tensor) -> torch.Tensor:
         b = layer.bias.grad if getattr(layer, "bias", None) is not None else None
         if isinstance(layer, nn.Embedding):
             rows.append(w.reshape(-1))
-        elif isinstance(layer, (nn.LayerNorm, nn.RMSNorm)):
+        elif isinstance(layer, (nn.LayerNorm, nn.RMSNorm, nn.GroupNorm, nn.InstanceNorm1d)):
             rows.append(torch.cat([w.reshape(-1)] + ([b.reshape(-1)] if b is not None else [])))
+        elif isinstance(layer, nn.modules.conv._ConvTransposeNd):
+            # weight (c_in, c_out, k...): rows are input channels; the bias sits in an extra
+            # row, in a padded block of c_out columns after the weight's c_out * k columns
+            w2 = w.reshape(w.shape[0], -1)
+            if b is not None:
+                full = torch.zeros(w2.shape[0] + 1, w2.shape[1] + b.numel())
+                full[:-1, : w2.shape[1]] = w2
+                full[-1, w2.shape[1]:] = b
+                w2 = full
+            rows.append(w2.reshape(-1))
         else:
             w2 = w.reshape(w.shape[0], -1)
             if b is not None:
