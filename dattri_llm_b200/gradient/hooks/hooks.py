@@ -217,12 +217,15 @@ def register_linear_io_hooks(
         if projection_kwargs is not None:
             buf["_proj_kw"] = projection_kwargs.get(name, projection_kwargs.get("__default__"))
         buf["_capture_style"] = capture_style
+        bwd = _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
+                             on_layer_backward)
+        # The output gradient is taken by a hook on the autograd node that produced the
+        # layer's output, registered in the forward hook: a full module backward hook would
+        # wrap every call's inputs and outputs in an extra autograd function (host time per
+        # layer and step) and forbids in-place ops on the layer's output.
         handles.append(module.register_forward_hook(
             _forward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
-                          on_layer_forward)))
-        handles.append(module.register_full_backward_hook(
-            _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
-                           on_layer_backward)))
+                          on_layer_forward, bwd)))
     return buffers, handles
 
 
@@ -230,10 +233,42 @@ def _device_index(t: torch.Tensor) -> int:
     return t.device.index if t.is_cuda else 0
 
 
-def _forward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback):
-    def hook(_module, inp, _out):
+def _on_output_grad(out: torch.Tensor, fire) -> None:
+    """Call ``fire(dL/d out)`` during the backward.
+
+    The hook sits on the autograd node that produced *out* (for a reshaped view such as
+    ``F.linear``'s 3-D output, on the node of its base), as a pre-hook: the node still runs
+    with the gradient w.r.t. the value the layer returned even when that value is modified
+    in place afterwards (an inplace activation), which a hook on the tensor would miss.
+    """
+    base = out._base
+    if base is not None:
+        if (base.grad_fn is not None and base.numel() == out.numel() and out.is_contiguous()
+                and base.is_contiguous()):
+            node, idx, shape = base.grad_fn, base.output_nr, out.shape
+        else:  # a general view: a plain tensor hook
+            out.register_hook(lambda g: fire(g) and None)
+            return
+    else:
+        node, idx, shape = out.grad_fn, out.output_nr, None
+
+    def pre(grads):
+        g = grads[idx]
+        if g is not None:
+            fire(g if shape is None else g.reshape(shape))
+
+    node.register_prehook(pre)
+
+
+def _forward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback, on_grad):
+    def hook(module, inp, out):
         if not torch.is_grad_enabled():
             return  # no backward will follow (eval / log-prob pass)
+        record_forward(module, inp)
+        if isinstance(out, torch.Tensor) and out.requires_grad and out.grad_fn is not None:
+            _on_output_grad(out, lambda g, _m=module: on_grad(_m, None, (g,)))
+
+    def record_forward(_module, inp):
         x = inp[0]
         a = x.detach()
         dev = _device_index(x)

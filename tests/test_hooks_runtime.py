@@ -245,3 +245,30 @@ def test_auto_style_follows_the_cost_rule():
         rep = rec.gradient.representation["block.fc1"]
         want = maybe_use_materialized_norm(tokens, D + 1, D)
         assert rep == ("materialized" if want else "factorized"), (tokens, rep)
+
+
+class InPlaceAfter(nn.Module):
+    """Layer outputs modified in place right after the layer (inplace ReLU, ``mul_``)."""
+
+    def __init__(self) -> None:
+        super().__init__()
+        self.fc1 = nn.Linear(D, D)
+        self.act = nn.ReLU(inplace=True)
+        self.fc2 = nn.Linear(D, 1)
+
+    def forward(self, x):
+        h = self.act(self.fc1(x))
+        y = self.fc2(h)
+        y.mul_(3.0)
+        return y.sum(dim=(1, 2))
+
+
+def test_in_place_ops_after_a_layer_do_not_change_its_capture():
+    torch.manual_seed(5)
+    model = InPlaceAfter()
+    x = _data(7)
+    rec = _capture(model, x, HookManagerConfig(linear_io=[r"^fc[12]$"]))
+    want = _per_sample_weight_grads(model, x, ["fc1.weight", "fc1.bias", "fc2.weight", "fc2.bias"])
+    for layer in ("fc1", "fc2"):
+        oracle = torch.cat([want[f"{layer}.weight"], want[f"{layer}.bias"][..., None]], -1).reshape(B, -1)
+        torch.testing.assert_close(_dense(rec.gradient, layer), oracle, rtol=1e-5, atol=1e-6)
