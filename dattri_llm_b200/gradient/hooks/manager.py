@@ -139,6 +139,7 @@ class HookManager:
         self._projector: ops.DattriProjector | None = None
         self._share = _StepShare()
         self._next_ids: list[str] | None = None
+        self._host_mirror: dict[int, torch.Tensor] | None = None
 
         self._step_count = 0
         self._collecting = False
@@ -199,6 +200,13 @@ class HookManager:
             elif key in kwargs:
                 captured[key] = kwargs[key]
         self._last_inputs = captured
+
+    def set_host_inputs(self, mirror: dict[int, torch.Tensor] | None) -> None:
+        """Host copies of the next step's device inputs, keyed by ``id()`` of the device
+        tensor (consumed by that step).  When every model input of the step is one of them,
+        its content hash is computed from the host copies: the same hash, without reading
+        device tensors back (which would wait for the GPU at every step)."""
+        self._host_mirror = mirror
 
     def set_sample_ids(self, ids: list[str] | None) -> None:
         """Identities of the samples of the next completed step (consumed by that step).
@@ -435,6 +443,7 @@ class HookManager:
         self._last_gradient = gradient
         batch = self._step_batch_size(gradient)
         ids, self._next_ids = self._next_ids, None
+        mirror, self._host_mirror = self._host_mirror, None
         if ids is not None:
             if len(ids) != batch:
                 raise ValueError(f"set_sample_ids supplied {len(ids)} identities for a step of {batch} samples.")
@@ -448,7 +457,12 @@ class HookManager:
                 if missing:
                     raise KeyError(f"sample_hash_fields {missing!r} were not found among the model "
                                    "inputs of this step; cannot assign sample identities.")
-            input_hash = hash_batch(self._last_inputs, batch)
+            inputs = self._last_inputs
+            if mirror:
+                hosted = {k: mirror.get(id(v)) if isinstance(v, torch.Tensor) else v for k, v in inputs.items()}
+                if all(h is not None for h in hosted.values()):
+                    inputs = hosted
+            input_hash = hash_batch(inputs, batch)
         return GradientRecord(step=step, input_hash=input_hash, gradient=gradient,
                               sample_id_key=self._sample_id_key)
 

@@ -219,6 +219,17 @@ def move_batch(batch: object, device: torch.device | str, non_blocking: bool = F
     return mv(batch)
 
 
+def _host_mirror(host: object, dev: object) -> dict[int, torch.Tensor]:
+    """``{id(device tensor): host tensor}`` over a batch and its moved copy."""
+    if isinstance(host, dict) and isinstance(dev, dict):
+        pairs = [(host[k], dev[k]) for k in host if k in dev]
+    elif isinstance(host, (list, tuple)) and isinstance(dev, (list, tuple)):
+        pairs = list(zip(host, dev))
+    else:
+        pairs = [(host, dev)]
+    return {id(d): h for h, d in pairs if isinstance(h, torch.Tensor) and isinstance(d, torch.Tensor)}
+
+
 def _host_hashable(batch: object) -> dict | None:
     """The tensor fields of a host batch the manager would hash, or ``None``."""
     if isinstance(batch, dict):
@@ -460,6 +471,9 @@ class GradientStreamer(GradientSource):
             # the first step has shown the two agree (the loss_fn may feed the model a subset
             # of the batch's fields); until then the manager hashes.
             self._hm.set_sample_ids(host_ids if self._host_ids_ok else None)
+        # Whatever the model is fed, a field moved from this host batch is hashed from its
+        # host copy (no device read-back at step end).
+        self._hm.set_host_inputs(_host_mirror(host_batch, batch))
         self._forward_backward(batch)
         if self.enable_update:
             self._lrs[self._index] = float(self._optimizer.param_groups[0]["lr"])

@@ -91,3 +91,57 @@ def test_frozen_probe_leaves_parameters_and_grads_alone():
     for name, p in model.named_parameters():
         torch.testing.assert_close(p, before[name], msg=name)
         assert p.grad is None
+
+
+def test_sample_hashes_come_from_host_copies(monkeypatch):
+    """When the model is fed fields of the batch under other names too (``labels=input_ids``),
+    the step's content hash is still computed from the host copies of the moved tensors
+    (no device read-back), and equals the hash of the model's inputs."""
+    import dattri_llm_b200.gradient.hooks.manager as manager
+    import dattri_llm_b200.gradient.streaming as streaming
+    from dattri_llm_b200.utils.hashing import hash_batch
+
+    moved = []
+
+    def fake_move(batch, device, non_blocking=False):  # a "device" copy distinct from the host batch
+        out = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in batch.items()}
+        moved.append((batch, out))
+        return out
+
+    seen = []
+    real_hash = manager.hash_batch
+
+    def spy(inputs, b):
+        seen.append(inputs)
+        return real_hash(inputs, b)
+
+    monkeypatch.setattr(streaming, "move_batch", fake_move)
+    monkeypatch.setattr(manager, "hash_batch", spy)
+    ds = _dataset()
+
+    class Alias(torch.nn.Module):  # the model also takes y under a second name
+        def __init__(self):
+            super().__init__()
+            self.inner = tiny.make_model(seed=2)
+
+        def forward(self, x, y, labels):
+            return self.inner(x=x, y=y)
+
+    model = Alias()
+
+    def loss(m, batch):
+        return ((m(x=batch["x"], y=batch["y"], labels=batch["y"]) - batch["y"]) ** 2).sum()
+
+    args = bw.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=BATCH)
+    streamer = bw.GradientStreamer(model, ds, args, batch_size=BATCH, loss_fn=loss,
+                                   config=bw.HookManagerConfig(linear_io=[r"^inner\.mlp\.fc[12]$"]))
+    with streamer:
+        got = [hashes for _, _, hashes in streamer]
+    assert streamer._host_ids_ok is False  # the host batch's hash is not the model inputs' hash
+    assert len(seen) == len(moved), "every step is hashed by the manager"
+    host_ids = {id(t) for host, _ in moved for t in host.values()}
+    for inputs in seen:
+        assert all(id(v) in host_ids for v in inputs.values() if isinstance(v, torch.Tensor))
+    want = [hash_batch({"x": host["x"], "y": host["y"], "labels": host["y"]}, host["x"].shape[0])
+            for host, _ in moved]
+    assert got == want
