@@ -30,6 +30,7 @@ from dattri_llm_b200.gradient import ops
 from dattri_llm_b200.gradient.gradient import Factorized, Gradient, GradientRecord
 from dattri_llm_b200.gradient.streaming import rebatch_blocks
 from dattri_llm_b200.utils.cache import CacheBudget, TensorCache
+from dattri_llm_b200.utils.tracing import trace_range
 
 InnerProduct = Callable[..., torch.Tensor]
 Transform = Callable[[Gradient], Gradient]
@@ -199,6 +200,10 @@ def score_sources(train_source: Iterable, test_source: Iterable, device, *, inne
         return rep.batch_size * (max(toks) if toks else 1)
 
     def score_block(train_rep: Gradient, test_blocks, dense_cache) -> torch.Tensor:
+        with trace_range("dattri.score.block"):
+            return _score_block(train_rep, test_blocks, dense_cache)
+
+    def _score_block(train_rep: Gradient, test_blocks, dense_cache) -> torch.Tensor:
         row = None
         if packed_test is not None:
             pk, cols = packed_test

@@ -62,6 +62,7 @@ from dattri_llm_b200.gradient.hooks.routing import RoutedTokenTracker
 from dattri_llm_b200.gradient.ops import PARAM_GRAD_TYPES, is_embedding
 from dattri_llm_b200.utils.autograd import queue_backward_end_callback
 from dattri_llm_b200.utils.hashing import hash_batch
+from dattri_llm_b200.utils.tracing import trace_range
 
 _TASK_ID = getattr(torch._C, "_current_graph_task_id", None)
 
@@ -423,6 +424,10 @@ class HookManager:
         return self._input_batch_size(default=b) if inputs else b
 
     def _finalize_step(self) -> GradientRecord:
+        with trace_range(f"dattri.capture.step[{self._step_count}]"):
+            return self._finalize_step_inner()
+
+    def _finalize_step_inner(self) -> GradientRecord:
         self._last_gradient = None
         gradient = self._assemble_gradient()
         step = self._step_count

@@ -38,6 +38,7 @@ from dattri_llm_b200.gradient.gradient import Factorized, Gradient, GradientReco
 from dattri_llm_b200.utils.cache import CACHE_RESIDENCIES, TensorCache, available_host_bytes
 from dattri_llm_b200.utils.distributed import dist_rank
 from dattri_llm_b200.utils.hashing import hash_sample
+from dattri_llm_b200.utils.tracing import trace_range
 
 DISK_FORMATS = ("pickle", "memmap")
 MEMMAP_FORMAT = 2
@@ -276,8 +277,9 @@ class GradientStorageManager:
 
     def save_bulk(self, records: list[GradientRecord]) -> str:
         """Save *records* as one group (one file pair, one index line)."""
-        records = [_host_record(r) for r in records]
-        loc = self._write_group(records, None)
+        with trace_range("dattri.store.write"):
+            records = [_host_record(r) for r in records]
+            loc = self._write_group(records, None)
         for i, r in enumerate(records):
             self._index_entry(r, loc, i)
         self._persist_index(records, loc)

@@ -38,6 +38,7 @@ from dattri_llm_b200.gradient.gradient import Gradient
 from dattri_llm_b200.gradient.hooks import REGISTER_ALL, HookManager, HookManagerConfig
 from dattri_llm_b200.gradient.snapshots import TrajectorySnapshots
 from dattri_llm_b200.utils.hashing import hash_batch
+from dattri_llm_b200.utils.tracing import trace_range
 
 logger = logging.getLogger(__name__)
 StreamBatch = tuple[int, Gradient, list[str]]
@@ -474,7 +475,8 @@ class GradientStreamer(GradientSource):
         # Whatever the model is fed, a field moved from this host batch is hashed from its
         # host copy (no device read-back at step end).
         self._hm.set_host_inputs(_host_mirror(host_batch, batch))
-        self._forward_backward(batch)
+        with trace_range(f"dattri.stream.batch[{self._index}]"):
+            self._forward_backward(batch)
         if self.enable_update:
             self._lrs[self._index] = float(self._optimizer.param_groups[0]["lr"])
             self._accum += 1
