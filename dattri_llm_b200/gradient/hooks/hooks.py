@@ -60,12 +60,22 @@ ParamGradBuffer = dict
 
 
 def is_linear_io_capable(module: nn.Module) -> bool:
-    """Whether *module*'s per-sample gradient factorizes as an outer product (by type)."""
-    return isinstance(module, _LINEAR_IO_TYPES)
+    """Whether *module*'s per-sample gradient factorizes as an outer product (by type).
+
+    A capture tap (a class with ``__bw_capture_tap__``, e.g. an expert-parallel expert's
+    stand-in) counts as the layer type its ``__bw_layer_type__`` names.
+    """
+    return isinstance(module, _LINEAR_IO_TYPES) or getattr(type(module), "__bw_capture_tap__", False)
 
 
 def has_trainable_params(module: nn.Module) -> bool:
-    """Whether *module* owns (or proxies) a parameter that requires grad."""
+    """Whether *module* owns (or proxies) a parameter that requires grad.
+
+    A capture tap that stands for a weight held elsewhere (``__bw_capture_frozen__``) is
+    always captured.
+    """
+    if getattr(type(module), "__bw_capture_frozen__", False):
+        return True
     proxied = getattr(module, "proxied_parameters", None)
     if proxied is not None:
         return any(p.requires_grad for p in proxied())

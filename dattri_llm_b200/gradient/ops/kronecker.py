@@ -95,9 +95,12 @@ def kfac_factors(a, g, layer_type: str, module_kwargs: dict | None = None,
 
 def fim_factors(a, g, layer_type: str, module_kwargs: dict | None = None,
                 include_bias: bool = True) -> torch.Tensor:
-    """``(d, d)`` empirical Fisher of one batch's per-sample gradients."""
+    """``(d, d)`` empirical Fisher of one batch's per-sample gradients (the same Gram
+    accumulation as the K-FAC covariances: a tcgen05 split-K GEMM for bf16 rows on sm_100)."""
     grad = materialize_factors(a, g, layer_type, module_kwargs, include_bias)
-    return (grad.T @ grad).float() / grad.shape[0]
+    grad = grad.reshape(grad.shape[0], -1)
+    fisher = torch.zeros(grad.shape[1], grad.shape[1], device=grad.device)
+    return gram_accumulate(grad, fisher) / grad.shape[0]
 
 
 def sym_inverse(matrix: torch.Tensor, damping: float = 0.0) -> torch.Tensor:

@@ -20,6 +20,20 @@ input-gradient GEMM (against the transposed gate/up weights) returns its rows to
 sources from its epilogue, and the router weights get ``<dy, expert output>``.
 Bounded cross-GPU barriers separate the phases.  The reference has no expert parallelism
 (it captures MoE layers with replicated experts, ``dattri_llm/gradient/hooks/routing.py``).
+
+Per-sample capture.  Every expert has two :class:`ExpertTap` stand-ins,
+``experts.dattri_experts.<e>.gate_up`` and ``.down``, and the router's map is the
+:class:`RouterTap` ``gate.dattri_router``: the layer names the replicated-expert proxies
+of ``gradient/hooks/override_layers/fused_experts.py`` give a Hugging Face MoE block, so a
+store written under expert parallelism reads like one written with replicated experts.
+A capture manager hooks the taps like ``nn.Linear`` layers.  While a tap is hooked, the layer runs the two-stage
+all-to-all form (:class:`_UpA2A`, :class:`_DownA2A`): the owner returns each row's SwiGLU
+output to the source in the forward and its gate/up output gradient in the backward, so
+the source holds both factors of every expert projection for its own samples.  It feeds
+them to the taps as ``(B, T, d)`` tensors, zero at the tokens not routed to the expert,
+the layout the replicated path regroups its rows into.  Rows carry their slot index, so
+no row fingerprinting is needed.  The same form runs on CPU over gloo, or whenever the
+fused kernels do not apply (any dtype other than bf16).
 """
 
 from __future__ import annotations
@@ -30,6 +44,225 @@ import torch.nn.functional as F
 from torch import nn
 
 from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
+
+
+class ExpertTap(nn.Module):
+    """Capture stand-in for one expert projection ``(out_features, in_features)``.
+
+    Its forward takes the projection's input at this rank's tokens (a ``(..., in)`` tensor,
+    zero where the token was not routed to the expert) and returns a stride-0 zero tensor
+    ``(..., out)`` whose gradient the expert-parallel backward sets to the projection's
+    output gradient at those tokens.  The expert's weight lives on its owner rank, so the
+    tap holds none; it is captured like a linear layer without bias, frozen or not.
+    """
+
+    __bw_layer_type__ = "nn.Linear"
+    __bw_capture_tap__ = True
+    __bw_capture_frozen__ = True
+    bias = None
+
+    def __init__(self, in_features: int, out_features: int) -> None:
+        super().__init__()
+        self.in_features, self.out_features = in_features, out_features
+
+    def hooked(self) -> bool:
+        """Whether a capture hook is installed on this tap."""
+        return bool(self._forward_hooks or self._forward_pre_hooks)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        anchor = torch.zeros((), dtype=x.dtype, device=x.device, requires_grad=True)
+        return _TapOut.apply(anchor, tuple(x.shape[:-1]) + (self.out_features,))
+
+
+class RouterTap(nn.Module):
+    """The router's linear map as a hookable layer: ``F.linear`` on the owning router's
+    weight (no parameter of its own), captured like ``nn.Linear`` when that weight trains."""
+
+    __bw_layer_type__ = "nn.Linear"
+    __bw_capture_tap__ = True
+    bias = None
+
+    def __init__(self, router: nn.Module) -> None:
+        super().__init__()
+        object.__setattr__(self, "_router", router)  # not a submodule: no parameter duplication
+
+    @property
+    def weight(self) -> torch.Tensor:
+        """The router's ``(E, H)`` weight."""
+        return self._router.weight
+
+    def proxied_parameters(self):
+        """The router weight this tap reads."""
+        yield self._router.weight
+
+    def hooked(self) -> bool:
+        """Whether a capture hook is installed on this tap."""
+        return bool(self._forward_hooks or self._forward_pre_hooks)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x, self._router.weight)
+
+
+class _Router(nn.Module):
+    """Router weight ``(E, H)`` (state-dict key ``gate.weight``, as in Hugging Face MoE
+    blocks) applied through its :class:`RouterTap` ``dattri_router``."""
+
+    def __init__(self, hidden: int, n_experts: int, device, dtype) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.zeros(n_experts, hidden, device=device, dtype=dtype))
+        self.dattri_router = RouterTap(self)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.dattri_router(x)
+
+
+class _ExpertTaps(nn.Module):
+    """Container of the experts' taps, so their names are ``experts.dattri_experts.<e>.*``:
+    the names the replicated-expert capture gives the same projections."""
+
+    def __init__(self, n_experts: int, hidden: int, intermediate: int) -> None:
+        super().__init__()
+        self.dattri_experts = nn.ModuleList([nn.ModuleDict({
+            "gate_up": ExpertTap(hidden, 2 * intermediate),
+            "down": ExpertTap(intermediate, hidden),
+        }) for _ in range(n_experts)])
+
+
+class _TapOut(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, anchor, shape):
+        return anchor.new_zeros(()).expand(shape)
+
+    @staticmethod
+    def backward(ctx, grad):
+        return None, None
+
+
+class _A2APlan:
+    """Routing of one layer call for the all-to-all form: slots sorted by owner rank,
+    per-rank row counts both ways (one small all-to-all plus a host read), and each
+    received row's local expert."""
+
+    def __init__(self, topi: torch.Tensor, mod: ExpertParallelMoE) -> None:
+        self.t, self.k = topi.shape
+        self.group, self.world = mod.group, mod.world
+        e_l = mod.experts_per_rank
+        flat = topi.reshape(-1)
+        owner = torch.div(flat, e_l, rounding_mode="floor")
+        self.order = torch.argsort(owner, stable=True)
+        send = torch.bincount(owner, minlength=self.world)
+        recv = send.clone()
+        if self.world > 1:
+            dist.all_to_all_single(recv, send, group=self.group)
+        self.send, self.recv = send.tolist(), recv.tolist()
+        self.local_expert = self.to_owner((flat[self.order] % e_l).contiguous())
+        self.experts_per_rank = e_l
+        self.flat = flat
+
+    def to_owner(self, rows: torch.Tensor) -> torch.Tensor:
+        """Rows in this rank's send order -> the rows every source sent to this rank."""
+        if self.world == 1:
+            return rows
+        out = rows.new_empty((sum(self.recv),) + tuple(rows.shape[1:]))
+        dist.all_to_all_single(out, rows.contiguous(), self.recv, self.send, group=self.group)
+        return out
+
+    def to_source(self, rows: torch.Tensor) -> torch.Tensor:
+        """Owner rows back to their sources, in each source's send order."""
+        if self.world == 1:
+            return rows
+        out = rows.new_empty((sum(self.send),) + tuple(rows.shape[1:]))
+        dist.all_to_all_single(out, rows.contiguous(), self.send, self.recv, group=self.group)
+        return out
+
+    def to_slots(self, rows: torch.Tensor) -> torch.Tensor:
+        """Rows in send order -> ``(t*k, ...)`` in slot order."""
+        out = torch.empty_like(rows)
+        out[self.order] = rows
+        return out
+
+    def expert_mm(self, x: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+        """``x[r] @ weights[local_expert[r]].T`` for every received row."""
+        out = x.new_empty(x.shape[0], weights.shape[1])
+        for e in range(self.experts_per_rank):
+            idx = (self.local_expert == e).nonzero().squeeze(1)
+            if idx.numel():
+                out[idx] = x[idx] @ weights[e].t()
+        return out
+
+    def tap_grads(self, hit: list[int], slot_rows: torch.Tensor, lead: tuple[int, ...]) -> list[torch.Tensor]:
+        """Per hit expert, *slot_rows* at its tokens scattered into a zero ``(*lead, d)``."""
+        out = []
+        for e in hit:
+            sel = (self.flat == e).nonzero().squeeze(1)
+            g = slot_rows.new_zeros(self.t, slot_rows.shape[1])
+            g[torch.div(sel, self.k, rounding_mode="floor")] = slot_rows[sel]
+            out.append(g.view(*lead, slot_rows.shape[1]))
+        return out
+
+
+def _swiglu(h: torch.Tensor) -> torch.Tensor:
+    g, u = h.float().chunk(2, -1)
+    return (F.silu(g) * u).to(h.dtype)
+
+
+def _swiglu_bwd(da: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    g, u = h.float().chunk(2, -1)
+    d = da.float()
+    s = torch.sigmoid(g)
+    return torch.cat([d * u * s * (1 + g * (1 - s)), d * g * s], -1).to(h.dtype)
+
+
+class _UpA2A(torch.autograd.Function):
+    """Dispatch, gate/up projection and SwiGLU at the owners; returns every slot's SwiGLU
+    output to its source: ``(t*k, I)`` in slot order."""
+
+    @staticmethod
+    def forward(ctx, x2, plan, mod, hit, lead, *taps):
+        rows = plan.to_owner(x2[torch.div(plan.order, plan.k, rounding_mode="floor")])
+        h = plan.expert_mm(rows, mod.gate_up)
+        act = plan.to_slots(plan.to_source(_swiglu(h)))
+        ctx.plan, ctx.mod, ctx.hit, ctx.lead = plan, mod, hit, lead
+        ctx.save_for_backward(h)
+        return act
+
+    @staticmethod
+    def backward(ctx, d_act):
+        plan, mod = ctx.plan, ctx.mod
+        (h,) = ctx.saved_tensors
+        d_rows = plan.to_owner(d_act.to(h.dtype)[plan.order])
+        dh = _swiglu_bwd(d_rows, h)
+        d_in = plan.expert_mm(dh, mod.gate_up_t)
+        hidden = d_in.shape[1]
+        back = plan.to_slots(plan.to_source(torch.cat([d_in, dh], 1) if ctx.hit else d_in))
+        dx2 = back[:, :hidden].reshape(plan.t, plan.k, hidden).sum(1)
+        taps = plan.tap_grads(ctx.hit, back[:, hidden:], ctx.lead) if ctx.hit else []
+        return (dx2, None, None, None, None, *taps)
+
+
+class _DownA2A(torch.autograd.Function):
+    """Down projection at the owners, rows returned to their sources and combined with
+    the router weights: ``y (t, H)``."""
+
+    @staticmethod
+    def forward(ctx, act, topv, plan, mod, hit, lead, *taps):
+        out = plan.to_slots(plan.to_source(plan.expert_mm(plan.to_owner(act[plan.order]), mod.down)))
+        w = topv.float()
+        y = (out.view(plan.t, plan.k, -1).float() * w[..., None]).sum(1).to(act.dtype)
+        ctx.plan, ctx.mod, ctx.hit, ctx.lead = plan, mod, hit, lead
+        ctx.save_for_backward(out, w)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        plan, mod = ctx.plan, ctx.mod
+        out, w = ctx.saved_tensors
+        dyf = dy.float()
+        d_slot = (dyf[:, None, :] * w[..., None]).reshape(plan.t * plan.k, -1).to(out.dtype)
+        d_topv = (out.view(plan.t, plan.k, -1).float() * dyf[:, None, :]).sum(-1)
+        d_act = plan.to_slots(plan.to_source(plan.expert_mm(plan.to_owner(d_slot[plan.order]), mod.down_t)))
+        taps = plan.tap_grads(ctx.hit, d_slot, ctx.lead) if ctx.hit else []
+        return (d_act, d_topv, None, None, None, None, *taps)
 
 
 class _EPMoE(torch.autograd.Function):
@@ -152,58 +385,156 @@ class _Buffers:
 
 class ExpertParallelMoE(nn.Module):
     """Top-k MoE MLP with experts sharded over the process group (frozen experts: the
-    attribution probe's case; the router may train).  Build collectively."""
+    attribution probe's case; the router may train).  Build collectively.
+
+    On CUDA in bf16 the forward is the fused peer-memory path above; while any of its
+    ``experts.dattri_experts`` taps is hooked for capture, and on other devices or dtypes, it is
+    the two-stage all-to-all form (``torch.distributed`` all-to-all, any backend)."""
 
     def __init__(self, hidden: int, intermediate: int, n_experts: int, top_k: int, *, max_tokens: int,
-                 norm_topk_prob: bool = False, group=None, device: torch.device | None = None) -> None:
+                 norm_topk_prob: bool = False, group=None, device: torch.device | None = None,
+                 dtype: torch.dtype = torch.bfloat16) -> None:
         super().__init__()
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if n_experts % self.world:
             raise ValueError(f"{n_experts} experts do not split over {self.world} ranks")
         if hidden % 8 or intermediate % 8:
             raise ValueError("hidden and intermediate sizes must be multiples of 8")
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev = torch.device(dev)
         self.hidden, self.intermediate, self.n_experts, self.top_k = hidden, intermediate, n_experts, top_k
         self.experts_per_rank = n_experts // self.world
         self.norm_topk_prob = norm_topk_prob
         self.max_tokens = max_tokens
         self.capacity = self.world * max_tokens * top_k
-        self.gate = nn.Linear(hidden, n_experts, bias=False, device=dev, dtype=torch.bfloat16)
+        self.dtype = dtype
+        self.fused = dev.type == "cuda" and dtype == torch.bfloat16
+        self.gate = _Router(hidden, n_experts, dev, dtype)
         e_l = self.experts_per_rank
-        self.register_buffer("gate_up", torch.zeros(e_l, 2 * intermediate, hidden, device=dev, dtype=torch.bfloat16))
-        self.register_buffer("down", torch.zeros(e_l, hidden, intermediate, device=dev, dtype=torch.bfloat16))
-        self.register_buffer("gate_up_t", torch.zeros(e_l, hidden, 2 * intermediate, device=dev, dtype=torch.bfloat16))
-        self.register_buffer("down_t", torch.zeros(e_l, intermediate, hidden, device=dev, dtype=torch.bfloat16))
-        bufs = _Buffers.get(self.capacity, max_tokens * top_k, hidden, dev, group)
-        self.recv_x, self.recv_meta = bufs.recv_x, bufs.recv_meta
-        self.combine, self.dx_slots, self.barrier = bufs.combine, bufs.dx_slots, bufs.barrier
+        self.register_buffer("gate_up", torch.zeros(e_l, 2 * intermediate, hidden, device=dev, dtype=dtype))
+        self.register_buffer("down", torch.zeros(e_l, hidden, intermediate, device=dev, dtype=dtype))
+        self.register_buffer("gate_up_t", torch.zeros(e_l, hidden, 2 * intermediate, device=dev, dtype=dtype))
+        self.register_buffer("down_t", torch.zeros(e_l, intermediate, hidden, device=dev, dtype=dtype))
+        self.experts = _ExpertTaps(n_experts, hidden, intermediate)
+        self._taps = [t for pair in self.experts.dattri_experts for t in pair.values()]
+        if self.fused:
+            bufs = _Buffers.get(self.capacity, max_tokens * top_k, hidden, dev, group)
+            self.recv_x, self.recv_meta = bufs.recv_x, bufs.recv_meta
+            self.combine, self.dx_slots, self.barrier = bufs.combine, bufs.dx_slots, bufs.barrier
+
+    @property
+    def dattri_experts(self) -> nn.ModuleList:
+        """The per-expert ``{"gate_up", "down"}`` taps."""
+        return self.experts.dattri_experts
 
     @torch.no_grad()
     def load_experts(self, gate_up_all: torch.Tensor, down_all: torch.Tensor, router: torch.Tensor) -> None:
         """Take this rank's slice of the full ``(E, 2I, H)`` / ``(E, H, I)`` expert weights and
         the ``(E, H)`` router weight (identical on every rank)."""
         e_l, r = self.experts_per_rank, self.rank
-        gu = gate_up_all[r * e_l:(r + 1) * e_l].to(self.gate_up.device, torch.bfloat16)
-        dn = down_all[r * e_l:(r + 1) * e_l].to(self.down.device, torch.bfloat16)
+        gu = gate_up_all[r * e_l:(r + 1) * e_l].to(self.gate_up.device, self.dtype)
+        dn = down_all[r * e_l:(r + 1) * e_l].to(self.down.device, self.dtype)
         self.gate_up.copy_(gu)
         self.down.copy_(dn)
         self.gate_up_t.copy_(gu.transpose(1, 2))
         self.down_t.copy_(dn.transpose(1, 2))
-        self.gate.weight.copy_(router.to(self.gate.weight.device, torch.bfloat16))
+        self.gate.weight.copy_(router.to(self.gate.weight.device, self.dtype))
 
-    def route(self, x2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """``(top-k probabilities, top-k expert ids)`` of every token."""
-        probs = torch.softmax(self.gate(x2).float(), dim=-1)
+    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(top-k probabilities, top-k expert ids)`` of every token, flattened to ``(t, k)``.
+
+        The router runs on *x* in its own shape, so a capture hook on ``gate`` sees the
+        ``(B, T, H)`` layout of the samples."""
+        probs = torch.softmax(self.gate(x).float().reshape(-1, self.n_experts), dim=-1)
         topv, topi = probs.topk(self.top_k, dim=-1)
         if self.norm_topk_prob:
             topv = topv / topv.sum(-1, keepdim=True)
         return topv, topi
 
+    def capturing(self) -> bool:
+        """Whether a gradient will be captured through the expert taps on this call."""
+        return torch.is_grad_enabled() and any(t._forward_hooks for t in self._taps)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
-        x2 = x.reshape(-1, self.hidden).to(torch.bfloat16).contiguous()
-        topv, topi = self.route(x2)
-        y = _EPMoE.apply(x2, topv, topi, self)
+        xd = x.to(self.dtype)
+        topv, topi = self.route(xd)
+        x2 = xd.reshape(-1, self.hidden).contiguous()
+        if self.fused and not self.capturing():
+            y = _EPMoE.apply(x2, topv, topi, self)
+        else:
+            y = self._all_to_all(x2, topv, topi, tuple(shape[:-1]))
         return y.view(*shape[:-1], self.hidden)
+
+    def _all_to_all(self, x2, topv, topi, lead):
+        plan = _A2APlan(topi, self)
+        hit = sorted(set(topi.reshape(-1).tolist())) if self.capturing() else []
+        # The taps run under grad mode (their hooks record only then); their inputs do not
+        # require grad.
+        up_taps = [self.dattri_experts[e]["gate_up"](self._tap_input(x2, plan, e, lead)) for e in hit]
+        act = _UpA2A.apply(x2, plan, self, hit, lead, *up_taps)
+        down_taps = [self.dattri_experts[e]["down"](self._tap_input(act, plan, e, lead, slots=True)) for e in hit]
+        return _DownA2A.apply(act, topv, plan, self, hit, lead, *down_taps)
+
+    @staticmethod
+    @torch.no_grad()
+    def _tap_input(rows_src, plan, e, lead, slots=False):
+        """Expert *e*'s projection input at this rank's tokens, zero elsewhere: from token
+        rows (``slots=False``) or from slot rows."""
+        sel = (plan.flat == e).nonzero().squeeze(1)
+        tok = torch.div(sel, plan.k, rounding_mode="floor")
+        out = rows_src.new_zeros(plan.t, rows_src.shape[1])
+        out[tok] = rows_src[sel if slots else tok]
+        return out.view(*lead, rows_src.shape[1])
+
+
+def _is_silu(act: object) -> bool:
+    return isinstance(act, nn.SiLU) or "silu" in type(act).__name__.lower()
+
+
+def expert_parallelize(model: nn.Module, *, max_tokens: int, group=None, device: torch.device | None = None,
+                       dtype: torch.dtype | None = None) -> list[str]:
+    """Replace every Hugging Face fused-experts MoE block of *model* (a ``gate`` router with an
+    ``(E, H)`` weight next to ``experts`` holding ``gate_up_proj (E, 2I, H)`` /
+    ``down_proj (E, H, I)`` with a SiLU gate, e.g. OLMoE's sparse MoE block) by an
+    :class:`ExpertParallelMoE` holding this rank's experts.  Call collectively, with the
+    same weights on every rank.  Returns the replaced blocks' names.
+
+    Raises:
+        ValueError: for a block whose experts are transposed, carry biases or use another
+            activation, or a router without ``top_k``.
+    """
+    from dattri_llm_b200.gradient.hooks.override_layers.fused_experts import DOWN, GATE_UP, is_fused_experts
+
+    replaced = []
+    for name, block in list(model.named_modules()):
+        experts, router = getattr(block, "experts", None), getattr(block, "gate", None)
+        if experts is None or router is None or not is_fused_experts(experts):
+            continue
+        gu, dn = getattr(experts, GATE_UP), getattr(experts, DOWN)
+        n_exp, two_i, hidden = gu.shape
+        w = getattr(router, "weight", None)
+        if not isinstance(w, torch.Tensor) or tuple(w.shape) != (n_exp, hidden):
+            continue
+        if getattr(experts, "is_transposed", False) or getattr(experts, "has_bias", False):
+            raise ValueError(f"{name}: transposed or biased experts are not supported under expert parallelism")
+        if not _is_silu(getattr(experts, "act_fn", None)):
+            raise ValueError(f"{name}: expert parallelism implements the SiLU-gated (SwiGLU) experts only")
+        top_k = getattr(router, "top_k", None)
+        if top_k is None:
+            raise ValueError(f"{name}: the router does not say its top_k")
+        ep = ExpertParallelMoE(hidden, two_i // 2, n_exp, int(top_k), max_tokens=max_tokens,
+                               norm_topk_prob=bool(getattr(router, "norm_topk_prob", False)), group=group,
+                               device=device if device is not None else gu.device,
+                               dtype=dtype if dtype is not None else gu.dtype)
+        ep.load_experts(gu.detach(), dn.detach(), w.detach())
+        ep.gate.weight.requires_grad_(w.requires_grad)
+        parent_name, _, child = name.rpartition(".")
+        parent = model.get_submodule(parent_name) if parent_name else None
+        if parent is None:
+            raise ValueError("the model itself is an MoE block; wrap it in a parent module")
+        setattr(parent, child, ep)
+        replaced.append(name)
+    return replaced

@@ -1,6 +1,7 @@
 """Peer-memory kernels on 2+ GPUs (one process per GPU, NCCL): the bounded cross-GPU
-barrier and the fused all-gather + score GEMM against NCCL all-gather + fp32 matmul.
-Skipped with fewer than two GPUs."""
+barrier and the fused all-gather + score GEMM against NCCL all-gather + fp32 matmul;
+expert parallelism (fused path, and per-sample capture over NCCL all-to-all against the
+replicated-expert capture).  Skipped with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -232,6 +233,68 @@ def test_expert_parallel_moe_matches_replicated():
         errs = dict(results)
     assert len(errs) == world
     assert max(errs.values()) < 3e-2, errs
+
+
+def _ep_capture_worker(rank: int, world: int, port: int, results) -> None:
+    import copy
+    import datetime
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import transformers
+
+        import dattri_llm_b200 as bw
+        from dattri_llm_b200.parallel.moe import expert_parallelize
+
+        cfg = transformers.OlmoeConfig(vocab_size=64, hidden_size=32, intermediate_size=16, num_hidden_layers=1,
+                                       num_attention_heads=4, num_key_value_heads=4, num_experts=4,
+                                       num_experts_per_tok=2, max_position_embeddings=64)
+        torch.manual_seed(0)
+        model = transformers.OlmoeForCausalLM(cfg).eval().to(dev)
+        ep_model = copy.deepcopy(model)
+        expert_parallelize(ep_model, max_tokens=64)  # fp32: the all-to-all form over NCCL
+        ids = torch.randint(0, 64, (3, 8), generator=torch.Generator().manual_seed(7 + rank)).to(dev)
+
+        def capture(m, **kw):
+            cap = bw.CaptureCallback()
+            hm = bw.HookManager(m, bw.HookManagerConfig(linear_io=[r"mlp"]), callbacks=[cap], **kw)
+            with hm.collect():
+                logits = m(input_ids=ids).logits
+                F.cross_entropy(logits[:, :-1].reshape(-1, 64).float(), ids[:, 1:].reshape(-1),
+                                reduction="sum").backward()
+            hm.remove()
+            return cap.record.gradient.materialize()
+
+        want = capture(model, moe_routed_layers=["model.layers.0.mlp"])
+        got = capture(ep_model)
+        worst = 0.0 if set(got.data) == set(want.data) else float("inf")
+        for n, v in want.data.items():
+            if n in got.data:
+                a, b = got.data[n].float().reshape(v.shape[0], -1), v.float().reshape(v.shape[0], -1)
+                worst = max(worst, float((a - b).abs().max() / b.abs().max().clamp_min(1e-12)))
+        torch.cuda.synchronize()
+        results[rank] = worst
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_capture_matches_replicated_over_nccl():
+    world = 2
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_ep_capture_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(errs.values()) < 1e-3, errs
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
