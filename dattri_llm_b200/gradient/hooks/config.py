@@ -199,6 +199,25 @@ def _warn_zero_layers() -> None:
     )
 
 
+def _tap_covered(modules: dict[str, nn.Module]) -> set[str]:
+    """Modules whose trainable parameters are all read by a capture tap (e.g. an
+    expert-parallel router's weight, captured per sample through its ``dattri_router``):
+    pattern and default selection give them no ``param_grad`` hook, which would count the
+    same weight twice."""
+    proxied: set[int] = set()
+    for m in modules.values():
+        if getattr(type(m), "__bw_capture_tap__", False) and hasattr(m, "proxied_parameters"):
+            proxied.update(id(p) for p in m.proxied_parameters())
+    if not proxied:
+        return set()
+    out = set()
+    for name, m in modules.items():
+        own = [p for _, p in m.named_parameters(recurse=False) if p.requires_grad]
+        if own and all(id(p) in proxied for p in own):
+            out.add(name)
+    return out
+
+
 def resolve_hook_assignments(root: nn.Module, config: HookManagerConfig) -> dict[str, str]:
     """The final ``{layer_name: hook_type}`` assignment of *config* on *root*.
 
@@ -218,11 +237,12 @@ def resolve_hook_assignments(root: nn.Module, config: HookManagerConfig) -> dict
             )
         assignment[name] = kind
 
+    covered = _tap_covered(modules)
     if config.is_default:
         for name, module in modules.items():
             if is_linear_io_capable(module):
                 assignment[name] = LINEAR_IO
-            elif has_trainable_params(module):
+            elif has_trainable_params(module) and name not in covered:
                 assignment[name] = PARAM_GRAD
         if not assignment:
             _warn_zero_layers()
@@ -249,7 +269,7 @@ def resolve_hook_assignments(root: nn.Module, config: HookManagerConfig) -> dict
     for name, module in modules.items():
         if is_linear_io_capable(module) and _matches(config.linear_io, name):
             assign(name, LINEAR_IO)
-        if has_trainable_params(module) and _matches(config.param_grad, name):
+        if has_trainable_params(module) and name not in covered and _matches(config.param_grad, name):
             assign(name, PARAM_GRAD)
         if is_invasive_capable(module) and _matches(config.invasive_linear_io, name):
             assign(name, INVASIVE_LINEAR_IO)
@@ -286,10 +306,11 @@ def default_hook_assignment(model: nn.Module, sample_input: object,
     root = getattr(model, "module", model)
     modules = dict(root.named_modules())
     candidate = {}
+    covered = _tap_covered(modules)
     for name, module in modules.items():
         if is_linear_io_capable(module):
             candidate[name] = LINEAR_IO
-        elif has_trainable_params(module):
+        elif has_trainable_params(module) and name not in covered:
             candidate[name] = PARAM_GRAD
     fired: set[str] = set()
     handles = []

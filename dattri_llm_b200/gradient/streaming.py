@@ -608,6 +608,13 @@ class GradientStreamer(GradientSource):
             if "offload" in tokens:
                 kw.setdefault("cpu_offload", CPUOffload(offload_params=True))
             return FSDP(model, **kw)
+        from dattri_llm_b200.parallel.moe import expert_parallel_buffers
+
+        # Expert-parallel layers hold a different expert shard on every rank: DDP must not
+        # broadcast rank 0's over them.
+        shards = expert_parallel_buffers(model)
+        if shards:
+            nn.parallel.DistributedDataParallel._set_params_and_buffers_to_ignore_for_model(model, shards)
         return nn.parallel.DistributedDataParallel(
             model, device_ids=[args.local_process_index] if args.device.type == "cuda" else None,
             find_unused_parameters=bool(args.ddp_find_unused_parameters))

@@ -538,3 +538,14 @@ def expert_parallelize(model: nn.Module, *, max_tokens: int, group=None, device:
         setattr(parent, child, ep)
         replaced.append(name)
     return replaced
+
+
+def expert_parallel_buffers(model: nn.Module) -> list[str]:
+    """Fully qualified names of the per-rank expert shards of every
+    :class:`ExpertParallelMoE` in *model*: buffers that differ by rank by design, which a
+    data-parallel wrapper must neither broadcast nor check for equality."""
+    out = []
+    for name, m in model.named_modules():
+        if isinstance(m, ExpertParallelMoE):
+            out += [f"{name}.{b}" if name else b for b, _ in m.named_buffers(recurse=False)]
+    return out

@@ -4,7 +4,9 @@ gradients, and its expert taps capture every sample's gradient of every expert's
 and down weights (owner-side factors returned to the source), equal to per-sample
 autograd on a dense replicated model.  A Hugging Face OLMoE model converted with
 ``expert_parallelize`` records the same layers, with the same values (raw and LoGra
-projected), as the replicated-expert capture of the original model."""
+projected), as the replicated-expert capture of the original model.  TracIn through the
+public API on two ranks (the streamer's DDP or FSDP wrapping, which must leave each rank's
+expert shard alone) gives the single-process scores."""
 
 from __future__ import annotations
 
@@ -125,6 +127,7 @@ def _check(rank: int) -> None:
                 continue
             _close(grad.data[name].reshape(B, -1), want_e, msg=name)
     assert any(n.startswith("moe.experts.dattri_experts.") for n in names)
+    assert "moe.gate" not in names  # the router weight is captured once, through its tap
     router = torch.stack([s["router"].reshape(-1) for s in per])
     _close(grad.data["moe.gate.dattri_router"].reshape(B, -1), router)
     fc = torch.stack([torch.cat([s["fc_w"], s["fc_b"][:, None]], 1).reshape(-1) for s in per])
@@ -176,12 +179,44 @@ def _check_olmoe(rank: int) -> None:
             _close(got.data[n].reshape(v.shape[0], -1), v.reshape(v.shape[0], -1), msg=n)
 
 
+class _SeqNet(_Net):
+    def forward(self, x, y=None):
+        return super().forward(x)
+
+
+def _ep_scores(fsdp: str = ""):
+    """TracIn scores of a model with an expert-parallel layer through the public API
+    (the streamer wraps it for data parallelism when a process group is up)."""
+    import tempfile
+
+    import dattri_llm_b200 as bw
+
+    g = torch.Generator().manual_seed(5)
+    xtr, ytr = torch.randn(8, T, D_IN, generator=g), torch.randn(8, generator=g)
+    xte, yte = torch.randn(3, T, D_IN, generator=g), torch.randn(3, generator=g)
+    model = _SeqNet(_weights())
+
+    def loss(m, batch):
+        return ((m(x=batch["x"], y=batch["y"]) - batch["y"]) ** 2).sum()
+
+    args = bw.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=2,
+                                   per_device_eval_batch_size=3, fsdp=fsdp)
+    att = bw.TracInAttributor(args, task=bw.AttributionTask(loss, model))
+    ds = [{"x": xtr[i], "y": ytr[i]} for i in range(8)]
+    ts = [{"x": xte[i], "y": yte[i]} for i in range(3)]
+    score = att.attribute(ds, ts, hook_config=bw.HookManagerConfig())
+    return {h: score.trajectory_agnostic(h) for h in score.train_ids}
+
+
 def _worker(rank, world, port, out):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         _check(rank)
         _check_olmoe(rank)
+        out[f"scores{rank}"] = _ep_scores()
+        out[f"fsdp{rank}"] = _ep_scores("full_shard")
         out[rank] = "ok"
     except Exception as e:  # surfaced in the parent
         import traceback
@@ -207,7 +242,13 @@ def test_two_ranks_gloo():
         out = m.dict()
         mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
         res = dict(out)
-    assert res == {0: "ok", 1: "ok"}, res
+    assert res[0] == "ok" and res[1] == "ok", res
+    want = _ep_scores()
+    for key in ("scores", "fsdp"):  # DDP, then FSDP full shard
+        merged = {**res[f"{key}0"], **res[f"{key}1"]}
+        assert set(merged) == set(want)
+        for h, row in want.items():
+            _close(merged[h], row, msg=key)
 
 
 def test_taps_are_not_hooked_outside_capture():
