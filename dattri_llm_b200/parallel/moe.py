@@ -140,13 +140,15 @@ class _TapOut(torch.autograd.Function):
 
 class _A2APlan:
     """Routing of one layer call for the all-to-all form: slots sorted by owner rank,
-    per-rank row counts both ways (one small all-to-all plus a host read), and each
-    received row's local expert."""
+    per-rank row counts both ways (one small all-to-all), received rows grouped by local
+    expert, and this rank's slots grouped by global expert.  All counts reach the host in
+    one read, so the per-expert loops below slice instead of synchronizing."""
 
     def __init__(self, topi: torch.Tensor, mod: ExpertParallelMoE) -> None:
         self.t, self.k = topi.shape
         self.group, self.world = mod.group, mod.world
         e_l = mod.experts_per_rank
+        n_exp = mod.n_experts
         flat = topi.reshape(-1)
         owner = torch.div(flat, e_l, rounding_mode="floor")
         self.order = torch.argsort(owner, stable=True)
@@ -155,9 +157,17 @@ class _A2APlan:
         if self.world > 1:
             dist.all_to_all_single(recv, send, group=self.group)
         self.send, self.recv = send.tolist(), recv.tolist()
-        self.local_expert = self.to_owner((flat[self.order] % e_l).contiguous())
-        self.experts_per_rank = e_l
-        self.flat = flat
+        local_expert = self.to_owner((flat[self.order] % e_l).contiguous())
+        # received rows grouped by local expert; this rank's slots grouped by global expert
+        self.by_expert = torch.argsort(local_expert, stable=True)
+        self.slots_by_expert = torch.argsort(flat, stable=True)
+        counts = torch.cat([torch.bincount(local_expert, minlength=e_l), torch.bincount(flat, minlength=n_exp)])
+        counts = counts.tolist()
+        self.rows_per_expert, self.slots_per_expert = counts[:e_l], counts[e_l:]
+        offs = [0]
+        for c in self.slots_per_expert:
+            offs.append(offs[-1] + c)
+        self.slot_offsets = offs
 
     def to_owner(self, rows: torch.Tensor) -> torch.Tensor:
         """Rows in this rank's send order -> the rows every source sent to this rank."""
@@ -181,20 +191,27 @@ class _A2APlan:
         out[self.order] = rows
         return out
 
+    def hit(self) -> list[int]:
+        """Global experts that received at least one of this rank's slots."""
+        return [e for e, c in enumerate(self.slots_per_expert) if c]
+
+    def expert_slots(self, e: int) -> torch.Tensor:
+        """Slot indices of this rank routed to global expert *e* (ascending)."""
+        return self.slots_by_expert[self.slot_offsets[e]:self.slot_offsets[e + 1]]
+
     def expert_mm(self, x: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
         """``x[r] @ weights[local_expert[r]].T`` for every received row."""
+        parts = x[self.by_expert].split(self.rows_per_expert)
+        y = torch.cat([part @ weights[e].t() for e, part in enumerate(parts)]) if parts else x.new_empty(0)
         out = x.new_empty(x.shape[0], weights.shape[1])
-        for e in range(self.experts_per_rank):
-            idx = (self.local_expert == e).nonzero().squeeze(1)
-            if idx.numel():
-                out[idx] = x[idx] @ weights[e].t()
+        out[self.by_expert] = y.view(x.shape[0], weights.shape[1])
         return out
 
     def tap_grads(self, hit: list[int], slot_rows: torch.Tensor, lead: tuple[int, ...]) -> list[torch.Tensor]:
         """Per hit expert, *slot_rows* at its tokens scattered into a zero ``(*lead, d)``."""
         out = []
         for e in hit:
-            sel = (self.flat == e).nonzero().squeeze(1)
+            sel = self.expert_slots(e)
             g = slot_rows.new_zeros(self.t, slot_rows.shape[1])
             g[torch.div(sel, self.k, rounding_mode="floor")] = slot_rows[sel]
             out.append(g.view(*lead, slot_rows.shape[1]))
@@ -470,7 +487,7 @@ class ExpertParallelMoE(nn.Module):
 
     def _all_to_all(self, x2, topv, topi, lead):
         plan = _A2APlan(topi, self)
-        hit = sorted(set(topi.reshape(-1).tolist())) if self.capturing() else []
+        hit = plan.hit() if self.capturing() else []
         # The taps run under grad mode (their hooks record only then); their inputs do not
         # require grad.
         up_taps = [self.dattri_experts[e]["gate_up"](self._tap_input(x2, plan, e, lead)) for e in hit]
@@ -483,7 +500,7 @@ class ExpertParallelMoE(nn.Module):
     def _tap_input(rows_src, plan, e, lead, slots=False):
         """Expert *e*'s projection input at this rank's tokens, zero elsewhere: from token
         rows (``slots=False``) or from slot rows."""
-        sel = (plan.flat == e).nonzero().squeeze(1)
+        sel = plan.expert_slots(e)
         tok = torch.div(sel, plan.k, rounding_mode="floor")
         out = rows_src.new_zeros(plan.t, rows_src.shape[1])
         out[tok] = rows_src[sel if slots else tok]
