@@ -18,6 +18,8 @@ import threading
 
 import torch
 
+from dattri_llm_b200.ops import checks as _checks
+
 _C = None
 _IMPORT_ERROR: Exception | None = None
 _LAUNCHES = [0]
@@ -31,12 +33,30 @@ def count_launch(n: int = 1) -> None:
 def launch_count() -> int:
     """Native kernels launched by this process so far."""
     return _LAUNCHES[0]
+
+
 _lock = threading.Lock()
 _err_words: dict[int, torch.Tensor] = {}
+_checked = None
 
 
 def native():
-    """The compiled extension module; raises with the build command if absent."""
+    """The compiled extension module; raises with the build command if absent.
+
+    With launch checks on (:func:`dattri_llm_b200.ops.checks.set_checks` or
+    ``DATTRI_B200_CHECKS=1``) the module comes wrapped so that the index arguments of
+    data-dependent launches are validated first.
+    """
+    global _checked
+    mod = _C if _C is not None else _load()
+    if not _checks.checks_enabled():
+        return mod
+    if _checked is None or _checked._module is not mod:
+        _checked = _checks.CheckedNative(mod)
+    return _checked
+
+
+def _load():
     global _C, _IMPORT_ERROR
     if _C is not None:
         return _C

@@ -141,10 +141,15 @@ def test_skinny_cluster_split_k(mode, m, n, k):
     ops.check_device_errors()
 
 
+@pytest.mark.parametrize("checked", [False, True])
 @pytest.mark.parametrize("scatter", [False, True])
-def test_gemm_ragged_expert_segments(scatter):
+def test_gemm_ragged_expert_segments(scatter, checked, monkeypatch):
     """Ragged grouped GEMM over expert row segments (empty and partial-tile segments
-    included), stored in place or scattered to rows of several destination buffers."""
+    included), stored in place or scattered to rows of several destination buffers; with
+    launch checks on, the validator accepts these tables and metadata."""
+    from dattri_llm_b200.ops import checks
+
+    monkeypatch.setattr(checks, "_enabled", checked)
     lens = [0, 130, 7, 256, 0, 61]
     n, kk = 192, 320
     rows = sum(lens)
