@@ -214,6 +214,10 @@ class KroneckerAttributor(BaseInnerProductAttributor):
         if streamer is not self._capture_streamer:
             return super().collect_gradients(streamer, store, **kwargs)
         self._capture_streamer = None
+        if kwargs.get("resume") and any(step == streamer.checkpoint_step for step, _ in store.own_records()):
+            # the skipped batches would be missing from covariances gathered now: the fit
+            # sweeps the completed store instead (or reads the file a finished run saved)
+            return super().collect_gradients(streamer, store, **kwargs)
         cb = KroneckerCovarianceCallback()
         streamer.hook_manager.add_callback(cb)
         result = super().collect_gradients(streamer, store, **kwargs)

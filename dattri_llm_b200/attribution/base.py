@@ -146,9 +146,11 @@ class BaseInnerProductAttributor(BaseAttributor):
                                   desc=desc if desc is not None else f"{self.algorithm}: test", verbose=verbose)
 
     # ------------------------------------------------------------ collection
-    def collect_gradients(self, streamer, store, *, offload_interval: int = 1, on_block=None):
-        """Run *streamer* into *store*."""
-        return collect_gradients(streamer, store, offload_interval=offload_interval, on_block=on_block)
+    def collect_gradients(self, streamer, store, *, offload_interval: int = 1, on_block=None,
+                          resume: bool = False):
+        """Run *streamer* into *store* (*resume*: skip the batches already stored)."""
+        return collect_gradients(streamer, store, offload_interval=offload_interval, on_block=on_block,
+                                 resume=resume)
 
     def cache_representations(self, source, store, *, transform=None, sample_id_key=None):
         """Persist ``transform(block)`` (materialized) for every block of *source*."""
@@ -159,8 +161,13 @@ class BaseInnerProductAttributor(BaseAttributor):
         return store
 
     def cache(self, train_dataset, test_dataset, *, cache_dir: str | None = None, hook_config=None,
-              enable_update: bool = False, on_train_block=None) -> list[tuple[str, str]]:
-        """Collect test then train gradients per checkpoint into ``<cache_dir>/ckpt_<k>/``."""
+              enable_update: bool = False, on_train_block=None, resume: bool = False) -> list[tuple[str, str]]:
+        """Collect test then train gradients per checkpoint into ``<cache_dir>/ckpt_<k>/``.
+
+        *resume* continues an interrupted run in the same *cache_dir*: batches already
+        stored are skipped (frozen probes only)."""
+        if resume and enable_update:
+            raise ValueError("resume=True needs a frozen probe (enable_update=False).")
         self.require_task("cache")
         cache_dir = cache_dir if cache_dir is not None else self.args.output_dir
         pairs = []
@@ -169,10 +176,10 @@ class BaseInnerProductAttributor(BaseAttributor):
             root = Path(cache_dir) / f"ckpt_{k}"
             train_dir, test_dir = str(root / "train_grads"), str(root / "test_grads")
             self.collect_gradients(self.generate_test_rep(test_dataset, checkpoint_step=k, hook_config=hook_config,
-                                                          shard=False), GradientStorageManager(test_dir))
+                                                          shard=False), GradientStorageManager(test_dir), resume=resume)
             self.collect_gradients(self.generate_train_rep(train_dataset, checkpoint_step=k,
                                                            enable_update=enable_update, hook_config=hook_config),
-                                   GradientStorageManager(train_dir), on_block=on_train_block)
+                                   GradientStorageManager(train_dir), on_block=on_train_block, resume=resume)
             pairs.append((train_dir, test_dir))
             if enable_update:
                 break

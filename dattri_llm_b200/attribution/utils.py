@@ -44,11 +44,21 @@ def normalize_layer_names(layer_name: str | list[str] | None) -> list[str] | Non
 
 
 def collect_gradients(streamer, store, *, offload_interval: int = 1, on_block=None,
-                      async_write: bool | None = None):
+                      async_write: bool | None = None, resume: bool = False):
     """Run *streamer* to completion into *store* (groups of *offload_interval* steps;
-    asynchronous writes per ``args.async_disk_write``)."""
+    asynchronous writes per ``args.async_disk_write``).
+
+    With *resume*, a collection that was interrupted picks up where it stopped: the
+    batches whose records this rank already wrote for the streamer's checkpoint (whole
+    groups; a group whose index line was cut off is redone) are skipped, checked against
+    the stored hashes, and the rest are appended.  Frozen probes only.
+    """
     if offload_interval < 1:
         raise ValueError(f"offload_interval must be >= 1, got {offload_interval}.")
+    if resume:
+        done = [h for step, h in store.own_records() if step == streamer.checkpoint_step]
+        if done:
+            streamer.skip_batches(len(done), expected_hashes=done)
     if async_write is None:
         async_write = getattr(getattr(streamer, "args", None), "async_disk_write", False)
     writer = None

@@ -6,7 +6,8 @@ so stores are interchangeable):
 * one directory per rank under distributed execution (``rank_<r>/``);
 * ``index.jsonl``: an append-only log, one JSON line per written group
   ``{"file": <rel path>, "records": [{"idx", "step", "hashes": [...]}, ...]}``;
-  a truncated last line (a crash mid-write) is ignored on read;
+  a line cut off by a crash mid-write is ignored on read, and the next append starts
+  on a new line;
 * ``index_meta.json``: ``{"format": 2, "sample_id_key", "gradient_accumulation_steps"}``;
 * groups ``batch_<n>.mmap.bin`` (raw tensor bytes, each part 8-byte aligned) +
   ``batch_<n>.mmap.meta`` (``torch.save`` of ``{"format": 2, "records": [...]}`` with
@@ -494,6 +495,26 @@ class GradientStorageManager:
         """``{identifier: [{"file", "idx", "step", "sample_idx"}]}``."""
         return self._index
 
+    def own_records(self) -> list[tuple[int, list[str]]]:
+        """``(step, hashes)`` of every record in this process's own directory (``rank_<r>/``
+        under distributed execution), in the order they were written.  A group counts only
+        once its index line is complete, so after a crash this lists whole groups."""
+        log = self._ensure_save_dir() / self._INDEX_LOG_FILE
+        out: list[tuple[int, list[str]]] = []
+        if not log.exists():
+            return out
+        with log.open(encoding="utf-8") as f:
+            for line in f:
+                line = line.strip()
+                if not line:
+                    continue
+                try:
+                    payload = json.loads(line)
+                except json.JSONDecodeError:
+                    continue  # cut off by a crash mid-write
+                out += [(int(r["step"]), [str(h) for h in r["hashes"]]) for r in payload["records"]]
+        return out
+
     def _read_all_indexes(self) -> dict[str, list[dict]]:
         merged: dict[str, list[dict]] = {}
         for d in [self._root] + [d for d in sorted(self._root.glob("rank_*")) if d.is_dir()]:
@@ -517,9 +538,10 @@ class GradientStorageManager:
                 try:
                     payload = json.loads(line)
                 except json.JSONDecodeError:
-                    warnings.warn(f"Ignoring a truncated final line in {log} -- the records it "
+                    # a line cut off by a crash mid-write (the next append starts a new line)
+                    warnings.warn(f"Ignoring a truncated line in {log} -- the records it "
                                   "described are not indexed.", stacklevel=2)
-                    break
+                    continue
                 _merge_index(merged, _expand_log_line(payload))
 
     def _persist_index(self, records, loc: str) -> None:
@@ -544,8 +566,14 @@ class GradientStorageManager:
             {"idx": i, "step": r.step,
              "hashes": [str(h) for h in (r.input_hash if isinstance(r.input_hash, list) else [r.input_hash])]}
             for i, r in enumerate(records)]}
-        with (d / self._INDEX_LOG_FILE).open("a", encoding="utf-8") as f:
-            f.write(json.dumps(line, separators=(",", ":")) + "\n")
+        log = d / self._INDEX_LOG_FILE
+        torn = False
+        if log.exists() and log.stat().st_size:
+            with log.open("rb") as f:
+                f.seek(-1, 2)
+                torn = f.read(1) != b"\n"  # a line cut off by a crash: end it first
+        with log.open("a", encoding="utf-8") as f:
+            f.write(("\n" if torn else "") + json.dumps(line, separators=(",", ":")) + "\n")
             f.flush()
 
     def _compute_next_batch_id(self) -> int:

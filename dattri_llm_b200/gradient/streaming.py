@@ -337,11 +337,54 @@ class GradientStreamer(GradientSource):
         self._pass_state: _ProbePassState | None = None
         self._hasher: ThreadPoolExecutor | None = None
         self._host_ids_ok: bool | None = None  # host batch hash == manager's model-input hash
+        self._skip_pending: tuple[int, list[list[str]] | None] = (0, None)
+        self._skip_left = 0
+        self._skip_expected: list[list[str]] | None = None
+        self._skip_mismatch: int | None = None
 
     args = property(lambda self: self._args, doc="The run configuration.")
     model = property(lambda self: self._model, doc="The unwrapped model.")
     forward_model = property(lambda self: self._fwd, doc="The model the forward runs on (wrapper if any).")
     hook_manager = property(lambda self: self._hm, doc="The capture manager.")
+    checkpoint_step = property(lambda self: self._checkpoint_step,
+                               doc="The step a frozen probe stamps on its records.")
+
+    def skip_batches(self, n: int, expected_hashes: list[list[str]] | None = None) -> None:
+        """Skip the first *n* batches of the next pass: resuming a collection whose first
+        *n* batches are already stored.  The skipped batches are read from the loader (so
+        the order stays the same) but not run.  With *expected_hashes* (the stored records'
+        hashes, one list per batch) each skipped batch is checked against its record, and
+        a batch that differs raises once the first computed step shows that the host
+        batch's hash is the model inputs' hash.
+
+        Raises:
+            ValueError: on a trajectory stream (``enable_update=True``), whose later steps
+                depend on the skipped updates.
+        """
+        if n < 0:
+            raise ValueError(f"n must be >= 0, got {n}.")
+        if n and self.enable_update:
+            raise ValueError("Only a frozen probe can resume: a trajectory's later steps depend on the "
+                             "updates of the skipped ones.")
+        self._skip_pending = (int(n), expected_hashes)
+
+    def _skip_one(self, host_batch) -> None:
+        i = self._index
+        expected = self._skip_expected
+        if expected is not None and i < len(expected) and self._skip_mismatch is None:
+            key = self._hm.sample_id_key
+            if key is not None and isinstance(host_batch, dict) and key in host_batch:
+                ids = host_batch[key]
+                got = [str(v) for v in (ids.tolist() if isinstance(ids, torch.Tensor) else list(ids))]
+                if got != expected[i]:
+                    raise RuntimeError(f"Cannot resume: batch {i}'s {key!r} values differ from the stored "
+                                       "record; the loader's order changed since the collection began.")
+            else:
+                hashable = _host_hashable(host_batch)
+                if hashable and hash_batch(hashable) != expected[i]:
+                    self._skip_mismatch = i
+        self._index += 1
+        self._skip_left -= 1
 
     @property
     def reusable(self) -> bool:
@@ -420,6 +463,9 @@ class GradientStreamer(GradientSource):
             raise RuntimeError("This streamer is single-shot (enable_update=True) and was already consumed; "
                                "the training trajectory cannot be replayed.")
         self._update_pending = False
+        self._skip_left, self._skip_expected = self._skip_pending
+        self._skip_pending = (0, None)
+        self._skip_mismatch = None
         if not self.enable_update:
             self._end_probe_pass()
             self._pass_state = _ProbePassState(self._model, self._fwd)
@@ -443,6 +489,9 @@ class GradientStreamer(GradientSource):
             self._optimizer_step()
         try:
             host_batch = next(self._it)
+            while self._skip_left > 0:
+                self._skip_one(host_batch)
+                host_batch = next(self._it)
         except StopIteration:
             self._end_probe_pass()
             raise
@@ -496,6 +545,9 @@ class GradientStreamer(GradientSource):
         hashes = list(record.input_hash) if isinstance(record.input_hash, list) else [record.input_hash]
         if self._host_ids_ok is None and host_ids is not None:
             self._host_ids_ok = list(host_ids) == hashes
+        if self._skip_mismatch is not None and self._host_ids_ok:
+            raise RuntimeError(f"Cannot resume: skipped batch {self._skip_mismatch} differs from its stored "
+                               "record; the loader's order changed since the collection began.")
         if self._pass_state is not None and not self._pass_state.holds_grads and self._any_trainable:
             self._fwd.zero_grad(set_to_none=True)
         step = self._index if self.enable_update else self._checkpoint_step
