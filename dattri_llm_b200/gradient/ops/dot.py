@@ -130,14 +130,46 @@ def pairwise_dot_factors(a, g, layer_type, module_kwargs=None, include_bias: boo
     return cross_gram(a, g, a, g, layer_type, mode)
 
 
+# Bound on the (B1*T1, D*K) per-token outer products of the native per-token gram.
+_TOKEN_OUTER_ELEMS = 1 << 27
+
+
+def _per_token_gram_native(a1: torch.Tensor, g1: torch.Tensor, m2: torch.Tensor) -> torch.Tensor:
+    """``K[i, t, j] = <g1_it a1_it^T, M2_j>`` for bf16 ``a1 (B, T, K)``, ``g1 (B, T, D)`` and
+    side 2 dense ``m2 (C, D*K)`` in the materialized ``(out, in)`` layout: every token's
+    outer product is one row of a tcgen05 GEMM against ``m2`` (fp32 accumulate), chunked
+    over tokens so the outer products stay within a bounded buffer."""
+    from dattri_llm_b200 import ops as native_ops
+
+    b, t, k = a1.shape
+    d = g1.shape[-1]
+    rows_a, rows_g = a1.reshape(b * t, k), g1.reshape(b * t, d)
+    m2 = m2.reshape(m2.shape[0], d * k).to(torch.bfloat16).contiguous()
+    out = torch.empty(b * t, m2.shape[0], dtype=torch.float32, device=a1.device)
+    step = max(1, _TOKEN_OUTER_ELEMS // (d * k))
+    for s in range(0, b * t, step):
+        outer = (rows_g[s:s + step].unsqueeze(-1) * rows_a[s:s + step].unsqueeze(-2)).reshape(-1, d * k)
+        out[s:s + step] = native_ops.matmul_tn(outer, m2, out_dtype=torch.float32)
+    return out.view(b, t, -1)
+
+
 def cross_gram_per_token(a1, g1, a2, g2, layer_type: str) -> torch.Tensor:
-    """``K[i, t, j]``: side-1 token ``t``'s share of ``<dW1_i, dW2_j>`` (sums to the gram)."""
+    """``K[i, t, j]``: side-1 token ``t``'s share of ``<dW1_i, dW2_j>`` (sums to the gram).
+
+    On sm_100 with bf16 factors the linear-family contraction runs on the tensor cores
+    (:func:`_per_token_gram_native`), side 2 summed over its tokens by the per-sample
+    outer-product GEMM first."""
     if is_embedding(layer_type):
         return _embedding_gram(a1, g1, a2, g2, per_token=True)
     a1, g1, a2, g2 = dtypes.align(a1, g1, a2, g2)
     a1, g1, a2, g2 = to_3d(a1), to_3d(g1), to_3d(a2), to_3d(g2)
     if is_norm(layer_type):
         return torch.einsum("btd,cd->btc", a1 * g1, (a2 * g2).sum(1))
+    if a1.ndim == 3 and _native(a1, g1, a2, g2):
+        from dattri_llm_b200 import ops as native_ops
+
+        m2 = native_ops.per_sample_outer(g2, a2, out_dtype=torch.bfloat16)  # (C, D, K) = g2^T a2
+        return _per_token_gram_native(a1, g1, m2).to(g1.dtype)
     if a1.ndim == 4:
         m2 = torch.einsum("csgk,csgd->cgkd", a2, g2)
         return torch.einsum("btgk,btgd,cgkd->btc", a1, g1, m2)
@@ -167,6 +199,8 @@ def cross_gram_per_token_dense(a1, g1, m2, layer_type: str) -> torch.Tensor:
     if is_conv_transpose(layer_type):
         m2 = m2.reshape(b2, a1f.shape[-1], g1f.shape[-1])
         return torch.einsum("blc,blp,ncp->bln", a1f, g1f, m2)
+    if _native(a1f, g1f) and m2.is_cuda:
+        return _per_token_gram_native(a1f, g1f, m2).to(g1f.dtype)
     m2 = m2.reshape(b2, g1f.shape[-1], a1f.shape[-1])
     return torch.einsum("btk,btd,cdk->btc", a1f, g1f, m2)
 
