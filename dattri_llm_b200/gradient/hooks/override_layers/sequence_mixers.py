@@ -111,8 +111,22 @@ def _conv_through_module(mixer: nn.Module, original: Callable) -> Callable:
     return conv_fn
 
 
-def _decoding(mixer, args, kwargs) -> bool:
-    cache = kwargs.get("cache_params", args[0] if args else None)
+_HIDDEN_KWARGS = ("hidden_states", "input_states", "x")
+
+
+def _hidden(args: tuple, kwargs: dict) -> tuple[torch.Tensor, tuple]:
+    """The mixer's input, passed first positionally or by keyword, and the positional
+    arguments after it."""
+    if args:
+        return args[0], args[1:]
+    for key in _HIDDEN_KWARGS:
+        if key in kwargs:
+            return kwargs[key], ()
+    raise TypeError(f"sequence mixer called without its input (positional or one of {_HIDDEN_KWARGS})")
+
+
+def _decoding(mixer, rest, kwargs) -> bool:
+    cache = kwargs.get("cache_params", rest[0] if rest else None)
     if cache is None:
         return False
     prev = getattr(cache, "has_previous_state", None)
@@ -139,14 +153,16 @@ def install_sequence_mixer_forward(root: nn.Module, mixer_names: list[str],
         mixer = modules[name]
         original = mixer.forward
         if is_mamba1_mixer(mixer):
-            def forward(h, *args, _m=mixer, _o=original, **kwargs):
-                if not should_intervene() or _decoding(_m, args, kwargs):
-                    return _o(h, *args, **kwargs)
+            def forward(*args, _m=mixer, _o=original, **kwargs):
+                h, rest = _hidden(args, kwargs)
+                if not should_intervene() or _decoding(_m, rest, kwargs):
+                    return _o(*args, **kwargs)
                 return mamba1_reference_forward(_m, h, kwargs.get("attention_mask"))
         elif is_functional_conv_mixer(mixer):
-            def forward(h, *args, _m=mixer, _o=original, _mod=_modeling(mixer), **kwargs):
-                if not should_intervene() or _decoding(_m, args, kwargs):
-                    return _o(h, *args, **kwargs)
+            def forward(*args, _m=mixer, _o=original, _mod=_modeling(mixer), **kwargs):
+                _h, rest = _hidden(args, kwargs)
+                if not should_intervene() or _decoding(_m, rest, kwargs):
+                    return _o(*args, **kwargs)
                 saved = {}
                 for attr, value in list(vars(_mod).items()):
                     if attr == _CONV_FN:
@@ -159,7 +175,7 @@ def install_sequence_mixer_forward(root: nn.Module, mixer_names: list[str],
                         saved[attr] = value
                         setattr(_mod, attr, False)
                 try:
-                    return _o(h, *args, **kwargs)
+                    return _o(*args, **kwargs)
                 finally:
                     for attr, value in saved.items():
                         setattr(_mod, attr, value)
