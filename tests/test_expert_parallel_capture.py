@@ -259,3 +259,46 @@ def test_taps_are_not_hooked_outside_capture():
     tap = model.moe.dattri_experts[0]["gate_up"]
     assert isinstance(tap, ExpertTap) and tap.out_features == 2 * INTER
     assert not any(True for _ in tap.parameters())
+
+
+def _collect_olmoe(model, batches, path, **kw):
+    import dattri_llm_b200 as bw
+
+    store = bw.GradientStorageManager(str(path))
+    hm = bw.HookManager(model, bw.HookManagerConfig(linear_io=[r"mlp"]),
+                        callbacks=[bw.OffloadCallback(offload_interval=1, file_manager=store)], **kw)
+    for ids in batches:
+        with hm.collect():
+            logits = model(input_ids=ids).logits
+            F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]).float(), ids[:, 1:].reshape(-1),
+                            reduction="sum").backward()
+        model.zero_grad(set_to_none=True)
+    hm.remove()
+    store.close()
+    return str(path)
+
+
+def test_kfac_and_tracin_from_expert_parallel_stores(tmp_path):
+    """K-FAC (zero rows of tokens not routed to an expert dropped from its covariances) and
+    TracIn scored from stores captured under expert parallelism equal the scores from
+    replicated-expert stores of the same model and data."""
+    import copy
+
+    import dattri_llm_b200 as bw
+    from dattri_llm_b200.parallel.moe import expert_parallelize
+
+    model = _olmoe()
+    ep_model = copy.deepcopy(model)
+    expert_parallelize(ep_model, max_tokens=64, device=torch.device("cpu"))
+    g = torch.Generator().manual_seed(9)
+    train = [torch.randint(0, 64, (3, 8), generator=g) for _ in range(2)]
+    test = [torch.randint(0, 64, (2, 8), generator=g)]
+    moe = {"moe_routed_layers": ["model.layers.0.mlp"]}
+    rep = (_collect_olmoe(model, train, tmp_path / "rtr", **moe), _collect_olmoe(model, test, tmp_path / "rte", **moe))
+    ep = (_collect_olmoe(ep_model, train, tmp_path / "etr"), _collect_olmoe(ep_model, test, tmp_path / "ete"))
+    args = bw.AttributionArguments(output_dir=str(tmp_path / "o"), use_cpu=True)
+    for cls, kw in ((bw.TracInAttributor, {}), (bw.KFACAttributor, {"damping": 0.1})):
+        want = cls(args).attribute_from_cache(*rep, **kw)
+        got = cls(args).attribute_from_cache(*ep, **kw)
+        assert got.row_train_ids == want.row_train_ids
+        _close(got.scores, want.scores, msg=cls.__name__)
