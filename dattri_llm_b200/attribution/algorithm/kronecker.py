@@ -336,9 +336,9 @@ class KroneckerAttributor(BaseInnerProductAttributor):
                 out.append(name)
         return out
 
-    def accumulate_fisher(self, acc: ops.FisherAccumulator, grad) -> None:
+    def accumulate_fisher(self, fisher_acc: ops.FisherAccumulator, grad) -> None:
         """Add one block to the direct-Fisher accumulator."""
-        acc.update(grad, self.fisher_layers(grad))
+        fisher_acc.update(grad, self.fisher_layers(grad))
         if self._direct_norm_layers:
             self._fisher_saw_embedding.update(n for n, v in grad.data.items()
                                               if ops.is_embedding(grad.layer_types[n]) and isinstance(v, Factorized))
