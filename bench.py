@@ -47,7 +47,7 @@ MICRO_BATCH = 8
 N_TEST = 1024
 PROJ_DIM = 64
 TOPK = 100
-PUBLISHED = None  # BASELINE.md publishes no number for this configuration
+PUBLISHED = None  # no published number exists for this configuration on any hardware
 METRIC = "train samples attributed/sec (capture+project+score), device-timed, 1/2/4/8 B200"
 
 
