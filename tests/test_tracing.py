@@ -122,3 +122,24 @@ def test_pipeline_phases_open_ranges(nvtx_log, tmp_path):
     assert "dattri.score.block" in names
     assert "dattri.store.write" in names
     assert sum(1 for k, _ in nvtx_log if k == "push") == sum(1 for k, _ in nvtx_log if k == "pop")
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_device_timer_and_nvtx_on_gpu():
+    """CUDA-event timing of queued work (no profiler attached: the NVTX calls are no-ops
+    that must still balance)."""
+    a = torch.randn(4096, 4096, device="cuda")
+    timer = DeviceTimer()
+    assert timer.device.type == "cuda"
+    set_tracing(True)
+    try:
+        with trace_range("gpu.matmul"), timer:
+            for _ in range(4):
+                a = a @ a / 64.0
+    finally:
+        set_tracing(False)
+    ms = timer.elapsed_ms()
+    assert 0.0 < ms < 10_000.0
+    row = throughput_row("matmul", 4 * 2 * 4096**3, ms, unit="flop/s")
+    assert row["value"] > 0
