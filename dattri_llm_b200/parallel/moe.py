@@ -26,9 +26,10 @@ Per-sample capture.  Every expert has two :class:`ExpertTap` stand-ins,
 :class:`RouterTap` ``gate.dattri_router``: the layer names the replicated-expert proxies
 of ``gradient/hooks/override_layers/fused_experts.py`` give a Hugging Face MoE block, so a
 store written under expert parallelism reads like one written with replicated experts.
-A capture manager hooks the taps like ``nn.Linear`` layers.  While a tap is hooked, the layer runs the two-stage
-all-to-all form (:class:`_UpA2A`, :class:`_DownA2A`): the owner returns each row's SwiGLU
-output to the source in the forward and its gate/up output gradient in the backward, so
+A capture manager hooks the taps like ``nn.Linear`` layers.  While a tap is hooked, the
+layer runs the two-stage all-to-all form (:class:`_UpA2A`, :class:`_DownA2A`): the owner
+returns each row's SwiGLU output to the source in the forward and its gate/up output
+gradient in the backward, so
 the source holds both factors of every expert projection for its own samples.  It feeds
 them to the taps as ``(B, T, d)`` tensors, zero at the tokens not routed to the expert,
 the layout the replicated path regroups its rows into.  Rows carry their slot index, so
