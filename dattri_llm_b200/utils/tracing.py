@@ -85,9 +85,12 @@ class DeviceTimer:
     """
 
     def __init__(self, device: torch.device | str | None = None) -> None:
-        dev = torch.device(device) if device is not None else None
-        if dev is None:
-            dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+        if device is not None:
+            dev = torch.device(device)
+        elif torch.cuda.is_available():
+            dev = torch.device("cuda", torch.cuda.current_device())
+        else:
+            dev = torch.device("cpu")
         self.device = dev
         self._cuda = dev.type == "cuda"
         self._pairs: list[tuple[object, object]] = []
