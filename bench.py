@@ -319,8 +319,6 @@ def run_ours(rank, world, local, steps, warmup):
     per_rank = N_TEST // world
     test_ids = _DS(N_TEST, cfg.vocab_size, seed=1).ids[rank * per_rank:(rank + 1) * per_rank].to(dev)
     parts = []
-    with torch.no_grad():
-        pass
     for s in range(0, per_rank, MICRO_BATCH):
         g = step_block(test_ids[s:s + MICRO_BATCH])
         parts.append(PackedDense.pack(g).matrix)
@@ -434,7 +432,9 @@ def run_ours_e2e(bw, model, hc, score_packed, rank, world, steps, warmup, vocab)
 def run_reference(rank, world, local, steps, warmup):
     ref = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "dattri_llm")):
-        return None
+        raise SystemExit("bench.py --impl reference: the reference is not installed under baseline/_ref "
+                         "(python -m pip install --no-index --no-build-isolation --no-deps "
+                         "--find-links /opt/wheelhouse --target baseline/_ref <copy of the reference>)")
     sys.path.insert(0, ref)
     import dattri_llm as R  # noqa: N812
     from transformers import LlamaConfig as HFConfig
@@ -490,7 +490,6 @@ def main():
     if a.warmup < 3:
         a.warmup = 3
     rank, world, local = _init_dist()
-    torch.backends.cuda.matmul.allow_tf32 = True
     cfg_json = {"model": "Llama-3.2-1B-arch (random init)", "global_batch": MICRO_BATCH * world,
                 "micro_batch_per_gpu": MICRO_BATCH, "seq_len": SEQ, "parallelism": f"dp{world}",
                 "n_test": N_TEST, "proj": f"logra {PROJ_DIM}x{PROJ_DIM} per linear (112 layers)",
@@ -509,14 +508,10 @@ def main():
                         "vs_baseline": None if PUBLISHED is None else value / PUBLISHED,
                         "clocks": clk, "e2e": e2e, "gpu_launches": launches})
         else:
-            res = run_reference(rank, world, local, a.steps, a.warmup)
-            if res is None:
-                out = {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
-            else:
-                ms, clk, e2e = res
-                value = MICRO_BATCH * world / (ms / 1e3)
-                out.update({"impl": "reference", "value": value, "unit": "train samples/s", "ms_per_step": ms,
-                            "vs_baseline": None, "clocks": clk, "e2e": e2e})
+            ms, clk, e2e = run_reference(rank, world, local, a.steps, a.warmup)
+            value = MICRO_BATCH * world / (ms / 1e3)
+            out.update({"impl": "reference", "value": value, "unit": "train samples/s", "ms_per_step": ms,
+                        "vs_baseline": None, "clocks": clk, "e2e": e2e})
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -16,7 +16,7 @@
 #include "gemm_tc.cuh"
 #include "ghost_gram.cuh"
 #include "fused.cuh"
-#include "kernels.cuh"
+#include "projector.cuh"
 #include "rows.cuh"
 #include "score_ag.cuh"
 #include "peer_sync.cuh"
@@ -1114,5 +1114,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd_inplace", &ce_bwd_inplace);
-  bw::register_kernels(m);
+  bw::register_projector(m);
 }

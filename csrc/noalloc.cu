@@ -35,7 +35,10 @@
 // dattri_b200_noalloc_setup() performs the scratch lookup alone.
 //
 // Return value: a cudaError_t as int (0 = launched).  Device-side wait timeouts land in
-// the error word, read with dattri_b200_noalloc_status().
+// the error word, read with dattri_b200_noalloc_status(), which is ordered after the
+// caller's stream.  The prototypes, with these limits, are in noalloc.cuh.
+#include "noalloc.cuh"
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -152,8 +155,17 @@ extern "C" __attribute__((visibility("default"))) int dattri_b200_gemm_bf16_spli
   return static_cast<int>(cudaGetLastError());
 }
 
-// Copy the current device's error word to *out (synchronous; 0 = no device error).
-extern "C" __attribute__((visibility("default"))) int dattri_b200_noalloc_status(int* out) {
+// Copy the current device's error word to *out once every call queued on `stream` has
+// finished (0 = no device error).  The copy is queued on `stream` itself, so it is ordered
+// after the GEMM even when `stream` does not synchronise with the legacy default stream.
+extern "C" __attribute__((visibility("default"))) int dattri_b200_noalloc_status(int* out,
+                                                                                  cudaStream_t stream) {
   if (out == nullptr) return cudaErrorInvalidValue;
-  return static_cast<int>(cudaMemcpyFromSymbol(out, g_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost));
+  int word = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&word, g_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  *out = word;
+  return cudaSuccess;
 }

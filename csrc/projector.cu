@@ -15,7 +15,7 @@
 
 #include <cmath>
 
-#include "kernels.cuh"
+#include "projector.cuh"
 
 namespace bw {
 namespace {

@@ -14,8 +14,6 @@ and projection weights directly, so hooks on ``conv1d`` / ``in_proj`` /
 
 Decoding steps (a cache with previous state) keep the original forward.
 Parity: reference ``dattri_llm/gradient/hooks/override_layers/sequence_mixers.py``.
-The library's own Mamba2 model (:mod:`dattri_llm_b200.models.mamba2`) applies its
-projections through modules and needs no override.
 """
 
 from __future__ import annotations

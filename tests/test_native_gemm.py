@@ -345,7 +345,7 @@ def test_mask_gather_matches_materialized(b, t, kr, kc, m):
 @pytest.mark.parametrize(("b1", "t", "b2", "t2", "k", "d"), [(3, 50, 5, 37, 64, 64), (2, 200, 7, 64, 40, 24)])
 def test_per_token_cross_gram_on_tensor_cores(b1, t, b2, t2, k, d):
     """Per-token cross-gram (factorized and dense side 2) against an fp32 einsum."""
-    from dattri_llm_b200.gradient.ops import dot
+    import dattri_llm_b200.gradient.ops.dot as dot
 
     g = torch.Generator(device="cuda").manual_seed(5)
     a1, g1 = (torch.randn(b1, t, n, device="cuda", generator=g).bfloat16() for n in (k, d))

@@ -26,7 +26,7 @@ def _lib():
                    ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_float, ctypes.c_int,
                    ctypes.c_void_p]
     lib.dattri_b200_noalloc_status.restype = ctypes.c_int
-    lib.dattri_b200_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    lib.dattri_b200_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
     lib.dattri_b200_noalloc_max_output.restype = ctypes.c_longlong
     return lib
 
@@ -48,7 +48,11 @@ def _existing(a, b, alpha=1.0):
     return out
 
 
-@pytest.mark.parametrize(("m", "n", "k", "splits"), [(256, 128, 4096, 8), (200, 72, 1000, 3), (1024, 2048, 512, 2)])
+# Shapes reach every kernel the entry point can launch: per-tile split-K (splits >= 2),
+# the CTA-pair kernel (splits 1, N > 128), the persistent kernel (splits 1, N <= 128 and
+# more tiles than SMs) and a K shorter than one 64-wide block (splits clamped to 1).
+@pytest.mark.parametrize(("m", "n", "k", "splits"), [(256, 128, 4096, 8), (200, 72, 1000, 3), (1024, 2048, 512, 2),
+                                                     (1024, 1024, 512, 1), (19200, 96, 64, 1), (300, 200, 48, 4)])
 def test_two_consecutive_calls_match_existing_entry_point(m, n, k, splits):
     lib = _lib()
     gen = torch.Generator(device="cuda").manual_seed(m + n + k)
@@ -57,9 +61,9 @@ def test_two_consecutive_calls_match_existing_entry_point(m, n, k, splits):
         b = torch.randn(n, k, device="cuda", generator=gen).to(torch.bfloat16)
         c = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
         assert _call(lib, a, b, c, splits, alpha=0.5) == 0
-        torch.cuda.synchronize()
         status = ctypes.c_int(-1)
-        assert lib.dattri_b200_noalloc_status(ctypes.byref(status)) == 0
+        stream = torch.cuda.current_stream().cuda_stream
+        assert lib.dattri_b200_noalloc_status(ctypes.byref(status), stream) == 0
         assert status.value == 0, f"device error word {status.value} on call {call}"
         want = _existing(a, b, alpha=0.5)
         exact = 0.5 * (a.float() @ b.float().T)
