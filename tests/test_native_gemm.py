@@ -345,7 +345,7 @@ def test_mask_gather_matches_materialized(b, t, kr, kc, m):
 @pytest.mark.parametrize(("b1", "t", "b2", "t2", "k", "d"), [(3, 50, 5, 37, 64, 64), (2, 200, 7, 64, 40, 24)])
 def test_per_token_cross_gram_on_tensor_cores(b1, t, b2, t2, k, d):
     """Per-token cross-gram (factorized and dense side 2) against an fp32 einsum."""
-    import dattri_llm_b200.gradient.ops.dot as dot
+    from dattri_llm_b200.gradient.ops.dot import cross_gram_per_token, cross_gram_per_token_dense
 
     g = torch.Generator(device="cuda").manual_seed(5)
     a1, g1 = (torch.randn(b1, t, n, device="cuda", generator=g).bfloat16() for n in (k, d))
@@ -353,8 +353,8 @@ def test_per_token_cross_gram_on_tensor_cores(b1, t, b2, t2, k, d):
     m2 = torch.einsum("csd,csk->cdk", g2.float(), a2.float())
     want = torch.einsum("btk,btd,cdk->btc", a1.float(), g1.float(), m2)
     scale = float(want.abs().max())
-    got = dot.cross_gram_per_token(a1, g1, a2, g2, "nn.Linear").float()
+    got = cross_gram_per_token(a1, g1, a2, g2, "nn.Linear").float()
     torch.testing.assert_close(got, want, rtol=3e-2, atol=2e-2 * scale)
-    got_dense = dot.cross_gram_per_token_dense(a1, g1, m2.bfloat16().reshape(b2, -1), "nn.Linear").float()
+    got_dense = cross_gram_per_token_dense(a1, g1, m2.bfloat16().reshape(b2, -1), "nn.Linear").float()
     torch.testing.assert_close(got_dense, want, rtol=3e-2, atol=2e-2 * scale)
     ops.check_device_errors()
