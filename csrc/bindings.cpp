@@ -135,6 +135,44 @@ void gemm_tn_seg(Tensor A, Tensor B, Tensor C, double alpha, int64_t seg, Tensor
   bw::gemm_tn_launch(a, b, p, bw::pick_bn(p.N), at::cuda::getCurrentCUDAStream());
 }
 
+// C (bf16, M x N_main) = A @ B^T and C2 (bf16, token-major (M / seg, N_tail, seg)) =
+// A @ Btail^T in ONE CTA-pair launch over A: a layer's output and its projected input (or,
+// in the backward, its input gradient and projected output gradient) from one read of A.
+void gemm_tn_tail(Tensor A, Tensor B, Tensor Btail, Tensor C, Tensor C2, int64_t seg, Tensor err) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check_err(err);
+  auto a = operand(A, "A");
+  auto b = operand(B, "B");
+  auto t = operand(Btail, "Btail");
+  TORCH_CHECK(a.batch == 1 && b.batch == 1 && t.batch == 1, "gemm_tn_tail takes 2-D operands");
+  TORCH_CHECK(a.cols == b.cols && a.cols == t.cols, "A, B and Btail disagree on K");
+  TORCH_CHECK(b.rows % 256 == 0, "B's rows (the main output width) must be a multiple of 256");
+  TORCH_CHECK(t.rows >= 1 && t.rows <= 256, "Btail must have 1..256 rows");
+  TORCH_CHECK(seg > 0 && a.rows % seg == 0, "rows of A must be a multiple of the segment length");
+  check_cuda(C, "C");
+  check_cuda(C2, "C2");
+  TORCH_CHECK(C.scalar_type() == torch::kBFloat16 && C.dim() == 2 && C.size(0) == a.rows && C.size(1) == b.rows &&
+                  C.stride(1) == 1,
+              "C must be a (M, N_main) bf16 matrix, contiguous along its rows");
+  TORCH_CHECK(C2.scalar_type() == torch::kBFloat16 && C2.is_contiguous() && C2.dim() == 3 &&
+                  C2.size(0) == a.rows / seg && C2.size(1) == t.rows && C2.size(2) == seg,
+              "C2 must be a contiguous (M / seg, N_tail, seg) bf16 tensor");
+  bw::GemmParams p{};
+  p.M = (int)a.rows;
+  p.N = (int)(b.rows + t.rows);
+  p.K = (int)a.cols;
+  p.alpha = 1.0f;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.n_main = (int)b.rows;
+  p.C2 = C2.data_ptr();
+  p.seg2 = seg;
+  p.err = err.data_ptr<int>();
+  if (p.M == 0) return;
+  TORCH_CHECK(bw::gemm_tn_tail_launch(a, b, t, p, at::cuda::getCurrentCUDAStream()),
+              "gemm_tn_tail: CTA pairs cannot run on this device");
+}
+
 // ---- grouped GEMM: one launch for many same-shaped batched problems --------------------
 struct MapKey {
   const void* ptr;
@@ -1102,6 +1140,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");
   m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");
+  m.def("gemm_tn_tail", &gemm_tn_tail, "C = A B^T (bf16 rows) and C2 = A Btail^T (token-major) in one launch");
   m.def("slot_reduce", &slot_reduce, "owner-side sum of reduce-scatter slots");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

@@ -128,6 +128,19 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
   }
   if (!row_ok) return;
   const int nbase = n0 + c0;
+  if (p.c_mode == kStoreBF16Tail && n0 >= p.n_main) {
+    // The tail tile: token-major into C2; consecutive lanes write consecutive tokens.
+    const int n2 = p.N - p.n_main;
+    __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(p.C2) + (long long)(row / p.seg2) * n2 * p.seg2 +
+                        row % p.seg2;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = nbase - p.n_main + j;
+      if (j < BN - c0 && n < n2) Cz[(long long)n * p.seg2] = __float2bfloat16(alpha * __uint_as_float(r[j]));
+    }
+    return;
+  }
+  const bool bf16_rows = p.c_mode == kStoreBF16 || p.c_mode == kStoreBF16Tail;  // tail tiles returned above
   if (p.c_mode == kSqAccF32) {  // every batch squares into the same matrix
     float* Cr = static_cast<float*>(Cbase) + (long long)row * p.ldc;
     if (c0 + 32 <= BN && nbase + 32 <= p.N && ((reinterpret_cast<uintptr_t>(Cr + nbase) & 15) == 0)) {
@@ -223,7 +236,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
         Cv[q] = v;
       }
     }
-  } else if (p.c_mode == kStoreBF16 && c0 + 32 <= BN && nbase + 32 <= p.N &&
+  } else if (bf16_rows && c0 + 32 <= BN && nbase + 32 <= p.N &&
              ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
                                            (long long)row * p.ldc + nbase) & 15) == 0)) {
     uint4* Cv = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
@@ -253,7 +266,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
           atomicAdd(Cz + n, v);
       }
     }
-  } else if (p.c_mode == kStoreBF16) {
+  } else if (bf16_rows) {
     __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c +
                         (long long)row * p.ldc;
 #pragma unroll
@@ -546,10 +559,13 @@ struct TileSched {
   int jobs;
   int n_rot;    // dense tiles: column-tile index rotation (a sharded B's own columns first)
   int n_major;  // dense tiles: column tile is the slow index (all row blocks of one B tile in turn)
+  int tail_w;   // CTA-pair kernel: width of the last column tile when N is not a multiple of 256
+                // (a multiple of 32, >= 64; 0 = every tile is 256 wide)
 };
 
 struct TileCoord {
   int m0, n0, za, zb, zc, limit;
+  int w;  // CTA-pair kernel: columns of this tile (256, or tail_w for the last column tile)
 };
 
 template <int BN>
@@ -739,6 +755,7 @@ __device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const
   tn += ts.n_rot;
   if (tn >= ts.tiles_n) tn -= ts.tiles_n;
   c.n0 = tn * 256;
+  c.w = (ts.tail_w != 0 && tn == ts.tiles_n - 1) ? ts.tail_w : 256;
   if (ts.tile_prefix != nullptr) {
     int lo = 0, hi = ts.jobs - 1;
     while (lo < hi) {
@@ -827,10 +844,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int own_lo = kStaged ? sa.self * sa.shard : 0;
       for (int tile = pair; tile < total && alive; tile += pairs) {
         const TileCoord c = decode_pair_tile(ts, p, tile);
-        const int brow = c.n0 + 128 * (int)rank;
+        // cta_group::2 splits the tile's N columns over the pair: each CTA stages w / 2 rows of B
+        const int brow = c.n0 + (c.w >> 1) * (int)rank;
         // mode 0: this CTA's B rows belong to one owner for the whole tile
         const CUtensorMap* bmap = &tmB;
         int brow_map = brow;
+        int bz = c.zb;
+        if constexpr (!kStaged) {
+          if (p.c_mode == kStoreBF16Tail && c.n0 >= p.n_main) {  // the tail tile reads the second B
+            bmap = &tmOwn;
+            brow_map = brow - p.n_main;
+            bz = 0;
+          }
+        }
         if constexpr (kStaged) {
           if (sa.mode == 0) {
             if (brow >= own_lo && brow < own_lo + sa.shard) {
@@ -871,7 +897,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
               tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kc, brow, 0);
             }
           } else {
-            tma_load_3d_pair(sB + s * C::kTileB, &tmB, bar, kc, brow, c.zb);
+            tma_load_3d_pair(sB + s * C::kTileB, bmap, bar, kc, brow_map, bz);  // rows past the end: zero fill
           }
           ++g;
         }
@@ -884,11 +910,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
   } else if (warp == 5) {
     if (lane == 0 && rank == 0) {
       // ---- MMA issuer (CTA 0) ----
-      constexpr uint32_t idesc = idesc_bf16_f32(256, 256);
       int g = 0, it = 0;
       bool alive = true;
       for (int tile = pair; tile < total && alive; tile += pairs, ++it) {
         const int b = it & 1;
+        const uint32_t idesc = idesc_bf16_f32(256, decode_pair_tile(ts, p, tile).w);
         if (!mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1, p.err, kErrWaitDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 256);
@@ -954,11 +980,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (!ok) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < 256; c0 += 32) {
+      for (int c0 = 0; c0 < c.w; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 256 + c0), r);
         tmem_ld_wait();
-        if (c0 + 32 >= 256) {
+        if (c0 + 32 >= c.w) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&acc_empty[b]), 0));
@@ -1155,14 +1181,26 @@ int pair_clusters() {
   return count[dev & 63];
 }
 
+// Width of the last column tile of an N-wide pair GEMM: the remainder rounded up to a multiple
+// of 32 (at least 64), so that a narrow remainder does not cost a whole 256-wide tile of MMAs
+// (0 when N is a multiple of 256).
+int pair_tail_width(int N) {
+  const int rem = N % 256;
+  if (rem == 0) return 0;
+  const int w = (rem + 31) / 32 * 32;
+  return w < 64 ? 64 : w;
+}
+
 // Launch the pair kernel on up to `max_tiles` 256 x 256 tiles; false if it cannot run here.
+// `tail`: the second B operand of the kStoreBF16Tail store (nullptr otherwise).
 bool launch_pair(const GemmOperand& A, const GemmOperand& B, const GemmParams& p, const TileSched& ts,
-                 long long max_tiles, cudaStream_t stream) {
+                 long long max_tiles, cudaStream_t stream, const GemmOperand* tail = nullptr) {
   const int clusters = pair_clusters();
   if (clusters <= 0) return false;
   if (max_tiles <= 0) return true;
   CUtensorMap ta = make_tmap_kmajor_bf16(A, 128);
   CUtensorMap tb = make_tmap_kmajor_bf16(B, 128);
+  CUtensorMap tt = tail != nullptr ? make_tmap_kmajor_bf16(*tail, 128) : tb;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(max_tiles, clusters), 1, 1);
   cfg.blockDim = dim3(kPThreads, 1, 1);
@@ -1176,7 +1214,7 @@ bool launch_pair(const GemmOperand& A, const GemmOperand& B, const GemmParams& p
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   StageArgs none{};
-  cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, p, ts, tb, none);
+  cudaLaunchKernelEx(&cfg, gemm_pair_kernel<false>, ta, tb, p, ts, tt, none);
   return true;
 }
 
@@ -1228,6 +1266,7 @@ void launch_ragged_bn(const GemmOperand& A, const GemmOperand& B, const GemmPara
   ts.jobs = jobs;
   if (BN == 256) {
     ts.tiles_n = (p.N + 255) / 256;
+    ts.tail_w = pair_tail_width(p.N);
     if (launch_pair(A, B, p, ts, (long long)max_blocks * ts.tiles_n, stream)) return;
   }
   ts.tiles_n = (p.N + BN - 1) / BN;
@@ -1336,6 +1375,24 @@ int pick_bn(int N) {
   return 256;
 }
 
+bool gemm_tn_tail_launch(const GemmOperand& A, const GemmOperand& B, const GemmOperand& Btail, GemmParams p,
+                         cudaStream_t stream) {
+  if (p.n_main % 256 != 0 || p.N - p.n_main <= 0 || p.N - p.n_main > 256 || B.rows != p.n_main ||
+      Btail.rows != p.N - p.n_main || A.batch != 1 || B.batch != 1 || Btail.batch != 1 || p.seg2 <= 0 ||
+      p.M % p.seg2 != 0)
+    throw std::runtime_error("gemm_tn_tail: main width must be a multiple of 256, the tail 1..256 rows, one batch");
+  p.c_mode = kStoreBF16Tail;
+  p.splits = 1;
+  p.batch = 1;
+  p.b_shared = 1;
+  TileSched ts{};
+  ts.tiles_n = p.n_main / 256 + 1;
+  ts.tiles_m = (p.M + 255) / 256;
+  ts.batch = 1;
+  ts.tail_w = pair_tail_width(p.N - p.n_main) == 0 ? 256 : pair_tail_width(p.N - p.n_main);
+  return launch_pair(A, B, p, ts, (long long)ts.tiles_n * ts.tiles_m, stream, &Btail);
+}
+
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream) {
   if (p.splits < 1) p.splits = 1;
@@ -1351,6 +1408,7 @@ void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, in
     ts.tiles_m = (p.M + 255) / 256;
     ts.batch = p.batch;
     ts.jobs = 0;
+    ts.tail_w = pair_tail_width(p.N);
     if (launch_pair(A, B, p, ts, (long long)ts.tiles_n * ts.tiles_m * ts.batch, stream)) return;
   }
   if (p.splits == 1 && bn >= 64 && p.K > 0 && tiles > sm_count()) {

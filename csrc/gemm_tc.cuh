@@ -21,6 +21,9 @@ enum GemmStore : int {
   kPeerSlotF32 = 7,  // reduce-scatter: element i (owner o = (i / 4) / per4) is STORED into
                      // peers[o][self_rank * 4 * per4 + i - o * 4 * per4] (the owner's slot for
                      // this rank); the owner sums its slots afterwards (splits must be 1)
+  kStoreBF16Tail = 9,  // columns n < n_main: bf16 C[m][n] (row stride ldc); columns n >= n_main
+                       // (the tail, from a second B operand): token-major bf16 C2, element
+                       // (m, n) at C2[m / seg2][n - n_main][m % seg2] (a (S, N - n_main, seg2) block)
 };
 
 // A K-major bf16 operand: `batch` matrices of rows x cols (cols = K, contiguous).
@@ -51,6 +54,9 @@ struct GemmParams {
   long long per4;       // kPeerSlotF32: float4 elements owned by each rank
   int self_rank;        // kPeerSlotF32: this rank (selects its slot in the owners' buffers)
   const int2* scatter;  // kStoreBF16Scatter: (rank, row) of every output row
+  int n_main;           // kStoreBF16Tail: columns that come from B (a multiple of 256)
+  void* C2;             // kStoreBF16Tail: the tail's token-major output
+  long long seg2;       // kStoreBF16Tail: tokens per segment (sample) of C2
 };
 
 // One job of a grouped launch (tensor maps in global memory, 64-byte aligned).
@@ -97,5 +103,12 @@ void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const
 int pick_bn(int N);
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream);
+// C = A @ [B; Btail]^T in one CTA-pair launch with the kStoreBF16Tail store: the main columns
+// (B's rows, p.n_main of them, a multiple of 256) in row-major bf16 and the tail (Btail's rows,
+// at most 256) token-major -- e.g. a layer's output and its projected activation from one pass
+// over the activation.  p.N = n_main + Btail's rows.  Returns false when CTA pairs cannot run
+// here (nothing launched).
+bool gemm_tn_tail_launch(const GemmOperand& A, const GemmOperand& B, const GemmOperand& Btail, GemmParams p,
+                         cudaStream_t stream);
 
 }  // namespace bw

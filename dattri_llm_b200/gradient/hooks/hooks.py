@@ -19,7 +19,13 @@ Projected capture (``projection_kwargs``): for a linear layer under the
 * when the layer will be materialized (``capture_style`` ``"materialized"`` or
   ``"auto"`` with ``T >= k_a k_g / (k_a + k_g)``) the projected factors are
   written token-major ``(B, k, T)`` straight from the GEMM epilogue, so the
-  per-sample ``g_p^T a_p`` is a second tcgen05 GEMM with no transpose copy.
+  per-sample ``g_p^T a_p`` is a second tcgen05 GEMM with no transpose copy;
+* a layer whose class declares ``__bw_fused_capture__`` (the library's models use
+  :class:`dattri_llm_b200.models.layers.TcLinear`) computes both projections inside its own
+  GEMMs: a :class:`_FusedCaptureLink` hands its forward ``P_a^T`` to append as a narrow
+  last column tile (``x P_a`` token-major from the same read of ``x``) and its backward
+  ``P_g^T`` plus a sink that receives ``dy P_g`` from the input-gradient GEMM -- no
+  separate projection launches and no second read of ``x`` or ``dy``.
 """
 
 from __future__ import annotations
@@ -123,6 +129,73 @@ class _DeferredOuter:
 
     def __init__(self, g: torch.Tensor, a: torch.Tensor) -> None:
         self.g, self.a, self.result = g, a, None
+
+
+class _TokenMajorGrad:
+    """A layer's output gradient delivered already projected, token-major ``(B, k, T)``
+    (from the input-gradient GEMM of a fused-capture layer)."""
+
+    __slots__ = ("g_pt",)
+
+    def __init__(self, g_pt: torch.Tensor) -> None:
+        self.g_pt = g_pt
+
+
+class _FusedCaptureLink:
+    """What a fused-capture layer's forward and backward need from its capture.
+
+    :meth:`before_forward` returns ``(P_a^T or None, slot or None)``: the slot when this
+    call's capture can take the fused route (LoGra, token-major materialize, native bf16,
+    nothing routed or offloaded), and ``P_a^T`` only when no sibling layer reading the same
+    input has projected it already this step.  The layer stores what it computed with
+    :meth:`after_forward`; the forward hook consumes it (:meth:`take`)."""
+
+    def __init__(self, name: str, buffers: dict, projector, offload: bool, routed, share) -> None:
+        self.name, self.buffers, self.projector = name, buffers, projector
+        self.offload, self.routed, self.share = offload, routed, share
+
+    def _eligible(self, x: torch.Tensor) -> bool:
+        buf = self.buffers[self.name]
+        return (torch.is_grad_enabled() and self.share is not None and not self.offload
+                and (self.routed is None or self.name not in self.routed.layers)
+                and _style(buf) == "logra" and _preprojects_activation(buf["_class_name"], "logra")
+                and buf["_capture_style"] != "factorized" and x.ndim == 3 and x.is_cuda)
+
+    def before_forward(self, module, x: torch.Tensor):
+        from dattri_llm_b200.ops.linear import CaptureSlot
+
+        if not self._eligible(x):
+            return None, None
+        buf = self.buffers[self.name]
+        (xa,) = dtypes.align(x)
+        pm = _projection_matrix(buf, "a", xa, self.projector)
+        k = pm.proj_dim
+        if not (ops.should_materialize(buf["_capture_style"], x.shape[1], k, k) and _token_major_ok(pm, xa)):
+            return None, None
+        key, root = _share_key(x, pm, True)
+        hit = self.share.get(key)
+        shared = hit is not None and hit[0]() is root
+        return (None if shared else pm.matrix_t), CaptureSlot(x.shape[1])
+
+    @staticmethod
+    def after_forward(module, a_pt: torch.Tensor | None, slot) -> None:
+        module.__dict__["_bw_fused_out"] = (a_pt, slot)
+
+    @staticmethod
+    def take(module):
+        return module.__dict__.pop("_bw_fused_out", None)
+
+
+class _AttrHandle:
+    """Hook-handle stand-in that deletes a module attribute on ``remove()``."""
+
+    def __init__(self, module: nn.Module, attr: str) -> None:
+        self.module, self.attr = weakref.ref(module), attr
+
+    def remove(self) -> None:
+        m = self.module()
+        if m is not None:
+            m.__dict__.pop(self.attr, None)
 
 
 class _StepShare:
@@ -229,6 +302,10 @@ def register_linear_io_hooks(
         buf["_capture_style"] = capture_style
         bwd = _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
                              on_layer_backward)
+        if getattr(type(module), "__bw_fused_capture__", False) and not _preconditioning(preconditioner):
+            module.__dict__["_bw_capture_link"] = _FusedCaptureLink(name, buffers, projector, offload_to_cpu,
+                                                                    routed, share)
+            handles.append(_AttrHandle(module, "_bw_capture_link"))
         # The output gradient is taken by a hook on the autograd node that produced the
         # layer's output, registered in the forward hook: a full module backward hook would
         # wrap every call's inputs and outputs in an extra autograd function (host time per
@@ -272,13 +349,25 @@ def _on_output_grad(out: torch.Tensor, fire) -> None:
 
 def _forward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback, on_grad):
     def hook(module, inp, out):
+        fused = _FusedCaptureLink.take(module)
         if not torch.is_grad_enabled():
             return  # no backward will follow (eval / log-prob pass)
-        record_forward(module, inp)
-        if isinstance(out, torch.Tensor) and out.requires_grad and out.grad_fn is not None:
-            _on_output_grad(out, lambda g, _m=module: on_grad(_m, None, (g,)))
+        entry = record_forward(module, inp, fused[0] if fused is not None else None)
+        if not (isinstance(out, torch.Tensor) and out.requires_grad and out.grad_fn is not None):
+            return
+        slot = fused[1] if fused is not None else None
+        if slot is not None and isinstance(entry, _Projected) and entry.token_major:
+            buf = buffers[name]
+            (oa,) = dtypes.align(out)
+            pm_g = _projection_matrix(buf, "g", oa, projector)
+            if _token_major_ok(pm_g, oa):
+                # the layer's input-gradient GEMM projects dy itself and delivers it here
+                slot.grad_tail_t = pm_g.matrix_t
+                slot.sink = lambda g_pt, _m=module: on_grad(_m, None, (_TokenMajorGrad(g_pt),))
+                return
+        _on_output_grad(out, lambda g, _m=module: on_grad(_m, None, (g,)))
 
-    def record_forward(_module, inp):
+    def record_forward(_module, inp, given_a_pt=None):
         x = inp[0]
         a = x.detach()
         dev = _device_index(x)
@@ -301,7 +390,7 @@ def _forward_hook(name, buffers, projector, preconditioner, offload, routed, sha
         else:
             entry = a
             if _preprojects_activation(buf["_class_name"], _style(buf)):
-                entry = _project_activation(buf, a, projector, share, x)
+                entry = _project_activation(buf, a, projector, share, x, given_a_pt)
                 emit = entry.a.transpose(1, 2) if entry.token_major else entry.a
                 emit_type, emit_kw = "nn.Linear", None
             with buf["_lock"]:
@@ -309,15 +398,26 @@ def _forward_hook(name, buffers, projector, preconditioner, offload, routed, sha
                 buf["_fwd_fires"] += 1
         if callback is not None:
             callback(name, emit, emit_type, emit_kw)
+        return entry if not _raw_capture(buf, preconditioner) else None
 
     return hook
 
 
 def _backward_hook(name, buffers, projector, preconditioner, offload, routed, share, callback):
     def hook(_module, _grad_input, grad_output):
+        buf = buffers[name]
+        if isinstance(grad_output[0], _TokenMajorGrad):  # projected inside the layer's own GEMM
+            g_pt = grad_output[0].g_pt
+            matched, g_p = _capture_projected(buf, None, _device_index(g_pt), projector, offload, preconditioner,
+                                              name, share, g_pt=g_pt)
+            if not matched:
+                _warn_orphan_backward(name)
+                return
+            if callback is not None:
+                callback(name, g_p, "nn.Linear", None)
+            return
         g = grad_output[0].detach()
         dev = _device_index(grad_output[0])
-        buf = buffers[name]
         if routed is not None and name in routed.layers:
             layout = routed.pop(name, dev)
             if layout is not None:
@@ -394,27 +494,38 @@ def project_token_major(pm: ops.ProjectionMatrix, x: torch.Tensor) -> torch.Tens
     return native_ops.gemm_tn_seg(flat, pm.matrix_t, t)
 
 
-def _project_activation(buf, a, projector, share, source) -> _Projected:
+def _share_key(source: torch.Tensor, pm: ops.ProjectionMatrix, token_major: bool):
+    """``(key, root)`` under which layers reading the same input tensor with the same matrix
+    (q/k/v, gate/up) share one activation projection per step.  A module with full backward
+    hooks sees its input through a per-module view (same storage, same version counter), so
+    siblings are matched through the view's base.  id() alone could be recycled once the
+    input is freed (frozen layers do not save it for backward); the weak reference to the
+    base proves it is the same tensor."""
+    root = source._base if source._base is not None else source
+    key = (id(root), source._version, source.data_ptr(), tuple(source.shape), tuple(source.stride()),
+           id(pm.matrix), token_major)
+    return key, root
+
+
+def _project_activation(buf, a, projector, share, source, given_a_pt=None) -> _Projected:
+    """The layer's projected activation: *given_a_pt* (token-major, computed by a fused
+    layer's own GEMM), a sibling's shared projection, or a fresh projection GEMM."""
     a3 = to_3d(dtypes.align(a)[0])
     pm = _projection_matrix(buf, "a", a3, projector)
     seq_len = a3.shape[1]
     k = pm.proj_dim
-    token_major = (ops.should_materialize(buf["_capture_style"], seq_len, k, k)
-                   and _token_major_ok(pm, a3))
+    token_major = given_a_pt is not None or (ops.should_materialize(buf["_capture_style"], seq_len, k, k)
+                                             and _token_major_ok(pm, a3))
     key = None
     if share is not None and a3.is_cuda:
-        # A module with full backward hooks sees its input through a per-module view
-        # (same storage, same version counter), so sibling layers (q/k/v, gate/up) are
-        # matched through the view's base.  id() alone could be recycled once the input is
-        # freed (frozen layers do not save it for backward); the weak reference to the
-        # base proves it is the same tensor.
-        root = source._base if source._base is not None else source
-        key = (id(root), source._version, source.data_ptr(), tuple(source.shape), tuple(source.stride()),
-               id(pm.matrix), token_major)
+        key, root = _share_key(source, pm, token_major)
         hit = share.get(key)
         if hit is not None and hit[0]() is root:
             return hit[1]
-    entry = _Projected(project_token_major(pm, a3) if token_major else pm(a3), token_major)
+    if given_a_pt is not None:
+        entry = _Projected(given_a_pt, True)
+    else:
+        entry = _Projected(project_token_major(pm, a3) if token_major else pm(a3), token_major)
     if key is not None:
         share.put(key, (weakref.ref(root), entry))
     return entry
@@ -445,9 +556,10 @@ def _keep_factors(buf: LayerBuffer, seq_len: int, k_a: int, k_g: int) -> bool:
     return not ops.should_materialize(buf["_capture_style"], seq_len, k_a, k_g)
 
 
-def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name, share=None):
+def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name, share=None, g_pt=None):
     """Pair *g* with its forward and store the projected / materialized / preconditioned
-    capture.  Returns ``(matched, projected g to hand the callbacks or None)``."""
+    capture.  Returns ``(matched, projected g to hand the callbacks or None)``.  *g_pt*: the
+    output gradient already projected token-major ``(B, k, T)`` (then *g* is ``None``)."""
     with buf["_lock"]:
         stack = buf["_pending"].get(dev)
         entry = stack.pop() if stack else None
@@ -477,24 +589,30 @@ def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_na
 
     if style == "logra":
         if isinstance(entry, _Projected):
-            g3 = to_3d(dtypes.align(g)[0])
-            pm_g = _projection_matrix(buf, "g", g3, projector)
-            if entry.token_major and _token_major_ok(pm_g, g3) and not buf["_act_parts"]:
+            g_p = None
+            if g_pt is None:
+                g3 = to_3d(dtypes.align(g)[0])
+                pm_g = _projection_matrix(buf, "g", g3, projector)
+                if entry.token_major and _token_major_ok(pm_g, g3) and not buf["_act_parts"]:
+                    g_pt = project_token_major(pm_g, g3)
+                else:
+                    g_p = pm_g(g3)
+            if g_pt is not None and entry.token_major and not buf["_act_parts"]:
                 from dattri_llm_b200 import ops as native_ops
 
-                g_pt = project_token_major(pm_g, g3)
                 b = g_pt.shape[0]
                 if share is not None and not offload:
                     # The per-sample outer product g_p^T a_p of every layer of the step runs
                     # in one grouped launch at step end (StepShare.flush_outer).
                     keep_dense(share.defer_outer(g_pt, entry.a))
                     return True, g_pt.transpose(1, 2)
-                dense = torch.empty(b, pm_g.proj_dim, entry.a.shape[1], dtype=g3.dtype, device=g3.device)
+                dense = torch.empty(b, g_pt.shape[1], entry.a.shape[1], dtype=g_pt.dtype, device=g_pt.device)
                 native_ops.gemm_tn(g_pt, entry.a, dense, mode=native_ops.STORE_BF16)
                 keep_dense(dense.reshape(b, -1))
                 return True, g_pt.transpose(1, 2)
+            if g_p is None:
+                g_p = g_pt.transpose(1, 2)
             a_p = entry.a.transpose(1, 2) if entry.token_major else entry.a
-            g_p = pm_g(g3)
             emit = g_p
         else:
             a = entry

@@ -8,6 +8,9 @@ and every projection is an ``nn.Linear`` the capture hooks see.
 
 B200 execution choices:
 
+* every projection is a :class:`~dattri_llm_b200.models.layers.TcLinear`: its forward and
+  input-gradient GEMMs run on the library's tcgen05 CTA-pair kernel, and a LoGra capture
+  computes its projections inside those GEMMs;
 * attention is ``scaled_dot_product_attention`` with grouped KV heads (no K/V
   repetition in memory);
 * RMSNorm and SwiGLU use the library's fused elementwise kernels on sm_100;
@@ -28,6 +31,8 @@ from types import SimpleNamespace
 import torch
 import torch.nn.functional as F
 from torch import nn
+
+from dattri_llm_b200.models.layers import TcLinear
 
 
 @dataclass
@@ -157,10 +162,10 @@ class LlamaAttention(nn.Module):
         super().__init__()
         d, hd = cfg.hidden_size, cfg.dim_per_head
         self.n_heads, self.n_kv, self.head_dim = cfg.num_attention_heads, cfg.num_key_value_heads, hd
-        self.q_proj = nn.Linear(d, self.n_heads * hd, bias=False)
-        self.k_proj = nn.Linear(d, self.n_kv * hd, bias=False)
-        self.v_proj = nn.Linear(d, self.n_kv * hd, bias=False)
-        self.o_proj = nn.Linear(self.n_heads * hd, d, bias=False)
+        self.q_proj = TcLinear(d, self.n_heads * hd, bias=False)
+        self.k_proj = TcLinear(d, self.n_kv * hd, bias=False)
+        self.v_proj = TcLinear(d, self.n_kv * hd, bias=False)
+        self.o_proj = TcLinear(self.n_heads * hd, d, bias=False)
 
     def forward(self, x: torch.Tensor, cos, sin, attention_mask: torch.Tensor | None = None,
                 half_tables: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
@@ -191,9 +196,9 @@ class LlamaMLP(nn.Module):
 
     def __init__(self, cfg: LlamaConfig) -> None:
         super().__init__()
-        self.gate_proj = nn.Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
-        self.up_proj = nn.Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
-        self.down_proj = nn.Linear(cfg.intermediate_size, cfg.hidden_size, bias=False)
+        self.gate_proj = TcLinear(cfg.hidden_size, cfg.intermediate_size, bias=False)
+        self.up_proj = TcLinear(cfg.hidden_size, cfg.intermediate_size, bias=False)
+        self.down_proj = TcLinear(cfg.intermediate_size, cfg.hidden_size, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         from dattri_llm_b200.ops import fused
@@ -259,7 +264,7 @@ class LlamaForCausalLM(nn.Module):
         self.config = cfg
         self.frozen_probe = frozen_probe
         self.model = LlamaModel(cfg)
-        self.lm_head = nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False)
+        self.lm_head = TcLinear(cfg.hidden_size, cfg.vocab_size, bias=False)
         if cfg.tie_word_embeddings:
             self.lm_head.weight = self.model.embed_tokens.weight
         self.reset_parameters()

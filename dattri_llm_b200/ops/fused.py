@@ -132,15 +132,18 @@ class _SwiGLU(torch.autograd.Function):
 class _LinearCrossEntropy(torch.autograd.Function):
     """Sum over rows of CE(h W^T, target); bf16 logits kept for the backward, which
     rewrites them into dlogits in place (a second backward through the same graph is
-    rejected)."""
+    rejected).  Both GEMMs (logits and the input gradient ``dlogits @ W``) run on the
+    tcgen05 CTA-pair kernel."""
 
     @staticmethod
     def forward(ctx, h, weight, target):
         from dattri_llm_b200.ops import count_launch, native
+        from dattri_llm_b200.ops.gemm import STORE_BF16, gemm_tn
 
         count_launch()
 
-        logits = torch.nn.functional.linear(h, weight)
+        logits = torch.empty(h.shape[0], weight.shape[0], dtype=torch.bfloat16, device=h.device)
+        gemm_tn(h, weight, logits, mode=STORE_BF16)
         loss, lse = native().ce_fwd(logits, target)
         ctx.logits = logits
         ctx.save_for_backward(h, weight, lse, target)
@@ -159,7 +162,13 @@ class _LinearCrossEntropy(torch.autograd.Function):
                                "(it reuses its logits buffer in place)")
         ctx.logits = None
         native().ce_bwd_inplace(logits, lse, target, g.reshape(1).float().contiguous())
-        dh = logits @ weight if ctx.needs_input_grad[0] else None
+        dh = None
+        if ctx.needs_input_grad[0]:
+            from dattri_llm_b200.ops.gemm import STORE_BF16, gemm_tn
+            from dattri_llm_b200.ops.linear import transposed
+
+            dh = torch.empty(h.shape[0], weight.shape[1], dtype=torch.bfloat16, device=h.device)
+            gemm_tn(logits, transposed(weight), dh, mode=STORE_BF16)
         dw = logits.t() @ h if ctx.needs_input_grad[1] else None
         return dh, dw, None
 

@@ -1,0 +1,106 @@
+"""Dense layers on the tcgen05 CTA-pair GEMM and the capture projections fused into them.
+
+* the pair kernel's narrow last column tile (N not a multiple of 256) against fp32;
+* one launch producing a layer's output and its token-major projected input against
+  two separate fp32 products;
+* :class:`TcLinear` forward / input gradient against ``F.linear`` in fp32;
+* a LoGra capture of a Llama decoder with the projections computed inside the layers'
+  GEMMs equals the capture with the hooks' own projection launches.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize(("m", "n", "k"), [(1024, 2112, 512), (600, 320, 256), (512, 64 + 256 * 3, 128),
+                                           (2048, 4000, 1024)])
+def test_pair_gemm_narrow_last_tile(m, n, k):
+    from dattri_llm_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    b = torch.randn(n, k, device="cuda", generator=g).bfloat16()
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_tn(a, b, out, mode=ops.STORE_BF16)
+    want = a.float() @ b.float().T
+    torch.testing.assert_close(out.float(), want, rtol=1.6e-2, atol=1e-2 * float(want.abs().max()))
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("segs", "t", "d_in", "n", "k"), [(4, 256, 512, 1024, 64), (2, 512, 2048, 512, 64),
+                                                          (3, 128, 256, 256, 192)])
+def test_gemm_with_projection_tail(segs, t, d_in, n, k):
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.ops.linear import gemm_with_tail
+
+    g = torch.Generator(device="cuda").manual_seed(n + k)
+    x = torch.randn(segs * t, d_in, device="cuda", generator=g).bfloat16()
+    w = torch.randn(n, d_in, device="cuda", generator=g).bfloat16()
+    p_t = torch.randn(k, d_in, device="cuda", generator=g).bfloat16()
+    y, a_pt = gemm_with_tail(x, w, p_t, t)
+    want_y = x.float() @ w.float().T
+    want_a = (x.float() @ p_t.float().T).view(segs, t, k).transpose(1, 2)
+    torch.testing.assert_close(y.float(), want_y, rtol=1.6e-2, atol=1e-2 * float(want_y.abs().max()))
+    torch.testing.assert_close(a_pt.float(), want_a, rtol=1.6e-2, atol=1e-2 * float(want_a.abs().max()))
+    ops.check_device_errors()
+
+
+def test_tc_linear_forward_and_input_gradient():
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.models.layers import TcLinear
+
+    torch.manual_seed(0)
+    lin = TcLinear(512, 768, bias=False).cuda().bfloat16()
+    x = torch.randn(4, 100, 512, device="cuda").bfloat16().requires_grad_(True)
+    y = lin(x)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xf = x.detach().float().requires_grad_(True)
+    yf = torch.nn.functional.linear(xf, lin.weight.float())
+    yf.backward(dy.float())
+    torch.testing.assert_close(y.float(), yf, rtol=1.6e-2, atol=1e-2 * float(yf.abs().max()))
+    torch.testing.assert_close(x.grad.float(), xf.grad, rtol=1.6e-2, atol=1e-2 * float(xf.grad.abs().max()))
+    ops.check_device_errors()
+
+
+def _capture_llama(fused: bool):
+    from dattri_llm_b200 import CaptureCallback, HookManager, HookManagerConfig
+    from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM, token_sum_loss
+    from dattri_llm_b200.ops import linear as tc
+
+    cfg = LlamaConfig.tiny(hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
+                           vocab_size=1024)
+    model = LlamaForCausalLM(cfg, frozen_probe=True)
+    model.reset_parameters(seed=0)
+    model = model.cuda().bfloat16().requires_grad_(False)
+    proj = {"__default__": {"style": "logra", "proj_dim": 64}}
+    cb = CaptureCallback()
+    hm = HookManager(model, HookManagerConfig(linear_io=[r"\.(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj)$"],
+                                              projection_kwargs=proj, include_frozen=True, capture_style="auto"),
+                     callbacks=[cb])
+    ids = torch.randint(0, cfg.vocab_size, (3, 128), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    old = tc.set_fused_capture(fused)
+    try:
+        with hm.collect():
+            token_sum_loss(model, {"input_ids": ids}).backward()
+    finally:
+        tc.set_fused_capture(old)
+        hm.remove()
+    return cb.record.gradient
+
+
+def test_fused_capture_equals_hook_projections():
+    from dattri_llm_b200 import ops
+
+    fused, plain = _capture_llama(True), _capture_llama(False)
+    assert sorted(fused.data) == sorted(plain.data) and len(fused.data) == 14
+    for name in plain.data:
+        got, want = fused.data[name], plain.data[name]
+        assert isinstance(got, torch.Tensor) and got.shape == want.shape, name
+        scale = float(want.float().abs().max())
+        torch.testing.assert_close(got.float(), want.float(), rtol=3e-2, atol=3e-2 * scale, msg=name)
+    ops.check_device_errors()
