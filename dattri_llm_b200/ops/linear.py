@@ -24,7 +24,7 @@ import weakref
 
 import torch
 
-_WT_CACHE: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+_WT_CACHE: dict[int, tuple] = {}  # id(weight) -> (weak ref, version key, weight^T)
 _FUSED_CAPTURE = [True]
 
 
@@ -41,13 +41,18 @@ def fused_capture_enabled() -> bool:
 
 
 def transposed(weight: torch.Tensor) -> torch.Tensor:
-    """``weight^T`` contiguous (the K-major operand of ``dy @ weight``), cached per version."""
-    hit = _WT_CACHE.get(weight)
+    """``weight^T`` contiguous (the K-major operand of ``dy @ weight``), cached per version.
+
+    Keyed by the tensor's identity (checked through a weak reference, and dropped when the
+    weight is freed); a new version, storage or shape recomputes it."""
     key = (weight._version, weight.data_ptr(), tuple(weight.shape), weight.dtype)
-    if hit is not None and hit[0] == key:
-        return hit[1]
+    hit = _WT_CACHE.get(id(weight))
+    if hit is not None and hit[0]() is weight and hit[1] == key:
+        return hit[2]
     wt = weight.detach().t().contiguous()
-    _WT_CACHE[weight] = (key, wt)
+    if hit is None or hit[0]() is not weight:
+        weakref.finalize(weight, _WT_CACHE.pop, id(weight), None)
+    _WT_CACHE[id(weight)] = (weakref.ref(weight), key, wt)
     return wt
 
 
