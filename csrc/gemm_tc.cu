@@ -16,6 +16,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -121,6 +122,34 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
           w[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
         *reinterpret_cast<uint4*>(Cr + n0 + c0 + cc) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  if ((p.c_mode == kStoreBF16 || (p.c_mode == kStoreBF16Tail && n0 < p.n_main)) && c0 + 32 <= BN &&
+      n0 + c0 + 32 <= p.N && (p.ldc & 7) == 0 &&
+      ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c) & 15) == 0)) {
+    // Row-major bf16 through the warp-private transpose: each store instruction writes eight
+    // whole 64-byte row segments (full 32-byte sectors) instead of 32 rows' 16-byte pieces.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = alpha * __uint_as_float(r[j]);
+    __syncwarp();
+    const int cc = (lane & 3) * 8;
+    __nv_bfloat16* Cz = static_cast<__nv_bfloat16*>(Cbase) + (long long)zc * p.batch_stride_c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int rr = q * 8 + (lane >> 2);
+      const int grow = m0 + warp * 32 + rr;
+      if (grow < limit) {
+        const float* t = tw + rr * 33 + cc;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * e], t[2 * e + 1]);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(Cz + (long long)grow * p.ldc + n0 + c0 + cc) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     __syncwarp();
@@ -559,9 +588,44 @@ struct TileSched {
   int jobs;
   int n_rot;    // dense tiles: column-tile index rotation (a sharded B's own columns first)
   int n_major;  // dense tiles: column tile is the slow index (all row blocks of one B tile in turn)
-  int tail_w;   // CTA-pair kernel: width of the last column tile when N is not a multiple of 256
-                // (a multiple of 32, >= 64; 0 = every tile is 256 wide)
+  int tail_w;   // CTA-pair kernel: width of the last column tile when N is not a multiple of the
+                // tile width (a multiple of 32, >= 64; 0 = every tile is full width)
+  int tile_w;   // CTA-pair kernel: column tile width, 256 (0 means 256) or 128
+  // Stream-K tail (CTA-pair kernel, dense tiles): the last sk_tiles tiles run as two K halves
+  // on two pairs in the same wave.  The first half stores its fp32 partial in sk_ws (one
+  // 256 x 256 block per split tile) and sets its warps' flags to sk_epoch; the second half
+  // waits for them (bounded), adds the partial and runs the epilogue.
+  int sk_tiles;
+  float* sk_ws;
+  int* sk_flags;  // split tile x 8 (CTA rank x epilogue warp), monotonic epochs
+  int sk_epoch;
 };
+
+// A pair kernel work unit: a whole tile (role 0) or a K half of a stream-K tile (role 1: the
+// first half, which hands its partial over; role 2: the second half, which finishes the tile).
+struct PairUnit {
+  int tile, k_lo, k_hi, role, sk;
+};
+
+__device__ __forceinline__ PairUnit pair_unit(const TileSched& ts, int total_tiles, int kblocks, int u) {
+  PairUnit w;
+  const int dp = total_tiles - ts.sk_tiles;
+  if (u < dp) {
+    w.tile = u;
+    w.k_lo = 0;
+    w.k_hi = kblocks;
+    w.role = 0;
+    w.sk = -1;
+  } else {
+    const int v = u - dp, half = v & 1, kh = kblocks >> 1;
+    w.sk = v >> 1;
+    w.tile = dp + w.sk;
+    w.k_lo = half ? kh : 0;
+    w.k_hi = half ? kblocks : kh;
+    w.role = 1 + half;
+  }
+  return w;
+}
 
 struct TileCoord {
   int m0, n0, za, zb, zc, limit;
@@ -754,8 +818,9 @@ __device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const
   }
   tn += ts.n_rot;
   if (tn >= ts.tiles_n) tn -= ts.tiles_n;
-  c.n0 = tn * 256;
-  c.w = (ts.tail_w != 0 && tn == ts.tiles_n - 1) ? ts.tail_w : 256;
+  const int tile_w = ts.tile_w != 0 ? ts.tile_w : 256;
+  c.n0 = tn * tile_w;
+  c.w = (ts.tail_w != 0 && tn == ts.tiles_n - 1) ? ts.tail_w : tile_w;
   if (ts.tile_prefix != nullptr) {
     int lo = 0, hi = ts.jobs - 1;
     while (lo < hi) {
@@ -810,8 +875,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int pair = blockIdx.x >> 1;
   const int pairs = gridDim.x >> 1;
   const int kblocks = (p.K + BK - 1) / BK;
-  const int total = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
-                                              : ts.tiles_n * ts.tiles_m * ts.batch;
+  const int total_tiles = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
+                                                    : ts.tiles_n * ts.tiles_m * ts.batch;
+  const int total = total_tiles + ts.sk_tiles;  // work units: a split tile counts twice
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -841,9 +907,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
       bool alive = true;
       unsigned ready = 0u;  // staged: remote owners already waited for
       const int kb_rot = (kStaged && sa.mode == 1) ? (sa.self * sa.shard) / BK : 0;
+      // B rows staged per CTA and k-step: half the tile width (the tensor map's box height)
+      const uint32_t tx_bytes = 2u * (uint32_t)(C::kTileA + ((ts.tile_w != 0 ? ts.tile_w : 256) / 2) * BK * 2);
       const int own_lo = kStaged ? sa.self * sa.shard : 0;
-      for (int tile = pair; tile < total && alive; tile += pairs) {
-        const TileCoord c = decode_pair_tile(ts, p, tile);
+      for (int u = pair; u < total && alive; u += pairs) {
+        const PairUnit un = pair_unit(ts, total_tiles, kblocks, u);
+        const TileCoord c = decode_pair_tile(ts, p, un.tile);
         // cta_group::2 splits the tile's N columns over the pair: each CTA stages w / 2 rows of B
         const int brow = c.n0 + (c.w >> 1) * (int)rank;
         // mode 0: this CTA's B rows belong to one owner for the whole tile
@@ -871,7 +940,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
           }
         }
-        for (int i = 0; i < kblocks; ++i) {
+        for (int i = un.k_lo; i < un.k_hi; ++i) {
           const int s = g % S;
           if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, kErrWaitEmpty)) {
             alive = false;
@@ -880,7 +949,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           int kb = i + kb_rot;
           if (kb >= kblocks) kb -= kblocks;
           const int kc = kb * BK;
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::kTileA + C::kTileB));
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], tx_bytes);
           const uint32_t bar = map_shared_rank(smem_u32(&full[s]), 0);
           tma_load_3d_pair(sA + s * C::kTileA, &tmA, bar, kc, c.m0 + 128 * (int)rank, c.za);
           if constexpr (kStaged) {
@@ -912,13 +981,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
       // ---- MMA issuer (CTA 0) ----
       int g = 0, it = 0;
       bool alive = true;
-      for (int tile = pair; tile < total && alive; tile += pairs, ++it) {
+      for (int u = pair; u < total && alive; u += pairs, ++it) {
         const int b = it & 1;
-        const uint32_t idesc = idesc_bf16_f32(256, decode_pair_tile(ts, p, tile).w);
+        const PairUnit un = pair_unit(ts, total_tiles, kblocks, u);
+        const uint32_t idesc = idesc_bf16_f32(256, decode_pair_tile(ts, p, un.tile).w);
         if (!mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1, p.err, kErrWaitDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 256);
-        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+        for (int kb = un.k_lo; kb < un.k_hi; ++kb, ++g) {
           const int s = g % S;
           if (!mbar_wait(&full[s], (g / S) & 1, p.err, kErrWaitFull)) {
             alive = false;
@@ -928,7 +998,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
           const uint64_t da = smem_desc_kmajor_sw128(sA + s * C::kTileA);
           const uint64_t db = smem_desc_kmajor_sw128(sB + s * C::kTileB);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) tc_mma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, ((kb - un.k_lo) | k) != 0);
           tc_commit_pair(&empty[s]);
         }
         tc_commit_pair(&acc_full[b]);
@@ -973,12 +1044,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     float* twp = tw + warp * (32 * 33);
     int it = 0;
-    for (int tile = pair; tile < total; tile += pairs, ++it) {
-      const TileCoord c = decode_pair_tile(ts, p, tile);
+    for (int u = pair; u < total; u += pairs, ++it) {
+      const PairUnit un = pair_unit(ts, total_tiles, kblocks, u);
+      const TileCoord c = decode_pair_tile(ts, p, un.tile);
       const int b = it & 1;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, p.err, kErrWaitDone));
       if (!ok) break;
       tc_fence_after();
+      // stream-K: this thread's row of the split tile's fp32 partial, and its warp's flag
+      float* part = un.sk >= 0 ? ts.sk_ws + (long long)un.sk * 65536 + (long long)(rank * 128 + warp * 32 + lane) * 256
+                               : nullptr;
+      int* flag = un.sk >= 0 ? ts.sk_flags + un.sk * 8 + rank * 4 + warp : nullptr;
+      if (un.role == 2) {
+        if (lane == 0) stage_wait(flag, ts.sk_epoch, p.err);
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < c.w; c0 += 32) {
         uint32_t r[32];
@@ -989,7 +1069,31 @@ __global__ void __launch_bounds__(kPThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&acc_empty[b]), 0));
         }
+        if (un.role == 1) {  // hand the first K half over: fp32, one 128-byte row segment per thread
+          float4* dst = reinterpret_cast<float4*>(part + c0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          continue;
+        }
+        if (un.role == 2) {
+          const float4* src = reinterpret_cast<const float4*>(part + c0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = src[q];
+            r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + v.x);
+            r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + v.y);
+            r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + v.z);
+            r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + v.w);
+          }
+        }
         store_chunk<256>(p, r, p.C, c.zc, c.m0 + 128 * (int)rank, c.n0, c0, warp, lane, c.limit, twp);
+      }
+      if (un.role == 1) {  // publish: the partial's stores before the flag (release, GPU scope)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(flag), "r"(ts.sk_epoch) : "memory");
       }
     }
   }
@@ -1184,11 +1288,69 @@ int pair_clusters() {
 // Width of the last column tile of an N-wide pair GEMM: the remainder rounded up to a multiple
 // of 32 (at least 64), so that a narrow remainder does not cost a whole 256-wide tile of MMAs
 // (0 when N is a multiple of 256).
-int pair_tail_width(int N) {
-  const int rem = N % 256;
+int pair_tail_width(int N, int tile_w = 256) {
+  const int rem = N % tile_w;
   if (rem == 0) return 0;
   const int w = (rem + 31) / 32 * 32;
   return w < 64 ? 64 : w;
+}
+
+// Column tile width of a dense pair GEMM.  Measured on the bench step's shapes, 128-wide
+// tiles (M = 256, N = 128 MMAs) ran 1.5-1.9x slower than 256-wide ones even where they
+// quantize into fewer waves (8192 x 2048 x 2048: 96 vs 57 us), so every dense launch keeps
+// 256; the width stays a kernel parameter (TileSched::tile_w).
+int pair_tile_width(long long /*row_tiles*/, int /*N*/, int /*clusters*/) { return 256; }
+
+// Stream-K tail buffers of one (device, stream): launches on one stream run in order, so they
+// can share one workspace; epochs tell this launch's flags from earlier ones'.
+struct SkBuffers {
+  float* ws = nullptr;
+  int* flags = nullptr;
+  int epoch = 0;
+};
+constexpr int kSkMaxTiles = 64;  // 16 MiB of fp32 partials per (device, stream)
+std::mutex g_sk_mutex;
+std::map<std::pair<int, cudaStream_t>, SkBuffers> g_sk_buffers;
+
+// Split the last, partly filled wave of a dense pair GEMM into K halves when that wave holds
+// at most half as many tiles as there are resident pairs: its 2 * rem half-tiles then run in
+// one wave of half the length (e.g. 256 tiles on 74 pairs: 3.5 waves of time instead of 4).
+// Only for plain stores, K of at least eight blocks, and outside stream capture (the epoch is
+// a launch argument).
+void plan_stream_k(TileSched& ts, const GemmParams& p, long long tiles, int clusters, cudaStream_t stream) {
+  ts.sk_tiles = 0;
+  if (clusters <= 0 || tiles <= clusters) return;
+  const long long rem = tiles % clusters;
+  if (rem == 0 || 2 * rem > clusters || rem > kSkMaxTiles || (p.K + BK - 1) / BK < 8) return;
+  if (!(p.c_mode == kStoreBF16 || p.c_mode == kStoreBF16Tail || (p.c_mode == kStoreF32 && !p.beta_accumulate)))
+    return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_sk_mutex);
+  SkBuffers& b = g_sk_buffers[{dev, stream}];
+  if (b.ws == nullptr) {
+    float* ws = nullptr;
+    int* flags = nullptr;
+    if (cudaMalloc(&ws, (size_t)kSkMaxTiles * 65536 * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&flags, (size_t)kSkMaxTiles * 8 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(flags, 0, (size_t)kSkMaxTiles * 8 * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      if (ws != nullptr) cudaFree(ws);
+      if (flags != nullptr) cudaFree(flags);
+      return;  // no workspace: plain waves
+    }
+    b.ws = ws;
+    b.flags = flags;
+  }
+  ts.sk_tiles = (int)rem;
+  ts.sk_ws = b.ws;
+  ts.sk_flags = b.flags;
+  ts.sk_epoch = ++b.epoch;
 }
 
 // Launch the pair kernel on up to `max_tiles` 256 x 256 tiles; false if it cannot run here.
@@ -1198,9 +1360,11 @@ bool launch_pair(const GemmOperand& A, const GemmOperand& B, const GemmParams& p
   const int clusters = pair_clusters();
   if (clusters <= 0) return false;
   if (max_tiles <= 0) return true;
+  // The B box is half a column tile: the rows one CTA of the pair stages per k-step.
+  const int bbox = (ts.tile_w != 0 ? ts.tile_w : 256) / 2;
   CUtensorMap ta = make_tmap_kmajor_bf16(A, 128);
-  CUtensorMap tb = make_tmap_kmajor_bf16(B, 128);
-  CUtensorMap tt = tail != nullptr ? make_tmap_kmajor_bf16(*tail, 128) : tb;
+  CUtensorMap tb = make_tmap_kmajor_bf16(B, bbox);
+  CUtensorMap tt = tail != nullptr ? make_tmap_kmajor_bf16(*tail, bbox) : tb;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(max_tiles, clusters), 1, 1);
   cfg.blockDim = dim3(kPThreads, 1, 1);
@@ -1386,11 +1550,16 @@ bool gemm_tn_tail_launch(const GemmOperand& A, const GemmOperand& B, const GemmO
   p.batch = 1;
   p.b_shared = 1;
   TileSched ts{};
-  ts.tiles_n = p.n_main / 256 + 1;
   ts.tiles_m = (p.M + 255) / 256;
   ts.batch = 1;
-  ts.tail_w = pair_tail_width(p.N - p.n_main) == 0 ? 256 : pair_tail_width(p.N - p.n_main);
-  return launch_pair(A, B, p, ts, (long long)ts.tiles_n * ts.tiles_m, stream, &Btail);
+  ts.tile_w = pair_tile_width(ts.tiles_m, p.n_main, pair_clusters());
+  if (p.n_main % ts.tile_w != 0 || p.N - p.n_main > ts.tile_w) ts.tile_w = 256;
+  ts.tiles_n = p.n_main / ts.tile_w + 1;
+  ts.tail_w = pair_tail_width(p.N - p.n_main, ts.tile_w) == 0 ? ts.tile_w
+                                                                 : pair_tail_width(p.N - p.n_main, ts.tile_w);
+  const long long ptiles = (long long)ts.tiles_n * ts.tiles_m;
+  plan_stream_k(ts, p, ptiles, pair_clusters(), stream);
+  return launch_pair(A, B, p, ts, ptiles, stream, &Btail);
 }
 
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
@@ -1404,12 +1573,15 @@ void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, in
   const bool skinny = tiles * 2 <= 160 && (p.K + BK - 1) / BK >= 8;
   if (p.splits == 1 && bn == 256 && p.K > 0 && !skinny) {
     TileSched ts{};
-    ts.tiles_n = (p.N + 255) / 256;
     ts.tiles_m = (p.M + 255) / 256;
     ts.batch = p.batch;
     ts.jobs = 0;
-    ts.tail_w = pair_tail_width(p.N);
-    if (launch_pair(A, B, p, ts, (long long)ts.tiles_n * ts.tiles_m * ts.batch, stream)) return;
+    ts.tile_w = pair_tile_width((long long)ts.tiles_m * p.batch, p.N, pair_clusters());
+    ts.tiles_n = (p.N + ts.tile_w - 1) / ts.tile_w;
+    ts.tail_w = pair_tail_width(p.N, ts.tile_w);
+    const long long ptiles = (long long)ts.tiles_n * ts.tiles_m * ts.batch;
+    plan_stream_k(ts, p, ptiles, pair_clusters(), stream);
+    if (launch_pair(A, B, p, ts, ptiles, stream)) return;
   }
   if (p.splits == 1 && bn >= 64 && p.K > 0 && tiles > sm_count()) {
     TileSched ts{};

@@ -106,3 +106,29 @@ def test_fused_capture_equals_hook_projections():
         scale = float(want.float().abs().max())
         torch.testing.assert_close(got.float(), want.float(), rtol=3e-2, atol=3e-2 * scale, msg=name)
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("m", "n", "k", "tail"), [(8192, 2048, 2048, 0), (8192, 2048, 1024, 64),
+                                                   (4096, 4096, 512, 0)])
+def test_pair_gemm_stream_k_last_wave(m, n, k, tail):
+    """Shapes whose last wave of 256 x 256 tiles is under half full (e.g. 256 tiles on 74 CTA
+    pairs): those tiles run as two K halves whose partials meet through a workspace.  Two
+    launches in a row (the second reuses the workspace under a new epoch) against fp32."""
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.ops.linear import gemm_with_tail
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    for _ in range(2):
+        a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+        b = torch.randn(n, k, device="cuda", generator=g).bfloat16()
+        want = a.float() @ b.float().T
+        if tail:
+            p_t = torch.randn(tail, k, device="cuda", generator=g).bfloat16()
+            out, a_pt = gemm_with_tail(a, b, p_t, 1024)
+            want_t = (a.float() @ p_t.float().T).view(m // 1024, 1024, tail).transpose(1, 2)
+            torch.testing.assert_close(a_pt.float(), want_t, rtol=1.6e-2, atol=1e-2 * float(want_t.abs().max()))
+        else:
+            out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            ops.gemm_tn(a, b, out, mode=ops.STORE_BF16)
+        torch.testing.assert_close(out.float(), want, rtol=1.6e-2, atol=1e-2 * float(want.abs().max()))
+    ops.check_device_errors()
