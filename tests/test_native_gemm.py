@@ -63,7 +63,8 @@ def test_device_projection_matches_host_generator(kind):
 
 @pytest.mark.parametrize(("b1", "s1", "b2", "s2", "k", "d"),
                          [(2, 64, 3, 64, 64, 64), (3, 50, 5, 17, 72, 40), (4, 1, 6, 1, 128, 64),
-                          (2, 300, 2, 200, 256, 128), (1, 7, 300, 3, 16, 24)])
+                          (2, 300, 2, 200, 256, 128), (1, 7, 300, 3, 16, 24), (8, 512, 32, 512, 64, 64),
+                          (5, 700, 9, 333, 128, 128)])
 def test_ghost_gram_matches_dense_oracle(b1, s1, b2, s2, k, d):
     a1 = torch.randn(b1, s1, k, device="cuda").bfloat16()
     g1 = torch.randn(b1, s1, d, device="cuda").bfloat16()
