@@ -1,140 +1,197 @@
 """Per-step parameters, batches and optimizer moments of a training trajectory.
 
-File layout (shared with the reference, ``dattri_llm/gradient/snapshots.py``):
-``theta_<s>.pt`` (trainable parameters; ``theta_<s>.ref`` holds the step whose
-file to reuse), ``batch_<s>.pt``, ``dynamics_<s>_{pre,post}.pt`` and the manifest
-``snapshots.json``.  A trajectory method replays any step from these files
-instead of storing its gradients.
+Trajectory methods (DVEmb, AdamW-influence, LESS replays) revisit every training step.
+Instead of storing per-step gradients they can store what regenerates them: the trainable
+parameters before the step, the step's batch and, for Adam-family optimizers, the moments
+before and after the update.  One directory holds one trajectory:
+
+    snapshots.json              marker file ({"format": 1}); identifies the directory
+    theta_<s>.pt                {parameter name: tensor} of the trainable parameters
+    theta_<s>.ref               the text "<t>": step s had the same parameters as step t
+    batch_<s>.pt                the batch of step s (tensors on the host)
+    dynamics_<s>_pre.pt         optimizer moments before step s's update
+    dynamics_<s>_post.pt        ... and after it
+
+The names and contents are the reference's (``dattri_llm/gradient/snapshots.py``), so a
+trajectory recorded by either framework replays in the other.  Files are written to a
+temporary name and renamed into place, so a reader never sees a half-written snapshot.
 """
 
 from __future__ import annotations
 
 import json
+import os
 import pathlib
-from collections.abc import Iterator, Mapping
+import re
+from collections.abc import Callable, Iterator, Mapping
 
 import torch
 from torch import nn
 
 MANIFEST_FILE = "snapshots.json"
+_ENTRY = re.compile(r"^(theta|batch|dynamics)_(\d+)(?:_(pre|post))?\.(pt|ref)$")
 
 
-def _to_cpu(obj: object) -> object:
+def _host_copy(obj: object) -> object:
+    """*obj* with every tensor detached and moved to the host (containers rebuilt)."""
     if isinstance(obj, torch.Tensor):
-        return obj.detach().to("cpu")
+        return obj.detach().cpu()
     if isinstance(obj, dict):
-        return {k: _to_cpu(v) for k, v in obj.items()}
+        return {key: _host_copy(val) for key, val in obj.items()}
     if isinstance(obj, (list, tuple)):
-        return type(obj)(_to_cpu(v) for v in obj)
+        return type(obj)(map(_host_copy, obj))
     return obj
 
 
-def _steps_of(root: pathlib.Path, pattern: str) -> set[int]:
-    return {int(p.stem.split("_")[1]) for p in root.glob(pattern)}
+def _write_atomic(path: pathlib.Path, write: Callable[[pathlib.Path], None]) -> None:
+    tmp = path.with_name(f".{path.name}.tmp{os.getpid()}")
+    write(tmp)
+    os.replace(tmp, path)
 
 
 class TrajectorySnapshots:
-    """A directory of per-step snapshots."""
+    """A snapshot directory (created, with its marker file, when missing)."""
 
     def __init__(self, root: str | pathlib.Path) -> None:
         self.root = pathlib.Path(root)
         self.root.mkdir(parents=True, exist_ok=True)
-        manifest = self.root / MANIFEST_FILE
-        if not manifest.exists():
-            manifest.write_text(json.dumps({"format": 1}))
+        marker = self.root / MANIFEST_FILE
+        if not marker.exists():
+            _write_atomic(marker, lambda p: p.write_text(json.dumps({"format": 1})))
 
     @staticmethod
     def is_snapshot_dir(path: object) -> bool:
-        """Whether *path* is a snapshot directory (has the manifest)."""
-        return isinstance(path, (str, pathlib.Path)) and (pathlib.Path(path) / MANIFEST_FILE).is_file()
+        """Whether *path* names a snapshot directory (it holds the marker file)."""
+        if not isinstance(path, (str, pathlib.Path)):
+            return False
+        return (pathlib.Path(path) / MANIFEST_FILE).is_file()
 
     def __repr__(self) -> str:
         return f"TrajectorySnapshots({str(self.root)!r}, steps={len(self.steps())})"
 
-    def save_parameters(self, step: int, model: nn.Module, *, same_as: int | None = None) -> None:
-        """Save the trainable parameters at *step* (or a reference to step *same_as*)."""
-        if same_as is not None:
-            (self.root / f"theta_{step}.ref").write_text(str(int(same_as)))
-            return
-        torch.save({n: p.detach().to("cpu") for n, p in model.named_parameters() if p.requires_grad},
-                   self.root / f"theta_{step}.pt")
-
-    def _parameter_file(self, step: int) -> pathlib.Path:
-        ref = self.root / f"theta_{step}.ref"
-        if ref.exists():
-            return self._parameter_file(int(ref.read_text()))
-        path = self.root / f"theta_{step}.pt"
-        if not path.exists():
-            raise KeyError(f"no parameter snapshot for step {step} in {self.root}.")
-        return path
-
-    def load_parameters(self, step: int, model: nn.Module) -> None:
-        """Copy step *step*'s parameters into *model*.
-
-        Raises:
-            KeyError: for a missing snapshot or parameter.
-        """
-        state = torch.load(self._parameter_file(step), weights_only=True)
-        with torch.no_grad():
-            for name, p in model.named_parameters():
-                if not p.requires_grad:
-                    continue
-                if name not in state:
-                    raise KeyError(f"parameter {name!r} has no snapshot at step {step}.")
-                p.copy_(state[name].to(p.device, p.dtype))
-
-    def save_batch(self, step: int, batch: object) -> None:
-        """Save the batch of *step* (moved to host)."""
-        torch.save(_to_cpu(batch), self.root / f"batch_{step}.pt")
-
-    def load_batch(self, step: int) -> object:
-        """The batch of *step*."""
-        path = self.root / f"batch_{step}.pt"
-        if not path.exists():
-            raise KeyError(f"no batch snapshot for step {step} in {self.root}.")
-        return torch.load(path, weights_only=False)
-
-    def save_dynamics(self, step: int, side: str, entry: dict) -> None:
-        """Save optimizer moments before (``"pre"``) or after (``"post"``) *step*'s update."""
-        if side not in ("pre", "post"):
-            raise ValueError(f"side must be 'pre' or 'post', got {side!r}.")
-        torch.save(_to_cpu(entry), self.root / f"dynamics_{step}_{side}.pt")
-
-    def load_dynamics(self, step: int, side: str) -> dict | None:
-        """The saved moments, or ``None``."""
-        path = self.root / f"dynamics_{step}_{side}.pt"
-        return torch.load(path, weights_only=False) if path.exists() else None
-
-    def dynamics_steps(self) -> list[int]:
-        """Steps with both pre and post moments."""
-        return sorted(_steps_of(self.root, "dynamics_*_pre.pt") & _steps_of(self.root, "dynamics_*_post.pt"))
+    # ------------------------------------------------------------------ directory scan
+    def _index(self) -> dict[str, set[int]]:
+        """Steps present per kind: ``theta`` (file or reference), ``batch``, ``pre``, ``post``."""
+        found: dict[str, set[int]] = {"theta": set(), "batch": set(), "pre": set(), "post": set()}
+        for entry in os.scandir(self.root):
+            m = _ENTRY.match(entry.name)
+            if m is None:
+                continue
+            kind, step, side, ext = m.group(1), int(m.group(2)), m.group(3), m.group(4)
+            if kind == "dynamics" and side is not None and ext == "pt":
+                found[side].add(step)
+            elif kind == "theta" or (kind == "batch" and ext == "pt"):
+                found[kind].add(step)
+        return found
 
     def steps(self) -> list[int]:
-        """Steps with both parameters and a batch."""
-        params = _steps_of(self.root, "theta_*.pt") | _steps_of(self.root, "theta_*.ref")
-        return sorted(params & _steps_of(self.root, "batch_*.pt"))
+        """Steps that can be replayed: parameters (or a reference to them) and a batch."""
+        idx = self._index()
+        return sorted(idx["theta"] & idx["batch"])
+
+    def dynamics_steps(self) -> list[int]:
+        """Steps with optimizer moments from both sides of the update."""
+        idx = self._index()
+        return sorted(idx["pre"] & idx["post"])
+
+    # ------------------------------------------------------------------ parameters
+    def save_parameters(self, step: int, model: nn.Module, *, same_as: int | None = None) -> None:
+        """Record the trainable parameters before *step*; with *same_as*, only note that they
+        equal the ones recorded for that step (no tensor file)."""
+        if same_as is not None:
+            _write_atomic(self.root / f"theta_{step}.ref", lambda p: p.write_text(str(int(same_as))))
+            return
+        state = {name: t.detach().cpu() for name, t in model.named_parameters() if t.requires_grad}
+        _write_atomic(self.root / f"theta_{step}.pt", lambda p: torch.save(state, p))
+
+    def _resolve_parameters(self, step: int) -> pathlib.Path:
+        """Follow ``.ref`` links from *step* to the tensor file they end at."""
+        seen: list[int] = []
+        while True:
+            link = self.root / f"theta_{step}.ref"
+            if not link.exists():
+                break
+            if step in seen:
+                raise KeyError(f"parameter references loop through steps {seen + [step]} in {self.root}")
+            seen.append(step)
+            step = int(link.read_text().strip())
+        target = self.root / f"theta_{step}.pt"
+        if not target.exists():
+            via = f" (reached through {seen})" if seen else ""
+            raise KeyError(f"step {step} has no recorded parameters in {self.root}{via}")
+        return target
+
+    def load_parameters(self, step: int, model: nn.Module) -> None:
+        """Write the parameters recorded for *step* into *model*'s trainable parameters.
+
+        Raises:
+            KeyError: the step, or one of the model's trainable parameters, was not recorded.
+        """
+        state = torch.load(self._resolve_parameters(step), weights_only=True)
+        trainable = [(name, t) for name, t in model.named_parameters() if t.requires_grad]
+        absent = [name for name, _ in trainable if name not in state]
+        if absent:
+            raise KeyError(f"the snapshot of step {step} lacks trainable parameter(s) {absent[:4]}")
+        with torch.no_grad():
+            for name, t in trainable:
+                t.copy_(state[name].to(device=t.device, dtype=t.dtype))
+
+    # ------------------------------------------------------------------ batches
+    def save_batch(self, step: int, batch: object) -> None:
+        """Record the batch of *step* (tensors copied to the host)."""
+        host = _host_copy(batch)
+        _write_atomic(self.root / f"batch_{step}.pt", lambda p: torch.save(host, p))
+
+    def load_batch(self, step: int) -> object:
+        """The batch recorded for *step*.
+
+        Raises:
+            KeyError: none was recorded.
+        """
+        path = self.root / f"batch_{step}.pt"
+        if not path.is_file():
+            raise KeyError(f"step {step} has no recorded batch in {self.root}")
+        return torch.load(path, weights_only=False)
+
+    # ------------------------------------------------------------------ optimizer moments
+    def save_dynamics(self, step: int, side: str, entry: dict) -> None:
+        """Record optimizer moments of *step*: *side* ``"pre"`` (before its update) or
+        ``"post"`` (after it)."""
+        if side not in ("pre", "post"):
+            raise ValueError(f"dynamics side is 'pre' or 'post', not {side!r}.")
+        host = _host_copy(entry)
+        _write_atomic(self.root / f"dynamics_{step}_{side}.pt", lambda p: torch.save(host, p))
+
+    def load_dynamics(self, step: int, side: str) -> dict | None:
+        """The moments recorded for *step* and *side*, or ``None`` when absent."""
+        path = self.root / f"dynamics_{step}_{side}.pt"
+        if not path.is_file():
+            return None
+        return torch.load(path, weights_only=False)
 
 
 class LazyDynamics(Mapping):
-    """``{step: assembled dynamics}`` read from a snapshot directory on access."""
+    """Read-only ``{step: assemble(pre, post)}`` over a snapshot directory's moments,
+    loaded from disk when a step is looked up (the step list is fixed at construction)."""
 
-    def __init__(self, snapshots: TrajectorySnapshots, assemble) -> None:
-        self._snapshots = snapshots
+    def __init__(self, snapshots: TrajectorySnapshots, assemble: Callable[[dict, dict], dict]) -> None:
+        self._source = snapshots
         self._assemble = assemble
-        self._steps = snapshots.dynamics_steps()
+        self._available = tuple(snapshots.dynamics_steps())
 
     def __getitem__(self, step: int) -> dict:
-        pre = self._snapshots.load_dynamics(step, "pre")
-        post = self._snapshots.load_dynamics(step, "post")
+        if step not in self._available:
+            raise KeyError(step)
+        pre, post = self._source.load_dynamics(step, "pre"), self._source.load_dynamics(step, "post")
         if pre is None or post is None:
             raise KeyError(step)
         return self._assemble(pre, post)
 
     def __iter__(self) -> Iterator[int]:
-        return iter(self._steps)
+        return iter(self._available)
 
     def __len__(self) -> int:
-        return len(self._steps)
+        return len(self._available)
 
     def __contains__(self, step: object) -> bool:
-        return step in self._steps
+        return step in self._available
