@@ -197,8 +197,9 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// Persistent form for narrow factors (K + D <= 256, e.g. LoGra-projected layers), 192 threads:
-// warp 4 = TMA producer, warp 5 = MMA issuer, warps 0-3 = epilogue.  A CTA walks a contiguous
+// Persistent form for narrow factors (K + D <= 256, e.g. LoGra-projected layers), 320 threads:
+// warp 8 = TMA producer, warp 9 = MMA issuer, warps 0-7 = epilogue (warps w and w + 4 read the
+// same TMEM lane quadrant -- the same 32 side-1 rows -- and split the tile's columns).  A CTA walks a contiguous
 // run of (row block, column block) tiles in row-major order.  The side-1 row block (A1 and G1,
 // at most four 64-wide blocks) is loaded once per row block and stays in shared memory; the
 // side-2 blocks stream through an 8-stage pipeline.  Two TMEM accumulator pairs (Ka | Kg, 256
@@ -207,8 +208,9 @@ __global__ void __launch_bounds__(128, 1)
 // across chunks and tiles and flushes it when the column sample j (or the row block) changes:
 // one warp-reduced fp32 atomic per (warp, j) instead of one per tile.
 constexpr int kRes = 4;   // resident side-1 blocks
-constexpr int kS2 = 8;    // side-2 stages
-constexpr int kScratch = 4 * 32 * 33 * 4;  // per epilogue warp: 32 rows x 33 floats
+constexpr int kS2 = 7;    // side-2 stages
+constexpr int kEpiWarps = 8;
+constexpr int kScratch = kEpiWarps * 32 * 33 * 4;  // per epilogue warp: 32 rows x 33 floats
 constexpr int kPSmem = (kRes + kS2) * kTile + kScratch + 1024 + 512;
 
 struct GhostRun {
@@ -230,7 +232,7 @@ struct GhostRun {
   }
 };
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     ghost_gram_persistent(const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tA2,
                           const __grid_constant__ CUtensorMap tG1, const __grid_constant__ CUtensorMap tG2,
                           GhostParams p) {
@@ -284,19 +286,19 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     mbar_init(s1_full, 1);
     mbar_init(s1_empty, 1);
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       int g = 0, cur_rb = -1, loads = 0;
       bool alive = true;
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = max(0, g - kS2); i < g; ++i) mbar_wait(&full[i % kS2], (i / kS2) & 1, p.err, kErrWaitFull);
       if (loads > 0) mbar_wait(s1_full, (loads - 1) & 1, p.err, kErrWaitFull);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
       int g = 0, it = 0, cur_rb = -1, loads = 0;
@@ -367,7 +369,9 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---- epilogue: warps 0-3, one side-1 row per thread ----
+    // ---- epilogue: warps 0-7, one side-1 row per thread, half of each tile's columns ----
+    const int quad = warp & 3;          // TMEM lane quadrant = the warp's 32 rows
+    const int col_half = (warp >> 2) * (BN / 2);
     int cur_rb = -1, cur_j = -1, my_i = 0, it = 0;
     long long my_tok = -1;
     bool row_ok = false, uniform_i = false;
@@ -391,11 +395,11 @@ __global__ void __launch_bounds__(192, 1)
         v = 0.f;
         cur_j = -1;
         cur_rb = rb;
-        const int row = rb * BM + warp * 32 + lane;
+        const int row = rb * BM + quad * 32 + lane;
         row_ok = row < p.M;
         my_i = row / p.S1;
         my_tok = (tok && row_ok) ? p.tok1[row] : -1;
-        uniform_i = __all_sync(0xffffffffu, (rb * BM + warp * 32) / p.S1 == my_i && row_ok);
+        uniform_i = __all_sync(0xffffffffu, (rb * BM + quad * 32) / p.S1 == my_i && row_ok);
       }
       const int b = it & 1;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, p.err, kErrWaitDone));
@@ -403,13 +407,13 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int n0 = cb * BN;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = col_half; c0 < col_half + BN / 2; c0 += 32) {
         uint32_t ra[32], rg[32];
-        const uint32_t lanebase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 256 + c0);
+        const uint32_t lanebase = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * 256 + c0);
         if (!tok) tmem_ld_32x32b_x32(lanebase, ra);
         tmem_ld_32x32b_x32(lanebase + 128u, rg);
         tmem_ld_wait();
-        if (c0 + 32 >= BN) {
+        if (c0 + 32 >= col_half + BN / 2) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -417,16 +421,11 @@ __global__ void __launch_bounds__(192, 1)
         const int cbase = n0 + c0;
         if (cbase >= p.N) continue;  // warp-uniform
         const long long col_tok = (tok && cbase + lane < p.N) ? p.tok2[cbase + lane] : -2;
-        float prod[32];
-#pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          if (tok) {
-            const long long t2 = __shfl_sync(0xffffffffu, col_tok, cc);
-            prod[cc] = t2 == my_tok ? __uint_as_float(rg[cc]) : 0.f;
-          } else {
-            prod[cc] = __uint_as_float(ra[cc]) * __uint_as_float(rg[cc]);  // zero past N (zero-filled rows)
-          }
-        }
+        // column cc's product (zero past N: those side-2 rows were zero-filled, or tok2 is -2)
+        auto product = [&](int cc) -> float {
+          if (tok) return __shfl_sync(0xffffffffu, col_tok, cc) == my_tok ? __uint_as_float(rg[cc]) : 0.f;
+          return __uint_as_float(ra[cc]) * __uint_as_float(rg[cc]);
+        };
         const int ncols = min(32, p.N - cbase);
         const int j_lo = cbase / p.S2, j_hi = (cbase + ncols - 1) / p.S2;
         if (j_lo == j_hi) {  // the whole chunk lies in one column sample: one sum
@@ -435,15 +434,19 @@ __global__ void __launch_bounds__(192, 1)
             v = 0.f;
             cur_j = j_lo;
           }
+          float q[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
 #pragma unroll
-          for (int w = 16; w > 0; w >>= 1)
-#pragma unroll
-            for (int cc = 0; cc < w; ++cc) prod[cc] += prod[cc + w];
-          v += prod[0];
+          for (int cc = 0; cc < 32; ++cc) {
+            if (tok)
+              q[cc & 3] += product(cc);
+            else
+              q[cc & 3] = fmaf(__uint_as_float(ra[cc]), __uint_as_float(rg[cc]), q[cc & 3]);
+          }
+          v += (q[0] + q[1]) + (q[2] + q[3]);
         } else {  // sample boundaries inside the chunk: walk the columns from shared memory
           float* row_scr = scratch + warp * (32 * 33) + lane * 33;
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) row_scr[cc] = prod[cc];
+          for (int cc = 0; cc < 32; ++cc) row_scr[cc] = product(cc);
           __syncwarp();
 #pragma unroll 1
           for (int cc = 0; cc < ncols; ++cc) {
@@ -464,7 +467,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == 9) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace
@@ -490,7 +493,7 @@ void ghost_gram_launch(const GemmOperand& a1, const GemmOperand& a2, const GemmO
     static int sms[64] = {0};
     if (sms[dev & 63] == 0) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
     const long long grid = p.diag_only ? rbn : std::min<long long>(rbn * cbn, sms[dev & 63]);
-    ghost_gram_persistent<<<(unsigned)grid, 192, kPSmem, stream>>>(t_a1, t_a2, t_g1, t_g2, p);
+    ghost_gram_persistent<<<(unsigned)grid, 320, kPSmem, stream>>>(t_a1, t_a2, t_g1, t_g2, p);
     return;
   }
   dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, 1);
