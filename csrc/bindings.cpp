@@ -173,6 +173,51 @@ void gemm_tn_tail(Tensor A, Tensor B, Tensor Btail, Tensor C, Tensor C2, int64_t
               "gemm_tn_tail: CTA pairs cannot run on this device");
 }
 
+// Transpose of the last two axes of a bf16 tensor ((..., R, C) -> (..., C, R), contiguous).
+Tensor transpose_last2(Tensor x) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() >= 2, "x: bf16 with at least two axes");
+  Tensor xc = x.stride(-1) == 1 && x.stride(-2) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                      (x.dim() == 2 || x.is_contiguous())
+                  ? x
+                  : x.contiguous();
+  const long long R = xc.size(-2), C = xc.size(-1);
+  std::vector<int64_t> shape(xc.sizes().begin(), xc.sizes().end());
+  std::swap(shape[shape.size() - 1], shape[shape.size() - 2]);
+  Tensor out = torch::empty(shape, xc.options());
+  const long long batch = R * C == 0 ? 0 : xc.numel() / (R * C);
+  TORCH_CHECK(R < (1LL << 31) && C < (1LL << 31) && batch < 65536, "transpose_last2: extent too large");
+  const bool vec_ok = (C % 8 == 0) && (R % 8 == 0);
+  if (!vec_ok) return xc.transpose(-1, -2).contiguous();
+  bw::transpose_bf16(reinterpret_cast<const __nv_bfloat16*>(xc.data_ptr()), xc.stride(-2),
+                     reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), R, (int)batch, (int)R, (int)C,
+                     at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
+// C (fp32, M x M) += alpha * At @ At^T: a covariance / Gram accumulation over the rows' K
+// samples (At is M x K, K-major), upper-triangle tiles mirrored, split-K atomic epilogue.
+void gram_acc(Tensor At, Tensor C, double alpha, Tensor err) {
+  const c10::cuda::CUDAGuard guard(At.device());
+  check_err(err);
+  auto a = operand(At, "At");
+  TORCH_CHECK(a.batch == 1, "gram_acc takes a 2-D operand");
+  check_cuda(C, "C");
+  TORCH_CHECK(C.scalar_type() == torch::kFloat32 && C.dim() == 2 && C.size(0) == a.rows && C.size(1) == a.rows &&
+                  C.stride(1) == 1,
+              "C must be a (M, M) fp32 matrix, contiguous along its rows");
+  bw::GemmParams p{};
+  p.M = p.N = (int)a.rows;
+  p.K = (int)a.cols;
+  p.alpha = (float)alpha;
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.err = err.data_ptr<int>();
+  if (p.M == 0 || p.K == 0) return;
+  bw::gram_acc_launch(a, p, at::cuda::getCurrentCUDAStream());
+}
+
 // ---- grouped GEMM: one launch for many same-shaped batched problems --------------------
 struct MapKey {
   const void* ptr;
@@ -651,8 +696,9 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
 }
 
 // Mask projection of factorized gradients: out (B, M) fp32 = sum_t R[b, t, rows] * C[b, t, cols].
-void mask_gather(Tensor R, Tensor C, Tensor rows, Tensor cols, Tensor out) {
+void mask_gather(Tensor R, Tensor C, Tensor rows, Tensor cols, Tensor out, Tensor err) {
   const c10::cuda::CUDAGuard guard(R.device());
+  check_err(err);
   for (auto* t : {&R, &C})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->is_contiguous() && t->dim() == 3 &&
                     t->size(2) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
@@ -666,7 +712,7 @@ void mask_gather(Tensor R, Tensor C, Tensor rows, Tensor cols, Tensor out) {
                   out.size(0) == R.size(0) && out.size(1) == M, "out: (B, M) fp32");
   bw::mask_gather(reinterpret_cast<const __nv_bfloat16*>(R.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(C.data_ptr()),
                   rows.data_ptr<int>(), cols.data_ptr<int>(), out.data_ptr<float>(), (int)R.size(0), (int)R.size(1),
-                  (int)R.size(2), (int)C.size(2), (int)M, at::cuda::getCurrentCUDAStream());
+                  (int)R.size(2), (int)C.size(2), (int)M, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
 }
 
 // MoE routing histogram (int32 counts, accumulated) of int64 expert ids.
@@ -1140,6 +1186,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");
   m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");
+  m.def("transpose_last2", &transpose_last2, "bf16 transpose of the last two axes (tiled through shared memory)");
+  m.def("gram_acc", &gram_acc, "C += alpha * At At^T (symmetric tiles, split-K, fp32 atomics)");
   m.def("gemm_tn_tail", &gemm_tn_tail, "C = A B^T (bf16 rows) and C2 = A Btail^T (token-major) in one launch");
   m.def("slot_reduce", &slot_reduce, "owner-side sum of reduce-scatter slots");
   m.def("allreduce_phase", &allreduce_phase, "NVLink peer all-reduce: 0 one-shot, 1 reduce-scatter, 2 all-gather");

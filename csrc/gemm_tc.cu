@@ -16,6 +16,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <stdexcept>
@@ -599,6 +600,12 @@ struct TileSched {
   float* sk_ws;
   int* sk_flags;  // split tile x 8 (CTA rank x epilogue warp), monotonic epochs
   int sk_epoch;
+  // Split-K with atomic epilogues (kAtomicF32): every tile runs as ksplit units over disjoint
+  // K ranges, each adding its partial into C.  0 or 1 = off.
+  int ksplit;
+  // Symmetric product (C = A A^T, kAtomicF32, dense, one batch): only the tiles on and above
+  // the diagonal run; an off-diagonal tile adds its transpose below the diagonal as well.
+  int sym;
 };
 
 // A pair kernel work unit: a whole tile (role 0) or a K half of a stream-K tile (role 1: the
@@ -609,6 +616,15 @@ struct PairUnit {
 
 __device__ __forceinline__ PairUnit pair_unit(const TileSched& ts, int total_tiles, int kblocks, int u) {
   PairUnit w;
+  if (ts.ksplit > 1) {
+    const int part = u % ts.ksplit;
+    w.tile = u / ts.ksplit;
+    w.k_lo = (int)((long long)kblocks * part / ts.ksplit);
+    w.k_hi = (int)((long long)kblocks * (part + 1) / ts.ksplit);
+    w.role = 0;
+    w.sk = -1;
+    return w;
+  }
   const int dp = total_tiles - ts.sk_tiles;
   if (u < dp) {
     w.tile = u;
@@ -808,6 +824,19 @@ struct PairCfg {
 __device__ __forceinline__ TileCoord decode_pair_tile(const TileSched& ts, const GemmParams& p, int tile) {
   TileCoord c;
   int rest, tn;
+  if (ts.sym) {  // upper triangle, row by row: (0,0) (0,1) .. (0,T-1) (1,1) ..
+    int tm = 0, left = tile;
+    while (left >= ts.tiles_n - tm) {
+      left -= ts.tiles_n - tm;
+      ++tm;
+    }
+    c.m0 = tm * 256;
+    c.n0 = (tm + left) * 256;
+    c.w = (ts.tail_w != 0 && tm + left == ts.tiles_n - 1) ? ts.tail_w : 256;
+    c.za = c.zb = c.zc = 0;
+    c.limit = p.M;
+    return c;
+  }
   if (ts.n_major) {  // dense only: tile = tn * (tiles_m * batch) + rest
     const int rows = ts.tiles_m * ts.batch;
     tn = tile / rows;
@@ -875,9 +904,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int pair = blockIdx.x >> 1;
   const int pairs = gridDim.x >> 1;
   const int kblocks = (p.K + BK - 1) / BK;
-  const int total_tiles = ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
-                                                    : ts.tiles_n * ts.tiles_m * ts.batch;
-  const int total = total_tiles + ts.sk_tiles;  // work units: a split tile counts twice
+  const int total_tiles = ts.sym ? ts.tiles_n * (ts.tiles_n + 1) / 2
+                          : ts.tile_prefix != nullptr ? ts.tile_prefix[ts.jobs] * ts.tiles_n
+                                                      : ts.tiles_n * ts.tiles_m * ts.batch;
+  // work units: a stream-K tile counts twice, a split-K tile ksplit times
+  const int total = ts.ksplit > 1 ? total_tiles * ts.ksplit : total_tiles + ts.sk_tiles;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -1089,6 +1120,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
         }
         store_chunk<256>(p, r, p.C, c.zc, c.m0 + 128 * (int)rank, c.n0, c0, warp, lane, c.limit, twp);
+        if (ts.sym && c.m0 != c.n0) {  // the mirrored block below the diagonal (atomic fp32)
+          const int row = c.m0 + 128 * (int)rank + warp * 32 + lane;
+          float* Cf = static_cast<float*>(p.C);
+          if (row < p.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = c.n0 + c0 + j;  // consecutive lanes add consecutive rows' entries
+              if (n < p.N) atomicAdd(Cf + (long long)n * p.ldc + row, p.alpha * __uint_as_float(r[j]));
+            }
+          }
+        }
       }
       if (un.role == 1) {  // publish: the partial's stores before the flag (release, GPU scope)
         __threadfence();
@@ -1537,6 +1579,29 @@ int pick_bn(int N) {
   if (N <= 64) return 64;
   if (N <= 128) return 128;
   return 256;
+}
+
+void gram_acc_launch(const GemmOperand& At, GemmParams p, cudaStream_t stream) {
+  // C (fp32, M x M) += alpha * At At^T over the upper-triangle tiles, split along K so that
+  // the units fill the resident CTA pairs.
+  if (At.batch != 1 || p.M != p.N) throw std::runtime_error("gram_acc: one square product");
+  p.c_mode = kAtomicF32;
+  p.splits = 1;
+  p.batch = 1;
+  p.b_shared = 1;
+  TileSched ts{};
+  ts.tiles_n = ts.tiles_m = (p.M + 255) / 256;
+  ts.batch = 1;
+  ts.sym = 1;
+  ts.tail_w = pair_tail_width(p.N);
+  const long long tiles = (long long)ts.tiles_n * (ts.tiles_n + 1) / 2;
+  const int clusters = pair_clusters();
+  const int kblocks = (p.K + BK - 1) / BK;
+  long long split = clusters > 0 ? clusters / tiles : 1;
+  split = std::max<long long>(1, std::min<long long>(split, kblocks / 4));
+  ts.ksplit = (int)split;
+  if (!launch_pair(At, At, p, ts, tiles * split, stream))
+    throw std::runtime_error("gram_acc: CTA pairs cannot run on this device");
 }
 
 bool gemm_tn_tail_launch(const GemmOperand& A, const GemmOperand& B, const GemmOperand& Btail, GemmParams p,

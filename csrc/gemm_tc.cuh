@@ -103,6 +103,11 @@ void gemm_staged_launch(const GemmOperand& A, const GemmOperand& stage_op, const
 int pick_bn(int N);
 void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, int bn,
                     cudaStream_t stream);
+// C (fp32, M x M, row stride p.ldc) += p.alpha * At @ At^T (At: M x K, K-major) -- a
+// covariance / Gram accumulation.  Only tiles on and above the diagonal are computed (each
+// off-diagonal one also adds its transpose), split along K over the CTA pairs, atomic fp32
+// epilogue.  p.M = p.N = At's rows, p.K = its columns.
+void gram_acc_launch(const GemmOperand& At, GemmParams p, cudaStream_t stream);
 // C = A @ [B; Btail]^T in one CTA-pair launch with the kStoreBF16Tail store: the main columns
 // (B's rows, p.n_main of them, a multiple of 256) in row-major bf16 and the tail (Btail's rows,
 // at most 256) token-major -- e.g. a layer's output and its projected activation from one pass

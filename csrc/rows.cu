@@ -348,4 +348,59 @@ void adam_direction(const float* g, const float* m0, const float* v0, float* out
       reinterpret_cast<float4*>(out), rows, p4, b1, b2, inv_bc1, inv_sqrt_bc2, eps);
 }
 
+namespace {
+
+// 64 x 64 tiles through shared memory: each thread moves two 16-byte vectors in (row-major
+// reads of the source) and two out (row-major writes of the destination); the 8-element
+// transpose happens on the shared tile (row pitch 65 elements, conflict-light).
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, long long lds,
+                                                             __nv_bfloat16* __restrict__ dst, long long ldd, int R,
+                                                             int C) {
+  __shared__ __nv_bfloat16 tile[64][66];
+  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+  const long long zs = (long long)blockIdx.z * R * lds, zd = (long long)blockIdx.z * C * ldd;
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int v = threadIdx.x + q * 256;  // 512 vectors: 64 rows x 8
+    const int r = v >> 3, c = (v & 7) * 8;
+    const int gr = r0 + r, gc = c0 + c;
+    __nv_bfloat16 e[8];
+    if (gr < R && gc + 8 <= C) {
+      *reinterpret_cast<uint4*>(e) = *reinterpret_cast<const uint4*>(src + zs + (long long)gr * lds + gc);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = (gr < R && gc + k < C) ? src[zs + (long long)gr * lds + gc + k] : __nv_bfloat16();
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[c + k][r] = e[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int v = threadIdx.x + q * 256;
+    const int r = v >> 3, c = (v & 7) * 8;  // r: destination row (source column), c: source row
+    const int gr = c0 + r, gc = r0 + c;
+    if (gr >= C) continue;
+    __nv_bfloat16 e[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = tile[r][c + k];
+    if (gc + 8 <= R) {
+      *reinterpret_cast<uint4*>(dst + zd + (long long)gr * ldd + gc) = *reinterpret_cast<const uint4*>(e);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (gc + k < R) dst[zd + (long long)gr * ldd + gc + k] = e[k];
+    }
+  }
+}
+
+}  // namespace
+
+void transpose_bf16(const __nv_bfloat16* src, long long lds, __nv_bfloat16* dst, long long ldd, int batch, int R,
+                    int C, cudaStream_t s) {
+  if (R <= 0 || C <= 0 || batch <= 0) return;
+  dim3 grid((C + 63) / 64, (R + 63) / 64, batch);
+  transpose_bf16_kernel<<<grid, 256, 0, s>>>(src, lds, dst, ldd, R, C);
+}
+
 }  // namespace bw

@@ -56,4 +56,9 @@ void swiglu_split_bwd(const __nv_bfloat16* da, const __nv_bfloat16* h, __nv_bflo
 void adam_direction(const float* g, const float* m0, const float* v0, float* out, long long rows, long long p,
                     float b1, float b2, float inv_bc1, float inv_sqrt_bc2, float eps, cudaStream_t s);
 
+// dst[z] (C x R, row stride ldd) = src[z]^T (src: R x C, row stride lds), bf16; batch z.
+// Row strides and base pointers 16-byte aligned (8 elements) for the vector path.
+void transpose_bf16(const __nv_bfloat16* src, long long lds, __nv_bfloat16* dst, long long ldd, int batch, int R,
+                    int C, cudaStream_t s);
+
 }  // namespace bw

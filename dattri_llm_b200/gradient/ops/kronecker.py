@@ -59,16 +59,17 @@ def _row_mask(a_f, g_f, layer_type):
 def gram_accumulate(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """``out += x^T x`` (fp32 *out*) for ``x (N, w)`` or grouped ``(G, N, w)``.
 
-    On sm_100 with bf16 rows this is a split-K tcgen05 GEMM whose epilogue adds
-    into *out* with fp32 atomics.
+    On sm_100 with bf16 rows this is one tcgen05 launch on CTA pairs that computes only
+    the tiles on and above the diagonal (mirroring each off-diagonal one), splits the row
+    sum over pairs along the samples, and adds into *out* with fp32 atomics.
     """
     from dattri_llm_b200 import ops as native_ops
 
-    if native_ops.use_native(x, out) and x.dtype == torch.bfloat16 and x.ndim == 2:
-        xt = x.t().contiguous()  # (w, N): the contraction axis contiguous
-        w, n = xt.shape
-        splits = native_ops.gemm.auto_splits(w, w, n, 1, 128 if w > 64 else 64)
-        native_ops.gemm_tn(xt, xt, out, mode=native_ops.STORE_ATOMIC_F32, splits=splits)
+    if (native_ops.use_native(x, out) and x.dtype == torch.bfloat16 and x.ndim == 2 and out.dtype == torch.float32
+            and out.is_contiguous() and x.shape[0] > 0):
+        xt = native_ops.gemm._k_aligned(native_ops.gemm.transpose_last2(x))  # (w, N): contraction axis contiguous
+        native_ops.count_launch()
+        native_ops.native().gram_acc(xt, out, 1.0, native_ops.error_word(x.device))
         return out
     out += (x.transpose(-1, -2) @ x).float()
     return out

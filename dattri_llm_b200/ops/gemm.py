@@ -27,6 +27,17 @@ def _k_aligned(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def transpose_last2(x: torch.Tensor) -> torch.Tensor:
+    """``x.transpose(-1, -2).contiguous()``; bf16 CUDA tensors on sm_100 go through the library's
+    tiled transpose kernel (16-byte vectors in and out through shared memory), others through torch."""
+    from dattri_llm_b200.ops import count_launch, native, use_native
+
+    if x.dtype == torch.bfloat16 and x.dim() >= 2 and use_native(x):
+        count_launch()
+        return native().transpose_last2(x)
+    return x.transpose(-1, -2).contiguous()
+
+
 def gemm_tn(
     a: torch.Tensor,
     b: torch.Tensor,

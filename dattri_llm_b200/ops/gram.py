@@ -21,8 +21,10 @@ def per_sample_outer(
     transposes ``(B, L, T)`` / ``(B, R, T)``; callers that already hold them (the
     capture kernels write projected factors transposed) pass *left_t* / *right_t*.
     """
-    lt = left_t if left_t is not None else left.transpose(1, 2).contiguous()
-    rt = right_t if right_t is not None else right.transpose(1, 2).contiguous()
+    from dattri_llm_b200.ops.gemm import transpose_last2
+
+    lt = left_t if left_t is not None else transpose_last2(left)
+    rt = right_t if right_t is not None else transpose_last2(right)
     if lt.dtype != torch.bfloat16:
         lt = lt.bfloat16()
     if rt.dtype != torch.bfloat16:
@@ -96,7 +98,7 @@ def mask_gather(rows_src: torch.Tensor, cols_src: torch.Tensor, rows: torch.Tens
     """``(B, M)`` fp32 ``out[b, m] = sum_t rows_src[b, t, rows[m]] * cols_src[b, t, cols[m]]``:
     fixed coordinates of per-sample gradients ``rows_src_b^T cols_src_b`` gathered without
     forming them (the ``mask`` projection style)."""
-    from dattri_llm_b200.ops import count_launch, native
+    from dattri_llm_b200.ops import count_launch, error_word, native
 
     def prep(x):
         x = x.contiguous().bfloat16()
@@ -108,5 +110,5 @@ def mask_gather(rows_src: torch.Tensor, cols_src: torch.Tensor, rows: torch.Tens
     out = torch.empty(r.shape[0], rows.numel(), dtype=torch.float32, device=r.device)
     count_launch()
     native().mask_gather(r, c, rows.to(device=r.device, dtype=torch.int32).contiguous(),
-                         cols.to(device=r.device, dtype=torch.int32).contiguous(), out)
+                         cols.to(device=r.device, dtype=torch.int32).contiguous(), out, error_word(r.device))
     return out

@@ -49,7 +49,9 @@ def transposed(weight: torch.Tensor) -> torch.Tensor:
     hit = _WT_CACHE.get(id(weight))
     if hit is not None and hit[0]() is weight and hit[1] == key:
         return hit[2]
-    wt = weight.detach().t().contiguous()
+    from dattri_llm_b200.ops.gemm import transpose_last2
+
+    wt = transpose_last2(weight.detach())
     if hit is None or hit[0]() is not weight:
         weakref.finalize(weight, _WT_CACHE.pop, id(weight), None)
     _WT_CACHE[id(weight)] = (weakref.ref(weight), key, wt)

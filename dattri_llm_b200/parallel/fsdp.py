@@ -170,8 +170,8 @@ class ShardedLinear(nn.Linear):
 
         if self._grad is None:
             raise RuntimeError("this ShardedLinear was built with a frozen weight; it keeps no gradient")
-        dyt = dy2.t().contiguous()  # (N, M): tokens contiguous
-        xt = x2.t().contiguous()    # (K, M)
+        dyt = ops.gemm.transpose_last2(dy2)  # (N, M): tokens contiguous
+        xt = ops.gemm.transpose_last2(x2)    # (K, M)
         shard = self.rows * self.in_features
         slots, ptrs = self._slots.next()
         ops.count_launch(2)

@@ -132,3 +132,36 @@ def test_pair_gemm_stream_k_last_wave(m, n, k, tail):
             ops.gemm_tn(a, b, out, mode=ops.STORE_BF16)
         torch.testing.assert_close(out.float(), want, rtol=1.6e-2, atol=1e-2 * float(want.abs().max()))
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("n", "w"), [(16384, 2048), (8192, 64), (1000, 300), (3000, 520)])
+def test_symmetric_gram_accumulate(n, w):
+    """K-FAC covariance accumulation ``out += x^T x``: upper-triangle tiles mirrored, the
+    sample sum split over CTA pairs with atomic fp32 epilogues; two accumulating calls
+    against fp64."""
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.gradient.ops.kronecker import gram_accumulate
+
+    g = torch.Generator(device="cuda").manual_seed(n + w)
+    out = torch.zeros(w, w, device="cuda")
+    want = torch.zeros(w, w, device="cuda", dtype=torch.float64)
+    for _ in range(2):
+        x = torch.randn(n, w, device="cuda", generator=g).bfloat16()
+        gram_accumulate(x, out)
+        want += x.double().T @ x.double()
+    torch.testing.assert_close(out.double(), want, rtol=1e-3, atol=1e-3 * float(want.abs().max()))
+    # mirrored entries are summed in a different order: symmetric to fp32 rounding
+    torch.testing.assert_close(out, out.T, rtol=1e-5, atol=1e-6 * float(out.abs().max()))
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("shape", [(16384, 2048), (3, 200, 136), (1000, 64)])
+def test_transpose_kernel(shape):
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.ops.gemm import transpose_last2
+
+    x = torch.randn(*shape, device="cuda").bfloat16()
+    torch.testing.assert_close(transpose_last2(x), x.transpose(-1, -2).contiguous(), rtol=0, atol=0)
+    sl = x[..., 8:]  # a strided source (row stride kept, 16-byte aligned start)
+    torch.testing.assert_close(transpose_last2(sl), sl.transpose(-1, -2).contiguous(), rtol=0, atol=0)
+    ops.check_device_errors()
