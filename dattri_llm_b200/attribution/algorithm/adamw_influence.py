@@ -24,7 +24,7 @@ from typing import ClassVar
 
 import torch
 
-from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, _dense_float
+from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, dense_block
 from dattri_llm_b200.gradient import ops
 from dattri_llm_b200.gradient.callbacks.optimizer_state_callback import OptimizerStateCallback, assemble_dynamics
 from dattri_llm_b200.gradient.snapshots import LazyDynamics
@@ -98,8 +98,8 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
             raise NotImplementedError(f"{type(self).__name__} needs one optimizer update per captured step; "
                                       f"gradient_accumulation_steps={self.args.gradient_accumulation_steps} is "
                                       "not supported.")
-        if self._projection is None and self._hook_config is not None:
-            self._projection = self._hook_config.projection_kwargs
+        if self._projection is None and self.trajectory_hook_config is not None:
+            self._projection = self.trajectory_hook_config.projection_kwargs
         self._recorder = OptimizerStateCallback(model, lambda: streamer.optimizer,
                                                 projection_kwargs=self._projection, snapshots=snapshots)
         return [self._recorder]
@@ -133,7 +133,7 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
         parts: dict[str, list] = {n: [] for n in layers}
         ids: list[str] = []
         for _s, block, hashes in train.for_steps([step]):
-            dense = _dense_float(block.to(self.args.device), dtype).data
+            dense = dense_block(block.to(self.args.device), dtype).data
             for n in layers:
                 parts[n].append(dense[n])
             ids.extend(hashes)
@@ -178,7 +178,7 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
         n_q = queries.shape[0]
         widths = None
         for _s, block, _h in train.for_steps([max(prop_steps)]):
-            dense = _dense_float(block.to(dev)).data
+            dense = dense_block(block.to(dev)).data
             widths = {n: dense[n].shape[1] for n in layers}
             break
         if widths is None:

@@ -22,7 +22,7 @@ from typing import ClassVar
 
 import torch
 
-from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, _dense_float
+from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, dense_block
 from dattri_llm_b200.gradient.gradient import Gradient, GradientRecord
 from dattri_llm_b200.gradient.snapshots import TrajectorySnapshots
 from dattri_llm_b200.gradient.storage_manager import GradientStorageManager
@@ -115,7 +115,7 @@ class DVEmbAttributor(TrajectoryAttributor):
 
     def _layer_slices(self, train_source, step: int):
         for _s, g, _h in train_source.for_steps([step]):
-            mat = _dense_float(g.to(self.args.device))
+            mat = dense_block(g.to(self.args.device))
             layers, slices, off = list(mat.data), {}, 0
             for n in layers:
                 slices[n] = (off, off + mat.data[n].shape[1])
@@ -144,7 +144,7 @@ class DVEmbAttributor(TrajectoryAttributor):
             delta_blocks: dict[str, torch.Tensor] = {}
             n_t = 0
             for _s, g, hashes in train_source.for_steps([ts]):
-                mat = _dense_float(g.to(dev))
+                mat = dense_block(g.to(dev))
                 shared = [n for n in layers if n in mat.data]
                 if not shared:
                     continue
@@ -193,7 +193,7 @@ class DVEmbAttributor(TrajectoryAttributor):
             delta = {n: torch.zeros_like(w[n]) for n in layers}
             n_t = 0
             for _s, g, hashes in train_source.for_steps([ts]):
-                mat = _dense_float(g.to(dev), block_dtype).data
+                mat = dense_block(g.to(dev), block_dtype).data
                 shared = [n for n in layers if n in mat]
                 if not shared:
                     continue
@@ -263,7 +263,7 @@ class DVEmbAttributor(TrajectoryAttributor):
                 emb = self.embed_trajectory(train, prop, out, **sweep)
                 if dvemb_dir is not None:
                     emb = self._tee_to_store(emb, GradientStorageManager(dvemb_dir), self._sample_id_key(train))
-                scores, rids, rsteps, tids, _ = self.score_sources(emb, test, transform_test=_dense_float)
+                scores, rids, rsteps, tids, _ = self.score_sources(emb, test, transform_test=dense_block)
             elif not loop_over_test:
                 w, tids = self.collect_test_matrix(test)
                 scores, rids, rsteps = self._propagate_test_and_score(w, len(tids), train, prop, out,
@@ -272,7 +272,7 @@ class DVEmbAttributor(TrajectoryAttributor):
                 tids, index = self.test_column_order(test)
                 scores, rids, rsteps = None, [], []
                 for _s, tg, th in test:
-                    wb = _dense_float(tg.to(self.args.device)).data
+                    wb = dense_block(tg.to(self.args.device)).data
                     cols = [index[h] for h in th]
                     bs, r_ids, r_steps = self._propagate_test_and_score(wb, len(cols), train, prop, out,
                                                                         block_dtype=block_dtype, **sweep)
