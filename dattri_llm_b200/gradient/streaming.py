@@ -238,6 +238,16 @@ def _host_hashable(batch: object) -> dict | None:
     return None
 
 
+def _fused_fsdp_ready(device: torch.device) -> bool:
+    """Peer-memory kernels can run: NCCL group of two or more ranks on sm_100 GPUs."""
+    if device.type != "cuda" or torch.cuda.get_device_capability(device)[0] != 10:
+        return False
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.parallel import symm
+
+    return ops.available() and symm.available(device)
+
+
 class GradientStreamer(GradientSource):
     """Yields per-step ``(step, Gradient, hashes)`` from a live forward+backward pass.
 
@@ -321,7 +331,7 @@ class GradientStreamer(GradientSource):
             raise ValueError("A shared hook_manager under distributed execution needs the sharing streamer's "
                              "forward_model= as well (pass ``other.forward_model``).")
         else:
-            self._fwd = self._wrap_model(model, args)
+            self._fwd = self._wrap_model(model, args, frozen=not enable_update)
         self._loader = self._build_loader()
         self._accum_steps = max(1, int(args.gradient_accumulation_steps))
         self._accum = 0
@@ -638,13 +648,21 @@ class GradientStreamer(GradientSource):
         return DataLoader(**kw)
 
     @staticmethod
-    def _wrap_model(model: nn.Module, args) -> nn.Module:
+    def _wrap_model(model: nn.Module, args, frozen: bool = False) -> nn.Module:
         fsdp = args.fsdp
         tokens = set(fsdp.split() if isinstance(fsdp, str) else (fsdp or []))
         if args.world_size <= 1:
             return model
         if args.device.type == "cuda":
             torch.cuda.set_device(args.local_process_index)
+        if tokens and frozen and "full_shard" in tokens and "offload" not in tokens and \
+                (args.fsdp_config or {}).get("fused", True) and _fused_fsdp_ready(args.device):
+            # An attribution probe (no update) on NCCL + sm_100: the linears are sharded in
+            # place and all-gather their weights inside their own GEMMs; nothing to wrap.
+            from dattri_llm_b200.parallel.fsdp import shard_frozen_linears
+
+            shard_frozen_linears(model)
+            return model
         if tokens:
             from torch.distributed.fsdp import CPUOffload, ShardingStrategy
             from torch.distributed.fsdp import FullyShardedDataParallel as FSDP

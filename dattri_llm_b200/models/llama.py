@@ -281,6 +281,14 @@ class LlamaForCausalLM(nn.Module):
             elif isinstance(m, nn.RMSNorm):
                 m.weight.fill_(1.0)
 
+    def get_input_embeddings(self) -> nn.Embedding:
+        """The token embedding (Hugging Face name)."""
+        return self.model.embed_tokens
+
+    def get_output_embeddings(self) -> nn.Linear:
+        """The LM head (Hugging Face name)."""
+        return self.lm_head
+
     def load_hf_state_dict(self, state_dict: dict) -> None:
         """Load a Hugging Face ``LlamaForCausalLM`` state dict (same key names)."""
         sd = {k: v for k, v in state_dict.items() if "rotary_emb" not in k}

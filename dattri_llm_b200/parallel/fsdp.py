@@ -22,6 +22,8 @@ FSDP's NCCL all-gather / reduce-scatter around cuBLAS GEMMs
 
 from __future__ import annotations
 
+import functools
+
 import torch
 import torch.distributed as dist
 from torch import nn
@@ -199,6 +201,78 @@ def sync_sharded_grads(model: nn.Module) -> None:
         if isinstance(m, ShardedLinear) and m._barrier is not None:
             m._barrier.wait()
             return
+
+
+class _FrozenShard:
+    """The sharded state of a frozen linear converted in place (:func:`shard_frozen_linears`):
+    the same fields :class:`_AGLinear` reads from a :class:`ShardedLinear`."""
+
+    def __init__(self, module: nn.Linear, group) -> None:
+        w = module.weight.detach()
+        self.in_features, self.out_features = module.in_features, module.out_features
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.rows = self.out_features // self.world
+        dev = w.device
+        self._w = SymmetricBuffer((self.rows, self.in_features), torch.bfloat16, dev, group)
+        self._wt = SymmetricBuffer((self.in_features, self.rows), torch.bfloat16, dev, group)
+        shard = w[self.rank * self.rows:(self.rank + 1) * self.rows].to(torch.bfloat16)
+        self._w.local.copy_(shard)
+        self._wt.local.copy_(shard.t())
+
+    def _reduce_scatter_wgrad(self, dy2, x2) -> None:  # pragma: no cover - frozen weights only
+        raise RuntimeError("a frozen sharded linear has no weight gradient")
+
+
+def _sharded_forward(module: nn.Module, x: torch.Tensor) -> torch.Tensor:
+    state = module._bw_frozen_shard
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    return _AGLinear.apply(x, module.weight, state)
+
+
+def can_shard_frozen(module: nn.Module, world: int) -> bool:
+    """Whether :func:`shard_frozen_linears` converts *module*: a bias-free ``nn.Linear``
+    (or subclass) with a frozen bf16-castable weight whose rows split into 64-row multiples
+    over *world* ranks and whose input width is a multiple of 8."""
+    return (isinstance(module, nn.Linear) and module.bias is None and not module.weight.requires_grad
+            and module.out_features % (world * 64) == 0 and module.in_features % 8 == 0
+            and module.weight.is_cuda)
+
+
+def shard_frozen_linears(model: nn.Module, group=None) -> list[str]:
+    """Shard every eligible frozen linear of *model* over *group*, in place (collective).
+
+    Each converted module keeps its identity -- and so every hook already registered on it
+    -- but its full weight is replaced by this rank's row shard, its forward by the fused
+    all-gather GEMM (``gemm_tn_staged`` mode 0) and its input gradient by the fused
+    transposed-shard GEMM (mode 1); ``module.in_features`` / ``out_features`` are
+    unchanged, so the capture engine still sees the full layer.  This is the FSDP
+    FULL_SHARD layout of an attribution probe (frozen weights: no gradient reduce-scatter)
+    with the parameter all-gather inside the GEMMs instead of NCCL around cuBLAS.  Returns
+    the converted names.
+    """
+    world = dist.get_world_size(group)
+    # Weights used outside their module's forward stay whole: tied weights, and the output
+    # embedding (a fused LM-head loss reads it directly).
+    uses: dict[int, int] = {}
+    for _n, p in model.named_parameters(remove_duplicate=False):
+        uses[id(p)] = uses.get(id(p), 0) + 1
+    out_emb = model.get_output_embeddings() if hasattr(model, "get_output_embeddings") else None
+    converted = []
+    for name, module in model.named_modules():
+        if getattr(module, "_bw_frozen_shard", None) is not None or not can_shard_frozen(module, world):
+            continue
+        if module is out_emb or uses.get(id(module.weight), 0) > 1:
+            continue
+        state = _FrozenShard(module, group)
+        module._bw_frozen_shard = state
+        module.weight = nn.Parameter(state._w.local, requires_grad=False)
+        module.forward = functools.partial(_sharded_forward, module)
+        converted.append(name)
+    if converted:
+        torch.cuda.synchronize(next(iter(model.parameters())).device)
+    dist.barrier(group=group)
+    return converted
 
 
 def shard_linears(model: nn.Module, names: list[str] | None = None, group=None) -> list[str]:

@@ -306,3 +306,80 @@ def test_sharded_linear_fused_collectives_match_dense():
         errs = dict(results)
     assert len(errs) == world
     assert max(errs.values()) < 2e-2, errs
+
+
+def _fused_fsdp_capture_worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+    import tempfile
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", WORLD_SIZE=str(world),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from dattri_llm_b200 import AttributionArguments, CaptureCallback, HookManager, HookManagerConfig, ops
+        from dattri_llm_b200.gradient.streaming import GradientStreamer
+        from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM, token_sum_loss
+
+        cfg = LlamaConfig.tiny(hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
+                               vocab_size=1024)
+
+        def build():
+            m = LlamaForCausalLM(cfg, frozen_probe=True)
+            m.reset_parameters(seed=0)
+            return m.to(dev).bfloat16().requires_grad_(False)
+
+        ids = torch.randint(0, cfg.vocab_size, (2, 128), generator=torch.Generator().manual_seed(rank)).to(dev)
+        proj = {"__default__": {"style": "logra", "proj_dim": 64}}
+        regex = [r"\.(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj)$"]
+
+        def manager(model):
+            cb = CaptureCallback()
+            hm = HookManager(model, HookManagerConfig(linear_io=regex, projection_kwargs=proj, include_frozen=True,
+                                                      capture_style="auto"), callbacks=[cb])
+            return hm, cb
+
+        plain = build()
+        hm, cb = manager(plain)
+        with hm.collect():
+            token_sum_loss(plain, {"input_ids": ids}).backward()
+        want = cb.record.gradient
+        hm.remove()
+        # the streamer's FSDP wrapping of a frozen probe: hooks first, then in-place sharding
+        sharded = build()
+        hm, cb = manager(sharded)
+        args = AttributionArguments(output_dir=tempfile.mkdtemp(), fsdp="full_shard")
+        assert GradientStreamer._wrap_model(sharded, args, frozen=True) is sharded
+        n_sharded = sum(getattr(m, "_bw_frozen_shard", None) is not None for m in sharded.modules())
+        assert n_sharded == 14, n_sharded
+        with hm.collect():
+            token_sum_loss(sharded, {"input_ids": ids}).backward()
+        got = cb.record.gradient
+        worst = 0.0
+        for name, w in want.data.items():
+            g = got.data[name]
+            worst = max(worst, float((g.float() - w.float()).abs().max() / w.float().abs().max()))
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        results[rank] = worst
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_fsdp_frozen_probe_capture_matches_unsharded():
+    """The streamer's FSDP path for a frozen probe shards the linears in place (weights
+    all-gathered inside their GEMMs over NVLink); the per-sample LoGra capture equals the
+    unsharded model's on every rank."""
+    world = 2
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_fused_fsdp_capture_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(errs.values()) < 3e-2, errs
