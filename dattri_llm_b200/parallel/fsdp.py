@@ -32,9 +32,11 @@ from dattri_llm_b200.parallel.symm import PeerBarrier, SymmetricBuffer
 
 
 class _Staging:
-    """A local staging matrix for one gathered weight shape, with its copy flags and the
-    launch counter that gates them (shared by every layer of that shape: launches on one
-    stream use it one after another)."""
+    """A local staging matrix for one gathered weight shape and staging mode, with its copy
+    flags and the launch counter that gates them (shared by every layer of that shape and
+    mode: launches on one stream use it one after another).  A flag counts the pieces of its
+    owner copied so far and a launch waits for ``epoch x pieces per owner``; the two modes
+    cut their shards into different numbers of pieces, so they never share a counter."""
 
     _pool: dict = {}
 
@@ -44,8 +46,8 @@ class _Staging:
         self.epoch = 0
 
     @classmethod
-    def get(cls, rows: int, cols: int, world: int, device: torch.device) -> _Staging:
-        key = (rows, cols, world, device)
+    def get(cls, rows: int, cols: int, world: int, device: torch.device, mode: int) -> _Staging:
+        key = (rows, cols, world, device, mode)
         st = cls._pool.get(key)
         if st is None:
             st = cls._pool[key] = cls(rows, cols, world, device)
@@ -99,7 +101,7 @@ class _AGLinear(torch.autograd.Function):
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         y = torch.empty(x2.shape[0], layer.out_features, dtype=torch.bfloat16, device=x.device)
-        _Staging.get(layer.out_features, k, layer.world, x.device).launch(x2, layer._w.peers, y, 0, layer.rank)
+        _Staging.get(layer.out_features, k, layer.world, x.device, 0).launch(x2, layer._w.peers, y, 0, layer.rank)
         ctx.layer = layer
         ctx.save_for_backward(x2 if weight_shard.requires_grad else x2.new_empty(0))
         ctx.in_shape = x.shape
@@ -116,7 +118,7 @@ class _AGLinear(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[0]:
             dx = torch.empty(dy2.shape[0], layer.in_features, dtype=torch.bfloat16, device=dy.device)
-            _Staging.get(layer.in_features, layer.out_features, layer.world, dy.device).launch(
+            _Staging.get(layer.in_features, layer.out_features, layer.world, dy.device, 1).launch(
                 dy2, layer._wt.peers, dx, 1, layer.rank)
             dx = dx.view(ctx.in_shape)
         if ctx.needs_input_grad[1]:
