@@ -10,7 +10,15 @@ every train sample against 1,024 test samples, with a running per-test top-100.
 
 Usage (one process per GPU; N > 1 under torchrun)::
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--config 2|3]
+
+``--config 3`` (not the default) is BASELINE config 3: a Llama-3-8B-architecture decoder
+(32 layers, d 4096, FFN 14336), bf16, FSDP FULL_SHARD over the N GPUs, sequence length 2048,
+micro-batch 2 per GPU, EK-FAC influence with 64 x 64 LoGra projections.  Both arms time the
+public ``EKFACAttributor.attribute(train, test, gradient_cache_residency="disk")`` call --
+capture with covariances, the fit (eigendecompositions and the eigenvalue sweep), the query
+side and the scoring -- over K micro-batches per GPU after one untimed call over W, as the
+reference's own FSDP benchmark does; the query set is 2 sequences (the same in both arms).
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a device
 synchronize, timed with CUDA events on the compute stream; the reported time is the
@@ -479,6 +487,156 @@ def run_reference(rank, world, local, steps, warmup):
     return ms, clk, e2e
 
 
+# --------------------------------------------------------------------------- config 3
+C3_SEQ, C3_MB, C3_NTEST, C3_DAMPING = 2048, 2, 2, 1e-3
+
+
+class _DS3(torch.utils.data.Dataset):
+    """Config-3 synthetic sequences: uniform token ids of length 2048, deterministic."""
+
+    def __init__(self, n: int, vocab: int, seed: int) -> None:
+        g = torch.Generator().manual_seed(seed)
+        self.ids = torch.randint(0, vocab, (n, C3_SEQ), generator=g)
+
+    def __len__(self):
+        return self.ids.shape[0]
+
+    def __getitem__(self, i):
+        return {"input_ids": self.ids[i]}
+
+
+def _c3_time(attribute, rank, world, steps, warmup, vocab, local):
+    """Untimed attribute() over *warmup* micro-batches per GPU, then CUDA events around one
+    attribute() over *steps* micro-batches per GPU; returns (ms per step, max over ranks)."""
+    n_warm, n_meas = C3_MB * warmup * world, C3_MB * steps * world
+    data = _DS3(n_warm + n_meas, vocab, seed=2)
+    test = _DS3(C3_NTEST, vocab, seed=1)
+    attribute(torch.utils.data.Subset(data, range(n_warm)), test, "warm")
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    _barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    ev0.record()
+    attribute(torch.utils.data.Subset(data, range(n_warm, n_warm + n_meas)), test, "timed")
+    ev1.record()
+    torch.cuda.synchronize()
+    host = time.perf_counter() - t0
+    _barrier(world)
+    clk = clocks.stop()
+    ms = _max_over_ranks(ev0.elapsed_time(ev1), world) / steps
+    return ms, clk, _max_over_ranks(host, world)
+
+
+def run_c3_ours(rank, world, local, steps, warmup):
+    sys.path.insert(0, HERE)
+    import dattri_llm_b200 as bw
+    from dattri_llm_b200 import ops as native_ops
+    from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM, token_sum_loss
+
+    native_ops.native()
+    dev = torch.device("cuda", local)
+    cfg = LlamaConfig.llama_3_8b()
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg, frozen_probe=True)
+    model.reset_parameters(seed=0)
+    model = model.to(torch.bfloat16).eval().requires_grad_(False)
+    proj = {"__default__": {"style": "logra", "proj_dim": PROJ_DIM, "proj_type": "rademacher", "proj_seed": 0}}
+    hc = bw.HookManagerConfig(linear_io=_layers_regex(), projection_kwargs=proj, capture_style="materialized",
+                              include_frozen=True)
+    task = bw.AttributionTask(token_sum_loss, model)
+    launches = [0]
+    root = tempfile.mkdtemp()
+
+    def attribute(train, test, tag):
+        args = bw.AttributionArguments(output_dir=os.path.join(root, tag, f"rank{rank}"),
+                                       per_device_train_batch_size=C3_MB, per_device_eval_batch_size=C3_MB,
+                                       fsdp="full_shard" if world > 1 else "")
+        n0 = native_ops.launch_count()
+        bw.EKFACAttributor(args, task=task).attribute(train, test, hook_config=hc, gradient_cache_residency="disk",
+                                                      damping=C3_DAMPING)
+        if tag == "timed":
+            launches[0] = native_ops.launch_count() - n0
+
+    ms, clk, host = _c3_time(attribute, rank, world, steps, warmup, cfg.vocab_size, local)
+    native_ops.check_device_errors(dev)
+    return ms, clk, host, launches[0]
+
+
+def run_c3_reference(rank, world, local, steps, warmup):
+    ref = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "dattri_llm")):
+        raise SystemExit("bench.py --impl reference: the reference is not installed under baseline/_ref")
+    sys.path.insert(0, ref)
+    import dattri_llm as R  # noqa: N812
+    from transformers import LlamaConfig as HFConfig
+    from transformers import LlamaForCausalLM as HFLlama
+
+    dev = torch.device("cuda", local)
+    hfc = HFConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                   num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=8192, rope_theta=500000.0,
+                   tie_word_embeddings=False, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = HFLlama(hfc)
+    model = model.to(torch.bfloat16).eval()
+    model.requires_grad_(False)
+    model.get_input_embeddings().requires_grad_(True)
+    fwd = model
+    if world > 1:  # the reference's own FSDP recipe: one unit per decoder block
+        import functools
+
+        from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
+        from torch.distributed.fsdp import ShardingStrategy
+        from torch.distributed.fsdp.wrap import transformer_auto_wrap_policy
+        from transformers.models.llama.modeling_llama import LlamaDecoderLayer
+
+        fwd = FSDP(model, device_id=dev, sharding_strategy=ShardingStrategy.FULL_SHARD, use_orig_params=True,
+                   auto_wrap_policy=functools.partial(transformer_auto_wrap_policy,
+                                                      transformer_layer_cls={LlamaDecoderLayer}))
+    proj = {"__default__": {"style": "logra", "proj_dim": PROJ_DIM, "proj_type": "rademacher", "proj_seed": 0}}
+    inner = fwd.module if world > 1 else model
+    layers = [n for n, m in inner.named_modules() if isinstance(m, torch.nn.Linear) and "lm_head" not in n]
+    hc = R.HookManagerConfig(linear_io=layers, projection_kwargs=proj, projector=counter_projector_factory(),
+                             capture_style="materialized", include_frozen=True)
+    task = R.AttributionTask(_token_sum_loss, fwd)
+    root = tempfile.mkdtemp()
+
+    def attribute(train, test, tag):
+        args = R.AttributionArguments(output_dir=os.path.join(root, tag, f"rank{rank}"),
+                                      per_device_train_batch_size=C3_MB, per_device_eval_batch_size=C3_MB,
+                                      dataloader_pin_memory=False)
+        R.EKFACAttributor(args, task=task).attribute(train, test, hook_config=hc, gradient_cache_residency="disk",
+                                                     damping=C3_DAMPING)
+
+    ms, clk, host = _c3_time(attribute, rank, world, steps, warmup, hfc.vocab_size, local)
+    return ms, clk, host
+
+
+def main_c3(a, rank, world, local):
+    cfg_json = {"model": "Llama-3-8B-arch (random init)", "global_batch": C3_MB * world, "micro_batch_per_gpu": C3_MB,
+                "seq_len": C3_SEQ, "parallelism": f"fsdp{world}" if world > 1 else "single",
+                "method": "EK-FAC (covariances at capture, disk gradient cache)", "proj": f"logra {PROJ_DIM}x{PROJ_DIM}",
+                "n_test": C3_NTEST, "timed": "one public attribute() call over K micro-batches per GPU",
+                "l2": "per-step weight traffic (16 GB of bf16 parameters) exceeds the 126 MB L2"}
+    out = {"metric": "train samples attributed/sec (EK-FAC attribute(), device-timed)", "n_gpus": world,
+           "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+           "data": "synthetic uniform token ids, random-init weights", "config": cfg_json}
+    if a.impl == "ours":
+        ms, clk, host, launches = run_c3_ours(rank, world, local, a.steps, a.warmup)
+        extra = {"gpu_launches": launches}
+    else:
+        ms, clk, host = run_c3_reference(rank, world, local, a.steps, a.warmup)
+        extra = {"impl": "reference"}
+    value = C3_MB * world / (ms / 1e3)
+    out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms, "vs_baseline": None, "clocks": clk,
+                "e2e": {"value": C3_MB * world * a.steps / host, "unit": "train samples/s (host clock)",
+                        "h2d_bytes_per_step": C3_MB * C3_SEQ * 8, "d2h_bytes_per_step": 0}, **extra})
+    return out
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -486,10 +644,22 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=[2, 3], default=2)
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
     rank, world, local = _init_dist()
+    if a.config == 3:
+        try:
+            out = main_c3(a, rank, world, local)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return
     cfg_json = {"model": "Llama-3.2-1B-arch (random init)", "global_batch": MICRO_BATCH * world,
                 "micro_batch_per_gpu": MICRO_BATCH, "seq_len": SEQ, "parallelism": f"dp{world}",
                 "n_test": N_TEST, "proj": f"logra {PROJ_DIM}x{PROJ_DIM} per linear (112 layers)",

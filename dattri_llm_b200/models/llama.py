@@ -271,12 +271,17 @@ class LlamaForCausalLM(nn.Module):
 
     @torch.no_grad()
     def reset_parameters(self, seed: int | None = None) -> None:
-        """Random init (normal, std ``initializer_range``), optionally seeded."""
-        gen = torch.Generator(device="cpu").manual_seed(seed) if seed is not None else None
+        """Random init (normal, std ``initializer_range``), optionally seeded.  The values are
+        drawn on the device the weights live on (a seeded draw is reproducible per device
+        type: CPU-built and CUDA-built models differ)."""
+        gens: dict = {}
         for m in self.modules():
             if isinstance(m, (nn.Linear, nn.Embedding)):
-                w = torch.empty(m.weight.shape, dtype=torch.float32).normal_(0.0, self.config.initializer_range,
-                                                                            generator=gen)
+                dev = m.weight.device
+                if seed is not None and dev not in gens:
+                    gens[dev] = torch.Generator(device=dev).manual_seed(seed)
+                w = torch.empty(m.weight.shape, dtype=torch.float32, device=dev)
+                w.normal_(0.0, self.config.initializer_range, generator=gens.get(dev))
                 m.weight.copy_(w)
             elif isinstance(m, nn.RMSNorm):
                 m.weight.fill_(1.0)
