@@ -173,6 +173,19 @@ void gemm_tn_tail(Tensor A, Tensor B, Tensor Btail, Tensor C, Tensor C2, int64_t
               "gemm_tn_tail: CTA pairs cannot run on this device");
 }
 
+// bf16x3 split operand of a 2-D fp32 matrix (any strides): (R, 3 Kp) bf16, Kp = K rounded up to 8.
+Tensor split3_bf16(Tensor x, int64_t pattern) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.dim() == 2, "x: 2-D fp32");
+  TORCH_CHECK(pattern == 0 || pattern == 1, "pattern 0 ([hi|hi|lo]) or 1 ([hi|lo|hi])");
+  const long long R = x.size(0), K = x.size(1), Kp = (K + 7) / 8 * 8;
+  Tensor out = torch::empty({R, 3 * Kp}, x.options().dtype(torch::kBFloat16));
+  bw::split3_bf16(x.data_ptr<float>(), x.stride(0), x.stride(1), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                  (int)R, (int)K, (int)Kp, (int)pattern, at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
 // Transpose of the last two axes of a bf16 tensor ((..., R, C) -> (..., C, R), contiguous).
 Tensor transpose_last2(Tensor x) {
   const c10::cuda::CUDAGuard guard(x.device());
@@ -1186,6 +1199,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, "MoE combine: router-weighted sum of the k returned rows");
   m.def("moe_combine_bwd_dispatch", &moe_combine_bwd_dispatch, "combine backward fused with the gradient dispatch");
   m.def("gemm_tn_rs", &gemm_tn_rs, "GEMM with the reduce-scatter in its epilogue (peer slot stores)");
+  m.def("split3_bf16", &split3_bf16, "bf16x3 split operand of an fp32 matrix (K-concatenated hi/lo segments)");
   m.def("transpose_last2", &transpose_last2, "bf16 transpose of the last two axes (tiled through shared memory)");
   m.def("gram_acc", &gram_acc, "C += alpha * At At^T (symmetric tiles, split-K, fp32 atomics)");
   m.def("gemm_tn_tail", &gemm_tn_tail, "C = A B^T (bf16 rows) and C2 = A Btail^T (token-major) in one launch");

@@ -1,3 +1,4 @@
+#include <algorithm>
 // Row-parallel fused kernels of the decoder path, one warp per row with the row held in
 // registers (one HBM read and one write per element):
 //   * RMSNorm forward with an optional fused residual add  (h = x + delta; y = rms(h) * w),
@@ -401,6 +402,42 @@ void transpose_bf16(const __nv_bfloat16* src, long long lds, __nv_bfloat16* dst,
   if (R <= 0 || C <= 0 || batch <= 0) return;
   dim3 grid((C + 63) / 64, (R + 63) / 64, batch);
   transpose_bf16_kernel<<<grid, 256, 0, s>>>(src, lds, dst, ldd, R, C);
+}
+
+namespace {
+
+// One row of a split operand: the logical (R, K) fp32 matrix element (r, k) sits at
+// src[r * ld_row + k * ld_col]; dst row r holds three K-wide bf16 segments (each padded to
+// Kp with zeros): pattern 0 = [hi, hi, lo], pattern 1 = [hi, lo, hi], where hi = bf16(x)
+// rounded to nearest and lo = bf16(x - hi).  A K-concatenated product of a pattern-0 A and
+// a pattern-1 B is hi_a hi_b + hi_a lo_b + lo_a hi_b: the bf16x3 splitting of Henry, Tang
+// and Heinecke (2019), accurate to about 2^-16 relative before the fp32 accumulation.
+__global__ void split3_bf16_kernel(const float* __restrict__ src, long long ld_row, long long ld_col,
+                                   __nv_bfloat16* __restrict__ dst, int R, int K, int Kp, int pattern) {
+  const long long total = (long long)R * Kp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / Kp;
+    const int k = (int)(i - r * Kp);
+    const float x = k < K ? src[r * ld_row + (long long)k * ld_col] : 0.f;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+    __nv_bfloat16* row = dst + r * 3LL * Kp;
+    row[k] = hi;
+    row[Kp + k] = pattern == 0 ? hi : lo;
+    row[2 * Kp + k] = pattern == 0 ? lo : hi;
+  }
+}
+
+}  // namespace
+
+void split3_bf16(const float* src, long long ld_row, long long ld_col, __nv_bfloat16* dst, int R, int K, int Kp,
+                 int pattern, cudaStream_t s) {
+  if (R <= 0 || Kp <= 0) return;
+  const long long total = (long long)R * Kp;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 16);
+  split3_bf16_kernel<<<(unsigned)blocks, threads, 0, s>>>(src, ld_row, ld_col, dst, R, K, Kp, pattern);
 }
 
 }  // namespace bw

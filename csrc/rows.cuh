@@ -61,4 +61,9 @@ void adam_direction(const float* g, const float* m0, const float* v0, float* out
 void transpose_bf16(const __nv_bfloat16* src, long long lds, __nv_bfloat16* dst, long long ldd, int batch, int R,
                     int C, cudaStream_t s);
 
+// bf16x3 split of a strided fp32 (R, K) matrix into a (R, 3 Kp) bf16 K-major operand:
+// pattern 0 = [hi | hi | lo], pattern 1 = [hi | lo | hi] (see rows.cu).
+void split3_bf16(const float* src, long long ld_row, long long ld_col, __nv_bfloat16* dst, int R, int K, int Kp,
+                 int pattern, cudaStream_t s);
+
 }  // namespace bw

@@ -25,6 +25,7 @@ from typing import ClassVar
 import torch
 
 from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, dense_block
+from dattri_llm_b200.ops.gemm import matmul_f32
 from dattri_llm_b200.gradient import ops
 from dattri_llm_b200.gradient.callbacks.optimizer_state_callback import OptimizerStateCallback, assemble_dynamics
 from dattri_llm_b200.gradient.snapshots import LazyDynamics
@@ -157,14 +158,14 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
             t = _StepTerms(dynamics[step], layers, dev)
             if step in output_steps:
                 z = t.push(g)
-                infl = z[:, :p] @ w_theta.T + z[:, p:2 * p] @ w_m.T + z[:, 2 * p:] @ w_v.T
-                rows.append((-(infl @ test_rep.T)).cpu())
+                infl = matmul_f32(z, torch.cat([w_theta, w_m, w_v], dim=1), b_transposed=True)
+                rows.append((-matmul_f32(infl, test_rep, b_transposed=True)).cpu())
                 rids.extend(ids)
                 rsteps.extend([step] * len(ids))
             coup = t.coupling(w_theta, w_m, w_v, g)
             w_theta, w_m, w_v = t.transition(w_theta, w_m, w_v)
             scale = float(g.shape[0]) if loss_reduction == "mean" else 1.0
-            w_theta += scale * (coup.T @ g)
+            w_theta += scale * matmul_f32(coup.t(), g)
         return (torch.cat(rows) if rows else torch.zeros(0, test_rep.shape[0])), rids, rsteps
 
     def sweep_queries(self, train, dynamics, queries: torch.Tensor, *, layers, prop_steps, output_steps,
@@ -209,8 +210,7 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
                     gc = blocks[n][c0:c0 + chunk].float()
                     if emit:
                         z = t.push(gc)
-                        scores[c0:c0 + chunk] -= (z[:, :w] @ u[n][0].T + z[:, w:2 * w] @ u[n][1].T
-                                                  + z[:, 2 * w:] @ u[n][2].T)
+                        scores[c0:c0 + chunk] -= matmul_f32(z, torch.cat(list(u[n]), dim=1), b_transposed=True)
                         del z
                     coup[c0:c0 + chunk] += t.coupling(*u[n], gc)
             if emit:
@@ -219,7 +219,7 @@ class AdamWInfluenceAttributor(TrajectoryAttributor):
                 rsteps.extend([step] * b)
             scale = float(b) if loss_reduction == "mean" else 1.0
             for n in layers:
-                fisher = coup.T @ blocks[n].float()
+                fisher = matmul_f32(coup.t(), blocks[n].float())
                 u[n] = list(terms[n].transition(*u[n]))
                 u[n][0] += scale * fisher
             del blocks, terms, coup, scores

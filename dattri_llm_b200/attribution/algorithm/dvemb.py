@@ -23,6 +23,7 @@ from typing import ClassVar
 import torch
 
 from dattri_llm_b200.attribution.algorithm.trajectory import TrajectoryAttributor, dense_block
+from dattri_llm_b200.ops.gemm import matmul_f32
 from dattri_llm_b200.gradient.gradient import Gradient, GradientRecord
 from dattri_llm_b200.gradient.snapshots import TrajectorySnapshots
 from dattri_llm_b200.gradient.storage_manager import GradientStorageManager
@@ -155,25 +156,25 @@ class DVEmbAttributor(TrajectoryAttributor):
                     s, e = slices[n]
                     flat[:, s:e] = mat.data[n]
                 if hessian_mode == "full":
-                    e_raw = flat if op is None else flat - flat @ op.T
+                    e_raw = flat if op is None else flat - matmul_f32(flat, op, b_transposed=True)
                 else:
                     e_raw = flat.clone()
                     for n in shared:
                         if blocks[n] is not None:
                             s, e = slices[n]
-                            e_raw[:, s:e] = flat[:, s:e] - flat[:, s:e] @ blocks[n].T
+                            e_raw[:, s:e] = flat[:, s:e] - matmul_f32(flat[:, s:e], blocks[n], b_transposed=True)
                 if emit:
                     emb = lr * e_raw
                     yield ts, Gradient(dict.fromkeys(shared, "materialized"),
                                        {n: emb[:, slices[n][0]:slices[n][1]].contiguous() for n in shared},
                                        {n: g.layer_types[n] for n in shared}), list(hashes)
                 if hessian_mode == "full":
-                    upd = e_raw.T @ flat
+                    upd = matmul_f32(e_raw.t(), flat)
                     delta = upd if delta is None else delta + upd
                 else:
                     for n in shared:
                         s, e = slices[n]
-                        upd = e_raw[:, s:e].T @ flat[:, s:e]
+                        upd = matmul_f32(e_raw[:, s:e].t(), flat[:, s:e])
                         delta_blocks[n] = upd if n not in delta_blocks else delta_blocks[n] + upd
             scale = float(n_t) if loss_reduction == "mean" else 1.0
             if delta is not None:
@@ -199,7 +200,7 @@ class DVEmbAttributor(TrajectoryAttributor):
                     continue
                 b = mat[shared[0]].shape[0]
                 n_t += b
-                per_layer = {n: mat[n].float() @ w[n].T for n in shared}
+                per_layer = {n: matmul_f32(mat[n].float(), w[n], b_transposed=True) for n in shared}
                 dmat = torch.zeros(b, n_cols, device=dev)
                 for n in shared:
                     dmat += per_layer[n]
@@ -208,7 +209,7 @@ class DVEmbAttributor(TrajectoryAttributor):
                     ids.extend(hashes)
                     steps.extend([ts] * b)
                 for n in shared:
-                    delta[n] += (dmat if hessian_mode == "full" else per_layer[n]).T @ mat[n].float()
+                    delta[n] += matmul_f32((dmat if hessian_mode == "full" else per_layer[n]).t(), mat[n].float())
             scale = float(n_t) if loss_reduction == "mean" else 1.0
             for n in layers:
                 w[n] -= lr * scale * delta[n]

@@ -42,8 +42,15 @@ def _flatten_for_kfac(a: torch.Tensor, g: torch.Tensor, layer_type: str):
 
 
 def _right_multiply(x: torch.Tensor, matrix: torch.Tensor) -> torch.Tensor:
+    """``x @ matrix`` over the last axis (grouped per-group matrices for 3-D *matrix*).  Dense
+    fp32 products run as the bf16x3 tcgen05 GEMM on sm_100 (``ops.matmul_f32``)."""
     if matrix.ndim == 3:
         return torch.einsum("...gk,gkj->...gj", x, matrix)
+    from dattri_llm_b200.ops.gemm import matmul_f32
+
+    if x.dtype == torch.float32 and matrix.dtype == torch.float32 and x.is_cuda:
+        flat = x.reshape(-1, x.shape[-1])
+        return matmul_f32(flat, matrix).reshape(*x.shape[:-1], matrix.shape[-1])
     return x @ matrix
 
 

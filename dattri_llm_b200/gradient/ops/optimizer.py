@@ -211,4 +211,8 @@ def adamw_influence_coupling(w_theta, w_m, w_v, g_z, g_t, d, s, *, lr: float, st
     r_theta = scale[None, :] * g_z
     r_m = (1.0 - beta1) * g_z
     r_v = 2.0 * (1.0 - beta2) * g_t.float()[None, :] * g_z
-    return r_theta @ w_theta.T + r_m @ w_m.T + r_v @ w_v.T
+    # the three products are one GEMM over the concatenated (theta, m, v) coordinates
+    from dattri_llm_b200.ops.gemm import matmul_f32
+
+    return matmul_f32(torch.cat([r_theta, r_m, r_v], dim=1), torch.cat([w_theta, w_m, w_v], dim=1).float(),
+                      b_transposed=True)

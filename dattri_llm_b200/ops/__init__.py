@@ -147,6 +147,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     gemm_grouped,
     gemm_tn,
     gemm_tn_seg,
+    matmul_f32,
     matmul_tn,
 )
 from dattri_llm_b200.ops.gram import (  # noqa: E402
@@ -179,6 +180,7 @@ __all__ = [
     "ghost_gram",
     "ghost_gram_tokens",
     "mask_gather",
+    "matmul_f32",
     "matmul_tn",
     "native",
     "norm_per_sample_grad",

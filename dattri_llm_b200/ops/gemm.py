@@ -38,6 +38,34 @@ def transpose_last2(x: torch.Tensor) -> torch.Tensor:
     return x.transpose(-1, -2).contiguous()
 
 
+_F32_MIN_WORK = 1 << 22  # below this M*N*K a torch matmul is cheaper than the split + launch
+
+
+def matmul_f32(a: torch.Tensor, b: torch.Tensor, *, b_transposed: bool = False) -> torch.Tensor:
+    """fp32 ``a @ b`` (``a @ b^T`` with *b_transposed*) on the tensor cores at fp32-class accuracy.
+
+    For fp32 CUDA matrices on sm_100 (large enough to pay off) each operand is split as
+    ``x = hi + lo`` with ``hi, lo`` bf16 and the three products ``hi_a hi_b + hi_a lo_b +
+    lo_a hi_b`` run as ONE tcgen05 GEMM over the K-concatenated splits, accumulated in fp32
+    (the bf16x3 method of Henry, Tang & Heinecke 2019: about 2^-16 relative error per
+    product, against TF32's 2^-11).  Other inputs use ``torch.matmul``.
+    """
+    from dattri_llm_b200.ops import count_launch, native, use_native
+
+    bt = b if b_transposed else b.t()  # (N, K) logical
+    m, k = a.shape
+    n = bt.shape[0]
+    if not (a.dim() == 2 and bt.dim() == 2 and a.dtype == torch.float32 and bt.dtype == torch.float32
+            and m * n * k >= _F32_MIN_WORK and use_native(a, bt)):
+        return a @ bt.t()
+    count_launch(3)
+    a3 = native().split3_bf16(a, 0)
+    b3 = native().split3_bf16(bt, 1)
+    out = torch.empty(m, n, dtype=torch.float32, device=a.device)
+    gemm_tn(a3, b3, out, mode=STORE_F32)
+    return out
+
+
 def gemm_tn(
     a: torch.Tensor,
     b: torch.Tensor,

@@ -165,3 +165,20 @@ def test_transpose_kernel(shape):
     sl = x[..., 8:]  # a strided source (row stride kept, 16-byte aligned start)
     torch.testing.assert_close(transpose_last2(sl), sl.transpose(-1, -2).contiguous(), rtol=0, atol=0)
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize(("m", "n", "k", "bt"), [(512, 768, 1024, False), (300, 200, 4100, True), (2048, 64, 512, True)])
+def test_matmul_f32_bf16x3(m, n, k, bt):
+    """fp32 products on the tensor cores through the bf16x3 split: relative error near 2^-16
+    against fp64, far below a plain bf16 (2^-8) or TF32 (2^-11) product."""
+    from dattri_llm_b200 import ops
+    from dattri_llm_b200.ops.gemm import matmul_f32
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(n, k, device="cuda", generator=g) if bt else torch.randn(k, n, device="cuda", generator=g)
+    got = matmul_f32(a, b, b_transposed=bt)
+    want = a.double() @ (b.double().T if bt else b.double())
+    rel = float((got.double() - want).abs().max() / want.abs().max())
+    assert rel < 2e-5, rel
+    ops.check_device_errors()
