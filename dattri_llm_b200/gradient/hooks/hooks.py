@@ -59,12 +59,6 @@ _LINEAR_IO_TYPES: tuple[type, ...] = (
     nn.Conv3d, nn.ConvTranspose1d, nn.ConvTranspose2d, nn.ConvTranspose3d,
 ) + ((HF_Conv1D,) if HF_Conv1D is not None else ()) + ((nn.RMSNorm,) if hasattr(nn, "RMSNorm") else ())
 
-#: One layer's ``linear_io`` capture buffer (a dict; keys documented in _new_buffer).
-LayerBuffer = dict
-#: One layer's ``param_grad`` buffer: ``{param_name: tensor | None}``.
-ParamGradBuffer = dict
-
-
 def is_linear_io_capable(module: nn.Module) -> bool:
     """Whether *module*'s per-sample gradient factorizes as an outer product (by type).
 
@@ -94,21 +88,103 @@ def _flatten_tokens(t: torch.Tensor, layer_type: str) -> torch.Tensor:
     return t
 
 
-def _new_buffer() -> LayerBuffer:
-    return {
-        "activation": None,        # last raw activation seen (raw capture)
-        "grad_output": None,       # last raw output gradient seen (raw capture)
-        "_act_parts": [],          # [(device, a or a_p)]
-        "_grad_parts": [],         # [(device, g or g_p)]
-        "_proj_parts": [],         # [(device, dense per-sample block)]
-        "_proj_kw": None,          # resolved projection config of the layer
-        "_proj_matrix": {},        # {"a"/"g": ProjectionMatrix}
-        "_capture_style": "factorized",
-        "_pending": {},            # {device: [forward entries awaiting a backward]}
-        "_fwd_fires": 0,           # grad-enabled forwards this step
-        "_pair_pos": [],           # [(device, invocation position)] per matched pair
-        "_lock": threading.Lock(),
-    }
+class LayerBuffer:
+    """What one hooked layer captures in the current step.
+
+    ``acts`` / ``grads`` hold ``(device, tensor)`` parts of the kept factors (raw, or
+    projected); ``dense`` holds materialized per-sample blocks (or :class:`_DeferredOuter`
+    stand-ins until the step's grouped launch); ``waiting[device]`` is the LIFO of forward
+    entries that still wait for their backward (autograd runs a device's graph in reverse
+    creation order); ``pairs`` records, per matched forward/backward, the device and the
+    invocation position (``k`` of the virtual ``name@k`` layers); ``forwards`` counts the
+    grad-enabled forwards of the step.  ``lock`` guards the lists against DataParallel
+    replica threads.
+    """
+
+    __slots__ = ("layer_type", "module_kwargs", "proj_kw", "capture_style", "matrices", "lock", "acts", "grads",
+                 "dense", "waiting", "forwards", "pairs", "last_activation", "last_grad")
+
+    def __init__(self, layer_type: str, module_kwargs: dict | None, proj_kw: dict | None,
+                 capture_style: str) -> None:
+        self.layer_type, self.module_kwargs = layer_type, module_kwargs
+        self.proj_kw, self.capture_style = proj_kw, capture_style
+        self.matrices: dict = {}  # {"a" / "g": ProjectionMatrix}, resolved on first use
+        self.lock = threading.Lock()
+        self.clear()
+
+    def clear(self) -> None:
+        """Forget the step's captures (configuration and matrices stay)."""
+        self.acts: list = []
+        self.grads: list = []
+        self.dense: list = []
+        self.waiting: dict = {}
+        self.forwards = 0
+        self.pairs: list = []
+        self.last_activation = None
+        self.last_grad = None
+
+    def snapshot(self) -> dict:
+        """Copies of the step's lists and counters (for a secondary pass)."""
+        return {"acts": list(self.acts), "grads": list(self.grads), "dense": list(self.dense),
+                "waiting": {dev: list(stack) for dev, stack in self.waiting.items()}, "forwards": self.forwards,
+                "pairs": list(self.pairs), "last_activation": self.last_activation, "last_grad": self.last_grad}
+
+    def restore(self, snap: dict | None) -> None:
+        """Undo to a :meth:`snapshot` (``None``: an empty step)."""
+        self.clear()
+        for field, value in (snap or {}).items():
+            setattr(self, field, value)
+
+    def keep_matched(self) -> bool:
+        """Drop forwards that never met a backward (activation checkpointing's first pass)
+        and renumber the matched invocations densely per device.  Returns whether any was
+        dropped."""
+        dropped = any(self.waiting.values())
+        if dropped:
+            positions: dict[int, list[int]] = {}
+            for dev, pos in self.pairs:
+                positions.setdefault(dev, []).append(pos)
+            dense_pos = {dev: {p: i for i, p in enumerate(sorted(ps))} for dev, ps in positions.items()}
+            if self.proj_kw is None:  # raw activations are appended at the forward, in call order
+                count: dict[int, int] = {}
+                kept = []
+                for dev, part in self.acts:
+                    pos = count.get(dev, 0)
+                    count[dev] = pos + 1
+                    if pos in dense_pos.get(dev, {}):
+                        kept.append((dev, part))
+                self.acts = kept
+            self.pairs = [(dev, dense_pos[dev][pos]) for dev, pos in self.pairs]
+        self.waiting = {}
+        self.forwards = len(self.pairs)
+        return dropped
+
+    def invocations(self) -> list[tuple[list, list, list]]:
+        """``[(acts, grads, dense)]`` per invocation position (one entry when the layer ran once)."""
+        n = 1 + max((pos for _dev, pos in self.pairs), default=0)
+        if n == 1:
+            return [(self.acts, self.grads, self.dense)]
+        by_pos: list[tuple[list, list, list]] = [([], [], []) for _ in range(n)]
+        if self.dense:
+            for part, (_dev, pos) in zip(self.dense, self.pairs, strict=True):
+                by_pos[pos][2].append(part)
+            return by_pos
+        if self.proj_kw is None:  # activations in forward order, per device
+            count: dict[int, int] = {}
+            for dev, part in self.acts:
+                pos = count.get(dev, 0)
+                count[dev] = pos + 1
+                by_pos[pos][0].append((dev, part))
+        else:  # projected activations are kept at the matched backward, like the gradients
+            for part, (_dev, pos) in zip(self.acts, self.pairs, strict=True):
+                by_pos[pos][0].append(part)
+        for part, (_dev, pos) in zip(self.grads, self.pairs, strict=True):
+            by_pos[pos][1].append(part)
+        return by_pos
+
+
+#: One layer's ``param_grad`` buffer: ``{param_name: tensor | None}``.
+ParamGradBuffer = dict
 
 
 class _Projected:
@@ -158,8 +234,8 @@ class _FusedCaptureLink:
         buf = self.buffers[self.name]
         return (torch.is_grad_enabled() and self.share is not None and not self.offload
                 and (self.routed is None or self.name not in self.routed.layers)
-                and _style(buf) == "logra" and _preprojects_activation(buf["_class_name"], "logra")
-                and buf["_capture_style"] != "factorized" and x.ndim == 3 and x.is_cuda)
+                and _style(buf) == "logra" and _preprojects_activation(buf.layer_type, "logra")
+                and buf.capture_style != "factorized" and x.ndim == 3 and x.is_cuda)
 
     def before_forward(self, module, x: torch.Tensor):
         from dattri_llm_b200.ops.linear import CaptureSlot
@@ -170,7 +246,7 @@ class _FusedCaptureLink:
         (xa,) = dtypes.align(x)
         pm = _projection_matrix(buf, "a", xa, self.projector)
         k = pm.proj_dim
-        if not (ops.should_materialize(buf["_capture_style"], x.shape[1], k, k) and _token_major_ok(pm, xa)):
+        if not (ops.should_materialize(buf.capture_style, x.shape[1], k, k) and _token_major_ok(pm, xa)):
             return None, None
         key, root = _share_key(x, pm, True)
         hit = self.share.get(key)
@@ -290,16 +366,15 @@ def register_linear_io_hooks(
             continue
         if not include_frozen and not has_trainable_params(module):
             continue
-        buf = buffers[name] = _new_buffer()
         layer_type = (type_overrides or {}).get(name) or canonical_class_name(module)
-        buf["_class_name"] = layer_type
         if kwargs_overrides is not None and name in kwargs_overrides:
-            buf["_module_kwargs"] = dict(kwargs_overrides[name])
+            module_kwargs = dict(kwargs_overrides[name])
         else:
-            buf["_module_kwargs"] = extract_module_kwargs(module, layer_type)
+            module_kwargs = extract_module_kwargs(module, layer_type)
+        proj_kw = None
         if projection_kwargs is not None:
-            buf["_proj_kw"] = projection_kwargs.get(name, projection_kwargs.get("__default__"))
-        buf["_capture_style"] = capture_style
+            proj_kw = projection_kwargs.get(name, projection_kwargs.get("__default__"))
+        buffers[name] = LayerBuffer(layer_type, module_kwargs, proj_kw, capture_style)
         bwd = _backward_hook(name, buffers, projector, preconditioner, offload_to_cpu, routed, share,
                              on_layer_backward)
         if getattr(type(module), "__bw_fused_capture__", False) and not _preconditioning(preconditioner):
@@ -376,26 +451,26 @@ def _forward_hook(name, buffers, projector, preconditioner, offload, routed, sha
             layout = routed.push(name, a, dev)
             if layout is not None:
                 a = layout.regroup(a)
-        a = _flatten_tokens(a, buf["_class_name"])
-        emit, emit_type, emit_kw = a, buf["_class_name"], buf["_module_kwargs"]
+        a = _flatten_tokens(a, buf.layer_type)
+        emit, emit_type, emit_kw = a, buf.layer_type, buf.module_kwargs
         if _raw_capture(buf, preconditioner):
             if offload:
                 a = a.cpu()
-            with buf["_lock"]:
-                buf["_pending"].setdefault(dev, []).append(len(buf["_act_parts"]))
-                buf["_act_parts"].append((dev, a))
-                buf["_fwd_fires"] += 1
-            buf["activation"] = a
+            with buf.lock:
+                buf.waiting.setdefault(dev, []).append(len(buf.acts))
+                buf.acts.append((dev, a))
+                buf.forwards += 1
+            buf.last_activation = a
             emit = a
         else:
             entry = a
-            if _preprojects_activation(buf["_class_name"], _style(buf)):
+            if _preprojects_activation(buf.layer_type, _style(buf)):
                 entry = _project_activation(buf, a, projector, share, x, given_a_pt)
                 emit = entry.a.transpose(1, 2) if entry.token_major else entry.a
                 emit_type, emit_kw = "nn.Linear", None
-            with buf["_lock"]:
-                buf["_pending"].setdefault(dev, []).append(entry)
-                buf["_fwd_fires"] += 1
+            with buf.lock:
+                buf.waiting.setdefault(dev, []).append(entry)
+                buf.forwards += 1
         if callback is not None:
             callback(name, emit, emit_type, emit_kw)
         return entry if not _raw_capture(buf, preconditioner) else None
@@ -422,20 +497,20 @@ def _backward_hook(name, buffers, projector, preconditioner, offload, routed, sh
             layout = routed.pop(name, dev)
             if layout is not None:
                 g = layout.regroup(g)
-        g = _flatten_tokens(g, buf["_class_name"])
-        emit, emit_type, emit_kw = g, buf["_class_name"], buf["_module_kwargs"]
+        g = _flatten_tokens(g, buf.layer_type)
+        emit, emit_type, emit_kw = g, buf.layer_type, buf.module_kwargs
         if _raw_capture(buf, preconditioner):
             if offload:
                 g = g.cpu()
-            with buf["_lock"]:
-                stack = buf["_pending"].get(dev)
+            with buf.lock:
+                stack = buf.waiting.get(dev)
                 if not stack:
                     _warn_orphan_backward(name)
                     return
                 stack.pop()
-                buf["_pair_pos"].append((dev, len(stack)))
-                buf["_grad_parts"].append((dev, g))
-            buf["grad_output"] = g
+                buf.pairs.append((dev, len(stack)))
+                buf.grads.append((dev, g))
+            buf.last_grad = g
             emit = g
         else:
             matched, g_p = _capture_projected(buf, g, dev, projector, offload, preconditioner, name, share)
@@ -461,17 +536,17 @@ def _warn_orphan_backward(layer_name: str) -> None:
 def _projection_matrix(buf: LayerBuffer, side: str, x: torch.Tensor, projector) -> ops.ProjectionMatrix:
     """The layer's projection for *side* ``"a"`` / ``"g"``, resolved once per dtype/device."""
     (x,) = dtypes.align(x)
-    pm = buf["_proj_matrix"].get(side)
+    pm = buf.matrices.get(side)
     if pm is not None and pm.matches(x):
         return pm
-    kw = {k: v for k, v in buf["_proj_kw"].items() if k != "style"}
+    kw = {k: v for k, v in buf.proj_kw.items() if k != "style"}
     seed = kw.pop("proj_seed", 0)
-    mk = buf["_module_kwargs"]
+    mk = buf.module_kwargs
     with_bias = side == "a" and mk is not None and mk.get("has_bias", False)
     pm = ops.DattriProjector.coerce(projector).resolve(
         x.shape[-1], proj_seed=seed + 1 if side == "a" else seed, include_bias=with_bias,
         device=x.device, dtype=x.dtype, **kw)
-    buf["_proj_matrix"][side] = pm
+    buf.matrices[side] = pm
     return pm
 
 
@@ -514,7 +589,7 @@ def _project_activation(buf, a, projector, share, source, given_a_pt=None) -> _P
     pm = _projection_matrix(buf, "a", a3, projector)
     seq_len = a3.shape[1]
     k = pm.proj_dim
-    token_major = given_a_pt is not None or (ops.should_materialize(buf["_capture_style"], seq_len, k, k)
+    token_major = given_a_pt is not None or (ops.should_materialize(buf.capture_style, seq_len, k, k)
                                              and _token_major_ok(pm, a3))
     key = None
     if share is not None and a3.is_cuda:
@@ -540,52 +615,52 @@ def _preconditioning(preconditioner) -> bool:
 
 
 def _style(buf: LayerBuffer) -> str | None:
-    return None if buf["_proj_kw"] is None else buf["_proj_kw"].get("style", "logra")
+    return None if buf.proj_kw is None else buf.proj_kw.get("style", "logra")
 
 
 def _raw_capture(buf: LayerBuffer, preconditioner) -> bool:
-    return (buf["_proj_kw"] is None and buf["_capture_style"] == "factorized"
+    return (buf.proj_kw is None and buf.capture_style == "factorized"
             and not _preconditioning(preconditioner))
 
 
 def _keep_factors(buf: LayerBuffer, seq_len: int, k_a: int, k_g: int) -> bool:
-    if buf["_act_parts"]:
+    if buf.acts:
         return True
-    if buf["_proj_parts"]:
+    if buf.dense:
         return False
-    return not ops.should_materialize(buf["_capture_style"], seq_len, k_a, k_g)
+    return not ops.should_materialize(buf.capture_style, seq_len, k_a, k_g)
 
 
 def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_name, share=None, g_pt=None):
     """Pair *g* with its forward and store the projected / materialized / preconditioned
     capture.  Returns ``(matched, projected g to hand the callbacks or None)``.  *g_pt*: the
     output gradient already projected token-major ``(B, k, T)`` (then *g* is ``None``)."""
-    with buf["_lock"]:
-        stack = buf["_pending"].get(dev)
+    with buf.lock:
+        stack = buf.waiting.get(dev)
         entry = stack.pop() if stack else None
         pos = (dev, len(stack)) if entry is not None else None
     if entry is None:
         return False, None
-    proj_kw = buf["_proj_kw"]
+    proj_kw = buf.proj_kw
     kw = dict(proj_kw or {})
     style = kw.pop("style", "logra") if proj_kw is not None else None
     pre = preconditioner if _preconditioning(preconditioner) else None
-    layer_type, mk = buf["_class_name"], buf["_module_kwargs"]
+    layer_type, mk = buf.layer_type, buf.module_kwargs
 
     def keep_factors(a_f, g_f):
         if offload:
             a_f, g_f = a_f.cpu(), g_f.cpu()
-        with buf["_lock"]:
-            buf["_act_parts"].append((dev, a_f))
-            buf["_grad_parts"].append((dev, g_f))
-            buf["_pair_pos"].append(pos)
+        with buf.lock:
+            buf.acts.append((dev, a_f))
+            buf.grads.append((dev, g_f))
+            buf.pairs.append(pos)
 
     def keep_dense(mat):
         if offload:
             mat = mat.cpu()
-        with buf["_lock"]:
-            buf["_proj_parts"].append((dev, mat))
-            buf["_pair_pos"].append(pos)
+        with buf.lock:
+            buf.dense.append((dev, mat))
+            buf.pairs.append(pos)
 
     if style == "logra":
         if isinstance(entry, _Projected):
@@ -593,11 +668,11 @@ def _capture_projected(buf, g, dev, projector, offload, preconditioner, layer_na
             if g_pt is None:
                 g3 = to_3d(dtypes.align(g)[0])
                 pm_g = _projection_matrix(buf, "g", g3, projector)
-                if entry.token_major and _token_major_ok(pm_g, g3) and not buf["_act_parts"]:
+                if entry.token_major and _token_major_ok(pm_g, g3) and not buf.acts:
                     g_pt = project_token_major(pm_g, g3)
                 else:
                     g_p = pm_g(g3)
-            if g_pt is not None and entry.token_major and not buf["_act_parts"]:
+            if g_pt is not None and entry.token_major and not buf.acts:
                 from dattri_llm_b200 import ops as native_ops
 
                 b = g_pt.shape[0]

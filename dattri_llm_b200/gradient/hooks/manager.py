@@ -1,35 +1,39 @@
-"""``HookManager``: turns per-layer hook fires into one ``GradientRecord`` per backward.
+"""``HookManager``: per-layer hook fires in, one ``GradientRecord`` per backward out.
 
-Step-completion barrier (parity: reference ``dattri_llm/gradient/hooks/manager.py``):
+The manager owns the capture of a model: it installs the per-layer hooks (and any forward
+overrides), and decides when a training step's backward is complete so that its gradient
+can be assembled and handed to the callbacks.  A step is complete when
 
-(a) every hooked layer that ran forward this step has received as many backward
-    fires as it had forwards, and
-(b) when linear-IO layers own trainable parameters, their gradients are final --
-    every post-accumulate-grad hook fired, or (under FSDP, whose reduce-scatter
-    writes gradients after the hooks) the end-of-backward engine callback ran;
-(c) every ``param_grad`` hook fired.
+* every hooked layer that ran a forward in the step got as many backward fires as it had
+  forwards (a forward that never gets one -- activation checkpointing's first pass -- is
+  dropped once the backward ends), and
+* the gradients of linear-IO layers' own trainable parameters are final: every
+  post-accumulate hook fired, or, under FSDP (which writes gradients after those hooks),
+  the engine's end-of-backward callback ran; and
+* every ``param_grad`` hook fired.
 
-When all hold, the step is assembled (invocations split into ``name@k`` virtual
-layers, parts from several devices concatenated), identified (content hashes,
-``sample_id_key`` values, or ids handed in with :meth:`HookManager.set_sample_ids`)
-and dispatched to the callbacks outside the lock, so a callback may run a
-secondary forward/backward through the same hooks.  Forwards left unmatched at
-the end of the backward (activation checkpointing's first pass) are reconciled
-away; a step in which no hooked layer received a gradient raises.
+:class:`_StepBarrier` holds this bookkeeping for the step in flight.  When it closes, each
+layer's buffer is turned into entries (a layer called k times yields virtual layers
+``name``, ``name@2`` ... ``name@k``; parts from several devices are concatenated), the
+samples are identified (ids handed in with :meth:`HookManager.set_sample_ids`, a
+``sample_id_key`` field, or content hashes -- computed from host copies of the inputs when
+the data pipeline provides them), and the callbacks run outside the lock, so a callback may
+itself run a forward/backward through the same hooks (the data-selection validation pass
+does, between :meth:`save_state` and :meth:`load_state`).  A backward that reaches no hooked
+layer at all raises.  Public API as in the reference's ``dattri_llm/gradient/hooks/manager.py``.
 
-B200-specific: the manager clears the per-step activation-projection share of
-the hooks (q/k/v, gate/up read one projection), and sample identities can be
-supplied by the data pipeline (hashed on the host from the pinned batch while
-the GPU runs) instead of being computed from device tensors at step end.
+B200 specifics: the step's deferred per-sample outer products run as one grouped tcgen05
+launch when the step closes, and the per-step activation-projection share (q/k/v and
+gate/up read one projection) is cleared with the buffers.
 """
 
 from __future__ import annotations
 
-import operator
 import threading
 import warnings
 from collections.abc import Callable, Generator, Iterable
 from contextlib import contextmanager
+from dataclasses import dataclass, field, replace
 
 import torch
 from torch import nn
@@ -44,6 +48,7 @@ from dattri_llm_b200.gradient.hooks.config import (
     resolve_hook_assignments,
 )
 from dattri_llm_b200.gradient.hooks.hooks import (
+    LayerBuffer,
     _StepShare,
     has_trainable_params,
     register_linear_io_hooks,
@@ -64,26 +69,61 @@ from dattri_llm_b200.utils.autograd import queue_backward_end_callback
 from dattri_llm_b200.utils.hashing import hash_batch
 from dattri_llm_b200.utils.tracing import trace_range
 
-_TASK_ID = getattr(torch._C, "_current_graph_task_id", None)
+_task_id_fn = getattr(torch._C, "_current_graph_task_id", None)
 
 
-def _graph_task_id() -> int:
-    """Id of the running backward graph task (-1 outside a backward)."""
-    return _TASK_ID() if _TASK_ID is not None else -1
+def _backward_task() -> int:
+    """Id of the autograd graph task running on this thread (-1 outside any backward)."""
+    return -1 if _task_id_fn is None else _task_id_fn()
 
 
-def _first_grad_tensor(output: object) -> torch.Tensor | None:
+def _grad_leaf_of(output: object) -> torch.Tensor | None:
+    """The first tensor requiring grad inside a (nested) model output."""
     if isinstance(output, torch.Tensor):
         return output if output.requires_grad else None
-    try:
-        values = output.values() if isinstance(output, dict) else output
-        for v in values:
-            found = _first_grad_tensor(v)
-            if found is not None:
-                return found
-    except TypeError:
+    items = output.values() if isinstance(output, dict) else output
+    if not isinstance(items, Iterable) or isinstance(items, (str, bytes)):
         return None
+    for item in items:
+        found = _grad_leaf_of(item)
+        if found is not None:
+            return found
     return None
+
+
+@dataclass
+class _StepBarrier:
+    """Completion bookkeeping of the step in flight.
+
+    ``ran``: layers with a forward this step; ``finished``: those whose backward fires
+    caught up with their forwards; ``fires``: backward fires per layer; ``unreached``:
+    layers whose forwards all went unmatched.  ``layers_closed`` / ``params_closed`` are
+    the two halves of the barrier (linear-IO side incl. its parameters' gradients, and the
+    ``param_grad`` side); ``weight_fires`` / ``param_fires`` count the parameter hooks;
+    ``weights_final`` is set by the end-of-backward callback; ``end_queued`` says that
+    callback is queued for this step, ``end_task`` which backward it belongs to (nested
+    recomputation backwards end first), and ``recomputed`` that a forward ran inside a
+    backward."""
+
+    ran: set = field(default_factory=set)
+    finished: set = field(default_factory=set)
+    fires: dict = field(default_factory=dict)
+    unreached: set = field(default_factory=set)
+    layers_closed: bool = True
+    params_closed: bool = True
+    weight_fires: int = 0
+    param_fires: int = 0
+    weights_final: bool = False
+    end_queued: bool = False
+    end_task: int = -1
+    recomputed: bool = False
+
+    def fresh(self, has_linear_io: bool, has_param_grad: bool) -> _StepBarrier:
+        return _StepBarrier(layers_closed=not has_linear_io, params_closed=not has_param_grad)
+
+    def copy(self) -> _StepBarrier:
+        return replace(self, ran=set(self.ran), finished=set(self.finished), fires=dict(self.fires),
+                       unreached=set(self.unreached))
 
 
 class HookManager:
@@ -108,106 +148,96 @@ class HookManager:
                  non_batch_first_layers: Iterable[str] | None = None,
                  moe_routed_layers: Iterable[str] | None = None, offload_to_cpu: bool = False,
                  optimizer: torch.optim.Optimizer | Callable[[], torch.optim.Optimizer] | None = None) -> None:
+        if isinstance(sample_hash_fields, (str, int)):
+            sample_hash_fields = [sample_hash_fields]
+        hash_fields = None if sample_hash_fields is None else tuple(sample_hash_fields)
+        if hash_fields is not None and sample_id_key is not None:
+            raise ValueError("give either sample_id_key (identify samples by a field) or sample_hash_fields "
+                             "(hash only some fields), not both.")
+        if hash_fields == ():
+            raise ValueError("sample_hash_fields is empty: name at least one input field to hash.")
         self._model = model
+        self._config = config if config is not None else HookManagerConfig()
         self._callbacks: list = list(callbacks or [])
+        self._sample_id_key = sample_id_key
+        self._sample_hash_fields = hash_fields
+        self._offload = offload_to_cpu
+        self._non_batch_first = set(non_batch_first_layers or ())
+        self._moe_blocks = set(moe_routed_layers or ())
         self._preconditioner = None
         if optimizer is not None:
             from dattri_llm_b200.gradient.optimizer_state import GradientPreconditioner, OptimizerSnapshot
 
-            root = getattr(model, "module", model)
+            inner = getattr(model, "module", model)
             self._preconditioner = GradientPreconditioner(
-                lambda: OptimizerSnapshot(root, optimizer() if callable(optimizer) else optimizer))
-        if isinstance(sample_hash_fields, (str, int)):
-            sample_hash_fields = [sample_hash_fields]
-        self._sample_hash_fields = None if sample_hash_fields is None else tuple(sample_hash_fields)
-        if self._sample_hash_fields is not None:
-            if sample_id_key is not None:
-                raise ValueError("sample_id_key and sample_hash_fields are alternative identifier "
-                                 "schemes; pass one of them.")
-            if not self._sample_hash_fields:
-                raise ValueError("sample_hash_fields must name at least one field.")
-        self._sample_id_key = sample_id_key
-        self._offload = offload_to_cpu
-        self._non_batch_first = set(non_batch_first_layers or ())
-        self._moe_declared = set(moe_routed_layers or ())
-        self._routed: RoutedTokenTracker | None = None
-        self._override_reverts: list = []
-        self._invasive_reverts: list = []
-        self._warned_silent: set[str] = set()
-        self._warned_broadcast: set[str] = set()
-        self._warned_orphans: set[frozenset] = set()
-        self._config = config if config is not None else HookManagerConfig()
-        self._projector: ops.DattriProjector | None = None
-        self._share = _StepShare()
-        self._next_ids: list[str] | None = None
-        self._host_mirror: dict[int, torch.Tensor] | None = None
-
-        self._step_count = 0
-        self._collecting = False
-        self._last_gradient: Gradient | None = None
-        self._step_lock = threading.Lock()
-        self._seen_bwd: set[str] = set()
-        self._bwd_counts: dict[str, int] = {}
-        self._active: set[str] = set()
-        self._orphaned: set[str] = set()
-        self._bwd_done = True
-        self._grad_done = True
-        self._mlp_hook_count = 0
-        self._n_mlp_params = 0
-        self._mlp_ready = False
-        self._end_scheduled = False
-        self._saw_recompute = False
-        self._outer_task = -1
-        self._last_inputs: dict = {}
-        self._registered = False
-        self._fwd_handle = None
-        self._out_handle = None
+                lambda: OptimizerSnapshot(inner, optimizer() if callable(optimizer) else optimizer))
+        # installation state
+        self._installed = False
+        self._reverts: list[Callable[[], None]] = []
+        self._model_hooks: list = []
+        self._layer_hooks: list = []
+        self._weight_hooks: list = []
+        self._param_hooks: list = []
+        self._layers: dict[str, LayerBuffer] = {}
+        self._params: dict[str, dict] = {}
+        self._n_weights = 0          # trainable parameters of linear-IO layers (post-accumulate hooks)
+        self._n_param_hooks = 0      # param_grad hooks
         self._has_linear_io = False
         self._has_param_grad = False
-        self._buffers: dict = {}
-        self._handles: list = []
-        self._mlp_handles: list = []
-        self._n_layers = 0
-        self._param_buffers: dict = {}
-        self._param_handles: list = []
-        self._n_params_hooked = 0
-        self._param_hook_count = 0
+        self._routed: RoutedTokenTracker | None = None
+        self._projector: ops.DattriProjector | None = None
+        self._share = _StepShare()
+        # step state
+        self._lock = threading.Lock()
+        self._barrier = _StepBarrier()
+        self._collecting = False
+        self._steps = 0
+        self._inputs: dict = {}
+        self._pending_ids: list[str] | None = None
+        self._host_inputs: dict[int, torch.Tensor] | None = None
+        self._last_gradient: Gradient | None = None
+        self._warned: set = set()
         self.register()
         for cb in self._callbacks:
             if hasattr(cb, "on_register"):
                 cb.on_register(self)
 
-    # ------------------------------------------------------------------ inputs
-    def _capture_model_input(self, _module, args: tuple, kwargs: dict) -> None:
+    # ------------------------------------------------------------------ model inputs
+    def _on_model_inputs(self, _module, args: tuple, kwargs: dict) -> None:
+        """Keep the forward's inputs: they identify the step's samples."""
         if not self._collecting:
             return
         if torch.is_grad_enabled():
             self._last_gradient = None
+
+        def field_of(f):
+            return f"_arg{f}" if isinstance(f, int) else f
+
         if self._sample_hash_fields is not None:
-            self._last_inputs = {
-                (f"_arg{f}" if isinstance(f, int) else f): (args[f] if isinstance(f, int) else kwargs[f])
-                for f in self._sample_hash_fields
-                if (f < len(args) if isinstance(f, int) else f in kwargs)
-            }
+            picked = {}
+            for f in self._sample_hash_fields:
+                if isinstance(f, int) and f < len(args):
+                    picked[field_of(f)] = args[f]
+                elif not isinstance(f, int) and f in kwargs:
+                    picked[f] = kwargs[f]
+            self._inputs = picked
             return
-        captured = {k: v for k, v in kwargs.items() if isinstance(v, torch.Tensor)}
-        if not captured:
-            captured = {f"_arg{i}": a for i, a in enumerate(args) if isinstance(a, torch.Tensor)}
+        found = {k: v for k, v in kwargs.items() if isinstance(v, torch.Tensor)}
+        if not found:
+            found = {field_of(i): a for i, a in enumerate(args) if isinstance(a, torch.Tensor)}
         key = self._sample_id_key
-        if key is not None:
-            if isinstance(key, int):
-                if key < len(args):
-                    captured[f"_arg{key}"] = args[key]
-            elif key in kwargs:
-                captured[key] = kwargs[key]
-        self._last_inputs = captured
+        if isinstance(key, int) and key < len(args):
+            found[field_of(key)] = args[key]
+        elif isinstance(key, str) and key in kwargs:
+            found[key] = kwargs[key]
+        self._inputs = found
 
     def set_host_inputs(self, mirror: dict[int, torch.Tensor] | None) -> None:
         """Host copies of the next step's device inputs, keyed by ``id()`` of the device
         tensor (consumed by that step).  When every model input of the step is one of them,
         its content hash is computed from the host copies: the same hash, without reading
         device tensors back (which would wait for the GPU at every step)."""
-        self._host_mirror = mirror
+        self._host_inputs = mirror
 
     def set_sample_ids(self, ids: list[str] | None) -> None:
         """Identities of the samples of the next completed step (consumed by that step).
@@ -215,480 +245,355 @@ class HookManager:
         Lets a data pipeline hash the batch on the host (from the pinned copy it sends
         to the GPU) instead of the manager reading device tensors back at step end.
         """
-        self._next_ids = None if ids is None else [str(i) for i in ids]
+        self._pending_ids = None if ids is None else [str(i) for i in ids]
 
-    # ------------------------------------------------------------------ barrier
-    def _dispatch_layer_forward(self, name, activation, layer_type, module_kwargs) -> None:
-        if name not in self._active:
-            with self._step_lock:
-                self._active.add(name)
-        if self._collecting:
-            task = _graph_task_id()
-            if task != -1:  # a forward inside a backward: checkpoint recomputation
-                with self._step_lock:
-                    self._saw_recompute = True
-                    if self._outer_task == -1:
-                        self._outer_task = task
-                    if (self._n_mlp_params > 0 and not self._end_scheduled
-                            and queue_backward_end_callback(self._on_backward_end)):
-                        self._end_scheduled = True
+    # ------------------------------------------------------------------ the barrier
+    def _queue_end_callback(self) -> None:
+        """Queue the end-of-backward callback once per step (caller holds the lock)."""
+        b = self._barrier
+        if not b.end_queued and queue_backward_end_callback(self._on_backward_finished):
+            b.end_queued = True
+            if b.end_task == -1:
+                b.end_task = _backward_task()
+
+    def _on_layer_forward(self, name, activation, layer_type, module_kwargs) -> None:
+        with self._lock:
+            self._barrier.ran.add(name)
+            if self._collecting and _backward_task() != -1:  # a forward inside a backward: recomputation
+                b = self._barrier
+                b.recomputed = True
+                if b.end_task == -1:
+                    b.end_task = _backward_task()
+                if self._n_weights:
+                    self._queue_end_callback()
         for cb in self._callbacks:
             cb.on_layer_forward(name, activation, layer_type, module_kwargs)
 
-    def _check_step_bwd_complete(self, name, grad_output, layer_type, module_kwargs) -> None:
+    def _on_layer_backward(self, name, grad_output, layer_type, module_kwargs) -> None:
         for cb in self._callbacks:
             cb.on_layer_backward(name, grad_output, layer_type, module_kwargs)
         if not self._collecting:
             return
-        record = None
-        with self._step_lock:
-            if (self._n_mlp_params > 0 and not self._end_scheduled
-                    and queue_backward_end_callback(self._on_backward_end)):
-                self._end_scheduled = True
-                if self._outer_task == -1:
-                    self._outer_task = _graph_task_id()
-            self._bwd_counts[name] = self._bwd_counts.get(name, 0) + 1
-            if self._bwd_counts[name] >= self._buffers[name]["_fwd_fires"]:
-                self._seen_bwd.add(name)
-            if self._bwd_hooks_done():
-                record = self._check_mlp_done()
+        with self._lock:
+            b = self._barrier
+            if self._n_weights:
+                self._queue_end_callback()
+            b.fires[name] = b.fires.get(name, 0) + 1
+            if b.fires[name] >= self._layers[name].forwards:
+                b.finished.add(name)
+            record = self._close_linear_side()
         if record is not None:
-            self._dispatch_step_end(record)
+            self._emit(record)
 
-    def _on_backward_end(self) -> None:
+    def _on_weight_grad_final(self, _layer, _param, _grad) -> None:
+        """Post-accumulate hook of a linear-IO layer's own trainable parameter."""
+        if not self._collecting:
+            return
+        with self._lock:
+            self._barrier.weight_fires += 1
+            record = self._close_linear_side()
+        if record is not None:
+            self._emit(record)
+
+    def _on_param_grad(self, _layer, _param, _grad) -> None:
+        """A ``param_grad`` hook fired."""
         if not self._collecting:
             return
         record = None
-        with self._step_lock:
-            if not self._end_scheduled:
-                return
-            if self._outer_task != -1 and _graph_task_id() != self._outer_task:
-                return  # end of a nested (recomputation) backward, not ours
-            self._mlp_ready = True
-            self._reconcile_unmatched_forwards()
-            orphaned = sorted(self._orphaned)
-            stalled = self._has_linear_io and bool(orphaned) and not self._active and not self._bwd_done
-            record = None if stalled else self._check_mlp_done()
+        with self._lock:
+            b = self._barrier
+            b.param_fires += 1
+            if b.param_fires >= self._n_param_hooks:
+                b.param_fires = 0
+                b.params_closed = True
+                record = self._close_if_ready()
+        if record is not None:
+            self._emit(record)
+
+    def _on_model_output(self, _module, _args, output) -> None:
+        if self._collecting and self._layers and torch.is_grad_enabled():
+            leaf = _grad_leaf_of(output)
+            if leaf is not None:
+                leaf.register_hook(self._on_backward_started)
+
+    def _on_backward_started(self, _grad) -> None:
+        if self._collecting:
+            with self._lock:
+                self._queue_end_callback()
+
+    def _on_backward_finished(self) -> None:
+        """Engine callback at the end of the step's backward."""
+        if not self._collecting:
+            return
+        with self._lock:
+            b = self._barrier
+            if not b.end_queued or (b.end_task != -1 and _backward_task() != b.end_task):
+                return  # not queued for us, or the end of a nested recomputation backward
+            b.weights_final = True
+            self._settle_unmatched()
+            unreached = sorted(b.unreached)
+            stalled = self._has_linear_io and bool(unreached) and not b.ran and not b.layers_closed
+            record = None if stalled else self._close_linear_side()
         if stalled:
+            shown = unreached[:8] + (["..."] if len(unreached) > 8 else [])
             raise RuntimeError(
-                f"No hooked layer received a gradient this step: {orphaned[:8]}"
-                f"{'...' if len(orphaned) > 8 else ''} ran forward but the backward pass did not "
-                "reach them, so the step cannot complete. A layer receives a gradient only when the "
-                "loss depends on its output through something that requires grad; with frozen layers "
-                "(include_frozen=True) a parameter or input upstream of them must require grad.",
-            )
-        if orphaned and record is not None:
-            key = frozenset(orphaned)
-            if key not in self._warned_orphans:
-                self._warned_orphans.add(key)
-                warnings.warn(
-                    f"Hooked layers {orphaned[:8]}{'...' if len(orphaned) > 8 else ''} ran forward "
-                    "but received no gradient this step and are left out of its record (a detached "
-                    "branch, or a frozen layer with nothing trainable upstream). Reported once per "
-                    "layer set.",
-                    stacklevel=2,
-                )
+                f"the backward reached none of the hooked layers that ran forward ({shown}), so the step "
+                "cannot be completed. A layer gets a gradient only if the loss depends on its output through "
+                "something that requires grad -- with frozen layers (include_frozen=True), a parameter or an "
+                "input upstream of them must require grad.")
+        if unreached and record is not None and frozenset(unreached) not in self._warned:
+            self._warned.add(frozenset(unreached))
+            shown = unreached[:8] + (["..."] if len(unreached) > 8 else [])
+            warnings.warn(f"hooked layers {shown} ran forward but got no gradient in this step (a detached "
+                          "branch, or frozen layers with nothing trainable upstream); they are left out of the "
+                          "step's record. Reported once per set of layers.", stacklevel=2)
         if record is not None:
-            self._dispatch_step_end(record)
+            self._emit(record)
 
-    def _capture_model_output(self, _module, _args, output) -> None:
-        if not self._collecting or self._n_layers == 0 or not torch.is_grad_enabled():
-            return
-        t = _first_grad_tensor(output)
-        if t is not None:
-            t.register_hook(self._on_backward_begin)
+    def _settle_unmatched(self) -> None:
+        """At the end of a backward: forget forwards that met no backward (caller holds the lock)."""
+        b = self._barrier
+        for name, buf in self._layers.items():
+            with buf.lock:
+                dropped = buf.keep_matched()
+                matched = buf.forwards
+            if matched == 0:
+                b.ran.discard(name)
+                if dropped:
+                    b.unreached.add(name)
+            elif b.fires.get(name, 0) >= matched:
+                b.finished.add(name)
 
-    def _on_backward_begin(self, _grad) -> None:
-        if not self._collecting:
-            return
-        with self._step_lock:
-            if not self._end_scheduled and queue_backward_end_callback(self._on_backward_end):
-                self._end_scheduled = True
-                if self._outer_task == -1:
-                    self._outer_task = _graph_task_id()
+    def _layers_finished(self) -> bool:
+        b = self._barrier
+        return not self._layers or (bool(b.ran) and len(b.finished) == len(b.ran))
 
-    def _reconcile_unmatched_forwards(self) -> None:
-        for name, buf in self._buffers.items():
-            with buf["_lock"]:
-                had_orphans = any(buf["_pending"].values())
-                if had_orphans:
-                    self._drop_orphan_forwards(buf)
-                buf["_pending"] = {}
-                matched = len(buf["_pair_pos"])
-                buf["_fwd_fires"] = matched
-            if matched == 0 and had_orphans:
-                self._active.discard(name)
-                self._orphaned.add(name)
-            elif matched == 0:
-                self._active.discard(name)
-            elif self._bwd_counts.get(name, 0) >= matched:
-                self._seen_bwd.add(name)
-
-    @staticmethod
-    def _drop_orphan_forwards(buf: dict) -> None:
-        """Keep only matched forwards and renumber invocation positions densely."""
-        matched: dict[int, list[int]] = {}
-        for dev, pos in buf["_pair_pos"]:
-            matched.setdefault(dev, []).append(pos)
-        remap = {dev: {p: r for r, p in enumerate(sorted(ps))} for dev, ps in matched.items()}
-        if buf["_proj_kw"] is None:
-            seen: dict[int, int] = {}
-            kept = []
-            for dev, part in buf["_act_parts"]:
-                pos = seen.get(dev, 0)
-                seen[dev] = pos + 1
-                if pos in remap.get(dev, {}):
-                    kept.append((dev, part))
-            buf["_act_parts"] = kept
-        buf["_pair_pos"] = [(dev, remap[dev][pos]) for dev, pos in buf["_pair_pos"]]
-
-    def _check_step_mlp_param_complete(self, _l, _p, _g) -> None:
-        if not self._collecting:
-            return
-        record = None
-        with self._step_lock:
-            self._mlp_hook_count += 1
-            if self._mlp_hook_count >= self._n_mlp_params:
-                record = self._check_mlp_done()
-        if record is not None:
-            self._dispatch_step_end(record)
-
-    def _bwd_hooks_done(self) -> bool:
-        if self._n_layers == 0:
-            return True
-        return len(self._active) > 0 and len(self._seen_bwd) == len(self._active)
-
-    def _check_mlp_done(self) -> GradientRecord | None:
-        params_done = (self._n_mlp_params == 0 or self._mlp_ready
-                       or self._mlp_hook_count >= self._n_mlp_params)
-        if self._bwd_hooks_done() and params_done:
-            self._bwd_done = True
-            return self._check_step_complete()
+    def _close_linear_side(self) -> GradientRecord | None:
+        """Barrier (a) + (b); on success try the whole step (caller holds the lock)."""
+        b = self._barrier
+        weights_ready = self._n_weights == 0 or b.weights_final or b.weight_fires >= self._n_weights
+        if self._layers_finished() and weights_ready:
+            b.layers_closed = True
+            return self._close_if_ready()
         return None
 
-    def _check_step_grad_complete(self, _l, _p, _g) -> None:
-        if not self._collecting:
-            return
-        record = None
-        with self._step_lock:
-            self._param_hook_count += 1
-            if self._param_hook_count >= self._n_params_hooked:
-                self._param_hook_count = 0
-                self._grad_done = True
-                record = self._check_step_complete()
-        if record is not None:
-            self._dispatch_step_end(record)
+    def _close_if_ready(self) -> GradientRecord | None:
+        b = self._barrier
+        return self._close_step() if b.layers_closed and b.params_closed else None
 
-    def _check_step_complete(self) -> GradientRecord | None:
-        return self._finalize_step() if self._bwd_done and self._grad_done else None
-
-    # ------------------------------------------------------------------ assembly
-    def _extract_sample_ids(self, expected: int) -> list[str]:
+    # ------------------------------------------------------------------ sample identity
+    def _id_field(self) -> str | None:
         key = self._sample_id_key
-        fld = f"_arg{key}" if isinstance(key, int) else key
-        if fld not in self._last_inputs:
-            raise KeyError(
-                f"sample_id_key={key!r} was not found among the captured model inputs "
-                f"{sorted(self._last_inputs)}; cannot assign sample identities.",
-            )
-        v = self._last_inputs[fld]
-        ids = v.reshape(-1).tolist() if isinstance(v, torch.Tensor) else list(v)
+        return None if key is None else (f"_arg{key}" if isinstance(key, int) else key)
+
+    def _ids_from_key(self, expected: int) -> list[str]:
+        fld = self._id_field()
+        if fld not in self._inputs:
+            raise KeyError(f"the model inputs of this step ({sorted(self._inputs)}) lack the sample_id_key field "
+                           f"{self._sample_id_key!r}; samples cannot be identified.")
+        value = self._inputs[fld]
+        ids = value.reshape(-1).tolist() if isinstance(value, torch.Tensor) else list(value)
         if len(ids) != expected:
-            raise ValueError(f"sample_id_key={key!r} yielded {len(ids)} identifiers but the step's "
-                             f"batch size is {expected}.")
+            raise ValueError(f"the sample_id_key field {self._sample_id_key!r} holds {len(ids)} ids for a step of "
+                             f"{expected} samples.")
         return [str(i) for i in ids]
 
-    def _shape_inputs(self) -> list:
-        """The captured model inputs that can tell the batch size: every one but the
-        sample-identifier field (its length is what gets checked against the batch)."""
-        key = self._sample_id_key
-        skip = None if key is None else (f"_arg{key}" if isinstance(key, int) else key)
-        return [v for k, v in self._last_inputs.items() if k != skip]
+    def _sized_inputs(self) -> list:
+        """Inputs that tell the batch size (the id field itself excluded: its length is checked)."""
+        skip = self._id_field()
+        return [v for k, v in self._inputs.items() if k != skip]
 
-    def _input_batch_size(self, default: int = 1) -> int:
-        for v in self._shape_inputs():
-            if isinstance(v, torch.Tensor) and v.ndim > 0:
-                return v.shape[0]
-        return default
+    def _batch_size(self, gradient: Gradient) -> int:
+        def leading(default):
+            return next((v.shape[0] for v in self._sized_inputs() if isinstance(v, torch.Tensor) and v.ndim > 0),
+                        default)
 
-    def _step_batch_size(self, gradient: Gradient) -> int:
         try:
             b = gradient.batch_size
         except ValueError:
-            return self._input_batch_size()
-        inputs = self._shape_inputs()
-        for v in inputs:
-            if (isinstance(v, torch.Tensor) and v.ndim > 0 and v.shape[0] == b) or (
-                    isinstance(v, (list, tuple)) and len(v) == b):
-                return b
-        return self._input_batch_size(default=b) if inputs else b
+            return leading(1)
+        sized = self._sized_inputs()
+        if not sized:
+            return b
+        agrees = any((isinstance(v, torch.Tensor) and v.ndim > 0 and v.shape[0] == b)
+                     or (isinstance(v, (list, tuple)) and len(v) == b) for v in sized)
+        return b if agrees else leading(b)
 
-    def _finalize_step(self) -> GradientRecord:
-        with trace_range(f"dattri.capture.step[{self._step_count}]"):
-            return self._finalize_step_inner()
-
-    def _finalize_step_inner(self) -> GradientRecord:
-        self._last_gradient = None
-        gradient = self._assemble_gradient()
-        step = self._step_count
-        self._step_count += 1
-        self._seen_bwd.clear()
-        self._bwd_counts.clear()
-        self._orphaned.clear()
-        self._mlp_hook_count = 0
-        self._param_hook_count = 0
-        self._mlp_ready = False
-        self._end_scheduled = False
-        self._saw_recompute = False
-        self._outer_task = -1
-        self._bwd_done = not self._has_linear_io
-        self._grad_done = not self._has_param_grad
-        self._reset_layer_buffers()
-        self._reset_param_buffers()
-        self._last_gradient = gradient
-        batch = self._step_batch_size(gradient)
-        ids, self._next_ids = self._next_ids, None
-        mirror, self._host_mirror = self._host_mirror, None
+    def _sample_identities(self, batch: int) -> list[str]:
+        ids, self._pending_ids = self._pending_ids, None
+        mirror, self._host_inputs = self._host_inputs, None
         if ids is not None:
             if len(ids) != batch:
-                raise ValueError(f"set_sample_ids supplied {len(ids)} identities for a step of {batch} samples.")
-            input_hash = ids
-        elif self._sample_id_key is not None:
-            input_hash = self._extract_sample_ids(batch)
-        else:
-            if self._sample_hash_fields is not None:
-                missing = [f for f in self._sample_hash_fields
-                           if (f"_arg{f}" if isinstance(f, int) else f) not in self._last_inputs]
-                if missing:
-                    raise KeyError(f"sample_hash_fields {missing!r} were not found among the model "
-                                   "inputs of this step; cannot assign sample identities.")
-            inputs = self._last_inputs
-            if mirror:
-                hosted = {k: mirror.get(id(v)) if isinstance(v, torch.Tensor) else v for k, v in inputs.items()}
-                if all(h is not None for h in hosted.values()):
-                    inputs = hosted
-            input_hash = hash_batch(inputs, batch)
-        return GradientRecord(step=step, input_hash=input_hash, gradient=gradient,
-                              sample_id_key=self._sample_id_key)
+                raise ValueError(f"set_sample_ids gave {len(ids)} identities for a step of {batch} samples.")
+            return ids
+        if self._sample_id_key is not None:
+            return self._ids_from_key(batch)
+        if self._sample_hash_fields is not None:
+            absent = [f for f in self._sample_hash_fields
+                      if (f"_arg{f}" if isinstance(f, int) else f) not in self._inputs]
+            if absent:
+                raise KeyError(f"sample_hash_fields {absent!r} are not among this step's model inputs; samples "
+                               "cannot be identified.")
+        inputs = self._inputs
+        if mirror:
+            on_host = {k: mirror.get(id(v)) if isinstance(v, torch.Tensor) else v for k, v in inputs.items()}
+            if all(v is not None for v in on_host.values()):
+                inputs = on_host
+        return hash_batch(inputs, batch)
 
-    def _dispatch_step_end(self, record: GradientRecord) -> None:
+    # ------------------------------------------------------------------ closing a step
+    def _close_step(self) -> GradientRecord:
+        with trace_range(f"dattri.capture.step[{self._steps}]"):
+            self._last_gradient = None
+            gradient = self._build_gradient()
+            step = self._steps
+            self._steps += 1
+            self._barrier = self._barrier.fresh(self._has_linear_io, self._has_param_grad)
+            self._clear_captures()
+            self._last_gradient = gradient
+            ids = self._sample_identities(self._batch_size(gradient))
+            return GradientRecord(step=step, input_hash=ids, gradient=gradient, sample_id_key=self._sample_id_key)
+
+    def _emit(self, record: GradientRecord) -> None:
         for cb in self._callbacks:
             cb.on_step_end(record)
 
     @staticmethod
-    def _concat_parts(parts: list) -> torch.Tensor:
-        ordered = [t for _, t in sorted(parts, key=operator.itemgetter(0))]
-        if len(ordered) == 1:
-            return ordered[0]
-        dev = ordered[0].device
-        return torch.cat([t if t.device == dev else t.to(dev) for t in ordered], dim=0)
-
-    @staticmethod
-    def _split_invocations(buf: dict) -> list[tuple[list, list, list]]:
-        pair_pos = buf["_pair_pos"]
-        n_inv = max((p for _, p in pair_pos), default=0) + 1
-        if n_inv <= 1:
-            return [(buf["_act_parts"], buf["_grad_parts"], buf["_proj_parts"])]
-        acts = [[] for _ in range(n_inv)]
-        grads = [[] for _ in range(n_inv)]
-        projs = [[] for _ in range(n_inv)]
-        if buf["_proj_parts"]:
-            for (dev, part), (_, pos) in zip(buf["_proj_parts"], pair_pos, strict=True):
-                projs[pos].append((dev, part))
-        elif buf["_proj_kw"] is None:
-            seen: dict[int, int] = {}
-            for dev, part in buf["_act_parts"]:
-                pos = seen.get(dev, 0)
-                seen[dev] = pos + 1
-                acts[pos].append((dev, part))
-            for (dev, part), (_, pos) in zip(buf["_grad_parts"], pair_pos, strict=True):
-                grads[pos].append((dev, part))
-        else:
-            for (dev, part), (_, pos) in zip(buf["_act_parts"], pair_pos, strict=True):
-                acts[pos].append((dev, part))
-            for (dev, part), (_, pos) in zip(buf["_grad_parts"], pair_pos, strict=True):
-                grads[pos].append((dev, part))
-        return list(zip(acts, grads, projs, strict=True))
+    def _merge_parts(parts: list) -> torch.Tensor:
+        """Device parts ``[(device index, tensor)]`` in device order, on the first device."""
+        tensors = [t for _dev, t in sorted(parts, key=lambda item: item[0])]
+        if len(tensors) == 1:
+            return tensors[0]
+        home = tensors[0].device
+        return torch.cat([t.to(home) for t in tensors], dim=0)
 
     def _flush_deferred(self) -> None:
-        """Run the step's deferred per-sample outer products and put their results in place."""
+        """Run the step's deferred per-sample outer products (one grouped launch per shape)."""
         self._share.flush_outer()
-        for buf in self._buffers.values():
-            with buf["_lock"]:
-                _StepShare.resolve(buf["_proj_parts"])
+        for buf in self._layers.values():
+            with buf.lock:
+                _StepShare.resolve(buf.dense)
 
-    def _assemble_gradient(self) -> Gradient:
+    def _entry(self, name: str, buf: LayerBuffer, acts, grads, dense):
+        """``(data, representation, layer type, indexing)`` of one invocation of a layer."""
+        batch_first = name not in self._non_batch_first
+        style = (buf.proj_kw or {}).get("style", "logra") if buf.proj_kw else None
+        if dense or style in ("dense", "mask") or self._config.capture_style == "materialized":
+            if not dense:
+                raise RuntimeError(f"nothing was captured for layer {name!r}: run backward() inside collect().")
+            return self._merge_parts(dense), "materialized", buf.layer_type, "batch"
+        if not acts or not grads:
+            raise RuntimeError(f"nothing was captured for layer {name!r}: run backward() inside collect().")
+        a, g = self._merge_parts(acts), self._merge_parts(grads)
+        if buf.proj_kw is not None:
+            tokens = a.shape[1 if batch_first else 0] > 1
+            return (Factorized(a, g, module_kwargs=None, batch_first=batch_first), "factorized", "nn.Linear",
+                    "batch_token" if tokens else "batch")
+        if a.ndim == 1 and is_embedding(buf.layer_type):
+            a, g = a.unsqueeze(0), g.unsqueeze(0)
+        per_token = a.ndim >= 3 or not a.is_floating_point()
+        return (Factorized(a, g, module_kwargs=buf.module_kwargs, batch_first=batch_first), "factorized",
+                buf.layer_type, "batch_token" if per_token else "batch")
+
+    def _build_gradient(self) -> Gradient:
         self._flush_deferred()
         data, rep, types, idx = {}, {}, {}, {}
-        for lname, buf in self._buffers.items():
-            if buf["_fwd_fires"] == 0:
-                self._warn_silent(lname)
+        for name, buf in self._layers.items():
+            if buf.forwards == 0:
+                self._warn_absent(name)
                 continue
-            batch_first = lname not in self._non_batch_first
-            proj_kw = buf["_proj_kw"]
-            style = proj_kw.get("style", "logra") if proj_kw else None
-            for k, (acts, grads, projs) in enumerate(self._split_invocations(buf)):
-                out = lname if k == 0 else f"{lname}@{k + 1}"
-                if projs or style in ("dense", "mask") or self._config.capture_style == "materialized":
-                    if not projs:
-                        raise RuntimeError(f"Layer '{lname}' has no buffered data. Ensure backward() "
-                                           "was called inside the collect() context.")
-                    data[out], rep[out], types[out], idx[out] = (
-                        self._concat_parts(projs), "materialized", buf["_class_name"], "batch")
-                    continue
-                if not acts or not grads:
-                    raise RuntimeError(f"Layer '{lname}' has no buffered data. Ensure backward() was "
-                                       "called inside the collect() context.")
-                a, g = self._concat_parts(acts), self._concat_parts(grads)
-                if proj_kw is not None:
-                    data[out] = Factorized(a, g, module_kwargs=None, batch_first=batch_first)
-                    rep[out], types[out] = "factorized", "nn.Linear"
-                    idx[out] = "batch_token" if a.shape[1 if batch_first else 0] > 1 else "batch"
-                    continue
-                if a.ndim == 1 and is_embedding(buf["_class_name"]):
-                    a, g = a.unsqueeze(0), g.unsqueeze(0)
-                data[out] = Factorized(a, g, module_kwargs=buf["_module_kwargs"], batch_first=batch_first)
-                rep[out], types[out] = "factorized", buf["_class_name"]
-                idx[out] = "batch_token" if a.ndim >= 3 or not a.is_floating_point() else "batch"
-        for lname, pbuf in self._param_buffers.items():
-            for pname, grad in pbuf.items():
-                if grad is None:
-                    continue
-                key = f"{lname}.{pname}"
-                data[key], rep[key], types[key], idx[key] = grad, "materialized", PARAM_GRAD_TYPES, "batch"
+            for k, (acts, grads, dense) in enumerate(buf.invocations()):
+                out = name if k == 0 else f"{name}@{k + 1}"
+                data[out], rep[out], types[out], idx[out] = self._entry(name, buf, acts, grads, dense)
+        for layer, grads in self._params.items():
+            for pname, grad in grads.items():
+                if grad is not None:
+                    key = f"{layer}.{pname}"
+                    data[key], rep[key], types[key], idx[key] = grad, "materialized", PARAM_GRAD_TYPES, "batch"
         if not data:
-            raise RuntimeError("No gradient data assembled. Ensure backward() was called inside the "
-                               "collect() context.")
-        self._warn_broadcast(data, types)
+            raise RuntimeError("the step assembled no gradient: run backward() inside collect().")
+        self._warn_shared_rows(data, types)
         return Gradient(rep, data, types, idx)
 
-    def _warn_silent(self, lname: str) -> None:
-        if lname in self._warned_silent:
+    def _warn_absent(self, name: str) -> None:
+        if ("absent", name) in self._warned:
             return
-        self._warned_silent.add(lname)
-        if ".dattri_experts." in lname or ".dattri_router" in lname:
-            warnings.warn(f"Fused MoE proxy {lname} did not run in this step, so its parameters are "
-                          "absent from the record.", stacklevel=2)
+        self._warned.add(("absent", name))
+        if ".dattri_experts." in name or ".dattri_router" in name:
+            warnings.warn(f"the fused-MoE stand-in {name} did not run in this step; its parameters are not in the "
+                          "record.", stacklevel=2)
             return
-        warnings.warn(
-            f"Hooked layer {lname} ran no forward in this step and is absent from its record. If the "
-            "model uses the layer's weight without calling the module (a functional call or a fused "
-            "kernel), it is never captured; see gradient.hooks.override_layers. Reported once per layer.",
-            stacklevel=2,
-        )
+        warnings.warn(f"hooked layer {name} ran no forward in this step and is not in its record. A model that "
+                      "uses the weight without calling the module (a functional call or a fused kernel) is never "
+                      "captured there -- see gradient.hooks.override_layers. Reported once per layer.", stacklevel=2)
 
-    def _warn_broadcast(self, data: dict, types: dict) -> None:
-        batch = max((v.activation.shape[0 if v.batch_first else 1] if isinstance(v, Factorized) else v.shape[0]
-                     for n, v in data.items() if types.get(n) != PARAM_GRAD_TYPES), default=0)
+    def _warn_shared_rows(self, data: dict, types: dict) -> None:
+        def rows(v):
+            return v.activation.shape[0 if v.batch_first else 1] if isinstance(v, Factorized) else v.shape[0]
+
+        batch = max((rows(v) for n, v in data.items() if types.get(n) != PARAM_GRAD_TYPES), default=0)
         if batch <= 1:
             return
         for name, v in data.items():
-            if not isinstance(v, Factorized) or name in self._warned_broadcast:
-                continue
-            if v.activation.shape[0 if v.batch_first else 1] == 1:
-                self._warned_broadcast.add(name)
-                warnings.warn(
-                    f"Layer '{name}' produced a broadcast (batch-collapsed) gradient: batch size 1 while "
-                    f"the step batch is {batch} (e.g. a positional embedding added to every sample). Its "
-                    "gradient is summed over the batch and is NOT per-sample; per-sample attribution "
-                    "treats it as a single shared row.",
-                    stacklevel=3,
-                )
+            if isinstance(v, Factorized) and rows(v) == 1 and ("shared", name) not in self._warned:
+                self._warned.add(("shared", name))
+                warnings.warn(f"layer {name!r} captured one row for a step of {batch} samples (an input shared by "
+                              "the whole batch, e.g. a positional embedding): its gradient is summed over the batch "
+                              "and is treated as one shared row, not per-sample.", stacklevel=3)
 
-    def _reset_layer_buffers(self) -> None:
-        self._active.clear()
+    def _clear_captures(self) -> None:
         self._share.clear()
         if self._routed is not None:
             self._routed.reset()
-        for buf in self._buffers.values():
-            buf["activation"] = None
-            buf["grad_output"] = None
-            buf["_act_parts"] = []
-            buf["_grad_parts"] = []
-            buf["_proj_parts"] = []
-            buf["_pending"] = {}
-            buf["_fwd_fires"] = 0
-            buf["_pair_pos"] = []
+        for buf in self._layers.values():
+            buf.clear()
+        for grads in self._params.values():
+            for pname in grads:
+                grads[pname] = None
 
-    def _reset_param_buffers(self) -> None:
-        for buf in self._param_buffers.values():
-            for p in buf:
-                buf[p] = None
-
-    # ------------------------------------------------------------------ state
+    # ------------------------------------------------------------------ secondary passes
     def save_state(self) -> dict:
-        """Snapshot of the in-flight step (for a secondary pass through the same hooks)."""
+        """Snapshot of the step in flight, for a secondary forward/backward through the same
+        hooks (restore it with :meth:`load_state`): ``{"layers", "params", "inputs", "step",
+        "last_gradient", "barrier", "pending_ids"}``."""
         self._flush_deferred()
-        return {
-            "layer_buffers": {n: {
-                "_act_parts": list(b["_act_parts"]), "_grad_parts": list(b["_grad_parts"]),
-                "_proj_parts": list(b["_proj_parts"]),
-                "_pending": {k: list(v) for k, v in b["_pending"].items()},
-                "_fwd_fires": b["_fwd_fires"], "_pair_pos": list(b["_pair_pos"]),
-                "activation": b["activation"], "grad_output": b["grad_output"],
-            } for n, b in self._buffers.items()},
-            "param_buffers": {n: dict(b) for n, b in self._param_buffers.items()},
-            "last_inputs": dict(self._last_inputs), "step_count": self._step_count,
-            "last_gradient": self._last_gradient, "seen_bwd": set(self._seen_bwd),
-            "active_layers": set(self._active), "bwd_replica_counts": dict(self._bwd_counts),
-            "mlp_param_hook_count": self._mlp_hook_count, "param_hook_count": self._param_hook_count,
-            "bwd_done": self._bwd_done, "grad_done": self._grad_done, "mlp_params_ready": self._mlp_ready,
-            "backward_end_scheduled": self._end_scheduled, "saw_recompute": self._saw_recompute,
-            "outer_task_id": self._outer_task, "next_ids": self._next_ids,
-        }
+        with self._lock:
+            barrier = self._barrier.copy()
+        return {"layers": {n: b.snapshot() for n, b in self._layers.items()},
+                "params": {n: dict(g) for n, g in self._params.items()}, "inputs": dict(self._inputs),
+                "step": self._steps, "last_gradient": self._last_gradient, "barrier": barrier,
+                "pending_ids": self._pending_ids}
 
     def clear_state(self) -> None:
         """Empty the layer and parameter buffers (the step counter is kept)."""
-        self._reset_layer_buffers()
-        self._reset_param_buffers()
+        with self._lock:
+            self._barrier.ran.clear()
+        self._clear_captures()
 
     def load_state(self, state: dict) -> None:
-        """Restore a :meth:`save_state` snapshot."""
-        for name, buf in self._buffers.items():
-            s = state["layer_buffers"].get(name, {})
-            buf["_act_parts"] = s.get("_act_parts", [])
-            buf["_grad_parts"] = s.get("_grad_parts", [])
-            buf["_proj_parts"] = s.get("_proj_parts", [])
-            buf["_pending"] = s.get("_pending", {})
-            buf["_fwd_fires"] = s.get("_fwd_fires", 0)
-            buf["_pair_pos"] = s.get("_pair_pos", [])
-            buf["activation"] = s.get("activation")
-            buf["grad_output"] = s.get("grad_output")
-        for name, buf in self._param_buffers.items():
-            buf.clear()
-            buf.update(state["param_buffers"].get(name, {}))
-        self._last_inputs = state["last_inputs"]
+        """Return to a :meth:`save_state` snapshot."""
+        for name, buf in self._layers.items():
+            buf.restore(state["layers"].get(name))
+        for name, grads in self._params.items():
+            grads.clear()
+            grads.update(state["params"].get(name, {}))
+        self._inputs = state["inputs"]
         self._last_gradient = state["last_gradient"]
-        self._next_ids = state.get("next_ids")
-        with self._step_lock:
-            self._step_count = state["step_count"]
-            self._seen_bwd = state["seen_bwd"]
-            self._active = state.get("active_layers", set())
-            self._bwd_counts = state["bwd_replica_counts"]
-            self._mlp_hook_count = state["mlp_param_hook_count"]
-            self._param_hook_count = state["param_hook_count"]
-            self._bwd_done = state["bwd_done"]
-            self._grad_done = state["grad_done"]
-            self._mlp_ready = state["mlp_params_ready"]
-            self._end_scheduled = state["backward_end_scheduled"]
-            self._saw_recompute = state.get("saw_recompute", False)
-            self._outer_task = state.get("outer_task_id", -1)
+        self._pending_ids = state["pending_ids"]
+        with self._lock:
+            self._steps = state["step"]
+            self._barrier = state["barrier"].copy()
 
     # ------------------------------------------------------------------ lifecycle
     @contextmanager
     def collect(self, deregister_on_exit: bool = False) -> Generator[HookManager, None, None]:
         """Capture every backward inside the block; callbacks' ``on_context_end`` runs at exit."""
         self.register()
-        self._reset_layer_buffers()
-        self._reset_param_buffers()
+        self._clear_captures()
+        with self._lock:
+            self._barrier = self._barrier.fresh(self._has_linear_io, self._has_param_grad)
         self._last_gradient = None
-        self._param_hook_count = 0
-        self._mlp_ready = False
-        self._end_scheduled = False
-        self._seen_bwd.clear()
-        self._bwd_counts.clear()
-        self._orphaned.clear()
-        self._last_inputs = {}
+        self._inputs = {}
         self._collecting = True
         try:
             yield self
@@ -697,162 +602,145 @@ class HookManager:
             for cb in self._callbacks:
                 cb.on_context_end()
             if deregister_on_exit:
-                last = self._last_gradient
+                kept = self._last_gradient
                 self.remove()
-                self._last_gradient = last
+                self._last_gradient = kept
 
-    def register(self) -> None:
-        """Install every hook and override (idempotent)."""
-        if self._registered:
-            return
-        model = self._model
-        root = getattr(model, "module", model)
-        self._fwd_handle = root.register_forward_pre_hook(self._capture_model_input, with_kwargs=True)
-        self._out_handle = root.register_forward_hook(self._capture_model_output)
-        assignment = resolve_hook_assignments(root, self._config)
-        type_overrides = dict(self._config.layer_types or {})
-        if self._moe_declared:
-            self._routed = RoutedTokenTracker(root, self._moe_declared)
+    def _install_overrides(self, root: nn.Module, assignment: dict, layer_types: dict) -> None:
+        """Forward overrides: fused-expert stand-ins for declared MoE blocks (their proxies
+        replace the blocks in the assignment) and module-by-module sequence mixers."""
+        if self._moe_blocks:
+            self._routed = RoutedTokenTracker(root, self._moe_blocks)
             fused = [n for n in find_fused_experts(root) if self._routed.covers(n)]
             if fused:
-                proxy_types, reverts = install_fused_experts(root, fused, lambda: self._collecting)
-                self._override_reverts.extend(reverts)
-                type_overrides.update(proxy_types)
-                for proxy in proxy_types:
-                    depth = 3 if ".dattri_experts." in proxy else 1
-                    assignment.pop(proxy.rsplit(".", depth)[0], None)
+                proxies, reverts = install_fused_experts(root, fused, lambda: self._collecting)
+                self._reverts.extend(reverts)
+                layer_types.update(proxies)
+                for proxy in proxies:
+                    owner = proxy.rsplit(".", 3 if ".dattri_experts." in proxy else 1)[0]
+                    assignment.pop(owner, None)
                     assignment[proxy] = LINEAR_IO
         mixers = find_sequence_mixers(root)
         if mixers:
-            self._override_reverts.extend(
-                install_sequence_mixer_forward(root, list(mixers), lambda: self._collecting))
-        lin = {n for n, t in assignment.items() if t == LINEAR_IO}
-        pgrad = {n for n, t in assignment.items() if t == PARAM_GRAD}
-        inv = {n for n, t in assignment.items() if t == INVASIVE_LINEAR_IO}
-        capture = lin | inv
-        self._has_linear_io = bool(capture)
-        self._has_param_grad = bool(pgrad)
-        self._bwd_done = True
-        self._n_mlp_params = 0
-        self._n_layers = 0
+            self._reverts.extend(install_sequence_mixer_forward(root, list(mixers), lambda: self._collecting))
+
+    def register(self) -> None:
+        """Install every hook and override (idempotent)."""
+        if self._installed:
+            return
+        model = self._model
+        root = getattr(model, "module", model)
+        self._model_hooks = [root.register_forward_pre_hook(self._on_model_inputs, with_kwargs=True),
+                             root.register_forward_hook(self._on_model_output)]
+        assignment = resolve_hook_assignments(root, self._config)
+        layer_types = dict(self._config.layer_types or {})
+        self._install_overrides(root, assignment, layer_types)
+        plain = {n for n, kind in assignment.items() if kind == LINEAR_IO}
+        invasive = {n for n, kind in assignment.items() if kind == INVASIVE_LINEAR_IO}
+        per_batch = {n for n, kind in assignment.items() if kind == PARAM_GRAD}
+        captured = plain | invasive
+        self._has_linear_io, self._has_param_grad = bool(captured), bool(per_batch)
         if self._preconditioner is not None:
-            self._validate_preconditioning(pgrad)
-        if self._has_linear_io:
-            self._bwd_done = False
+            self._check_preconditionable(per_batch)
+        self._n_weights = 0
+        if captured:
             if self._config.projection_kwargs is not None and self._projector is None:
                 self._projector = ops.DattriProjector(self._config.projector)
             if self._preconditioner is not None:
                 self._preconditioner.projector = self._projector
-            self._buffers, self._handles = register_linear_io_hooks(
-                model, layer_names=capture, on_layer_forward=self._dispatch_layer_forward,
-                on_layer_backward=self._check_step_bwd_complete, type_overrides=type_overrides,
-                kwargs_overrides=self._config.module_kwargs,
-                projection_kwargs=self._config.projection_kwargs,
-                capture_style=self._config.capture_style, projector=self._projector,
-                offload_to_cpu=self._offload, preconditioner=self._preconditioner,
-                include_frozen=self._config.include_frozen, routed=self._routed,
-                step_share=self._share)
-            self._n_layers = len(self._buffers)
-            self._warn_frozen(root, capture)
-            self._n_mlp_params, self._mlp_handles = register_linear_param_hooks(
-                model, layer_names=lin, on_linear_param_grad=self._check_step_mlp_param_complete)
-            if inv:
-                self._invasive_reverts = install_invasive_forward(model, inv, lambda: self._collecting)
-        self._grad_done = True
-        self._n_params_hooked = 0
-        if self._has_param_grad:
-            self._grad_done = False
-            self._param_buffers, self._param_handles = register_param_grad_hooks(
-                model, layer_names=pgrad, on_param_grad=self._check_step_grad_complete,
-                offload_to_cpu=self._offload)
-            self._n_params_hooked = len(self._param_handles)
-        if self._config.layer_types:
-            unused = sorted(set(self._config.layer_types) - set(self._buffers) - set(self._param_buffers))
-            if unused:
-                warnings.warn(f"HookManagerConfig.layer_types designated a type for layers that were "
-                              f"not hooked: {unused}. These overrides had no effect.", stacklevel=2)
-        if self._non_batch_first:
-            unused = sorted(self._non_batch_first - set(self._buffers))
-            if unused:
-                warnings.warn("non_batch_first_layers names layers not hooked with factorized "
-                              f"(linear_io) capture; the flag had no effect: {unused}.", stacklevel=2)
+            self._layers, self._layer_hooks = register_linear_io_hooks(
+                model, layer_names=captured, on_layer_forward=self._on_layer_forward,
+                on_layer_backward=self._on_layer_backward, type_overrides=layer_types,
+                kwargs_overrides=self._config.module_kwargs, projection_kwargs=self._config.projection_kwargs,
+                capture_style=self._config.capture_style, projector=self._projector, offload_to_cpu=self._offload,
+                preconditioner=self._preconditioner, include_frozen=self._config.include_frozen,
+                routed=self._routed, step_share=self._share)
+            self._warn_frozen(root, captured)
+            self._n_weights, self._weight_hooks = register_linear_param_hooks(
+                model, layer_names=plain, on_linear_param_grad=self._on_weight_grad_final)
+            if invasive:
+                self._reverts.extend(install_invasive_forward(model, invasive, lambda: self._collecting))
+        self._n_param_hooks = 0
+        if per_batch:
+            self._params, self._param_hooks = register_param_grad_hooks(
+                model, layer_names=per_batch, on_param_grad=self._on_param_grad, offload_to_cpu=self._offload)
+            self._n_param_hooks = len(self._param_hooks)
+        self._barrier = self._barrier.fresh(self._has_linear_io, self._has_param_grad)
+        self._warn_unused_options(layer_types)
+        self._installed = True
+
+    def _warn_unused_options(self, layer_types: dict) -> None:
+        hooked = set(self._layers) | set(self._params)
+        unused = sorted(set(self._config.layer_types or {}) - hooked)
+        if unused:
+            warnings.warn(f"HookManagerConfig.layer_types names layers that are not hooked ({unused}); those type "
+                          "overrides do nothing.", stacklevel=3)
+        unused = sorted(self._non_batch_first - set(self._layers))
+        if unused:
+            warnings.warn(f"non_batch_first_layers names layers without factorized (linear_io) capture ({unused}); "
+                          "the flag does nothing for them.", stacklevel=3)
         if self._routed is not None:
-            self._routed.bind(self._buffers)
-            unused = sorted(d for d in self._moe_declared
-                            if not any(n == d or n.startswith(d + ".") for n in self._routed.layers))
+            self._routed.bind(self._layers)
+            unused = sorted(blk for blk in self._moe_blocks
+                            if not any(n == blk or n.startswith(blk + ".") for n in self._routed.layers))
             if unused:
-                warnings.warn("moe_routed_layers names modules with no layer hooked with factorized "
-                              f"(linear_io) capture; the flag had no effect: {unused}.", stacklevel=2)
-        self._registered = True
+                warnings.warn(f"moe_routed_layers names modules with no factorized (linear_io) capture inside "
+                              f"({unused}); the flag does nothing for them.", stacklevel=3)
 
     def remove(self) -> None:
         """Remove every hook and override (idempotent)."""
-        if not self._registered:
+        if not self._installed:
             return
-        self._fwd_handle.remove()
-        self._fwd_handle = None
-        if self._out_handle is not None:
-            self._out_handle.remove()
-            self._out_handle = None
-        remove_hooks(self._handles)
-        for revert in self._override_reverts:
+        remove_hooks(self._model_hooks)
+        remove_hooks(self._layer_hooks)
+        remove_hooks(self._weight_hooks)
+        remove_hooks(self._param_hooks)
+        for revert in self._reverts:
             revert()
-        self._override_reverts = []
+        self._reverts = []
         if self._routed is not None:
             self._routed.remove()
             self._routed = None
-        for revert in self._invasive_reverts:
-            revert()
-        self._invasive_reverts = []
-        self._buffers.clear()
-        remove_hooks(self._mlp_handles)
-        remove_hooks(self._param_handles)
-        self._param_buffers.clear()
+        self._layers.clear()
+        self._params.clear()
         self._last_gradient = None
         self._share.clear()
         if self._projector is not None:
             self._projector.close()
             self._projector = None
-        self._registered = False
+        self._installed = False
 
     def _warn_frozen(self, root: nn.Module, candidates: set[str]) -> None:
         modules = dict(root.named_modules())
 
-        def frozen(n):
-            m = modules.get(n)
+        def frozen(name):
+            m = modules.get(name)
             return m is not None and not has_trainable_params(m)
 
         if self._config.include_frozen:
-            names = sorted(n for n in self._buffers if frozen(n))
+            names = sorted(n for n in self._layers if frozen(n))
             if names:
                 warnings.warn(
-                    f"{len(names)} hooked layer(s) have no trainable parameter (include_frozen=True), "
-                    f"e.g. {names[:3]}. They receive a gradient only through something upstream that "
-                    "requires grad (typically the input embedding); a step in which no hooked layer "
-                    "receives one cannot complete and raises at the end of that backward -- under "
-                    "DDP/FSDP the other ranks may then wait in their collectives.",
-                    stacklevel=3,
-                )
-        elif not self._buffers:
+                    f"{len(names)} hooked layer(s) have no trainable parameter (include_frozen=True), e.g. "
+                    f"{names[:3]}. Such a layer gets a gradient only through something upstream that requires "
+                    "grad (typically the input embedding); a step in which no hooked layer gets one cannot be "
+                    "completed and raises at the end of its backward -- under DDP/FSDP the other ranks may then "
+                    "wait in their collectives.", stacklevel=3)
+        elif not self._layers:
             skipped = sorted(n for n in candidates if frozen(n))
             if skipped:
-                warnings.warn(
-                    f"No layer hooked: the {len(skipped)} linear-IO candidate(s) (e.g. {skipped[:3]}) "
-                    "have no trainable parameter and include_frozen is False. Pass "
-                    "HookManagerConfig(include_frozen=True) to capture frozen layers.",
-                    stacklevel=3,
-                )
+                warnings.warn(f"no layer is hooked: the {len(skipped)} linear-IO candidate(s) (e.g. {skipped[:3]}) "
+                              "have no trainable parameter and include_frozen is False; pass "
+                              "HookManagerConfig(include_frozen=True) to capture frozen layers.", stacklevel=3)
 
-    def _validate_preconditioning(self, param_grad_layers: set[str]) -> None:
-        if param_grad_layers:
-            raise ValueError("HookManager(optimizer=...) preconditions per-sample (linear_io) captures; "
-                             f"these layers are assigned param_grad: {sorted(param_grad_layers)[:5]}.")
+    def _check_preconditionable(self, per_batch_layers: set[str]) -> None:
+        if per_batch_layers:
+            raise ValueError("HookManager(optimizer=...) preconditions per-sample (linear_io) captures, but these "
+                             f"layers are assigned param_grad: {sorted(per_batch_layers)[:5]}.")
         for name, kw in (self._config.projection_kwargs or {}).items():
             if kw.get("style", "logra") == "logra":
-                raise ValueError(
-                    f"projection_kwargs[{name!r}] uses style 'logra', which cannot be preconditioned: "
-                    "the optimizer map needs exact gradient entries. Use no projection, 'mask', or 'dense'.",
-                )
+                raise ValueError(f"projection_kwargs[{name!r}] uses the 'logra' style, whose factors cannot go "
+                                 "through the optimizer's per-coordinate map; use no projection, 'mask' or 'dense'.")
 
     # ------------------------------------------------------------------ properties
     @property
@@ -869,8 +757,8 @@ class HookManager:
     def precondition(self, enabled: bool) -> None:
         if self._preconditioner is None:
             if enabled:
-                raise ValueError("This HookManager has no optimizer; pass optimizer= at construction "
-                                 "to precondition captures.")
+                raise ValueError("this HookManager was built without an optimizer; pass optimizer= at "
+                                 "construction to precondition captures.")
             return
         self._preconditioner.enabled = bool(enabled)
 
@@ -913,27 +801,27 @@ class HookManager:
     @property
     def layer_names(self) -> list[str]:
         """Layers hooked with linear-IO capture."""
-        return list(self._buffers)
+        return list(self._layers)
 
     @property
     def layer_name(self) -> list[str]:
         """Alias of :attr:`layer_names`."""
-        return list(self._buffers)
+        return list(self._layers)
 
     @property
     def param_layer_names(self) -> list[str]:
         """Layers hooked with param_grad capture."""
-        return list(self._param_buffers)
+        return list(self._params)
 
     @property
     def steps_collected(self) -> int:
         """Completed steps so far."""
-        return self._step_count
+        return self._steps
 
     def reset_steps(self, to: int = 0) -> None:
         """Restart the step counter at *to*."""
-        with self._step_lock:
-            self._step_count = to
+        with self._lock:
+            self._steps = to
 
     def get_gradient(self) -> Gradient:
         """The last completed step's gradient.
@@ -942,6 +830,6 @@ class HookManager:
             RuntimeError: before any step completed.
         """
         if self._last_gradient is None:
-            raise RuntimeError("No gradient available: no step has completed yet. Ensure backward() "
-                               "was called inside the collect() context before calling get_gradient().")
+            raise RuntimeError("no step has completed yet: call get_gradient() after a backward() run inside "
+                               "collect().")
         return self._last_gradient
