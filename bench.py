@@ -10,7 +10,7 @@ every train sample against 1,024 test samples, with a running per-test top-100.
 
 Usage (one process per GPU; N > 1 under torchrun)::
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--config 2|3]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--config 2|3|4]
 
 ``--config 3`` (not the default) is BASELINE config 3: a Llama-3-8B-architecture decoder
 (32 layers, d 4096, FFN 14336), bf16, FSDP FULL_SHARD over the N GPUs, sequence length 2048,
@@ -19,6 +19,16 @@ public ``EKFACAttributor.attribute(train, test, gradient_cache_residency="disk")
 capture with covariances, the fit (eigendecompositions and the eigenvalue sweep), the query
 side and the scoring -- over K micro-batches per GPU after one untimed call over W, as the
 reference's own FSDP benchmark does; the query set is 2 sequences (the same in both arms).
+
+``--config 4`` is BASELINE config 4: Hugging Face's OLMoE architecture (16 layers, d 2048,
+64 experts top-8, expert FFN 1024, vocab 50304), bf16, sequence length 2048, micro-batch 1 per
+GPU.  Capture: every expert's gate/up and down projection and every router, declared in
+``moe_routed_layers`` (per-sample regrouping of the routed rows), LoGra-projected to 16 x 16,
+``capture_style="auto"``; TracIn scores against 4 queries through the public streamer and
+``score_sources`` in both arms.  With N > 1 this framework runs the MoE blocks expert-parallel
+(``expert_parallelize``); the reference has no expert parallelism and keeps every expert on
+every rank.  K train steps are timed after W, inside one scoring loop, as in config 2's
+reference arm.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a device
 synchronize, timed with CUDA events on the compute stream; the reported time is the
@@ -615,6 +625,111 @@ def run_c3_reference(rank, world, local, steps, warmup):
     return ms, clk, host
 
 
+# --------------------------------------------------------------------------- config 4
+C4_SEQ, C4_MB, C4_NTEST, C4_PROJ = 2048, 1, 4, 16
+
+
+class _DS4(torch.utils.data.Dataset):
+    """Config-4 synthetic sequences (uniform token ids, length 2048), deterministic."""
+
+    def __init__(self, n: int, vocab: int, seed: int) -> None:
+        g = torch.Generator().manual_seed(seed)
+        self.ids = torch.randint(0, vocab, (n, C4_SEQ), generator=g)
+
+    def __len__(self):
+        return self.ids.shape[0]
+
+    def __getitem__(self, i):
+        return {"input_ids": self.ids[i]}
+
+
+def _olmoe(dev):
+    """Hugging Face OLMoE-1B-7B architecture, random init on the device, frozen-probe recipe."""
+    from transformers import OlmoeConfig, OlmoeForCausalLM
+
+    cfg = OlmoeConfig(vocab_size=50304, hidden_size=2048, intermediate_size=1024, num_hidden_layers=16,
+                      num_attention_heads=16, num_key_value_heads=16, num_experts=64, num_experts_per_tok=8,
+                      max_position_embeddings=4096, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = OlmoeForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    model.requires_grad_(False)
+    model.get_input_embeddings().requires_grad_(True)
+    return model, cfg
+
+
+def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=None):
+    """One public scoring loop: K steps timed with CUDA events (max over ranks)."""
+    blocks = [f"model.layers.{i}.mlp" for i in range(16)]
+    proj = {"__default__": {"style": "logra", "proj_dim": C4_PROJ, "proj_type": "rademacher", "proj_seed": 0}}
+    kw = {"projector": projector} if projector is not None else {}
+    hc = lib.HookManagerConfig(linear_io=[r"\.mlp\.(experts|gate)$"], projection_kwargs=proj, capture_style="auto",
+                               include_frozen=True, **kw)
+    cap = lib.CaptureCallback()
+    hm = lib.HookManager(model, hc, callbacks=[cap], moe_routed_layers=blocks)
+    args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C4_MB,
+                                    per_device_eval_batch_size=C4_MB, dataloader_pin_memory=True)
+    att = lib.TracInAttributor(args, task=lib.AttributionTask(_token_sum_loss, model))
+    n = (warmup + steps + 1) * C4_MB
+    train = lib.GradientStreamer(model, _DS4(n * world, vocab, seed=2), args, batch_size=C4_MB,
+                                 loss_fn=_token_sum_loss, hook_manager=hm, forward_model=model)
+    test = att.generate_test_rep(_DS4(C4_NTEST, vocab, seed=1), hook_manager=hm, forward_model=model, shard=False)
+    timed = _TimedBlocks(train, warmup, steps)
+    clocks = ClockSampler(local)
+    clocks.start()
+    with train, test:
+        att.score_sources(timed, test)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(timed.ev0.elapsed_time(timed.ev1), world) / steps
+    host = _max_over_ranks(timed.t1 - timed.t0, world)
+    return ms, clk, host
+
+
+def main_c4(a, rank, world, local):
+    dev = torch.device("cuda", local)
+    cfg_json = {"model": "OLMoE-1B-7B-arch (random init, Hugging Face modeling)", "global_batch": C4_MB * world,
+                "micro_batch_per_gpu": C4_MB, "seq_len": C4_SEQ, "n_test": C4_NTEST,
+                "capture": f"expert gate_up/down + routers, moe_routed_layers, logra {C4_PROJ}x{C4_PROJ}, auto",
+                "l2": "per-step expert weights (13 GB bf16) exceed the 126 MB L2"}
+    out = {"metric": "train samples attributed/sec (TracIn over routed-expert captures, device-timed)",
+           "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak",
+           "dtype": "bf16", "data": "synthetic uniform token ids, random-init weights", "config": cfg_json}
+    if a.impl == "ours":
+        sys.path.insert(0, HERE)
+        import dattri_llm_b200 as bw
+        from dattri_llm_b200 import ops as native_ops
+
+        native_ops.native()
+        model, cfg = _olmoe(dev)
+        cfg_json["parallelism"] = f"ep{world}" if world > 1 else "single"
+        if world > 1:
+            from dattri_llm_b200.parallel.moe import expert_parallelize
+
+            expert_parallelize(model, max_tokens=C4_MB * C4_SEQ)
+        n0 = native_ops.launch_count()
+        ms, clk, host = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        extra = {"gpu_launches": native_ops.launch_count() - n0}
+    else:
+        ref = os.path.join(HERE, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref, "dattri_llm")):
+            raise SystemExit("bench.py --impl reference: the reference is not installed under baseline/_ref")
+        sys.path.insert(0, ref)
+        import dattri_llm as R  # noqa: N812
+
+        model, cfg = _olmoe(dev)
+        cfg_json["parallelism"] = f"replicated-experts{world}" if world > 1 else "single"
+        ms, clk, host = _c4_score(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
+                                  projector=counter_projector_factory())
+        extra = {"impl": "reference"}
+    value = C4_MB * world / (ms / 1e3)
+    out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms, "vs_baseline": None, "clocks": clk,
+                "e2e": {"value": C4_MB * world * a.steps / host, "unit": "train samples/s (host clock)",
+                        "h2d_bytes_per_step": C4_MB * C4_SEQ * 8, "d2h_bytes_per_step": 0}, **extra})
+    return out
+
+
 def main_c3(a, rank, world, local):
     cfg_json = {"model": "Llama-3-8B-arch (random init)", "global_batch": C3_MB * world, "micro_batch_per_gpu": C3_MB,
                 "seq_len": C3_SEQ, "parallelism": f"fsdp{world}" if world > 1 else "single",
@@ -644,14 +759,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 3], default=2)
+    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2)
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
     rank, world, local = _init_dist()
-    if a.config == 3:
+    if a.config in (3, 4):
         try:
-            out = main_c3(a, rank, world, local)
+            out = (main_c3 if a.config == 3 else main_c4)(a, rank, world, local)
         finally:
             if world > 1:
                 import torch.distributed as dist
