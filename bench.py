@@ -678,7 +678,7 @@ def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=No
     timed = _TimedBlocks(train, warmup, steps)
     clocks = ClockSampler(local)
     clocks.start()
-    with train, test:
+    with hm.collect(), train, test:
         att.score_sources(timed, test)
     clk = clocks.stop()
     torch.cuda.synchronize()

@@ -137,7 +137,7 @@ def test_sample_hashes_come_from_host_copies(monkeypatch):
                                    config=bw.HookManagerConfig(linear_io=[r"^inner\.mlp\.fc[12]$"]))
     with streamer:
         got = [hashes for _, _, hashes in streamer]
-    assert streamer._host_ids_ok is False  # the host batch's hash is not the model inputs' hash
+    assert streamer.host_hash_trusted is False  # the host batch's hash is not the model inputs' hash
     assert len(seen) == len(moved), "every step is hashed by the manager"
     host_ids = {id(t) for host, _ in moved for t in host.values()}
     for inputs in seen:
