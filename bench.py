@@ -669,7 +669,7 @@ def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=No
     cap = lib.CaptureCallback()
     hm = lib.HookManager(model, hc, callbacks=[cap], moe_routed_layers=blocks)
     args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C4_MB,
-                                    per_device_eval_batch_size=C4_MB, dataloader_pin_memory=True)
+                                    per_device_eval_batch_size=C4_NTEST, dataloader_pin_memory=True)
     att = lib.TracInAttributor(args, task=lib.AttributionTask(_token_sum_loss, model))
     n = (warmup + steps + 1) * C4_MB
     train = lib.GradientStreamer(model, _DS4(n * world, vocab, seed=2), args, batch_size=C4_MB,

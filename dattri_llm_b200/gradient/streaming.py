@@ -116,24 +116,42 @@ class DiskGradientSource(GradientSource):
 
 
 class _MergedBlocks:
-    """Dense blocks being concatenated along the sample axis."""
+    """Dense blocks being concatenated along the sample axis.  A sample-indexed layer that
+    some blocks lack (a routed expert that none of their tokens reached) gets zero rows for
+    them: its gradient for those samples is zero."""
 
     def __init__(self) -> None:
         self.parts: dict[str, list[torch.Tensor]] = {}
+        self.kinds: dict[str, tuple] = {}  # layer -> (representation, layer type, indexing)
         self.ids: list[str] = []
         self.steps: list[int] = []
-        self.layout = None
+
+    def fits(self, block) -> bool:
+        """Whether *block* can join: every layer only one side has is sample-indexed."""
+        for name in set(block.data) ^ set(self.parts):
+            indexing = block.indexing[name] if name in block.data else self.kinds[name][2]
+            if indexing != "batch":
+                return False
+        return True
 
     def add(self, step: int, block, hashes) -> None:
-        self.layout = (block.representation, block.layer_types, block.indexing)
+        before, n = len(self.ids), block.batch_size
         for name, t in block.data.items():
-            self.parts.setdefault(name, []).append(t)
+            if name not in self.parts:
+                self.parts[name] = [t.new_zeros((before, *t.shape[1:]))] if before else []
+                self.kinds[name] = (block.representation[name], block.layer_types[name], block.indexing[name])
+            self.parts[name].append(t)
+        for name, ts in self.parts.items():
+            if name not in block.data:
+                ts.append(ts[-1].new_zeros((n, *ts[-1].shape[1:])))
         self.ids.extend(hashes)
-        self.steps.extend([step] * block.batch_size)
+        self.steps.extend([step] * n)
 
     def take(self):
         data = {n: ts[0] if len(ts) == 1 else torch.cat(ts) for n, ts in self.parts.items()}
-        rep, types, idx = self.layout
+        rep = {n: k[0] for n, k in self.kinds.items()}
+        types = {n: k[1] for n, k in self.kinds.items()}
+        idx = {n: k[2] for n, k in self.kinds.items()}
         merged = (self.steps, Gradient(rep, data, types, idx, validate_on_init=False), self.ids)
         self.__init__()
         return merged
@@ -152,6 +170,8 @@ def rebatch_blocks(source: Iterable[StreamBatch], batch_size: int):
                 yield pending.take()
             yield [step] * block.batch_size, block, list(hashes)
             continue
+        if not pending.fits(block):
+            yield pending.take()
         pending.add(step, block, hashes)
         if len(pending.ids) >= batch_size:
             yield pending.take()

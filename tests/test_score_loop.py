@@ -93,3 +93,18 @@ def test_rebatch_concatenates_dense_and_passes_factorized_through():
     assert out[1][1] is fac
     with pytest.raises(ValueError):
         list(rebatch_blocks(src, batch_size=0))
+
+
+def test_rebatch_zero_fills_a_layer_some_blocks_lack():
+    """A routed expert no token of a block reached is absent from that block: its rows are zero."""
+    d1, d2 = _dense_block(2, 1), _dense_block(1, 2)
+    extra = torch.randn(1, 6)
+    d2 = Gradient({**d2.representation, "e": "materialized"}, {**d2.data, "e": extra},
+                  {**d2.layer_types, "e": "nn.Linear"}, {**d2.indexing, "e": "batch"})
+    d3 = _dense_block(2, 3)
+    (steps, merged, ids), = list(rebatch_blocks([(0, d1, ["a", "b"]), (1, d2, ["c"]), (2, d3, ["d", "e"])],
+                                                batch_size=5))
+    assert ids == ["a", "b", "c", "d", "e"] and steps == [0, 0, 1, 2, 2]
+    want = torch.cat([torch.zeros(2, 6), extra, torch.zeros(2, 6)])
+    torch.testing.assert_close(merged.data["e"], want)
+    assert merged.data["u"].shape[0] == 5
