@@ -49,6 +49,7 @@ from dattri_llm_b200.gradient.hooks.config import (
 )
 from dattri_llm_b200.gradient.hooks.hooks import (
     LayerBuffer,
+    _projection_matrix,
     _StepShare,
     has_trainable_params,
     register_linear_io_hooks,
@@ -63,6 +64,9 @@ from dattri_llm_b200.gradient.hooks.override_layers import (
     install_invasive_forward,
     install_sequence_mixer_forward,
 )
+from dattri_llm_b200.gradient.callbacks.base import HookManagerCallback
+from dattri_llm_b200.gradient.hooks.override_layers.fused_experts import PROXY_EXPERTS
+from dattri_llm_b200.gradient.hooks.override_layers.grouped_experts import GroupedExpertCapture
 from dattri_llm_b200.gradient.hooks.routing import RoutedTokenTracker
 from dattri_llm_b200.gradient.ops import PARAM_GRAD_TYPES, is_embedding
 from dattri_llm_b200.utils.autograd import queue_backward_end_callback
@@ -187,6 +191,7 @@ class HookManager:
         self._routed: RoutedTokenTracker | None = None
         self._projector: ops.DattriProjector | None = None
         self._share = _StepShare()
+        self._group_forwards: dict[str, int] = {}  # grouped expert blocks: forwards of this step
         # step state
         self._lock = threading.Lock()
         self._barrier = _StepBarrier()
@@ -363,6 +368,13 @@ class HookManager:
                     b.unreached.add(name)
             elif b.fires.get(name, 0) >= matched:
                 b.finished.add(name)
+        for key, forwards in self._group_forwards.items():
+            fired = b.fires.get(key, 0)
+            if key in b.ran and fired < forwards:
+                if fired:
+                    b.finished.add(key)
+                else:  # its forward's graph was never backpropagated (recomputation's first pass)
+                    b.ran.discard(key)
 
     def _layers_finished(self) -> bool:
         b = self._barrier
@@ -543,6 +555,7 @@ class HookManager:
 
     def _clear_captures(self) -> None:
         self._share.clear()
+        self._group_forwards.clear()
         if self._routed is not None:
             self._routed.reset()
         for buf in self._layers.values():
@@ -551,18 +564,91 @@ class HookManager:
             for pname in grads:
                 grads[pname] = None
 
+    # ------------------------------------------------------------------ grouped expert blocks
+    def routed_shape(self, x: torch.Tensor) -> tuple[int, int] | None:
+        """``(batch, tokens)`` of a declared MoE block whose flattened input is *x*."""
+        return None if self._routed is None else self._routed.identity_shape(x)
+
+    def _watched_per_layer(self) -> bool:
+        """Whether a callback looks at individual layers' activations or gradients."""
+        base = (HookManagerCallback.on_layer_forward, HookManagerCallback.on_layer_backward)
+        return any(getattr(type(cb), hook.__name__, hook) is not hook for cb in self._callbacks for hook in base)
+
+    def grouped_matrices(self, block: GroupedExpertCapture, x: torch.Tensor, tokens: int) -> dict | None:
+        """The projections of a grouped expert block (``up_a``, ``up_g``, ``down_a``,
+        ``down_g``) when its captures allow the grouped path, else ``None``: every expert
+        projection hooked with one LoGra projection and materialized at *tokens* tokens, no
+        preconditioning or offload, no per-layer callback, not inside a backward."""
+        if not self._collecting or self._offload or _backward_task() != -1 or self._watched_per_layer():
+            return None
+        if self._preconditioner is not None and self._preconditioner.enabled:
+            return None
+        sides = []
+        for names in (block.up_names, block.down_names):
+            bufs = [self._layers.get(n) for n in names]
+            first = bufs[0]
+            if first is None or first.proj_kw is None or first.proj_kw.get("style", "logra") != "logra":
+                return None
+            if any(b is None or b.proj_kw != first.proj_kw or b.capture_style != first.capture_style
+                   or b.forwards or b.acts or b.waiting for b in bufs):
+                return None
+            sides.append(first)
+        up, down = sides
+        experts = block.experts
+        widths = {"up_a": (up, "a", x.shape[1]), "up_g": (up, "g", experts.gate_up_proj.shape[1]),
+                  "down_a": (down, "a", experts.down_proj.shape[2]), "down_g": (down, "g", x.shape[1])}
+        out = {}
+        for key, (buf, side, width) in widths.items():
+            pm = _projection_matrix(buf, side, x.new_empty(1, width), self._projector)
+            if pm.bias_row is not None or (x.is_cuda and pm.matrix_t is None):
+                return None
+            out[key] = pm
+        for a_key, g_key, buf in (("up_a", "up_g", up), ("down_a", "down_g", down)):
+            if not ops.should_materialize(buf.capture_style, tokens, out[a_key].proj_dim, out[g_key].proj_dim):
+                return None
+        return out
+
+    def grouped_forward(self, block: GroupedExpertCapture) -> None:
+        """A grouped block ran forward: the step waits for its backward."""
+        key = f"{block.name}#grouped"
+        with self._lock:
+            self._barrier.ran.add(key)
+            self._group_forwards[key] = self._group_forwards.get(key, 0) + 1
+
+    def grouped_backward(self, block: GroupedExpertCapture, parts: dict, device: torch.device) -> None:
+        """A grouped block's backward delivered ``{expert projection name: (B, k_g * k_a)}``."""
+        dev = device.index if device.type == "cuda" else 0
+        key = f"{block.name}#grouped"
+        with self._lock:
+            b = self._barrier
+            invocation = b.fires.get(key, 0)
+            forwards = self._group_forwards.get(key, 0)
+            position = max(forwards - 1 - invocation, 0)  # backwards run in reverse forward order
+            for name, mat in parts.items():
+                buf = self._layers[name]
+                with buf.lock:
+                    buf.dense.append((dev, mat))
+                    buf.pairs.append((dev, position))
+                    buf.forwards += 1
+            b.fires[key] = invocation + 1
+            if b.fires[key] >= forwards:
+                b.finished.add(key)
+            record = self._close_linear_side()
+        if record is not None:
+            self._emit(record)
+
     # ------------------------------------------------------------------ secondary passes
     def save_state(self) -> dict:
         """Snapshot of the step in flight, for a secondary forward/backward through the same
         hooks (restore it with :meth:`load_state`): ``{"layers", "params", "inputs", "step",
-        "last_gradient", "barrier", "pending_ids"}``."""
+        "last_gradient", "barrier", "pending_ids", "groups"}``."""
         self._flush_deferred()
         with self._lock:
             barrier = self._barrier.copy()
         return {"layers": {n: b.snapshot() for n, b in self._layers.items()},
                 "params": {n: dict(g) for n, g in self._params.items()}, "inputs": dict(self._inputs),
                 "step": self._steps, "last_gradient": self._last_gradient, "barrier": barrier,
-                "pending_ids": self._pending_ids}
+                "pending_ids": self._pending_ids, "groups": dict(self._group_forwards)}
 
     def clear_state(self) -> None:
         """Empty the layer and parameter buffers (the step counter is kept)."""
@@ -580,6 +666,7 @@ class HookManager:
         self._inputs = state["inputs"]
         self._last_gradient = state["last_gradient"]
         self._pending_ids = state["pending_ids"]
+        self._group_forwards = dict(state.get("groups", {}))
         with self._lock:
             self._steps = state["step"]
             self._barrier = state["barrier"].copy()
@@ -613,7 +700,9 @@ class HookManager:
             self._routed = RoutedTokenTracker(root, self._moe_blocks)
             fused = [n for n in find_fused_experts(root) if self._routed.covers(n)]
             if fused:
-                proxies, reverts = install_fused_experts(root, fused, lambda: self._collecting)
+                proxies, reverts = install_fused_experts(
+                    root, fused, lambda: self._collecting,
+                    grouped=lambda name, experts: GroupedExpertCapture(self, name, experts, PROXY_EXPERTS))
                 self._reverts.extend(reverts)
                 layer_types.update(proxies)
                 for proxy in proxies:

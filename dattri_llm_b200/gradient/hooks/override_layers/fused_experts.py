@@ -167,10 +167,13 @@ def _override_router(router: nn.Module, proxy: RouterLinear, should_intervene) -
 
 
 def install_fused_experts(root: nn.Module, experts_names: list[str],
-                          should_intervene: Callable[[], bool]):
+                          should_intervene: Callable[[], bool], grouped: Callable | None = None):
     """Attach per-expert proxies and override the forwards while *should_intervene()*.
 
-    Returns ``(proxy_types, reverts)``: ``{proxy_layer_name: "nn.Linear"}`` and undo callables.
+    *grouped*: ``(experts_name, experts) -> capture`` with a ``try_forward(x, index, weights)``
+    that runs the whole block (returning ``None`` when it does not apply); the per-expert
+    loop runs otherwise.  Returns ``(proxy_types, reverts)``: ``{proxy_layer_name:
+    "nn.Linear"}`` and undo callables.
     """
     modules = dict(root.named_modules())
     types: dict[str, str] = {}
@@ -195,11 +198,16 @@ def install_fused_experts(root: nn.Module, experts_names: list[str],
             types[f"{name}.{PROXY_EXPERTS}.{e}.gate_up"] = "nn.Linear"
             types[f"{name}.{PROXY_EXPERTS}.{e}.down"] = "nn.Linear"
         original = experts.forward
+        bulk = grouped(name, experts) if grouped is not None else None
 
-        def forward(*args, _e=experts, _p=proxies, _o=original, **kwargs):
+        def forward(*args, _e=experts, _p=proxies, _o=original, _g=bulk, **kwargs):
             if not should_intervene():
                 return _o(*args, **kwargs)
             index, weights = _routing_args(args[1:], kwargs)
+            if _g is not None:
+                out = _g.try_forward(args[0], index, weights)
+                if out is not None:
+                    return out
             return _experts_loop(_e, _p, args[0], index, weights)
 
         experts.forward = forward

@@ -202,10 +202,23 @@ class RoutedTokenTracker:
             stack = self._pending.get((layer_name, dev))
             return stack.pop() if stack else None
 
+    def identity_shape(self, x: torch.Tensor) -> tuple[int, int] | None:
+        """``(batch, tokens)`` when *x* -- the 2-D input a module under a declared block just
+        received -- is that block's whole ``(B, T, d)`` input flattened, else ``None``."""
+        with self._lock:
+            layout = self._latest.get(self._dev(x))
+        if layout is None or layout.sample is not None or layout.rows != x.shape[0]:
+            return None
+        return layout.batch, layout.tokens
+
     def _match(self, x: torch.Tensor, src: _Source) -> RowLayout | None:
         n = x.shape[0]
-        if n == src.batch * src.tokens and torch.equal(x, src.flat):
-            return RowLayout(src.batch, src.tokens, n)
+        if n == src.batch * src.tokens:
+            # the block's input flattened: a view of the recorded storage needs no comparison
+            # (and no device read-back)
+            same_view = x.data_ptr() == src.flat.data_ptr() and x.stride() == src.flat.stride()
+            if same_view or torch.equal(x, src.flat):
+                return RowLayout(src.batch, src.tokens, n)
         if src.keys is None:
             k = self._fingerprint(src.flat)
             src.order = torch.argsort(k, stable=True)

@@ -16,6 +16,7 @@ from __future__ import annotations
 import torch
 
 from dattri_llm_b200.gradient.ops import dtypes
+from dattri_llm_b200.gradient.ops.norm import norm_per_sample_grad
 from dattri_llm_b200.gradient.ops.preprocess import preprocess_factors, to_3d
 from dattri_llm_b200.gradient.ops.types import is_conv_transpose, is_embedding, is_norm
 
@@ -45,28 +46,6 @@ def _outer_over_tokens(left: torch.Tensor, right: torch.Tensor) -> torch.Tensor:
     return torch.bmm(left.transpose(1, 2), right)
 
 
-def _native_norm(a, g, layer_type, module_kwargs, include_bias, per_token):
-    """LayerNorm / RMSNorm over the last axis on sm_100 bf16: one fused pass that
-    recomputes ``x_hat`` and reduces over tokens (``None`` when it does not apply)."""
-    if (per_token or module_kwargs is None or layer_type not in ("nn.LayerNorm", "nn.RMSNorm")
-            or a.dtype != torch.bfloat16 or g.dtype != torch.bfloat16 or a.shape != g.shape or a.ndim < 2):
-        return None
-    shape = tuple(module_kwargs.get("normalized_shape", (a.shape[-1],)))
-    d = a.shape[-1]
-    if len(shape) != 1 or shape[0] != d or d % 8 or d > 16384:
-        return None
-    from dattri_llm_b200 import ops as native_ops
-
-    if not native_ops.use_native(a, g):
-        return None
-    eps = module_kwargs.get("eps")
-    if eps is None:
-        eps = torch.finfo(a.dtype).eps
-    has_bias = bool(module_kwargs.get("has_bias", False)) and include_bias
-    a3, g3 = a.reshape(a.shape[0], -1, d), g.reshape(g.shape[0], -1, d)
-    return native_ops.norm_per_sample_grad(a3, g3, eps=eps, layer_norm=layer_type == "nn.LayerNorm", bias=has_bias)
-
-
 def materialize_factors(
     a: torch.Tensor,
     g: torch.Tensor,
@@ -80,9 +59,8 @@ def materialize_factors(
     Norm layers sum the token axis unless ``per_token=True`` (``(B, T*d)``).
     Embeddings need ``module_kwargs`` (the width is ``num_embeddings * E``).
     """
-    native_norm = _native_norm(a, g, layer_type, module_kwargs, include_bias, per_token)
-    if native_norm is not None:
-        return native_norm
+    if is_norm(layer_type):
+        return norm_per_sample_grad(a, g, layer_type, module_kwargs, include_bias, per_token)
     a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
     if is_embedding(layer_type):
         if module_kwargs is None:
@@ -93,9 +71,6 @@ def materialize_factors(
         return _materialize_embedding(a, g, module_kwargs["num_embeddings"])
     a, g = dtypes.align(a, g)
     a_f, g_f = to_3d(a), to_3d(g)
-    if is_norm(layer_type):
-        prod = a_f * g_f
-        return prod.flatten(1) if per_token else prod.sum(1)
     if a_f.ndim == 4:
         if is_conv_transpose(layer_type):
             return torch.einsum("btgc,btgp->bgcp", a_f, g_f).flatten(1)

@@ -1,8 +1,11 @@
-"""Model families with B200-tuned implementations: a GPT-2-style decoder and Llama
-(``models.llama``).  Every projection is an ``nn.Linear`` and every norm an
-``nn.LayerNorm`` / ``nn.RMSNorm``-shaped module, so the capture hooks see them like
-any user model."""
+"""Model families with B200-tuned implementations: a GPT-2-style decoder (``models.gpt2``)
+and Llama (``models.llama``), both built from :class:`TcLinear` projections (tcgen05 GEMMs
+with an optional fused LoGra projection tail) and ``nn.LayerNorm`` / ``nn.RMSNorm``-shaped
+norms, so the capture hooks see them like any user model."""
 
 from dattri_llm_b200.models.gpt2 import GPT2Config, GPT2LMHeadModel
+from dattri_llm_b200.models.layers import TcLinear
+from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM, LlamaModel, token_sum_loss
 
-__all__ = ["GPT2Config", "GPT2LMHeadModel"]
+__all__ = ["GPT2Config", "GPT2LMHeadModel", "LlamaConfig", "LlamaForCausalLM", "LlamaModel", "TcLinear",
+           "token_sum_loss"]
