@@ -59,13 +59,14 @@ class TracInAttributor(BaseInnerProductAttributor):
 
     @staticmethod
     def _norm(rep, layers, dense_cache) -> torch.Tensor:
-        total = torch.zeros(rep.batch_size, device=rep.device)
+        rows = rep.batch_size
+        total = torch.zeros(rows, device=rep.device)
         for name in layers:
             v = rep.data[name]
             if dense_cache is not None and name in dense_cache:
                 v = dense_cache.get(name)
             sq = ops.grad_norm_sq(v, rep.layer_types[name]).float()
-            total += sq.expand(rep.batch_size) if sq.shape[0] == 1 else sq
+            total += sq.expand(rows) if sq.shape[0] == 1 else sq
         return total.clamp_min(0).sqrt()
 
     def attribute(self, train_dataset, test_dataset, *, hook_config=None, verbose: bool = False,

@@ -141,7 +141,8 @@ class PackedDense:
         layout = cls.layout_of(block)
         if layout is None:
             return None
-        parts = [block.data[n].reshape(block.batch_size, -1) for n, _ in layout]
+        rows = block.batch_size  # a scan over every layer: once, not per layer
+        parts = [block.data[n].reshape(rows, -1) for n, _ in layout]
         dtype = dtype or parts[0].dtype
         return cls(torch.cat([p.to(dtype) for p in parts], dim=1), layout)
 

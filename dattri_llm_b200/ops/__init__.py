@@ -149,6 +149,7 @@ from dattri_llm_b200.ops.gemm import (  # noqa: E402
     gemm_tn_seg,
     matmul_f32,
     matmul_tn,
+    transpose_last2,
 )
 from dattri_llm_b200.ops.gram import (  # noqa: E402
     ghost_dot,
@@ -181,6 +182,7 @@ __all__ = [
     "ghost_gram_tokens",
     "mask_gather",
     "matmul_f32",
+    "transpose_last2",
     "matmul_tn",
     "native",
     "norm_per_sample_grad",

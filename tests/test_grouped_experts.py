@@ -22,11 +22,11 @@ transformers = pytest.importorskip("transformers")
 import dattri_llm_b200 as bw  # noqa: E402
 from dattri_llm_b200.gradient.hooks.override_layers.grouped_experts import set_grouped_experts  # noqa: E402
 
-E, LAYERS = 8, 2
+E = 8
 
 
-def _model(device, dtype):
-    cfg = transformers.OlmoeConfig(vocab_size=96, hidden_size=64, intermediate_size=32, num_hidden_layers=LAYERS,
+def _model(device, dtype, layers=2):
+    cfg = transformers.OlmoeConfig(vocab_size=96, hidden_size=64, intermediate_size=32, num_hidden_layers=layers,
                                    num_attention_heads=4, num_key_value_heads=4, num_experts=E,
                                    num_experts_per_tok=2, max_position_embeddings=64)
     torch.manual_seed(0)
@@ -43,7 +43,7 @@ def _loss(model, ids):
 
 
 def _capture(model, ids, grouped: bool, proj_dim: int = 4):
-    blocks = [f"model.layers.{i}.mlp" for i in range(LAYERS)]
+    blocks = [f"model.layers.{i}.mlp" for i in range(len(model.model.layers))]
     proj = {"__default__": {"style": "logra", "proj_dim": proj_dim, "proj_type": "rademacher", "proj_seed": 0}}
     cfg = bw.HookManagerConfig(linear_io=[r"\.mlp\.(experts|gate)$"], projection_kwargs=proj, capture_style="auto",
                                include_frozen=True)
@@ -69,14 +69,14 @@ def _capture(model, ids, grouped: bool, proj_dim: int = 4):
     return data, model.get_input_embeddings().weight.grad.float().clone(), calls["n"]
 
 
-def _compare(device, dtype, rtol, atol, proj_dim=4):
-    model = _model(device, dtype)
+def _compare(device, dtype, rtol, atol, proj_dim=4, layers=2):
+    model = _model(device, dtype, layers)
     ids = torch.randint(0, 96, (3, 16), generator=torch.Generator().manual_seed(5)).to(device)
     grouped, emb_g, proxy_calls = _capture(model, ids, grouped=True, proj_dim=proj_dim)
     looped, emb_l, loop_calls = _capture(model, ids, grouped=False, proj_dim=proj_dim)
     assert proxy_calls == 0 and loop_calls > 0
     experts = [n for n in grouped if ".dattri_experts." in n]
-    assert len(experts) == 2 * E * LAYERS
+    assert len(experts) == 2 * E * layers
     for name, want in looped.items():
         _close(grouped[name], want, rtol, atol, name)
     for name in set(experts) - set(looped):  # experts no token reached: zero rows
@@ -108,4 +108,6 @@ def test_grouped_path_steps_aside_for_trainable_experts():
 def test_grouped_expert_capture_matches_per_expert_capture_gpu():
     if not torch.cuda.is_available():
         pytest.skip("needs a GPU")
-    _compare("cuda", torch.bfloat16, rtol=None, atol=3e-2, proj_dim=16)
+    # one block: in bf16 a second block's routing can flip on near-tied router scores, since
+    # the two paths round the first block's output differently (fp32 vs bf16 combine sums)
+    _compare("cuda", torch.bfloat16, rtol=None, atol=3e-2, proj_dim=16, layers=1)
