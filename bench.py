@@ -730,6 +730,151 @@ def main_c4(a, rank, world, local):
     return out
 
 
+# --------------------------------------------------------------------------- config 5
+C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 2, 256, 4, 64
+C5_DROP = 0.9  # keep the top 10 % of every step's pool micro-batch
+
+
+class _DS5(torch.utils.data.Dataset):
+    """Config-5 synthetic sequences (uniform token ids, length 2048), deterministic."""
+
+    def __init__(self, n: int, vocab: int, seed: int) -> None:
+        g = torch.Generator().manual_seed(seed)
+        self.ids = torch.randint(0, vocab, (n, C5_SEQ), generator=g)
+
+    def __len__(self):
+        return self.ids.shape[0]
+
+    def __getitem__(self, i):
+        return {"input_ids": self.ids[i]}
+
+
+def _mamba2_config(**small):
+    """Mamba2-2.7B architecture: 64 mixers, d 2560, expand 2, state 128, head dim 64."""
+    from transformers import Mamba2Config
+
+    kw = {"vocab_size": 50288, "hidden_size": 2560, "num_hidden_layers": 64, "expand": 2, "state_size": 128,
+          "head_dim": 64, "num_heads": 80, "n_groups": 1, "chunk_size": 256, "tie_word_embeddings": True}
+    kw.update(small)
+    return Mamba2Config(**kw)
+
+
+def _mamba2(cfg, dev, ours: bool):
+    """Random-init Hugging Face Mamba2 in bf16; our arm runs its linears on the library's
+    tcgen05 kernels (same parameters)."""
+    from transformers import Mamba2ForCausalLM
+
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Mamba2ForCausalLM(cfg)
+    model = model.to(torch.bfloat16).train()
+    if ours:
+        from dattri_llm_b200.models.layers import tc_linearize
+
+        tc_linearize(model)
+    return model
+
+
+def _c5_hook_config(lib):
+    proj = {"__default__": {"style": "mask", "proj_dim": C5_MASK, "proj_seed": 0}}
+    return lib.HookManagerConfig(linear_io=[r"mixer\.(in_proj|out_proj)$"], projection_kwargs=proj), proj
+
+
+def _c5_target(lib, model, hc, dev, vocab, n_test=C5_NTEST, test_mb=C5_TEST_MB):
+    """The fixed selection target: the mean masked gradient of the test sequences."""
+    import dataclasses
+
+    cap = lib.CaptureCallback()
+    hm = lib.HookManager(model, hc, callbacks=[cap])
+    ids = _DS5(n_test, vocab, seed=1).ids
+    total = None
+    with hm.collect():
+        for i in range(0, n_test, test_mb):
+            model.zero_grad(set_to_none=True)
+            _token_sum_loss(model, {"input_ids": ids[i:i + test_mb].to(dev)}).backward()
+            part = {n: v.float().sum(0, keepdim=True) for n, v in cap.record.gradient.data.items()}
+            total = part if total is None else {n: total[n] + part[n] for n in part}
+            grad = cap.record.gradient
+    hm.remove()
+    model.zero_grad(set_to_none=True)
+    return dataclasses.replace(grad, data={n: v / n_test for n, v in total.items()})
+
+
+def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_NTEST):
+    """One LESS-style trajectory with online selection through the public streamer: Adam-
+    preconditioned masked captures (k = 64 per linear, 8192 in all), their optimizer state
+    recorded every step, each step's pool micro-batch scored against the fixed target and
+    its bottom 90 % dropped.  K steps timed with CUDA events (max over ranks)."""
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    hc, proj = _c5_hook_config(lib)
+    target = _c5_target(lib, model, hc, dev, vocab, n_test=n_test)
+    args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C5_MB,
+                                    learning_rate=1e-5, dataloader_pin_memory=dev.type == "cuda")
+    n = (warmup + steps + 1) * C5_MB * world
+    train = lib.GradientStreamer(model, _DS5(n, vocab, seed=2), args, batch_size=C5_MB, enable_update=True,
+                                 loss_fn=_token_sum_loss, config=hc, precondition=True)
+    hm = train.hook_manager
+    hm.add_callback(lib.OptimizerStateCallback(model, lambda: train.optimizer, projection_kwargs=proj))
+    hm.add_callback(lib.DataSelectionCallback(model=train.forward_model, target="fixed", target_gradient=target,
+                                              scoring_kwargs={"score_mode": "materialized"},
+                                              selection_kwargs={"threshold": C5_DROP,
+                                                                "threshold_mode": "bottom_fraction"}))
+    timed = _TimedBlocks(train, warmup, steps)
+    clocks = ClockSampler(local)
+    clocks.start()
+    with train:
+        for _ in timed:
+            pass
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(timed.ev0.elapsed_time(timed.ev1), world) / steps
+    host = _max_over_ranks(timed.t1 - timed.t0, world)
+    return ms, clk, host
+
+
+def main_c5(a, rank, world, local):
+    dev = torch.device("cuda", local)
+    cfg = _mamba2_config()
+    cfg_json = {"model": "Mamba2-2.7B-arch (random init, Hugging Face modeling)", "global_batch": C5_MB * world,
+                "micro_batch_per_gpu": C5_MB, "seq_len": C5_SEQ, "parallelism": f"ddp{world}" if world > 1 else "single",
+                "method": (f"LESS-style Adam-preconditioned masked captures of every in_proj/out_proj "
+                           f"(k={C5_MASK} per linear, {2 * cfg.num_hidden_layers * C5_MASK} in all) + "
+                           "OptimizerStateCallback + online DataSelectionCallback (fixed target: mean of "
+                           f"{C5_NTEST} test sequences; bottom {int(C5_DROP * 100)} % of each step's pool "
+                           "micro-batch dropped), AdamW trajectory"),
+                "timed": "K trajectory steps of the public GradientStreamer",
+                "l2": "per-step parameter traffic (5.4 GB bf16 + optimizer state) exceeds the 126 MB L2"}
+    out = {"metric": "train samples attributed/sec (LESS capture + online selection in training, device-timed)",
+           "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak",
+           "dtype": "bf16", "data": "synthetic uniform token ids, random-init weights", "config": cfg_json}
+    if a.impl == "ours":
+        sys.path.insert(0, HERE)
+        import dattri_llm_b200 as bw
+        from dattri_llm_b200 import ops as native_ops
+
+        native_ops.native()
+        model = _mamba2(cfg, dev, ours=True)
+        n0 = native_ops.launch_count()
+        ms, clk, host = _c5_run(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        native_ops.check_device_errors(dev)
+        extra = {"gpu_launches": native_ops.launch_count() - n0}
+    else:
+        ref = os.path.join(HERE, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref, "dattri_llm")):
+            raise SystemExit("bench.py --impl reference: the reference is not installed under baseline/_ref")
+        sys.path.insert(0, ref)
+        import dattri_llm as R  # noqa: N812
+
+        model = _mamba2(cfg, dev, ours=False)
+        ms, clk, host = _c5_run(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        extra = {"impl": "reference"}
+    value = C5_MB * world / (ms / 1e3)
+    out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms, "vs_baseline": None, "clocks": clk,
+                "e2e": {"value": C5_MB * world * a.steps / host, "unit": "train samples/s (host clock)",
+                        "h2d_bytes_per_step": C5_MB * C5_SEQ * 8, "d2h_bytes_per_step": 0}, **extra})
+    return out
+
+
 def main_c3(a, rank, world, local):
     cfg_json = {"model": "Llama-3-8B-arch (random init)", "global_batch": C3_MB * world, "micro_batch_per_gpu": C3_MB,
                 "seq_len": C3_SEQ, "parallelism": f"fsdp{world}" if world > 1 else "single",
@@ -759,14 +904,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2)
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2)
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
     rank, world, local = _init_dist()
-    if a.config in (3, 4):
+    if a.config in (3, 4, 5):
         try:
-            out = (main_c3 if a.config == 3 else main_c4)(a, rank, world, local)
+            out = {3: main_c3, 4: main_c4, 5: main_c5}[a.config](a, rank, world, local)
         finally:
             if world > 1:
                 import torch.distributed as dist

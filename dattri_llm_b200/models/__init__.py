@@ -4,8 +4,8 @@ with an optional fused LoGra projection tail) and ``nn.LayerNorm`` / ``nn.RMSNor
 norms, so the capture hooks see them like any user model."""
 
 from dattri_llm_b200.models.gpt2 import GPT2Config, GPT2LMHeadModel
-from dattri_llm_b200.models.layers import TcLinear
+from dattri_llm_b200.models.layers import TcLinear, tc_linearize
 from dattri_llm_b200.models.llama import LlamaConfig, LlamaForCausalLM, LlamaModel, token_sum_loss
 
 __all__ = ["GPT2Config", "GPT2LMHeadModel", "LlamaConfig", "LlamaForCausalLM", "LlamaModel", "TcLinear",
-           "token_sum_loss"]
+           "tc_linearize", "token_sum_loss"]

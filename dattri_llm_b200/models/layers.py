@@ -32,3 +32,15 @@ class TcLinear(nn.Linear):
         if link is not None:
             link.after_forward(self, a_pt, slot)
         return y
+
+
+def tc_linearize(model: nn.Module) -> list[str]:
+    """Turn every bias-free ``nn.Linear`` of *model* into a :class:`TcLinear` in place (the
+    same parameters, hooks and names; only the GEMMs change).  Lets a Hugging Face model
+    run its projections on the library's kernels.  Returns the converted module names."""
+    done = []
+    for name, module in model.named_modules():
+        if type(module) is nn.Linear and module.bias is None:
+            module.__class__ = TcLinear
+            done.append(name)
+    return done
