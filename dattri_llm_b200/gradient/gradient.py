@@ -77,37 +77,90 @@ def base_layer_name(name: str) -> str:
     return name.split("@", 1)[0]
 
 
-def _pad_tokens(t: torch.Tensor, target: int, axis: int, value: float = 0) -> torch.Tensor:
-    if t.shape[axis] == target:
+def _grow_tokens(t: torch.Tensor, length: int, axis: int, fill: float = 0) -> torch.Tensor:
+    """*t* right-padded with *fill* along *axis* to *length* positions."""
+    short = length - t.shape[axis]
+    if short <= 0:
         return t
-    shape = list(t.shape)
-    shape[axis] = target - shape[axis]
-    return torch.cat([t, t.new_full(shape, value)], dim=axis)
+    pad_shape = list(t.shape)
+    pad_shape[axis] = short
+    return torch.cat([t, t.new_full(pad_shape, fill)], dim=axis)
 
 
-def _pad_to_common_tokens(a: Factorized, b: Factorized) -> tuple[Factorized, Factorized]:
-    """Right-pad the shorter token axis; padded positions get an exactly-zero gradient
-    (integer ids get the layer's ``padding_idx`` or 0), which every consumer treats as inert."""
-    axis = 1 if a.batch_first else 0
-    target = max(a.activation.shape[axis], b.activation.shape[axis])
+def _same_token_length(x: Factorized, y: Factorized) -> tuple[Factorized, Factorized]:
+    """Both factor pairs right-padded to the longer token axis.  A padded position carries
+    a zero output gradient, so it contributes nothing anywhere; integer activations (token
+    ids) are padded with the layer's ``padding_idx`` (or 0)."""
+    axis = 1 if x.batch_first else 0
+    length = max(x.activation.shape[axis], y.activation.shape[axis])
 
-    def pad(f: Factorized) -> Factorized:
-        if f.activation.shape[axis] == target:
+    def grown(f: Factorized) -> Factorized:
+        if f.activation.shape[axis] == length:
             return f
-        fill = 0
-        if not f.activation.is_floating_point():
-            p = (f.module_kwargs or {}).get("padding_idx")
-            fill = p if p is not None else 0
-        return f._rebuild(_pad_tokens(f.activation, target, axis, fill),
-                          _pad_tokens(f.pre_activation_grad, target, axis))
+        pad_id = (f.module_kwargs or {}).get("padding_idx")
+        fill = 0 if f.activation.is_floating_point() or pad_id is None else pad_id
+        return f._rebuild(_grow_tokens(f.activation, length, axis, fill),
+                          _grow_tokens(f.pre_activation_grad, length, axis))
 
-    return pad(a), pad(b)
+    return grown(x), grown(y)
 
 
 def _layer_batch(value: GradientData) -> int:
+    """Samples held by one layer's payload."""
     if isinstance(value, Factorized):
         return value.activation.shape[0 if value.batch_first else 1]
     return value.shape[0]
+
+
+def _factorized_rows(name: str, kind: str, value) -> tuple[int, tuple]:
+    """Check one factorized payload; returns ``(samples, activation shape)``."""
+    if not isinstance(value, Factorized):
+        raise TypeError(f"layer {name!r} is declared factorized but holds a {type(value).__name__}.")
+    bf = value.as_batch_first()
+    a, g = bf.activation, bf.pre_activation_grad
+    if kind == "nn.EmbeddingBag":
+        ok = a.ndim == 2 and g.ndim == 2 and a.shape[0] == g.shape[0]
+        want = "2-D bags and 2-D gradients with one row per bag"
+    elif ops.is_embedding(kind):
+        ok = a.ndim == 2 and g.ndim == 3 and a.shape == g.shape[:2]
+        want = "(B, T) ids and (B, T, E) gradients"
+    elif ops.is_conv(kind) or ops.is_conv_transpose(kind):
+        ok = a.shape[0] == g.shape[0]
+        want = "factors with the same leading sample axis"
+    else:
+        ok = a.shape[:-1] == g.shape[:-1]
+        want = "factors that agree on every axis but the feature axis"
+    if not ok:
+        raise ValueError(f"layer {name!r} ({kind}): expected {want}, got activation {tuple(a.shape)} and gradient "
+                         f"{tuple(g.shape)}.")
+    return a.shape[0], tuple(value.activation.shape)
+
+
+def _dense_rows(name: str, kind: str, value, indexing: str) -> tuple[int, tuple]:
+    """Check one materialized payload; returns ``(samples, shape)``."""
+    if not isinstance(value, torch.Tensor):
+        raise TypeError(f"layer {name!r} is declared materialized but holds a {type(value).__name__}.")
+    if value.ndim == 0:
+        raise ValueError(f"layer {name!r} holds a scalar; a per-sample payload needs a leading sample axis.")
+    if kind != ops.PARAM_GRAD_TYPES and indexing == "batch_token" and value.ndim != 3:
+        raise ValueError(f"layer {name!r} is batch_token indexed, which needs a (B, T, d) tensor, not "
+                         f"{value.ndim}-D.")
+    return value.shape[0], tuple(value.shape)
+
+
+def _mix_shared_rows(name: str, kind: str, x, y, wx: float, wy: float):
+    """The shared (broadcast) row of two blocks merged as their sample-weighted mean."""
+    total = wx + wy
+    if isinstance(x, torch.Tensor) and isinstance(y, torch.Tensor):
+        return (wx * x + wy * y) / total, None
+    if not (isinstance(x, Factorized) and isinstance(y, Factorized)):
+        raise TypeError(f"layer {name!r} is factorized in one block and materialized in the other.")
+    xb, yb = x.as_batch_first(), y.as_batch_first()
+    if xb.activation.shape == yb.activation.shape and torch.equal(xb.activation, yb.activation):
+        grad = (wx * xb.pre_activation_grad + wy * yb.pre_activation_grad) / total
+        return Factorized(xb.activation, grad, module_kwargs=xb.module_kwargs), None
+    dense = (wx * ops.materialize(x, kind) + wy * ops.materialize(y, kind)) / total
+    return dense, "materialized"
 
 
 @dataclass(frozen=True, eq=False)
@@ -236,56 +289,28 @@ class Gradient:
                 disagree on the batch size.
         """
         if not self.data:
-            raise ValueError("data cannot be empty")
-        missing = set(self.data) - set(self.representation)
-        if missing:
-            raise ValueError(f"Missing representation for layers: {sorted(missing)}")
-        batch = first = None
+            raise ValueError("a Gradient block needs at least one layer.")
+        unlisted = sorted(set(self.data) - set(self.representation))
+        if unlisted:
+            raise ValueError(f"layers without a representation entry: {unlisted}.")
+        reference_rows = None  # (samples, layer, shape) of the first per-sample layer
         for name, value in self.data.items():
-            lt = self.layer_types[name]
+            kind = self.layer_types[name]
             if self.representation[name] == "factorized":
-                if not isinstance(value, Factorized):
-                    raise TypeError(f"{name} must be Factorized")
-                shape = tuple(value.activation.shape)
-                bf = value.as_batch_first()
-                a, g = bf.activation, bf.pre_activation_grad
-                if lt == "nn.EmbeddingBag":
-                    if a.ndim != 2 or g.ndim != 2:
-                        raise ValueError(f"{name} has invalid embedding-bag factor dimensions")
-                    if a.shape[0] != g.shape[0]:
-                        raise ValueError(f"{name} embedding-bag batch dimension mismatch")
-                elif ops.is_embedding(lt):
-                    if a.ndim != 2 or g.ndim != 3:
-                        raise ValueError(f"{name} has invalid embedding factor dimensions")
-                    if a.shape != g.shape[:2]:
-                        raise ValueError(f"{name} embedding batch/token dimensions mismatch")
-                elif ops.is_conv(lt) or ops.is_conv_transpose(lt):
-                    if a.shape[0] != g.shape[0]:
-                        raise ValueError(f"{name} conv factor batch size mismatch: {a.shape[0]} != {g.shape[0]}")
-                elif a.shape[:-1] != g.shape[:-1]:
-                    raise ValueError(f"{name} factor batch/token dimensions mismatch")
-                cur = a.shape[0]
+                rows, shape = _factorized_rows(name, kind, value)
             else:
-                if not isinstance(value, torch.Tensor):
-                    raise TypeError(f"{name} must be Tensor")
-                if value.ndim < 1:
-                    raise ValueError(f"{name} must be at least 1D")
-                if lt != ops.PARAM_GRAD_TYPES and self._layer_indexing(name) == "batch_token" and value.ndim != 3:
-                    raise ValueError(f"{name} declared as batch_token but tensor is {value.ndim}D, expected 3D")
-                cur, shape = value.shape[0], tuple(value.shape)
-            if lt == ops.PARAM_GRAD_TYPES or cur == 1:
-                continue
-            if batch is None:
-                batch, first = cur, (name, shape)
-            elif batch != cur:
+                rows, shape = _dense_rows(name, kind, value, self._layer_indexing(name))
+            if kind == ops.PARAM_GRAD_TYPES or rows == 1:
+                continue  # batch-level or broadcast: no per-sample axis to agree on
+            if reference_rows is None:
+                reference_rows = (rows, name, shape)
+            elif rows != reference_rows[0]:
                 raise ValueError(
-                    f"All layers must have the same batch size: {first[0]} has {batch} samples "
-                    f"(captured shape {first[1]}) but {name} has {cur} (captured shape {shape}). "
-                    "The sample axis is read from dim 0 of every per-sample layer; a layer whose "
-                    "input is sequence-first (T, B, ...) must be declared in "
-                    "HookManager(non_batch_first_layers=...), and a layer fed flattened or routed "
-                    "token rows (an MoE router or expert) in HookManager(moe_routed_layers=...).",
-                )
+                    f"layers disagree on the batch size: {reference_rows[1]!r} has {reference_rows[0]} samples "
+                    f"(shape {reference_rows[2]}), {name!r} has {rows} (shape {shape}). Every per-sample layer "
+                    "carries its samples on axis 0: declare sequence-first (T, B, ...) inputs in "
+                    "HookManager(non_batch_first_layers=...) and routed token rows (MoE routers / experts) in "
+                    "HookManager(moe_routed_layers=...).")
 
     def clone(self) -> Gradient:
         """Deep copy with every tensor cloned."""
@@ -350,131 +375,113 @@ class Gradient:
         Raises:
             KeyError: for unknown names.
         """
-        names = set(layer_names)
+        wanted = set(layer_names)
         if include_derived:
-            names |= {n for n in self.layer_names if base_layer_name(n) in names}
-        missing = names - self.layer_names
-        if missing:
-            raise KeyError(f"Unknown layers: {sorted(missing)}")
-        return Gradient({n: self.representation[n] for n in names}, {n: self.data[n] for n in names},
-                        {k: v for k, v in self.layer_types.items() if k in names},
-                        {n: i for n, i in self.indexing.items() if n in names})
+            wanted.update(n for n in self.data if base_layer_name(n) in wanted)
+        unknown = sorted(wanted - set(self.data))
+        if unknown:
+            raise KeyError(f"the block has no layers {unknown}.")
+        keep = [n for n in self.data if n in wanted]
+        return Gradient({n: self.representation[n] for n in keep}, {n: self.data[n] for n in keep},
+                        {n: self.layer_types[n] for n in keep}, {n: self.indexing[n] for n in keep})
+
+    def _require_token_axis(self, what: str) -> None:
+        flat = sorted(n for n in self.data if self._layer_indexing(n) != "batch_token")
+        if flat:
+            raise ValueError(f"{what} along tokens needs every layer batch_token indexed; {flat} are not.")
 
     def concatenate(self, other: Gradient, dim: Literal["batch", "token"] = "batch") -> Gradient:
         """Concatenate along the batch (unequal token lengths zero-padded; broadcast layers
         averaged by batch size) or the token axis."""
         self._check_compatible(other, require_same_batch=False)
+        rows_self, rows_other = self.batch_size, other.batch_size
         if dim == "token":
-            bad = [n for n in self.layer_names if self._layer_indexing(n) != "batch_token"]
-            if bad:
-                raise ValueError(
-                    f"Token concatenation requires all layers to have indexing='batch_token'. "
-                    f"Non-conforming: {sorted(bad)}",
-                )
-            if self.batch_size != other.batch_size:
-                raise ValueError("Token concatenation requires the same batch size")
+            self._require_token_axis("concatenation")
+            if rows_self != rows_other:
+                raise ValueError(f"concatenating along tokens needs equal batch sizes, got {rows_self} and "
+                                 f"{rows_other}.")
         data, rep, idx = {}, dict(self.representation), dict(self.indexing)
-        b_self, b_other = self.batch_size, other.batch_size
-
-        def axis(batch_first: bool) -> int:
-            return (0 if batch_first else 1) if dim == "batch" else (1 if batch_first else 0)
-
-        for name in self.layer_names:
-            a, b = self.data[name], other.data[name]
-            bc_a = _layer_batch(a) == 1 and b_self > 1
-            bc_b = _layer_batch(b) == 1 and b_other > 1
-            if dim == "batch" and (bc_a or bc_b):
-                if bc_a != bc_b:
-                    raise ValueError(
-                        f"{name} is a broadcast (batch-collapsed) gradient on one side but "
-                        "per-sample on the other; the two cannot be concatenated along the batch axis.",
-                    )
-                wa, wb = float(b_self), float(b_other)
-                if isinstance(a, Factorized) and isinstance(b, Factorized):
-                    abf, bbf = a.as_batch_first(), b.as_batch_first()
-                    if abf.activation.shape == bbf.activation.shape and torch.equal(abf.activation, bbf.activation):
-                        g = (wa * abf.pre_activation_grad + wb * bbf.pre_activation_grad) / (wa + wb)
-                        data[name] = Factorized(abf.activation, g, module_kwargs=abf.module_kwargs)
-                    else:
-                        lt = self.layer_types[name]
-                        data[name] = (wa * ops.materialize(a, lt) + wb * ops.materialize(b, lt)) / (wa + wb)
-                        rep[name], idx[name] = "materialized", "batch"
-                elif isinstance(a, torch.Tensor) and isinstance(b, torch.Tensor):
-                    data[name] = (wa * a + wb * b) / (wa + wb)
-                else:
-                    raise TypeError(f"{name} has mismatched data types")
+        for name in self.data:
+            x, y = self.data[name], other.data[name]
+            shared_x, shared_y = _layer_batch(x) == 1 < rows_self, _layer_batch(y) == 1 < rows_other
+            if dim == "batch" and (shared_x or shared_y):
+                if shared_x != shared_y:
+                    raise ValueError(f"layer {name!r} holds one shared row in one block and per-sample rows in "
+                                     "the other; they cannot be stacked along the batch.")
+                data[name], new_rep = _mix_shared_rows(name, self.layer_types[name], x, y, float(rows_self),
+                                                       float(rows_other))
+                if new_rep is not None:
+                    rep[name], idx[name] = new_rep, "batch"
                 continue
-            if isinstance(a, Factorized) and isinstance(b, Factorized):
-                if a.batch_first != b.batch_first:
-                    raise ValueError(f"{name} has mismatched batch_first layout between gradients")
-                if dim == "batch" and self._layer_indexing(name) == "batch_token":
-                    a, b = _pad_to_common_tokens(a, b)
-                ax = axis(a.batch_first)
-                data[name] = a._rebuild(torch.cat([a.activation, b.activation], dim=ax),
-                                        torch.cat([a.pre_activation_grad, b.pre_activation_grad], dim=ax))
-            elif isinstance(a, torch.Tensor) and isinstance(b, torch.Tensor):
-                if dim == "batch" and self._layer_indexing(name) == "batch_token":
-                    t = max(a.shape[1], b.shape[1])
-                    a, b = _pad_tokens(a, t, 1), _pad_tokens(b, t, 1)
-                data[name] = torch.cat([a, b], dim=axis(True))
-            else:
-                raise TypeError(f"{name} has mismatched data types")
-        out = Gradient(rep, data, self.layer_types, idx)
-        out.validate()
-        return out
+            data[name] = self._joined(name, x, y, dim)
+        joined = Gradient(rep, data, self.layer_types, idx)
+        joined.validate()
+        return joined
+
+    def _joined(self, name: str, x, y, dim: str):
+        """One layer's payloads of two blocks joined along *dim*."""
+        tokens_indexed = self._layer_indexing(name) == "batch_token"
+        if isinstance(x, Factorized) and isinstance(y, Factorized):
+            if x.batch_first != y.batch_first:
+                raise ValueError(f"layer {name!r} is batch-first in one block and sequence-first in the other.")
+            if dim == "batch" and tokens_indexed:
+                x, y = _same_token_length(x, y)
+            sample_axis = 0 if x.batch_first else 1
+            axis = sample_axis if dim == "batch" else 1 - sample_axis
+            return x._rebuild(torch.cat([x.activation, y.activation], dim=axis),
+                              torch.cat([x.pre_activation_grad, y.pre_activation_grad], dim=axis))
+        if isinstance(x, torch.Tensor) and isinstance(y, torch.Tensor):
+            if dim == "batch" and tokens_indexed:
+                length = max(x.shape[1], y.shape[1])
+                x, y = _grow_tokens(x, length, 1), _grow_tokens(y, length, 1)
+            return torch.cat([x, y], dim=0 if dim == "batch" else 1)
+        raise TypeError(f"layer {name!r} is factorized in one block and materialized in the other.")
 
     def aggregate(self, dim: Literal["token"] = "token") -> Gradient:
         """Sum out the token axis of ``"batch_token"`` layers (the chain rule:
         ``dL/dW = sum_t g_t a_t^T``); every layer ends ``"batch"`` indexed."""
         if dim != "token":
-            raise NotImplementedError("Only token aggregation is supported")
+            raise NotImplementedError(f"aggregate() sums out the token axis; dim={dim!r} is not one.")
         data, rep = {}, {}
-        for name, v in self.data.items():
-            if self._layer_indexing(name) == "batch_token":
-                if isinstance(v, Factorized):
-                    data[name], rep[name] = ops.materialize(v, self.layer_types[name]), "materialized"
-                else:
-                    data[name], rep[name] = v.sum(dim=1), self.representation[name]
+        for name, value in self.data.items():
+            data[name], rep[name] = value, self.representation[name]
+            if self._layer_indexing(name) != "batch_token":
+                continue
+            if isinstance(value, Factorized):
+                data[name], rep[name] = ops.materialize(value, self.layer_types[name]), "materialized"
             else:
-                data[name], rep[name] = v, self.representation[name]
+                data[name] = value.sum(dim=1)
         return Gradient(rep, data, self.layer_types, {})
 
     def slice(self, dim: Literal["batch", "token"], index: int | Sequence[int] | torch.Tensor) -> Gradient:
         """Slice every layer along the batch or token axis (a broadcast layer's shared row
         is copied to every requested sample)."""
         if dim == "token":
-            bad = [n for n in self.layer_names if self._layer_indexing(n) != "batch_token"]
-            if bad:
-                raise ValueError(
-                    f"Token slicing requires all layers to have indexing='batch_token'. "
-                    f"Non-conforming: {sorted(bad)}",
-                )
+            self._require_token_axis("slicing")
+        scalar = isinstance(index, int)
+        count = 1 if scalar else (index.numel() if torch.is_tensor(index) else len(index))
 
-        def cut(x: torch.Tensor, ax: int) -> torch.Tensor:
-            li = index
-            if dim == "batch" and x.shape[ax] == 1:
-                if isinstance(index, int):
-                    li = 0
-                else:
-                    n = index.numel() if torch.is_tensor(index) else len(index)
-                    li = torch.zeros(n, dtype=torch.long, device=x.device)
-            sl = [slice(None)] * x.ndim
-            sl[ax] = li
-            y = x[tuple(sl)]
-            return y.unsqueeze(ax) if isinstance(li, int) else y
+        def take(t: torch.Tensor, axis: int) -> torch.Tensor:
+            picks = index
+            if dim == "batch" and t.shape[axis] == 1:  # a shared row serves every sample
+                picks = 0 if scalar else torch.zeros(count, dtype=torch.long, device=t.device)
+            if scalar:
+                return t.narrow(axis, picks, 1)
+            return t.index_select(axis, torch.as_tensor(picks, device=t.device).reshape(-1))
 
-        def axis(bf: bool) -> int:
-            return (0 if bf else 1) if dim == "batch" else (1 if bf else 0)
+        def axis_of(batch_first: bool) -> int:
+            sample = 0 if batch_first else 1
+            return sample if dim == "batch" else 1 - sample
 
         data = {}
-        for name, v in self.data.items():
+        for name, value in self.data.items():
             if self.layer_types[name] == ops.PARAM_GRAD_TYPES:
-                data[name] = v
-            elif isinstance(v, Factorized):
-                ax = axis(v.batch_first)
-                data[name] = v._rebuild(cut(v.activation, ax), cut(v.pre_activation_grad, ax))
+                data[name] = value
+            elif isinstance(value, Factorized):
+                ax = axis_of(value.batch_first)
+                data[name] = value._rebuild(take(value.activation, ax), take(value.pre_activation_grad, ax))
             else:
-                data[name] = cut(v, axis(True))
+                data[name] = take(value, axis_of(True))
         return Gradient(dict(self.representation), data, self.layer_types, dict(self.indexing))
 
     def similarity(self, other: Gradient, metric: Literal["dot", "cosine"] = "dot",
@@ -533,23 +540,23 @@ class Gradient:
         return ops.grad_norm_sq(self.data[name], self.layer_types[name], mode=mode)
 
     def _check_compatible(self, other: Gradient, require_same_batch: bool) -> None:
-        if self.layer_names != other.layer_names:
-            raise ValueError("Layer sets differ")
-        bad = {n for n in self.layer_names if self.representation.get(n) != other.representation.get(n)}
-        if bad:
-            raise ValueError(f"Layers have differing representations: {sorted(bad)}")
-        bad = {n for n in self.layer_names if self._layer_indexing(n) != other._layer_indexing(n)}
-        if bad:
-            raise ValueError(f"Layers have differing indexing: {sorted(bad)}")
-        if self.layer_types != other.layer_types:
-            raise ValueError(f"Layer types differ: {self.layer_types} vs {other.layer_types}")
+        if set(self.data) != set(other.data):
+            raise ValueError(f"the blocks hold different layers: {sorted(set(self.data) ^ set(other.data))}.")
+        for what, mine, theirs in (("representation", self.representation, other.representation),
+                                   ("indexing", {n: self._layer_indexing(n) for n in self.data},
+                                    {n: other._layer_indexing(n) for n in other.data}),
+                                   ("layer type", self.layer_types, other.layer_types)):
+            odd = sorted(n for n in self.data if mine.get(n) != theirs.get(n))
+            if odd:
+                raise ValueError(f"the blocks disagree on the {what} of layers {odd}.")
         if require_same_batch:
             if self.batch_size != other.batch_size:
-                raise ValueError("Batch sizes differ")
-            st, ot = self.token_dim, other.token_dim
-            bad = {n for n in self.layer_names if st[n] != ot[n]}
-            if bad:
-                raise ValueError(f"Token dimensions differ for layers: {sorted(bad)}")
+                raise ValueError(f"the blocks have different batch sizes ({self.batch_size} and "
+                                 f"{other.batch_size}).")
+            mine_t, theirs_t = self.token_dim, other.token_dim
+            odd = sorted(n for n in self.data if mine_t[n] != theirs_t[n])
+            if odd:
+                raise ValueError(f"the blocks have different token lengths in layers {odd}.")
 
 
 @dataclass
