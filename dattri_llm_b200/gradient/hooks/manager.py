@@ -700,9 +700,11 @@ class HookManager:
             self._routed = RoutedTokenTracker(root, self._moe_blocks)
             fused = [n for n in find_fused_experts(root) if self._routed.covers(n)]
             if fused:
+                tracker = self._routed
                 proxies, reverts = install_fused_experts(
                     root, fused, lambda: self._collecting,
-                    grouped=lambda name, experts: GroupedExpertCapture(self, name, experts, PROXY_EXPERTS))
+                    grouped=lambda name, experts: GroupedExpertCapture(self, name, experts, PROXY_EXPERTS),
+                    place=lambda x: tracker.place if tracker.identity_shape(x) is not None else None)
                 self._reverts.extend(reverts)
                 layer_types.update(proxies)
                 for proxy in proxies:

@@ -1,16 +1,23 @@
-"""Per-expert proxies for MoE blocks whose experts are fused 3-D parameters.
+"""Hookable stand-ins for MoE blocks whose experts are fused 3-D parameters.
 
-Transformers-5 style MoE blocks hold every expert in two stacked parameters
-(``gate_up_proj (E, ., .)``, ``down_proj (E, ., .)``) and apply them with batched
-kernels, so no per-expert ``nn.Linear`` exists to hook.  While collecting, the
-block's forward is replaced by an explicit per-expert loop through
-:class:`SliceLinear` proxies (views of expert ``e``'s slice), which the capture
-hooks see as ordinary linear layers; a router applied with a functional
-``F.linear`` gets a :class:`RouterLinear` proxy the same way.  Gradients still
-accumulate into the fused parameters.  Proxy names (``<block>.dattri_experts.<e>.
-gate_up`` / ``.down``, ``<router>.dattri_router``) are layer names in the stored
-records and match the reference's
-(``dattri_llm/gradient/hooks/override_layers/fused_experts.py:59-382``).
+Transformers-5 MoE blocks keep every expert in two stacked parameters
+(``gate_up_proj (E, 2I, H)``, ``down_proj (E, H, I)``) and apply them in bulk, so there is
+no per-expert ``nn.Linear`` a capture hook could sit on; the router, too, is often an
+``F.linear`` on a bare weight.  While a capture collects, such a block gets:
+
+* per expert, two :class:`SliceLinear` stand-ins (``gate_up`` / ``down``) that read slice
+  ``e`` of the fused parameters -- gradients still land in the fused parameters;
+* for the router, a :class:`RouterLinear` stand-in that the router's own forward calls in
+  place of ``F.linear``;
+* a forward that either hands the whole block to a grouped capture (one function for all
+  experts, :mod:`.grouped_experts`) or loops over the experts that received tokens,
+  feeding each stand-in the rows routed to it and telling the row tracker where those rows
+  came from.
+
+Stand-in names -- ``<experts>.dattri_experts.<e>.gate_up`` / ``.down`` and
+``<router>.dattri_router`` -- are layer names in stored records, the same as the
+reference's (``dattri_llm/gradient/hooks/override_layers/fused_experts.py``), so stores
+are interchangeable.
 """
 
 from __future__ import annotations
@@ -21,52 +28,55 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
-_linear = F.linear
+_F_LINEAR = F.linear
 GATE_UP = "gate_up_proj"
 DOWN = "down_proj"
 PROXY_EXPERTS = "dattri_experts"
 PROXY_ROUTER = "dattri_router"
-_INDEX_KWARGS = ("top_k_index", "router_indices", "selected_experts", "topk_indices")
-_WEIGHT_KWARGS = ("top_k_weights", "routing_weights", "router_scores", "topk_weights")
+# keyword spellings of the routing arguments across model families
+_INDEX_NAMES = ("top_k_index", "router_indices", "selected_experts", "topk_indices")
+_WEIGHT_NAMES = ("top_k_weights", "routing_weights", "router_scores", "topk_weights")
 
 
 class SliceLinear(nn.Module):
-    """A linear layer whose weight is slice *index* of a fused 3-D parameter."""
+    """A bias-optional linear map whose weight is slice *index* of a fused 3-D parameter of
+    *owner* (held by reference, not as a submodule, so no parameter is registered twice)."""
 
     def __init__(self, owner: nn.Module, weight_name: str, index: int, bias_name: str | None = None,
                  *, transposed: bool = False) -> None:
         super().__init__()
-        object.__setattr__(self, "_owner", owner)  # not a submodule: no parameter duplication
-        self._weight_name, self._bias_name = weight_name, bias_name
+        self.__dict__["_owner"] = owner
+        self._names = (weight_name, bias_name)
         self._index, self._transposed = index, transposed
 
     @property
     def weight(self) -> torch.Tensor:
-        """Expert *index*'s ``(out, in)`` weight view."""
-        w = getattr(self._owner, self._weight_name)[self._index]
-        return w.transpose(0, 1) if self._transposed else w
+        """This expert's ``(out, in)`` weight view."""
+        w = getattr(self._owner, self._names[0])[self._index]
+        return w.t() if self._transposed else w
 
     @property
     def bias(self) -> torch.Tensor | None:
-        """Expert *index*'s bias view (``None`` without biases)."""
-        return None if self._bias_name is None else getattr(self._owner, self._bias_name)[self._index]
+        """This expert's bias view (``None`` without biases)."""
+        name = self._names[1]
+        return None if name is None else getattr(self._owner, name)[self._index]
 
     def proxied_parameters(self) -> Iterator[nn.Parameter]:
-        """The fused parameters this proxy reads."""
-        yield getattr(self._owner, self._weight_name)
-        if self._bias_name is not None:
-            yield getattr(self._owner, self._bias_name)
+        """The fused parameters this stand-in reads."""
+        for name in self._names:
+            if name is not None:
+                yield getattr(self._owner, name)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return _linear(x, self.weight, self.bias)
+        return _F_LINEAR(x, self.weight, self.bias)
 
 
 class RouterLinear(nn.Module):
-    """Hookable stand-in for a router applied with ``F.linear`` on its own weight."""
+    """The router's ``F.linear`` on its own weight, as a hookable module."""
 
     def __init__(self, router: nn.Module) -> None:
         super().__init__()
-        object.__setattr__(self, "_router", router)
+        self.__dict__["_router"] = router
 
     @property
     def weight(self) -> torch.Tensor:
@@ -75,32 +85,32 @@ class RouterLinear(nn.Module):
 
     @property
     def bias(self) -> torch.Tensor | None:
-        """The router's bias, if any."""
+        """The router's bias, if it has one."""
         return getattr(self._router, "bias", None)
 
     def proxied_parameters(self) -> Iterator[nn.Parameter]:
-        """The router parameters this proxy reads."""
+        """The router parameters this stand-in reads."""
         yield self._router.weight
         if self.bias is not None:
             yield self.bias
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        b = self.bias
-        return _linear(x, self.weight.to(x.dtype), None if b is None else b.to(x.dtype))
+        bias = self.bias
+        return _F_LINEAR(x, self.weight.to(x.dtype), None if bias is None else bias.to(x.dtype))
 
 
 def is_fused_experts(module: nn.Module) -> bool:
-    """Whether *module* holds experts as fused ``gate_up_proj`` / ``down_proj`` 3-D tensors."""
-    gu, dn = getattr(module, GATE_UP, None), getattr(module, DOWN, None)
-    return (isinstance(gu, torch.Tensor) and isinstance(dn, torch.Tensor) and gu.ndim == 3
-            and dn.ndim == 3 and gu.shape[0] == dn.shape[0])
+    """Whether *module* keeps its experts as fused ``gate_up_proj`` / ``down_proj`` 3-D tensors."""
+    up, down = getattr(module, GATE_UP, None), getattr(module, DOWN, None)
+    return (isinstance(up, torch.Tensor) and isinstance(down, torch.Tensor) and up.ndim == down.ndim == 3
+            and up.shape[0] == down.shape[0])
 
 
 def is_fused_router(module: nn.Module, num_experts: int) -> bool:
-    """A leaf module with an ``(E, d)`` weight that is not an ``nn.Linear``."""
+    """A childless, non-``nn.Linear`` module holding an ``(E, d)`` weight parameter."""
     w = getattr(module, "weight", None)
     return (isinstance(w, nn.Parameter) and w.ndim == 2 and w.shape[0] == num_experts
-            and not isinstance(module, nn.Linear) and not any(True for _ in module.children()))
+            and not isinstance(module, nn.Linear) and next(module.children(), None) is None)
 
 
 def find_fused_experts(root: nn.Module) -> dict[str, nn.Module]:
@@ -108,126 +118,136 @@ def find_fused_experts(root: nn.Module) -> dict[str, nn.Module]:
     return {n: m for n, m in root.named_modules() if is_fused_experts(m)}
 
 
-def _routing_args(args: tuple, kwargs: dict):
-    if len(args) >= 2:
-        return args[0], args[1]
-    index = next((kwargs[k] for k in _INDEX_KWARGS if k in kwargs), None)
-    weights = next((kwargs[k] for k in _WEIGHT_KWARGS if k in kwargs), None)
-    if len(args) == 1:
-        if index is None:
-            index = args[0]
-        else:
-            weights = args[0]
-    if index is None or weights is None:
-        raise TypeError(
-            f"fused experts forward called without recognisable routing arguments: positional "
-            f"{len(args)}, keywords {sorted(kwargs)}.",
-        )
-    return index, weights
+def _routing_arguments(args: tuple, kwargs: dict) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(expert index, routing weights)`` from an experts forward's arguments after the
+    hidden states (positional, or under any of the families' keyword names)."""
+    found = {"index": next((kwargs[k] for k in _INDEX_NAMES if k in kwargs), None),
+             "weights": next((kwargs[k] for k in _WEIGHT_NAMES if k in kwargs), None)}
+    positional = list(args[:2])
+    for slot in ("index", "weights"):
+        if found[slot] is None and positional:
+            found[slot] = positional.pop(0)
+    if found["index"] is None or found["weights"] is None:
+        raise TypeError(f"a fused-experts forward was called without recognisable routing arguments "
+                        f"({len(args)} positional, keywords {sorted(kwargs)}).")
+    return found["index"], found["weights"]
 
 
-def _experts_loop(experts, proxies, x, top_k_index, top_k_weights) -> torch.Tensor:
-    """Reference per-expert loop: gather routed rows, gate_up -> model gate -> down, weight,
-    scatter-add back."""
-    n_exp = len(proxies)
+def _loop_over_experts(experts: nn.Module, stand_ins: nn.ModuleList, x: torch.Tensor, index: torch.Tensor,
+                       weights: torch.Tensor, place: Callable | None) -> torch.Tensor:
+    """The block through the stand-ins: per expert with tokens, its rows through
+    ``gate_up`` -> the model's gate -> ``down``, weighted and added back at their tokens."""
+    n_experts = len(stand_ins)
     out = torch.zeros_like(x)
     with torch.no_grad():
-        hit = torch.zeros(n_exp + 1, dtype=torch.bool, device=x.device)
-        hit[top_k_index.reshape(-1).clamp(max=n_exp)] = True
-        experts_hit = hit[:n_exp].nonzero().flatten().tolist()
-    for e in experts_hit:
-        tok, pos = torch.where(top_k_index == e)
-        h = proxies[e]["down"](experts._apply_gate(proxies[e]["gate_up"](x[tok])))
-        out.index_add_(0, tok, (h * top_k_weights[tok, pos, None]).to(out.dtype))
+        used = torch.bincount(index.reshape(-1).clamp(max=n_experts), minlength=n_experts + 1)[:n_experts]
+        active = used.nonzero().flatten().tolist()  # one host read per block
+    for e in active:
+        tokens, slots = torch.where(index == e)
+        rows = x.index_select(0, tokens)
+        if place is not None:
+            place(rows, tokens)
+        pair = stand_ins[e]
+        hidden = pair["down"](experts._apply_gate(pair["gate_up"](rows)))
+        out.index_add_(0, tokens, (hidden * weights[tokens, slots, None]).to(out.dtype))
     return out
 
 
-def _override_router(router: nn.Module, proxy: RouterLinear, should_intervene) -> Callable[[], None]:
+def _patch_router(router: nn.Module, stand_in: RouterLinear, should_intervene: Callable[[], bool]):
+    """Make the router's forward call *stand_in* where it applies ``F.linear`` to its own
+    weight (while collecting); returns the undo."""
     original = router.forward
 
-    def patched(x, weight, bias=None):
-        return proxy(x) if weight.shape == router.weight.shape else _linear(x, weight, bias)
+    def linear(x, weight, bias=None):
+        return stand_in(x) if weight.shape == router.weight.shape else _F_LINEAR(x, weight, bias)
 
     def forward(*args, **kwargs):
         if not should_intervene():
             return original(*args, **kwargs)
-        F.linear = patched
+        F.linear = linear
         try:
             return original(*args, **kwargs)
         finally:
-            F.linear = _linear
+            F.linear = _F_LINEAR
 
     router.forward = forward
 
-    def revert():
+    def undo():
         del router.forward
         delattr(router, PROXY_ROUTER)
 
-    return revert
+    return undo
 
 
-def install_fused_experts(root: nn.Module, experts_names: list[str],
-                          should_intervene: Callable[[], bool], grouped: Callable | None = None):
-    """Attach per-expert proxies and override the forwards while *should_intervene()*.
+def _attach_stand_ins(name: str, experts: nn.Module) -> tuple[nn.ModuleList, dict[str, str]]:
+    n_experts = getattr(experts, GATE_UP).shape[0]
+    transposed = bool(getattr(experts, "is_transposed", False))
+    biased = bool(getattr(experts, "has_bias", False)) and hasattr(experts, GATE_UP + "_bias")
+    stand_ins = nn.ModuleList()
+    types = {}
+    for e in range(n_experts):
+        stand_ins.append(nn.ModuleDict({
+            "gate_up": SliceLinear(experts, GATE_UP, e, GATE_UP + "_bias" if biased else None, transposed=transposed),
+            "down": SliceLinear(experts, DOWN, e, DOWN + "_bias" if biased else None, transposed=transposed),
+        }))
+        for part in ("gate_up", "down"):
+            types[f"{name}.{PROXY_EXPERTS}.{e}.{part}"] = "nn.Linear"
+    experts.add_module(PROXY_EXPERTS, stand_ins)
+    return stand_ins, types
 
-    *grouped*: ``(experts_name, experts) -> capture`` with a ``try_forward(x, index, weights)``
-    that runs the whole block (returning ``None`` when it does not apply); the per-expert
-    loop runs otherwise.  Returns ``(proxy_types, reverts)``: ``{proxy_layer_name:
-    "nn.Linear"}`` and undo callables.
+
+def install_fused_experts(root: nn.Module, experts_names: list[str], should_intervene: Callable[[], bool],
+                          grouped: Callable | None = None, place: Callable | None = None):
+    """Attach the stand-ins to each named fused-experts module (and its sibling router) and
+    override the forwards while *should_intervene()*.
+
+    *grouped*: ``(experts_name, experts) -> capture`` whose ``try_forward(x, index, weights)``
+    runs the whole block (``None`` when it does not apply).  *place*: ``(x) ->
+    callable(rows, tokens) or None`` -- the row tracker's placement for a block input, used by
+    the per-expert loop.  Returns ``(stand-in layer types, undo callables)``.
     """
     modules = dict(root.named_modules())
     types: dict[str, str] = {}
-    reverts: list[Callable[[], None]] = []
+    undos: list[Callable[[], None]] = []
     for name in experts_names:
         experts = modules[name]
         if not is_fused_experts(experts):
-            raise ValueError(f"{name} is not a fused experts module.")
+            raise ValueError(f"{name} holds no fused expert parameters.")
         if hasattr(experts, PROXY_EXPERTS):
-            raise RuntimeError(f"{name} already carries fused-expert proxies.")
-        n_exp = getattr(experts, GATE_UP).shape[0]
-        transposed = bool(getattr(experts, "is_transposed", False))
-        has_bias = bool(getattr(experts, "has_bias", False)) and hasattr(experts, GATE_UP + "_bias")
-        proxies = nn.ModuleList([nn.ModuleDict({
-            "gate_up": SliceLinear(experts, GATE_UP, e, GATE_UP + "_bias" if has_bias else None,
-                                   transposed=transposed),
-            "down": SliceLinear(experts, DOWN, e, DOWN + "_bias" if has_bias else None,
-                                transposed=transposed),
-        }) for e in range(n_exp)])
-        experts.add_module(PROXY_EXPERTS, proxies)
-        for e in range(n_exp):
-            types[f"{name}.{PROXY_EXPERTS}.{e}.gate_up"] = "nn.Linear"
-            types[f"{name}.{PROXY_EXPERTS}.{e}.down"] = "nn.Linear"
-        original = experts.forward
+            raise RuntimeError(f"{name} already carries expert stand-ins.")
+        stand_ins, block_types = _attach_stand_ins(name, experts)
+        types.update(block_types)
         bulk = grouped(name, experts) if grouped is not None else None
+        original = experts.forward
 
-        def forward(*args, _e=experts, _p=proxies, _o=original, _g=bulk, **kwargs):
+        def forward(*args, _experts=experts, _stand_ins=stand_ins, _original=original, _bulk=bulk, **kwargs):
             if not should_intervene():
-                return _o(*args, **kwargs)
-            index, weights = _routing_args(args[1:], kwargs)
-            if _g is not None:
-                out = _g.try_forward(args[0], index, weights)
+                return _original(*args, **kwargs)
+            x = args[0]
+            index, weights = _routing_arguments(args[1:], kwargs)
+            if _bulk is not None:
+                out = _bulk.try_forward(x, index, weights)
                 if out is not None:
                     return out
-            return _experts_loop(_e, _p, args[0], index, weights)
+            placer = place(x) if place is not None else None
+            return _loop_over_experts(_experts, _stand_ins, x, index, weights, placer)
 
         experts.forward = forward
 
-        def revert(_e=experts):
-            del _e.forward
-            delattr(_e, PROXY_EXPERTS)
+        def undo(_experts=experts):
+            del _experts.forward
+            delattr(_experts, PROXY_EXPERTS)
 
-        reverts.append(revert)
+        undos.append(undo)
         parent_name = name.rpartition(".")[0]
-        parent = modules.get(parent_name, root if not parent_name else None)
-        if parent is None:
-            continue
-        for child_name, child in parent.named_children():
-            if not is_fused_router(child, n_exp) or hasattr(child, PROXY_ROUTER):
-                continue
-            proxy = RouterLinear(child)
-            child.add_module(PROXY_ROUTER, proxy)
+        parent = modules.get(parent_name) if parent_name else root
+        router = next(((n, m) for n, m in (parent.named_children() if parent is not None else ())
+                       if is_fused_router(m, len(stand_ins)) and not hasattr(m, PROXY_ROUTER)), None)
+        if router is not None:
+            child_name, module = router
+            stand_in = RouterLinear(module)
+            module.add_module(PROXY_ROUTER, stand_in)
             full = f"{parent_name}.{child_name}" if parent_name else child_name
             types[f"{full}.{PROXY_ROUTER}"] = "nn.Linear"
-            reverts.append(_override_router(child, proxy, should_intervene))
-            break
-    return types, reverts
+            undos.append(_patch_router(module, stand_in, should_intervene))
+    return types, undos

@@ -111,3 +111,15 @@ def test_grouped_expert_capture_matches_per_expert_capture_gpu():
     # one block: in bf16 a second block's routing can flip on near-tied router scores, since
     # the two paths round the first block's output differently (fp32 vs bf16 combine sums)
     _compare("cuda", torch.bfloat16, rtol=None, atol=3e-2, proj_dim=16, layers=1)
+
+
+def test_exact_row_positions_pair_repeated_rows_in_order():
+    from dattri_llm_b200.gradient.hooks.routing import _exact_positions
+
+    grid = torch.tensor([[1.0, 2.0], [0.0, 0.0], [3.0, 4.0], [0.0, 0.0], [5.0, 6.0]])
+    picks = torch.tensor([4, 1, 0, 3])  # two identical zero rows among them
+    got = _exact_positions(grid[picks], grid)
+    assert got.tolist() == [4, 1, 0, 3]
+    assert _exact_positions(torch.tensor([[9.0, 9.0]]), grid) is None  # a row the grid does not hold
+    three_zeros = torch.zeros(3, 2)
+    assert _exact_positions(three_zeros, grid) is None  # more copies than the grid has
