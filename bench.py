@@ -731,7 +731,7 @@ def main_c4(a, rank, world, local):
 
 
 # --------------------------------------------------------------------------- config 5
-C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 2, 256, 4, 64
+C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 2, 256, 2, 64
 C5_DROP = 0.9  # keep the top 10 % of every step's pool micro-batch
 
 
@@ -760,8 +760,9 @@ def _mamba2_config(**small):
 
 
 def _mamba2(cfg, dev, ours: bool):
-    """Random-init Hugging Face Mamba2 in bf16; our arm runs its linears on the library's
-    tcgen05 kernels (same parameters)."""
+    """Random-init Hugging Face Mamba2 in bf16.  Our arm installs the library's SSD forward
+    (batched-matmul chunked scan instead of the library model's broadcast products) and runs
+    its linears on the tcgen05 kernels; parameters and module names are unchanged."""
     from transformers import Mamba2ForCausalLM
 
     torch.manual_seed(0)
@@ -769,9 +770,9 @@ def _mamba2(cfg, dev, ours: bool):
         model = Mamba2ForCausalLM(cfg)
     model = model.to(torch.bfloat16).train()
     if ours:
-        from dattri_llm_b200.models.layers import tc_linearize
+        from dattri_llm_b200.models.mamba2 import accelerate_mamba2
 
-        tc_linearize(model)
+        accelerate_mamba2(model)
     return model
 
 
