@@ -731,8 +731,8 @@ def main_c4(a, rank, world, local):
 
 
 # --------------------------------------------------------------------------- config 5
-C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 2, 256, 2, 64
-C5_DROP = 0.9  # keep the top 10 % of every step's pool micro-batch
+C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 1, 256, 1, 64
+C5_DROP = 0.9  # keep the top 10 % of the pool; with one sequence per GPU the global pool is N sequences
 
 
 class _DS5(torch.utils.data.Dataset):

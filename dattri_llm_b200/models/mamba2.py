@@ -7,7 +7,9 @@ so training runs out of memory at any useful batch.  :func:`ssd_chunked` compute
 chunked SSD (Dao & Gu 2024, "Transformers are SSMs", Listing 1) as batched matrix
 products: per chunk, the causal ``(C B^T) . L`` mixing applied to ``x dt``, per-chunk end
 states, the inter-chunk recurrence, and the states' contribution to each position.  Its
-largest intermediate is one ``(batch, heads, chunks, chunk, chunk)`` fp32 tensor.
+largest intermediate is one ``(batch, heads, chunks, chunk, chunk)`` fp32 tensor, and in a
+training step the scan is recomputed in the backward, so only its inputs are kept per
+layer.
 
 :func:`accelerate_mamba2` installs that forward on every ``Mamba2Mixer`` of a model (the
 cache-free training / scoring call; decoding keeps the library's path) and moves the
@@ -23,6 +25,7 @@ import types
 import torch
 import torch.nn.functional as F
 from torch import nn
+from torch.utils.checkpoint import checkpoint
 
 from dattri_llm_b200.models.layers import tc_linearize
 
@@ -86,6 +89,15 @@ def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torc
     return y[:, :length] if pad else y
 
 
+def _scan_with_skip(x, dt, a_head, b_groups, c_groups, d_skip, chunk: int) -> torch.Tensor:
+    """``ssd_chunked(...) + D x`` with B and C given per group ``(batch, length, groups, state)``
+    and widened to the heads here (recomputed in the backward, so never kept)."""
+    heads = x.shape[2]
+    b = b_groups.repeat_interleave(heads // b_groups.shape[2], dim=2)
+    c = c_groups.repeat_interleave(heads // c_groups.shape[2], dim=2)
+    return ssd_chunked(x, dt, a_head, b, c, chunk) + d_skip[:, None] * x
+
+
 def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attention_mask=None, **kwargs):
     """``Mamba2Mixer.forward`` for the cache-free call, through :func:`ssd_chunked`."""
     masked = attention_mask is not None and not bool(attention_mask.all())
@@ -104,10 +116,15 @@ def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attenti
     a_head = -torch.exp(self.A_log.float())
     dt = F.softplus(dt + self.dt_bias).clamp(self.time_step_limit[0], self.time_step_limit[1]).float()
     x = x.reshape(bsz, length, self.num_heads, self.head_dim).float()
-    per_group = self.num_heads // self.n_groups
-    b = b.reshape(bsz, length, self.n_groups, self.ssm_state_size).float().repeat_interleave(per_group, dim=2)
-    c = c.reshape(bsz, length, self.n_groups, self.ssm_state_size).float().repeat_interleave(per_group, dim=2)
-    y = ssd_chunked(x, dt, a_head, b, c, self.chunk_size) + self.D[:, None] * x
+    b = b.reshape(bsz, length, self.n_groups, self.ssm_state_size).float()
+    c = c.reshape(bsz, length, self.n_groups, self.ssm_state_size).float()
+    args = (x, dt, a_head, b, c, self.D, self.chunk_size)
+    if torch.is_grad_enabled():
+        # the scan's (chunk x chunk) intermediates are rebuilt in the backward instead of
+        # being kept for all layers at once: only the scan's inputs stay alive
+        y = checkpoint(_scan_with_skip, *args, use_reentrant=False)
+    else:
+        y = _scan_with_skip(*args)
     scanned = self.norm(y.reshape(bsz, length, -1), gate)
     return self.out_proj(scanned.to(dtype))
 
