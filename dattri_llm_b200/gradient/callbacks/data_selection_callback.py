@@ -69,6 +69,16 @@ def _concat_batches(batches: list) -> object:
     raise TypeError(f"Cannot concatenate val batches of type {type(first).__name__}.")
 
 
+def _token_contraction(g: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    """``(out, in) = g^T a`` over the token rows of ``g (N, out)`` and ``a (N, in)``, fp32."""
+    from dattri_llm_b200 import ops as native_ops
+
+    aligned = g.shape[0] % 8 == 0 and g.shape[1] % 8 == 0 and a.shape[1] % 8 == 0
+    if aligned and g.dtype == a.dtype == torch.bfloat16 and native_ops.use_native(g, a):
+        return native_ops.per_sample_outer(g[None], a[None], out_dtype=torch.float32)[0]
+    return g.float().T @ a.float()
+
+
 class DataSelectionCallback(HookManagerCallback):
     """Score every sample of each step and remove the selected ones' gradient contributions.
 
@@ -323,7 +333,12 @@ class DataSelectionCallback(HookManagerCallback):
 
     @staticmethod
     def _weight_contribution(lt: str, mk: dict | None, a_d, g_d, shape: tuple[int, ...]) -> torch.Tensor:
-        """Sum of the dropped samples' weight gradients, flat in the parameter's layout."""
+        """Sum of the dropped samples' weight gradients, flat in the parameter's layout.  For a
+        linear layer that is ONE contraction over every dropped token, ``G^T A`` (a tcgen05
+        GEMM with fp32 accumulation for bf16 factors on sm_100), instead of one ``(out, in)``
+        gradient per sample summed afterwards."""
+        if lt == "nn.Linear" and a_d.is_floating_point() and a_d.dim() == g_d.dim() >= 2:
+            return _token_contraction(g_d.reshape(-1, g_d.shape[-1]), a_d.reshape(-1, a_d.shape[-1])).reshape(-1)
         contrib = ops.materialize(Factorized(a_d, g_d, mk), lt, include_bias=False).sum(0)
         if ops.is_embedding(lt):
             return contrib

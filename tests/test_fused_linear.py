@@ -183,3 +183,17 @@ def test_matmul_f32_bf16x3(m, n, k, bt):
     rel = float((got.double() - want).abs().max() / want.abs().max())
     assert rel < 5e-5, rel
     ops.check_device_errors()
+
+
+@pytest.mark.gpu
+def test_data_selection_token_contraction_on_tensor_cores():
+    """The dropped samples' linear-layer contribution is one tcgen05 contraction over their
+    tokens; it equals the fp32 sum of per-sample weight gradients."""
+    from dattri_llm_b200.gradient.callbacks.data_selection_callback import DataSelectionCallback
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(3, 96, 256, device="cuda", generator=g).bfloat16()
+    d = torch.randn(3, 96, 128, device="cuda", generator=g).bfloat16()
+    got = DataSelectionCallback._weight_contribution("nn.Linear", None, a, d, (128, 256))
+    want = torch.einsum("bto,bti->oi", d.float(), a.float()).reshape(-1)
+    torch.testing.assert_close(got, want, rtol=2e-3, atol=2e-3)
