@@ -358,10 +358,17 @@ class LayerFisherAccumulator:
         self.update_from_grad(materialize_factors(a, g, layer_type, module_kwargs, include_bias))
 
     def update_from_grad(self, grad: torch.Tensor) -> None:
-        """Add one batch of dense per-sample gradients ``(B, d)``."""
+        """Add one batch of dense per-sample gradients ``(B, d)`` (the Gram accumulation of
+        :func:`gram_accumulate`: fp32 sums, one tcgen05 launch for bf16 rows on sm_100)."""
+        grad = grad.reshape(grad.shape[0], -1)
+        wide = grad.dtype == torch.float64
         if self._F is None:
-            self._F = torch.zeros(grad.shape[-1], grad.shape[-1], dtype=grad.dtype, device=grad.device)
-        self._F += grad.T @ grad
+            self._F = torch.zeros(grad.shape[-1], grad.shape[-1], dtype=torch.float64 if wide else torch.float32,
+                                  device=grad.device)
+        if wide:
+            self._F += grad.T @ grad
+        else:
+            gram_accumulate(grad if grad.dtype == torch.bfloat16 else grad.float(), self._F)
         self._n += grad.shape[0]
 
     def all_reduce(self) -> None:

@@ -197,3 +197,18 @@ def test_data_selection_token_contraction_on_tensor_cores():
     got = DataSelectionCallback._weight_contribution("nn.Linear", None, a, d, (128, 256))
     want = torch.einsum("bto,bti->oi", d.float(), a.float()).reshape(-1)
     torch.testing.assert_close(got, want, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.gpu
+def test_direct_fisher_accumulates_on_the_gram_kernel():
+    """The direct empirical Fisher of bf16 per-sample gradients (K-FAC's non-Kronecker
+    layers) accumulates through the symmetric tcgen05 Gram kernel: equal to fp32 G^T G."""
+    from dattri_llm_b200.gradient.ops.kronecker import LayerFisherAccumulator
+
+    g = torch.Generator(device="cuda").manual_seed(4)
+    acc = LayerFisherAccumulator()
+    batches = [torch.randn(16, 384, device="cuda", generator=g).bfloat16() for _ in range(3)]
+    for b in batches:
+        acc.update_from_grad(b)
+    want = sum(b.float().T @ b.float() for b in batches) / 48
+    torch.testing.assert_close(acc.result(), want, rtol=2e-3, atol=2e-3)
