@@ -135,21 +135,26 @@ _TOKEN_OUTER_ELEMS = 1 << 27
 
 
 def _per_token_gram_native(a1: torch.Tensor, g1: torch.Tensor, m2: torch.Tensor) -> torch.Tensor:
-    """``K[i, t, j] = <g1_it a1_it^T, M2_j>`` for bf16 ``a1 (B, T, K)``, ``g1 (B, T, D)`` and
-    side 2 dense ``m2 (C, D*K)`` in the materialized ``(out, in)`` layout: every token's
-    outer product is one row of a tcgen05 GEMM against ``m2`` (fp32 accumulate), chunked
-    over tokens so the outer products stay within a bounded buffer."""
+    """``K[i, t, j] = <g1_it a1_it^T, M2_j> = g1_it . (M2_j a1_it)`` for bf16 ``a1 (B, T, K)``,
+    ``g1 (B, T, D)`` and side 2 dense ``m2 (C, D*K)`` in the materialized ``(out, in)``
+    layout.  One tcgen05 GEMM maps every token's activation through every ``M2_j`` at once,
+    ``Y = a1 [M2_1; ...; M2_C]^T`` (fp32), and the dot with ``g1`` reduces ``Y`` over ``D``:
+    the ``(D, K)`` outer product of a token is never formed (``T C D`` intermediate values per
+    sample instead of ``T D K``: fewer whenever side 2 has fewer samples than the layer has
+    inputs).  Chunked over side 2 to bound ``Y``."""
     from dattri_llm_b200 import ops as native_ops
 
     b, t, k = a1.shape
     d = g1.shape[-1]
-    rows_a, rows_g = a1.reshape(b * t, k), g1.reshape(b * t, d)
-    m2 = m2.reshape(m2.shape[0], d * k).to(torch.bfloat16).contiguous()
-    out = torch.empty(b * t, m2.shape[0], dtype=torch.float32, device=a1.device)
-    step = max(1, _TOKEN_OUTER_ELEMS // (d * k))
-    for s in range(0, b * t, step):
-        outer = (rows_g[s:s + step].unsqueeze(-1) * rows_a[s:s + step].unsqueeze(-2)).reshape(-1, d * k)
-        out[s:s + step] = native_ops.matmul_tn(outer, m2, out_dtype=torch.float32)
+    n = b * t
+    rows_a, rows_g = a1.reshape(n, k), g1.reshape(n, d).float()
+    m2 = m2.reshape(m2.shape[0], d, k).to(torch.bfloat16).contiguous()
+    out = torch.empty(n, m2.shape[0], dtype=torch.float32, device=a1.device)
+    step = max(1, _TOKEN_OUTER_ELEMS // (n * d))
+    for c0 in range(0, m2.shape[0], step):
+        block = m2[c0:c0 + step]
+        mapped = native_ops.matmul_tn(rows_a, block.reshape(-1, k), out_dtype=torch.float32)
+        out[:, c0:c0 + block.shape[0]] = torch.einsum("ncd,nd->nc", mapped.view(n, block.shape[0], d), rows_g)
     return out.view(b, t, -1)
 
 
