@@ -24,6 +24,7 @@
 #include "mask_gather.cuh"
 #include "moe_ep.cuh"
 #include "norm_grad.cuh"
+#include "embed_grad.cuh"
 
 namespace {
 
@@ -689,7 +690,8 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
                   src.stride(0) % 8 == 0 && src.size(1) % 8 == 0, "src must be (T, H) bf16 with 16-byte rows");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "src must be 16-byte aligned");
   const int world = (int)peer_rows.size();
-  TORCH_CHECK(world >= 1 && world <= 8 && (int)peer_meta.size() == world, "1..8 ranks");
+  TORCH_CHECK(world >= 1 && world <= 8 && (peer_meta.empty() || (int)peer_meta.size() == world),
+              "1..8 ranks, one origin table per rank or none");
   const long long rows = src.size(0) * rows_per_token;
   TORCH_CHECK(dst_rank.scalar_type() == torch::kInt32 && dst_row.scalar_type() == torch::kInt32 &&
                   dst_rank.numel() == rows && dst_row.numel() == rows && dst_rank.is_contiguous() && dst_row.is_contiguous(),
@@ -699,12 +701,13 @@ void moe_dispatch(Tensor src, int64_t rows_per_token, Tensor dst_rank, Tensor ds
   for (int r = 0; r < world; ++r) {
     TORCH_CHECK(peer_rows[r].scalar_type() == torch::kBFloat16 && peer_rows[r].size(-1) == src.size(1) &&
                     peer_rows[r].is_contiguous(), "receive buffers must be (R, H) bf16");
-    TORCH_CHECK(peer_meta[r].scalar_type() == torch::kInt32 && peer_meta[r].is_contiguous(), "origin tables: int32");
     pr.push_back(peer_rows[r].data_ptr());
+    if (peer_meta.empty()) continue;
+    TORCH_CHECK(peer_meta[r].scalar_type() == torch::kInt32 && peer_meta[r].is_contiguous(), "origin tables: int32");
     pm.push_back(reinterpret_cast<int2*>(peer_meta[r].data_ptr<int>()));
   }
   bw::moe_dispatch(src.data_ptr(), src.stride(0), dst_rank.data_ptr<int>(), dst_row.data_ptr<int>(), pr.data(),
-                   pm.data(), world, (int)rows, (int)src.size(1), (int)self, (int)rows_per_token,
+                   pm.empty() ? nullptr : pm.data(), world, (int)rows, (int)src.size(1), (int)self, (int)rows_per_token,
                    at::cuda::getCurrentCUDAStream());
 }
 
@@ -786,7 +789,8 @@ void moe_combine_bwd_dispatch(Tensor dy, Tensor slots, Tensor w, Tensor dw, Tens
                   dst_rank.numel() == rows && dst_row.numel() == rows && dst_rank.is_contiguous() &&
                   dst_row.is_contiguous(), "dst_rank / dst_row: int32 per (token, slot)");
   const int world = (int)peer_rows.size();
-  TORCH_CHECK(world >= 1 && world <= 8 && (int)peer_meta.size() == world, "1..8 ranks");
+  TORCH_CHECK(world >= 1 && world <= 8 && (peer_meta.empty() || (int)peer_meta.size() == world),
+              "1..8 ranks, one origin table per rank or none");
   std::vector<void*> pr;
   std::vector<int2*> pm;
   for (int r = 0; r < world; ++r) {
@@ -1171,6 +1175,27 @@ void ce_bwd_inplace(Tensor logits, Tensor lse, Tensor target, Tensor gscale) {
 
 }  // namespace
 
+// Dense per-sample embedding gradients (B * vocab, E) from the token keys sorted ascending
+// (key = b * vocab + id), the token row of g behind each key, and g (n, E).  bf16 or fp32,
+// the output in g's dtype; E * elem size a multiple of 16 bytes.
+Tensor embedding_dense_grad(Tensor keys, Tensor order, Tensor g, int64_t rows) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  TORCH_CHECK(g.is_cuda() && g.dim() == 2 && g.is_contiguous(), "g must be a contiguous (n, E) CUDA tensor");
+  TORCH_CHECK(g.scalar_type() == torch::kBFloat16 || g.scalar_type() == torch::kFloat32, "g must be bf16 or fp32");
+  TORCH_CHECK(keys.is_cuda() && order.is_cuda() && keys.scalar_type() == torch::kInt64 &&
+                  order.scalar_type() == torch::kInt64 && keys.is_contiguous() && order.is_contiguous() &&
+                  keys.numel() == g.size(0) && order.numel() == g.size(0),
+              "keys and order must be contiguous int64 vectors of g's row count");
+  const int elem = (int)g.element_size();
+  const int E = (int)g.size(1);
+  TORCH_CHECK((E * elem) % 16 == 0, "the embedding width must fill whole 16-byte vectors");
+  TORCH_CHECK(g.size(0) < (1ll << 31), "too many tokens");
+  auto out = torch::empty({rows, (int64_t)E}, g.options());
+  bw::embedding_dense_grad(keys.data_ptr<int64_t>(), order.data_ptr<int64_t>(), g.data_ptr(), out.data_ptr(), rows,
+                           (int)g.size(0), E, elem, at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
@@ -1187,6 +1212,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
+  m.def("embedding_dense_grad", &embedding_dense_grad, "dense per-sample embedding gradients, every row written once");
   m.def("gemm_ragged", &gemm_ragged, "ragged grouped GEMM over expert row segments (optionally scattered home)",
         py::arg("A"), py::arg("B3"), py::arg("C"), py::arg("tile_prefix"), py::arg("base"), py::arg("len"),
         py::arg("max_tiles"), py::arg("peer_C"), py::arg("scatter"), py::arg("err"), py::arg("bn") = 0);

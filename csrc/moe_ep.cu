@@ -50,7 +50,7 @@ __global__ void dispatch_kernel(const uint4* __restrict__ src, const int* __rest
         if (v < vec_per_row) d[v] = x[u];
       }
     }
-    if (lane == 0) peers.meta[dr][drow] = make_int2(self, r);
+    if (lane == 0 && peers.meta[dr] != nullptr) peers.meta[dr][drow] = make_int2(self, r);
   }
 }
 
@@ -222,7 +222,7 @@ void moe_dispatch(const void* src, long long token_stride, const int* dst_rank, 
   PeerRows p{};
   for (int r = 0; r < world && r < kMaxRanks; ++r) {
     p.rows[r] = static_cast<uint4*>(peer_rows[r]);
-    p.meta[r] = peer_meta[r];
+    p.meta[r] = peer_meta != nullptr ? peer_meta[r] : nullptr;
   }
   if (rows <= 0) return;
   const int ctas = (rows + 3) / 4;  // four warps (rows) per CTA

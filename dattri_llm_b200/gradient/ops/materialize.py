@@ -8,7 +8,8 @@ embedding ``(B, vocab * E)``.
 
 On an sm_100 device the linear/conv contraction ``g^T a`` over tokens runs on the
 tensor cores (:func:`dattri_llm_b200.ops.per_sample_outer`), the norm reduction in
-one fused pass and the embedding scatter as a sorted segment reduction.
+one fused pass, and the embedding scatter as one pass that writes every output row once
+(the tokens sorted by sample and id, each row's tokens summed in fp32).
 """
 
 from __future__ import annotations
@@ -31,6 +32,11 @@ def _materialize_embedding(ids: torch.Tensor, g: torch.Tensor, vocab: int) -> to
             f"Embedding token id {int(ids.max())} is out of range for num_embeddings={vocab}; "
             "the module_kwargs do not match the captured data.",
         )
+    from dattri_llm_b200 import ops as native_ops
+
+    if (native_ops.use_native(grad) and grad.dtype in (torch.bfloat16, torch.float32)
+            and (e * grad.element_size()) % 16 == 0):
+        return native_ops.embedding_dense_grad(ids, grad.reshape(b, t, e), vocab)
     flat = (ids.long() + torch.arange(b, device=ids.device)[:, None] * vocab).reshape(-1)
     out = torch.zeros(b * vocab, e, dtype=grad.dtype, device=grad.device)
     out.index_add_(0, flat, grad.reshape(-1, e))

@@ -158,7 +158,7 @@ from dattri_llm_b200.ops.gram import (  # noqa: E402
     mask_gather,
     per_sample_outer,
 )
-from dattri_llm_b200.ops.norm import norm_per_sample_grad  # noqa: E402
+from dattri_llm_b200.ops.norm import embedding_dense_grad, norm_per_sample_grad  # noqa: E402
 from dattri_llm_b200.ops.optim import adam_direction  # noqa: E402
 from dattri_llm_b200.ops.projection import projection_matrix_t  # noqa: E402
 
@@ -185,6 +185,7 @@ __all__ = [
     "transpose_last2",
     "matmul_tn",
     "native",
+    "embedding_dense_grad",
     "norm_per_sample_grad",
     "per_sample_outer",
     "projection_matrix_t",

@@ -221,3 +221,25 @@ def test_moe_dispatch_and_combine_with_emulated_ranks():
         torch.testing.assert_close(recv[dr][rr].float(), (w.reshape(-1)[r] * dy[r // k].float()).bfloat16().float())
         assert meta[dr][rr].tolist() == [2, r]
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_embedding_dense_grad_matches_index_add(dtype):
+    from dattri_llm_b200.gradient.ops.materialize import materialize_factors
+
+    b, t, e, vocab = 3, 257, 192, 1000
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    ids = torch.randint(0, 40, (b, t), device="cuda", generator=gen)  # many repeats per sample
+    ids[1, :5] = vocab - 1  # the last row
+    ids[2, 7] = 0
+    g = torch.randn(b, t, e, device="cuda", generator=gen).to(dtype)
+    n0 = ops.launch_count()
+    out = ops.embedding_dense_grad(ids, g, vocab)
+    assert ops.launch_count() == n0 + 1
+    ref = torch.zeros(b * vocab, e, device="cuda")
+    ref.index_add_(0, (ids + torch.arange(b, device="cuda")[:, None] * vocab).reshape(-1), g.float().reshape(-1, e))
+    assert out.dtype == dtype and out.shape == (b, vocab * e)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    torch.testing.assert_close(out.float(), ref.reshape(b, vocab * e), rtol=tol, atol=tol)
+    via = materialize_factors(ids, g, "nn.Embedding", module_kwargs={"num_embeddings": vocab})
+    torch.testing.assert_close(via.float(), out.float(), rtol=0, atol=0)
