@@ -28,6 +28,8 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from dattri_llm_b200.gradient.hooks.override_layers._forward_slot import swap_forward
+
 _F_LINEAR = F.linear
 GATE_UP = "gate_up_proj"
 DOWN = "down_proj"
@@ -170,10 +172,10 @@ def _patch_router(router: nn.Module, stand_in: RouterLinear, should_intervene: C
         finally:
             F.linear = _F_LINEAR
 
-    router.forward = forward
+    restore = swap_forward(router, forward)
 
     def undo():
-        del router.forward
+        restore()
         delattr(router, PROXY_ROUTER)
 
     return undo
@@ -232,10 +234,10 @@ def install_fused_experts(root: nn.Module, experts_names: list[str], should_inte
             placer = place(x) if place is not None else None
             return _loop_over_experts(_experts, _stand_ins, x, index, weights, placer)
 
-        experts.forward = forward
+        restore = swap_forward(experts, forward)
 
-        def undo(_experts=experts):
-            del _experts.forward
+        def undo(_experts=experts, _restore=restore):
+            _restore()
             delattr(_experts, PROXY_EXPERTS)
 
         undos.append(undo)

@@ -16,6 +16,7 @@ import torch
 from torch import nn
 
 from dattri_llm_b200.gradient.ops import canonical_class_name
+from dattri_llm_b200.gradient.hooks.override_layers._forward_slot import swap_forward
 
 
 def is_invasive_capable(module: nn.Module) -> bool:
@@ -56,20 +57,11 @@ def install_invasive_forward(model: nn.Module, layer_names: set[str],
                 f"{canonical_class_name(module)}, not nn.Linear.",
             )
         original = module.forward
-        had_own = "forward" in vars(module)
 
         def forward(x, *args, _mod=module, _orig=original, **kwargs):
             if should_intervene():
                 return InvasiveLinearFunction.apply(x, _mod.weight, _mod.bias)
             return _orig(x, *args, **kwargs)
 
-        module.forward = forward
-
-        def revert(_mod=module, _orig=original, _had=had_own):
-            if _had:
-                _mod.forward = _orig
-            else:
-                vars(_mod).pop("forward", None)
-
-        reverts.append(revert)
+        reverts.append(swap_forward(module, forward))
     return reverts

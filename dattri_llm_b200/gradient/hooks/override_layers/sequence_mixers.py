@@ -25,6 +25,8 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from dattri_llm_b200.gradient.hooks.override_layers._forward_slot import swap_forward
+
 MAMBA1_MIXER_CLASSES: set[str] = {"MambaMixer", "FalconMambaMixer", "JambaMambaMixer"}
 _MAMBA1_ATTRS = ("in_proj", "conv1d", "x_proj", "dt_proj", "out_proj", "A_log", "D", "act",
                  "time_step_rank", "ssm_state_size")
@@ -179,10 +181,5 @@ def install_sequence_mixer_forward(root: nn.Module, mixer_names: list[str],
                         setattr(_mod, attr, value)
         else:
             raise ValueError(f"{name} is not a sequence mixer an override serves.")
-        mixer.forward = forward
-
-        def revert(_m=mixer):
-            del _m.forward
-
-        reverts.append(revert)
+        reverts.append(swap_forward(mixer, forward))
     return reverts

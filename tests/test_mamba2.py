@@ -50,3 +50,36 @@ def test_ssd_chunked_matches_the_recurrence():
             + dt[:, t, :, None, None] * x[:, t, :, :, None] * bb[:, t, :, None, :]
         want.append(torch.einsum("bhpn,bhn->bhp", state, cc[:, t]))
     torch.testing.assert_close(ssd_chunked(x, dt, a, bb, cc, chunk=8), torch.stack(want, 1), rtol=1e-4, atol=1e-5)
+
+
+def test_capture_overrides_keep_the_installed_forward():
+    """A capture manager wraps the mixers while it collects; removing it must put back the
+    library's SSD forward, not the model class's naive one, and the forward it wraps while
+    collecting must be the SSD one too."""
+    import dattri_llm_b200 as bw
+    from dattri_llm_b200.models import mamba2 as m2
+
+    warnings.filterwarnings("ignore")
+    model = _model()
+    accelerate_mamba2(model, linears=False)
+    mixers = [m for m in model.modules() if isinstance(m, transformers.models.mamba2.modeling_mamba2.Mamba2Mixer)]
+    ids = torch.randint(0, 64, (2, 16), generator=torch.Generator().manual_seed(3))
+    calls = {"n": 0}
+    real = m2.ssd_chunked
+
+    def counting(*args, **kwargs):
+        calls["n"] += 1
+        return real(*args, **kwargs)
+
+    m2.ssd_chunked = counting
+    try:
+        for _ in range(2):  # the second manager wraps what the first one's removal left
+            hm = bw.HookManager(model, bw.HookManagerConfig(linear_io=[r"mixer\.(in_proj|out_proj)$"]),
+                                callbacks=[bw.CaptureCallback()])
+            with hm.collect():
+                model(input_ids=ids).logits.float().pow(2).sum().backward()
+            hm.remove()
+            assert all(m.forward.__func__ is m2._mixer_forward for m in mixers)
+    finally:
+        m2.ssd_chunked = real
+    assert calls["n"] >= 2 * len(mixers) * 2  # forward + recomputed backward, both passes
