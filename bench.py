@@ -244,6 +244,7 @@ class _TimedBlocks:
         self.t0 = self.t1 = None
         self.reusable = getattr(source, "reusable", False)
         self.args = getattr(source, "args", None)
+        self.prof = _Profiling(os.environ.get("DATTRI_BENCH_PROFILE", ""))
 
     def __len__(self):
         return len(self.source)
@@ -252,12 +253,14 @@ class _TimedBlocks:
         for i, item in enumerate(self.source):
             if i == self.warm:
                 torch.cuda.synchronize()
+                self.prof.start()
                 self.t0 = time.perf_counter()
                 self.ev0.record()
             if i == self.warm + self.steps:
                 self.ev1.record()
                 torch.cuda.synchronize()
                 self.t1 = time.perf_counter()
+                self.prof.stop(_env_int("RANK", 0))
             yield item
 
     def __getattr__(self, name):
@@ -269,6 +272,7 @@ class _Profiling:
     """Optional profiling of the timed steps (off unless ``DATTRI_BENCH_PROFILE`` is set):
     ``cuda`` brackets them with cudaProfilerStart/Stop (for ``ncu --profile-from-start off``,
     which then sees every launch of those steps, the autograd thread's included);
+    ``python`` runs them under ``cProfile`` (host time by function);
     ``torch`` runs them under ``torch.profiler`` and writes the per-kernel device-time table
     and the device-busy fraction to ``DATTRI_BENCH_PROFILE_OUT`` (default
     ``bench_profile.txt``).  A number printed by a profiled run is not a benchmark value."""
@@ -279,6 +283,11 @@ class _Profiling:
     def start(self) -> None:
         if self.mode == "cuda":
             torch.cuda.profiler.start()
+        elif self.mode == "python":
+            import cProfile
+
+            self._prof = cProfile.Profile()
+            self._prof.enable()
         elif self.mode == "torch":
             from torch.profiler import ProfilerActivity, profile
 
@@ -288,6 +297,13 @@ class _Profiling:
     def stop(self, rank: int) -> None:
         if self.mode == "cuda":
             torch.cuda.profiler.stop()
+        elif self.mode == "python" and self._prof is not None:
+            import pstats
+
+            self._prof.disable()
+            if rank == 0:
+                with open(os.environ.get("DATTRI_BENCH_PROFILE_OUT", "bench_profile.txt"), "w") as f:
+                    pstats.Stats(self._prof, stream=f).sort_stats("cumulative").print_stats(60)
         elif self._prof is not None:
             self._prof.__exit__(None, None, None)
             if rank == 0:
@@ -659,15 +675,21 @@ def _olmoe(dev):
     return model, cfg
 
 
-def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=None):
-    """One public scoring loop: K steps timed with CUDA events (max over ranks)."""
+def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=None, expert_parallel=False):
+    """One public scoring loop: K steps timed with CUDA events (max over ranks).  With
+    *expert_parallel* the MoE blocks are :class:`ExpertParallelMoE` modules whose expert and
+    router taps carry the same names as the replicated-expert stand-ins (no routed-row
+    declaration: each row's origin travels with it)."""
     blocks = [f"model.layers.{i}.mlp" for i in range(16)]
     proj = {"__default__": {"style": "logra", "proj_dim": C4_PROJ, "proj_type": "rademacher", "proj_seed": 0}}
     kw = {"projector": projector} if projector is not None else {}
-    hc = lib.HookManagerConfig(linear_io=[r"\.mlp\.(experts|gate)$"], projection_kwargs=proj, capture_style="auto",
+    layers = [r"\.mlp\.(experts|gate)$"]
+    if expert_parallel:
+        layers = [r"\.mlp\.experts\.dattri_experts\.\d+\.(gate_up|down)$", r"\.mlp\.gate\.dattri_router$"]
+    hc = lib.HookManagerConfig(linear_io=layers, projection_kwargs=proj, capture_style="auto",
                                include_frozen=True, **kw)
     cap = lib.CaptureCallback()
-    hm = lib.HookManager(model, hc, callbacks=[cap], moe_routed_layers=blocks)
+    hm = lib.HookManager(model, hc, callbacks=[cap], moe_routed_layers=None if expert_parallel else blocks)
     args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C4_MB,
                                     per_device_eval_batch_size=C4_NTEST, dataloader_pin_memory=True)
     att = lib.TracInAttributor(args, task=lib.AttributionTask(_token_sum_loss, model))
@@ -709,7 +731,8 @@ def main_c4(a, rank, world, local):
 
             expert_parallelize(model, max_tokens=C4_MB * C4_SEQ)
         n0 = native_ops.launch_count()
-        ms, clk, host = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        ms, clk, host = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
+                                  expert_parallel=world > 1)
         extra = {"gpu_launches": native_ops.launch_count() - n0}
     else:
         ref = os.path.join(HERE, "baseline", "_ref")
@@ -808,7 +831,10 @@ def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_NTES
     its bottom 90 % dropped.  K steps timed with CUDA events (max over ranks)."""
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     hc, proj = _c5_hook_config(lib)
-    target = _c5_target(lib, model, hc, dev, vocab, n_test=n_test)
+    # the target is set-up work outside the timed steps; our arm averages it over micro-batches
+    # of 8 test sequences, the reference's model path (the library's naive SSD) over single ones
+    test_mb = 8 if lib.__name__.startswith("dattri_llm_b200") else C5_TEST_MB
+    target = _c5_target(lib, model, hc, dev, vocab, n_test=n_test, test_mb=test_mb)
     args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C5_MB,
                                     learning_rate=1e-5, dataloader_pin_memory=dev.type == "cuda")
     n = (warmup + steps + 1) * C5_MB * world
