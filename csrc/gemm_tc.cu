@@ -1644,6 +1644,12 @@ void gemm_tn_launch(const GemmOperand& A, const GemmOperand& B, GemmParams p, in
     ts.tile_w = pair_tile_width((long long)ts.tiles_m * p.batch, p.N, pair_clusters());
     ts.tiles_n = (p.N + ts.tile_w - 1) / ts.tile_w;
     ts.tail_w = pair_tail_width(p.N, ts.tile_w);
+    // Row-block-fastest order when B is far larger than the L2 and A is not (an LM head's
+    // forward): in column-fastest order every row block streams all of B from HBM again,
+    // while walking all row blocks of one column tile in turn reads B once and keeps A,
+    // the operand that repeats, resident in the L2.
+    const double a_bytes = 2.0 * p.M * p.K, b_bytes = 2.0 * p.N * p.K;
+    ts.n_major = p.batch == 1 && ts.tiles_n > ts.tiles_m && b_bytes > 64e6 && a_bytes <= 64e6 ? 1 : 0;
     const long long ptiles = (long long)ts.tiles_n * ts.tiles_m * ts.batch;
     plan_stream_k(ts, p, ptiles, pair_clusters(), stream);
     if (launch_pair(A, B, p, ts, ptiles, stream)) return;

@@ -207,10 +207,12 @@ def test_gemm_reduce_scatter_slots_emulated():
 
 
 @pytest.mark.parametrize("mode", ["f32", "f32acc", "bf16", "bf16t", "atomic"])
-@pytest.mark.parametrize(("z", "m", "n", "k"), [(1, 8192, 2048, 512), (1, 8000, 1000, 328), (3, 4096, 640, 256)])
+@pytest.mark.parametrize(("z", "m", "n", "k"), [(1, 8192, 2048, 512), (1, 8000, 1000, 328), (3, 4096, 640, 256),
+                                                 (1, 1000, 33000, 1024)])
 def test_persistent_gemm_many_tiles(mode, z, m, n, k):
     """More than one wave of output tiles takes the persistent kernel (two TMEM accumulators,
-    epilogue overlapped with the next tile's MMAs); partial row / column tiles included."""
+    epilogue overlapped with the next tile's MMAs); partial row / column tiles included.  The
+    last shape's B (66 MB) outgrows half the L2 while A does not: row-block-fastest order."""
     a = torch.randn(z, m, k, device="cuda").bfloat16()
     b = torch.randn(n, k, device="cuda").bfloat16()
     want = a.float() @ b.float().T
