@@ -755,6 +755,10 @@ def main_c4(a, rank, world, local):
 
 # --------------------------------------------------------------------------- config 5
 C5_SEQ, C5_MB, C5_NTEST, C5_TEST_MB, C5_MASK = 2048, 1, 256, 1, 64
+# Test sequences averaged into the fixed selection target: set-up work before the timed steps
+# (the steps score against the one averaged vector whatever its count); DATTRI_C5_TARGET_SEQS
+# lowers it to save set-up time on the reference's model path, and the JSON line records it.
+C5_TARGET_SEQS = _env_int("DATTRI_C5_TARGET_SEQS", C5_NTEST)
 C5_DROP = 0.9  # keep the top 10 % of the pool; with one sequence per GPU the global pool is N sequences
 
 
@@ -824,7 +828,7 @@ def _c5_target(lib, model, hc, dev, vocab, n_test=C5_NTEST, test_mb=C5_TEST_MB):
     return dataclasses.replace(grad, data={n: v / n_test for n, v in total.items()})
 
 
-def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_NTEST):
+def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_TARGET_SEQS):
     """One LESS-style trajectory with online selection through the public streamer: Adam-
     preconditioned masked captures (k = 64 per linear, 8192 in all), their optimizer state
     recorded every step, each step's pool micro-batch scored against the fixed target and
@@ -832,8 +836,8 @@ def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_NTES
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     hc, proj = _c5_hook_config(lib)
     # the target is set-up work outside the timed steps; our arm averages it over micro-batches
-    # of 8 test sequences, the reference's model path (the library's naive SSD) over single ones
-    test_mb = 8 if lib.__name__.startswith("dattri_llm_b200") else C5_TEST_MB
+    # of 2 test sequences, the reference's model path (the library's naive SSD) over single ones
+    test_mb = 2 if lib.__name__.startswith("dattri_llm_b200") else C5_TEST_MB
     target = _c5_target(lib, model, hc, dev, vocab, n_test=n_test, test_mb=test_mb)
     args = lib.AttributionArguments(output_dir=tempfile.mkdtemp(), per_device_train_batch_size=C5_MB,
                                     learning_rate=1e-5, dataloader_pin_memory=dev.type == "cuda")
@@ -867,7 +871,7 @@ def main_c5(a, rank, world, local):
                 "method": (f"LESS-style Adam-preconditioned masked captures of every in_proj/out_proj "
                            f"(k={C5_MASK} per linear, {2 * cfg.num_hidden_layers * C5_MASK} in all) + "
                            "OptimizerStateCallback + online DataSelectionCallback (fixed target: mean of "
-                           f"{C5_NTEST} test sequences; bottom {int(C5_DROP * 100)} % of each step's pool "
+                           f"{C5_TARGET_SEQS} test sequences; bottom {int(C5_DROP * 100)} % of each step's pool "
                            "micro-batch dropped), AdamW trajectory"),
                 "timed": "K trajectory steps of the public GradientStreamer",
                 "l2": "per-step parameter traffic (5.4 GB bf16 + optimizer state) exceeds the 126 MB L2"}

@@ -6,10 +6,12 @@ reducing them -- 40 GB per layer for four 2,048-token sequences of the 2.7B arch
 so training runs out of memory at any useful batch.  :func:`ssd_chunked` computes the same
 chunked SSD (Dao & Gu 2024, "Transformers are SSMs", Listing 1) as batched matrix
 products: per chunk, the causal ``(C B^T) . L`` mixing applied to ``x dt``, per-chunk end
-states, the inter-chunk recurrence, and the states' contribution to each position.  Its
-largest intermediate is one ``(batch, heads, chunks, chunk, chunk)`` fp32 tensor, and in a
-training step the scan is recomputed in the backward, so only its inputs are kept per
-layer.
+states, the inter-chunk recurrence, and the states' contribution to each position.  The
+products that involve only B and C are formed once per group (Mamba2-2.7B has one group for
+its 80 heads), not once per head, and each head's intra-chunk decay is one exponential of
+cumulative-sum differences.  Its largest intermediate is one ``(batch, heads, chunks, chunk,
+chunk)`` fp32 tensor; above 2,048 tokens per call the scan is recomputed in the backward,
+so only its inputs are kept per layer.
 
 :func:`accelerate_mamba2` installs that forward on every ``Mamba2Mixer`` of a model (the
 cache-free training / scoring call; decoding keeps the library's path) and moves the
@@ -32,13 +34,22 @@ from dattri_llm_b200.models.layers import tc_linearize
 
 def _segment_sums(a: torch.Tensor) -> torch.Tensor:
     """``out[..., i, j] = a[..., j+1] + ... + a[..., i]`` for ``i >= j`` (``-inf`` above the
-    diagonal): the log-decay from position ``j`` to ``i`` of one chunk.  Summed as a masked
-    cumulative sum, so no large cumulative values are subtracted."""
+    diagonal): the log-decay from position ``j`` to ``i``.  Summed as a masked cumulative sum,
+    so no large cumulative values are subtracted (used across chunks, where the totals grow)."""
     n = a.shape[-1]
     lower = torch.ones(n, n, dtype=torch.bool, device=a.device).tril(-1)
     spread = a[..., None].expand(*a.shape, n).masked_fill(~lower, 0)
     sums = spread.cumsum(dim=-2)
     return sums.masked_fill(~torch.ones(n, n, dtype=torch.bool, device=a.device).tril(), float("-inf"))
+
+
+def _causal_decay(cum: torch.Tensor) -> torch.Tensor:
+    """``exp(cum[..., i] - cum[..., j])`` for ``i >= j``, 0 above the diagonal: the decay from
+    position ``j`` to ``i`` inside one chunk, from the chunk's cumulative log-decay (one pass;
+    within a chunk the cumulative values stay small enough for the difference)."""
+    n = cum.shape[-1]
+    upper = torch.ones(n, n, dtype=torch.bool, device=cum.device).triu(1)
+    return (cum[..., :, None] - cum[..., None, :]).masked_fill_(upper, float("-inf")).exp_()
 
 
 def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torch.Tensor, c: torch.Tensor,
@@ -49,13 +60,17 @@ def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torc
         x: ``(batch, length, heads, head_dim)``.
         dt: ``(batch, length, heads)``, already softplus'ed and clamped.
         a_head: ``(heads,)``, negative.
-        b, c: ``(batch, length, heads, state)``.
+        b, c: ``(batch, length, groups, state)``; ``heads`` is a multiple of ``groups`` and
+            head ``h`` reads group ``h // (heads // groups)``.  The group-level products
+            (``C B^T``, ``C`` against the states) are formed once per group, not per head.
         chunk: chunk length.
 
     Returns:
         ``(batch, length, heads, head_dim)``.
     """
-    bsz, length, heads, _hd = x.shape
+    bsz, length, heads, hd = x.shape
+    groups = b.shape[2]
+    rep = heads // groups
     pad = (-length) % chunk
     xdt = x * dt[..., None]
     log_a = a_head * dt  # (batch, length, heads)
@@ -63,39 +78,37 @@ def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torc
         xdt, b, c = (F.pad(t, (0, 0, 0, 0, 0, pad)) for t in (xdt, b, c))
         log_a = F.pad(log_a, (0, 0, 0, pad))
     n_chunks = (length + pad) // chunk
-
-    def chunked(t):  # (batch, length, ...) -> (batch, chunks, chunk, ...)
-        return t.reshape(bsz, n_chunks, chunk, *t.shape[2:])
-
-    xdt, b, c = chunked(xdt), chunked(b), chunked(c)
-    log_a = chunked(log_a).permute(0, 3, 1, 2)          # (batch, heads, chunks, chunk)
-    cum = log_a.cumsum(dim=-1)
-    # 1. within each chunk: causal (C B^T) . decay, applied to x dt
-    mix = torch.einsum("bcihn,bcjhn->bhcij", c, b) * torch.exp(_segment_sums(log_a))
-    y = torch.einsum("bhcij,bcjhp->bcihp", mix, xdt)
-    del mix
-    # 2. each chunk's end state from its own inputs
-    to_end = torch.exp(cum[..., -1:] - cum)              # (batch, heads, chunks, chunk)
-    b_weighted = b * to_end.permute(0, 2, 3, 1)[..., None]
-    states = torch.einsum("bcjhn,bcjhp->bchpn", b_weighted, xdt)
+    xdt = xdt.reshape(bsz, n_chunks, chunk, groups, rep, hd)
+    b = b.reshape(bsz, n_chunks, chunk, groups, -1)
+    c = c.reshape(bsz, n_chunks, chunk, groups, -1)
+    cum = log_a.reshape(bsz, n_chunks, chunk, groups, rep).permute(0, 3, 4, 1, 2).cumsum(dim=-1)  # (b,g,r,c,s)
+    # 1. within each chunk: (C B^T) per group, times each head's causal decay, applied to x dt
+    cb = torch.einsum("bcsgn,bctgn->bgcst", c, b)
+    mix = cb[:, :, None] * _causal_decay(cum)                          # (b, g, r, c, s, t)
+    y = torch.einsum("bgrcst,bctgrp->bcsgrp", mix, xdt)
+    del mix, cb
+    # 2. each chunk's end state from its own inputs (the decay applied to x dt, not to B)
+    to_end = torch.exp(cum[..., -1:] - cum)                            # (b, g, r, c, s)
+    states = torch.einsum("bctgrp,bctgn->bcgrpn", xdt * to_end.permute(0, 3, 4, 1, 2)[..., None], b)
     # 3. carry states across chunk boundaries
     states = torch.cat([torch.zeros_like(states[:, :1]), states], dim=1)
-    across = torch.exp(_segment_sums(F.pad(cum[..., -1], (1, 0))))  # (batch, heads, chunks+1, chunks+1)
-    states = torch.einsum("bhzc,bchpn->bzhpn", across, states)[:, :-1]
+    across = torch.exp(_segment_sums(F.pad(cum[..., -1], (1, 0))))    # (b, g, r, c+1, c+1)
+    states = torch.einsum("bgrzc,bcgrpn->bzgrpn", across, states)[:, :-1]
     # 4. the incoming state's contribution to every position of the chunk
-    from_start = torch.exp(cum).permute(0, 2, 3, 1)     # (batch, chunks, chunk, heads)
-    y = y + torch.einsum("bcihn,bchpn->bcihp", c, states) * from_start[..., None]
-    y = y.reshape(bsz, n_chunks * chunk, heads, -1)
+    from_start = torch.exp(cum).permute(0, 3, 4, 1, 2)[..., None]      # (b, c, s, g, r, 1)
+    y = y + torch.einsum("bcsgn,bcgrpn->bcsgrp", c, states) * from_start
+    y = y.reshape(bsz, n_chunks * chunk, heads, hd)
     return y[:, :length] if pad else y
 
 
 def _scan_with_skip(x, dt, a_head, b_groups, c_groups, d_skip, chunk: int) -> torch.Tensor:
-    """``ssd_chunked(...) + D x`` with B and C given per group ``(batch, length, groups, state)``
-    and widened to the heads here (recomputed in the backward, so never kept)."""
-    heads = x.shape[2]
-    b = b_groups.repeat_interleave(heads // b_groups.shape[2], dim=2)
-    c = c_groups.repeat_interleave(heads // c_groups.shape[2], dim=2)
-    return ssd_chunked(x, dt, a_head, b, c, chunk) + d_skip[:, None] * x
+    """``ssd_chunked(...) + D x`` with B and C given per group ``(batch, length, groups, state)``."""
+    return ssd_chunked(x, dt, a_head, b_groups, c_groups, chunk) + d_skip[:, None] * x
+
+
+# A scan over more tokens than this keeps only its inputs and is recomputed in the backward;
+# below it the (chunk x chunk) intermediates of all layers fit next to the model.
+_RECOMPUTE_TOKENS = 2048
 
 
 def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attention_mask=None, **kwargs):
@@ -119,7 +132,7 @@ def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attenti
     b = b.reshape(bsz, length, self.n_groups, self.ssm_state_size).float()
     c = c.reshape(bsz, length, self.n_groups, self.ssm_state_size).float()
     args = (x, dt, a_head, b, c, self.D, self.chunk_size)
-    if torch.is_grad_enabled():
+    if torch.is_grad_enabled() and bsz * length > _RECOMPUTE_TOKENS:
         # the scan's (chunk x chunk) intermediates are rebuilt in the backward instead of
         # being kept for all layers at once: only the scan's inputs stay alive
         y = checkpoint(_scan_with_skip, *args, use_reentrant=False)
