@@ -729,7 +729,7 @@ def main_c4(a, rank, world, local):
         if world > 1:
             from dattri_llm_b200.parallel.moe import expert_parallelize
 
-            expert_parallelize(model, max_tokens=C4_MB * C4_SEQ)
+            expert_parallelize(model, max_tokens=max(C4_MB, C4_NTEST) * C4_SEQ)  # the query batch too
         n0 = native_ops.launch_count()
         ms, clk, host = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
                                   expert_parallel=world > 1)

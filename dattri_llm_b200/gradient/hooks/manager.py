@@ -29,6 +29,8 @@ gate/up read one projection) is cleared with the buffers.
 
 from __future__ import annotations
 
+import sys
+
 import threading
 import warnings
 from collections.abc import Callable, Generator, Iterable
@@ -714,6 +716,19 @@ class HookManager:
         mixers = find_sequence_mixers(root)
         if mixers:
             self._reverts.extend(install_sequence_mixer_forward(root, list(mixers), lambda: self._collecting))
+        self._bind_expert_parallel(root)
+
+    def _bind_expert_parallel(self, root: nn.Module) -> None:
+        """Let every fused expert-parallel block take its expert taps' captures itself (the
+        grouped capture inside the peer-memory kernels) when the captures allow it."""
+        if "dattri_llm_b200.parallel.moe" not in sys.modules:
+            return  # no expert-parallel block can exist
+        from dattri_llm_b200.parallel.moe import EPGroupedCapture, ExpertParallelMoE
+
+        for name, mod in root.named_modules():
+            if isinstance(mod, ExpertParallelMoE) and mod.fused:
+                mod.grouped_capture = EPGroupedCapture(self, name, mod)
+                self._reverts.append(lambda m=mod: setattr(m, "grouped_capture", None))
 
     def register(self) -> None:
         """Install every hook and override (idempotent)."""

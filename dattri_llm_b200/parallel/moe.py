@@ -283,9 +283,11 @@ class _DownA2A(torch.autograd.Function):
         return (d_act, d_topv, None, None, None, None, *taps)
 
 
-class _EPMoE(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x2, topv, topi, mod):
+class _Routed:
+    """One fused call's routing: the receive layout, this rank's owner-side ragged-GEMM tables
+    and the rows it received (read once on the host, to size the expert buffers)."""
+
+    def __init__(self, mod: ExpertParallelMoE, x2: torch.Tensor, topi: torch.Tensor) -> None:
         from dattri_llm_b200 import ops
 
         t, k = topi.shape
@@ -299,85 +301,253 @@ class _EPMoE(torch.autograd.Function):
         # int32 scratch: [counts | cursor | tile_prefix | base | len | total]
         work = torch.zeros(2 * n_exp + 3 * e_l + 2, dtype=torch.int32, device=dev)
         counts, cursor = work[:n_exp], work[n_exp:2 * n_exp]
-        prefix = work[2 * n_exp:2 * n_exp + e_l + 1]
-        base = work[2 * n_exp + e_l + 1:2 * n_exp + 2 * e_l + 1]
-        lens = work[2 * n_exp + 2 * e_l + 1:2 * n_exp + 3 * e_l + 1]
-        rows_dev = work[2 * n_exp + 3 * e_l + 1:]
+        self.prefix = work[2 * n_exp:2 * n_exp + e_l + 1]
+        self.base = work[2 * n_exp + e_l + 1:2 * n_exp + 2 * e_l + 1]
+        self.lens = work[2 * n_exp + 2 * e_l + 1:2 * n_exp + 3 * e_l + 1]
+        self.rows_dev = work[2 * n_exp + 3 * e_l + 1:]
         ops.count_launch()
         ops.native().moe_count(topi, counts)
         all_counts = torch.empty(world, n_exp, dtype=torch.int32, device=dev)
         dist.all_gather_into_tensor(all_counts, counts, group=mod.group)  # the control plane
-        dest32 = torch.empty(rows, dtype=torch.int32, device=dev)
-        row32 = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.dest = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.row = torch.empty(rows, dtype=torch.int32, device=dev)
         ops.count_launch()
-        ops.native().moe_place(topi, all_counts, rank, e_l, cursor, dest32, row32, prefix, base, lens, rows_dev)
-
+        ops.native().moe_place(topi, all_counts, rank, e_l, cursor, self.dest, self.row, self.prefix, self.base,
+                               self.lens, self.rows_dev)
         mod.barrier.wait()  # every rank is done with the previous use of the receive buffers
         ops.count_launch()
-        ops.native().moe_dispatch(x2, k, dest32, row32, mod.recv_x.peers, mod.recv_meta.peers, rank)
+        ops.native().moe_dispatch(x2, k, self.dest, self.row, mod.recv_x.peers, mod.recv_meta.peers, rank)
         mod.barrier.wait()  # every row has landed
         # One host read per layer (it sizes the expert buffers exactly); the dispatch above is
         # already queued, so the GPU stays busy while the host waits.
-        total_in = int(rows_dev.item())
-        max_tiles = (total_in + 255) // 256 + e_l  # 256-row blocks of the ragged GEMM
+        self.total_in = int(self.rows_dev.item())
+        self.max_tiles = (self.total_in + 255) // 256 + e_l  # 256-row blocks of the ragged GEMM
+        self.t, self.k = t, k
 
+    def owners_forward(self, mod: ExpertParallelMoE) -> tuple[torch.Tensor, torch.Tensor]:
+        """Experts' gate/up (``h``), SwiGLU (``a``) and down projection of the received rows; the
+        down GEMM's epilogue stores every output row into its source's combine buffer."""
+        from dattri_llm_b200 import ops
+
+        dev = mod.recv_x.local.device
+        n = self.total_in
         err = ops.error_word(dev)
-        h = torch.empty(max(total_in, 1), 2 * mod.intermediate, dtype=torch.bfloat16, device=dev)
-        a = torch.empty(max(total_in, 1), mod.intermediate, dtype=torch.bfloat16, device=dev)
-        if total_in:
-            xin = mod.recv_x.local[:total_in]
+        h = torch.empty(max(n, 1), 2 * mod.intermediate, dtype=torch.bfloat16, device=dev)
+        a = torch.empty(max(n, 1), mod.intermediate, dtype=torch.bfloat16, device=dev)
+        if n:
             ops.count_launch(3)
-            ops.native().gemm_ragged(xin, mod.gate_up, h, prefix, base, lens, max_tiles, [], None, err)
-            ops.native().swiglu_split(h, a, rows_dev)
-            # The down GEMM stores every output row back into its source rank's combine buffer.
-            ops.native().gemm_ragged(a[:total_in], mod.down, None, prefix, base, lens, max_tiles,
-                                     mod.combine.peers, mod.recv_meta.local[:total_in], err)
-        mod.barrier.wait()  # every output row is home
-        w = topv.float().contiguous()
-        slots = mod.combine.local[:t * k]
-        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
-            slots = slots.clone()  # the combine buffer is reused by the next layer
-        y = torch.empty(t, mod.hidden, dtype=torch.bfloat16, device=dev)
+            ops.native().gemm_ragged(mod.recv_x.local[:n], mod.gate_up, h, self.prefix, self.base, self.lens,
+                                     self.max_tiles, [], None, err)
+            ops.native().swiglu_split(h, a, self.rows_dev)
+            ops.native().gemm_ragged(a[:n], mod.down, None, self.prefix, self.base, self.lens, self.max_tiles,
+                                     mod.combine.peers, mod.recv_meta.local[:n], err)
+        return h, a
+
+    def dispatch_grads(self, mod: ExpertParallelMoE, dy: torch.Tensor, slots: torch.Tensor,
+                       w: torch.Tensor) -> torch.Tensor:
+        """Backward of the combine: router-weight gradients, and every slot's gradient stored
+        into its owner's receive buffer (one kernel); returns ``d topv`` (fp32)."""
+        from dattri_llm_b200 import ops
+
+        dtopv = torch.empty(self.t, self.k, dtype=torch.float32, device=dy.device)
+        mod.barrier.wait()
         ops.count_launch()
-        ops.native().moe_combine(slots, w, y)
-        ctx.mod = mod
-        ctx.save_for_backward(w, slots, dest32, row32, h, prefix, base, lens, rows_dev)
-        ctx.total_in, ctx.max_tiles, ctx.topv_dtype = total_in, max_tiles, topv.dtype
+        ops.native().moe_combine_bwd_dispatch(dy, slots, w, dtopv, self.dest, self.row, mod.recv_x.peers,
+                                              mod.recv_meta.peers, mod.rank)
+        mod.barrier.wait()
+        return dtopv
+
+    def owners_backward(self, mod: ExpertParallelMoE, h: torch.Tensor) -> torch.Tensor | None:
+        """Owner side of the backward: the experts' input gradient of the received slot
+        gradients, returned to the sources' ``dx_slots`` from the GEMM epilogue; returns the
+        gate/up output gradient ``dh`` of the received rows (``None`` with no rows)."""
+        from dattri_llm_b200 import ops
+
+        n = self.total_in
+        if not n:
+            return None
+        err = ops.error_word(h.device)
+        dout = mod.recv_x.local[:n]
+        da = torch.empty(n, mod.intermediate, dtype=torch.bfloat16, device=h.device)
+        dh = torch.empty_like(h[:n])
+        ops.count_launch(3)
+        ops.native().gemm_ragged(dout, mod.down_t, da, self.prefix, self.base, self.lens, self.max_tiles, [], None,
+                                 err)
+        ops.native().swiglu_split_bwd(da, h[:n].contiguous(), dh, self.rows_dev)
+        ops.native().gemm_ragged(dh, mod.gate_up_t, None, self.prefix, self.base, self.lens, self.max_tiles,
+                                 mod.dx_slots.peers, mod.recv_meta.local[:n], err)
+        return dh
+
+    def return_rows(self, mod: ExpertParallelMoE, rows: torch.Tensor, buf) -> None:
+        """Store received row r of *rows* into its source rank's symmetric *buf* at its slot
+        (the origin the dispatch recorded), 16-byte peer stores."""
+        from dattri_llm_b200 import ops
+
+        n = self.total_in
+        if not n:
+            return
+        meta = mod.recv_meta.local[:n]
+        ops.count_launch()
+        ops.native().moe_dispatch(rows.contiguous(), 1, meta[:, 0].contiguous(), meta[:, 1].contiguous(), buf.peers,
+                                  [], mod.rank)
+
+    def combine_dx(self, mod: ExpertParallelMoE, w: torch.Tensor) -> torch.Tensor:
+        """``dx[t] = sum_j dx_slots[t * k + j]`` once every row is home."""
+        from dattri_llm_b200 import ops
+
+        dx = torch.empty(self.t, mod.hidden, dtype=torch.bfloat16, device=w.device)
+        ops.count_launch()
+        ops.native().moe_combine(mod.dx_slots.local[:self.t * self.k], torch.ones_like(w), dx)
+        return dx
+
+
+def _combine(mod: ExpertParallelMoE, topv: torch.Tensor, t: int, k: int, keep: bool):
+    """``y`` from the combine buffer (router-weighted sum of the k returned rows) plus the fp32
+    weights and the slot rows (a copy when *keep*: the buffer is reused by the next layer)."""
+    from dattri_llm_b200 import ops
+
+    w = topv.float().contiguous()
+    slots = mod.combine.local[:t * k]
+    if keep:
+        slots = slots.clone()
+    y = torch.empty(t, mod.hidden, dtype=torch.bfloat16, device=w.device)
+    ops.count_launch()
+    ops.native().moe_combine(slots, w, y)
+    return y, w, slots
+
+
+class _EPMoE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2, topv, topi, mod):
+        rt = _Routed(mod, x2, topi)
+        h, _a = rt.owners_forward(mod)
+        mod.barrier.wait()  # every output row is home
+        y, w, slots = _combine(mod, topv, rt.t, rt.k, ctx.needs_input_grad[0] or ctx.needs_input_grad[1])
+        ctx.mod, ctx.rt, ctx.topv_dtype = mod, rt, topv.dtype
+        ctx.save_for_backward(w, slots, h)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        from dattri_llm_b200 import ops
+        mod, rt = ctx.mod, ctx.rt
+        w, slots, h = ctx.saved_tensors
+        dtopv = rt.dispatch_grads(mod, dy.to(torch.bfloat16).contiguous(), slots, w)
+        rt.owners_backward(mod, h)
+        mod.barrier.wait()
+        return rt.combine_dx(mod, w), dtopv.to(ctx.topv_dtype), None, None
 
-        mod = ctx.mod
-        w, slots, dest32, row32, h, prefix, base, lens, rows_dev = ctx.saved_tensors
-        t, k = w.shape
-        dev = dy.device
+
+class _EPGroupedMoE(torch.autograd.Function):
+    """The fused expert-parallel block with the grouped capture of every expert projection.
+
+    Per-sample capture needs four factors per routed row: the gate/up input (the token's own
+    hidden state) and the down projection's output gradient (``w * dy`` of the slot) are on the
+    source rank already and are projected there; the down input (the SwiGLU output) and the
+    gate/up output gradient exist only at the expert's owner, which projects them and stores
+    the ``k``-wide rows back into the source's symmetric buffer at their slot (the origin the
+    dispatch recorded), so only ``k`` columns per row cross NVLink.  Each source then forms
+    every (expert, sample)'s ``sum_t g_p^T a_p`` over its own slots in one batched GEMM and
+    hands the ``(E, B, k_g * k_a)`` blocks to the capture manager under the taps' names."""
+
+    @staticmethod
+    def forward(ctx, x2, topv, topi, mod, block, batch, tokens):
+        pm = block.matrices
+        rt = _Routed(mod, x2, topi)
+        h, a = rt.owners_forward(mod)
+        a_buf = mod.capture_rows(pm["down_a"].proj_dim)
+        if rt.total_in:
+            rt.return_rows(mod, pm["down_a"](a[:rt.total_in]), a_buf)
+        mod.barrier.wait()  # every output row and projected down input is home
+        y, w, slots = _combine(mod, topv, rt.t, rt.k, True)
+        n = rt.t * rt.k
+        a_down = a_buf.local[:n].clone()
+        slot_tok = torch.div(torch.arange(n, device=x2.device), rt.k, rounding_mode="floor")
+        a_up = pm["up_a"](x2).index_select(0, slot_tok)
+        ctx.mod, ctx.rt, ctx.block, ctx.topv_dtype = mod, rt, block, topv.dtype
+        ctx.shape = (batch, tokens)
+        ctx.save_for_backward(w, slots, h, a_up, a_down, topi.reshape(-1), slot_tok)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from dattri_llm_b200.gradient.hooks.override_layers.grouped_experts import _NativeKernels, _per_sample_outer
+
+        mod, rt, block = ctx.mod, ctx.rt, ctx.block
+        w, slots, h, a_up, a_down, experts, slot_tok = ctx.saved_tensors
+        pm = block.matrices
         dy = dy.to(torch.bfloat16).contiguous()
-        dtopv = torch.empty(t, k, dtype=torch.float32, device=dev)
-        mod.barrier.wait()
-        ops.count_launch()
-        # router-weight gradient and the slot gradients' dispatch to the owners in one kernel
-        ops.native().moe_combine_bwd_dispatch(dy, slots, w, dtopv, dest32, row32, mod.recv_x.peers,
-                                              mod.recv_meta.peers, mod.rank)
-        mod.barrier.wait()
-        total_in = ctx.total_in
-        if total_in:
-            err = ops.error_word(dev)
-            dout = mod.recv_x.local[:total_in]
-            da = torch.empty(total_in, mod.intermediate, dtype=torch.bfloat16, device=dev)
-            dh = torch.empty_like(h[:total_in])
-            ops.count_launch(3)
-            ops.native().gemm_ragged(dout, mod.down_t, da, prefix, base, lens, ctx.max_tiles, [], None, err)
-            ops.native().swiglu_split_bwd(da, h[:total_in].contiguous(), dh, rows_dev)
-            # The input-gradient GEMM returns every row to its source rank.
-            ops.native().gemm_ragged(dh, mod.gate_up_t, None, prefix, base, lens, ctx.max_tiles,
-                                     mod.dx_slots.peers, mod.recv_meta.local[:total_in], err)
-        mod.barrier.wait()
-        dx = torch.empty(t, mod.hidden, dtype=torch.bfloat16, device=dev)
-        ops.count_launch()
-        ops.native().moe_combine(mod.dx_slots.local[:t * k], torch.ones_like(w), dx)  # sum of the k slots
-        return dx, dtopv.to(ctx.topv_dtype), None, None
+        dtopv = rt.dispatch_grads(mod, dy, slots, w)
+        dh = rt.owners_backward(mod, h)
+        g_buf = mod.capture_rows(pm["up_g"].proj_dim)
+        if dh is not None:
+            rt.return_rows(mod, pm["up_g"](dh), g_buf)
+        mod.barrier.wait()  # every input-gradient row and projected gate/up gradient is home
+        dx = rt.combine_dx(mod, w)
+        n = rt.t * rt.k
+        g_up = g_buf.local[:n].clone()
+        g_slots = (w[..., None] * dy.float()[:, None, :]).to(torch.bfloat16).reshape(n, -1)
+        g_down = pm["down_g"](g_slots)
+        batch, tokens = ctx.shape
+        plan = _SlotPlan(experts, slot_tok, mod.n_experts, batch, tokens)
+        dense_up = _per_sample_outer(g_up, a_up, plan, _NativeKernels)
+        dense_down = _per_sample_outer(g_down, a_down, plan, _NativeKernels)
+        block.deliver(dense_up, dense_down, dy.device)
+        return dx, dtopv.to(ctx.topv_dtype), None, None, None, None, None
+
+
+class _SlotPlan:
+    """Where each of this rank's slot rows sits in the token-major per-(expert, sample)
+    layout of the batched outer product: segment ``expert * batch + sample``, position the
+    token within its sample (unique: a token's k slots go to k different experts)."""
+
+    def __init__(self, experts: torch.Tensor, slot_tok: torch.Tensor, n_experts: int, batch: int,
+                 tokens: int) -> None:
+        self.n_experts, self.batch, self.tokens = n_experts, batch, tokens
+        self.segment = experts * batch + torch.div(slot_tok, tokens, rounding_mode="floor")
+        self.position = slot_tok % tokens
+
+
+class EPGroupedCapture:
+    """Binds one :class:`ExpertParallelMoE` to a capture manager (*host*) for the grouped
+    capture: the manager answers :meth:`grouped_matrices` for the block's expert taps and
+    takes each backward's per-expert blocks through :meth:`grouped_backward`, as for a
+    replicated fused-experts block (``gradient/hooks/override_layers/grouped_experts.py``)."""
+
+    def __init__(self, host, name: str, mod: ExpertParallelMoE) -> None:
+        self.host, self.name, self.mod = host, name, mod
+        prefix = f"{name}.experts.dattri_experts" if name else "experts.dattri_experts"
+        self.up_names = [f"{prefix}.{e}.gate_up" for e in range(mod.n_experts)]
+        self.down_names = [f"{prefix}.{e}.down" for e in range(mod.n_experts)]
+        self.experts = _ExpertShapes(mod)
+        self.matrices: dict = {}
+
+    def try_forward(self, x: torch.Tensor, x2: torch.Tensor, topv: torch.Tensor,
+                    topi: torch.Tensor) -> torch.Tensor | None:
+        """The block's output through the grouped path, or ``None`` when the captures do not
+        allow it (the caller then runs the all-to-all form)."""
+        if x.ndim != 3 or x2.dtype != torch.bfloat16 or not x2.is_cuda:
+            return None
+        batch, tokens = int(x.shape[0]), int(x.shape[1])
+        matrices = self.host.grouped_matrices(self, x2, tokens)
+        if matrices is None or any(m.proj_dim % 8 for m in matrices.values()):
+            return None
+        self.matrices = matrices
+        self.host.grouped_forward(self)
+        return _EPGroupedMoE.apply(x2, topv, topi, self.mod, self, batch, tokens)
+
+    def deliver(self, dense_up: torch.Tensor, dense_down: torch.Tensor, device: torch.device) -> None:
+        """Hand the ``(E, B, k_g * k_a)`` results of one backward to the manager."""
+        parts = dict(zip(self.up_names, dense_up.unbind(0)))
+        parts.update(zip(self.down_names, dense_down.unbind(0)))
+        self.host.grouped_backward(self, parts, device)
+
+
+class _ExpertShapes:
+    """The expert weight shapes the manager's checks read (``gate_up_proj (E, 2I, H)``,
+    ``down_proj (E, H, I)``; the leading axis is this rank's share)."""
+
+    def __init__(self, mod: ExpertParallelMoE) -> None:
+        self.gate_up_proj, self.down_proj = mod.gate_up, mod.down
 
 
 class _Buffers:
@@ -392,6 +562,17 @@ class _Buffers:
         self.combine = SymmetricBuffer((slots, hidden), torch.bfloat16, dev, group)
         self.dx_slots = SymmetricBuffer((slots, hidden), torch.bfloat16, dev, group)
         self.barrier = PeerBarrier(dev, group)
+        self.slots, self.dev, self.group = slots, dev, group
+        self.capture: dict[int, SymmetricBuffer] = {}
+
+    def capture_rows(self, width: int) -> SymmetricBuffer:
+        """A ``(slots, width)`` bf16 symmetric buffer for projected rows returned to their
+        sources; created on first use (every rank reaches the same layer call, so the
+        allocation is collective)."""
+        buf = self.capture.get(width)
+        if buf is None:
+            buf = self.capture[width] = SymmetricBuffer((self.slots, width), torch.bfloat16, self.dev, self.group)
+        return buf
 
     @classmethod
     def get(cls, capacity: int, slots: int, hidden: int, dev: torch.device, group) -> _Buffers:
@@ -405,9 +586,12 @@ class ExpertParallelMoE(nn.Module):
     """Top-k MoE MLP with experts sharded over the process group (frozen experts: the
     attribution probe's case; the router may train).  Build collectively.
 
-    On CUDA in bf16 the forward is the fused peer-memory path above; while any of its
-    ``experts.dattri_experts`` taps is hooked for capture, and on other devices or dtypes, it is
-    the two-stage all-to-all form (``torch.distributed`` all-to-all, any backend)."""
+    On CUDA in bf16 the forward is the fused peer-memory path above.  While its
+    ``experts.dattri_experts`` taps are hooked by a capture manager that allows the grouped
+    capture (one LoGra projection per side, materialized), it is the same fused path with the
+    captures taken inside it (:class:`_EPGroupedMoE`); under other captures, and on other
+    devices or dtypes, it is the two-stage all-to-all form (``torch.distributed`` all-to-all,
+    any backend)."""
 
     def __init__(self, hidden: int, intermediate: int, n_experts: int, top_k: int, *, max_tokens: int,
                  norm_topk_prob: bool = False, group=None, device: torch.device | None = None,
@@ -441,6 +625,8 @@ class ExpertParallelMoE(nn.Module):
             bufs = _Buffers.get(self.capacity, max_tokens * top_k, hidden, dev, group)
             self.recv_x, self.recv_meta = bufs.recv_x, bufs.recv_meta
             self.combine, self.dx_slots, self.barrier = bufs.combine, bufs.dx_slots, bufs.barrier
+            self.capture_rows = bufs.capture_rows
+        self.grouped_capture: EPGroupedCapture | None = None  # set by a capture manager
 
     @property
     def dattri_experts(self) -> nn.ModuleList:
@@ -480,9 +666,12 @@ class ExpertParallelMoE(nn.Module):
         xd = x.to(self.dtype)
         topv, topi = self.route(xd)
         x2 = xd.reshape(-1, self.hidden).contiguous()
+        y = None
         if self.fused and not self.capturing():
             y = _EPMoE.apply(x2, topv, topi, self)
-        else:
+        elif self.fused and self.grouped_capture is not None and torch.is_grad_enabled():
+            y = self.grouped_capture.try_forward(xd, x2, topv, topi)
+        if y is None:
             y = self._all_to_all(x2, topv, topi, tuple(shape[:-1]))
         return y.view(*shape[:-1], self.hidden)
 

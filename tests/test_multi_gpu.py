@@ -297,6 +297,89 @@ def test_expert_parallel_capture_matches_replicated_over_nccl():
     assert max(errs.values()) < 1e-3, errs
 
 
+def _ep_grouped_worker(rank: int, world: int, port: int, results) -> None:
+    """bf16 OLMoE block with LoGra 16 x 16 materialized expert captures: the fused
+    expert-parallel path with the grouped capture against the replicated-expert grouped
+    capture of the same rank's samples."""
+    import copy
+    import datetime
+    import warnings
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import transformers
+
+        import dattri_llm_b200 as bw
+        from dattri_llm_b200 import ops
+        from dattri_llm_b200.parallel.moe import ExpertTap, expert_parallelize
+
+        cfg = transformers.OlmoeConfig(vocab_size=96, hidden_size=128, intermediate_size=64, num_hidden_layers=1,
+                                       num_attention_heads=4, num_key_value_heads=4, num_experts=8,
+                                       num_experts_per_tok=2, max_position_embeddings=64)
+        torch.manual_seed(0)
+        model = transformers.OlmoeForCausalLM(cfg).to(dev, torch.bfloat16).eval()
+        model.requires_grad_(False)
+        model.get_input_embeddings().requires_grad_(True)
+        ep_model = copy.deepcopy(model)
+        expert_parallelize(ep_model, max_tokens=64)
+        ids = torch.randint(0, 96, (3, 16), generator=torch.Generator().manual_seed(11 + rank)).to(dev)
+        proj = {"__default__": {"style": "logra", "proj_dim": 16, "proj_type": "rademacher", "proj_seed": 0}}
+        taps = {"n": 0}
+        for m in ep_model.modules():
+            if isinstance(m, ExpertTap):
+                m.register_forward_hook(lambda *_: taps.__setitem__("n", taps["n"] + 1))
+
+        def capture(m, **kw):
+            cap = bw.CaptureCallback()
+            hc = bw.HookManagerConfig(linear_io=[r"\.mlp\.(experts|gate)$", r"dattri_(experts|router)"],
+                                      projection_kwargs=proj, capture_style="auto", include_frozen=True)
+            hm = bw.HookManager(m, hc, callbacks=[cap], **kw)
+            with warnings.catch_warnings():
+                warnings.simplefilter("ignore")
+                with hm.collect():
+                    logits = m(input_ids=ids).logits
+                    F.cross_entropy(logits[:, :-1].reshape(-1, 96).float(), ids[:, 1:].reshape(-1),
+                                    reduction="sum").backward()
+            hm.remove()
+            return {n: v.float() for n, v in cap.record.gradient.data.items()}
+
+        want = capture(model, moe_routed_layers=["model.layers.0.mlp"])
+        got = capture(ep_model)
+        ops.check_device_errors(dev)
+        names = [n for n in want if ".dattri_experts." in n]
+        worst = 0.0 if (set(got) == set(want) and len(names) == 16 and taps["n"] == 0) else float("inf")
+        for n in names:
+            a, b = got[n].reshape(got[n].shape[0], -1), want[n].reshape(want[n].shape[0], -1)
+            if b.abs().max() == 0:
+                worst = max(worst, float(a.abs().max()))
+                continue
+            worst = max(worst, float((a - b).norm() / b.norm()))
+        torch.cuda.synchronize()
+        results[rank] = (worst, taps["n"], sorted(set(got) ^ set(want))[:4])
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_expert_parallel_grouped_capture_matches_replicated(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_ep_grouped_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        errs = dict(results)
+    assert len(errs) == world
+    assert max(e[0] for e in errs.values()) < 3e-2, errs
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_sharded_linear_fused_collectives_match_dense():
     world = 2
