@@ -25,6 +25,7 @@
 #include "moe_ep.cuh"
 #include "norm_grad.cuh"
 #include "embed_grad.cuh"
+#include "gated_norm.cuh"
 
 namespace {
 
@@ -1196,6 +1197,46 @@ Tensor embedding_dense_grad(Tensor keys, Tensor order, Tensor g, int64_t rows) {
   return out;
 }
 
+// Gated RMSNorm (Mamba2 mixer): y (R, D) fp32 contiguous, g (R, D) bf16 with unit column
+// stride, w (D) bf16; returns (out bf16 (R, D), rstd fp32 (R)).
+std::vector<Tensor> gated_rms_fwd(Tensor y, Tensor g, Tensor w, double eps) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.is_contiguous(),
+              "y must be a contiguous (R, D) fp32 CUDA tensor");
+  TORCH_CHECK(g.scalar_type() == torch::kBFloat16 && g.dim() == 2 && g.sizes() == y.sizes() && g.stride(1) == 1,
+              "g must be (R, D) bf16 with unit column stride");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == y.size(1), "w: (D) bf16");
+  TORCH_CHECK(y.size(1) <= bw::kGatedNormMaxCols, "D above the kernel's limit");
+  auto out = torch::empty(y.sizes(), y.options().dtype(torch::kBFloat16));
+  auto rstd = torch::empty({y.size(0)}, y.options());
+  bw::gated_rms_fwd(y.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), g.stride(0),
+                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rstd.data_ptr<float>(), (int)y.size(0),
+                    (int)y.size(1), (float)eps, at::cuda::getCurrentCUDAStream());
+  return {out, rstd};
+}
+
+// Its backward: returns (dy fp32, dg bf16 contiguous, dw fp32).
+std::vector<Tensor> gated_rms_bwd(Tensor dout, Tensor y, Tensor g, Tensor w, Tensor rstd) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  TORCH_CHECK(dout.scalar_type() == torch::kBFloat16 && dout.is_contiguous() && dout.sizes() == y.sizes(),
+              "dout must be contiguous (R, D) bf16");
+  TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.is_contiguous() && g.scalar_type() == torch::kBFloat16 &&
+                  g.sizes() == y.sizes() && g.stride(1) == 1 && w.scalar_type() == torch::kBFloat16 &&
+                  w.numel() == y.size(1) && rstd.scalar_type() == torch::kFloat32 && rstd.numel() == y.size(0),
+              "saved tensors of gated_rms_fwd expected");
+  auto dy = torch::empty_like(y);
+  auto dg = torch::empty(y.sizes(), y.options().dtype(torch::kBFloat16));
+  auto dw = torch::empty({y.size(1)}, y.options());
+  auto part = torch::empty({bw::gated_rms_bwd_parts((int)y.size(0)), y.size(1)}, y.options());
+  bw::gated_rms_bwd(reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), y.data_ptr<float>(),
+                    reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), g.stride(0),
+                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), dy.data_ptr<float>(),
+                    reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), part.data_ptr<float>(), dw.data_ptr<float>(),
+                    (int)y.size(0), (int)y.size(1), at::cuda::getCurrentCUDAStream());
+  return {dy, dg, dw};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
@@ -1212,6 +1253,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
+  m.def("gated_rms_fwd", &gated_rms_fwd, "gated RMSNorm w * rmsnorm(y * silu(g)) (Mamba2 mixer), bf16 out");
+  m.def("gated_rms_bwd", &gated_rms_bwd, "backward of gated_rms_fwd");
   m.def("embedding_dense_grad", &embedding_dense_grad, "dense per-sample embedding gradients, every row written once");
   m.def("gemm_ragged", &gemm_ragged, "ragged grouped GEMM over expert row segments (optionally scattered home)",
         py::arg("A"), py::arg("B3"), py::arg("C"), py::arg("tile_prefix"), py::arg("base"), py::arg("len"),

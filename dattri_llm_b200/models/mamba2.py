@@ -30,6 +30,7 @@ from torch import nn
 from torch.utils.checkpoint import checkpoint
 
 from dattri_llm_b200.models.layers import tc_linearize
+from dattri_llm_b200.ops import fused
 
 
 def _segment_sums(a: torch.Tensor) -> torch.Tensor:
@@ -138,8 +139,14 @@ def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attenti
         y = checkpoint(_scan_with_skip, *args, use_reentrant=False)
     else:
         y = _scan_with_skip(*args)
-    scanned = self.norm(y.reshape(bsz, length, -1), gate)
-    return self.out_proj(scanned.to(dtype))
+    y = y.reshape(bsz, length, -1)
+    norm = self.norm
+    if (dtype == torch.bfloat16 and not (norm._forward_hooks or norm._forward_pre_hooks or norm._backward_hooks)
+            and fused.gated_rms_norm_enabled(y, gate, norm.weight)):
+        scanned = fused.gated_rms_norm(y, gate, norm.weight, norm.variance_epsilon)  # nothing watches the norm
+    else:
+        scanned = norm(y, gate).to(dtype)
+    return self.out_proj(scanned)
 
 
 def accelerate_mamba2(model: nn.Module, *, linears: bool = True) -> int:

@@ -207,3 +207,50 @@ def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
 def linear_cross_entropy(h: torch.Tensor, weight: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     """``sum_i CE(h_i W^T, target_i)`` (targets ``-100`` ignored) without fp32 logits."""
     return _LinearCrossEntropy.apply(h.contiguous(), weight, target.contiguous().long())
+
+
+class _GatedRMSNorm(torch.autograd.Function):
+    """``bf16(w * rmsnorm(y * silu(g)))`` over the last axis (``csrc/gated_norm.cu``): y fp32,
+    g bf16 (a column slice is fine), w bf16; the backward gives dy (fp32), dg (bf16) and dw."""
+
+    @staticmethod
+    def forward(ctx, y, g, w, eps):
+        from dattri_llm_b200.ops import count_launch, native
+
+        lead, d = y.shape[:-1], y.shape[-1]
+        y2 = y.reshape(-1, d).contiguous()
+        g2 = g.reshape(-1, d)
+        if g2.stride(-1) != 1:
+            g2 = g2.contiguous()
+        count_launch()
+        out, rstd = native().gated_rms_fwd(y2, g2, w.contiguous(), float(eps))
+        ctx.save_for_backward(y2, g2, w, rstd)
+        ctx.lead = lead
+        return out.view(*lead, d)
+
+    @staticmethod
+    def backward(ctx, dout):
+        from dattri_llm_b200.ops import count_launch, native
+
+        y2, g2, w, rstd = ctx.saved_tensors
+        d = y2.shape[-1]
+        count_launch(2)
+        dy, dg, dw = native().gated_rms_bwd(dout.reshape(-1, d).to(torch.bfloat16).contiguous(), y2, g2,
+                                            w.contiguous(), rstd)
+        return (dy.view(*ctx.lead, d), dg.view(*ctx.lead, d), dw.to(w.dtype) if ctx.needs_input_grad[2] else None,
+                None)
+
+
+def gated_rms_norm_enabled(y: torch.Tensor, g: torch.Tensor, w: torch.Tensor) -> bool:
+    """Whether :func:`gated_rms_norm` applies: fp32 ``y``, bf16 ``g`` and ``w`` on sm_100,
+    the width within the kernel's limit."""
+    from dattri_llm_b200.ops import use_native
+
+    return (y.dtype == torch.float32 and g.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+            and y.shape == g.shape and y.shape[-1] == w.numel() and y.shape[-1] <= 8192 and use_native(y, g, w))
+
+
+def gated_rms_norm(y: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """``bf16(w * rmsnorm(y * silu(g)))``: the Mamba2 mixer's gated norm and its cast to the
+    model dtype in one kernel each way."""
+    return _GatedRMSNorm.apply(y, g, w, eps)

@@ -243,3 +243,29 @@ def test_embedding_dense_grad_matches_index_add(dtype):
     torch.testing.assert_close(out.float(), ref.reshape(b, vocab * e), rtol=tol, atol=tol)
     via = materialize_factors(ids, g, "nn.Embedding", module_kwargs={"num_embeddings": vocab})
     torch.testing.assert_close(via.float(), out.float(), rtol=0, atol=0)
+
+
+def test_gated_rms_norm_matches_the_mamba2_module():
+    from transformers.models.mamba2.modeling_mamba2 import MambaRMSNormGated
+
+    rows, d = 300, 5120
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    y = torch.randn(rows, d, device="cuda", generator=gen).requires_grad_()
+    proj = torch.randn(rows, d + 64, device="cuda", generator=gen).bfloat16()
+    g = proj[:, 32:32 + d].detach().requires_grad_()  # a column slice, as the mixer's gate is
+    norm = MambaRMSNormGated(d, eps=1e-5).cuda()
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(d, device="cuda", generator=gen))
+    w = norm.weight.detach().bfloat16().requires_grad_()
+    out = fused.gated_rms_norm(y, g, w, 1e-5)
+    dout = torch.randn(rows, d, device="cuda", generator=gen).bfloat16()
+    out.backward(dout)
+    yr, gr = y.detach().clone().requires_grad_(), g.detach().float().requires_grad_()
+    norm.weight.data.copy_(w.detach().float())
+    ref = norm(yr, gr)
+    ref.backward(dout.float())
+    assert out.dtype == torch.bfloat16
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(y.grad, yr.grad, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(g.grad.float(), gr.grad, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(w.grad.float(), norm.weight.grad, rtol=1e-2, atol=1e-1)
