@@ -26,6 +26,7 @@
 #include "norm_grad.cuh"
 #include "embed_grad.cuh"
 #include "gated_norm.cuh"
+#include "ssd.cuh"
 
 namespace {
 
@@ -1237,6 +1238,45 @@ std::vector<Tensor> gated_rms_bwd(Tensor dout, Tensor y, Tensor g, Tensor w, Ten
   return {dy, dg, dw};
 }
 
+// Intra-chunk SSD (Mamba2): cb (B, G, C, S, S), cum (B, H, C, S), x (B, C, S, H, 64), all fp32
+// contiguous; returns y like x.
+void check_ssd(const Tensor& cb, const Tensor& cum, const Tensor& x) {
+  for (const Tensor* t : {&cb, &cum, &x})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous(),
+                "SSD operands must be contiguous fp32 CUDA tensors");
+  TORCH_CHECK(cb.dim() == 5 && cum.dim() == 4 && x.dim() == 5, "cb (B,G,C,S,S), cum (B,H,C,S), x (B,C,S,H,P)");
+  const auto B = x.size(0), C = x.size(1), S = x.size(2), H = x.size(3), G = cb.size(1);
+  TORCH_CHECK(x.size(4) == 64 && S % 64 == 0, "head dim 64 and a chunk length that is a multiple of 64");
+  TORCH_CHECK(cb.size(0) == B && cb.size(2) == C && cb.size(3) == S && cb.size(4) == S && H % G == 0,
+              "cb does not match x");
+  TORCH_CHECK(cum.size(0) == B && cum.size(1) == H && cum.size(2) == C && cum.size(3) == S, "cum does not match x");
+}
+
+Tensor ssd_intra_fwd(Tensor cb, Tensor cum, Tensor x) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_ssd(cb, cum, x);
+  auto y = torch::empty_like(x);
+  bw::ssd_intra_fwd(cb.data_ptr<float>(), cum.data_ptr<float>(), x.data_ptr<float>(), y.data_ptr<float>(),
+                    (int)x.size(0), (int)x.size(1), (int)x.size(2), (int)x.size(3), (int)cb.size(1),
+                    at::cuda::getCurrentCUDAStream());
+  return y;
+}
+
+// Its backward: returns (dcb, dcum, dx).
+std::vector<Tensor> ssd_intra_bwd(Tensor cb, Tensor cum, Tensor x, Tensor dy) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_ssd(cb, cum, x);
+  TORCH_CHECK(dy.sizes() == x.sizes() && dy.scalar_type() == torch::kFloat32 && dy.is_contiguous(),
+              "dy must be a contiguous fp32 tensor shaped like x");
+  auto dx = torch::empty_like(x);
+  auto dcb = torch::zeros_like(cb);
+  auto dcum = torch::zeros_like(cum);
+  bw::ssd_intra_bwd(cb.data_ptr<float>(), cum.data_ptr<float>(), x.data_ptr<float>(), dy.data_ptr<float>(),
+                    dx.data_ptr<float>(), dcb.data_ptr<float>(), dcum.data_ptr<float>(), (int)x.size(0),
+                    (int)x.size(1), (int)x.size(2), (int)x.size(3), (int)cb.size(1), at::cuda::getCurrentCUDAStream());
+  return {dcb, dcum, dx};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
@@ -1253,6 +1293,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
+  m.def("ssd_intra_fwd", &ssd_intra_fwd, "intra-chunk SSD: y = ((C B^T) . exp(cum_s - cum_t)) x, causal");
+  m.def("ssd_intra_bwd", &ssd_intra_bwd, "backward of ssd_intra_fwd: (dcb, dcum, dx)");
   m.def("gated_rms_fwd", &gated_rms_fwd, "gated RMSNorm w * rmsnorm(y * silu(g)) (Mamba2 mixer), bf16 out");
   m.def("gated_rms_bwd", &gated_rms_bwd, "backward of gated_rms_fwd");
   m.def("embedding_dense_grad", &embedding_dense_grad, "dense per-sample embedding gradients, every row written once");

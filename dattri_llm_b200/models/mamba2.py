@@ -85,9 +85,14 @@ def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torc
     cum = log_a.reshape(bsz, n_chunks, chunk, groups, rep).permute(0, 3, 4, 1, 2).cumsum(dim=-1)  # (b,g,r,c,s)
     # 1. within each chunk: (C B^T) per group, times each head's causal decay, applied to x dt
     cb = torch.einsum("bcsgn,bctgn->bgcst", c, b)
-    mix = cb[:, :, None] * _causal_decay(cum)                          # (b, g, r, c, s, t)
-    y = torch.einsum("bgrcst,bctgrp->bcsgrp", mix, xdt)
-    del mix, cb
+    if fused.ssd_intra_enabled(xdt, chunk):  # the decayed (chunk x chunk) matrices stay on chip
+        y = fused.ssd_intra(cb, cum.reshape(bsz, heads, n_chunks, chunk),
+                            xdt.reshape(bsz, n_chunks, chunk, heads, hd)).view(xdt.shape)
+    else:
+        mix = cb[:, :, None] * _causal_decay(cum)                      # (b, g, r, c, s, t)
+        y = torch.einsum("bgrcst,bctgrp->bcsgrp", mix, xdt)
+        del mix
+    del cb
     # 2. each chunk's end state from its own inputs (the decay applied to x dt, not to B)
     to_end = torch.exp(cum[..., -1:] - cum)                            # (b, g, r, c, s)
     states = torch.einsum("bctgrp,bctgn->bcgrpn", xdt * to_end.permute(0, 3, 4, 1, 2)[..., None], b)

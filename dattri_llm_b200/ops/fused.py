@@ -254,3 +254,41 @@ def gated_rms_norm(y: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float
     """``bf16(w * rmsnorm(y * silu(g)))``: the Mamba2 mixer's gated norm and its cast to the
     model dtype in one kernel each way."""
     return _GatedRMSNorm.apply(y, g, w, eps)
+
+
+class _SSDIntra(torch.autograd.Function):
+    """Intra-chunk SSD mixing (``csrc/ssd.cu``): ``y[b,c,s,h] = sum_{t<=s} cb[b,g,c,s,t]
+    exp(cum[b,h,c,s] - cum[b,h,c,t]) x[b,c,t,h]`` with the decayed matrix never stored."""
+
+    @staticmethod
+    def forward(ctx, cb, cum, x):
+        from dattri_llm_b200.ops import count_launch, native
+
+        cb, cum, x = cb.contiguous(), cum.contiguous(), x.contiguous()
+        count_launch()
+        y = native().ssd_intra_fwd(cb, cum, x)
+        ctx.save_for_backward(cb, cum, x)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from dattri_llm_b200.ops import count_launch, native
+
+        cb, cum, x = ctx.saved_tensors
+        count_launch(2)
+        dcb, dcum, dx = native().ssd_intra_bwd(cb, cum, x, dy.contiguous().float())
+        return dcb, dcum, dx
+
+
+def ssd_intra_enabled(x: torch.Tensor, chunk: int) -> bool:
+    """Whether :func:`ssd_intra` applies: fp32 CUDA on sm_100, head dim 64, chunk a multiple of 64."""
+    from dattri_llm_b200.ops import use_native
+
+    return x.dtype == torch.float32 and x.shape[-1] == 64 and chunk % 64 == 0 and use_native(x)
+
+
+def ssd_intra(cb: torch.Tensor, cum: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """Fused intra-chunk SSD: *cb* ``(B, G, C, S, S)`` group-level ``C_s . B_t``, *cum*
+    ``(B, H, C, S)`` cumulative log-decay per chunk, *x* ``(B, C, S, H, P)``; returns ``y``
+    like *x* (fp32)."""
+    return _SSDIntra.apply(cb, cum, x)

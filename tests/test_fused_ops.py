@@ -269,3 +269,29 @@ def test_gated_rms_norm_matches_the_mamba2_module():
     torch.testing.assert_close(y.grad, yr.grad, rtol=1e-3, atol=1e-3)
     torch.testing.assert_close(g.grad.float(), gr.grad, rtol=1e-2, atol=1e-2)
     torch.testing.assert_close(w.grad.float(), norm.weight.grad, rtol=1e-2, atol=1e-1)
+
+
+@pytest.mark.parametrize(("b", "c", "s", "h", "g"), [(2, 3, 128, 6, 2), (1, 2, 256, 4, 1)])
+def test_ssd_intra_matches_torch(b, c, s, h, g):
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    cb = torch.randn(b, g, c, s, s, device="cuda", generator=gen).requires_grad_()
+    cum = (-0.05 * torch.rand(b, h, c, s, device="cuda", generator=gen)).cumsum(-1).requires_grad_()
+    x = torch.randn(b, c, s, h, 64, device="cuda", generator=gen).requires_grad_()
+    y = fused.ssd_intra(cb, cum, x)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    refs = [t.detach().double().requires_grad_() for t in (cb, cum, x)]
+    cb_r, cum_r, x_r = refs
+    causal = torch.ones(s, s, dtype=torch.bool, device="cuda").tril()
+    decay = (cum_r[..., :, None] - cum_r[..., None, :]).masked_fill(~causal, float("-inf")).exp()
+    mix = cb_r.repeat_interleave(h // g, dim=1) * decay  # (b, h, c, s, t)
+    y_r = torch.einsum("bhcst,bcthp->bcshp", mix, x_r)
+    y_r.backward(dy.double())
+
+    def rel(a, want):
+        return float((a.double() - want).norm() / want.norm())
+
+    assert rel(y, y_r) < 1e-5
+    assert rel(x.grad, x_r.grad) < 1e-5
+    assert rel(cb.grad, cb_r.grad) < 1e-5
+    assert rel(cum.grad, cum_r.grad) < 1e-4
