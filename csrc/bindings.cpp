@@ -27,6 +27,7 @@
 #include "embed_grad.cuh"
 #include "gated_norm.cuh"
 #include "ssd.cuh"
+#include "conv1d.cuh"
 
 namespace {
 
@@ -1277,6 +1278,59 @@ std::vector<Tensor> ssd_intra_bwd(Tensor cb, Tensor cum, Tensor x, Tensor dy) {
   return {dcb, dcum, dx};
 }
 
+// Causal depthwise conv (4 taps) + SiLU: x (B, L, C) bf16 with unit channel stride (a column
+// slice of a larger projection is fine), w (C, 1, 4) bf16, bias (C) bf16 or None.
+void check_conv(const Tensor& x, const Tensor& w, const c10::optional<Tensor>& bias) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 3 && x.stride(2) == 1,
+              "x must be (B, L, C) bf16 with unit channel stride");
+  TORCH_CHECK(x.size(2) % 2 == 0 && x.stride(1) % 2 == 0 && x.stride(0) % 2 == 0 &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 4 == 0,
+              "channel pairs must be 4-byte aligned");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == x.size(2) * bw::kConvTaps,
+              "w must be a contiguous (C, 1, 4) bf16 tensor");
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == x.size(2),
+                "bias must be (C) bf16");
+}
+
+Tensor causal_conv_silu_fwd(Tensor x, Tensor w, c10::optional<Tensor> bias) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_conv(x, w, bias);
+  auto out = torch::empty({x.size(0), x.size(1), x.size(2)}, x.options());
+  const bool hb = bias.has_value() && bias->defined();
+  bw::causal_conv_silu_fwd(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(1), x.stride(0),
+                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                           hb ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)x.size(0), (int)x.size(1),
+                           (int)x.size(2), at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
+// Its backward: returns (dx bf16 (B, L, C) contiguous, dw fp32 (C, 4), dbias fp32 (C)).
+std::vector<Tensor> causal_conv_silu_bwd(Tensor dout, Tensor x, Tensor w, c10::optional<Tensor> bias) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_conv(x, w, bias);
+  TORCH_CHECK(dout.scalar_type() == torch::kBFloat16 && dout.is_contiguous() && dout.sizes() == x.sizes(),
+              "dout must be contiguous (B, L, C) bf16");
+  const int B = (int)x.size(0), L = (int)x.size(1), C = (int)x.size(2);
+  auto f32 = x.options().dtype(torch::kFloat32);
+  auto dx = torch::empty({B, L, C}, x.options());
+  const int parts = bw::causal_conv_bwd_parts(B, L);
+  auto dw_part = torch::empty({parts, C, bw::kConvTaps}, f32);
+  auto db_part = torch::empty({parts, C}, f32);
+  auto dw = torch::empty({C, bw::kConvTaps}, f32);
+  auto db = torch::empty({C}, f32);
+  const bool hb = bias.has_value() && bias->defined();
+  bw::causal_conv_silu_bwd(reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                           reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(1), x.stride(0),
+                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                           hb ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+                           reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dw_part.data_ptr<float>(),
+                           db_part.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(), B, L, C,
+                           at::cuda::getCurrentCUDAStream());
+  return {dx, dw, db};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of dattri_llm_b200";
   m.def("gemm_tn", &gemm_tn, "C (op)= alpha * A @ B^T on tcgen05 tensor cores");
@@ -1293,6 +1347,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_peers", &gemm_tn_peers, "A @ B^T with B sharded over the peers, read over NVLink in the GEMM");
   m.def("gemm_tn_staged", &gemm_tn_staged, "A @ B^T with B's peer shards all-gathered inside the launch");
   m.def("norm_per_sample_grad", &norm_per_sample_grad, "per-sample LayerNorm/RMSNorm parameter gradients");
+  m.def("causal_conv_silu_fwd", &causal_conv_silu_fwd, "causal depthwise conv (4 taps) + SiLU, token-major");
+  m.def("causal_conv_silu_bwd", &causal_conv_silu_bwd, "backward of causal_conv_silu_fwd: (dx, dw, dbias)");
   m.def("ssd_intra_fwd", &ssd_intra_fwd, "intra-chunk SSD: y = ((C B^T) . exp(cum_s - cum_t)) x, causal");
   m.def("ssd_intra_bwd", &ssd_intra_bwd, "backward of ssd_intra_fwd: (dcb, dcum, dx)");
   m.def("gated_rms_fwd", &gated_rms_fwd, "gated RMSNorm w * rmsnorm(y * silu(g)) (Mamba2 mixer), bf16 out");

@@ -5,7 +5,8 @@
 // The unfused module runs about eight elementwise passes forward and fifteen backward over
 // fp32 (tokens x 5,120) tensors per layer; here the forward reads y and g once and writes
 // the bf16 output (the cast the mixer applies before its out_proj is folded in), and the
-// backward reads dout, y and g once and writes dy and dg.  One CTA per row in the forward;
+// backward reads dout, y and g (a second time from L1 / L2) and writes dy and dg.  One CTA per
+// row in the forward;
 // the backward gives each CTA a run of rows so the weight gradient is summed per CTA in
 // registers, written as one partial row per CTA and summed over the CTAs by a second launch
 // (no atomics on the D-wide result).
@@ -43,28 +44,23 @@ __global__ void __launch_bounds__(kThreads)
   const long long row = blockIdx.x;
   const float* yr = y + row * cols;
   const __nv_bfloat16* gr = g + row * ldg;
-  float h[kMaxPer];
   float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    h[i] = 0.f;
-    if (c < cols) {
-      const float gv = __bfloat162float(gr[c]);
-      h[i] = yr[c] * gv * sigmoid(gv);
-      ss += h[i] * h[i];
-    }
+  for (int c = threadIdx.x; c < cols; c += kThreads) {
+    const float gv = __bfloat162float(gr[c]);
+    const float h = yr[c] * gv * sigmoid(gv);
+    ss += h * h;
   }
   const float r = rsqrtf(block_sum(ss, scratch) / cols + eps);
   if (threadIdx.x == 0) rstd[row] = r;
   __nv_bfloat16* o = out + row * cols;
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    if (c < cols) o[c] = __float2bfloat16(__bfloat162float(w[c]) * h[i] * r);
+  for (int c = threadIdx.x; c < cols; c += kThreads) {  // the row again, now from L1 / L2
+    const float gv = __bfloat162float(gr[c]);
+    o[c] = __float2bfloat16(__bfloat162float(w[c]) * yr[c] * gv * sigmoid(gv) * r);
   }
 }
 
+// Each row is read twice (the second time from L1 / L2) instead of being held in registers,
+// so the only per-column registers are the weight-gradient sums.
 __global__ void __launch_bounds__(kThreads)
     gated_rms_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const float* __restrict__ y,
                          const __nv_bfloat16* __restrict__ g, long long ldg, const __nv_bfloat16* __restrict__ w,
@@ -82,33 +78,27 @@ __global__ void __launch_bounds__(kThreads)
     const __nv_bfloat16* gr = g + (long long)row * ldg;
     const __nv_bfloat16* dr = dout + (long long)row * cols;
     const float r = rstd[row];
-    float n[kMaxPer], dn[kMaxPer];
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
       const int c = threadIdx.x + i * kThreads;
-      n[i] = dn[i] = 0.f;
       if (c < cols) {
         const float gv = __bfloat162float(gr[c]);
         const float d = __bfloat162float(dr[c]);
-        n[i] = yr[c] * gv * sigmoid(gv) * r;
-        dn[i] = d * __bfloat162float(w[c]);
-        dw_acc[i] += d * n[i];
-        dot += dn[i] * n[i];
+        const float n = yr[c] * gv * sigmoid(gv) * r;
+        dw_acc[i] += d * n;
+        dot += d * __bfloat162float(w[c]) * n;
       }
     }
     const float mean = block_sum(dot, scratch) * inv_cols;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      if (c < cols) {
-        const float gv = __bfloat162float(gr[c]);
-        const float yv = yr[c];
-        const float s = sigmoid(gv);
-        const float dh = r * (dn[i] - n[i] * mean);
-        dy[(long long)row * cols + c] = dh * gv * s;
-        dg[(long long)row * cols + c] = __float2bfloat16(dh * yv * s * (1.f + gv * (1.f - s)));
-      }
+    for (int c = threadIdx.x; c < cols; c += kThreads) {
+      const float gv = __bfloat162float(gr[c]);
+      const float yv = yr[c];
+      const float s = sigmoid(gv);
+      const float n = yv * gv * s * r;
+      const float dh = r * (__bfloat162float(dr[c]) * __bfloat162float(w[c]) - n * mean);
+      dy[(long long)row * cols + c] = dh * gv * s;
+      dg[(long long)row * cols + c] = __float2bfloat16(dh * yv * s * (1.f + gv * (1.f - s)));
     }
   }
   float* part = dw_part + (long long)blockIdx.x * cols;  // this CTA's row of partial sums

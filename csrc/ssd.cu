@@ -11,8 +11,9 @@
 //   ssd_fwd_kernel     y tile (64 rows x 64 head channels) per (chunk, head, row block)
 //   ssd_bwd_dx_kernel  dx[t] = sum_{s >= t} M[s, t] dy[s]         per (chunk, head, t block)
 //   ssd_bwd_dm_kernel  dM = dy x^T per (s block, t block) of the lower triangle, looping over
-//                      the heads of a group: d(C.B^T) summed over those heads in registers,
-//                      and d cum from the row and column sums of dM * M
+//                      a slice of the heads of a group: d(C.B^T) summed over those heads in
+//                      registers (one atomic add per slice), and d cum from the row and column
+//                      sums of dM * M
 //
 // with M[s, t] = (C_s . B_t) exp(cum_s - cum_t) for t <= s, 0 otherwise.  fp32 throughout
 // (CUDA-core FMAs on 4 x 4 register tiles); the chunk's log-decay is non-increasing, so every
@@ -28,6 +29,7 @@ constexpr int kP = 64;   // head channels
 constexpr int kT = 64;   // rows of a tile (positions in the chunk)
 constexpr int kK = 32;   // positions per inner step
 constexpr int kThreads = 256;
+constexpr int kHeadSplits = 8;  // d(C.B^T) CTAs per (tile pair, chunk, group): each sums a slice of the heads
 
 __global__ void __launch_bounds__(kThreads)
     ssd_fwd_kernel(const float* __restrict__ cb, const float* __restrict__ cum, const float* __restrict__ x,
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(kThreads)
         make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
 }
 
-// One CTA per (lower-triangle tile pair, chunk, batch x group).  Thread (ty, tx) owns rows
+// One CTA per (lower-triangle tile pair, chunk, batch x group x head slice).  Thread (ty, tx) owns rows
 // s0 + ty + 16 i and columns t0 + tx + 16 j (i, j < 4), so the x tile rows it reads differ
 // by one between neighbouring lanes (conflict-free with the 65-word row pitch).
 __global__ void __launch_bounds__(kThreads)
@@ -150,7 +152,12 @@ __global__ void __launch_bounds__(kThreads)
   while ((sb + 1) * (sb + 2) / 2 <= pair) ++sb;
   const int tb = pair - sb * (sb + 1) / 2;
   const int s0 = sb * kT, t0 = tb * kT, c = blockIdx.y;
-  const int b = blockIdx.z / G, g = blockIdx.z - b * G, rep = H / G;
+  // blockIdx.z = (b * G + g) * kHeadSplits + part: each CTA takes a slice of the group's heads
+  const int rep = H / G;
+  const int per = (rep + kHeadSplits - 1) / kHeadSplits;
+  const int part = blockIdx.z % kHeadSplits, bg = blockIdx.z / kHeadSplits;
+  const int b = bg / G, g = bg - b * G;
+  const int r_begin = part * per, r_end = min(rep, r_begin + per);
   const long long hp = (long long)H * kP;
   const long long cb_off = (((long long)b * G + g) * C + c) * S * S;
   float cbv[4][4], dcb_acc[4][4];
@@ -164,7 +171,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   const float* xrow = x + ((long long)b * C + c) * S * hp;
   const float* dyrow = dy + ((long long)b * C + c) * S * hp;
-  for (int r = 0; r < rep; ++r) {
+  for (int r = r_begin; r < r_end; ++r) {
     const int h = g * rep + r;
     const float* cump = cum + (((long long)b * H + h) * C + c) * S;
     __syncthreads();  // the previous head's tiles and column sums are consumed
@@ -229,12 +236,13 @@ __global__ void __launch_bounds__(kThreads)
       atomicAdd(dcum + (((long long)b * H + h) * C + c) * S + t0 + tid, -v);
     }
   }
+  if (r_begin >= r_end) return;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = s0 + ty + 16 * i, t = t0 + tx + 16 * j;
-      if (t <= s) dcb[cb_off + (long long)s * S + t] = dcb_acc[i][j];
+      if (t <= s) atomicAdd(dcb + cb_off + (long long)s * S + t, dcb_acc[i][j]);  // one add per head slice
     }
 }
 
@@ -251,7 +259,8 @@ void ssd_intra_bwd(const float* cb, const float* cum, const float* x, const floa
   if (B <= 0 || C <= 0) return;
   ssd_bwd_dx_kernel<<<dim3(S / kT, C, B * H), kThreads, 0, s>>>(cb, cum, dy, dx, C, S, H, G);
   const int nb = S / kT;
-  ssd_bwd_dm_kernel<<<dim3(nb * (nb + 1) / 2, C, B * G), kThreads, 0, s>>>(cb, cum, x, dy, dcb, dcum, C, S, H, G);
+  ssd_bwd_dm_kernel<<<dim3(nb * (nb + 1) / 2, C, B * G * kHeadSplits), kThreads, 0, s>>>(cb, cum, x, dy, dcb, dcum,
+                                                                                         C, S, H, G);
 }
 
 }  // namespace bw

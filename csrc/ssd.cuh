@@ -13,8 +13,7 @@ namespace bw {
 void ssd_intra_fwd(const float* cb, const float* cum, const float* x, float* y, int B, int C, int S, int H, int G,
                    cudaStream_t s);
 
-// Its backward from dy: dx (written), dcb (written; zero above the diagonal tiles is the
-// caller's: pass a zeroed buffer) and dcum (accumulated: pass a zeroed buffer).
+// Its backward from dy: dx (written), dcb and dcum (accumulated: pass zeroed buffers).
 void ssd_intra_bwd(const float* cb, const float* cum, const float* x, const float* dy, float* dx, float* dcb,
                    float* dcum, int B, int C, int S, int H, int G, cudaStream_t s);
 

@@ -130,7 +130,13 @@ def _mixer_forward(self, hidden_states: torch.Tensor, cache_params=None, attenti
     d_mlp = (projected.shape[-1] - 2 * self.intermediate_size - 2 * groups_state - self.num_heads) // 2
     _, _, gate, xbc, dt = projected.split([d_mlp, d_mlp, self.intermediate_size, self.conv_dim, self.num_heads],
                                           dim=-1)
-    xbc = self.act(self.conv1d(xbc.transpose(1, 2))[..., :length].transpose(1, 2))
+    conv = self.conv1d
+    if (self.activation in ("silu", "swish") and not (conv._forward_hooks or conv._forward_pre_hooks
+                                                     or conv._backward_hooks)
+            and fused.causal_conv_silu_enabled(xbc, conv)):
+        xbc = fused.causal_conv_silu(xbc, conv.weight, conv.bias)  # nothing watches the convolution
+    else:
+        xbc = self.act(conv(xbc.transpose(1, 2))[..., :length].transpose(1, 2))
     x, b, c = xbc.split([self.intermediate_size, groups_state, groups_state], dim=-1)
     a_head = -torch.exp(self.A_log.float())
     dt = F.softplus(dt + self.dt_bias).clamp(self.time_step_limit[0], self.time_step_limit[1]).float()

@@ -292,3 +292,48 @@ def ssd_intra(cb: torch.Tensor, cum: torch.Tensor, x: torch.Tensor) -> torch.Ten
     ``(B, H, C, S)`` cumulative log-decay per chunk, *x* ``(B, C, S, H, P)``; returns ``y``
     like *x* (fp32)."""
     return _SSDIntra.apply(cb, cum, x)
+
+
+class _CausalConvSiLU(torch.autograd.Function):
+    """``silu(causal depthwise conv1d(x))`` over the token axis of a ``(B, L, C)`` bf16 tensor
+    (``csrc/conv1d.cu``); weight ``(C, 1, 4)``, optional bias ``(C)``."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        from dattri_llm_b200.ops import count_launch, native
+
+        w = weight.contiguous()
+        count_launch()
+        out = native().causal_conv_silu_fwd(x, w, bias)
+        ctx.save_for_backward(x, w, bias)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from dattri_llm_b200.ops import count_launch, native
+
+        x, w, bias = ctx.saved_tensors
+        count_launch(3)
+        dx, dw, db = native().causal_conv_silu_bwd(dout.to(torch.bfloat16).contiguous(), x, w, bias)
+        dw = dw.view_as(w).to(w.dtype) if ctx.needs_input_grad[1] else None
+        db = db.to(bias.dtype) if bias is not None and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def causal_conv_silu_enabled(x: torch.Tensor, conv) -> bool:
+    """Whether :func:`causal_conv_silu` computes *conv* (an ``nn.Conv1d``) on ``x (B, L, C)``:
+    depthwise, 4 taps, causal padding, bf16 on sm_100, even channel count and offsets."""
+    from dattri_llm_b200.ops import use_native
+
+    w = conv.weight
+    return (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 3 and x.stride(2) == 1
+            and conv.groups == conv.in_channels == conv.out_channels == x.shape[2] and tuple(w.shape[1:]) == (1, 4)
+            and tuple(conv.padding) == (3,) and tuple(conv.stride) == (1,) and tuple(conv.dilation) == (1,)
+            and (conv.bias is None or conv.bias.dtype == torch.bfloat16) and x.shape[2] % 2 == 0
+            and x.stride(1) % 2 == 0 and x.stride(0) % 2 == 0 and x.data_ptr() % 4 == 0 and use_native(x, w))
+
+
+def causal_conv_silu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """``silu(conv1d(x^T, weight, bias, padding=3, groups=C)[..., :L])^T`` token-major, one kernel
+    each way (the Mamba2 mixer's convolution and activation)."""
+    return _CausalConvSiLU.apply(x, weight, bias)

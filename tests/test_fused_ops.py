@@ -295,3 +295,27 @@ def test_ssd_intra_matches_torch(b, c, s, h, g):
     assert rel(x.grad, x_r.grad) < 1e-5
     assert rel(cb.grad, cb_r.grad) < 1e-5
     assert rel(cum.grad, cum_r.grad) < 1e-4
+
+
+@pytest.mark.parametrize(("b", "length", "bias"), [(2, 77, True), (1, 2048, False)])
+def test_causal_conv_silu_matches_conv1d(b, length, bias):
+    c = 96
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    proj = torch.randn(b, length, c + 40, device="cuda", generator=gen).bfloat16()
+    x = proj[..., 20:20 + c].detach().requires_grad_()  # a channel slice of a wider projection
+    conv = torch.nn.Conv1d(c, c, 4, groups=c, padding=3, bias=bias).cuda().bfloat16()
+    assert fused.causal_conv_silu_enabled(x, conv)
+    out = fused.causal_conv_silu(x, conv.weight, conv.bias)
+    dout = torch.randn(b, length, c, device="cuda", generator=gen).bfloat16()
+    out.backward(dout)
+    xr = x.detach().float().requires_grad_()
+    wr = conv.weight.detach().float().requires_grad_()
+    br = conv.bias.detach().float().requires_grad_() if bias else None
+    ref = F.silu(F.conv1d(xr.transpose(1, 2), wr, br, padding=3, groups=c)[..., :length]).transpose(1, 2)
+    ref.backward(dout.float())
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=1e-2, atol=1e-2)
+    tol = 2e-2 * float(wr.grad.abs().max())
+    torch.testing.assert_close(conv.weight.grad.float(), wr.grad, rtol=2e-2, atol=tol)
+    if bias:
+        torch.testing.assert_close(conv.bias.grad.float(), br.grad, rtol=2e-2, atol=2e-2 * float(br.grad.abs().max()))
