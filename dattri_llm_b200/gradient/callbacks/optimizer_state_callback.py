@@ -141,20 +141,35 @@ class OptimizerStateCallback(HookManagerCallback):
     def _wanted(self, layer_name: str) -> bool:
         return self._only is None or layer_name in self._only
 
-    def _moments(self, layer_name: str) -> tuple[torch.Tensor, torch.Tensor]:
-        """fp32 host copies of (exp_avg, exp_avg_sq) at the layer's coordinates; zeros for a
-        parameter the optimizer has not stepped yet."""
-        reader, idx = self.snapshot, self.coordinates(layer_name)
-        size = reader.width(layer_name) if idx is None else idx.numel()
-        out = []
-        for key in ("exp_avg", "exp_avg_sq"):
-            val = reader.state(layer_name, key, idx)
-            out.append(torch.zeros(size) if val is None else val.detach().to("cpu", torch.float32, copy=True))
-        return out[0], out[1]
+    def _moments(self, names: list[str]) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        """fp32 host copies of (exp_avg, exp_avg_sq) at each layer's coordinates; zeros for a
+        parameter the optimizer has not stepped yet.  The layers' device values travel to the
+        host in one copy per device (one synchronization per record, not one per tensor)."""
+        reader = self.snapshot
+        slots: list[tuple[str, int, torch.Tensor | int]] = []  # (layer, moment, device value or size)
+        for name in names:
+            idx = self.coordinates(name)
+            size = reader.width(name) if idx is None else idx.numel()
+            for m, key in enumerate(("exp_avg", "exp_avg_sq")):
+                val = reader.state(name, key, idx)
+                slots.append((name, m, size if val is None else val.detach().reshape(-1)))
+        by_device: dict[torch.device, list[torch.Tensor]] = {}
+        for _name, _m, v in slots:
+            if isinstance(v, torch.Tensor):
+                by_device.setdefault(v.device, []).append(v)
+        host: dict[int, torch.Tensor] = {}
+        for vals in by_device.values():
+            flat = torch.cat([v.float() for v in vals]).to("cpu")
+            for v, part in zip(vals, flat.split([v.numel() for v in vals]), strict=True):
+                host[id(v)] = part.clone()  # each record owns its storage
+        out: dict[str, list[torch.Tensor]] = {name: [None, None] for name in names}
+        for name, m, v in slots:
+            out[name][m] = host[id(v)] if isinstance(v, torch.Tensor) else torch.zeros(v)
+        return {name: (pair[0], pair[1]) for name, pair in out.items()}
 
     def _record(self, layer_names: Iterable[str]) -> dict:
         names = [n for n in layer_names if self._wanted(n)]
-        record: dict = {"layers": {name: self._moments(name) for name in names}}
+        record: dict = {"layers": self._moments(names)}
         if names:
             hyper = self.snapshot.hyperparameters(names[0])
             record["step"] = self.snapshot.step_count(names[0])

@@ -22,6 +22,7 @@ reference's ``dattri_llm/gradient/optimizer_state.py``.
 from __future__ import annotations
 
 import math
+import weakref
 from collections.abc import Callable, Iterable
 from dataclasses import dataclass, field
 
@@ -197,6 +198,24 @@ def _fsdp2_param(root: nn.Module, module: nn.Module, role: str) -> nn.Parameter 
     return None
 
 
+_IDX_ON_DEVICE: dict[tuple[int, str], tuple] = {}  # (id(idx), device) -> (weak ref, copy)
+
+
+def _on_device(idx: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """*idx* on *device*, copied once per index tensor and device (coordinates are fixed per
+    layer; a host-to-device copy per read would stall the host every time)."""
+    if idx.device == device:
+        return idx
+    key = (id(idx), str(device))
+    hit = _IDX_ON_DEVICE.get(key)
+    if hit is not None and hit[0]() is idx:
+        return hit[1]
+    moved = idx.to(device)
+    weakref.finalize(idx, _IDX_ON_DEVICE.pop, key, None)
+    _IDX_ON_DEVICE[key] = (weakref.ref(idx), moved)
+    return moved
+
+
 class OptimizerSnapshot:
     """Per-layer optimizer state in each hooked layer's gradient layout (see the module
     docstring).  *model* may be wrapped (DDP / FSDP); layer names are resolved inside."""
@@ -296,7 +315,7 @@ class OptimizerSnapshot:
         else:
             parts = [weight.reshape(-1)] + ([] if bias is None else [bias.reshape(-1).to(weight.dtype)])
             flat = torch.cat(parts)
-        return flat if idx is None else flat[idx.to(flat.device)]
+        return flat if idx is None else flat[_on_device(idx, flat.device)]
 
     # ------------------------------------------------------------------ hyperparameters
     def group(self, layer_name: str) -> dict:
