@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kThreads)
   const float* yr = y + row * cols;
   const __nv_bfloat16* gr = g + row * ldg;
   float ss = 0.f;
+#pragma unroll 4
   for (int c = threadIdx.x; c < cols; c += kThreads) {
     const float gv = __bfloat162float(gr[c]);
     const float h = yr[c] * gv * sigmoid(gv);
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(kThreads)
   const float r = rsqrtf(block_sum(ss, scratch) / cols + eps);
   if (threadIdx.x == 0) rstd[row] = r;
   __nv_bfloat16* o = out + row * cols;
+#pragma unroll 4
   for (int c = threadIdx.x; c < cols; c += kThreads) {  // the row again, now from L1 / L2
     const float gv = __bfloat162float(gr[c]);
     o[c] = __float2bfloat16(__bfloat162float(w[c]) * yr[c] * gv * sigmoid(gv) * r);
@@ -60,7 +62,8 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Each row is read twice (the second time from L1 / L2) instead of being held in registers,
-// so the only per-column registers are the weight-gradient sums.
+// so the only per-column registers are the weight-gradient sums; the loops over a row are
+// unrolled so several columns' loads are in flight at once.
 __global__ void __launch_bounds__(kThreads)
     gated_rms_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const float* __restrict__ y,
                          const __nv_bfloat16* __restrict__ g, long long ldg, const __nv_bfloat16* __restrict__ w,
@@ -91,7 +94,8 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
     const float mean = block_sum(dot, scratch) * inv_cols;
-    for (int c = threadIdx.x; c < cols; c += kThreads) {
+  #pragma unroll 4
+  for (int c = threadIdx.x; c < cols; c += kThreads) {
       const float gv = __bfloat162float(gr[c]);
       const float yv = yr[c];
       const float s = sigmoid(gv);

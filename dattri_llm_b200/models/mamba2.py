@@ -22,6 +22,7 @@ Parameters, module names and hook points are unchanged: ``in_proj``, ``conv1d`` 
 
 from __future__ import annotations
 
+import contextlib
 import types
 
 import torch
@@ -51,6 +52,56 @@ def _causal_decay(cum: torch.Tensor) -> torch.Tensor:
     n = cum.shape[-1]
     upper = torch.ones(n, n, dtype=torch.bool, device=cum.device).triu(1)
     return (cum[..., :, None] - cum[..., None, :]).masked_fill_(upper, float("-inf")).exp_()
+
+
+@contextlib.contextmanager
+def _tf32_products():
+    """fp32 matrix products on TF32 tensor cores inside the block (fp32 accumulation; the
+    precision the SSD chunk products of the reference Mamba2 kernels use), the previous
+    setting restored after it."""
+    previous = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        yield
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = previous
+
+
+def _swap(eq: str) -> tuple[str, str]:
+    """For ``"A,B->C"`` with every index in two of the three terms: the equations of ``dA``
+    (``"C,B->A"``) and ``dB`` (``"A,C->B"``)."""
+    lhs, out = eq.split("->")
+    a, b = lhs.split(",")
+    return f"{out},{b}->{a}", f"{a},{out}->{b}"
+
+
+class _TF32Product(torch.autograd.Function):
+    """A two-operand fp32 einsum whose forward and backward products run on TF32 tensor
+    cores (the chunk-state products of the SSD scan: batched GEMMs of 5,120 x 128 x 256 per
+    chunk that fp32 CUDA-core kernels run an order of magnitude slower)."""
+
+    @staticmethod
+    def forward(ctx, eq, a, b):
+        ctx.eq = eq
+        ctx.save_for_backward(a, b)
+        with _tf32_products():
+            return torch.einsum(eq, a, b)
+
+    @staticmethod
+    def backward(ctx, dout):
+        a, b = ctx.saved_tensors
+        eq_a, eq_b = _swap(ctx.eq)
+        with _tf32_products():
+            da = torch.einsum(eq_a, dout, b) if ctx.needs_input_grad[1] else None
+            db = torch.einsum(eq_b, a, dout) if ctx.needs_input_grad[2] else None
+        return None, da, db
+
+
+def _product(eq: str, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``einsum(eq, a, b)``, on TF32 tensor cores for fp32 CUDA operands."""
+    if a.is_cuda and a.dtype == torch.float32 and b.dtype == torch.float32:
+        return _TF32Product.apply(eq, a, b)
+    return torch.einsum(eq, a, b)
 
 
 def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torch.Tensor, c: torch.Tensor,
@@ -95,14 +146,14 @@ def ssd_chunked(x: torch.Tensor, dt: torch.Tensor, a_head: torch.Tensor, b: torc
     del cb
     # 2. each chunk's end state from its own inputs (the decay applied to x dt, not to B)
     to_end = torch.exp(cum[..., -1:] - cum)                            # (b, g, r, c, s)
-    states = torch.einsum("bctgrp,bctgn->bcgrpn", xdt * to_end.permute(0, 3, 4, 1, 2)[..., None], b)
+    states = _product("bctgrp,bctgn->bcgrpn", xdt * to_end.permute(0, 3, 4, 1, 2)[..., None], b)
     # 3. carry states across chunk boundaries
     states = torch.cat([torch.zeros_like(states[:, :1]), states], dim=1)
     across = torch.exp(_segment_sums(F.pad(cum[..., -1], (1, 0))))    # (b, g, r, c+1, c+1)
-    states = torch.einsum("bgrzc,bcgrpn->bzgrpn", across, states)[:, :-1]
+    states = _product("bgrzc,bcgrpn->bzgrpn", across, states)[:, :-1]
     # 4. the incoming state's contribution to every position of the chunk
     from_start = torch.exp(cum).permute(0, 3, 4, 1, 2)[..., None]      # (b, c, s, g, r, 1)
-    y = y + torch.einsum("bcsgn,bcgrpn->bcsgrp", c, states) * from_start
+    y = y + _product("bcsgn,bcgrpn->bcsgrp", c, states) * from_start
     y = y.reshape(bsz, n_chunks * chunk, heads, hd)
     return y[:, :length] if pad else y
 

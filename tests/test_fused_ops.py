@@ -319,3 +319,31 @@ def test_causal_conv_silu_matches_conv1d(b, length, bias):
     torch.testing.assert_close(conv.weight.grad.float(), wr.grad, rtol=2e-2, atol=tol)
     if bias:
         torch.testing.assert_close(conv.bias.grad.float(), br.grad, rtol=2e-2, atol=2e-2 * float(br.grad.abs().max()))
+
+
+def test_ssd_chunked_on_gpu_matches_fp64_cpu():
+    """The whole chunked scan on the GPU (fused intra-chunk kernels, TF32 chunk-state
+    products) against the same code in fp64 on the CPU: outputs and input gradients."""
+    from dattri_llm_b200.models.mamba2 import ssd_chunked
+
+    bsz, length, heads, hd, groups, state, chunk = 2, 300, 8, 64, 2, 32, 64
+    gen = torch.Generator().manual_seed(9)
+    x = torch.randn(bsz, length, heads, hd, generator=gen)
+    dt = 0.1 * torch.rand(bsz, length, heads, generator=gen)
+    a = -1.0 - torch.rand(heads, generator=gen)
+    b = torch.randn(bsz, length, groups, state, generator=gen)
+    c = torch.randn(bsz, length, groups, state, generator=gen)
+    dy = torch.randn(bsz, length, heads, hd, generator=gen)
+    cpu = [t.double().requires_grad_() for t in (x, dt, a, b, c)]
+    gpu = [t.cuda().requires_grad_() for t in (x, dt, a, b, c)]
+    want = ssd_chunked(*cpu, chunk)
+    want.backward(dy.double())
+    got = ssd_chunked(*gpu, chunk)
+    got.backward(dy.cuda())
+
+    def rel(u, v):
+        return float((u.double().cpu() - v).norm() / v.norm())
+
+    assert rel(got, want) < 5e-3
+    for g_, w_, name in zip(gpu, cpu, ("x", "dt", "a", "b", "c"), strict=True):
+        assert rel(g_.grad, w_.grad) < 1e-2, name
