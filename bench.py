@@ -237,8 +237,9 @@ class _TimedBlocks:
     """Wraps a gradient source: CUDA events (and host times) at block *warm* and after
     block ``warm + steps - 1`` has been consumed by the scoring loop."""
 
-    def __init__(self, source, warm: int, steps: int) -> None:
+    def __init__(self, source, warm: int, steps: int, counter=None) -> None:
         self.source, self.warm, self.steps = source, warm, steps
+        self.counter, self.launches = counter, None  # native launches inside the timed blocks
         self.ev0 = torch.cuda.Event(enable_timing=True)
         self.ev1 = torch.cuda.Event(enable_timing=True)
         self.t0 = self.t1 = None
@@ -256,8 +257,11 @@ class _TimedBlocks:
                 self.prof.start()
                 self.t0 = time.perf_counter()
                 self.ev0.record()
+                self.n0 = self.counter() if self.counter is not None else None
             if i == self.warm + self.steps:
                 self.ev1.record()
+                if self.counter is not None:
+                    self.launches = self.counter() - self.n0
                 torch.cuda.synchronize()
                 self.t1 = time.perf_counter()
                 self.prof.stop(_env_int("RANK", 0))
@@ -675,7 +679,8 @@ def _olmoe(dev):
     return model, cfg
 
 
-def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=None, expert_parallel=False):
+def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=None, expert_parallel=False,
+              counter=None):
     """One public scoring loop: K steps timed with CUDA events (max over ranks).  With
     *expert_parallel* the MoE blocks are :class:`ExpertParallelMoE` modules whose expert and
     router taps carry the same names as the replicated-expert stand-ins (no routed-row
@@ -697,7 +702,7 @@ def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=No
     train = lib.GradientStreamer(model, _DS4(n * world, vocab, seed=2), args, batch_size=C4_MB,
                                  loss_fn=_token_sum_loss, hook_manager=hm, forward_model=model)
     test = att.generate_test_rep(_DS4(C4_NTEST, vocab, seed=1), hook_manager=hm, forward_model=model, shard=False)
-    timed = _TimedBlocks(train, warmup, steps)
+    timed = _TimedBlocks(train, warmup, steps, counter=counter)
     clocks = ClockSampler(local)
     clocks.start()
     with hm.collect(), train, test:
@@ -706,7 +711,7 @@ def _c4_score(lib, model, rank, world, local, steps, warmup, vocab, projector=No
     torch.cuda.synchronize()
     ms = _max_over_ranks(timed.ev0.elapsed_time(timed.ev1), world) / steps
     host = _max_over_ranks(timed.t1 - timed.t0, world)
-    return ms, clk, host
+    return ms, clk, host, timed.launches
 
 
 def main_c4(a, rank, world, local):
@@ -730,10 +735,9 @@ def main_c4(a, rank, world, local):
             from dattri_llm_b200.parallel.moe import expert_parallelize
 
             expert_parallelize(model, max_tokens=max(C4_MB, C4_NTEST) * C4_SEQ)  # the query batch too
-        n0 = native_ops.launch_count()
-        ms, clk, host = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
-                                  expert_parallel=world > 1)
-        extra = {"gpu_launches": native_ops.launch_count() - n0}
+        ms, clk, host, launches = _c4_score(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
+                                            expert_parallel=world > 1, counter=native_ops.launch_count)
+        extra = {"gpu_launches": launches}
     else:
         ref = os.path.join(HERE, "baseline", "_ref")
         if not os.path.isdir(os.path.join(ref, "dattri_llm")):
@@ -743,8 +747,8 @@ def main_c4(a, rank, world, local):
 
         model, cfg = _olmoe(dev)
         cfg_json["parallelism"] = f"replicated-experts{world}" if world > 1 else "single"
-        ms, clk, host = _c4_score(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
-                                  projector=counter_projector_factory())
+        ms, clk, host, _ = _c4_score(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
+                                     projector=counter_projector_factory())
         extra = {"impl": "reference"}
     value = C4_MB * world / (ms / 1e3)
     out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms, "vs_baseline": None, "clocks": clk,
@@ -828,7 +832,7 @@ def _c5_target(lib, model, hc, dev, vocab, n_test=C5_NTEST, test_mb=C5_TEST_MB):
     return dataclasses.replace(grad, data={n: v / n_test for n, v in total.items()})
 
 
-def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_TARGET_SEQS):
+def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_TARGET_SEQS, counter=None):
     """One LESS-style trajectory with online selection through the public streamer: Adam-
     preconditioned masked captures (k = 64 per linear, 8192 in all), their optimizer state
     recorded every step, each step's pool micro-batch scored against the fixed target and
@@ -850,7 +854,7 @@ def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_TARG
                                               scoring_kwargs={"score_mode": "materialized"},
                                               selection_kwargs={"threshold": C5_DROP,
                                                                 "threshold_mode": "bottom_fraction"}))
-    timed = _TimedBlocks(train, warmup, steps)
+    timed = _TimedBlocks(train, warmup, steps, counter=counter)
     clocks = ClockSampler(local)
     clocks.start()
     with train:
@@ -860,7 +864,7 @@ def _c5_run(lib, model, rank, world, local, steps, warmup, vocab, n_test=C5_TARG
     torch.cuda.synchronize()
     ms = _max_over_ranks(timed.ev0.elapsed_time(timed.ev1), world) / steps
     host = _max_over_ranks(timed.t1 - timed.t0, world)
-    return ms, clk, host
+    return ms, clk, host, timed.launches
 
 
 def main_c5(a, rank, world, local):
@@ -885,10 +889,10 @@ def main_c5(a, rank, world, local):
 
         native_ops.native()
         model = _mamba2(cfg, dev, ours=True)
-        n0 = native_ops.launch_count()
-        ms, clk, host = _c5_run(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        ms, clk, host, launches = _c5_run(bw, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size,
+                                          counter=native_ops.launch_count)
         native_ops.check_device_errors(dev)
-        extra = {"gpu_launches": native_ops.launch_count() - n0}
+        extra = {"gpu_launches": launches}
     else:
         ref = os.path.join(HERE, "baseline", "_ref")
         if not os.path.isdir(os.path.join(ref, "dattri_llm")):
@@ -897,7 +901,7 @@ def main_c5(a, rank, world, local):
         import dattri_llm as R  # noqa: N812
 
         model = _mamba2(cfg, dev, ours=False)
-        ms, clk, host = _c5_run(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
+        ms, clk, host, _ = _c5_run(R, model, rank, world, local, a.steps, a.warmup, cfg.vocab_size)
         extra = {"impl": "reference"}
     value = C5_MB * world / (ms / 1e3)
     out.update({"value": value, "unit": "train samples/s", "ms_per_step": ms, "vs_baseline": None, "clocks": clk,
