@@ -1178,24 +1178,24 @@ void ce_bwd_inplace(Tensor logits, Tensor lse, Tensor target, Tensor gscale) {
 
 }  // namespace
 
-// Dense per-sample embedding gradients (B * vocab, E) from the token keys sorted ascending
-// (key = b * vocab + id), the token row of g behind each key, and g (n, E).  bf16 or fp32,
-// the output in g's dtype; E * elem size a multiple of 16 bytes.
-Tensor embedding_dense_grad(Tensor keys, Tensor order, Tensor g, int64_t rows) {
+// Dense per-sample embedding gradients (B * vocab, E) from the token rows of g (n, E) sorted
+// by key b * vocab + id (`order`) and each output row's first position in that order
+// (`starts`, R + 1 entries).  bf16 or fp32, the output in g's dtype; E * elem size a multiple
+// of 16 bytes.
+Tensor embedding_dense_grad(Tensor starts, Tensor order, Tensor g, int64_t rows) {
   const c10::cuda::CUDAGuard guard(g.device());
   TORCH_CHECK(g.is_cuda() && g.dim() == 2 && g.is_contiguous(), "g must be a contiguous (n, E) CUDA tensor");
   TORCH_CHECK(g.scalar_type() == torch::kBFloat16 || g.scalar_type() == torch::kFloat32, "g must be bf16 or fp32");
-  TORCH_CHECK(keys.is_cuda() && order.is_cuda() && keys.scalar_type() == torch::kInt64 &&
-                  order.scalar_type() == torch::kInt64 && keys.is_contiguous() && order.is_contiguous() &&
-                  keys.numel() == g.size(0) && order.numel() == g.size(0),
-              "keys and order must be contiguous int64 vectors of g's row count");
+  TORCH_CHECK(starts.is_cuda() && order.is_cuda() && starts.scalar_type() == torch::kInt64 &&
+                  order.scalar_type() == torch::kInt64 && starts.is_contiguous() && order.is_contiguous() &&
+                  starts.numel() == rows + 1 && order.numel() == g.size(0),
+              "starts (rows + 1) and order (one per row of g) must be contiguous int64 vectors");
   const int elem = (int)g.element_size();
   const int E = (int)g.size(1);
   TORCH_CHECK((E * elem) % 16 == 0, "the embedding width must fill whole 16-byte vectors");
-  TORCH_CHECK(g.size(0) < (1ll << 31), "too many tokens");
   auto out = torch::empty({rows, (int64_t)E}, g.options());
-  bw::embedding_dense_grad(keys.data_ptr<int64_t>(), order.data_ptr<int64_t>(), g.data_ptr(), out.data_ptr(), rows,
-                           (int)g.size(0), E, elem, at::cuda::getCurrentCUDAStream());
+  bw::embedding_dense_grad(starts.data_ptr<int64_t>(), order.data_ptr<int64_t>(), g.data_ptr(), out.data_ptr(), rows,
+                           E, elem, at::cuda::getCurrentCUDAStream());
   return out;
 }
 

@@ -5,7 +5,7 @@
 // The library call runs cuDNN's generic depthwise kernel on the transposed (channels x tokens)
 // view, a separate SiLU, and the transposes around them.  Here each thread owns two adjacent
 // channels (one 4-byte bf16 pair, so a warp reads 128 contiguous bytes of a token row) over a
-// run of 32 tokens and slides a 4-token window along it: every input is read once, straight
+// run of 16 tokens and slides a 4-token window along it: every input is read once, straight
 // from the token-major projection it is a slice of.  The backward recomputes the
 // pre-activation, keeps the last four pre-activation gradients in registers to form dx, and
 // sums the tap and bias gradients per run into partial rows that a second launch adds up.
@@ -16,7 +16,7 @@
 namespace bw {
 namespace {
 
-constexpr int kRun = 32;       // tokens per thread
+constexpr int kRun = 16;       // tokens per thread (short runs: more threads, more loads in flight)
 constexpr int kCThreads = 128;  // channel pairs per CTA
 constexpr int K = kConvTaps;
 
@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kCThreads)
     win1[k] = v.y;
   }
   __nv_bfloat16* ob = out + ((long long)b * L) * C + c;
+#pragma unroll 4
   for (int t = t0; t < t1; ++t) {
     const float2 v = load2(xb + (long long)t * ldx);
     win0[K - 1] = v.x;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(kCThreads)
 #pragma unroll
   for (int k = 0; k < K; ++k) gw0[k] = gw1[k] = 0.f;
   // t runs K - 1 tokens past the run: dx[t'] needs the pre-activation gradients of t' .. t' + 3
+#pragma unroll 4
   for (int t = t0; t < t1 + K - 1; ++t) {
     float d0 = 0.f, d1 = 0.f;
     if (t < L) {

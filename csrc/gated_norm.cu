@@ -6,10 +6,9 @@
 // fp32 (tokens x 5,120) tensors per layer; here the forward reads y and g once and writes
 // the bf16 output (the cast the mixer applies before its out_proj is folded in), and the
 // backward reads dout, y and g (a second time from L1 / L2) and writes dy and dg.  One CTA per
-// row in the forward;
-// the backward gives each CTA a run of rows so the weight gradient is summed per CTA in
-// registers, written as one partial row per CTA and summed over the CTAs by a second launch
-// (no atomics on the D-wide result).
+// row in the forward; the backward gives each CTA a run of rows so the weight gradient is
+// summed per CTA in shared memory, written as one partial row per CTA and summed over the
+// CTAs by a second launch (no atomics on the D-wide result).
 #include <cuda_bf16.h>
 
 #include "gated_norm.cuh"
@@ -18,7 +17,6 @@ namespace bw {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxPer = kGatedNormMaxCols / kThreads;
 constexpr int kRowsPerCta = 2;  // 1,024 CTAs for 2,048 rows: enough loads in flight
 
 __device__ __forceinline__ float block_sum(float v, float* scratch) {
@@ -62,17 +60,18 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Each row is read twice (the second time from L1 / L2) instead of being held in registers,
-// so the only per-column registers are the weight-gradient sums; the loops over a row are
-// unrolled so several columns' loads are in flight at once.
+// and the weight-gradient sums of the CTA's rows live in shared memory (each thread owns its
+// columns there, so no two threads touch one entry): few registers, many warps per SM, which
+// is what this latency-bound pass needs.  The row loops are unrolled so several columns'
+// loads are in flight at once.
 __global__ void __launch_bounds__(kThreads)
     gated_rms_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const float* __restrict__ y,
                          const __nv_bfloat16* __restrict__ g, long long ldg, const __nv_bfloat16* __restrict__ w,
                          const float* __restrict__ rstd, float* __restrict__ dy, __nv_bfloat16* __restrict__ dg,
                          float* __restrict__ dw_part, int rows, int cols) {
   __shared__ float scratch[kThreads / 32];
-  float dw_acc[kMaxPer];
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) dw_acc[i] = 0.f;
+  extern __shared__ float dw_acc[];  // [cols]
+  for (int c = threadIdx.x; c < cols; c += kThreads) dw_acc[c] = 0.f;
   const int r0 = blockIdx.x * kRowsPerCta;
   const int r1 = min(rows, r0 + kRowsPerCta);
   const float inv_cols = 1.f / cols;
@@ -82,20 +81,17 @@ __global__ void __launch_bounds__(kThreads)
     const __nv_bfloat16* dr = dout + (long long)row * cols;
     const float r = rstd[row];
     float dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      if (c < cols) {
-        const float gv = __bfloat162float(gr[c]);
-        const float d = __bfloat162float(dr[c]);
-        const float n = yr[c] * gv * sigmoid(gv) * r;
-        dw_acc[i] += d * n;
-        dot += d * __bfloat162float(w[c]) * n;
-      }
+#pragma unroll 4
+    for (int c = threadIdx.x; c < cols; c += kThreads) {
+      const float gv = __bfloat162float(gr[c]);
+      const float d = __bfloat162float(dr[c]);
+      const float n = yr[c] * gv * sigmoid(gv) * r;
+      dw_acc[c] += d * n;
+      dot += d * __bfloat162float(w[c]) * n;
     }
     const float mean = block_sum(dot, scratch) * inv_cols;
-  #pragma unroll 4
-  for (int c = threadIdx.x; c < cols; c += kThreads) {
+#pragma unroll 4
+    for (int c = threadIdx.x; c < cols; c += kThreads) {
       const float gv = __bfloat162float(gr[c]);
       const float yv = yr[c];
       const float s = sigmoid(gv);
@@ -106,11 +102,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   float* part = dw_part + (long long)blockIdx.x * cols;  // this CTA's row of partial sums
-#pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    if (c < cols) part[c] = dw_acc[i];
-  }
+  for (int c = threadIdx.x; c < cols; c += kThreads) part[c] = dw_acc[c];
 }
 
 // dw[c] = sum over the CTAs' partial rows (column sums; consecutive threads, consecutive columns).
@@ -138,7 +130,8 @@ void gated_rms_bwd(const __nv_bfloat16* dout, const float* y, const __nv_bfloat1
                    int rows, int cols, cudaStream_t s) {
   if (rows <= 0) return;
   const int grid = gated_rms_bwd_parts(rows);
-  gated_rms_bwd_kernel<<<grid, kThreads, 0, s>>>(dout, y, g, ldg, w, rstd, dy, dg, dw_part, rows, cols);
+  gated_rms_bwd_kernel<<<grid, kThreads, (size_t)cols * sizeof(float), s>>>(dout, y, g, ldg, w, rstd, dy, dg, dw_part,
+                                                                            rows, cols);
   column_sum_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, s>>>(dw_part, dw, grid, cols);
 }
 

@@ -21,6 +21,10 @@ Rows (ids of the hot-op inventory):
   per_sample_outer K5 (B, T, d)^T (B, T, k) -> (B, d, k)      vs torch.bmm
   adam_dir        K18 m_hat / (sqrt(v_hat) + eps)             vs the elementwise chain
   project_seg     K1  a @ P stored token-major (B, k, T)      vs matmul + transpose copy
+  embed_dense     K10 dense (B, vocab * E) embedding grads    vs zero fill + index_add
+  gated_norm      Mamba2 gated RMSNorm, forward + backward   vs the module's elementwise chain
+  causal_conv     Mamba2 conv1d (4 taps) + SiLU, fwd + bwd    vs cuDNN depthwise conv + SiLU
+  ssd_intra       Mamba2 intra-chunk SSD, fwd + bwd          vs materialized decay + einsum
 """
 
 from __future__ import annotations
@@ -258,6 +262,87 @@ def bench_project_seg(peaks):
          {"shape": f"T={b * t} d={d} k={k}"})
 
 
+def bench_embed_dense(peaks):
+    from dattri_llm_b200 import ops
+
+    b, t, e, v = 8, 1024, 1024, 8192
+    ids = torch.randint(0, v, (b, t), device="cuda")
+    g = torch.randn(b, t, e, device="cuda").bfloat16()
+
+    def ref():  # zero fill + scatter-add of every token row at its (sample, id)
+        out = torch.zeros(b * v, e, dtype=g.dtype, device="cuda")
+        out.index_add_(0, (ids + torch.arange(b, device="cuda")[:, None] * v).reshape(-1), g.reshape(-1, e))
+        return out
+
+    ours = _time(lambda: ops.embedding_dense_grad(ids, g, v))
+    _row("embed_dense", ours, _time(ref), 2 * (g.numel() + b * v * e), 0, peaks,
+         {"shape": f"B={b} T={t} E={e} V={v}"})
+
+
+def bench_gated_norm(peaks):
+    from dattri_llm_b200.ops import fused
+
+    rows, d, eps = 2048, 5120, 1e-5
+    y = torch.randn(rows, d, device="cuda", requires_grad=True)
+    g = torch.randn(rows, d, device="cuda").bfloat16().requires_grad_()
+    w = torch.ones(d, device="cuda").bfloat16().requires_grad_()
+    dout = torch.randn(rows, d, device="cuda").bfloat16()
+
+    def ref():  # the Hugging Face module's chain (fp32), its cast, and the backward
+        h = y * torch.nn.functional.silu(g.float())
+        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+        (w * h).to(torch.bfloat16).backward(dout)
+
+    def ours_fn():
+        fused.gated_rms_norm(y, g, w, eps).backward(dout)
+
+    nbytes = (4 + 2 + 2) * rows * d + (2 + 4 + 2 + 2 + 4 + 2) * rows * d  # forward + backward streams
+    _row("gated_norm_fwd_bwd", _time(ours_fn), _time(ref), nbytes, 0, peaks, {"shape": f"rows={rows} d={d}"})
+
+
+def bench_causal_conv(peaks):
+    from dattri_llm_b200.ops import fused
+
+    b, length, c = 1, 2048, 5376
+    proj = torch.randn(b, length, c + 5200, device="cuda").bfloat16()
+    x = proj[..., 5120:5120 + c].detach().requires_grad_()
+    conv = torch.nn.Conv1d(c, c, 4, groups=c, padding=3).cuda().bfloat16()
+    dout = torch.randn(b, length, c, device="cuda").bfloat16()
+
+    def ref():  # the mixer's module call: transposes, cuDNN depthwise conv, slice, SiLU
+        out = torch.nn.functional.silu(conv(x.transpose(1, 2))[..., :length].transpose(1, 2))
+        out.backward(dout)
+
+    def ours_fn():
+        fused.causal_conv_silu(x, conv.weight, conv.bias).backward(dout)
+
+    _row("causal_conv_silu_fwd_bwd", _time(ours_fn), _time(ref), 2 * b * length * c * 5, 0, peaks,
+         {"shape": f"B={b} L={length} C={c}"})
+
+
+def bench_ssd_intra(peaks):
+    from dattri_llm_b200.ops import fused
+
+    b, c, s, h, g, p = 1, 8, 256, 80, 1, 64  # one Mamba2-2.7B layer at 2,048 tokens
+    cb = torch.randn(b, g, c, s, s, device="cuda", requires_grad=True)
+    cum = (-0.05 * torch.rand(b, h, c, s, device="cuda")).cumsum(-1).requires_grad_()
+    x = torch.randn(b, c, s, h, p, device="cuda", requires_grad=True)
+    dy = torch.randn(b, c, s, h, p, device="cuda")
+    causal = torch.ones(s, s, dtype=torch.bool, device="cuda").tril()
+
+    def ref():  # the materialized form: per-head decayed (chunk x chunk) matrices, einsum
+        decay = (cum[..., :, None] - cum[..., None, :]).masked_fill(~causal, float("-inf")).exp()
+        mix = cb.repeat_interleave(h // g, dim=1) * decay
+        torch.einsum("bhcst,bcthp->bcshp", mix, x).backward(dy)
+
+    def ours_fn():
+        fused.ssd_intra(cb, cum, x).backward(dy)
+
+    flops = 3 * 2 * b * h * c * (s * (s + 1) // 2) * p  # y, dx and dM over the causal half
+    _row("ssd_intra_fwd_bwd", _time(ours_fn), _time(ref), 4 * (3 * x.numel() + 2 * cb.numel()), flops, peaks,
+         {"shape": f"B={b} C={c} S={s} H={h} G={g} P={p}", "note": "fp32 CUDA cores; tensor_frac vs the bf16 peak"})
+
+
 BENCHES = {
     "ghost_gram": bench_ghost_gram,
     "ghost_dot": bench_ghost_dot,
@@ -269,6 +354,10 @@ BENCHES = {
     "per_sample_outer": bench_per_sample_outer,
     "adam_dir": bench_adam_dir,
     "project_seg": bench_project_seg,
+    "embed_dense": bench_embed_dense,
+    "gated_norm": bench_gated_norm,
+    "causal_conv": bench_causal_conv,
+    "ssd_intra": bench_ssd_intra,
 }
 
 

@@ -20,14 +20,15 @@ def embedding_dense_grad(ids: torch.Tensor, g: torch.Tensor, vocab: int) -> torc
     """``(B, vocab * E)`` per-sample embedding gradients: row ``v`` of sample ``b`` is the sum
     of ``g[b, t]`` over the tokens ``t`` with ``ids[b, t] == v``.  ``g`` is ``(B, T, E)`` bf16
     or fp32 (the result keeps its dtype); the tokens are sorted by ``b * vocab + id`` here
-    (stable, so sums run in token order) and the kernel writes every output row once."""
+    (stable, so sums run in token order), each output row's first token is located by a
+    search over the sorted keys, and the kernel writes every output row once."""
     from dattri_llm_b200.ops import count_launch, native
 
     b, t = ids.shape
     e = g.shape[-1]
     keys = (ids.long() + torch.arange(b, device=ids.device)[:, None] * vocab).reshape(-1)
     keys, order = torch.sort(keys, stable=True)
+    starts = torch.searchsorted(keys, torch.arange(b * vocab + 1, device=ids.device))  # row r: [starts[r], starts[r+1])
     count_launch()
-    out = native().embedding_dense_grad(keys.contiguous(), order.contiguous(), g.reshape(b * t, e).contiguous(),
-                                        b * vocab)
+    out = native().embedding_dense_grad(starts, order.contiguous(), g.reshape(b * t, e).contiguous(), b * vocab)
     return out.reshape(b, vocab * e)
