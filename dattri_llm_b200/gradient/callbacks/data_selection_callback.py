@@ -79,6 +79,19 @@ def _token_contraction(g: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
     return g.float().T @ a.float()
 
 
+
+def _sum_over_ranks(buf: torch.Tensor, world: int) -> None:
+    """In-place sum of the packed dropped contributions over ranks: the NVLink peer all-reduce
+    kernels when the group is the whole NCCL world on sm_100 GPUs (every rank packs the same
+    layout, so the call is collective), else ``torch.distributed.all_reduce``."""
+    import torch.distributed as dist
+
+    from dattri_llm_b200.parallel import symm
+
+    if world == dist.get_world_size() and symm.all_reduce_sum_(buf):
+        return
+    dist.all_reduce(buf)
+
 class DataSelectionCallback(HookManagerCallback):
     """Score every sample of each step and remove the selected ones' gradient contributions.
 
@@ -442,7 +455,7 @@ class DataSelectionCallback(HookManagerCallback):
             return
         if use_dist:
             buf = torch.cat([f for _, f in entries]).to(dev)
-            dist.all_reduce(buf)
+            _sum_over_ranks(buf, world)
             buf /= world
             off = 0
             for p, f in entries:
@@ -473,7 +486,7 @@ class DataSelectionCallback(HookManagerCallback):
             if not entries:
                 return
             buf = torch.cat([f for _, f in entries]).to(dev)
-            dist.all_reduce(buf)
+            _sum_over_ranks(buf, world)
             buf /= world
             off = 0
             for p, f in entries:
