@@ -548,12 +548,15 @@ def _c3_time(attribute, rank, world, steps, warmup, vocab, local):
     torch.cuda.synchronize()
     clocks.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prof = _Profiling(os.environ.get("DATTRI_BENCH_PROFILE", ""))
+    prof.start()
     t0 = time.perf_counter()
     ev0.record()
     attribute(torch.utils.data.Subset(data, range(n_warm, n_warm + n_meas)), test, "timed")
     ev1.record()
     torch.cuda.synchronize()
     host = time.perf_counter() - t0
+    prof.stop(rank)
     _barrier(world)
     clk = clocks.stop()
     ms = _max_over_ranks(ev0.elapsed_time(ev1), world) / steps

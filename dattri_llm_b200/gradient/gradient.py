@@ -25,6 +25,30 @@ GradientRepresentation = Literal["materialized", "factorized"]
 Indexing = Literal["batch", "batch_token"]
 
 
+
+def _dense_to_gpu_together(data: dict, device) -> dict[str, torch.Tensor]:
+    """``{name: tensor on device}`` for the host-resident dense tensors of *data* when *device*
+    is a GPU and there are several: per dtype, one pinned staging buffer, one copy, and views
+    of the device buffer (the layers' own storages are not shared with the host)."""
+    if device is None or torch.device(device).type != "cuda":
+        return {}
+    names = [n for n, v in data.items() if isinstance(v, torch.Tensor) and v.device.type == "cpu"]
+    if len(names) < 8:
+        return {}
+    target = torch.device(device)
+    out: dict[str, torch.Tensor] = {}
+    by_dtype: dict[torch.dtype, list[str]] = {}
+    for n in names:
+        by_dtype.setdefault(data[n].dtype, []).append(n)
+    for dt, group in by_dtype.items():
+        sizes = [data[n].numel() for n in group]
+        staging = torch.empty(sum(sizes), dtype=dt, pin_memory=True)
+        torch.cat([data[n].reshape(-1) for n in group], out=staging)
+        flat = staging.to(target, non_blocking=True)
+        for n, piece in zip(group, flat.split(sizes), strict=True):
+            out[n] = piece.view(data[n].shape)
+    return out
+
 @dataclass(frozen=True, eq=False)
 class Factorized:
     """A per-layer factorized ("ghost") gradient: an (activation, output-gradient) pair.
@@ -319,8 +343,12 @@ class Gradient:
         return Gradient(dict(self.representation), data, dict(self.layer_types), dict(self.indexing))
 
     def to(self, device=None, dtype=None, non_blocking: bool = False) -> Gradient:
-        """Every payload moved to *device* / cast to *dtype*."""
-        data = {n: v.to(device=device, dtype=dtype, non_blocking=non_blocking) if isinstance(v, Factorized)
+        """Every payload moved to *device* / cast to *dtype*.  Host-resident dense layers bound
+        for a GPU travel together, one copy per dtype (a record carries one tensor per
+        captured layer, and one blocking copy each would stall the host hundreds of times)."""
+        moved = _dense_to_gpu_together(self.data, device) if dtype is None else {}
+        data = {n: moved[n] if n in moved
+                else v.to(device=device, dtype=dtype, non_blocking=non_blocking) if isinstance(v, Factorized)
                 else v.to(device=device, dtype=dtype if (dtype is not None and v.is_floating_point()) else None,
                           non_blocking=non_blocking)
                 for n, v in self.data.items()}

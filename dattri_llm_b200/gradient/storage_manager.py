@@ -25,10 +25,13 @@ from __future__ import annotations
 
 from dattri_llm_b200.options import CacheResidency, DiskFormat  # noqa: F401  (re-exported option types)
 import contextlib
+import io
 import json
 import operator
+import pickle
 import tempfile
 import warnings
+import zipfile
 from collections.abc import Iterable
 from pathlib import Path
 
@@ -63,14 +66,65 @@ def _records_nbytes(records: list[GradientRecord]) -> int:
 
 
 def _host_record(record: GradientRecord) -> GradientRecord:
-    if record.gradient.device.type == "cpu":
+    """*record* with every payload on the host.  The dense layers of one device and dtype
+    travel in one copy (a record holds one tensor per captured layer -- hundreds -- and a
+    blocking copy each would stall the host once per layer); factorized payloads move as
+    they are."""
+    g = record.gradient
+    if g.device.type == "cpu":
         return record
-    return GradientRecord(record.step, record.input_hash, record.gradient.to("cpu"),
-                          getattr(record, "sample_id_key", None))
+    groups: dict[tuple, list[str]] = {}
+    for name, v in g.data.items():
+        if isinstance(v, torch.Tensor) and v.is_cuda:
+            groups.setdefault((v.device, v.dtype), []).append(name)
+    data = dict(g.data)
+    for names in groups.values():
+        flat = torch.cat([g.data[n].reshape(-1) for n in names]).to("cpu")
+        for n, piece in zip(names, flat.split([g.data[n].numel() for n in names]), strict=True):
+            data[n] = piece.view(g.data[n].shape)
+    for name, v in data.items():
+        if isinstance(v, Factorized):
+            data[name] = v.to(device="cpu")
+        elif v.is_cuda:
+            data[name] = v.to("cpu")
+    host = Gradient(dict(g.representation), data, dict(g.layer_types), dict(g.indexing))
+    return GradientRecord(record.step, record.input_hash, host, getattr(record, "sample_id_key", None))
 
 
 def _memmappable(records: list[GradientRecord]) -> bool:
     return all(isinstance(v, (torch.Tensor, Factorized)) for r in records for v in r.gradient.data.values())
+
+
+class _PlainPickle:
+    """A ``pickle_module`` for ``torch.save`` of tensor-free objects: its pickler is the C one,
+    with no per-object ``persistent_id`` hook (it would find no tensor or storage to record)."""
+
+    class Pickler:
+        def __init__(self, file, protocol=2) -> None:
+            self._file, self._protocol = file, protocol
+
+        def dump(self, obj) -> None:
+            pickle.dump(obj, self._file, protocol=self._protocol)
+
+
+class _NoGlobals(pickle.Unpickler):
+    """Unpickler of plain data (dicts, lists, strings, numbers): any class or function
+    reference, or any tensor record, is refused."""
+
+    def find_class(self, module, name):
+        raise pickle.UnpicklingError(f"{module}.{name} is not plain data")
+
+
+def _load_meta(path: Path) -> object:
+    """A memmap group's metadata.  Plain-data archives are read by the C unpickler with every
+    global refused (as safe as ``weights_only``, much faster for large metadata); anything
+    else goes through ``torch.load(weights_only=True)``."""
+    try:
+        with zipfile.ZipFile(path) as zf:
+            member = next(n for n in zf.namelist() if n.endswith("/data.pkl"))
+            return _NoGlobals(io.BytesIO(zf.read(member))).load()
+    except (zipfile.BadZipFile, StopIteration, pickle.UnpicklingError, EOFError, ValueError):
+        return torch.load(path, weights_only=True)
 
 
 def write_memmap_group(records: list[GradientRecord], handle_path: Path) -> None:
@@ -111,7 +165,10 @@ def write_memmap_group(records: list[GradientRecord], handle_path: Path) -> None
     with Path(f"{handle_path}.bin").open("wb") as f:
         for c in chunks:
             f.write(memoryview(c))
-    torch.save({"format": MEMMAP_FORMAT, "records": metas}, Path(f"{handle_path}.meta"))
+    # the metadata holds no tensors: the C pickler writes it (torch.save's own pickler calls a
+    # Python hook per object, an order of magnitude slower for hundreds of layers per record);
+    # the file is the same torch zip archive, so any torch.load reads it
+    torch.save({"format": MEMMAP_FORMAT, "records": metas}, Path(f"{handle_path}.meta"), pickle_module=_PlainPickle)
 
 
 def read_memmap_group(handle_path: Path) -> list[GradientRecord]:
@@ -120,7 +177,7 @@ def read_memmap_group(handle_path: Path) -> list[GradientRecord]:
     Raises:
         ValueError: for another memmap format version.
     """
-    payload = torch.load(Path(f"{handle_path}.meta"), weights_only=True)
+    payload = _load_meta(Path(f"{handle_path}.meta"))
     if not isinstance(payload, dict) or payload.get("format") != MEMMAP_FORMAT:
         found = payload.get("format") if isinstance(payload, dict) else "pre-v2"
         raise ValueError(

@@ -70,3 +70,37 @@ def test_ghost_route_matches_materialized_route_on_gpu():
     scale = ref.abs().max().item()
     torch.testing.assert_close(ghost.cpu().double(), ref, rtol=0, atol=1e-2 * scale)
     torch.testing.assert_close(mat.cpu().double(), ref, rtol=0, atol=2e-2 * scale)
+
+
+def test_host_record_batches_dense_layers_and_keeps_values():
+    from dattri_llm_b200.gradient.gradient import Factorized, Gradient, GradientRecord
+    from dattri_llm_b200.gradient.storage_manager import _host_record
+
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    dense = {f"l{i}": torch.randn(3, 5 + i, device="cuda", generator=gen).to(dt)
+             for i, dt in enumerate([torch.bfloat16, torch.float32, torch.bfloat16])}
+    fac = Factorized(torch.randn(3, 4, 6, device="cuda", generator=gen), torch.randn(3, 4, 2, device="cuda",
+                                                                                     generator=gen))
+    data = {**dense, "f": fac}
+    g = Gradient({n: "materialized" for n in dense} | {"f": "factorized"}, data,
+                 {n: "nn.Linear" for n in data}, {n: "batch" for n in data})
+    host = _host_record(GradientRecord(0, ["a", "b", "c"], g)).gradient
+    for n, v in dense.items():
+        assert host.data[n].device.type == "cpu" and host.data[n].dtype == v.dtype
+        assert torch.equal(host.data[n], v.cpu())
+    assert host.data["f"].activation.device.type == "cpu"
+    assert torch.equal(host.data["f"].activation, fac.activation.cpu())
+
+
+def test_gradient_to_gpu_moves_host_layers_together():
+    from dattri_llm_b200.gradient.gradient import Gradient
+
+    gen = torch.Generator().manual_seed(2)
+    data = {f"l{i}": torch.randn(2, 3 + i, generator=gen).to(torch.bfloat16 if i % 3 else torch.float32)
+            for i in range(12)}
+    g = Gradient({n: "materialized" for n in data}, data, {n: "nn.Linear" for n in data}, {n: "batch" for n in data})
+    moved = g.to("cuda")
+    torch.cuda.synchronize()
+    for n, v in data.items():
+        assert moved.data[n].is_cuda and moved.data[n].dtype == v.dtype and moved.data[n].shape == v.shape
+        assert torch.equal(moved.data[n].cpu(), v)

@@ -100,3 +100,38 @@ def test_rejects_unknown_options(tmp_path):
         GradientStorageManager(str(tmp_path / "s"), residency="gpu")
     with pytest.raises(ValueError):
         GradientStorageManager(str(tmp_path / "s"), disk_format="hdf5")
+
+
+def test_memmap_metadata_reads_back_through_torch_load_and_refuses_globals(tmp_path):
+    """The metadata is written by the C pickler into torch's zip archive: ``torch.load`` reads
+    it as written, and the fast reader refuses anything that is not plain data (a file holding
+    a tensor falls back to ``torch.load(weights_only=True)``)."""
+    import pickle
+
+    from dattri_llm_b200.gradient import storage_manager as sm
+
+    meta = {"format": 2, "records": [{"step": 3, "input_hash": ["h"], "sample_id_key": None,
+                                      "layers": {"l": {"kind": "dense", "parts": {"data": {
+                                          "byte_off": 0, "nbytes": 8, "shape": [1, 2], "dtype": "float32"}}}}}]}
+    path = tmp_path / "g.mmap.meta"
+    torch.save(meta, path, pickle_module=sm._PlainPickle)
+    assert torch.load(path, weights_only=True) == meta
+    assert sm._load_meta(path) == meta
+    other = tmp_path / "t.meta"
+    torch.save({"t": torch.arange(3)}, other)
+    assert torch.equal(sm._load_meta(other)["t"], torch.arange(3))
+
+    class Evil:
+        def __reduce__(self):
+            return (print, ("executed",))
+
+    bad = tmp_path / "bad.meta"
+    torch.save({"x": 1}, bad)
+    import zipfile
+
+    with zipfile.ZipFile(bad) as zf:
+        names = zf.namelist()
+    member = next(n for n in names if n.endswith("/data.pkl"))
+    with pytest.raises(pickle.UnpicklingError):
+        sm._NoGlobals(__import__("io").BytesIO(pickle.dumps(Evil()))).load()
+    assert member.endswith("data.pkl")
