@@ -668,12 +668,28 @@ class EKFACAttributor(KroneckerAttributor):
         self.mode = mode
 
     def _eigenbases(self, covariances: dict) -> Mapping:
+        """``{layer: (U_A, U_G)}``.  Factors of one size are eigendecomposed together, one
+        batched call per size and memory budget (capture-time projections make every factor
+        k x k: two calls instead of two per layer, each of which waits for the device)."""
         dev = self.args.device
         bases = self._tables.new(self.options.factor_cache_residency)
-        for layer in list(covariances):
-            a_cov, g_cov = covariances.pop(layer)
-            _, u_a, _, u_g = ops.kfac_eigh(a_cov.to(dev), g_cov.to(dev))
-            bases[layer] = (u_a, u_g)
+        layers = list(covariances)
+        by_size: dict[int, list[tuple[str, int, torch.Tensor]]] = {}
+        for layer in layers:
+            for side, cov in enumerate(covariances.pop(layer)):
+                by_size.setdefault(int(cov.shape[-1]), []).append((layer, side, cov))
+        vectors: dict[tuple[str, int], torch.Tensor] = {}
+        budget = 1 << 30  # bytes of fp32 factors per batched call
+        for n, items in by_size.items():
+            per_call = max(1, budget // (4 * n * n))
+            for i in range(0, len(items), per_call):
+                chunk = items[i:i + per_call]
+                stacked = torch.stack([cov.to(dev).float() for _, _, cov in chunk])
+                _, u = torch.linalg.eigh(stacked)
+                for (layer, side, _), u_i in zip(chunk, u.unbind(0), strict=True):
+                    vectors[(layer, side)] = u_i
+        for layer in layers:
+            bases[layer] = (vectors[(layer, 0)], vectors[(layer, 1)])
         return bases
 
     def sweep_factors(self, train_source, fisher_acc):
