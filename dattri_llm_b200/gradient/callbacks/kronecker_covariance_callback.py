@@ -20,12 +20,18 @@ from dattri_llm_b200.gradient.callbacks.base import HookManagerCallback
 
 
 class KroneckerCovarianceCallback(HookManagerCallback):
-    """Per-layer ``(A, G)`` accumulated over every captured step."""
+    """Per-layer ``(A, G)`` accumulated over every captured step.
+
+    Within a step the matched pairs of 2-D linear layers wait until the step ends and are
+    then added together, grouped by shape (:func:`ops.kfac_accumulate_grouped`: one batched
+    Gram product per side for all layers of a shape); other layers, and accumulators that
+    reduce through symmetric memory across GPUs, update as their pair arrives."""
 
     def __init__(self, *, include_bias: bool = True) -> None:
         self._include_bias = include_bias
         self._accumulators: dict[str, ops.LayerKroneckerAccumulator] = {}
         self._pending: dict[str, list[torch.Tensor]] = {}
+        self._step_rows: list[tuple[str, torch.Tensor, torch.Tensor]] = []  # (layer, a rows, g rows)
 
     def on_layer_forward(self, layer_name, activation, layer_type, module_kwargs) -> None:
         """Stack the activation until its backward."""
@@ -39,17 +45,40 @@ class KroneckerCovarianceCallback(HookManagerCallback):
         pending = self._pending.get(layer_name)
         if not pending:
             return
-        self._accumulators.setdefault(layer_name, ops.LayerKroneckerAccumulator()).update(
-            pending.pop(), grad_output, layer_type, module_kwargs, include_bias=self._include_bias)
+        acc = self._accumulators.setdefault(layer_name, ops.LayerKroneckerAccumulator())
+        activation = pending.pop()
+        if ops.is_linear(layer_type):
+            a_f, g_f = ops.flatten_kfac_factors(activation, grad_output, layer_type, module_kwargs,
+                                                include_bias=self._include_bias)
+            if acc.grouped_ok(a_f, g_f):
+                self._step_rows.append((layer_name, a_f, g_f))
+                return
+        acc.update(activation, grad_output, layer_type, module_kwargs, include_bias=self._include_bias)
+
+    def on_step_end(self, record) -> None:
+        """Add the step's waiting pairs, grouped by shape."""
+        self._flush()
+
+    def _flush(self) -> None:
+        rows, self._step_rows = self._step_rows, []
+        groups: dict[tuple, list[tuple[str, torch.Tensor, torch.Tensor]]] = {}
+        for name, a_f, g_f in rows:
+            key = (tuple(a_f.shape), tuple(g_f.shape), a_f.dtype, g_f.dtype, a_f.device)
+            groups.setdefault(key, []).append((name, a_f, g_f))
+        for items in groups.values():
+            ops.kfac_accumulate_grouped([self._accumulators[n] for n, _, _ in items],
+                                        [a for _, a, _ in items], [g for _, _, g in items])
 
     def all_reduce(self) -> None:
         """Sum every layer's accumulators over ranks (sorted order on every rank)."""
+        self._flush()
         from dattri_llm_b200.parallel.covariance import all_reduce_accumulators
 
         all_reduce_accumulators([self._accumulators[n] for n in sorted(self._accumulators)])
 
     def result(self) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
         """``{layer: (A, G)}`` means (layers without gradient-carrying rows omitted)."""
+        self._flush()
         out = {}
         for name, acc in self._accumulators.items():
             with contextlib.suppress(RuntimeError):
@@ -60,3 +89,4 @@ class KroneckerCovarianceCallback(HookManagerCallback):
         """Drop every accumulator."""
         self._accumulators.clear()
         self._pending.clear()
+        self._step_rows = []

@@ -45,8 +45,10 @@ from dattri_llm_b200.gradient.ops.kronecker import (
     ekfac_precondition,
     fim,
     fim_factors,
+    flatten_kfac_factors,
     kfac,
     kfac_cross,
+    kfac_accumulate_grouped,
     kfac_cross_factors,
     kfac_eigh,
     kfac_factors,

@@ -312,6 +312,11 @@ class LayerKroneckerAccumulator:
             gram_accumulate(g_f, self._G)
         self._count = self._count + n
 
+    def grouped_ok(self, a_f: torch.Tensor, g_f: torch.Tensor) -> bool:
+        """Whether this layer's flattened ``(N, w)`` factors may join a step's grouped update
+        (:func:`kfac_accumulate_grouped`): plain (not symmetric-memory) sums, 2-D rows."""
+        return self._symm is None and a_f.ndim == 2 and g_f.ndim == 2 and not self._use_symm(a_f, g_f)
+
     def all_reduce(self) -> None:
         """Sum the accumulators and counts over ranks (collective)."""
         if self._symm is not None:
@@ -457,3 +462,45 @@ class FisherAccumulator:
     def skipped(self) -> dict[str, int]:
         """Layers left out for width, with their width."""
         return dict(self._skipped)
+
+
+def kfac_accumulate_grouped(accs: list[LayerKroneckerAccumulator], a_fs: list[torch.Tensor],
+                            g_fs: list[torch.Tensor]) -> None:
+    """One step's flattened ``(N, w_a)`` / ``(N, w_g)`` factors of many layers of one shape added
+    to their accumulators together: the row masks, both Gram products (one batched GEMM each;
+    tcgen05 on sm_100 with bf16 rows) and the sums run once for all layers, instead of a
+    handful of small launches per layer (capture-time projections make every layer's factors
+    the same ``k``-wide shape)."""
+    from dattri_llm_b200 import ops as native_ops
+
+    a = torch.stack(a_fs)                            # (L, N, w_a)
+    g = torch.stack(g_fs)                            # (L, N, w_g)
+    keep = (g != 0).any(dim=-1)                      # rows that carry a gradient
+    a = a * keep.unsqueeze(-1).to(a.dtype)
+    counts = keep.sum(dim=-1)                        # (L,)
+    grams = []
+    for x in (a, g):
+        out = torch.zeros(x.shape[0], x.shape[-1], x.shape[-1], dtype=torch.float32, device=x.device)
+        if native_ops.use_native(x) and x.dtype == torch.bfloat16 and x.shape[1] > 0:
+            xt = native_ops.gemm._k_aligned(native_ops.gemm.transpose_last2(x))  # (L, w, N)
+            native_ops.gemm_tn(xt, xt, out, mode=native_ops.STORE_F32)
+        else:  # layer by layer, the same products as gram_accumulate's
+            for i in range(x.shape[0]):
+                out[i] += (x[i].transpose(-1, -2) @ x[i]).float()
+        grams.append(out)
+    for acc, x_a, x_g in zip(accs, a_fs, g_fs, strict=True):
+        if acc._A is None:
+            acc._A = torch.zeros(x_a.shape[-1], x_a.shape[-1], device=x_a.device)
+            acc._G = torch.zeros(x_g.shape[-1], x_g.shape[-1], device=x_g.device)
+        if not isinstance(acc._count, torch.Tensor):
+            acc._count = torch.tensor(acc._count, dtype=torch.int64, device=x_a.device)
+    torch._foreach_add_([acc._A for acc in accs], list(grams[0].unbind(0)))
+    torch._foreach_add_([acc._G for acc in accs], list(grams[1].unbind(0)))
+    torch._foreach_add_([acc._count for acc in accs], list(counts.unbind(0)))
+
+
+def flatten_kfac_factors(a, g, layer_type: str, module_kwargs: dict | None = None,
+                         include_bias: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """The ``(N, w)`` rows a K-FAC accumulator sums (preprocessed, flattened over tokens)."""
+    a, g = preprocess_factors(a, g, layer_type, module_kwargs, include_bias)
+    return _flatten_for_kfac(a, g, layer_type)

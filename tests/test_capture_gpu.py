@@ -104,3 +104,25 @@ def test_gradient_to_gpu_moves_host_layers_together():
     for n, v in data.items():
         assert moved.data[n].is_cuda and moved.data[n].dtype == v.dtype and moved.data[n].shape == v.shape
         assert torch.equal(moved.data[n].cpu(), v)
+
+
+def test_grouped_kfac_accumulation_matches_per_layer_updates():
+    from dattri_llm_b200.gradient.ops.kronecker import LayerKroneckerAccumulator, kfac_accumulate_grouped
+
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    layers = 5
+    a_fs = [torch.randn(600, 64, device="cuda", generator=gen).bfloat16() for _ in range(layers)]
+    g_fs = [torch.randn(600, 64, device="cuda", generator=gen).bfloat16() for _ in range(layers)]
+    for g in g_fs:
+        g[::7] = 0  # rows without a gradient are masked out of A and of the count
+    one = [LayerKroneckerAccumulator(fused_reduce=False) for _ in range(layers)]
+    grouped = [LayerKroneckerAccumulator(fused_reduce=False) for _ in range(layers)]
+    for _ in range(2):  # two steps
+        for acc, a, g in zip(one, a_fs, g_fs, strict=True):
+            acc.update(a, g, "nn.Linear", None, include_bias=False)
+        kfac_accumulate_grouped(grouped, a_fs, g_fs)
+    for want, got in zip(one, grouped, strict=True):
+        (wa, wg), (ga, gg) = want.result(), got.result()
+        assert want._n == got._n
+        torch.testing.assert_close(ga, wa, rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(gg, wg, rtol=1e-4, atol=1e-4)
