@@ -228,6 +228,8 @@ class OptimizerSnapshot:
             raise NotImplementedError(_FLAT_PARAMS_MSG)
         self._group_of = {id(p): g for g in optimizer.param_groups for p in g["params"]}
         self._layers: dict[str, _Layer] = {}
+        self._host_steps: dict[int, int] = {}  # id(param) -> updates, for counts kept on the GPU
+        self._step_hook = None
 
     @property
     def optimizer(self) -> torch.optim.Optimizer:
@@ -344,8 +346,26 @@ class OptimizerSnapshot:
             steps = [st["step"] for st in self._optimizer.state.values() if "step" in st]
             step = max(steps, default=0)
         if isinstance(step, torch.Tensor):
-            step = step.item()
+            step = self._device_step(src.param, step) if step.is_cuda else step.item()
         return int(step or 0)
+
+    def _device_step(self, param: torch.Tensor, step: torch.Tensor) -> int:
+        """The update count of *param* when the optimizer keeps it in a GPU tensor (fused or
+        capturable AdamW): read once, then counted on the host by a post-step hook, since a
+        read per call would wait for every kernel queued before it."""
+        key = id(param)
+        if key not in self._host_steps:
+            self._host_steps[key] = int(step.item())
+            if self._step_hook is None:
+                self._step_hook = self._optimizer.register_step_post_hook(self._count_step)
+        return self._host_steps[key]
+
+    def _count_step(self, optimizer, args, kwargs) -> None:
+        """Post-step hook: a parameter with a gradient has just been updated once more."""
+        for group in optimizer.param_groups:
+            for p in group["params"]:
+                if p.grad is not None and id(p) in self._host_steps:
+                    self._host_steps[id(p)] += 1
 
     # ------------------------------------------------------------------ state tensors
     def _assemble(self, layer_name: str, key: str, idx, include_bias: bool, reduce: bool):

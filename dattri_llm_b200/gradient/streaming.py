@@ -698,8 +698,12 @@ class GradientStreamer(GradientSource):
         if a.optim == "sgd":
             opt = torch.optim.SGD(groups, lr=a.learning_rate)
         elif a.optim in ("adamw_torch", "adamw"):
+            # GPU parameters take torch's fused AdamW (one update kernel per dtype and device
+            # instead of a dozen multi-tensor passes): the same update rule
+            params = decayed + plain
+            fused = bool(params) and all(p.is_cuda and p.is_floating_point() for p in params)
             opt = torch.optim.AdamW(groups, lr=a.learning_rate, betas=(a.adam_beta1, a.adam_beta2),
-                                    eps=a.adam_epsilon)
+                                    eps=a.adam_epsilon, fused=True if fused else None)
         else:
             raise ValueError(f"optimizer {a.optim!r} is not supported by the streamer: use 'adamw_torch' or 'sgd'.")
         updates = -(-len(self._loader) // self._window)

@@ -126,3 +126,29 @@ def test_grouped_kfac_accumulation_matches_per_layer_updates():
         assert want._n == got._n
         torch.testing.assert_close(ga, wa, rtol=1e-4, atol=1e-4)
         torch.testing.assert_close(gg, wg, rtol=1e-4, atol=1e-4)
+
+
+def test_fused_adamw_step_count_and_preconditioning_match_foreach():
+    """The streamer gives GPU parameters torch's fused AdamW, which keeps the update count on
+    the GPU; the optimizer snapshot counts it on the host after one read, and its Adam
+    preconditioning matches the multi-tensor optimizer's."""
+    from dattri_llm_b200.gradient.optimizer_state import OptimizerSnapshot
+
+    snaps, dirs = [], []
+    for fused in (True, False):
+        torch.manual_seed(0)
+        model = torch.nn.Sequential(torch.nn.Linear(16, 32, bias=False), torch.nn.Linear(32, 8, bias=False)).cuda()
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-2, fused=fused, foreach=None if fused else True)
+        snap = OptimizerSnapshot(model, opt)
+        x = torch.randn(4, 16, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+        for i in range(3):
+            model(x).pow(2).sum().backward()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            if i == 0:
+                assert snap.step_count("0") == 1  # first read of the GPU count
+        assert snap.step_count("0") == 3 and snap.step_count("1") == 3
+        g = torch.randn(5, 32 * 16, device="cuda", generator=torch.Generator(device="cuda").manual_seed(2))
+        dirs.append(snap.precondition("0", g))
+        snaps.append(snap)
+    torch.testing.assert_close(dirs[0], dirs[1], rtol=1e-3, atol=1e-3)
